@@ -1,0 +1,174 @@
+"""ctypes bindings for the CPU oracle (oracle.c).  TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this package, as the parity checker.  The product library never uses it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = os.path.join(_HERE, "liblaya_oracle.so")
+
+
+def build() -> str:
+    """Compile liblaya_oracle.so with its Makefile (gcc, no GPU needed)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB
+
+
+class Question(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("n_options", ctypes.c_int32),
+                ("option_len", ctypes.c_int32), ("suffix_len", ctypes.c_int32),
+                ("options", ctypes.POINTER(ctypes.c_int32)),
+                ("suffix", ctypes.POINTER(ctypes.c_int32))]
+
+
+class Answer(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("n_options", ctypes.c_int32),
+                ("choice", ctypes.c_int32), ("score", ctypes.c_float),
+                ("noul", ctypes.c_float), ("confidence", ctypes.c_float),
+                ("probabilities", ctypes.c_float * 16), ("logits", ctypes.c_float * 16)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB) or os.path.getmtime(_LIB) < os.path.getmtime(os.path.join(_HERE, "oracle.c")):
+            build()
+        L = ctypes.CDLL(_LIB)
+        P = ctypes.c_void_p
+        L.or_half.restype = ctypes.c_float
+        L.or_half.argtypes = [ctypes.c_uint16]
+        L.or_decode.argtypes = [ctypes.c_uint32, P, ctypes.c_size_t, P]
+        L.or_gguf_check.argtypes = [P, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
+        L.or_matrix_apply.argtypes = [P, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, P]
+        L.or_softmax.argtypes = [P, ctypes.c_int, P]
+        L.or_confidence.restype = ctypes.c_float
+        L.or_confidence.argtypes = [P, ctypes.c_int]
+        L.or_model_load.restype = P
+        L.or_model_load.argtypes = [P, ctypes.c_size_t, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
+        L.or_model_free.argtypes = [P]
+        L.or_model_dim.argtypes = [P, ctypes.c_int]
+        L.or_forward.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
+        L.or_head.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
+        L.or_decide.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(Question), ctypes.POINTER(Answer)]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray) -> ctypes.c_void_p:
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def half(x: int) -> float:
+    return lib().or_half(x)
+
+
+def layout(kind: int) -> tuple[int, int]:
+    return {0: (1, 4), 1: (1, 2), 2: (32, 18), 8: (32, 34), 12: (256, 144), 14: (256, 210)}[kind]
+
+
+def decode(kind: int, raw: bytes | np.ndarray) -> np.ndarray:
+    b = np.frombuffer(bytes(raw), dtype=np.uint8) if not isinstance(raw, np.ndarray) else np.ascontiguousarray(raw, dtype=np.uint8)
+    block, size = layout(kind)
+    out = np.zeros(len(b) // size * block, dtype=np.float32)
+    if lib().or_decode(kind, _p(b), len(b), _p(out)) != 0:
+        raise ValueError(f"unsupported kind {kind}")
+    return out
+
+
+def gguf_check(blob: bytes) -> str | None:
+    """None when the image parses, else the loader's error message."""
+    b = np.frombuffer(blob, dtype=np.uint8) if blob else np.zeros(1, np.uint8)
+    err = ctypes.create_string_buffer(256)
+    rc = lib().or_gguf_check(_p(b), len(blob), err, 256)
+    return None if rc == 0 else err.value.decode()
+
+
+def matrix_apply(w: np.ndarray, x: np.ndarray, bias: np.ndarray | None = None, threads: int = 1) -> np.ndarray:
+    w = np.ascontiguousarray(w, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = w.shape
+    m = x.size // cols
+    out = np.zeros((m, rows), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().or_matrix_apply(_p(w), rows, cols, _p(x), m, None if b is None else _p(b), threads, _p(out))
+    return out
+
+
+def softmax(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    p = np.zeros_like(x)
+    lib().or_softmax(_p(x), len(x), _p(p))
+    return p
+
+
+def confidence(p) -> float:
+    p = np.ascontiguousarray(p, np.float32)
+    return lib().or_confidence(_p(p), len(p))
+
+
+class Model:
+    """The oracle decoder: GGUF image → F32 weights (as the reference loads them)."""
+
+    def __init__(self, blob: bytes | np.ndarray, threads: int = 1):
+        self._buf = np.frombuffer(blob, dtype=np.uint8) if not isinstance(blob, np.ndarray) else blob
+        err = ctypes.create_string_buffer(256)
+        h = lib().or_model_load(_p(self._buf), len(self._buf), threads, err, 256)
+        if not h:
+            raise ValueError(err.value.decode())
+        self.h = ctypes.c_void_p(h)
+        L = lib()
+        self.d, self.layers, self.vocab, self.heads, self.kv, self.hd, self.ffn, self.ctx = (
+            L.or_model_dim(self.h, i) for i in range(8))
+
+    def close(self):
+        if self.h:
+            lib().or_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def forward(self, ids, read) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        read = np.ascontiguousarray(read, np.int32)
+        out = np.zeros((len(read), self.d), np.float32)
+        if lib().or_forward(self.h, _p(ids), len(ids), _p(read), len(read), _p(out)):
+            raise ValueError("invalid token sequence")
+        return out
+
+    def head(self, hidden, cand=None) -> np.ndarray:
+        hidden = np.ascontiguousarray(hidden, np.float32).reshape(-1, self.d)
+        n = 0 if cand is None else len(cand)
+        c = np.ascontiguousarray(cand if cand is not None else [0], np.int32)
+        out = np.zeros((hidden.shape[0], n or self.vocab), np.float32)
+        if lib().or_head(self.h, _p(hidden), hidden.shape[0], _p(c), n, _p(out)):
+            raise ValueError("invalid candidate id")
+        return out
+
+    def decide(self, ids, kind: int, options, suffix=()) -> dict:
+        ids = np.ascontiguousarray(ids, np.int32)
+        opts = np.ascontiguousarray(options, np.int32)
+        if opts.ndim == 1:
+            opts = opts.reshape(-1, 1)
+        suf = np.ascontiguousarray(suffix if len(suffix) else [0], np.int32)
+        q = Question(kind, opts.shape[0], opts.shape[1], len(suffix),
+                     opts.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                     suf.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+        a = Answer()
+        rc = lib().or_decide(self.h, _p(ids), len(ids), ctypes.byref(q), ctypes.byref(a))
+        if rc:
+            raise ValueError(f"oracle decide failed ({rc})")
+        k = a.n_options
+        return {"kind": a.kind, "choice": a.choice, "score": a.score, "noul": a.noul,
+                "confidence": a.confidence, "probabilities": list(a.probabilities[:k]),
+                "logits": list(a.logits[:k])}
