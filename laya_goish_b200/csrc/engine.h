@@ -1,0 +1,149 @@
+// Host engine of the decision hot path: one immutable weight replica per
+// GPU ("backends own immutable weights; request-local state must not escape
+// a call", src/models/mod.rs:12), a batched prefill + shared-prefix branch
+// forward, heads and the decision rules.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gguf.h"
+#include "kernels.h"
+#include "laya_cuda.h"
+
+namespace laya {
+
+constexpr int PAGE = 64;  // tokens per KV page (one attention key block)
+
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define LAYA_CK(x)                                 \
+  do {                                             \
+    cudaError_t e_ = (x);                          \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #x); \
+  } while (0)
+
+struct Config {
+  std::string arch;
+  int L = 0, d = 0, H = 0, KV = 0, hd = 0, ffn = 0, V = 0, ctx = 0;
+  float eps = 1e-5f, theta = 1e4f;
+  bool bias = false;
+  int wkind = 0;
+  bool quantized = false;  // any layer matrix stored in a block-quantised type
+  float temperature[3] = {1, 1, 1};
+  bool has_bucket[3][4] = {};
+  float bucket[3][4] = {};
+};
+
+// Grow-only device buffer.
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  int ensure(size_t bytes);
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+  void release();
+};
+
+struct HostBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  int ensure(size_t bytes);
+  void release();
+};
+
+struct Layer {
+  const float* attn_norm = nullptr;
+  const float* ffn_norm = nullptr;
+  QTensor wq{}, wk{}, wv{}, wo{}, wg{}, wu{}, wd{};
+  const float* bqkv = nullptr;
+  // F16 operands of the tcgen05 GEMMs, resident for F16 models; null for
+  // quantised models, which decode into per-layer staging before each GEMM.
+  const half* wqkv16 = nullptr;
+  const half* wgu16 = nullptr;  // gate/up rows interleaved per 128
+  const half* wo16 = nullptr;
+  const half* wd16 = nullptr;
+};
+
+struct ProfEvent {
+  int cat;
+  cudaEvent_t a, b;
+};
+
+struct Replica {
+  int device = 0, num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  size_t weight_bytes = 0;
+  std::vector<Layer> layers;
+  QTensor embd{}, head{};
+  const float* out_norm = nullptr;
+  const half* head16 = nullptr;  // F16 lm_head for full-vocabulary rows (lazy for quantised models)
+  const float2* rope = nullptr;  // [ctx][hd/2] (cos, sin)
+  unsigned* err = nullptr;
+  std::map<std::string, QTensor> named;
+  // scratch
+  DevBuf ids, pos, slot, x, h, qb, att, act, items, tables, rows, hid32, hid16, cand, row_of, clog, flog, lse, cow;
+  DevBuf wqkv_s, wo_s, wgu_s, wd_s;  // F16 staging of one layer (quantised models)
+  DevBuf kc, vc;
+  int kv_pages = 0;
+  HostBuf pin;
+  // decode scratch
+  DevBuf dx16, dlogits, dargmax, dpart;
+  // timing of the current call
+  bool arm_start = false;
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+  double call_ms = 0;
+  long long launches = 0, h2d = 0, d2h = 0;
+  // profiling
+  bool prof = false;
+  std::vector<ProfEvent> prof_events;
+  std::vector<cudaEvent_t> event_pool;
+  std::map<std::string, std::pair<long long, double>> prof_acc;
+};
+
+struct Model {
+  Config cfg;
+  std::vector<Replica> reps;
+  std::mutex mu;  // calls on one model are serialised
+};
+
+// Token-level plan of one forward pass (prefill or branch).
+struct PassPlan {
+  std::vector<int> ids, pos, slot;
+  std::vector<AttnItem> items;
+  std::vector<int> read_rows;  // rows whose final-normed hidden is needed
+};
+
+std::string read_config(const Gguf& g, Config* c);
+int load_replica(Model& m, const Gguf& g, int device, Replica& r);
+void free_replica(Replica& r);
+int ensure_kv(Model& m, Replica& r, int pages);
+int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>& tables, int read_base,
+                int (*canceled)(void*), void* user, std::mutex* cancel_mu);
+int ensure_head16(Model& m, Replica& r);
+int decide_shard(Model& m, Replica& r, const laya_batch& b, int r0, int r1, laya_answer* out,
+                 int (*canceled)(void*), void* user, std::mutex* cancel_mu);
+int validate_batch(const Config& c, const laya_batch* b);
+int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int n_seqs, int steps, int32_t* out,
+               float* stats);
+
+// profiling helpers
+enum ProfCat { P_GEMM_QKV, P_GEMM_O, P_GEMM_GU, P_GEMM_DOWN, P_GEMM_HEAD, P_ATTN, P_DEQUANT, P_GEMV, P_ATTN_DEC, P_NCAT };
+extern const char* kProfNames[P_NCAT];
+void prof_begin(Replica& r, int cat, cudaEvent_t* a);
+void prof_end(Replica& r, int cat, cudaEvent_t a);
+void prof_collect(Replica& r);
+int timing_begin_call(Replica& r);
+int timing_mark_start(Replica& r);
+int timing_mark_end(Replica& r);
+
+}  // namespace laya

@@ -1,0 +1,387 @@
+// Prefill GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   Y[M x N] = X[M x K] . W[N x K]^T   (F16 operands, F32 accumulation)
+//
+// This replaces the reference's F32 AVX2 kernel Matrix::apply
+// (src/tensor.rs:10-102): same contract (W row-major [rows=N][cols=K],
+// one output row per token, optional bias), computed as a persistent,
+// warp-specialised kernel:
+//   warp 0     : TMA producer — 128x64 A tile + 256x64 B tile per stage,
+//                128-byte swizzle, 4-stage shared-memory ring
+//   warp 1     : allocates 512 TMEM columns; one elected thread issues
+//                tcgen05.mma (M=128, N=256, K=16) and commits to mbarriers
+//   warps 2..5 : epilogue — tcgen05.ld from TMEM, fused bias / residual add
+//                (tensor::add, src/tensor.rs:123-128) / SwiGLU
+//                (src/models/openthai/model.rs:225-230) / QKV + RoPE + KV-cache
+//                write, then stores to HBM
+// Two 256-column accumulators in TMEM let the epilogue of tile i overlap the
+// MMAs of tile i+1.  Every TMA load reads this GPU's own memory and none
+// uses cluster multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "ptx.cuh"
+
+namespace laya {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int GEMM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int GEMM_SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 + 256;
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+
+__device__ __forceinline__ void store_f16x32(half* dst, const float* v, int n) {
+  if (n == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      uint4 u;
+      half2 h0 = __floats2half2_rn(v[8 * i], v[8 * i + 1]);
+      half2 h1 = __floats2half2_rn(v[8 * i + 2], v[8 * i + 3]);
+      half2 h2 = __floats2half2_rn(v[8 * i + 4], v[8 * i + 5]);
+      half2 h3 = __floats2half2_rn(v[8 * i + 6], v[8 * i + 7]);
+      u.x = *reinterpret_cast<uint32_t*>(&h0);
+      u.y = *reinterpret_cast<uint32_t*>(&h1);
+      u.z = *reinterpret_cast<uint32_t*>(&h2);
+      u.w = *reinterpret_cast<uint32_t*>(&h3);
+      reinterpret_cast<uint4*>(dst)[i] = u;
+    }
+  } else {
+    for (int i = 0; i < n; i++) dst[i] = __float2half_rn(v[i]);
+  }
+}
+
+__device__ __forceinline__ void store_f32x32(float* dst, const float* v, int n) {
+  if (n == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    for (int i = 0; i < n; i++) dst[i] = v[i];
+  }
+}
+
+template <int EPI, int HD>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = a.m_tiles * a.n_tiles;
+  const int kblocks = (a.K + BK - 1) / BK;
+  const long long budget = a.budget;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued[STAGES];
+      for (int s = 0; s < STAGES; s++) issued[s] = -1;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, budget)) {
+            atomicOr(a.err, 1u);
+            ok = false;
+            break;
+          }
+          issued[stage] = (int)phase;
+          mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // On a timeout, leave no copy in flight: wait (bounded) for every
+      // stage this thread filled to land before the CTA exits.
+      if (!ok)
+        for (int s = 0; s < STAGES; s++)
+          if (issued[s] >= 0) mbar_wait(&full[s], (uint32_t)issued[s], budget);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idesc = idesc_f16_f32(BM, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, budget)) {
+          atomicOr(a.err, 2u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&full[stage], phase, budget)) {
+            atomicOr(a.err, 4u);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            umma_f16(tmem_d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // Epilogue: warp w may read TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    const int quarter = warp % 4;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+      if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
+        atomicOr(a.err, 8u);
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * BM + quarter * 32 + lane;
+      const bool live = row < a.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int col0 = nt * BN;
+      if constexpr (EPI == EPI_F32 || EPI == EPI_F16 || EPI == EPI_RESID) {
+        for (int c = 0; c < BN / 32; c++) {
+          const int cb = col0 + c * 32;
+          if (cb >= a.N) break;
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          const int n = min(32, a.N - cb);
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+          if (a.bias)
+            for (int i = 0; i < n; i++) v[i] += a.bias[cb + i];
+          if (live) {
+            if constexpr (EPI == EPI_F32) {
+              store_f32x32(reinterpret_cast<float*>(a.out) + (size_t)row * a.ldo + cb, v, n);
+            } else if constexpr (EPI == EPI_F16) {
+              store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb, v, n);
+            } else {
+              float* x = a.resid + (size_t)row * a.ldo + cb;
+              if (n == 32) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                  float4 o = reinterpret_cast<float4*>(x)[i];
+                  o.x += v[4 * i];
+                  o.y += v[4 * i + 1];
+                  o.z += v[4 * i + 2];
+                  o.w += v[4 * i + 3];
+                  reinterpret_cast<float4*>(x)[i] = o;
+                }
+              } else {
+                for (int i = 0; i < n; i++) x[i] += v[i];
+              }
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
+        // B rows of tile nt: [0,128) gate rows, [128,256) up rows of FFN
+        // columns nt*128 .. nt*128+127 (interleaved at load time).
+        for (int c = 0; c < 4; c++) {
+          const int fc = nt * 128 + c * 32;
+          if (fc >= a.N / 2) break;
+          uint32_t rg[32], ru[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, rg);
+          tmem_ld32(tbase + 128 + c * 32, ru);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = silu_f(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+          if (live) store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + fc, v, min(32, a.N / 2 - fc));
+        }
+      } else if constexpr (EPI == EPI_QKV) {
+        // Columns: [0,qd) q heads, [qd,qd+kd) k heads, [qd+kd,qd+2kd) v heads.
+        // One head (hd columns) at a time: bias, rotate-half RoPE for q/k
+        // (src/tensor.rs:158-171), then q -> Q rows, k/v -> paged KV cache.
+        constexpr int hd = HD;
+        int pos = 0, slot = 0;
+        if (live) {
+          pos = a.pos[row];
+          slot = a.slot[row];
+        }
+        for (int hc = 0; hc < BN; hc += hd) {
+          const int cb = col0 + hc;
+          if (cb >= a.N) break;
+          float v[hd];
+#pragma unroll
+          for (int c = 0; c < hd / 32; c++) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(tbase + hc + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[c * 32 + i] = __uint_as_float(r[i]);
+          }
+          if (!live) continue;
+          if (a.bias) {
+#pragma unroll
+            for (int i = 0; i < hd; i++) v[i] += a.bias[cb + i];
+          }
+          const bool is_v = cb >= a.qd + a.kd;
+          if (!is_v) {
+            const float2* cs = a.rope + (size_t)pos * (hd / 2);
+#pragma unroll
+            for (int j = 0; j < hd / 2; j++) {
+              const float2 t = cs[j];
+              const float x0 = v[j], x1 = v[j + hd / 2];
+              v[j] = x0 * t.x - x1 * t.y;
+              v[j + hd / 2] = x1 * t.x + x0 * t.y;
+            }
+          }
+          if (cb < a.qd) {
+            half* dst = reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb;
+#pragma unroll
+            for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
+          } else {
+            const int kvh = is_v ? (cb - a.qd - a.kd) / hd : (cb - a.qd) / hd;
+            const int page = slot / a.page_size, off = slot % a.page_size;
+            half* base = is_v ? a.vcache : a.kcache;
+            half* dst = base + (((size_t)page * a.kvh + kvh) * a.page_size + off) * hd;
+#pragma unroll
+            for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major F16 matrix [rows][cols] as a 2-D TMA map with a box of
+// box_rows x 64 columns and 128-byte swizzle.
+static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI, int HD>
+static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
+                              cudaStream_t st) {
+  static bool configured[64] = {false};  // per device, per instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_tc_kernel<EPI, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
+  }
+  gemm_tc_kernel<EPI, HD><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
+                        cudaStream_t st) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaSuccess;
+  if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, A, a.M, a.K, lda, BM) || !make_map(&tb, B, a.N, a.K, ldb, BN)) return cudaErrorInvalidValue;
+  a.m_tiles = (a.M + BM - 1) / BM;
+  a.n_tiles = (a.N + BN - 1) / BN;
+  const int total = a.m_tiles * a.n_tiles;
+  const int grid = total < num_sms ? total : num_sms;
+  switch (epi) {
+    case EPI_F32: return launch_epi<EPI_F32, 64>(ta, tb, a, grid, st);
+    case EPI_F16: return launch_epi<EPI_F16, 64>(ta, tb, a, grid, st);
+    case EPI_RESID: return launch_epi<EPI_RESID, 64>(ta, tb, a, grid, st);
+    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU, 64>(ta, tb, a, grid, st);
+    case EPI_QKV:
+      if (a.hd == 64) return launch_epi<EPI_QKV, 64>(ta, tb, a, grid, st);
+      if (a.hd == 128) return launch_epi<EPI_QKV, 128>(ta, tb, a, grid, st);
+      return cudaErrorInvalidValue;
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace laya

@@ -1,0 +1,41 @@
+// Host interface of the tcgen05 prefill GEMM (gemm.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace laya {
+
+// Epilogues fused into the GEMM.
+enum Epi : int {
+  EPI_F32 = 0,     // out F32 [M][ldo] = acc (+bias)
+  EPI_F16 = 1,     // out F16 [M][ldo] = acc (+bias)
+  EPI_RESID = 2,   // resid F32 [M][ldo] += acc            (tensor::add)
+  EPI_SWIGLU = 3,  // out F16 [M][ldo] = silu(gate) * up   (gate/up rows interleaved per 128)
+  EPI_QKV = 4,     // bias + RoPE; q -> out F16 [M][ldo]; k, v -> paged KV cache
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int m_tiles, n_tiles;   // filled by gemm_launch
+  const float* bias;      // [N] or null
+  void* out;
+  int ldo;
+  float* resid;
+  // EPI_QKV
+  int qd, kd, hd, kvh;
+  const int* pos;         // [M] absolute token positions
+  const int* slot;        // [M] KV slot = page * page_size + offset
+  const float2* rope;     // [positions][hd/2] (cos, sin)
+  half* kcache;
+  half* vcache;           // [pages][kvh][page_size][hd]
+  int page_size;
+  unsigned* err;          // device error word; nonzero after a timed-out wait
+  long long budget;       // wait budget in SM clock cycles
+};
+
+// A: [M][lda] F16 row-major activations, B: [N][ldb] F16 row-major weights
+// (K contiguous).  lda, ldb multiples of 8; A, B 16-byte aligned.
+cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
+                        cudaStream_t st);
+
+}  // namespace laya

@@ -1,0 +1,531 @@
+// Memory-bound kernels of the decision hot path and the paged causal GQA
+// attention.  Each cites the reference function it replaces.
+#include <cfloat>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace laya {
+
+// ---------------------------------------------------------------- dequant
+
+// gguf::decode (src/gguf.rs:250-336) on the original GGUF block bytes:
+// one thread per block (per element for F32/F16), same arithmetic order,
+// explicit round-to-nearest so the result is bit-identical.
+__global__ void dequant_raw_kernel(int kind, const uint8_t* __restrict__ b, size_t nblocks, float* __restrict__ out) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= nblocks) return;
+  switch (kind) {
+    case K_F32: {
+      const uint8_t* c = b + i * 4;
+      out[i] = bits_f32(c[0] | (c[1] << 8) | (c[2] << 16) | ((uint32_t)c[3] << 24));
+    } break;
+    case K_F16: {
+      const uint8_t* c = b + i * 2;
+      out[i] = half_bits(c[0] | (c[1] << 8));
+    } break;
+    case K_Q8_0: {
+      const uint8_t* c = b + i * 34;
+      float d = half_bits(c[0] | (c[1] << 8));
+      for (int j = 0; j < 32; j++) out[i * 32 + j] = __fmul_rn(d, (float)(int8_t)c[2 + j]);
+    } break;
+    case K_Q4_0: {
+      const uint8_t* c = b + i * 18;
+      float d = half_bits(c[0] | (c[1] << 8));
+      for (int j = 0; j < 16; j++) {
+        out[i * 32 + j] = __fmul_rn(d, __fsub_rn((float)(c[2 + j] & 15), 8.f));
+        out[i * 32 + j + 16] = __fmul_rn(d, __fsub_rn((float)(c[2 + j] >> 4), 8.f));
+      }
+    } break;
+    case K_Q4_K: {
+      const uint8_t* c = b + i * 144;
+      float d = half_bits(c[0] | (c[1] << 8)), dm = half_bits(c[2] | (c[3] << 8));
+      const uint8_t* sc = c + 4;
+      const uint8_t* qs = c + 16;
+      float* o = out + i * 256;
+      for (int g = 0; g < 4; g++) {
+        uint32_t s[2], m[2];
+        for (int t = 0; t < 2; t++) {
+          int j = g * 2 + t;
+          if (j < 4) {
+            s[t] = sc[j] & 63;
+            m[t] = sc[j + 4] & 63;
+          } else {
+            s[t] = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4);
+            m[t] = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+          }
+        }
+        for (int j = 0; j < 32; j++) {
+          uint32_t q = qs[g * 32 + j];
+          o[g * 64 + j] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s[0]), (float)(q & 15)), __fmul_rn(dm, (float)m[0]));
+          o[g * 64 + 32 + j] =
+              __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s[1]), (float)(q >> 4)), __fmul_rn(dm, (float)m[1]));
+        }
+      }
+    } break;
+    case K_Q6_K: {
+      const uint8_t* c = b + i * 210;
+      const uint8_t* ql = c;
+      const uint8_t* qh = c + 128;
+      const int8_t* sc = reinterpret_cast<const int8_t*>(c + 192);
+      float d = half_bits(c[208] | (c[209] << 8));
+      float* o = out + i * 256;
+      for (int n = 0; n < 2; n++)
+        for (int l = 0; l < 32; l++) {
+          int lo = n * 64 + l;
+          uint32_t hi = qh[n * 32 + l];
+          int si = n * 8 + l / 16;
+          uint32_t q[4] = {(ql[lo] & 15u) | ((hi & 3u) << 4), (ql[lo + 32] & 15u) | (((hi >> 2) & 3u) << 4),
+                           (uint32_t)(ql[lo] >> 4) | (((hi >> 4) & 3u) << 4),
+                           (uint32_t)(ql[lo + 32] >> 4) | (((hi >> 6) & 3u) << 4)};
+          for (int j = 0; j < 4; j++)
+            o[n * 128 + j * 32 + l] = __fmul_rn(__fmul_rn(d, (float)sc[si + j * 2]), __fsub_rn((float)q[j], 32.f));
+        }
+    } break;
+  }
+}
+
+cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st) {
+  if (!nblocks) return cudaSuccess;
+  dequant_raw_kernel<<<(unsigned)((nblocks + 255) / 256), 256, 0, st>>>(kind, blocks, nblocks, out);
+  return cudaGetLastError();
+}
+
+// Decodes a weight from its HBM layout into an F16 matrix row block used as
+// the tcgen05 B operand.  Output row of source row n:
+// (n / grp) * gstride + goff + (n % grp), so q/k/v rows can be stacked and
+// gate/up rows interleaved per 128 rows for the fused SwiGLU epilogue.
+__global__ void dequant_f16_kernel(QTensor t, half* __restrict__ out, int ldo, int grp, int gstride, int goff) {
+  const int groups = t.cols / 32;
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)t.rows * groups) return;
+  const int n = (int)(i / groups), g = (int)(i % groups);
+  float v[32];
+  dq32(t, n, g * 32, v);
+  const size_t orow = (size_t)(n / grp) * gstride + goff + (n % grp);
+  uint4* dst = reinterpret_cast<uint4*>(out + orow * ldo + g * 32);
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    half2 h[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) h[j] = __floats2half2_rn(v[8 * c + 2 * j], v[8 * c + 2 * j + 1]);
+    dst[c] = *reinterpret_cast<uint4*>(h);
+  }
+}
+
+cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstride, int goff, cudaStream_t st) {
+  size_t n = (size_t)t.rows * (t.cols / 32);
+  if (!n) return cudaSuccess;
+  dequant_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(t, out, ldo, grp, gstride, goff);
+  return cudaGetLastError();
+}
+
+// Decodes whole rows to F32 (row list optional): the embedding lookup of
+// src/models/openthai/model.rs:205-213 and the tensor read-back used by the
+// parity tests.
+__global__ void rows_f32_kernel(QTensor t, const int* __restrict__ ids, int nrows, float* __restrict__ out) {
+  const int groups = t.cols / 32;
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)nrows * groups) return;
+  const int r = (int)(i / groups), g = (int)(i % groups);
+  const int n = ids ? ids[r] : r;
+  float v[32];
+  dq32(t, n, g * 32, v);
+  float4* dst = reinterpret_cast<float4*>(out + (size_t)r * t.cols + g * 32);
+#pragma unroll
+  for (int c = 0; c < 8; c++) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st) {
+  size_t n = (size_t)nrows * (t.cols / 32);
+  if (!n) return cudaSuccess;
+  rows_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(t, ids, nrows, out);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- RMSNorm
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < (int)(blockDim.x / 32) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// rms (src/models/openthai/model.rs:84-94), offset 0, eps from the GGUF:
+// y = x / sqrt(mean(x^2) + eps) * w.  One block per output row; optional
+// source-row gather (answer-position gather, model.rs:232-235).
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const int* __restrict__ rows, const float* __restrict__ w,
+                               int d, float eps, half* __restrict__ out16, float* __restrict__ out32) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const float* xr = x + (size_t)(rows ? rows[r] : r) * d;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+    float4 v = *reinterpret_cast<const float4*>(xr + i);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = block_sum(ss, red);
+  const float scale = 1.f / sqrtf(ss / (float)d + eps);
+  for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+    float4 v = *reinterpret_cast<const float4*>(xr + i);
+    float4 g = *reinterpret_cast<const float4*>(w + i);
+    float y0 = v.x * scale * g.x, y1 = v.y * scale * g.y, y2 = v.z * scale * g.z, y3 = v.w * scale * g.w;
+    if (out16) {
+      half2 a = __floats2half2_rn(y0, y1), b = __floats2half2_rn(y2, y3);
+      uint2 u = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+      *reinterpret_cast<uint2*>(out16 + (size_t)r * d + i) = u;
+    }
+    if (out32) *reinterpret_cast<float4*>(out32 + (size_t)r * d + i) = make_float4(y0, y1, y2, y3);
+  }
+}
+
+cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
+                    float* out32, cudaStream_t st) {
+  if (!nrows) return cudaSuccess;
+  rmsnorm_kernel<<<nrows, 256, 0, st>>>(x, rows, w, d, eps, out16, out32);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- heads
+
+// Restricted head: logits of the candidate rows of the untied lm_head only
+// (slot head of src/models/openthai/model.rs:236-240 restricted to the
+// candidate ids, read as in src/models/openthai/decision.rs:268-279).
+// One warp per (row, candidate); F32 hidden, weights decoded on the fly.
+__global__ void head_restricted_kernel(QTensor w, const float* __restrict__ hid, const int* __restrict__ cand,
+                                       const int* __restrict__ row_of, int n, float* __restrict__ out) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (gw >= n) return;
+  const int id = cand[gw];
+  const float* h = hid + (size_t)row_of[gw] * w.cols;
+  float acc = 0.f;
+  for (int g = lane; g < w.cols / 32; g += 32) {
+    float v[32];
+    dq32(w, id, g * 32, v);
+    const float4* hp = reinterpret_cast<const float4*>(h + g * 32);
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      float4 x = hp[c];
+      acc += v[4 * c] * x.x + v[4 * c + 1] * x.y + v[4 * c + 2] * x.z + v[4 * c + 3] * x.w;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
+  if (lane == 0) out[gw] = acc;
+}
+
+cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,
+                            cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  head_restricted_kernel<<<(n * 32 + 255) / 256, 256, 0, st>>>(w, hid, cand, row_of, n, out);
+  return cudaGetLastError();
+}
+
+// Full-vocabulary log-sum-exp per row, for multi-token options scored by
+// summed log-probabilities: lse = max + log(sum(exp(x - max))).
+__global__ void lse_kernel(const float* __restrict__ logits, int V, float* __restrict__ out) {
+  __shared__ float red[32];
+  const int i = blockIdx.x;
+  const float* x = logits + (size_t)i * V;
+  float mx = -FLT_MAX;
+  for (int c = threadIdx.x; c < V; c += blockDim.x) mx = fmaxf(mx, x[c]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : -FLT_MAX;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffff, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float s = 0.f;
+  for (int c = threadIdx.x; c < V; c += blockDim.x) s += expf(x[c] - mx);
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) out[i] = mx + logf(s);
+}
+
+cudaError_t lse_rows(const float* logits, int V, int n, float* out, cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  lse_kernel<<<n, 512, 0, st>>>(logits, V, out);
+  return cudaGetLastError();
+}
+
+// F32 [rows][cols] -> F16 [rows][ld], zero padding columns cols..ld-1.
+__global__ void f32_to_f16_pad_kernel(const float* __restrict__ x, int rows, int cols, int ld, half* __restrict__ y) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)rows * ld) return;
+  const int r = (int)(i / ld), c = (int)(i % ld);
+  y[i] = __float2half_rn(c < cols ? x[(size_t)r * cols + c] : 0.f);
+}
+
+cudaError_t f32_to_f16_pad(const float* x, int rows, int cols, int ld, half* y, cudaStream_t st) {
+  size_t n = (size_t)rows * ld;
+  if (!n) return cudaSuccess;
+  f32_to_f16_pad_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, rows, cols, ld, y);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- KV pages
+
+// Copy-on-write of partially filled shared-prefix pages: each pair copies
+// one page (K and V, every layer) so a branch can append after it.
+__global__ void kv_copy_kernel(half* kc, half* vc, const int2* __restrict__ pairs, size_t page_elems,
+                               size_t layer_elems, int layers) {
+  const int2 p = pairs[blockIdx.y];
+  const size_t n16 = page_elems / 8;
+  for (int l = 0; l < layers; l++) {
+    const uint4* ks = reinterpret_cast<const uint4*>(kc + l * layer_elems + (size_t)p.x * page_elems);
+    const uint4* vs = reinterpret_cast<const uint4*>(vc + l * layer_elems + (size_t)p.x * page_elems);
+    uint4* kd = reinterpret_cast<uint4*>(kc + l * layer_elems + (size_t)p.y * page_elems);
+    uint4* vd = reinterpret_cast<uint4*>(vc + l * layer_elems + (size_t)p.y * page_elems);
+    for (size_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
+      kd[i] = ks[i];
+      vd[i] = vs[i];
+    }
+  }
+}
+
+cudaError_t kv_copy(half* kc, half* vc, const int2* pairs, int npairs, size_t page_elems, size_t layer_elems,
+                    int layers, cudaStream_t st) {
+  if (!npairs) return cudaSuccess;
+  kv_copy_kernel<<<dim3(8, npairs), 256, 0, st>>>(kc, vc, pairs, page_elems, layer_elems, layers);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- attention
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Causal GQA attention over the paged KV cache (src/models/openthai/model.rs:276-294:
+// softmax(q.k * scale) over keys j <= i, then .v, with kv head = h / (H/KV)).
+// One CTA = 64 query rows of one sequence x one query head; 4 warps of 16
+// rows; flash-style online softmax over 64-key blocks (one page each),
+// double-buffered cp.async loads, XOR-swizzled shared memory.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_kernel(const half* __restrict__ q, int ldq, half* __restrict__ o, int ldo,
+                                                   const half* __restrict__ kc, const half* __restrict__ vc,
+                                                   const int* __restrict__ tables, const AttnItem* __restrict__ items,
+                                                   int H, int KV, float scale_log2) {
+  constexpr int BQ = 64, BKV = 64, CH = HD / 8;
+  extern __shared__ uint4 smem_attn[];
+  half* sQ = reinterpret_cast<half*>(smem_attn);
+  half* sK = sQ + BQ * HD;
+  half* sV = sK + 2 * BKV * HD;
+  const AttnItem it = items[blockIdx.x];
+  const int h = blockIdx.y, kvh = h / (H / KV);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_keys = it.pos0 + it.q_len;
+  const int n_blocks = (n_keys + BKV - 1) / BKV;
+  auto sw = [](int r, int c) { return r * HD + ((c ^ (r & 7)) << 3); };
+
+  for (int i = threadIdx.x; i < BQ * CH; i += 128) {
+    const int r = i / CH, c = i % CH;
+    if (r < it.q_len)
+      cp_async16(sQ + sw(r, c), q + (size_t)(it.q_row + r) * ldq + h * HD + c * 8);
+    else
+      *reinterpret_cast<uint4*>(sQ + sw(r, c)) = make_uint4(0, 0, 0, 0);
+  }
+  auto load_kv = [&](int kb, int buf) {
+    const int page = tables[it.table_off + kb];
+    const size_t base = ((size_t)page * KV + kvh) * BKV * HD;
+    const int valid = min(BKV, n_keys - kb * BKV);
+    half* dk = sK + buf * BKV * HD;
+    half* dv = sV + buf * BKV * HD;
+    for (int i = threadIdx.x; i < BKV * CH; i += 128) {
+      const int r = i / CH, c = i % CH;
+      if (r < valid) {
+        cp_async16(dk + sw(r, c), kc + base + r * HD + c * 8);
+        cp_async16(dv + sw(r, c), vc + base + r * HD + c * 8);
+      } else {
+        *reinterpret_cast<uint4*>(dk + sw(r, c)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dv + sw(r, c)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  load_kv(0, 0);
+  cp_commit();
+
+  const int g = lane / 4, t = lane % 4;
+  const int row0 = warp * 16 + g;
+  const int pos_a = it.pos0 + row0, pos_b = pos_a + 8;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float acc[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  uint32_t qf[HD / 16][4];
+
+  for (int kb = 0; kb < n_blocks; kb++) {
+    if (kb + 1 < n_blocks) {
+      load_kv(kb + 1, (kb + 1) & 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; kk++) ldsm_x4(qf[kk], sQ + sw(warp * 16 + (lane % 16), kk * 2 + lane / 16));
+    }
+    const half* bK = sK + (kb & 1) * BKV * HD;
+    const half* bV = sV + (kb & 1) * BKV * HD;
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; kk++) {
+#pragma unroll
+      for (int nj = 0; nj < 8; nj += 2) {
+        uint32_t b[4];
+        const int mat = lane / 8;
+        ldsm_x4(b, bK + sw(nj * 8 + (lane % 8) + (mat / 2) * 8, kk * 2 + (mat % 2)));
+        mma16816(s[nj], qf[kk], b[0], b[1]);
+        mma16816(s[nj + 1], qf[kk], b[2], b[3]);
+      }
+    }
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int key = kb * BKV + j * 8 + 2 * t;
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        float va = s[j][e] * scale_log2, vb = s[j][2 + e] * scale_log2;
+        if (key + e > pos_a || key + e >= n_keys) va = -INFINITY;
+        if (key + e > pos_b || key + e >= n_keys) vb = -INFINITY;
+        s[j][e] = va;
+        s[j][2 + e] = vb;
+        mx_a = fmaxf(mx_a, va);
+        mx_b = fmaxf(mx_b, vb);
+      }
+    }
+#pragma unroll
+    for (int o2 = 1; o2 <= 2; o2 <<= 1) {
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffff, mx_a, o2));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffff, mx_b, o2));
+    }
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    const float ca = exp2f(m_a - mn_a), cb = exp2f(m_b - mn_b);
+    m_a = mn_a;
+    m_b = mn_b;
+    float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      s[j][0] = exp2f(s[j][0] - mn_a);
+      s[j][1] = exp2f(s[j][1] - mn_a);
+      s[j][2] = exp2f(s[j][2] - mn_b);
+      s[j][3] = exp2f(s[j][3] - mn_b);
+      sum_a += s[j][0] + s[j][1];
+      sum_b += s[j][2] + s[j][3];
+    }
+#pragma unroll
+    for (int o2 = 1; o2 <= 2; o2 <<= 1) {
+      sum_a += __shfl_xor_sync(0xffffffff, sum_a, o2);
+      sum_b += __shfl_xor_sync(0xffffffff, sum_b, o2);
+    }
+    l_a = l_a * ca + sum_a;
+    l_b = l_b * cb + sum_b;
+#pragma unroll
+    for (int i = 0; i < HD / 8; i++) {
+      acc[i][0] *= ca;
+      acc[i][1] *= ca;
+      acc[i][2] *= cb;
+      acc[i][3] *= cb;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      uint32_t pa[4] = {pack_h2(s[2 * kk][0], s[2 * kk][1]), pack_h2(s[2 * kk][2], s[2 * kk][3]),
+                        pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]), pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+#pragma unroll
+      for (int nd = 0; nd < HD / 8; nd += 2) {
+        uint32_t b[4];
+        const int mat = lane / 8;
+        ldsm_x4_t(b, bV + sw(kk * 16 + (lane % 8) + (mat % 2) * 8, nd + mat / 2));
+        mma16816(acc[nd], pa, b[0], b[1]);
+        mma16816(acc[nd + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  const float ia = 1.f / l_a, ib = 1.f / l_b;
+  if (row0 < it.q_len) {
+    half* dst = o + (size_t)(it.q_row + row0) * ldo + h * HD;
+#pragma unroll
+    for (int i = 0; i < HD / 8; i++)
+      *reinterpret_cast<uint32_t*>(dst + i * 8 + 2 * t) = pack_h2(acc[i][0] * ia, acc[i][1] * ia);
+  }
+  if (row0 + 8 < it.q_len) {
+    half* dst = o + (size_t)(it.q_row + row0 + 8) * ldo + h * HD;
+#pragma unroll
+    for (int i = 0; i < HD / 8; i++)
+      *reinterpret_cast<uint32_t*>(dst + i * 8 + 2 * t) = pack_h2(acc[i][2] * ib, acc[i][3] * ib);
+  }
+}
+
+template <int HD>
+static cudaError_t attn_launch(const AttnParams& p, cudaStream_t st) {
+  const int smem = 5 * 64 * HD * 2;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
+  }
+  attn_kernel<HD><<<dim3(p.n_items, p.H), 128, smem, st>>>(p.q, p.ldq, p.o, p.ldo, p.kc, p.vc, p.tables, p.items, p.H,
+                                                             p.KV, p.scale_log2);
+  return cudaGetLastError();
+}
+
+cudaError_t attention(const AttnParams& p, cudaStream_t st) {
+  if (!p.n_items) return cudaSuccess;
+  if (p.hd == 64) return attn_launch<64>(p, st);
+  if (p.hd == 128) return attn_launch<128>(p, st);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace laya

@@ -1,0 +1,46 @@
+// Host interface of the memory-bound kernels and the attention (kernels.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace laya {
+
+// One attention work unit: query rows [q_row, q_row + q_len) of one sequence
+// at absolute positions pos0.., attending keys 0 .. pos0+q_len-1 through the
+// page list tables[table_off ..] (one 64-token page per key block).
+struct AttnItem {
+  int q_row, q_len, pos0, table_off;
+};
+
+struct AttnParams {
+  const half* q;
+  int ldq;
+  half* o;
+  int ldo;
+  const half* kc;  // this layer's K pages [pages][KV][64][hd]
+  const half* vc;
+  const int* tables;
+  const AttnItem* items;
+  int n_items, H, KV, hd;
+  float scale_log2;
+};
+
+cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st);
+cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstride, int goff, cudaStream_t st);
+cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st);
+cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
+                    float* out32, cudaStream_t st);
+cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,
+                            cudaStream_t st);
+cudaError_t lse_rows(const float* logits, int V, int n, float* out, cudaStream_t st);
+cudaError_t f32_to_f16_pad(const float* x, int rows, int cols, int ld, half* y, cudaStream_t st);
+cudaError_t kv_copy(half* kc, half* vc, const int2* pairs, int npairs, size_t page_elems, size_t layer_elems,
+                    int layers, cudaStream_t st);
+cudaError_t attention(const AttnParams& p, cudaStream_t st);
+
+}  // namespace laya

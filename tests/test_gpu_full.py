@@ -1,0 +1,50 @@
+"""Parity at the benchmark configurations' full sizes (Llama-16L, d 2048,
+V 32000): one request of cfg0 (F16, 256 tokens, check over 2 candidates)
+and cfg1 (Q8_0, 512 tokens, choose over 4) against the oracle, plus
+size-independent properties at the full batch size (determinism, batch
+invariance)."""
+import numpy as np
+import pytest
+
+import oracle
+from laya_goish_b200 import engine, synth
+from laya_goish_b200.engine import Question
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", params=["cfg0", "cfg1"])
+def full(request):
+    path = synth.model_path(request.param)
+    e = engine.Engine(path)
+    yield request.param, path, e
+    e.close()
+
+
+def test_full_config_decide_matches_oracle(full):
+    cfg, path, e = full
+    rng = np.random.default_rng({"cfg0": 0, "cfg1": 1}[cfg])
+    V = 32000
+    n, k, kind = (256, 2, "noul") if cfg == "cfg0" else (512, 4, "choice")
+    prompt = synth.token_ids(rng, V, n)
+    q = Question(kind, synth.candidates(rng, V, k))
+    got = e.decide(prompt, [q])[0]
+    o = oracle.Model(open(path, "rb").read(), threads=16)
+    kind_i, opts, suf = q.arrays()
+    want = o.decide(prompt, kind_i, opts, suf)
+    o.close()
+    p, w = np.array(got["probabilities"]), np.array(want["probabilities"])
+    assert np.allclose(p, w, atol=1e-3, rtol=1e-2), (p, w)
+    if kind == "choice":
+        assert got["choice"] == want["choice"]
+
+
+def test_full_batch_determinism_and_invariance(full):
+    cfg, _, e = full
+    rng = np.random.default_rng(5)
+    prompts = [synth.token_ids(rng, 32000, 512) for _ in range(16)]
+    q = [Question("choice", synth.candidates(rng, 32000, 4))]
+    a = e.decide_batch(prompts, q)
+    assert a == e.decide_batch(prompts, q)
+    alone = e.decide_batch(prompts[3:4], q)[0][0]
+    assert np.allclose(alone["probabilities"], a[3][0]["probabilities"], atol=1e-5)
