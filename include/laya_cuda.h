@@ -135,6 +135,27 @@ int laya_forward(laya_model* m, const int32_t* ids, int n, const int32_t* read, 
  * (for parity checks of the upload transcoding).  out: element count floats. */
 int laya_tensor_f32(laya_model* m, const char* name, float* out, size_t max_elems);
 
+/* Allocation-free Matrix::apply.  No counterpart in the reference.
+ * For callers that cannot allocate device memory — a host program whose own
+ * pool already owns all of HBM, or a thread that must not stall on
+ * cudaMalloc/cudaFree — this computes what laya_matrix_apply computes, but
+ * w (GGUF bytes of type `kind`), x [m][cols] F32, bias [rows] F32 (may be
+ * NULL) and out [m][rows] F32 are DEVICE pointers the caller owns, and the
+ * F16 staging of the GEMM lives in a fixed array of LAYA_STATIC_SCRATCH_BYTES
+ * inside the library, which every GPU that loads the library holds until
+ * the process exits.  Work runs on `stream` (a cudaStream_t, NULL for the
+ * legacy default stream) on the current device; the call returns after it
+ * finished.  Needing more than the limit — 256 B + rows*cols*4 +
+ * (rows + m) * ceil8(cols) * 2 bytes, each part rounded up to 256 — is
+ * rejected with LAYA_E_INVALID.  The first call on a device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls on a device share the one array: calls that overlap on the GPU
+ * (concurrent host threads or streams) race and must be serialised by the
+ * caller.  It calls no cudaMalloc/cudaFree and no allocating library. */
+#define LAYA_STATIC_SCRATCH_BYTES (16u << 20)
+int laya_matrix_apply_static(uint32_t kind, const uint8_t* w, int rows, int cols, const float* x, int m,
+                             const float* bias, float* out, void* stream);
+
 /* ---- timing of the last laya_decide_batch / laya_decode call ---- */
 typedef struct laya_timing {
   double device_ms;   /* CUDA-event time on the device stream(s), inputs already in HBM; max over devices */
