@@ -50,9 +50,9 @@ def attention_flops(cfg, n) -> float:
     return 4.0 * (n * (n + 1) / 2) * cfg.heads * cfg.hd * cfg.layers
 
 
-def inputs(rank: int):
+def inputs(rank: int, requests: int = REQUESTS):
     rng = np.random.default_rng(1000 + rank)
-    prompts = [synth.token_ids(rng, CFG.vocab, TOKENS) for _ in range(REQUESTS)]
+    prompts = [synth.token_ids(rng, CFG.vocab, TOKENS) for _ in range(requests)]
     cand = synth.candidates(np.random.default_rng(1), CFG.vocab, OPTIONS)
     return prompts, cand
 
@@ -190,7 +190,7 @@ def run_ours(args):
     from laya_goish_b200 import engine
     from laya_goish_b200.engine import Question
 
-    prompts, cand = inputs(rank)
+    prompts, cand = inputs(rank, args.requests)
     qs = [Question("choice", cand)]
     e = engine.Engine(path, devices=[local])
     for _ in range(args.warmup):
@@ -220,13 +220,13 @@ def run_ours(args):
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dev_ms, wall = float(t[0]), float(t[1])
-    total_req = REQUESTS * world * args.steps
+    total_req = args.requests * world * args.steps
     value = total_req / (dev_ms / 1000.0)
     e2e = total_req / wall
     # roofline of the dominant kernel class: the tcgen05 GEMMs
     gemm_ms = sum(v[1] for k, v in prof.items() if k.startswith("gemm_"))
     gemm_launches = sum(v[0] for k, v in prof.items() if k.startswith("gemm_"))
-    gemm_flops = gemm_flops_per_token(CFG) * REQUESTS * TOKENS * args.steps
+    gemm_flops = gemm_flops_per_token(CFG) * args.requests * TOKENS * args.steps
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None
     pk, pk_kind = peaks()
     peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
@@ -236,7 +236,7 @@ def run_ours(args):
         "metric": "decide requests/s", "value": value, "unit": "req/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "requests_per_gpu": REQUESTS, "prompt_tokens": TOKENS,
+        "config": {"workload": WORKLOAD, "requests_per_gpu": args.requests, "prompt_tokens": TOKENS,
                    "weights": "Q8_0 (RTN from seeded F16 N(0,0.02))", "compute": "F16 operands, F32 accumulation",
                    "l2": "working set > L2 (weights 1.03 GB, activations 0.5 GB/layer); no flush needed",
                    "parallelism": f"request sharding x{world}, full replica per GPU, no collective"},
@@ -270,6 +270,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=REQUESTS,
+                    help="requests per GPU (64 is the benchmark; smaller only for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
