@@ -67,28 +67,38 @@ def peaks():
 
 
 class Clocks:
-    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+    """Samples nvidia-smi clocks and throttle reasons every 100 ms.  Started
+    before the warm-up; summary() keeps the samples whose timestamps fall in
+    the timed window [begin(), end()]."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: int):
         self.device = device
         self.p = None
+        self.t0 = self.t1 = None
+        self.lines = []
 
-    def __enter__(self):
+    def start(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                       "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
                                       stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def begin(self):
+        self.t0 = time.time()
+
+    def end(self):
+        self.t1 = time.time()
+
+    def stop(self):
         if self.p:
+            time.sleep(0.25)
             self.p.terminate()
             try:
                 out, _ = self.p.communicate(timeout=5)
@@ -98,15 +108,20 @@ class Clocks:
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self) -> dict:
+        import datetime
+
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                if self.t0 is not None and not (self.t0 - 0.1 <= ts <= (self.t1 or ts) + 0.1):
+                    continue
+                sm.append(float(f[2]))
+                mx = max(mx, float(f[3]))
             except ValueError:
                 continue
             for name, v in zip(names, f[5:9]):
@@ -114,6 +129,21 @@ class Clocks:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reduce_max(values, dist, device):
+    """Element-wise max of per-rank timings over all ranks (identity without a process group)."""
+    import torch
+
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.cpu()]
+
+
+def throughput(units_per_rank: int, world: int, steps: int, max_ms: float) -> float:
+    """Whole-job units per second: every rank's units over the slowest rank's time."""
+    return units_per_rank * world * steps / (max_ms / 1000.0)
 
 
 def cpu_baseline(path: str, prompts, cand, sample_requests: int = 1) -> dict:
@@ -193,6 +223,7 @@ def run_ours(args):
     prompts, cand = inputs(rank, args.requests)
     qs = [Question("choice", cand)]
     e = engine.Engine(path, devices=[local])
+    clk = Clocks(local).start()
     for _ in range(args.warmup):
         e.decide_batch(prompts, qs)
     e.profile(True)
@@ -201,28 +232,26 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     dev_ms, wall, launches, h2d, d2h = 0.0, 0.0, 0, 0, 0
-    with Clocks(local) as clk:
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            e.decide_batch(prompts, qs)
-            wall += time.perf_counter() - t0
-            t = e.timing()
-            dev_ms += t["device_ms"]
-            launches += t["launches"]
-            h2d += t["h2d_bytes"]
-            d2h += t["d2h_bytes"]
+    clk.begin()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        e.decide_batch(prompts, qs)
+        wall += (time.perf_counter() - t0) * 1000.0
+        t = e.timing()
+        dev_ms += t["device_ms"]
+        launches += t["launches"]
+        h2d += t["h2d_bytes"]
+        d2h += t["d2h_bytes"]
     torch.cuda.synchronize()
+    clk.end()
     if dist:
         dist.barrier()
+    clk.stop()
     prof = e.profile_read()
     e.profile(False)
-    t = torch.tensor([dev_ms, wall], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dev_ms, wall = float(t[0]), float(t[1])
-    total_req = args.requests * world * args.steps
-    value = total_req / (dev_ms / 1000.0)
-    e2e = total_req / wall
+    dev_ms, wall = reduce_max([dev_ms, wall], dist, "cuda")
+    value = throughput(args.requests, world, args.steps, dev_ms)
+    e2e = throughput(args.requests, world, args.steps, wall)
     # roofline of the dominant kernel class: the tcgen05 GEMMs
     gemm_ms = sum(v[1] for k, v in prof.items() if k.startswith("gemm_"))
     gemm_launches = sum(v[0] for k, v in prof.items() if k.startswith("gemm_"))

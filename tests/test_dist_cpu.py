@@ -1,0 +1,54 @@
+"""The N>1 bench path on CPU: two gloo ranks reduce their timings with MAX
+(the slowest rank sets the time) and the whole-job throughput counts every
+rank's requests (weak scaling, no data-path collective)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import datetime
+    import bench
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        dev_ms, wall = bench.reduce_max([100.0 + 50 * rank, 300.0 - rank], dist, "cpu")
+        q.put((rank, dev_ms, wall, bench.throughput(64, world, 10, dev_ms)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_max_reduction_and_weak_throughput():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    got = sorted(q.get(timeout=10) for _ in range(2))
+    for rank, dev_ms, wall, tput in got:
+        assert dev_ms == 150.0 and wall == 300.0  # max over ranks on every rank
+        assert tput == pytest.approx(64 * 2 * 10 / 0.150)
+
+
+def test_single_process_reduction_is_identity():
+    import bench
+
+    assert bench.reduce_max([1.5, 2.5], None, "cpu") == [1.5, 2.5]
+    assert bench.throughput(64, 1, 10, 1000.0) == pytest.approx(640.0)

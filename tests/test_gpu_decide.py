@@ -153,3 +153,19 @@ def test_open_rejects_malformed_gguf():
     with pytest.raises(engine.LayaError) as ex:
         engine.Engine("/nonexistent/model.gguf")
     assert ex.value.code == engine._lib.E_IO
+
+
+def test_multi_replica_sharding_matches_single(tiny_paths):
+    # Two replicas on one GPU exercise the in-process request sharding (one host
+    # thread per replica, contiguous request ranges, answers in request order).
+    path = tiny_paths["tiny-llama-q8_0"]
+    rng = np.random.default_rng(11)
+    prompts = [synth.token_ids(rng, 1000, int(n)) for n in (30, 200, 5, 64, 90, 17, 128)]
+    qs = [Question("choice", [10, 11, 12]), Question("score", [[3, 4], [5, 6]], suffix=[7])]
+    with engine.Engine(path, devices=[0]) as one, engine.Engine(path, devices=[0, 0]) as two:
+        assert two.info["n_devices"] == 2
+        a = one.decide_batch(prompts, qs)
+        b = two.decide_batch(prompts, qs)
+    for i in range(len(prompts)):
+        for j in range(len(qs)):
+            assert np.allclose(a[i][j]["probabilities"], b[i][j]["probabilities"], atol=1e-5), (i, j)
