@@ -292,6 +292,58 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_decode(args):
+    """cfg4: KV-cached greedy decode on the cfg1 Q8_0 decoder.  Context of
+    `--ctx` seeded ids per sequence, `--gen` generated tokens, `--batch`
+    sequences per GPU.  Reports ms per decode step and the HBM GB/s of the
+    GEMV launches (Q8_0 weight bytes incl. lm_head per step / GEMV time) and of
+    the whole step (weights + KV bytes / step time).  Not the contract line:
+    the default invocation measures configs[1]."""
+    import torch
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    from laya_goish_b200 import engine
+
+    path = synth.model_path("cfg1")
+    rng = np.random.default_rng(4)
+    ctxs = [synth.token_ids(rng, CFG.vocab, args.ctx) for _ in range(args.batch)]
+    e = engine.Engine(path, devices=[local])
+    e.decode(ctxs[:1], 4)  # warm-up
+    e.profile(True)
+    e.profile_read()
+    clk = Clocks(local).start()
+    clk.begin()
+    toks, st = e.decode(ctxs, args.gen)
+    clk.end()
+    clk.stop()
+    t = e.timing()
+    prof = e.profile_read()
+    e.close()
+    steps = args.gen - 1
+    ms = t["device_ms"] / steps
+    qd, kd = CFG.heads * CFG.hd, CFG.kv * CFG.hd
+    per_layer = CFG.d * (qd + 2 * kd) + qd * CFG.d + 3 * CFG.d * CFG.ffn
+    wbytes = (per_layer * CFG.layers + CFG.vocab * CFG.d) * 34 / 32
+    kv_bytes = args.batch * CFG.layers * 2 * (args.ctx + args.gen / 2) * kd * 2
+    pk, pk_kind = peaks()
+    # the per-kernel profile covers decode step 1 (run outside the graph); later
+    # steps replay the same launches as one CUDA graph
+    gemv_ms = prof.get("gemv", (0, 0.0))[1]
+    out = {"workload": f"cfg4 decode: Llama-16L Q8_0, batch {args.batch}, ctx {args.ctx}, {args.gen} greedy tokens",
+           "ms_per_token": ms, "tokens_per_s": args.batch / (ms / 1000),
+           "step_gbs": (wbytes + kv_bytes) / (ms / 1000) / 1e9,
+           "gemv_gbs": (wbytes / (gemv_ms / 1000) / 1e9) if gemv_ms else None,
+           "peak_gbs": pk["hbm_gbs"], "peak_kind": pk_kind,
+           "weight_bytes_per_step": wbytes, "kv_bytes_per_step": kv_bytes,
+           "prefill_ms": st["prefill_ms"], "kernel_ms_step1": {k: v[1] for k, v in sorted(prof.items()) if not k.startswith("prefill:")},
+           "launches_per_step": t["launches"] / steps, "clocks": clk.summary()}
+    if out["gemv_gbs"]:
+        out["gemv_frac"] = out["gemv_gbs"] / pk["hbm_gbs"]
+    out["step_frac"] = out["step_gbs"] / pk["hbm_gbs"]
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -299,12 +351,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode"])
+    ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
+    ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
+    ap.add_argument("--gen", type=int, default=128, help="decode: generated tokens")
     ap.add_argument("--requests", type=int, default=REQUESTS,
                     help="requests per GPU (64 is the benchmark; smaller only for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "decode":
+        run_decode(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -56,6 +56,15 @@ __host__ __device__ __forceinline__ float half_bits(uint32_t x) {
 }
 
 #ifdef __CUDACC__
+// Programmatic dependent launch: a kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may start before the
+// previous kernel in the stream has finished.  pdl_wait() blocks until that
+// kernel completed and its writes are visible (a no-op for ordinary
+// launches); pdl_trigger() lets the next kernel start.  Call pdl_trigger()
+// only after pdl_wait(), so at most one kernel ever overlaps.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Decodes elements [k0, k0+32) of row n (k0 % 32 == 0), bit-exact with the
 // reference decoder's arithmetic order (src/gguf.rs:250-336): no FMA
 // contraction, explicit round-to-nearest multiplies.

@@ -2,105 +2,498 @@
 // KV cache and no decode loop, src/models/laya/decision.rs:302).
 //
 // Each step appends one token per sequence.  Small batches run the linear
-// layers as bandwidth-bound GEMVs that read the quantised weights once with
-// 128-bit loads and decode them in registers; larger batches reuse the
-// tcgen05 GEMM path.  Attention over the paged cache is split along the
-// key axis so that even a single sequence spreads over all SMs.
-#include <cfloat>
+// layers as bandwidth-bound GEMVs that stream the quantised weights once with
+// 128-bit loads (four 32-element groups in flight per lane), decode them in
+// registers and fuse SwiGLU and the residual add; larger batches reuse the
+// tcgen05 GEMM.  Attention stages each 64-token K/V page in shared memory and
+// splits the key axis across CTAs so a single sequence still covers the GPU.
+// All per-step inputs live at fixed device addresses, advanced by a
+// one-thread-block kernel, so the whole step is captured once as a CUDA
+// graph and replayed for every generated token.
 #include <algorithm>
+#include <cfloat>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 
 #include "engine.h"
 #include "gemm.h"
+#include "launch.h"
 
 namespace laya {
 
 // ---------------------------------------------------------------- GEMV
 
-// y[b][n] (+)= sum_k x[b][k] * W[n][k] for B <= 16 rows of F16 x.
-// One warp per ROWS output rows; lanes stride over 32-element groups of K,
-// decoding the weights once per group (dq32) and reusing them for all B.
-template <int B, int ROWS>
-__global__ void __launch_bounds__(256) gemv_kernel(QTensor w, const half* __restrict__ x, int ldx,
-                                                   float* __restrict__ y, int ldy, int accumulate) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  const int n0 = warp * ROWS;
-  if (n0 >= w.rows) return;
-  const int groups = w.cols / 32;
-  float acc[ROWS][B];
+struct GemvSeg {
+  QTensor w;
+  float* y;  // y[b * ldy + row]
+  int ldy;
+  int acc;   // add into y (fused residual) instead of storing
+};
+
+// Up to three matrices share one launch (q, k, v); in SwiGLU mode a warp
+// computes the gate row and the up row of one FFN column and writes
+// silu(gate) * up as F16 (src/models/openthai/model.rs:225-230).
+struct GemvPlan {
+  GemvSeg seg[3];
+  int nseg;
+  int rows;  // warps' rows: sum of segment rows, or ffn in SwiGLU mode
+  const half* x;
+  int ldx;
+  int swiglu;  // 0 off, 1 gate = seg[0] and up = seg[1], 2 interleaved gate/up rows in seg[0]
+  half* act;
+  int ld_act;
+  unsigned long long* best;  // greedy mode: per batch row, max of pack_logit(value, row)
+  // Fused RMSNorm input (src/models/openthai/model.rs:84-94): when xres is
+  // set, x = rmsnorm(xres[b], norm_w, eps) is built per block in shared
+  // memory (F16) instead of being read from a separate normalised buffer.
+  const float* xres;
+  const float* norm_w;
+  float eps;
+};
+
+// Order-preserving packing of (logit, row) into 64 bits: larger logits win,
+// equal logits resolve to the lower row (the argmax ties-to-lowest rule).
+__device__ __forceinline__ unsigned long long pack_logit(float v, int row) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)row);
+}
+__device__ __forceinline__ int unpack_row(unsigned long long k) { return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu)); }
+
+// Raw 16-byte slots of the next groups of one row, loaded ahead of their use
+// so many loads are in flight.  A Q8_0 group (32 int8 + scale) takes 2
+// slots, an F16 group 4; lane l holds groups l, l+32, ...
+template <int NV>
+struct RowRaw {
+  static_assert(NV >= 4 && NV % 4 == 0, "a batch must hold at least one F16 group (4 slots)");
+  uint4 v[NV];
+  uint32_t sc[NV / 2];
+};
+
+// Groups held per batch: always >= 1 because NV >= 4.
+__device__ __forceinline__ int groups_per_batch(int kind, int nv) { return kind == K_Q8_0 ? nv / 2 : nv / 4; }
+
+template <int NV>
+__device__ __forceinline__ void row_load(const QTensor& w, int n, int g0, int groups, RowRaw<NV>& r) {
+  if (w.kind == K_Q8_0) {
+    const uint4* qp = reinterpret_cast<const uint4*>(w.q + (size_t)n * w.cols);
+    const uint16_t* sp = w.s + (size_t)n * groups;
 #pragma unroll
-  for (int r = 0; r < ROWS; r++)
-#pragma unroll
-    for (int b = 0; b < B; b++) acc[r][b] = 0.f;
-  for (int g = lane; g < groups; g += 32) {
-    float wv[ROWS][32];
-#pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-      if (n0 + r < w.rows) dq32(w, n0 + r, g * 32, wv[r]);
-      else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) wv[r][i] = 0.f;
+    for (int u = 0; u < NV / 2; u++) {
+      const int g = g0 + 32 * u;
+      if (g < groups) {
+        r.v[2 * u] = __ldg(qp + 2 * g);
+        r.v[2 * u + 1] = __ldg(qp + 2 * g + 1);
+        r.sc[u] = __ldg(sp + g);
       }
     }
+  } else if (w.kind == K_F16) {
+    const uint4* qp = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(w.q) + (size_t)n * w.cols);
 #pragma unroll
-    for (int b = 0; b < B; b++) {
-      const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)b * ldx + g * 32);
+    for (int u = 0; u < NV / 4; u++) {
+      const int g = g0 + 32 * u;
+      if (g < groups)
+#pragma unroll
+        for (int c = 0; c < 4; c++) r.v[4 * u + c] = __ldg(qp + 4 * g + c);
+    }
+  }
+}
+
+// int8 byte j of w (as stored, two's complement) to float without I2F:
+// bytes are biased by 128 and placed in the mantissa of 2^23, and the exact
+// difference with 2^23 + 128 recovers q (integers below 2^24 are exact).
+__device__ __forceinline__ float q8_to_f(uint32_t wbiased, int j) {
+  return __uint_as_float(__byte_perm(wbiased, 0x4B000000u, 0x7540u + j)) - 8388736.f;
+}
+
+// Activation access: F32 rows staged in shared memory (fast path), or F16
+// rows in global memory.
+struct XSrc {
+  const float* xs;  // [B][K] F32 in shared memory, or null
+  const half* xg;   // [B][ldx] F16 in global memory
+  int ld;
+};
+
+// Staged rows keep each 32-element group in 36 floats: lanes own different
+// groups, and the 144-byte stride puts consecutive lanes 4 banks apart.
+__device__ __forceinline__ int xs_index(int k) { return (k >> 5) * 36 + (k & 31); }
+
+template <int B, bool XS>
+__device__ __forceinline__ void load_x8(const XSrc& x, int b, int k, float (&v)[8]) {
+  if (XS) {
+    const float* base = x.xs + (size_t)b * x.ld + xs_index(k);
+    const float4 a = *reinterpret_cast<const float4*>(base);
+    const float4 c = *reinterpret_cast<const float4*>(base + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(x.xg + (size_t)b * x.ld + k);
+    const half2* h = reinterpret_cast<const half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float2 f = __half22float2(h[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  }
+}
+
+template <int B, int NV, bool XS>
+__device__ __forceinline__ void row_use(const QTensor& w, const RowRaw<NV>& r, int g0, int groups, const XSrc& x,
+                                        float (&acc)[B]) {
+  if (w.kind == K_Q8_0) {
+#pragma unroll
+    for (int u = 0; u < NV / 2; u++) {
+      const int g = g0 + 32 * u;
+      if (g >= groups) break;
+      const float d = half_bits(r.sc[u]);
+      const uint32_t wd[8] = {r.v[2 * u].x ^ 0x80808080u,     r.v[2 * u].y ^ 0x80808080u,
+                              r.v[2 * u].z ^ 0x80808080u,     r.v[2 * u].w ^ 0x80808080u,
+                              r.v[2 * u + 1].x ^ 0x80808080u, r.v[2 * u + 1].y ^ 0x80808080u,
+                              r.v[2 * u + 1].z ^ 0x80808080u, r.v[2 * u + 1].w ^ 0x80808080u};
+      float part[B];
+#pragma unroll
+      for (int b = 0; b < B; b++) part[b] = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        uint4 u = __ldg(xp + c);
-        const half2* hp = reinterpret_cast<const half2*>(&u);
+        float wf[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) wf[j] = q8_to_f(wd[2 * c + j / 4], j % 4);
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+          float xv[8];
+          load_x8<B, XS>(x, b, g * 32 + c * 8, xv);
+#pragma unroll
+          for (int j = 0; j < 8; j++) part[b] = fmaf(wf[j], xv[j], part[b]);
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < B; b++) acc[b] = fmaf(d, part[b], acc[b]);
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < NV / 4; u++) {
+      const int g = g0 + 32 * u;
+      if (g >= groups) break;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        float wf[8];
+        const half2* h = reinterpret_cast<const half2*>(&r.v[4 * u + c]);
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-          float2 f = __half22float2(hp[e]);
+          const float2 f = __half22float2(h[e]);
+          wf[2 * e] = f.x;
+          wf[2 * e + 1] = f.y;
+        }
 #pragma unroll
-          for (int r = 0; r < ROWS; r++) {
-            acc[r][b] = fmaf(wv[r][c * 8 + 2 * e], f.x, acc[r][b]);
-            acc[r][b] = fmaf(wv[r][c * 8 + 2 * e + 1], f.y, acc[r][b]);
-          }
+        for (int b = 0; b < B; b++) {
+          float xv[8];
+          load_x8<B, XS>(x, b, g * 32 + c * 8, xv);
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[b] = fmaf(wf[j], xv[j], acc[b]);
         }
       }
     }
   }
-#pragma unroll
-  for (int r = 0; r < ROWS; r++)
-#pragma unroll
-    for (int b = 0; b < B; b++) {
-      float v = acc[r][b];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
-      acc[r][b] = v;
+}
+
+// Dot products of one row with the B activation rows: the first batch of
+// groups is already in `raw` (loaded before pdl_wait); block types without
+// a prefetch path decode through dq32.
+template <int B, int NV, bool FAST, bool XS>
+__device__ __forceinline__ void row_dot(const QTensor& w, int n, const XSrc& x, int lane, RowRaw<NV>& raw,
+                                        bool first_loaded, float (&acc)[B]) {
+  const int groups = w.cols / 32;
+  if (FAST || w.kind == K_Q8_0 || w.kind == K_F16) {
+    const int gpb = groups_per_batch(w.kind, NV);
+    const int step = 32 * (gpb > 0 ? gpb : 1);
+    for (int g0 = lane; g0 < groups; g0 += step) {
+      if (g0 != lane || !first_loaded) row_load<NV>(w, n, g0, groups, raw);
+      row_use<B, NV, XS>(w, raw, g0, groups, x, acc);
     }
-  if (lane == 0) {
+  } else {
+    for (int g = lane; g < groups; g += 32) {
+      float wf[32];
+      dq32(w, n, g * 32, wf);
 #pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-      if (n0 + r >= w.rows) break;
+      for (int c = 0; c < 4; c++)
 #pragma unroll
-      for (int b = 0; b < B; b++) {
-        float* dst = y + (size_t)b * ldy + n0 + r;
-        *dst = accumulate ? *dst + acc[r][b] : acc[r][b];
-      }
+        for (int b = 0; b < B; b++) {
+          float xv[8];
+          load_x8<B, XS>(x, b, g * 32 + c * 8, xv);
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[b] = fmaf(wf[c * 8 + j], xv[j], acc[b]);
+        }
     }
   }
 }
 
 template <int B>
-static cudaError_t gemv_b(const QTensor& w, const half* x, int ldx, float* y, int ldy, int acc, cudaStream_t st) {
-  constexpr int ROWS = B >= 16 ? 1 : 2;
-  const int warps = (w.rows + ROWS - 1) / ROWS;
-  gemv_kernel<B, ROWS><<<(warps * 32 + 255) / 256, 256, 0, st>>>(w, x, ldx, y, ldy, acc);
-  return cudaGetLastError();
+__device__ __forceinline__ void warp_sum(float (&acc)[B]) {
+#pragma unroll
+  for (int b = 0; b < B; b++) {
+    float v = acc[b];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+    acc[b] = v;
+  }
 }
 
-cudaError_t gemv(const QTensor& w, const half* x, int ldx, int nb, float* y, int ldy, int acc, cudaStream_t st) {
+// Builds the block's F32 activation rows in shared memory, once per block:
+// either x = rmsnorm(xres[b], norm_w, eps) from the F32 residual stream
+// (src/models/openthai/model.rs:84-94), or the F16 rows of p.x widened.
+template <int B>
+__device__ __forceinline__ void stage_x(const GemvPlan& p, int K, float* xs) {
+  __shared__ float red[8][B];
+  __shared__ float scale[B];
+  const int tid = threadIdx.x, lane = tid % 32, wb = tid / 32;
+  if (p.xres) {
+    float ss[B];
+#pragma unroll
+    for (int b = 0; b < B; b++) ss[b] = 0.f;
+    for (int k = tid * 4; k < K; k += blockDim.x * 4)
+#pragma unroll
+      for (int b = 0; b < B; b++) {
+        const float4 v = *reinterpret_cast<const float4*>(p.xres + (size_t)b * K + k);
+        ss[b] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+      float v = ss[b];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+      if (lane == 0) red[wb][b] = v;
+    }
+    __syncthreads();
+    if (tid < B) {
+      float t = 0.f;
+      for (int i = 0; i < (int)(blockDim.x / 32); i++) t += red[i][tid];
+      scale[tid] = 1.f / sqrtf(t / (float)K + p.eps);
+    }
+    __syncthreads();
+    for (int k = tid * 4; k < K; k += blockDim.x * 4) {
+      const float4 g = *reinterpret_cast<const float4*>(p.norm_w + k);
+#pragma unroll
+      for (int b = 0; b < B; b++) {
+        const float4 v = *reinterpret_cast<const float4*>(p.xres + (size_t)b * K + k);
+        const float sc = scale[b];
+        *reinterpret_cast<float4*>(xs + (size_t)b * (K / 32 * 36) + xs_index(k)) =
+            make_float4(v.x * sc * g.x, v.y * sc * g.y, v.z * sc * g.z, v.w * sc * g.w);
+      }
+    }
+  } else {
+    for (int k = tid * 8; k < K; k += blockDim.x * 8)
+#pragma unroll
+      for (int b = 0; b < B; b++) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p.x + (size_t)b * p.ldx + k);
+        const half2* h = reinterpret_cast<const half2*>(&u);
+        float4 lo, hi;
+        float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]), f2 = __half22float2(h[2]),
+               f3 = __half22float2(h[3]);
+        lo = make_float4(f0.x, f0.y, f1.x, f1.y);
+        hi = make_float4(f2.x, f2.y, f3.x, f3.y);
+        *reinterpret_cast<float4*>(xs + (size_t)b * (K / 32 * 36) + xs_index(k)) = lo;
+        *reinterpret_cast<float4*>(xs + (size_t)b * (K / 32 * 36) + xs_index(k + 4)) = hi;
+      }
+  }
+  __syncthreads();
+}
+
+constexpr size_t kGemvSmem = 96 * 1024;  // largest F32 activation stage per block
+
+// Persistent warps: warp w handles output rows w, w + W, ... two at a time
+// (or the gate and up rows of one FFN column in SwiGLU mode), so each lane
+// keeps several 16-byte weight loads in flight and the grid (sized to fill
+// the SMs) streams continuously.  The first weight loads are issued before
+// pdl_wait(): weights never depend on the previous kernel, so their latency
+// overlaps that kernel's tail.  In greedy mode (p.best) the rows are logits:
+// the block keeps the running (logit, row) maximum and merges it with one
+// atomicMax per batch row.
+template <int B, bool FAST, bool XS>
+__global__ void __launch_bounds__(256, (B <= 2 ? 3 : B <= 8 ? 2 : 1)) gemv2_kernel(const GemvPlan p) {
+  constexpr int NV = 4;  // slots per row batch: Q8_0 2 groups, F16 1 group
+  extern __shared__ uint4 gemv_smem[];
+  const int lane = threadIdx.x % 32;
+  const int W = gridDim.x * (blockDim.x / 32);
+  const int w0 = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int K = p.seg[0].w.cols;
+  // activations: XS = staged as F32 rows in shared memory (they fit), else F16 from global
+  constexpr bool staged = XS;
+  XSrc x{staged ? reinterpret_cast<const float*>(gemv_smem) : nullptr, p.x, staged ? K / 32 * 36 : p.ldx};
+  if (p.swiglu) {
+    const QTensor& wg = p.seg[0].w;
+    const QTensor& wu = p.swiglu == 2 ? p.seg[0].w : p.seg[1].w;
+    RowRaw<NV> rg, ru;
+    auto rows_of = [&](int r, int& ng, int& nu) {
+      ng = p.swiglu == 2 ? (r / 128) * 256 + r % 128 : r;
+      nu = p.swiglu == 2 ? ng + 128 : r;
+    };
+    if (w0 < p.rows) {
+      int ng, nu;
+      rows_of(w0, ng, nu);
+      row_load<NV>(wg, ng, lane, wg.cols / 32, rg);
+      row_load<NV>(wu, nu, lane, wu.cols / 32, ru);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (staged) stage_x<B>(p, K, reinterpret_cast<float*>(gemv_smem));
+    for (int r = w0; r < p.rows; r += W) {
+      int ng, nu;
+      rows_of(r, ng, nu);
+      float g[B], u[B];
+#pragma unroll
+      for (int b = 0; b < B; b++) g[b] = u[b] = 0.f;
+      if (r != w0) {
+        row_load<NV>(wg, ng, lane, wg.cols / 32, rg);
+        row_load<NV>(wu, nu, lane, wu.cols / 32, ru);
+      }
+      row_dot<B, NV, FAST, XS>(wg, ng, x, lane, rg, true, g);
+      row_dot<B, NV, FAST, XS>(wu, nu, x, lane, ru, true, u);
+      warp_sum<B>(g);
+      warp_sum<B>(u);
+      if (lane < B) {
+        float gv = 0.f, uv = 0.f;
+#pragma unroll
+        for (int b = 0; b < B; b++)
+          if (b == lane) {
+            gv = g[b];
+            uv = u[b];
+          }
+        p.act[(size_t)lane * p.ld_act + r] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
+      }
+    }
+    return;
+  }
+  auto locate = [&](int r, int& s, int& n) {
+    s = 0;
+    n = r;
+    if (p.nseg > 1 && n >= p.seg[0].w.rows) {
+      n -= p.seg[0].w.rows;
+      s = 1;
+      if (p.nseg > 2 && n >= p.seg[1].w.rows) {
+        n -= p.seg[1].w.rows;
+        s = 2;
+      }
+    }
+  };
+  auto mat = [&](int s) -> const QTensor& { return s == 0 ? p.seg[0].w : s == 1 ? p.seg[1].w : p.seg[2].w; };
+  RowRaw<NV> ra, rb;
+  {
+    int s, n;
+    if (w0 < p.rows) {
+      locate(w0, s, n);
+      row_load<NV>(mat(s), n, lane, mat(s).cols / 32, ra);
+    }
+    if (w0 + W < p.rows) {
+      locate(w0 + W, s, n);
+      row_load<NV>(mat(s), n, lane, mat(s).cols / 32, rb);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (staged) stage_x<B>(p, K, reinterpret_cast<float*>(gemv_smem));
+  unsigned long long best[B];
+#pragma unroll
+  for (int b = 0; b < B; b++) best[b] = 0ull;
+  auto finish = [&](int r, int s, int n, float (&acc)[B]) {
+    warp_sum<B>(acc);
+    if (p.best) {
+#pragma unroll
+      for (int b = 0; b < B; b++) {
+        const unsigned long long k = pack_logit(acc[b], r);
+        best[b] = k > best[b] ? k : best[b];
+      }
+    } else if (lane < B) {
+      float v = 0.f;
+#pragma unroll
+      for (int b = 0; b < B; b++)
+        if (b == lane) v = acc[b];
+      float* y = s == 0 ? p.seg[0].y : s == 1 ? p.seg[1].y : p.seg[2].y;
+      const int ldy = s == 0 ? p.seg[0].ldy : s == 1 ? p.seg[1].ldy : p.seg[2].ldy;
+      const int accf = s == 0 ? p.seg[0].acc : s == 1 ? p.seg[1].acc : p.seg[2].acc;
+      float* dst = y + (size_t)lane * ldy + n;
+      *dst = accf ? *dst + v : v;
+    }
+  };
+  for (int r = w0; r < p.rows; r += 2 * W) {
+    const int r2 = r + W;
+    int sa, na, sb = 0, nb2 = 0;
+    locate(r, sa, na);
+    if (r2 < p.rows) locate(r2, sb, nb2);
+    if (r != w0) {  // both rows' first batches are issued before either is used
+      row_load<NV>(mat(sa), na, lane, mat(sa).cols / 32, ra);
+      if (r2 < p.rows) row_load<NV>(mat(sb), nb2, lane, mat(sb).cols / 32, rb);
+    }
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; b++) acc[b] = 0.f;
+    row_dot<B, NV, FAST, XS>(mat(sa), na, x, lane, ra, true, acc);
+    finish(r, sa, na, acc);
+    if (r2 < p.rows) {
+#pragma unroll
+      for (int b = 0; b < B; b++) acc[b] = 0.f;
+      row_dot<B, NV, FAST, XS>(mat(sb), nb2, x, lane, rb, true, acc);
+      finish(r2, sb, nb2, acc);
+    }
+  }
+  if (p.best) {
+    __shared__ unsigned long long blk[8][B];
+    const int wb = threadIdx.x / 32;
+    if (lane == 0)
+#pragma unroll
+      for (int b = 0; b < B; b++) blk[wb][b] = best[b];
+    __syncthreads();
+    if (threadIdx.x < B) {
+      unsigned long long k = 0ull;
+      for (int i = 0; i < (int)(blockDim.x / 32); i++) k = blk[i][threadIdx.x] > k ? blk[i][threadIdx.x] : k;
+      atomicMax(p.best + threadIdx.x, k);
+    }
+  }
+}
+
+template <int B, bool FAST, bool XS>
+static cudaError_t gemv2_bx(const GemvPlan& p, dim3 grid, size_t smem, cudaStream_t st) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv2_kernel<B, FAST, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
+  }
+  return launch_k(gemv2_kernel<B, FAST, XS>, grid, dim3(256), smem, st, true, p);
+}
+
+template <int B, bool FAST>
+static cudaError_t gemv2_b(const GemvPlan& p, dim3 grid, size_t smem, cudaStream_t st) {
+  return smem ? gemv2_bx<B, FAST, true>(p, grid, smem, st) : gemv2_bx<B, FAST, false>(p, grid, smem, st);
+}
+
+template <bool FAST>
+static cudaError_t gemv2_k(const GemvPlan& p, int nb, int num_sms, cudaStream_t st) {
+  // enough warps to fill every SM at the kernel's occupancy, at most one per row
+  const int per_sm = nb <= 2 ? 3 : nb <= 8 ? 2 : 1;
+  const int blocks = std::min((p.rows + 7) / 8, num_sms * per_sm);
+  const dim3 grid((unsigned)std::max(blocks, 1));
+  const size_t need = (size_t)nb * (p.seg[0].w.cols / 32 * 36) * 4;
+  if (p.xres && need > kGemvSmem) return cudaErrorInvalidValue;
+  const size_t smem = need <= kGemvSmem ? need : 0;
   switch (nb) {
-    case 1: return gemv_b<1>(w, x, ldx, y, ldy, acc, st);
-    case 2: return gemv_b<2>(w, x, ldx, y, ldy, acc, st);
-    case 4: return gemv_b<4>(w, x, ldx, y, ldy, acc, st);
-    case 8: return gemv_b<8>(w, x, ldx, y, ldy, acc, st);
-    case 16: return gemv_b<16>(w, x, ldx, y, ldy, acc, st);
+    case 1: return gemv2_b<1, FAST>(p, grid, smem, st);
+    case 2: return gemv2_b<2, FAST>(p, grid, smem, st);
+    case 4: return gemv2_b<4, FAST>(p, grid, smem, st);
+    case 8: return gemv2_b<8, FAST>(p, grid, smem, st);
+    case 16: return gemv2_b<16, FAST>(p, grid, smem, st);
   }
   return cudaErrorInvalidValue;
+}
+
+static cudaError_t gemv2(const GemvPlan& p, int nb, int num_sms, cudaStream_t st) {
+  bool fast = true;
+  for (int i = 0; i < (p.nseg > 0 ? p.nseg : 1); i++)
+    fast &= p.seg[i].w.kind == K_Q8_0 || p.seg[i].w.kind == K_F16;
+  return fast ? gemv2_k<true>(p, nb, num_sms, st) : gemv2_k<false>(p, nb, num_sms, st);
 }
 
 // ---------------------------------------------------------------- small kernels
@@ -111,6 +504,8 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, const float* _
                                    int hd, int kvh, const int* __restrict__ pos, const int* __restrict__ slot,
                                    const float2* __restrict__ rope, half* __restrict__ q, half* __restrict__ kc,
                                    half* __restrict__ vc) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const int n = qd + 2 * kd, half_hd = hd / 2;
   const float* row = qkv + (size_t)b * n;
@@ -147,230 +542,344 @@ __global__ void rope_append_kernel(const float* __restrict__ qkv, const float* _
   }
 }
 
-// act[b][f] = silu(gate) * up (src/models/openthai/model.rs:225-230); gate/up
-// either interleaved per 128 columns in one [B][2*ffn] buffer or separate.
-__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, int ffn, int interleaved,
-                              half* __restrict__ act) {
-  const int b = blockIdx.y;
-  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < ffn; f += gridDim.x * blockDim.x) {
-    float gv, uv;
-    if (interleaved) {
-      const size_t base = (size_t)b * 2 * ffn + (size_t)(f / 128) * 256 + f % 128;
-      gv = g[base];
-      uv = g[base + 128];
-    } else {
-      gv = g[(size_t)b * ffn + f];
-      uv = u[(size_t)b * ffn + f];
-    }
-    act[(size_t)b * ffn + f] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
-  }
-}
-
-// Greedy token: argmax over the vocabulary, ties to the lowest id.
-__global__ void argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ out) {
-  __shared__ float sv[32];
-  __shared__ int si[32];
+// Greedy token from full-vocabulary logits (large batches, where the head
+// runs on the tensor-core GEMM): best[b] = max over ids of pack_logit.
+__global__ void argmax_best_kernel(const float* __restrict__ logits, int V, unsigned long long* __restrict__ best) {
+  __shared__ unsigned long long sk[32];
+  pdl_wait();
+  pdl_trigger();
   const float* x = logits + (size_t)blockIdx.x * V;
-  float best = -FLT_MAX;
-  int bi = 0x7fffffff;
+  unsigned long long k = 0ull;
   for (int c = threadIdx.x; c < V; c += blockDim.x) {
-    const float v = x[c];
-    if (v > best || (v == best && c < bi)) {
-      best = v;
-      bi = c;
-    }
+    const unsigned long long kc = pack_logit(x[c], c);
+    k = kc > k ? kc : k;
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffff, best, o);
-    const int oi = __shfl_xor_sync(0xffffffff, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
+    const unsigned long long ok = __shfl_xor_sync(0xffffffff, k, o);
+    k = ok > k ? ok : k;
   }
-  if (threadIdx.x % 32 == 0) {
-    sv[threadIdx.x / 32] = best;
-    si[threadIdx.x / 32] = bi;
-  }
+  if (threadIdx.x % 32 == 0) sk[threadIdx.x / 32] = k;
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)blockDim.x / 32; w++)
-      if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
-        best = sv[w];
-        bi = si[w];
-      }
-    out[blockIdx.x] = bi;
+    for (int w = 1; w < (int)blockDim.x / 32; w++) k = sk[w] > k ? sk[w] : k;
+    best[blockIdx.x] = k;
   }
 }
-
-__global__ void f32_to_f16_kernel(const float* __restrict__ x, size_t n, half* __restrict__ y) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    y[i] = __float2half_rn(x[i]);
-}
-
-// ---------------------------------------------------------------- decode attention
 
 struct DecSeq {
   int table_off, n_keys;
 };
 
-// One CTA per (sequence, kv head, key split); one warp per query head of the
-// GQA group.  Lanes own keys for the scores and head-dim slices for P.V.
-// Writes the split's (max, sum, unnormalised output) for the combine step.
-template <int HD>
-__global__ void attn_decode_kernel(const half* __restrict__ q, const half* __restrict__ kc, const half* __restrict__ vc,
-                                   const int* __restrict__ tables, const DecSeq* __restrict__ seqs, int H, int KV,
-                                   float scale_log2, int split_len, int splits, float* __restrict__ part) {
-  const int b = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
-  const int G = H / KV;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  if (warp >= G) return;
-  const int h = kvh * G + warp;
-  const DecSeq s = seqs[b];
-  const int k0 = sp * split_len, k1 = min(s.n_keys, k0 + split_len);
-  constexpr int DPL = HD / 32;  // head dims per lane
-  float qv[HD];
-  const half* qp = q + ((size_t)b * H + h) * HD;
-#pragma unroll
-  for (int i = 0; i < HD; i += 8) {
-    uint4 u = *reinterpret_cast<const uint4*>(qp + i);
-    const half2* hp = reinterpret_cast<const half2*>(&u);
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      float2 f = __half22float2(hp[e]);
-      qv[i + 2 * e] = f.x;
-      qv[i + 2 * e + 1] = f.y;
-    }
+// Start of decode step s = ++counter: the greedy token of the previous step
+// (or of the prefill) is taken from best[], recorded in toks[s-1] and fed to
+// this step, best[] is cleared for this step's head, and the step's
+// position, KV slot and key count move to fixed device addresses.
+__global__ void advance_kernel(int* counter, unsigned long long* __restrict__ best, int* __restrict__ toks,
+                               const int* __restrict__ pos_all, const int* __restrict__ slot_all,
+                               const DecSeq* __restrict__ seq_all, int nb, int* __restrict__ cur_tok,
+                               int* __restrict__ cur_pos, int* __restrict__ cur_slot, DecSeq* __restrict__ cur_seq) {
+  __shared__ int s;
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) s = *counter + 1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    const int tok = unpack_row(best[i]);
+    toks[(size_t)(s - 1) * nb + i] = tok;
+    cur_tok[i] = tok;
+    best[i] = 0ull;
+    cur_pos[i] = pos_all[(size_t)s * nb + i];
+    cur_slot[i] = slot_all[(size_t)s * nb + i];
+    cur_seq[i] = seq_all[(size_t)s * nb + i];
   }
-  float m = -INFINITY, l = 0.f, acc[DPL];
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = s;
+}
+
+// Records the last step's greedy tokens.
+__global__ void finalize_kernel(const unsigned long long* __restrict__ best, int* __restrict__ toks, int row, int nb) {
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) toks[(size_t)row * nb + i] = unpack_row(best[i]);
+}
+
+// ---------------------------------------------------------------- decode attention
+
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+// One CTA (4 warps) per (sequence, kv head, split of whole pages).  Each
+// 64-token K/V page is staged in shared memory with cp.async (double
+// buffered; K rows padded to 16-byte-aligned, bank-conflict-free strides);
+// all threads score the G query heads of the GQA group against the page,
+// then each warp updates the online softmax and P.V of its heads.  Writes
+// the split's (max, sum, unnormalised output) for attn_combine_kernel.
+template <int HD, int G>
+__global__ void __launch_bounds__(128) attn_dec2_kernel(const half* __restrict__ q, const half* __restrict__ kc,
+                                                        const half* __restrict__ vc, const int* __restrict__ tables,
+                                                        const DecSeq* __restrict__ seqs, int KV, float scale_log2,
+                                                        int split_pages, int splits, float* __restrict__ part) {
+  constexpr int KP = HD + 8, DPL = HD / 32, HPW = (G + 3) / 4;
+  extern __shared__ uint4 dsm[];
+  half* sK = reinterpret_cast<half*>(dsm);                 // [2][64][KP]
+  half* sV = sK + 2 * 64 * KP;                             // [2][64][HD]
+  float* sQ = reinterpret_cast<float*>(sV + 2 * 64 * HD);  // [G][HD]
+  float* sP = sQ + G * HD;                                 // [G][64]
+  const int b = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
+  const int H = KV * G;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  pdl_wait();
+  pdl_trigger();
+  const DecSeq s = seqs[b];
+  const int n_pages = (s.n_keys + PAGE - 1) / PAGE;
+  const int p0 = sp * split_pages, p1 = min(n_pages, p0 + split_pages);
+  for (int i = tid; i < G * HD; i += 128) sQ[i] = __half2float(q[((size_t)b * H + kvh * G) * HD + i]);
+  float m[HPW], l[HPW], acc[HPW][DPL];
 #pragma unroll
-  for (int i = 0; i < DPL; i++) acc[i] = 0.f;
-  for (int j0 = k0; j0 < k1; j0 += 32) {
-    const int j = j0 + lane;
-    float sc = -INFINITY;
-    if (j < k1) {
-      const int page = tables[s.table_off + j / PAGE];
-      const half* kp = kc + (((size_t)page * KV + kvh) * PAGE + j % PAGE) * HD;
+  for (int hh = 0; hh < HPW; hh++) {
+    m[hh] = -INFINITY;
+    l[hh] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) acc[hh][d] = 0.f;
+  }
+  auto load = [&](int p, int buf) {
+    const int page = tables[s.table_off + p];
+    const half* kp = kc + ((size_t)page * KV + kvh) * PAGE * HD;
+    const half* vp = vc + ((size_t)page * KV + kvh) * PAGE * HD;
+    for (int i = tid; i < PAGE * HD / 8; i += 128) {
+      const int r = i / (HD / 8), c = i % (HD / 8);
+      cp16(sK + (size_t)buf * 64 * KP + r * KP + c * 8, kp + r * HD + c * 8);
+      cp16(sV + (size_t)buf * 64 * HD + r * HD + c * 8, vp + r * HD + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (p0 < p1) load(p0, 0);
+  for (int p = p0; p < p1; p++) {
+    const int buf = (p - p0) & 1;
+    if (p + 1 < p1) {
+      load(p + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const half* bK = sK + (size_t)buf * 64 * KP;
+    const half* bV = sV + (size_t)buf * 64 * HD;
+    for (int i = tid; i < G * 64; i += 128) {
+      const int g = i / 64, j = i % 64;
+      const half* kr = bK + j * KP;
+      const float* qg = sQ + g * HD;
       float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < HD; i += 8) {
-        uint4 u = __ldg(reinterpret_cast<const uint4*>(kp + i));
-        const half2* hp = reinterpret_cast<const half2*>(&u);
+      for (int c = 0; c < HD; c += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(kr + c);
+        const half2* h = reinterpret_cast<const half2*>(&u);
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-          float2 f = __half22float2(hp[e]);
-          dot = fmaf(qv[i + 2 * e], f.x, dot);
-          dot = fmaf(qv[i + 2 * e + 1], f.y, dot);
+          const float2 f = __half22float2(h[e]);
+          dot = fmaf(qg[c + 2 * e], f.x, dot);
+          dot = fmaf(qg[c + 2 * e + 1], f.y, dot);
         }
       }
-      sc = dot * scale_log2;
+      sP[g * 64 + j] = (p * PAGE + j) < s.n_keys ? dot * scale_log2 : -INFINITY;
     }
-    float mx = sc;
+    __syncthreads();
 #pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
-    const float mn = fmaxf(m, mx);
-    const float corr = exp2f(m - mn);
-    const float p = j < k1 ? exp2f(sc - mn) : 0.f;
-    float ps = p;
+    for (int hh = 0; hh < HPW; hh++) {
+      const int g = warp + 4 * hh;
+      if (g >= G) break;
+      const float s0 = sP[g * 64 + lane], s1 = sP[g * 64 + 32 + lane];
+      float mx = fmaxf(s0, s1);
 #pragma unroll
-    for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xffffffff, ps, o);
-    l = l * corr + ps;
-    m = mn;
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
+      const float mn = fmaxf(m[hh], mx);
+      const float corr = mn == -INFINITY ? 1.f : exp2f(m[hh] - mn);
+      const float e0 = s0 == -INFINITY ? 0.f : exp2f(s0 - mn);
+      const float e1 = s1 == -INFINITY ? 0.f : exp2f(s1 - mn);
+      float sum = e0 + e1;
 #pragma unroll
-    for (int i = 0; i < DPL; i++) acc[i] *= corr;
-    const int cnt = min(32, k1 - j0);
-    for (int jj = 0; jj < cnt; jj++) {
-      const float pj = __shfl_sync(0xffffffff, p, jj);
-      const int key = j0 + jj;
-      const int page = tables[s.table_off + key / PAGE];
-      const half* vp = vc + (((size_t)page * KV + kvh) * PAGE + key % PAGE) * HD + lane * DPL;
-      if constexpr (DPL == 2) {
-        const float2 f = __half22float2(*reinterpret_cast<const half2*>(vp));
-        acc[0] = fmaf(pj, f.x, acc[0]);
-        acc[1] = fmaf(pj, f.y, acc[1]);
-      } else {
-        const uint2 u = *reinterpret_cast<const uint2*>(vp);
-        const half2* hp = reinterpret_cast<const half2*>(&u);
-        const float2 f0 = __half22float2(hp[0]), f1 = __half22float2(hp[1]);
-        acc[0] = fmaf(pj, f0.x, acc[0]);
-        acc[1] = fmaf(pj, f0.y, acc[1]);
-        acc[2] = fmaf(pj, f1.x, acc[2]);
-        acc[3] = fmaf(pj, f1.y, acc[3]);
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
+      l[hh] = l[hh] * corr + sum;
+      m[hh] = mn;
+#pragma unroll
+      for (int d = 0; d < DPL; d++) acc[hh][d] *= corr;
+#pragma unroll 16
+      for (int j = 0; j < 64; j++) {
+        const float pj = __shfl_sync(0xffffffff, j < 32 ? e0 : e1, j & 31);
+        const half* vr = bV + j * HD + lane * DPL;
+        if constexpr (DPL == 2) {
+          const float2 f = __half22float2(*reinterpret_cast<const half2*>(vr));
+          acc[hh][0] = fmaf(pj, f.x, acc[hh][0]);
+          acc[hh][1] = fmaf(pj, f.y, acc[hh][1]);
+        } else {
+          const uint2 u = *reinterpret_cast<const uint2*>(vr);
+          const half2* h2 = reinterpret_cast<const half2*>(&u);
+          const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+          acc[hh][0] = fmaf(pj, f0.x, acc[hh][0]);
+          acc[hh][1] = fmaf(pj, f0.y, acc[hh][1]);
+          acc[hh][2] = fmaf(pj, f1.x, acc[hh][2]);
+          acc[hh][3] = fmaf(pj, f1.y, acc[hh][3]);
+        }
       }
     }
-  }
-  float* dst = part + (((size_t)b * H + h) * splits + sp) * (HD + 2);
-  if (lane == 0) {
-    dst[0] = m;
-    dst[1] = l;
+    __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < DPL; i++) dst[2 + lane * DPL + i] = acc[i];
+  for (int hh = 0; hh < HPW; hh++) {
+    const int g = warp + 4 * hh;
+    if (g >= G) break;
+    float* dst = part + (((size_t)b * H + kvh * G + g) * splits + sp) * (HD + 2);
+    if (lane == 0) {
+      dst[0] = m[hh];
+      dst[1] = l[hh];
+    }
+#pragma unroll
+    for (int d = 0; d < DPL; d++) dst[2 + lane * DPL + d] = acc[hh][d];
+  }
 }
 
 // Merges the key splits: o = sum_s 2^(m_s - M) acc_s / sum_s 2^(m_s - M) l_s.
+// The split weights are computed once into shared memory; then the threads
+// (dims x split subsets) sum independent, coalesced loads.
 __global__ void attn_combine_kernel(const float* __restrict__ part, int H, int HD, int splits, half* __restrict__ o) {
+  extern __shared__ float cs[];  // [splits] weights, then [blockDim] partial sums
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x, h = blockIdx.y;
   const float* p = part + ((size_t)b * H + h) * splits * (HD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < splits; s++) M = fmaxf(M, p[s * (HD + 2)]);
-  float L = 0.f;
-  for (int s = 0; s < splits; s++) {
-    const float ms = p[s * (HD + 2)];
-    if (ms != -INFINITY) L += exp2f(ms - M) * p[s * (HD + 2) + 1];
+  float mx = -INFINITY;
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) mx = fmaxf(mx, p[(size_t)s * (HD + 2)]);
+#pragma unroll
+  for (int o2 = 16; o2; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o2));
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = red[0];
+    for (int w = 1; w < (int)blockDim.x / 32; w++) m = fmaxf(m, red[w]);
+    red[0] = m;
   }
-  for (int dd = threadIdx.x; dd < HD; dd += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < splits; s++) {
-      const float ms = p[s * (HD + 2)];
-      if (ms != -INFINITY) acc += exp2f(ms - M) * p[s * (HD + 2) + 2 + dd];
-    }
-    o[((size_t)b * H + h) * HD + dd] = __float2half_rn(acc / L);
+  __syncthreads();
+  const float M = red[0];
+  __syncthreads();
+  float l = 0.f;
+  for (int s = threadIdx.x; s < splits; s += blockDim.x) {
+    const float ms = p[(size_t)s * (HD + 2)];
+    const float wgt = ms == -INFINITY ? 0.f : exp2f(ms - M);
+    cs[s] = wgt;
+    l += wgt * p[(size_t)s * (HD + 2) + 1];
+  }
+#pragma unroll
+  for (int o2 = 16; o2; o2 >>= 1) l += __shfl_xor_sync(0xffffffff, l, o2);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = l;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)blockDim.x / 32; w++) t += red[w];
+    red[0] = t;
+  }
+  __syncthreads();
+  const float inv = 1.f / red[0];
+  const int ways = blockDim.x / HD;  // threads per dimension
+  const int dd = threadIdx.x % HD, part_i = threadIdx.x / HD;
+  float acc = 0.f;
+  if (part_i < ways) {
+#pragma unroll 8
+    for (int s = part_i; s < splits; s += ways) acc += cs[s] * p[(size_t)s * (HD + 2) + 2 + dd];
+  }
+  float* ps = cs + splits;
+  ps[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x < HD) {
+    float t = 0.f;
+    for (int i = 0; i < ways; i++) t += ps[i * HD + threadIdx.x];
+    o[((size_t)b * H + h) * HD + threadIdx.x] = __float2half_rn(t * inv);
   }
 }
 
 // ---------------------------------------------------------------- host
 
-static int decode_attention(Model& m, Replica& r, int nb, const half* q, const half* kc, const half* vc,
-                            const DecSeq* seqs, int max_keys, half* out) {
-  const Config& c = m.cfg;
-  int splits = std::max(1, (2 * r.num_sms * 4 + nb * c.KV - 1) / (nb * c.KV));
-  const int max_splits = (max_keys + PAGE - 1) / PAGE;
-  splits = std::min(splits, max_splits);
-  int split_len = (max_keys + splits - 1) / splits;
-  split_len = (split_len + 31) / 32 * 32;
-  splits = (max_keys + split_len - 1) / split_len;
-  const size_t part_elems = (size_t)nb * c.H * splits * (c.hd + 2);
-  if (int rc = r.dpart.ensure(part_elems * 4)) return rc;
-  const float scale_log2 = (1.f / sqrtf((float)c.hd)) * 1.4426950408889634f;
-  const int G = c.H / c.KV;
-  dim3 grid(nb, c.KV, splits);
-  {
-    cudaEvent_t a;
-    prof_begin(r, P_ATTN_DEC, &a);
-    r.launches += 2;
-    if (c.hd == 64)
-      attn_decode_kernel<64><<<grid, 32 * G, 0, r.stream>>>(q, kc, vc, r.tables.as<int>(), seqs, c.H,
-                                                          c.KV, scale_log2, split_len, splits, r.dpart.as<float>());
-    else
-      attn_decode_kernel<128><<<grid, 32 * G, 0, r.stream>>>(q, kc, vc, r.tables.as<int>(), seqs, c.H,
-                                                           c.KV, scale_log2, split_len, splits, r.dpart.as<float>());
-    LAYA_CK(cudaGetLastError());
-    attn_combine_kernel<<<dim3(nb, c.H), 128, 0, r.stream>>>(r.dpart.as<float>(), c.H, c.hd, splits, out);
-    LAYA_CK(cudaGetLastError());
-    prof_end(r, P_ATTN_DEC, a);
+struct AttnShape {
+  int splits, split_pages;
+};
+
+static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_keys) {
+  const int pages = (max_keys + PAGE - 1) / PAGE;
+  int splits = std::max(1, (4 * r.num_sms + nb * c.KV - 1) / (nb * c.KV));
+  splits = std::min(splits, pages);
+  const int split_pages = (pages + splits - 1) / splits;
+  return {(pages + split_pages - 1) / split_pages, split_pages};
+}
+
+template <int HD, int G>
+static cudaError_t launch_dec2(dim3 grid, cudaStream_t st, const half* q, const half* kc, const half* vc,
+                               const int* tables, const DecSeq* seqs, int KV, float sl2, int split_pages, int splits,
+                               float* part) {
+  const int smem = (2 * 64 * (HD + 8) + 2 * 64 * HD) * 2 + (G * HD + G * 64) * 4;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_dec2_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
   }
+  return launch_k(attn_dec2_kernel<HD, G>, grid, dim3(128), smem, st, true, q, kc, vc, tables, seqs, KV, sl2,
+                  split_pages, splits, part);
+}
+
+static int decode_attention(Model& m, Replica& r, int nb, const half* q, const half* kc, const half* vc,
+                            const DecSeq* seqs, const AttnShape& sh, half* out) {
+  const Config& c = m.cfg;
+  const float sl2 = (1.f / sqrtf((float)c.hd)) * 1.4426950408889634f;
+  const int G = c.H / c.KV;
+  const dim3 grid(nb, c.KV, sh.splits);
+  cudaEvent_t a;
+  prof_begin(r, P_ATTN_DEC, &a);
+  r.launches += 2;
+  cudaError_t e = cudaErrorNotSupported;
+  const int* tb = r.tables.as<int>();
+  float* part = r.dpart.as<float>();
+#define LAYA_DEC2(HDV, GV)                                                                                         \
+  if (c.hd == HDV && G == GV)                                                                                      \
+    e = launch_dec2<HDV, GV>(grid, r.stream, q, kc, vc, tb, seqs, c.KV, sl2, sh.split_pages, sh.splits, part);
+  LAYA_DEC2(64, 1)
+  LAYA_DEC2(64, 2)
+  LAYA_DEC2(64, 4)
+  LAYA_DEC2(64, 8)
+  LAYA_DEC2(128, 1)
+  LAYA_DEC2(128, 2)
+  LAYA_DEC2(128, 4)
+  LAYA_DEC2(128, 7)
+  LAYA_DEC2(128, 8)
+#undef LAYA_DEC2
+  if (e == cudaErrorNotSupported) return fail(LAYA_E_INVALID, "unsupported head grouping for decode");
+  if (e != cudaSuccess) return cuda_fail(e, "attn_dec2_kernel");
+  const int cthreads = c.hd <= 64 ? 256 : 256;
+  LAYA_CK(launch_k(attn_combine_kernel, dim3(nb, c.H), dim3(cthreads), (size_t)(sh.splits + cthreads) * 4, r.stream,
+                   true, (const float*)part, c.H, c.hd, sh.splits, out));
+  prof_end(r, P_ATTN_DEC, a);
   return 0;
 }
 
-static int run_gemv(Replica& r, const QTensor& w, const half* x, int ldx, int nb, float* y, int ldy, int acc) {
+static int run_gemv(Replica& r, const GemvPlan& p, int nb) {
   cudaEvent_t a;
   prof_begin(r, P_GEMV, &a);
   r.launches++;
-  LAYA_CK(gemv(w, x, ldx, nb, y, ldy, acc, r.stream));
+  LAYA_CK(gemv2(p, nb, r.num_sms, r.stream));
   prof_end(r, P_GEMV, a);
   return 0;
+}
+
+static GemvPlan plan1(const QTensor& w, const half* x, int ldx, float* y, int ldy, int acc) {
+  GemvPlan p{};
+  p.seg[0] = {w, y, ldy, acc};
+  p.nseg = 1;
+  p.rows = w.rows;
+  p.x = x;
+  p.ldx = ldx;
+  return p;
 }
 
 // Batches above this size run the linear layers on the tcgen05 GEMM.
@@ -378,20 +887,32 @@ static constexpr int kGemvMaxBatch = 16;
 
 static int pad_batch(int nb) { return nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : nb <= 8 ? 8 : 16; }
 
-// One decode step for nb sequences: tokens tok_in, positions pos, KV slots
-// slot; writes the greedy tokens to tok_out.  Everything stays on the device,
-// so consecutive steps run back to back.
-static int decode_step(Model& m, Replica& r, int nb, const int* tok_in, const int* pos, const int* slot,
-                       const DecSeq* seqs, int max_keys, int* tok_out) {
+// Fixed device addresses of the per-step inputs.
+struct StepIO {
+  int* counter;
+  unsigned long long* best;  // [nb] packed (logit, id) maxima of the current step
+  int* toks;  // [steps][nb] greedy tokens
+  const int *pos_all, *slot_all;
+  const DecSeq* seq_all;
+  int *cur_tok, *cur_pos, *cur_slot;
+  DecSeq* cur_seq;
+};
+
+// One decode step for nb sequences; every pointer it uses is fixed, so the
+// launch sequence can be captured once and replayed.
+static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const AttnShape& sh) {
   const Config& c = m.cfg;
   const int qd = c.H * c.hd, kd = c.KV * c.hd, d = c.d, ffn = c.ffn;
   cudaStream_t st = r.stream;
   const bool small = nb <= kGemvMaxBatch;
   const int nbp = small ? pad_batch(nb) : nb;  // GEMV batch (padded rows are zero)
   int rc;
+  r.launches++;
+  LAYA_CK(launch_k(advance_kernel, dim3(1), dim3(256), 0, st, true, io.counter, io.best, io.toks, io.pos_all,
+                   io.slot_all, io.seq_all, nb, io.cur_tok, io.cur_pos, io.cur_slot, io.cur_seq));
   float* x = r.x.as<float>();
   r.launches++;
-  LAYA_CK(rows_f32(r.embd, tok_in, nb, x, st));
+  LAYA_CK(rows_f32(r.embd, io.cur_tok, nb, x, st, true));
   half* h = r.h.as<half>();
   float* f = r.dlogits.as<float>();  // F32 scratch for GEMV outputs
   const size_t layer_elems = (size_t)r.kv_pages * c.KV * PAGE * c.hd;
@@ -415,23 +936,30 @@ static int decode_step(Model& m, Replica& r, int nb, const int* tok_in, const in
     const Layer& L = r.layers[l];
     half* kcl = r.kc.as<half>() + l * layer_elems;
     half* vcl = r.vc.as<half>() + l * layer_elems;
-    r.launches++;
-    LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
+    if (!small) {
+      r.launches++;
+      LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
+    }
     if (small) {
+      GemvPlan p{};
       if (L.wqkv16) {
         QTensor fused = L.wq;
         fused.rows = qd + 2 * kd;
-        if ((rc = run_gemv(r, fused, h, d, nbp, f, qd + 2 * kd, 0))) return rc;
+        p = plan1(fused, h, d, f, qd + 2 * kd, 0);
       } else {
-        if ((rc = run_gemv(r, L.wq, h, d, nbp, f, qd + 2 * kd, 0)) ||
-            (rc = run_gemv(r, L.wk, h, d, nbp, f + qd, qd + 2 * kd, 0)) ||
-            (rc = run_gemv(r, L.wv, h, d, nbp, f + qd + kd, qd + 2 * kd, 0)))
-          return rc;
+        p.seg[0] = {L.wq, f, qd + 2 * kd, 0};
+        p.seg[1] = {L.wk, f + qd, qd + 2 * kd, 0};
+        p.seg[2] = {L.wv, f + qd + kd, qd + 2 * kd, 0};
+        p.nseg = 3;
+        p.rows = qd + 2 * kd;
       }
+      p.xres = x;  // RMSNorm fused into the GEMV (padded batch rows of x are zero)
+      p.norm_w = L.attn_norm;
+      p.eps = c.eps;
+      if ((rc = run_gemv(r, p, nbp))) return rc;
       r.launches++;
-      rope_append_kernel<<<nb, 256, 0, st>>>(f, L.bqkv, qd, kd, c.hd, c.KV, pos, slot, r.rope, r.qb.as<half>(), kcl,
-                                             vcl);
-      LAYA_CK(cudaGetLastError());
+      LAYA_CK(launch_k(rope_append_kernel, dim3(nb), dim3(256), 0, st, true, (const float*)f, L.bqkv, qd, kd, c.hd,
+                       c.KV, (const int*)io.cur_pos, (const int*)io.cur_slot, r.rope, r.qb.as<half>(), kcl, vcl));
     } else {
       const half* wqkv = L.wqkv16;
       if (!wqkv) {
@@ -452,17 +980,17 @@ static int decode_step(Model& m, Replica& r, int nb, const int* tok_in, const in
       a.kd = kd;
       a.hd = c.hd;
       a.kvh = c.KV;
-      a.pos = pos;
-      a.slot = slot;
+      a.pos = io.cur_pos;
+      a.slot = io.cur_slot;
       a.rope = r.rope;
       a.kcache = kcl;
       a.vcache = vcl;
       a.page_size = PAGE;
       if ((rc = gemm_d(P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
     }
-    if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, seqs, max_keys, r.att.as<half>()))) return rc;
+    if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, io.cur_seq, sh, r.att.as<half>()))) return rc;
     if (small) {
-      if ((rc = run_gemv(r, L.wo, r.att.as<half>(), qd, nbp, x, d, 1))) return rc;
+      if ((rc = run_gemv(r, plan1(L.wo, r.att.as<half>(), qd, x, d, 1), nbp))) return rc;
     } else {
       const half* wo = L.wo16;
       if (!wo) {
@@ -477,22 +1005,30 @@ static int decode_step(Model& m, Replica& r, int nb, const int* tok_in, const in
       b.ldo = d;
       if ((rc = gemm_d(P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
     }
-    r.launches++;
-    LAYA_CK(rmsnorm(x, nullptr, nb, L.ffn_norm, d, c.eps, h, nullptr, st));
-    if (small) {
+    if (!small) {
       r.launches++;
+      LAYA_CK(rmsnorm(x, nullptr, nb, L.ffn_norm, d, c.eps, h, nullptr, st));
+    }
+    if (small) {
+      GemvPlan p{};
+      p.xres = x;
+      p.norm_w = L.ffn_norm;
+      p.eps = c.eps;
+      p.rows = ffn;
+      p.act = r.act.as<half>();
+      p.ld_act = ffn;
       if (L.wgu16) {
-        if ((rc = run_gemv(r, L.wg, h, d, nbp, f, 2 * ffn, 0))) return rc;
-        swiglu_kernel<<<dim3((ffn + 255) / 256, nb), 256, 0, st>>>(f, nullptr, ffn, 1, r.act.as<half>());
+        p.seg[0] = {L.wg, nullptr, 0, 0};  // interleaved gate/up operand
+        p.nseg = 1;
+        p.swiglu = 2;
       } else {
-        if ((rc = run_gemv(r, L.wg, h, d, nbp, f, ffn, 0)) ||
-            (rc = run_gemv(r, L.wu, h, d, nbp, f + (size_t)nbp * ffn, ffn, 0)))
-          return rc;
-        swiglu_kernel<<<dim3((ffn + 255) / 256, nb), 256, 0, st>>>(f, f + (size_t)nbp * ffn, ffn, 0,
-                                                                   r.act.as<half>());
+        p.seg[0] = {L.wg, nullptr, 0, 0};
+        p.seg[1] = {L.wu, nullptr, 0, 0};
+        p.nseg = 2;
+        p.swiglu = 1;
       }
-      LAYA_CK(cudaGetLastError());
-      if ((rc = run_gemv(r, L.wd, r.act.as<half>(), ffn, nbp, x, d, 1))) return rc;
+      if ((rc = run_gemv(r, p, nbp))) return rc;
+      if ((rc = run_gemv(r, plan1(L.wd, r.act.as<half>(), ffn, x, d, 1), nbp))) return rc;
     } else {
       const half* wgu = L.wgu16;
       if (!wgu) {
@@ -522,11 +1058,19 @@ static int decode_step(Model& m, Replica& r, int nb, const int* tok_in, const in
     }
   }
   // final norm + full-vocabulary logits + greedy argmax
-  r.launches++;
-  LAYA_CK(rmsnorm(x, nullptr, nb, r.out_norm, d, c.eps, h, nullptr, st));
+  if (!small) {
+    r.launches++;
+    LAYA_CK(rmsnorm(x, nullptr, nb, r.out_norm, d, c.eps, h, nullptr, st));
+  }
   float* logits = r.dlogits.as<float>();
   if (small) {
-    if ((rc = run_gemv(r, r.head, h, d, nbp, logits, c.V, 0))) return rc;
+    // head GEMV with the final RMSNorm and the greedy argmax fused
+    GemvPlan hp = plan1(r.head, nullptr, d, nullptr, 0, 0);
+    hp.xres = x;
+    hp.norm_w = r.out_norm;
+    hp.eps = c.eps;
+    hp.best = io.best;
+    if ((rc = run_gemv(r, hp, nbp))) return rc;
   } else {
     GemmArgs a{};
     a.M = nb;
@@ -535,11 +1079,15 @@ static int decode_step(Model& m, Replica& r, int nb, const int* tok_in, const in
     a.out = logits;
     a.ldo = c.V;
     if ((rc = gemm_d(P_GEMM_HEAD, EPI_F32, h, d, r.head16, d, a))) return rc;
+    r.launches++;
+    LAYA_CK(launch_k(argmax_best_kernel, dim3(nb), dim3(256), 0, st, false, (const float*)logits, c.V, io.best));
   }
-  r.launches++;
-  argmax_kernel<<<nb, 256, 0, st>>>(logits, c.V, tok_out);
-  LAYA_CK(cudaGetLastError());
   return 0;
+}
+
+static bool graphs_enabled() {
+  const char* e = std::getenv("LAYA_DECODE_GRAPH");
+  return !(e && e[0] == '0');
 }
 
 int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int n_seqs, int steps, int32_t* out,
@@ -559,7 +1107,7 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   if (!small && (rc = ensure_head16(m, r))) return rc;
   // pages: context + generated tokens per sequence
   std::vector<int> tables, toff(n_seqs), clen(n_seqs);
-  int pages = 0;
+  int pages = 0, max_keys = 0;
   PassPlan pre;
   for (int i = 0; i < n_seqs; i++) {
     const int len = (int)(off[i + 1] - off[i]);
@@ -574,6 +1122,7 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
     }
     for (int t0 = 0; t0 < len; t0 += 64) pre.items.push_back({row0 + t0, std::min(64, len - t0), t0, toff[i]});
     pre.read_rows.push_back(row0 + len - 1);
+    max_keys = std::max(max_keys, len + steps);
   }
   if ((rc = ensure_kv(m, r, pages))) return rc;
   LAYA_CK(cudaMemsetAsync(r.err, 0, 4, r.stream));
@@ -581,30 +1130,51 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   if ((rc = r.hid32.ensure((size_t)R * c.d * 4)) || (rc = r.hid16.ensure((size_t)R * c.d * 2))) return rc;
   const int qd = c.H * c.hd, kd = c.KV * c.hd;
   const int nbp = small ? pad_batch(n_seqs) : n_seqs;
-  // per-step metadata for all steps, uploaded once: positions, slots, key counts
-  std::vector<int> pos_all((size_t)steps * n_seqs), slot_all((size_t)steps * n_seqs);
-  std::vector<DecSeq> seq_all((size_t)steps * n_seqs);
-  std::vector<int> step_keys(steps, 0);
+  // per-step inputs for all steps, uploaded once
+  const size_t nmeta = (size_t)steps * n_seqs;
+  std::vector<int> pos_all(nmeta, 0), slot_all(nmeta, 0);
+  std::vector<DecSeq> seq_all(nmeta, DecSeq{0, 0});
   for (int s = 1; s < steps; s++)
     for (int i = 0; i < n_seqs; i++) {
       const int p = clen[i] + s - 1;
       pos_all[(size_t)s * n_seqs + i] = p;
       slot_all[(size_t)s * n_seqs + i] = tables[toff[i] + p / PAGE] * PAGE + p % PAGE;
       seq_all[(size_t)s * n_seqs + i] = {toff[i], p + 1};
-      step_keys[s] = std::max(step_keys[s], p + 1);
     }
   auto t0 = std::chrono::steady_clock::now();
   // prefill the contexts, then the first greedy token from the last position
   if ((rc = run_forward(m, r, pre, tables, 0, nullptr, nullptr, nullptr))) return rc;
-  if ((rc = r.dlogits.ensure(std::max((size_t)nbp * c.V, (size_t)nbp * std::max(qd + 2 * kd, 2 * c.ffn)) * 4)) ||
-      (rc = r.dargmax.ensure((size_t)steps * n_seqs * 4)))
+  if ((rc = r.dlogits.ensure(std::max((size_t)nbp * c.V, (size_t)nbp * std::max(qd + 2 * kd, 2 * c.ffn)) * 4)))
     return rc;
+  // device state: [counter | best | toks | pos_all | slot_all | seq_all | cur_tok | cur_pos | cur_slot | cur_seq]
+  const size_t best_bytes = ((size_t)n_seqs * 8 + 255) / 256 * 256;
+  const size_t meta_bytes =
+      256 + best_bytes + nmeta * 4 * 3 + nmeta * sizeof(DecSeq) + (size_t)n_seqs * (12 + sizeof(DecSeq)) + 256;
+  if ((rc = r.dargmax.ensure(meta_bytes))) return rc;
+  char* base = static_cast<char*>(r.dargmax.p);
+  StepIO io;
+  io.counter = reinterpret_cast<int*>(base);
+  io.best = reinterpret_cast<unsigned long long*>(base + 256);
+  io.toks = reinterpret_cast<int*>(base + 256 + best_bytes);
+  int* dpos = io.toks + nmeta;
+  int* dslot = dpos + nmeta;
+  DecSeq* dseq = reinterpret_cast<DecSeq*>(dslot + nmeta);
+  io.pos_all = dpos;
+  io.slot_all = dslot;
+  io.seq_all = dseq;
+  io.cur_tok = reinterpret_cast<int*>(dseq + nmeta);
+  io.cur_pos = io.cur_tok + n_seqs;
+  io.cur_slot = io.cur_pos + n_seqs;
+  io.cur_seq = reinterpret_cast<DecSeq*>(io.cur_slot + n_seqs);
+  LAYA_CK(cudaMemsetAsync(io.best, 0, best_bytes, r.stream));
   if (small) {
     // GEMV operands want F16 hidden rows, zero-padded to the GEMV batch
     if ((rc = r.dx16.ensure((size_t)nbp * c.d * 2))) return rc;
     LAYA_CK(cudaMemsetAsync(r.dx16.p, 0, (size_t)nbp * c.d * 2, r.stream));
     LAYA_CK(cudaMemcpyAsync(r.dx16.p, r.hid16.p, (size_t)R * c.d * 2, cudaMemcpyDeviceToDevice, r.stream));
-    if ((rc = run_gemv(r, r.head, r.dx16.as<half>(), c.d, nbp, r.dlogits.as<float>(), c.V, 0))) return rc;
+    GemvPlan hp = plan1(r.head, r.dx16.as<half>(), c.d, nullptr, 0, 0);
+    hp.best = io.best;
+    if ((rc = run_gemv(r, hp, nbp))) return rc;
   } else {
     GemmArgs a{};
     a.M = R;
@@ -616,61 +1186,82 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
     a.budget = 4000000000ll;
     r.launches++;
     LAYA_CK(gemm_launch(EPI_F32, r.hid16.as<half>(), c.d, r.head16, c.d, a, r.num_sms, r.stream));
+    r.launches++;
+    argmax_best_kernel<<<R, 256, 0, r.stream>>>(r.dlogits.as<float>(), c.V, io.best);
+    LAYA_CK(cudaGetLastError());
   }
-  int* toks = r.dargmax.as<int>();  // [steps][n_seqs] greedy tokens
-  r.launches++;
-  argmax_kernel<<<R, 256, 0, r.stream>>>(r.dlogits.as<float>(), c.V, toks);
-  LAYA_CK(cudaGetLastError());
   // decode buffers sized for the padded batch; padded rows stay zero
   if ((rc = r.x.ensure((size_t)nbp * c.d * 4)) || (rc = r.h.ensure((size_t)nbp * c.d * 2)) ||
       (rc = r.qb.ensure((size_t)nbp * qd * 2)) || (rc = r.att.ensure((size_t)nbp * qd * 2)) ||
       (rc = r.act.ensure((size_t)nbp * c.ffn * 2)))
     return rc;
+  const AttnShape sh = attn_shape(r, c, n_seqs, max_keys);
+  if ((rc = r.dpart.ensure((size_t)n_seqs * c.H * sh.splits * (c.hd + 2) * 4)) ||
+      (rc = r.tables.ensure(tables.size() * 4)))
+    return rc;
+  LAYA_CK(cudaMemsetAsync(r.x.p, 0, (size_t)nbp * c.d * 4, r.stream));  // padded rows stay zero
   LAYA_CK(cudaMemsetAsync(r.h.p, 0, (size_t)nbp * c.d * 2, r.stream));
   LAYA_CK(cudaMemsetAsync(r.att.p, 0, (size_t)nbp * qd * 2, r.stream));
   LAYA_CK(cudaMemsetAsync(r.act.p, 0, (size_t)nbp * c.ffn * 2, r.stream));
-  DevBuf dmeta;
-  const size_t nmeta = (size_t)steps * n_seqs;
-  if ((rc = dmeta.ensure(nmeta * (8 + sizeof(DecSeq))))) return rc;
-  int* dpos = dmeta.as<int>();
-  int* dslot = dpos + nmeta;
-  DecSeq* dseq = reinterpret_cast<DecSeq*>(dslot + nmeta);
-  if ((rc = r.tables.ensure(tables.size() * 4))) {
-    dmeta.release();
-    return rc;
-  }
-  cudaError_t e = cudaMemcpyAsync(r.tables.p, tables.data(), tables.size() * 4, cudaMemcpyHostToDevice, r.stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(dpos, pos_all.data(), nmeta * 4, cudaMemcpyHostToDevice, r.stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(dslot, slot_all.data(), nmeta * 4, cudaMemcpyHostToDevice, r.stream);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(dseq, seq_all.data(), nmeta * sizeof(DecSeq), cudaMemcpyHostToDevice, r.stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(r.stream);
+  LAYA_CK(cudaMemsetAsync(io.counter, 0, 4, r.stream));
+  LAYA_CK(cudaMemcpyAsync(r.tables.p, tables.data(), tables.size() * 4, cudaMemcpyHostToDevice, r.stream));
+  LAYA_CK(cudaMemcpyAsync(dpos, pos_all.data(), nmeta * 4, cudaMemcpyHostToDevice, r.stream));
+  LAYA_CK(cudaMemcpyAsync(dslot, slot_all.data(), nmeta * 4, cudaMemcpyHostToDevice, r.stream));
+  LAYA_CK(cudaMemcpyAsync(dseq, seq_all.data(), nmeta * sizeof(DecSeq), cudaMemcpyHostToDevice, r.stream));
+  LAYA_CK(cudaStreamSynchronize(r.stream));
   r.h2d += (long long)(tables.size() * 4 + nmeta * (8 + sizeof(DecSeq)));
-  if (e != cudaSuccess) {
-    dmeta.release();
-    return cuda_fail(e, "decode metadata upload");
+  if (r.prof) {
+    // keep the prefill's kernels apart from the per-step breakdown
+    prof_collect(r);
+    std::map<std::string, std::pair<long long, double>> pre_acc;
+    for (auto& kv : r.prof_acc) pre_acc["prefill:" + kv.first] = kv.second;
+    r.prof_acc.swap(pre_acc);
   }
   auto t1 = std::chrono::steady_clock::now();
-  if ((rc = timing_mark_start(r))) {
-    dmeta.release();
-    return rc;
+  if ((rc = timing_mark_start(r))) return rc;
+  // step 1 runs directly (it also configures kernels and collects the per-kernel
+  // profile); the remaining steps replay a captured graph of the same launches
+  if (steps > 1 && (rc = decode_step(m, r, n_seqs, io, sh))) return rc;
+  if (steps > 2) {
+    if (graphs_enabled()) {
+      const bool prof = r.prof;
+      r.prof = false;
+      cudaGraph_t graph = nullptr;
+      cudaGraphExec_t exec = nullptr;
+      const long long launches0 = r.launches;
+      LAYA_CK(cudaStreamBeginCapture(r.stream, cudaStreamCaptureModeThreadLocal));
+      rc = decode_step(m, r, n_seqs, io, sh);
+      cudaError_t e = cudaStreamEndCapture(r.stream, &graph);
+      r.prof = prof;
+      const long long per_step = r.launches - launches0;
+      if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+      }
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+      e = cudaGraphInstantiate(&exec, graph, 0);
+      if (e == cudaSuccess)
+        for (int s = 2; s < steps && e == cudaSuccess; s++) e = cudaGraphLaunch(exec, r.stream);
+      r.launches += per_step * (steps - 3);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(r.stream);
+      if (exec) cudaGraphExecDestroy(exec);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess) return cuda_fail(e, "decode graph");
+    } else {
+      for (int s = 2; s < steps && !rc; s++) rc = decode_step(m, r, n_seqs, io, sh);
+      if (rc) return rc;
+    }
   }
-  for (int s = 1; s < steps && !rc; s++) {
-    const size_t o = (size_t)s * n_seqs;
-    rc = decode_step(m, r, n_seqs, toks + o - n_seqs, dpos + o, dslot + o, dseq + o, step_keys[s], toks + o);
-  }
-  if (!rc) rc = timing_mark_end(r);
+  r.launches++;
+  finalize_kernel<<<1, 256, 0, r.stream>>>(io.best, io.toks, steps - 1, n_seqs);
+  LAYA_CK(cudaGetLastError());
+  if ((rc = timing_mark_end(r))) return rc;
   auto t2 = std::chrono::steady_clock::now();
-  if (!rc) {
-    std::vector<int> tk(nmeta);
-    e = cudaMemcpy(tk.data(), toks, nmeta * 4, cudaMemcpyDeviceToHost);
-    r.d2h += (long long)nmeta * 4;
-    if (e != cudaSuccess) rc = cuda_fail(e, "decode token read-back");
-    for (int s = 0; s < steps && !rc; s++)
-      for (int i = 0; i < n_seqs; i++) out[(size_t)i * steps + s] = tk[(size_t)s * n_seqs + i];
-  }
-  dmeta.release();
-  if (rc) return rc;
+  std::vector<int> tk(nmeta);
+  LAYA_CK(cudaMemcpy(tk.data(), io.toks, nmeta * 4, cudaMemcpyDeviceToHost));
+  r.d2h += (long long)nmeta * 4;
+  for (int s = 0; s < steps; s++)
+    for (int i = 0; i < n_seqs; i++) out[(size_t)i * steps + s] = tk[(size_t)s * n_seqs + i];
   unsigned err = 0;
   LAYA_CK(cudaMemcpy(&err, r.err, 4, cudaMemcpyDeviceToHost));
   if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");

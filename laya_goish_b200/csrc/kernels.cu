@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 
 namespace laya {
 
@@ -124,6 +125,8 @@ cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstri
 // src/models/openthai/model.rs:205-213 and the tensor read-back used by the
 // parity tests.
 __global__ void rows_f32_kernel(QTensor t, const int* __restrict__ ids, int nrows, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int groups = t.cols / 32;
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i >= (size_t)nrows * groups) return;
@@ -136,11 +139,10 @@ __global__ void rows_f32_kernel(QTensor t, const int* __restrict__ ids, int nrow
   for (int c = 0; c < 8; c++) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
 
-cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st) {
+cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st, bool pdl) {
   size_t n = (size_t)nrows * (t.cols / 32);
   if (!n) return cudaSuccess;
-  rows_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(t, ids, nrows, out);
-  return cudaGetLastError();
+  return launch_k(rows_f32_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, pdl, t, ids, nrows, out);
 }
 
 // ---------------------------------------------------------------- RMSNorm
@@ -169,6 +171,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const int* __restrict__ rows, const float* __restrict__ w,
                                int d, float eps, half* __restrict__ out16, float* __restrict__ out32) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const float* xr = x + (size_t)(rows ? rows[r] : r) * d;
   float ss = 0.f;
@@ -192,10 +196,9 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const int* __restric
 }
 
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
-                    float* out32, cudaStream_t st) {
+                    float* out32, cudaStream_t st, bool pdl) {
   if (!nrows) return cudaSuccess;
-  rmsnorm_kernel<<<nrows, 256, 0, st>>>(x, rows, w, d, eps, out16, out32);
-  return cudaGetLastError();
+  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, x, rows, w, d, eps, out16, out32);
 }
 
 // ---------------------------------------------------------------- heads

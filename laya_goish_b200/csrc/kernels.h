@@ -32,9 +32,10 @@ struct AttnParams {
 
 cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st);
 cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstride, int goff, cudaStream_t st);
-cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st);
+// pdl: launch with programmatic dependent launch allowed (decode graph).
+cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st, bool pdl = false);
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
-                    float* out32, cudaStream_t st);
+                    float* out32, cudaStream_t st, bool pdl = false);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,
                             cudaStream_t st);
 cudaError_t lse_rows(const float* logits, int V, int n, float* out, cudaStream_t st);
