@@ -5,18 +5,23 @@
 // This replaces the reference's F32 AVX2 kernel Matrix::apply
 // (src/tensor.rs:10-102): same contract (W row-major [rows=N][cols=K],
 // one output row per token, optional bias), computed as a persistent,
-// warp-specialised kernel:
-//   warp 0     : TMA producer — 128x64 A tile + 256x64 B tile per stage,
-//                128-byte swizzle, 4-stage shared-memory ring
-//   warp 1     : allocates 512 TMEM columns; one elected thread issues
-//                tcgen05.mma (M=128, N=256, K=16) and commits to mbarriers
-//   warps 2..5 : epilogue — tcgen05.ld from TMEM, fused bias / residual add
-//                (tensor::add, src/tensor.rs:123-128) / SwiGLU
-//                (src/models/openthai/model.rs:225-230) / QKV + RoPE + KV-cache
-//                write, then stores to HBM
-// Two 256-column accumulators in TMEM let the epilogue of tile i overlap the
-// MMAs of tile i+1.  Every TMA load reads this GPU's own memory and none
-// uses cluster multicast.
+// warp-specialised kernel in two shapes:
+//
+// gemm_pair_kernel (M > 128): clusters of two CTAs on two SMs share one
+//   256x256 output tile through tcgen05.mma.cta_group::2.  Each CTA stages
+//   its own 128 rows of A and 128 rows of B per 64-wide K block (32 KB per
+//   stage, 6 stages), so an SM moves a third fewer operand bytes from L2 per
+//   FLOP than with single-CTA 128x256 tiles.
+// gemm_tc_kernel (M <= 128): one CTA per 128x256 tile, 4 stages of 48 KB.
+//
+// Roles in both: warp 0 is the TMA producer (128-byte swizzle), warp 1
+// allocates 512 TMEM columns (two 256-column accumulators, so the epilogue of
+// tile i overlaps the MMAs of tile i+1) and one elected thread issues the
+// MMAs, warps 2..5 are the epilogue — tcgen05.ld from TMEM, fused bias /
+// residual add (tensor::add, src/tensor.rs:123-128) / SwiGLU
+// (src/models/openthai/model.rs:225-230) / QKV + RoPE + KV-cache write, then
+// stores to HBM.  Every TMA load reads this GPU's own memory into the issuing
+// CTA's own shared memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -51,7 +56,9 @@ __device__ __forceinline__ void store_f16x32(half* dst, const float* v, int n) {
       reinterpret_cast<uint4*>(dst)[i] = u;
     }
   } else {
-    for (int i = 0; i < n; i++) dst[i] = __float2half_rn(v[i]);
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+      if (i < n) dst[i] = __float2half_rn(v[i]);
   }
 }
 
@@ -61,7 +68,190 @@ __device__ __forceinline__ void store_f32x32(float* dst, const float* v, int n) 
     for (int i = 0; i < 8; i++)
       reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   } else {
-    for (int i = 0; i < n; i++) dst[i] = v[i];
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+      if (i < n) dst[i] = v[i];
+  }
+}
+
+// Epilogue of one accumulator: this thread owns output row `row` (TMEM lane
+// row % 128 of the warp's quarter) and the BN columns of tile column nt.
+// Start pulling this thread's residual row segment of tile column nt into L2
+// (one bulk prefetch of up to 1 KB), a full tile of MMAs before it is needed.
+template <int EPI>
+__device__ __forceinline__ void resid_prefetch(const GemmArgs& a, int row, int nt) {
+  if constexpr (EPI == EPI_RESID) {
+    const int col0 = nt * BN;
+    const int n = min(BN, a.N - col0);
+    const float* p = a.resid + (size_t)row * a.ldo + col0;
+    if (row < a.M && n > 0 && (n & 3) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0)
+      l2_prefetch_bulk(p, (uint32_t)n * 4);
+  }
+}
+
+template <int EPI, int HD>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase, int row, int nt) {
+  const bool live = row < a.M;
+  const int col0 = nt * BN;
+  if constexpr (EPI == EPI_RESID) {
+    // x[row][col0 ..] += acc.  The residual row was prefetched into L2 when
+    // the tile started (resid_prefetch); here the eight 16-byte loads of the
+    // next 32-column chunk are issued before the current chunk is added, so
+    // one L2 round trip overlaps the TMEM read and the stores of the last.
+    float* xrow = a.resid + (size_t)row * a.ldo;
+    const bool vec = ((a.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.resid) & 15) == 0);
+    float4 cur[8];
+    if (live && vec && col0 + 32 <= a.N) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) cur[i] = reinterpret_cast<const float4*>(xrow + col0)[i];
+    }
+    for (int c = 0; c < BN / 32; c++) {
+      const int cb = col0 + c * 32;
+      if (cb >= a.N) break;
+      const int n = min(32, a.N - cb);
+      float4 nxt[8];
+      const bool pre = live && vec && c + 1 < BN / 32 && cb + 64 <= a.N;
+      if (pre) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) nxt[i] = reinterpret_cast<const float4*>(xrow + cb + 32)[i];
+      }
+      uint32_t r[32];
+      __syncwarp();
+      tmem_ld32(tbase + c * 32, r);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+      if (a.bias)
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+          if (i < n) v[i] += a.bias[cb + i];
+      if (live) {
+        if (vec && n == 32) {
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            float4 o = cur[i];
+            o.x += v[4 * i];
+            o.y += v[4 * i + 1];
+            o.z += v[4 * i + 2];
+            o.w += v[4 * i + 3];
+            reinterpret_cast<float4*>(xrow + cb)[i] = o;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            if (i < n) xrow[cb + i] += v[i];
+        }
+      }
+      if (pre) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) cur[i] = nxt[i];
+      }
+    }
+  } else if constexpr (EPI == EPI_F32 || EPI == EPI_F16) {
+    for (int c = 0; c < BN / 32; c++) {
+      const int cb = col0 + c * 32;
+      if (cb >= a.N) break;
+      uint32_t r[32];
+      __syncwarp();
+      tmem_ld32(tbase + c * 32, r);
+      tmem_ld_wait();
+      const int n = min(32, a.N - cb);
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+      if (a.bias)
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+          if (i < n) v[i] += a.bias[cb + i];
+      if (live) {
+        if constexpr (EPI == EPI_F32) {
+          store_f32x32(reinterpret_cast<float*>(a.out) + (size_t)row * a.ldo + cb, v, n);
+        } else {
+          store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb, v, n);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // B rows of tile nt: [0,128) gate rows, [128,256) up rows of FFN
+    // columns nt*128 .. nt*128+127 (interleaved at load time).
+    for (int c = 0; c < 4; c++) {
+      const int fc = nt * 128 + c * 32;
+      if (fc >= a.N / 2) break;
+      uint32_t rg[32], ru[32];
+      __syncwarp();
+      tmem_ld32(tbase + c * 32, rg);
+      tmem_ld32(tbase + 128 + c * 32, ru);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; i++) v[i] = silu_f(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+      if (live) store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + fc, v, min(32, a.N / 2 - fc));
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    // Columns: [0,qd) q heads, [qd,qd+kd) k heads, [qd+kd,qd+2kd) v heads.
+    // One head (hd columns) at a time: bias, rotate-half RoPE for q/k
+    // (src/tensor.rs:158-171), then q -> Q rows, k/v -> paged KV cache.
+    constexpr int hd = HD;
+    int pos = 0, slot = 0;
+    if (live) {
+      pos = a.pos[row];
+      slot = a.slot[row];
+    }
+    for (int hc = 0; hc < BN; hc += hd) {
+      const int cb = col0 + hc;
+      if (cb >= a.N) break;
+      float v[hd];
+#pragma unroll
+      for (int c = 0; c < hd / 32; c++) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(tbase + hc + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      if (!live) continue;
+      if (a.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(a.bias + cb);
+#pragma unroll
+        for (int i = 0; i < hd / 4; i++) {
+          const float4 b = __ldg(b4 + i);
+          v[4 * i] += b.x;
+          v[4 * i + 1] += b.y;
+          v[4 * i + 2] += b.z;
+          v[4 * i + 3] += b.w;
+        }
+      }
+      const bool is_v = cb >= a.qd + a.kd;
+      if (!is_v) {
+        // (cos, sin) pairs of positions j, j+1 per 16-byte load.
+        const float4* cs = reinterpret_cast<const float4*>(a.rope + (size_t)pos * (hd / 2));
+#pragma unroll
+        for (int j2 = 0; j2 < hd / 4; j2++) {
+          const float4 t = __ldg(cs + j2);
+          const int j = 2 * j2;
+          const float x0 = v[j], x1 = v[j + hd / 2];
+          v[j] = x0 * t.x - x1 * t.y;
+          v[j + hd / 2] = x1 * t.x + x0 * t.y;
+          const float y0 = v[j + 1], y1 = v[j + 1 + hd / 2];
+          v[j + 1] = y0 * t.z - y1 * t.w;
+          v[j + 1 + hd / 2] = y1 * t.z + y0 * t.w;
+        }
+      }
+      if (cb < a.qd) {
+        half* dst = reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb;
+#pragma unroll
+        for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
+      } else {
+        const int kvh = is_v ? (cb - a.qd - a.kd) / hd : (cb - a.qd) / hd;
+        const int page = slot / a.page_size, off = slot % a.page_size;
+        half* base = is_v ? a.vcache : a.kcache;
+        half* dst = base + (((size_t)page * a.kvh + kvh) * a.page_size + off) * hd;
+#pragma unroll
+        for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
+      }
+    }
   }
 }
 
@@ -184,121 +374,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
       const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+      const int row = mt * BM + quarter * 32 + lane;
+      resid_prefetch<EPI>(a, row, nt);
       if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
         atomicOr(a.err, 8u);
         break;
       }
       tc_fence_after();
-      const int row = mt * BM + quarter * 32 + lane;
-      const bool live = row < a.M;
-      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const int col0 = nt * BN;
-      if constexpr (EPI == EPI_F32 || EPI == EPI_F16 || EPI == EPI_RESID) {
-        for (int c = 0; c < BN / 32; c++) {
-          const int cb = col0 + c * 32;
-          if (cb >= a.N) break;
-          uint32_t r[32];
-          __syncwarp();
-          tmem_ld32(tbase + c * 32, r);
-          tmem_ld_wait();
-          const int n = min(32, a.N - cb);
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-          if (a.bias)
-            for (int i = 0; i < n; i++) v[i] += a.bias[cb + i];
-          if (live) {
-            if constexpr (EPI == EPI_F32) {
-              store_f32x32(reinterpret_cast<float*>(a.out) + (size_t)row * a.ldo + cb, v, n);
-            } else if constexpr (EPI == EPI_F16) {
-              store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb, v, n);
-            } else {
-              float* x = a.resid + (size_t)row * a.ldo + cb;
-              if (n == 32) {
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                  float4 o = reinterpret_cast<float4*>(x)[i];
-                  o.x += v[4 * i];
-                  o.y += v[4 * i + 1];
-                  o.z += v[4 * i + 2];
-                  o.w += v[4 * i + 3];
-                  reinterpret_cast<float4*>(x)[i] = o;
-                }
-              } else {
-                for (int i = 0; i < n; i++) x[i] += v[i];
-              }
-            }
-          }
-        }
-      } else if constexpr (EPI == EPI_SWIGLU) {
-        // B rows of tile nt: [0,128) gate rows, [128,256) up rows of FFN
-        // columns nt*128 .. nt*128+127 (interleaved at load time).
-        for (int c = 0; c < 4; c++) {
-          const int fc = nt * 128 + c * 32;
-          if (fc >= a.N / 2) break;
-          uint32_t rg[32], ru[32];
-          __syncwarp();
-          tmem_ld32(tbase + c * 32, rg);
-          tmem_ld32(tbase + 128 + c * 32, ru);
-          tmem_ld_wait();
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = silu_f(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
-          if (live) store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + fc, v, min(32, a.N / 2 - fc));
-        }
-      } else if constexpr (EPI == EPI_QKV) {
-        // Columns: [0,qd) q heads, [qd,qd+kd) k heads, [qd+kd,qd+2kd) v heads.
-        // One head (hd columns) at a time: bias, rotate-half RoPE for q/k
-        // (src/tensor.rs:158-171), then q -> Q rows, k/v -> paged KV cache.
-        constexpr int hd = HD;
-        int pos = 0, slot = 0;
-        if (live) {
-          pos = a.pos[row];
-          slot = a.slot[row];
-        }
-        for (int hc = 0; hc < BN; hc += hd) {
-          const int cb = col0 + hc;
-          if (cb >= a.N) break;
-          float v[hd];
-#pragma unroll
-          for (int c = 0; c < hd / 32; c++) {
-            uint32_t r[32];
-            __syncwarp();
-            tmem_ld32(tbase + hc + c * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; i++) v[c * 32 + i] = __uint_as_float(r[i]);
-          }
-          if (!live) continue;
-          if (a.bias) {
-#pragma unroll
-            for (int i = 0; i < hd; i++) v[i] += a.bias[cb + i];
-          }
-          const bool is_v = cb >= a.qd + a.kd;
-          if (!is_v) {
-            const float2* cs = a.rope + (size_t)pos * (hd / 2);
-#pragma unroll
-            for (int j = 0; j < hd / 2; j++) {
-              const float2 t = cs[j];
-              const float x0 = v[j], x1 = v[j + hd / 2];
-              v[j] = x0 * t.x - x1 * t.y;
-              v[j + hd / 2] = x1 * t.x + x0 * t.y;
-            }
-          }
-          if (cb < a.qd) {
-            half* dst = reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb;
-#pragma unroll
-            for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
-          } else {
-            const int kvh = is_v ? (cb - a.qd - a.kd) / hd : (cb - a.qd) / hd;
-            const int page = slot / a.page_size, off = slot % a.page_size;
-            half* base = is_v ? a.vcache : a.kcache;
-            half* dst = base + (((size_t)page * a.kvh + kvh) * a.page_size + off) * hd;
-#pragma unroll
-            for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
-          }
-        }
-      }
+      epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -313,6 +396,173 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- CTA pair
+constexpr int PAIR_STAGES = 6;
+constexpr int PA_BYTES = 128 * BK * 2;  // this CTA's 128 rows of the 256-row A tile
+constexpr int PB_BYTES = 128 * BK * 2;  // this CTA's 128 rows of the 256-row B tile
+constexpr int PAIR_SMEM = PAIR_STAGES * (PA_BYTES + PB_BYTES) + 1024 + 256;
+static_assert(PAIR_SMEM <= 227 * 1024, "pair GEMM shared memory");
+
+// Launched in clusters of two CTAs.  Tile t of the cluster's sequence covers
+// output rows mt*256 .. +255 (rank r owns mt*256 + 128r ..) and columns
+// nt*256 .. +255.  Barriers:
+//   full[s]   leader only; one arrival (leader's expect_tx of both CTAs'
+//             64 KB) plus the transaction bytes of both CTAs' loads
+//   empty[s]  each CTA; arrived by the leader's MMA commit to both CTAs
+//   tfull[b]  each CTA; arrived by the leader's commit to both CTAs
+//   tempty[b] leader only; 8 arrivals, one per epilogue warp of either CTA
+template <int EPI, int HD>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PAIR_STAGES * PA_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + PAIR_STAGES * PB_BYTES);
+  uint64_t* empty = full + PAIR_STAGES;
+  uint64_t* tfull = empty + PAIR_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barrier inits and the allocation visible to both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = a.m_tiles * a.n_tiles;
+  const int kblocks = (a.K + BK - 1) / BK;
+  const long long budget = a.budget;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < total && ok; tile += nclusters) {
+        const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, budget)) {
+            atomicOr(a.err, 1u);
+            ok = false;
+            break;
+          }
+          const uint32_t fbar = cluster_addr(&full[stage], 0);
+          if (leader) mbar_expect_tx(&full[stage], 2 * (PA_BYTES + PB_BYTES));
+          tma_load_2d_pair(sA + stage * PA_BYTES, &tmA, fbar, kb * BK, mt * 256 + rank * 128);
+          tma_load_2d_pair(sB + stage * PB_BYTES, &tmB, fbar, kb * BK, nt * 256 + rank * 128);
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every stage's last fill is consumed (its empty barrier
+      // completes) before this CTA may exit, so no MMA still reads this
+      // CTA's shared memory and no commit arrives here after exit.
+      for (int i = 0; i < PAIR_STAGES; i++) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, budget)) atomicOr(a.err, 16u);
+        if (++stage == PAIR_STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      const uint32_t idesc = idesc_f16_f32(256, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < total && ok; tile += nclusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, budget)) {
+          atomicOr(a.err, 2u);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; kb++) {
+          if (!mbar_wait(&full[stage], phase, budget)) {
+            atomicOr(a.err, 4u);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(smem_u32(sA + stage * PA_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + stage * PB_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)
+            umma_f16_pair(tmem_d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit_pair(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    const int quarter = warp % 4;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < total; tile += nclusters) {
+      const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+      const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
+      resid_prefetch<EPI>(a, row, nt);
+      if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
+        atomicOr(a.err, 8u);
+        break;
+      }
+      tc_fence_after();
+      epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  cluster_sync();  // both CTAs done with TMEM and each other's barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -360,12 +610,68 @@ static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, cons
   return cudaGetLastError();
 }
 
+template <int EPI, int HD>
+static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
+                               cudaStream_t st) {
+  // Per device: the attribute is set once and the number of CTA pairs that
+  // fit at once is queried once, so the persistent grid never exceeds what is
+  // co-resident (a pair left for a second wave would double the time).
+  static int clusters_fit[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = gemm_pair_kernel<EPI, HD>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = PAIR_SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (clusters_fit[dev & 63] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(2 * (num_sms / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n <= 0) return cudaErrorInvalidConfiguration;
+    clusters_fit[dev & 63] = n;
+  }
+  const int total = a.m_tiles * a.n_tiles;
+  int clusters = clusters_fit[dev & 63];
+  if (clusters > num_sms / 2) clusters = num_sms / 2;
+  if (clusters > total) clusters = total;
+  cfg.gridDim = dim3(2 * clusters);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
+}
+
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
                         cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaSuccess;
   if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
+  if (a.M > BM && num_sms >= 2) {
+    if (!make_map(&ta, A, a.M, a.K, lda, 128) || !make_map(&tb, B, a.N, a.K, ldb, 128))
+      return cudaErrorInvalidValue;
+    a.m_tiles = (a.M + 255) / 256;
+    a.n_tiles = (a.N + BN - 1) / BN;
+    switch (epi) {
+      case EPI_F32: return launch_pair<EPI_F32, 64>(ta, tb, a, num_sms, st);
+      case EPI_F16: return launch_pair<EPI_F16, 64>(ta, tb, a, num_sms, st);
+      case EPI_RESID: return launch_pair<EPI_RESID, 64>(ta, tb, a, num_sms, st);
+      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU, 64>(ta, tb, a, num_sms, st);
+      case EPI_QKV:
+        if (a.hd == 64) return launch_pair<EPI_QKV, 64>(ta, tb, a, num_sms, st);
+        if (a.hd == 128) return launch_pair<EPI_QKV, 128>(ta, tb, a, num_sms, st);
+        return cudaErrorInvalidValue;
+    }
+    return cudaErrorInvalidValue;
+  }
   if (!make_map(&ta, A, a.M, a.K, lda, BM) || !make_map(&tb, B, a.N, a.K, ldb, BN)) return cudaErrorInvalidValue;
   a.m_tiles = (a.M + BM - 1) / BM;
   a.n_tiles = (a.N + BN - 1) / BN;
