@@ -56,6 +56,15 @@ __host__ __device__ __forceinline__ float half_bits(uint32_t x) {
 }
 
 #ifdef __CUDACC__
+// Order-preserving packing of (logit, row) into 64 bits: larger logits win,
+// equal logits resolve to the lower row (the argmax ties-to-lowest rule).
+__device__ __forceinline__ unsigned long long pack_logit(float v, int row) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)row);
+}
+__device__ __forceinline__ int unpack_row(unsigned long long k) { return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu)); }
+
 // Programmatic dependent launch: a kernel launched with
 // cudaLaunchAttributeProgrammaticStreamSerialization may start before the
 // previous kernel in the stream has finished.  pdl_wait() blocks until that

@@ -18,6 +18,7 @@
 
 #include "engine.h"
 #include "gemm.h"
+#include "gemv.h"
 #include "launch.h"
 
 namespace laya {
@@ -52,14 +53,6 @@ struct GemvPlan {
   float eps;
 };
 
-// Order-preserving packing of (logit, row) into 64 bits: larger logits win,
-// equal logits resolve to the lower row (the argmax ties-to-lowest rule).
-__device__ __forceinline__ unsigned long long pack_logit(float v, int row) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)row);
-}
-__device__ __forceinline__ int unpack_row(unsigned long long k) { return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu)); }
 
 // Raw 16-byte slots of the next groups of one row, loaded ahead of their use
 // so many loads are in flight.  A Q8_0 group (32 int8 + scale) takes 2
@@ -872,6 +865,30 @@ static int run_gemv(Replica& r, const GemvPlan& p, int nb) {
   return 0;
 }
 
+static Gemv3Args gv3_base(Replica& r, int mode, int nb, int K) {
+  Gemv3Args a{};
+  a.mode = mode;
+  a.nb = nb;
+  a.K = K;
+  a.err = r.err;
+  a.budget = 4000000000ll;
+  return a;
+}
+
+static int run_gemv3(Replica& r, const Gemv3Args& a) {
+  cudaEvent_t ev;
+  prof_begin(r, P_GEMV, &ev);
+  r.launches++;
+  LAYA_CK(gemv3_launch(a, r.num_sms, r.stream));
+  prof_end(r, P_GEMV, ev);
+  return 0;
+}
+
+static bool gemv3_enabled() {
+  const char* e = std::getenv("LAYA_GEMV3");
+  return !(e && e[0] == '0');
+}
+
 static GemvPlan plan1(const QTensor& w, const half* x, int ldx, float* y, int ldy, int acc) {
   GemvPlan p{};
   p.seg[0] = {w, y, ldy, acc};
@@ -936,11 +953,58 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     const Layer& L = r.layers[l];
     half* kcl = r.kc.as<half>() + l * layer_elems;
     half* vcl = r.vc.as<half>() + l * layer_elems;
+    Gemv3Args gq = gv3_base(r, GV_QKV, nb, d);
+    gq.seg[0] = L.wq;
+    gq.seg[1] = L.wk;
+    gq.seg[2] = L.wv;
+    gq.xres = x;  // RMSNorm fused (src/models/openthai/model.rs:84-94)
+    gq.norm_w = L.attn_norm;
+    gq.eps = c.eps;
+    gq.qd = qd;
+    gq.kd = kd;
+    gq.hd = c.hd;
+    gq.kvh = c.KV;
+    gq.bias = L.bqkv;
+    gq.pos = io.cur_pos;
+    gq.slot = io.cur_slot;
+    gq.rope = r.rope;
+    gq.q = r.qb.as<half>();
+    gq.kcache = kcl;
+    gq.vcache = vcl;
+    gq.page_size = PAGE;
+    Gemv3Args go = gv3_base(r, GV_PLAIN, nb, qd);
+    go.seg[0] = L.wo;
+    go.x = r.att.as<half>();
+    go.ldx = qd;
+    go.y = x;  // residual add (tensor::add, src/tensor.rs:123-128)
+    go.ldy = d;
+    go.acc = 1;
+    Gemv3Args gg = gv3_base(r, GV_SWIGLU, nb, d);
+    gg.seg[0] = L.wg;
+    gg.seg[1] = L.wu;
+    gg.interleaved = L.wgu16 != nullptr;
+    gg.xres = x;
+    gg.norm_w = L.ffn_norm;
+    gg.eps = c.eps;
+    gg.act = r.act.as<half>();
+    gg.ld_act = ffn;
+    Gemv3Args gd = gv3_base(r, GV_PLAIN, nb, ffn);
+    gd.seg[0] = L.wd;
+    gd.x = r.act.as<half>();
+    gd.ldx = ffn;
+    gd.y = x;
+    gd.ldy = d;
+    gd.acc = 1;
+    // the streaming GEMV serves the whole layer when it supports every operand
+    const bool v3 = small && gemv3_enabled() && gemv3_supported(gq) && gemv3_supported(go) &&
+                    gemv3_supported(gg) && gemv3_supported(gd);
     if (!small) {
       r.launches++;
       LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
     }
-    if (small) {
+    if (small && v3) {
+      if ((rc = run_gemv3(r, gq))) return rc;
+    } else if (small) {
       GemvPlan p{};
       if (L.wqkv16) {
         QTensor fused = L.wq;
@@ -989,7 +1053,9 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       if ((rc = gemm_d(P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
     }
     if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, io.cur_seq, sh, r.att.as<half>()))) return rc;
-    if (small) {
+    if (small && v3) {
+      if ((rc = run_gemv3(r, go))) return rc;
+    } else if (small) {
       if ((rc = run_gemv(r, plan1(L.wo, r.att.as<half>(), qd, x, d, 1), nbp))) return rc;
     } else {
       const half* wo = L.wo16;
@@ -1009,7 +1075,10 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       r.launches++;
       LAYA_CK(rmsnorm(x, nullptr, nb, L.ffn_norm, d, c.eps, h, nullptr, st));
     }
-    if (small) {
+    if (small && v3) {
+      if ((rc = run_gemv3(r, gg))) return rc;
+      if ((rc = run_gemv3(r, gd))) return rc;
+    } else if (small) {
       GemvPlan p{};
       p.xres = x;
       p.norm_w = L.ffn_norm;
@@ -1063,7 +1132,16 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     LAYA_CK(rmsnorm(x, nullptr, nb, r.out_norm, d, c.eps, h, nullptr, st));
   }
   float* logits = r.dlogits.as<float>();
-  if (small) {
+  Gemv3Args gh = gv3_base(r, GV_ARGMAX, nb, d);
+  gh.seg[0] = r.head;
+  gh.xres = x;
+  gh.norm_w = r.out_norm;
+  gh.eps = c.eps;
+  gh.best = io.best;
+  if (small && gemv3_enabled() && gemv3_supported(gh)) {
+    // head GEMV with the final RMSNorm and the greedy argmax fused
+    if ((rc = run_gemv3(r, gh))) return rc;
+  } else if (small) {
     // head GEMV with the final RMSNorm and the greedy argmax fused
     GemvPlan hp = plan1(r.head, nullptr, d, nullptr, 0, 0);
     hp.xres = x;
@@ -1167,7 +1245,14 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   io.cur_slot = io.cur_pos + n_seqs;
   io.cur_seq = reinterpret_cast<DecSeq*>(io.cur_slot + n_seqs);
   LAYA_CK(cudaMemsetAsync(io.best, 0, best_bytes, r.stream));
-  if (small) {
+  Gemv3Args gh0 = gv3_base(r, GV_ARGMAX, R, c.d);
+  gh0.seg[0] = r.head;
+  gh0.x = r.hid16.as<half>();  // final-normed F16 hidden rows of the prefill
+  gh0.ldx = c.d;
+  gh0.best = io.best;
+  if (small && gemv3_enabled() && gemv3_supported(gh0)) {
+    if ((rc = run_gemv3(r, gh0))) return rc;
+  } else if (small) {
     // GEMV operands want F16 hidden rows, zero-padded to the GEMV batch
     if ((rc = r.dx16.ensure((size_t)nbp * c.d * 2))) return rc;
     LAYA_CK(cudaMemsetAsync(r.dx16.p, 0, (size_t)nbp * c.d * 2, r.stream));

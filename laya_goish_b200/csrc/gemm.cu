@@ -568,6 +568,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
 // ---------------------------------------------------------------- host side
 
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
+
+bool encode_tiled(CUtensorMap* m, int dtype, int rank, const void* base, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, int swizzle) {
+  auto fn = encode_fn();
+  if (!fn || rank < 1 || rank > 5) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; i++) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; i++) st[i] = strides[i];
+  return fn(m, (CUtensorMapDataType)dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, e,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {

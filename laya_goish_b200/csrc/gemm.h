@@ -1,6 +1,7 @@
 // Host interface of the tcgen05 prefill GEMM (gemm.cu).
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace laya {
@@ -32,6 +33,13 @@ struct GemmArgs {
   unsigned* err;          // device error word; nonzero after a timed-out wait
   long long budget;       // wait budget in SM clock cycles
 };
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point: `rank`
+// dimensions (innermost first), byte strides of dimensions 1..rank-1, box
+// extents, a CUtensorMapDataType and a CUtensorMapSwizzle; element strides
+// 1, zero fill out of bounds.  False when the driver rejects the map.
+bool encode_tiled(CUtensorMap* m, int dtype, int rank, const void* base, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, int swizzle);
 
 // A: [M][lda] F16 row-major activations, B: [N][ldb] F16 row-major weights
 // (K contiguous).  lda, ldb multiples of 8; A, B 16-byte aligned.

@@ -1,0 +1,576 @@
+// Streaming decode GEMV: y = W . x for 1..16 activation rows, W in Q8_0
+// (int8 + F16 scale per 32 elements, structure-of-arrays) or F16.  This is
+// Matrix::apply (src/tensor.rs:10-102) at decode batch sizes, where the
+// weight stream from HBM is the whole cost.
+//
+// Work unit: a tile of 16 weight rows over all K.  Each CTA (one per SM)
+// takes a contiguous range of tiles.  One producer thread streams the tiles
+// into a shared-memory ring with TMA: per stage, two 3-D tensor-map boxes of
+// 8 rows x 1 KB (128-byte swizzle) and, for Q8_0, two boxes of scales; up to
+// 8 stages, as many as shared memory holds beside the activations.  The
+// first stages are requested before griddepcontrol.wait, because weights
+// never depend on the previous kernel.  The activation rows
+// are staged once per CTA in shared memory as F16 (with the RMSNorm applied
+// when it is fused).  Eight compute warps split each stage's K range and
+// reduce with mma.sync m16n8k16: weights are
+// the 16-row A operand (int8 -> F16 exactly through a byte permute), the
+// activation rows the 8-column B operand (batch row = column), F32
+// accumulators; each Q8_0 group's partial product is scaled by its F16 scale
+// in F32, in the reference's order (scale x sum over the group).  The tensor
+// cores are only a reduction engine here: the bound is HBM bandwidth.
+//
+// A lane's 8 consecutive K elements feed fragment columns {2t, 2t+1, 2t+8,
+// 2t+9} of two MMAs; A and B use the same permutation of K, so each lane
+// loads 8 contiguous weights per row and 8 contiguous activations.
+//
+// Rows are placed so that fragment rows g and g+8 (held by the same lane)
+// are partners: the RoPE pair (j, j + hd/2) of a q/k head, or the gate and
+// up rows of one FFN column.  RoPE + KV-cache append and SwiGLU are
+// therefore applied in registers in the epilogue.
+#include <algorithm>
+#include <cstring>
+
+#include "gemm.h"
+
+#include "gemv.h"
+#include "launch.h"
+#include "ptx.cuh"
+
+namespace laya {
+
+constexpr int GV_BYTES = 1024;   // weight bytes per row per stage (Q8_0: 1024 elements, F16: 512)
+// Stage layout: two 8-row halves (tile rows 0-7 and 8-15), each one TMA box
+// [8 planes of 128 B][8 rows][128 B] with 128-byte swizzle (16-byte unit u
+// of row r sits at unit u ^ (r % 8)), then the halves' Q8_0 scales, [8 rows][64 B].
+constexpr int GV_HALF_W = 8 * 8 * 128;
+constexpr int GV_HALF_S = 8 * 64;
+constexpr int GV_STAGE = 18 * 1024;  // 2 * GV_HALF_W + 2 * GV_HALF_S = 17408, kept 1024-byte aligned
+constexpr int GV_MAX_STAGES = 8;     // ring depth: as many stages as shared memory holds
+constexpr int GV_WARPS = 16;                   // compute warps; warp GV_WARPS is the producer
+constexpr int GV_THREADS = (GV_WARPS + 1) * 32;
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Same with a zero accumulator (C = 0).
+__device__ __forceinline__ void mma16816_z(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+// Four int8 (two's complement) -> two half2, exactly: the biased byte b =
+// q + 128 becomes the F16 1024 + b (exponent 0x64, b in the mantissa), and
+// 1024 + 128 is subtracted.
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t b = w ^ 0x80808080u;
+  uint32_t l = __byte_perm(b, 0x64646464u, 0x4140);
+  uint32_t h = __byte_perm(b, 0x64646464u, 0x4342);
+  const half2 off = __float2half2_rn(1152.f);
+  half2 hl = __hsub2(*reinterpret_cast<half2*>(&l), off);
+  half2 hh = __hsub2(*reinterpret_cast<half2*>(&h), off);
+  lo = *reinterpret_cast<uint32_t*>(&hl);
+  hi = *reinterpret_cast<uint32_t*>(&hh);
+}
+
+__device__ __forceinline__ void named_sync() { asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory"); }
+
+// Source row i (0..15) of tile t: segment and row index, or false when the
+// row lies past the matrix (ragged last tile).
+__device__ __forceinline__ bool tile_row(const Gemv3Args& a, int t, int i, int& seg, int& row) {
+  const int lo = i & 7;
+  if (a.mode == GV_SWIGLU) {
+    const int c = 8 * t + lo;
+    if (a.interleaved) {
+      seg = 0;
+      row = (c / 128) * 256 + c % 128 + (i >= 8 ? 128 : 0);
+      return c < a.seg[0].rows / 2;
+    }
+    seg = i >= 8 ? 1 : 0;
+    row = c;
+    return c < a.seg[0].rows;
+  }
+  if (a.mode == GV_QKV) {
+    const int tq = a.qd / 16, tk = a.kd / 16;
+    if (t < tq + tk) {
+      const bool isk = t >= tq;
+      const int tt = isk ? t - tq : t;
+      const int per = a.hd / 16;
+      const int h = tt / per, u = tt % per;
+      seg = isk ? 1 : 0;
+      row = h * a.hd + 8 * u + lo + (i >= 8 ? a.hd / 2 : 0);
+      return true;
+    }
+    seg = 2;
+    row = (t - tq - tk) * 16 + i;
+    return row < a.kd;
+  }
+  seg = 0;
+  row = t * 16 + i;
+  return row < a.seg[0].rows;
+}
+
+// Byte offset of the weight ring: barriers, cross-warp sums and the staged
+// activation rows come first (the ring starts 1024-byte aligned, as the
+// 128-byte swizzle requires).
+__host__ __device__ constexpr size_t gv_ring_offset(int nb, int K, int nt) {
+  return ((size_t)2 * GV_MAX_STAGES * 8 + (size_t)2 * GV_WARPS * 32 * 4 * nt * 4 + (size_t)nb * (K + 8) * 2 + 1023) /
+         1024 * 1024;
+}
+
+// Tensor maps of the (up to three) weight segments and their Q8_0 scales.
+struct GvMaps {
+  CUtensorMap w[3];
+  CUtensorMap s[3];
+};
+
+// One 32-element group (chunk c of a stage) as MMA fragments: rows g and
+// g+8 of the tile, and the activation rows n*8 + g.
+template <int NT>
+struct Frag {
+  uint32_t ag[4], ah[4];
+  float dg, dh;
+  uint4 xv[NT];
+};
+
+template <int NT, bool Q8>
+__device__ __forceinline__ void load_frag(Frag<NT>& f, const uint8_t* sb, int c, int kel0, const half* xs,
+                                          int xpitch, int nb, int g, int tq) {
+  if constexpr (Q8) {
+    // chunk c = bytes [32c, 32c + 32) of each row; lane takes 8 of them
+    const int p = c >> 2, u = ((c & 3) << 1) | (tq >> 1);
+    const int off = p * 1024 + g * 128 + ((u ^ g) << 4) + ((tq & 1) << 3);
+    const uint2 wg = *reinterpret_cast<const uint2*>(sb + off);
+    const uint2 wh = *reinterpret_cast<const uint2*>(sb + GV_HALF_W + off);
+    i8x4_to_h2x2(wg.x, f.ag[0], f.ag[1]);
+    i8x4_to_h2x2(wg.y, f.ag[2], f.ag[3]);
+    i8x4_to_h2x2(wh.x, f.ah[0], f.ah[1]);
+    i8x4_to_h2x2(wh.y, f.ah[2], f.ah[3]);
+    // F16 -> F32 is exact for every finite scale
+    const uint8_t* sc = sb + 2 * GV_HALF_W;
+    f.dg = __half2float(*reinterpret_cast<const half*>(sc + g * 64 + 2 * c));
+    f.dh = __half2float(*reinterpret_cast<const half*>(sc + GV_HALF_S + g * 64 + 2 * c));
+  } else {
+    // chunk c = bytes [64c, 64c + 64) of each row; lane takes 16 of them
+    const int p = c >> 1, u = ((c & 1) << 2) | tq;
+    const int off = p * 1024 + g * 128 + ((u ^ g) << 4);
+    const uint4 wg = *reinterpret_cast<const uint4*>(sb + off);
+    const uint4 wh = *reinterpret_cast<const uint4*>(sb + GV_HALF_W + off);
+    f.ag[0] = wg.x;
+    f.ag[1] = wg.y;
+    f.ag[2] = wg.z;
+    f.ag[3] = wg.w;
+    f.ah[0] = wh.x;
+    f.ah[1] = wh.y;
+    f.ah[2] = wh.z;
+    f.ah[3] = wh.w;
+    f.dg = f.dh = 1.f;
+  }
+  const int k = kel0 + c * 32 + 8 * tq;
+#pragma unroll
+  for (int n = 0; n < NT; n++) {
+    const int b = n * 8 + g;
+    f.xv[n] = b < nb ? *reinterpret_cast<const uint4*>(xs + (size_t)b * xpitch + k) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <int NT, bool Q8>
+__device__ __forceinline__ void mma_frag(const Frag<NT>& f, float (&acc)[NT][4]) {
+#pragma unroll
+  for (int n = 0; n < NT; n++) {
+    if constexpr (Q8) {
+      // each Q8_0 group is summed alone, then scaled by its F16 scale
+      float p[4];
+      mma16816_z(p, f.ag[0], f.ah[0], f.ag[1], f.ah[1], f.xv[n].x, f.xv[n].y);
+      mma16816(p, f.ag[2], f.ah[2], f.ag[3], f.ah[3], f.xv[n].z, f.xv[n].w);
+      acc[n][0] = fmaf(f.dg, p[0], acc[n][0]);
+      acc[n][1] = fmaf(f.dg, p[1], acc[n][1]);
+      acc[n][2] = fmaf(f.dh, p[2], acc[n][2]);
+      acc[n][3] = fmaf(f.dh, p[3], acc[n][3]);
+    } else {
+      mma16816(acc[n], f.ag[0], f.ah[0], f.ag[1], f.ah[1], f.xv[n].x, f.xv[n].y);
+      mma16816(acc[n], f.ag[2], f.ah[2], f.ag[3], f.ah[3], f.xv[n].z, f.xv[n].w);
+    }
+  }
+}
+
+template <int NT, bool Q8, bool NORM>
+__global__ void __launch_bounds__(GV_THREADS, 1)
+    gemv3_kernel(const __grid_constant__ GvMaps maps, const Gemv3Args a, int tiles, int nst) {
+  // [full | empty barriers][cross-warp sums][activation rows][nst-stage ring]
+  extern __shared__ uint8_t gsm_raw[];
+  uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
+  uint64_t* empty = full + GV_MAX_STAGES;
+  float4* red = reinterpret_cast<float4*>(empty + GV_MAX_STAGES);  // [2][GV_WARPS][NT][32] partial sums
+  half* xs = reinterpret_cast<half*>(red + 2 * GV_WARPS * 32 * NT);
+  uint8_t* ring = gsm + gv_ring_offset(a.nb, a.K, NT);
+  __shared__ float nred[GV_WARPS][16];
+  __shared__ float nscale[16];
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int K = a.K;
+  const int row_bytes = Q8 ? K : 2 * K;
+  const int kstages = (row_bytes + GV_BYTES - 1) / GV_BYTES;
+  const int t0 = (int)((long long)blockIdx.x * tiles / gridDim.x);
+  const int t1 = (int)((long long)(blockIdx.x + 1) * tiles / gridDim.x);
+  const long long budget = a.budget;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GV_WARPS);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == GV_WARPS) {
+    // ---------------- producer: one thread, four TMA loads per stage (the
+    // two 8-row halves of the tile and their scales); rows past a matrix
+    // and K past its end arrive as zeros.
+    int stage = 0;
+    uint32_t phase = 0;
+    const uint32_t tx = 2 * GV_HALF_W + (Q8 ? 2 * GV_HALF_S : 0);
+    if (lane == 0) {
+      for (int i = 0; i < 3; i++) {
+        tma_prefetch_desc(&maps.w[i]);
+        if (Q8) tma_prefetch_desc(&maps.s[i]);
+      }
+    }
+    for (int t = t0; t < t1; t++) {
+      int seg0 = 0, row0 = 0, seg1 = 0, row1 = 0;
+      tile_row(a, t, 0, seg0, row0);
+      tile_row(a, t, 8, seg1, row1);
+      for (int ks = 0; ks < kstages; ks++) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, budget)) {
+          if (lane == 0) atomicOr(a.err, 32u);
+        }
+        if (lane == 0) {
+          uint8_t* sb = ring + stage * GV_STAGE;
+          mbar_expect_tx(&full[stage], tx);
+          tma_load_3d(sb, &maps.w[seg0], &full[stage], 0, row0, ks * 8);
+          tma_load_3d(sb + GV_HALF_W, &maps.w[seg1], &full[stage], 0, row1, ks * 8);
+          if (Q8) {
+            tma_load_2d(sb + 2 * GV_HALF_W, &maps.s[seg0], &full[stage], ks * 32, row0);
+            tma_load_2d(sb + 2 * GV_HALF_W + GV_HALF_S, &maps.s[seg1], &full[stage], ks * 32, row1);
+          }
+        }
+        __syncwarp();
+        if (++stage == nst) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    // Every fill is consumed before the CTA exits (no copy left in flight).
+    for (int i = 0; i < nst; i++) {
+      if (!mbar_wait(&empty[stage], phase ^ 1, budget) && lane == 0) atomicOr(a.err, 64u);
+      if (++stage == nst) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    return;
+  }
+
+  // ---------------- compute warps
+  const int g = lane >> 2, tq = lane & 3;
+  const int tid = threadIdx.x;
+  const int xpitch = K + 8;
+  pdl_wait();
+  if constexpr (!NORM) {
+    // F16 activation rows -> shared memory
+    for (int b = 0; b < a.nb; b++)
+      for (int k = tid * 8; k < K; k += GV_WARPS * 32 * 8)
+        *reinterpret_cast<uint4*>(xs + (size_t)b * xpitch + k) =
+            *reinterpret_cast<const uint4*>(a.x + (size_t)b * a.ldx + k);
+    named_sync();
+  } else {
+    // x = rmsnorm(xres[b]) * norm_w  (src/models/openthai/model.rs:84-94), F16 rows in shared memory
+    for (int b = 0; b < a.nb; b++) {
+      float ss = 0.f;
+      for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) nred[warp][b] = ss;
+    }
+    named_sync();
+    if (tid < a.nb) {
+      float tsum = 0.f;
+      for (int i = 0; i < GV_WARPS; i++) tsum += nred[i][tid];
+      nscale[tid] = 1.f / sqrtf(tsum / (float)K + a.eps);
+    }
+    named_sync();
+    for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
+      const float4 wv = *reinterpret_cast<const float4*>(a.norm_w + k);
+      for (int b = 0; b < a.nb; b++) {
+        const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
+        const float sc = nscale[b];
+        half2 h0 = __floats2half2_rn(v.x * sc * wv.x, v.y * sc * wv.y);
+        half2 h1 = __floats2half2_rn(v.z * sc * wv.z, v.w * sc * wv.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(xs + (size_t)b * xpitch + k) = u;
+      }
+    }
+    named_sync();
+  }
+  pdl_trigger();
+
+  unsigned long long best[NT][2];
+#pragma unroll
+  for (int n = 0; n < NT; n++) best[n][0] = best[n][1] = 0ull;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int t = t0; t < t1; t++) {
+    float acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[n][j] = 0.f;
+    for (int ks = 0; ks < kstages; ks++) {
+      if (!mbar_wait(&full[stage], phase, budget)) {
+        if (lane == 0) atomicOr(a.err, 128u);
+      }
+      const uint8_t* sb = ring + stage * GV_STAGE;
+      const int kb = ks * GV_BYTES;
+      const int nbytes = min(GV_BYTES, row_bytes - kb);
+      const int chunks = nbytes / (Q8 ? 32 : 64);  // 32-element groups in this stage
+      const int kel0 = Q8 ? kb : kb / 2;           // first K index of the stage
+      // A full stage has 32 (Q8_0) or 16 (F16) groups: warp w takes groups
+      // w and w + 16, all loads issued before the MMAs.
+      constexpr int CPW = Q8 ? 2 : 1;
+      Frag<NT> f[CPW];
+#pragma unroll
+      for (int i = 0; i < CPW; i++)
+        if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, warp + i * GV_WARPS, kel0, xs, xpitch, a.nb, g, tq);
+#pragma unroll
+      for (int i = 0; i < CPW; i++)
+        if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == nst) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    // Cross-warp sum: every warp holds partial sums over its share of K;
+    // warp 0 adds them up (one 16-byte load per warp) and runs the epilogue.
+    float4* rb = red + ((t - t0) & 1) * (GV_WARPS * NT * 32);
+#pragma unroll
+    for (int n = 0; n < NT; n++) rb[(warp * NT + n) * 32 + lane] = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
+    named_sync();
+    if (warp != 0) continue;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+      float4 sum = rb[n * 32 + lane];
+#pragma unroll
+      for (int w = 1; w < GV_WARPS; w++) {
+        const float4 v = rb[(w * NT + n) * 32 + lane];
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      acc[n][0] = sum.x;
+      acc[n][1] = sum.y;
+      acc[n][2] = sum.z;
+      acc[n][3] = sum.w;
+    }
+    // Epilogue.  Lane (g, tq) holds rows g and g+8 for batch rows
+    // n*8 + 2tq and n*8 + 2tq + 1.
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int b = n * 8 + 2 * tq + e;
+        if (b >= a.nb) continue;
+        const float vg = acc[n][e], vh = acc[n][2 + e];
+        if (a.mode == GV_PLAIN || a.mode == GV_ARGMAX) {
+          const int r0 = t * 16 + g, r1 = r0 + 8;
+          if (a.mode == GV_PLAIN) {
+            float* yb = a.y + (size_t)b * a.ldy;
+            if (r0 < a.seg[0].rows) yb[r0] = a.acc ? yb[r0] + vg : vg;
+            if (r1 < a.seg[0].rows) yb[r1] = a.acc ? yb[r1] + vh : vh;
+          } else {
+            if (r0 < a.seg[0].rows) {
+              const unsigned long long kk = pack_logit(vg, r0);
+              best[n][e] = kk > best[n][e] ? kk : best[n][e];
+            }
+            if (r1 < a.seg[0].rows) {
+              const unsigned long long kk = pack_logit(vh, r1);
+              best[n][e] = kk > best[n][e] ? kk : best[n][e];
+            }
+          }
+        } else if (a.mode == GV_SWIGLU) {
+          const int c = 8 * t + g;
+          const int ffn = a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows;
+          if (c < ffn) a.act[(size_t)b * a.ld_act + c] = __float2half_rn(vg / (1.f + __expf(-vg)) * vh);
+        } else {  // GV_QKV
+          const int tqn = a.qd / 16, tkn = a.kd / 16;
+          const int slot = a.slot[b];
+          const int page = slot / a.page_size, off = slot % a.page_size;
+          if (t < tqn + tkn) {
+            const bool isk = t >= tqn;
+            const int tt = isk ? t - tqn : t;
+            const int per = a.hd / 16;
+            const int h = tt / per, j = 8 * (tt % per) + g;
+            const int col0 = (isk ? a.qd : 0) + h * a.hd + j;  // fused q|k|v column of row g
+            float x0 = vg, x1 = vh;
+            if (a.bias) {
+              x0 += a.bias[col0];
+              x1 += a.bias[col0 + a.hd / 2];
+            }
+            // rotate-half RoPE (src/tensor.rs:158-171)
+            const float2 cs = a.rope[(size_t)a.pos[b] * (a.hd / 2) + j];
+            const float y0 = x0 * cs.x - x1 * cs.y, y1 = x1 * cs.x + x0 * cs.y;
+            half* dst = isk ? a.kcache + (((size_t)page * a.kvh + h) * a.page_size + off) * a.hd
+                            : a.q + (size_t)b * a.qd + h * a.hd;
+            dst[j] = __float2half_rn(y0);
+            dst[j + a.hd / 2] = __float2half_rn(y1);
+          } else {
+            const int r0 = (t - tqn - tkn) * 16 + g;
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+              const int r = r0 + 8 * hh;
+              if (r >= a.kd) continue;
+              float v = hh ? vh : vg;
+              if (a.bias) v += a.bias[a.qd + a.kd + r];
+              const int h = r / a.hd, jj = r % a.hd;
+              a.vcache[(((size_t)page * a.kvh + h) * a.page_size + off) * a.hd + jj] = __float2half_rn(v);
+            }
+          }
+        }
+      }
+  }
+  if (a.mode == GV_ARGMAX && warp == 0) {
+    // lanes with the same tq hold the same batch rows: reduce over g
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        unsigned long long k = best[n][e];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+          k = ok > k ? ok : k;
+        }
+        const int b = n * 8 + 2 * tq + e;
+        if (g == 0 && b < a.nb && k) atomicMax(a.best + b, k);
+      }
+  }
+}
+
+constexpr size_t GV_SMEM_BUDGET = 225 * 1024;  // dynamic shared memory per CTA (one CTA per SM)
+
+// Ring stages that fit beside the staged activations: 2 .. GV_MAX_STAGES,
+// or 0 when even two do not fit.
+static int gemv3_stages(const Gemv3Args& a, int nt) {
+  const size_t off = gv_ring_offset(a.nb, a.K, nt) + 1024;  // + alignment slack
+  if (off + 2 * GV_STAGE > GV_SMEM_BUDGET) return 0;
+  return (int)std::min<size_t>(GV_MAX_STAGES, (GV_SMEM_BUDGET - off) / GV_STAGE);
+}
+
+bool gemv3_supported(const Gemv3Args& a) {
+  if (a.nb < 1 || a.nb > 16 || a.K <= 0 || a.K % 256) return false;
+  const int nseg = a.mode == GV_QKV ? 3 : (a.mode == GV_SWIGLU && !a.interleaved) ? 2 : 1;
+  for (int i = 0; i < nseg; i++) {
+    const QTensor& w = a.seg[i];
+    if ((w.kind != K_Q8_0 && w.kind != K_F16) || w.kind != a.seg[0].kind || w.cols != a.K || !w.q) return false;
+    if (reinterpret_cast<uintptr_t>(w.q) & 15) return false;
+    if (w.kind == K_Q8_0 && (!w.s || (reinterpret_cast<uintptr_t>(w.s) & 15))) return false;
+  }
+  if (a.mode == GV_QKV && (a.hd % 16 || a.qd % 16 || a.kd % 16 || !a.pos || !a.slot || !a.rope)) return false;
+  if (gemv3_stages(a, a.nb <= 8 ? 1 : 2) < 2) return false;
+  if (a.xres) {
+    if (!a.norm_w) return false;
+  } else if (!a.x || (a.ldx % 8) || (reinterpret_cast<uintptr_t>(a.x) & 15)) {
+    return false;
+  }
+  return true;
+}
+
+template <int NT, bool Q8, bool NORM>
+static cudaError_t gemv3_go(const Gemv3Args& a, int tiles, int num_sms, cudaStream_t st) {
+  auto kern = gemv3_kernel<NT, Q8, NORM>;
+  const int nst = gemv3_stages(a, NT);
+  const size_t smem = gv_ring_offset(a.nb, a.K, NT) + 1024 + (size_t)nst * GV_STAGE;
+  GvMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  const int nseg = a.mode == GV_QKV ? 3 : (a.mode == GV_SWIGLU && !a.interleaved) ? 2 : 1;
+  for (int i = 0; i < nseg; i++) {
+    const QTensor& w = a.seg[i];
+    const uint64_t rows = (uint64_t)w.rows, K = (uint64_t)a.K;
+    const uint32_t wbox[3] = {Q8 ? 128u : 64u, 8u, 8u};
+    if (Q8) {
+      // [rows][K] int8 viewed as (128-byte span, row, 128-byte plane)
+      const uint64_t dims[3] = {128, rows, K / 128}, strides[2] = {K, 128};
+      if (!encode_tiled(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w.q, dims, strides, wbox,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+      const uint64_t sdims[2] = {K / 32, rows}, sstrides[1] = {K / 16};
+      const uint32_t sbox[2] = {32, 8};
+      if (!encode_tiled(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.s, sdims, sstrides, sbox,
+                        CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    } else {
+      const uint64_t dims[3] = {64, rows, K / 64}, strides[2] = {2 * K, 128};
+      if (!encode_tiled(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w.q, dims, strides, wbox,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    }
+  }
+  for (int i = nseg; i < 3; i++) {
+    maps.w[i] = maps.w[0];
+    maps.s[i] = maps.s[0];
+  }
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GV_SMEM_BUDGET);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
+  }
+  // one CTA per SM, each with a contiguous range of tiles
+  const int grid = std::min(tiles, num_sms);
+  return launch_k(kern, dim3(grid), dim3(GV_THREADS), smem, st, true, maps, a, tiles, nst);
+}
+
+cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st) {
+  if (!gemv3_supported(a)) return cudaErrorInvalidValue;
+  int tiles = 0;
+  if (a.mode == GV_QKV)
+    tiles = a.qd / 16 + a.kd / 16 + (a.kd + 15) / 16;
+  else if (a.mode == GV_SWIGLU)
+    tiles = ((a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows) + 7) / 8;
+  else
+    tiles = (a.seg[0].rows + 15) / 16;
+  if (tiles <= 0) return cudaSuccess;
+  const bool q8 = a.seg[0].kind == K_Q8_0;
+  const bool norm = a.xres != nullptr;
+  if (a.nb <= 8) {
+    if (q8) return norm ? gemv3_go<1, true, true>(a, tiles, num_sms, st) : gemv3_go<1, true, false>(a, tiles, num_sms, st);
+    return norm ? gemv3_go<1, false, true>(a, tiles, num_sms, st) : gemv3_go<1, false, false>(a, tiles, num_sms, st);
+  }
+  if (q8) return norm ? gemv3_go<2, true, true>(a, tiles, num_sms, st) : gemv3_go<2, true, false>(a, tiles, num_sms, st);
+  return norm ? gemv3_go<2, false, true>(a, tiles, num_sms, st) : gemv3_go<2, false, false>(a, tiles, num_sms, st);
+}
+
+}  // namespace laya

@@ -96,6 +96,14 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
+// 3-D tiled load into this CTA's shared memory (this GPU's own memory).
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 // CTA-pair form of tma_load_2d: the tile lands in this CTA's shared memory,
 // its transaction bytes are counted on `bar_cluster`, which may be the
 // barrier of the pair's leader CTA.  Source is this GPU's own global memory.
