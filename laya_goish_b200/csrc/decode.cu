@@ -884,6 +884,80 @@ static int run_gemv3(Replica& r, const Gemv3Args& a) {
   return 0;
 }
 
+// Weight-side arguments of the four GEMV launches of layer l (i = 0 qkv,
+// 1 attention output, 2 gate/up, 3 down) and of the head (l = L).
+static Gemv3Args gv3_weights(const Model& m, const Replica& r, int l, int i) {
+  const Config& c = m.cfg;
+  Gemv3Args a{};
+  a.nb = 1;
+  if (l == c.L) {
+    a.mode = GV_ARGMAX;
+    a.K = c.d;
+    a.seg[0] = r.head;
+    return a;
+  }
+  const Layer& L = r.layers[l];
+  switch (i) {
+    case 0:
+      a.mode = GV_QKV;
+      a.K = c.d;
+      a.seg[0] = L.wq;
+      a.seg[1] = L.wk;
+      a.seg[2] = L.wv;
+      a.qd = c.H * c.hd;
+      a.kd = c.KV * c.hd;
+      a.hd = c.hd;
+      a.kvh = c.KV;
+      break;
+    case 1:
+      a.mode = GV_PLAIN;
+      a.K = c.H * c.hd;
+      a.seg[0] = L.wo;
+      break;
+    case 2:
+      a.mode = GV_SWIGLU;
+      a.K = c.d;
+      a.seg[0] = L.wg;
+      a.seg[1] = L.wu;
+      a.interleaved = L.wgu16 != nullptr;
+      break;
+    default:
+      a.mode = GV_PLAIN;
+      a.K = c.ffn;
+      a.seg[0] = L.wd;
+  }
+  return a;
+}
+
+// Builds the packed streaming images once per replica (device memory held
+// until close).  A layer whose operands do not all pack keeps the
+// warp-per-row GEMV.
+static int ensure_gv_packed(const Model& m, Replica& r) {
+  const Config& c = m.cfg;
+  if ((int)r.gv_packed.size() == 4 * c.L + 1) return 0;
+  std::vector<const uint8_t*> out(4 * c.L + 1, nullptr);
+  for (int l = 0; l <= c.L; l++) {
+    const int nops = l == c.L ? 1 : 4;
+    std::vector<size_t> bytes(nops);
+    bool ok = true;
+    for (int i = 0; i < nops; i++) {
+      bytes[i] = gemv3_packed_bytes(gv3_weights(m, r, l, i));
+      ok &= bytes[i] > 0;
+    }
+    if (!ok) continue;
+    for (int i = 0; i < nops; i++) {
+      void* p = nullptr;
+      LAYA_CK(cudaMalloc(&p, bytes[i]));
+      r.allocs.push_back(p);
+      LAYA_CK(gemv3_pack(gv3_weights(m, r, l, i), static_cast<uint8_t*>(p), r.stream));
+      out[4 * l + i] = static_cast<const uint8_t*>(p);
+    }
+  }
+  LAYA_CK(cudaStreamSynchronize(r.stream));
+  r.gv_packed = out;
+  return 0;
+}
+
 static bool gemv3_enabled() {
   const char* e = std::getenv("LAYA_GEMV3");
   return !(e && e[0] == '0');
@@ -996,8 +1070,15 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     gd.ldy = d;
     gd.acc = 1;
     // the streaming GEMV serves the whole layer when it supports every operand
-    const bool v3 = small && gemv3_enabled() && gemv3_supported(gq) && gemv3_supported(go) &&
-                    gemv3_supported(gg) && gemv3_supported(gd);
+    bool v3 = small && gemv3_enabled() && (int)r.gv_packed.size() == 4 * c.L + 1;
+    if (v3) {
+      gq.packed = r.gv_packed[4 * l];
+      go.packed = r.gv_packed[4 * l + 1];
+      gg.packed = r.gv_packed[4 * l + 2];
+      gd.packed = r.gv_packed[4 * l + 3];
+      v3 = gq.packed && go.packed && gg.packed && gd.packed && gemv3_supported(gq) && gemv3_supported(go) &&
+           gemv3_supported(gg) && gemv3_supported(gd);
+    }
     if (!small) {
       r.launches++;
       LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
@@ -1138,7 +1219,8 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
   gh.norm_w = r.out_norm;
   gh.eps = c.eps;
   gh.best = io.best;
-  if (small && gemv3_enabled() && gemv3_supported(gh)) {
+  gh.packed = (int)r.gv_packed.size() == 4 * c.L + 1 ? r.gv_packed[4 * c.L] : nullptr;
+  if (small && gemv3_enabled() && gh.packed && gemv3_supported(gh)) {
     // head GEMV with the final RMSNorm and the greedy argmax fused
     if ((rc = run_gemv3(r, gh))) return rc;
   } else if (small) {
@@ -1183,6 +1265,7 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   if ((rc = timing_begin_call(r))) return rc;
   const bool small = n_seqs <= kGemvMaxBatch;
   if (!small && (rc = ensure_head16(m, r))) return rc;
+  if (small && gemv3_enabled() && (rc = ensure_gv_packed(m, r))) return rc;
   // pages: context + generated tokens per sequence
   std::vector<int> tables, toff(n_seqs), clen(n_seqs);
   int pages = 0, max_keys = 0;
@@ -1250,7 +1333,8 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   gh0.x = r.hid16.as<half>();  // final-normed F16 hidden rows of the prefill
   gh0.ldx = c.d;
   gh0.best = io.best;
-  if (small && gemv3_enabled() && gemv3_supported(gh0)) {
+  gh0.packed = (int)r.gv_packed.size() == 4 * c.L + 1 ? r.gv_packed[4 * c.L] : nullptr;
+  if (small && gemv3_enabled() && gh0.packed && gemv3_supported(gh0)) {
     if ((rc = run_gemv3(r, gh0))) return rc;
   } else if (small) {
     // GEMV operands want F16 hidden rows, zero-padded to the GEMV batch

@@ -87,6 +87,10 @@ struct Replica {
   QTensor embd{}, head{};
   const float* out_norm = nullptr;
   const half* head16 = nullptr;  // F16 lm_head for full-vocabulary rows (lazy for quantised models)
+  // Packed streaming images of the decode GEMV operands (gemv3_pack), built
+  // on the first small-batch decode: per layer qkv, o, gate/up, down, then
+  // the head; null where the streaming GEMV does not apply.
+  std::vector<const uint8_t*> gv_packed;
   const float2* rope = nullptr;  // [ctx][hd/2] (cos, sin)
   unsigned* err = nullptr;
   std::map<std::string, QTensor> named;

@@ -4,20 +4,23 @@
 // weight stream from HBM is the whole cost.
 //
 // Work unit: a tile of 16 weight rows over all K.  Each CTA (one per SM)
-// takes a contiguous range of tiles.  One producer thread streams the tiles
-// into a shared-memory ring with TMA: per stage, two 3-D tensor-map boxes of
-// 8 rows x 1 KB (128-byte swizzle) and, for Q8_0, two boxes of scales; up to
-// 8 stages, as many as shared memory holds beside the activations.  The
-// first stages are requested before griddepcontrol.wait, because weights
-// never depend on the previous kernel.  The activation rows
-// are staged once per CTA in shared memory as F16 (with the RMSNorm applied
-// when it is fused).  Eight compute warps split each stage's K range and
-// reduce with mma.sync m16n8k16: weights are
-// the 16-row A operand (int8 -> F16 exactly through a byte permute), the
-// activation rows the 8-column B operand (batch row = column), F32
-// accumulators; each Q8_0 group's partial product is scaled by its F16 scale
-// in F32, in the reference's order (scale x sum over the group).  The tensor
-// cores are only a reduction engine here: the bound is HBM bandwidth.
+// takes a contiguous range of tiles.  The weights are read from a packed
+// image built once per model (gemv3_pack): every stage of every tile (16
+// rows x 1 KB of K, plus the Q8_0 scales) is one contiguous 17 KB block,
+// already swizzled and with the epilogue's partner rows in place, so one
+// producer thread moves it with a single 1-D bulk async copy (a few large
+// copies per SM keep HBM busy; many small copies or tensor-map boxes per
+// stage do not).  Up to 8 stages are in flight, as many as shared memory
+// holds beside the activations; the first are requested before
+// griddepcontrol.wait, because weights never depend on the previous kernel.
+// The activation rows are staged once per CTA in shared memory as F16 (with
+// the RMSNorm applied when it is fused).  Sixteen compute warps split each
+// stage's K range and reduce with mma.sync m16n8k16: weights are the 16-row
+// A operand (int8 -> F16 exactly through a byte permute), the activation
+// rows the 8-column B operand (batch row = column), F32 accumulators; each
+// Q8_0 group's partial product is scaled by its F16 scale in F32, in the
+// reference's order (scale x sum over the group).  The tensor cores are only
+// a reduction engine here: the bound is HBM bandwidth.
 //
 // A lane's 8 consecutive K elements feed fragment columns {2t, 2t+1, 2t+8,
 // 2t+9} of two MMAs; A and B use the same permutation of K, so each lane
@@ -30,7 +33,6 @@
 #include <algorithm>
 #include <cstring>
 
-#include "gemm.h"
 
 #include "gemv.h"
 #include "launch.h"
@@ -39,15 +41,24 @@
 namespace laya {
 
 constexpr int GV_BYTES = 1024;   // weight bytes per row per stage (Q8_0: 1024 elements, F16: 512)
-// Stage layout: two 8-row halves (tile rows 0-7 and 8-15), each one TMA box
-// [8 planes of 128 B][8 rows][128 B] with 128-byte swizzle (16-byte unit u
-// of row r sits at unit u ^ (r % 8)), then the halves' Q8_0 scales, [8 rows][64 B].
+// Stage image (in HBM and in shared memory): two 8-row halves (tile rows
+// 0-7 and 8-15), each [8 planes of 128 B of K][8 rows][128 B] with the
+// 16-byte unit u of row r stored at unit u ^ (r % 8) (conflict-free fragment
+// loads), then for Q8_0 the halves' scales, [8 rows][32 x F16].
 constexpr int GV_HALF_W = 8 * 8 * 128;
 constexpr int GV_HALF_S = 8 * 64;
-constexpr int GV_STAGE = 18 * 1024;  // 2 * GV_HALF_W + 2 * GV_HALF_S = 17408, kept 1024-byte aligned
+constexpr int GV_STAGE = 18 * 1024;  // shared-memory stride of a stage (1024-byte aligned)
+__host__ __device__ constexpr int gv_stage_bytes(bool q8) { return 2 * GV_HALF_W + (q8 ? 2 * GV_HALF_S : 0); }
 constexpr int GV_MAX_STAGES = 8;     // ring depth: as many stages as shared memory holds
 constexpr int GV_WARPS = 16;                   // compute warps; warp GV_WARPS is the producer
-constexpr int GV_THREADS = (GV_WARPS + 1) * 32;
+constexpr int GV_THREADS = (GV_WARPS + 2) * 32;  // + producer warp + epilogue warp
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -124,15 +135,10 @@ __device__ __forceinline__ bool tile_row(const Gemv3Args& a, int t, int i, int& 
 // activation rows come first (the ring starts 1024-byte aligned, as the
 // 128-byte swizzle requires).
 __host__ __device__ constexpr size_t gv_ring_offset(int nb, int K, int nt) {
-  return ((size_t)2 * GV_MAX_STAGES * 8 + (size_t)2 * GV_WARPS * 32 * 4 * nt * 4 + (size_t)nb * (K + 8) * 2 + 1023) /
+  return ((size_t)(2 * GV_MAX_STAGES + 4) * 8 + (size_t)2 * GV_WARPS * 32 * 4 * nt * 4 + (size_t)nb * (K + 8) * 2 +
+          1023) /
          1024 * 1024;
 }
-
-// Tensor maps of the (up to three) weight segments and their Q8_0 scales.
-struct GvMaps {
-  CUtensorMap w[3];
-  CUtensorMap s[3];
-};
 
 // One 32-element group (chunk c of a stage) as MMA fragments: rows g and
 // g+8 of the tile, and the activation rows n*8 + g.
@@ -204,15 +210,47 @@ __device__ __forceinline__ void mma_frag(const Frag<NT>& f, float (&acc)[NT][4])
   }
 }
 
+// Builds stage (t, ks) of the packed image: block b = t * kstages + ks.
+// Rows past a matrix and K past its end are zero.
+__global__ void gemv3_pack_kernel(const Gemv3Args a, int kstages, uint8_t* __restrict__ dst) {
+  const int b = blockIdx.x, t = b / kstages, ks = b % kstages;
+  const bool q8 = a.seg[0].kind == K_Q8_0;
+  const int K = a.K, row_bytes = q8 ? K : 2 * K;
+  uint8_t* out = dst + (size_t)b * gv_stage_bytes(q8);
+  for (int i16 = threadIdx.x; i16 < 16 * 64 + (q8 ? 16 * 4 : 0); i16 += blockDim.x) {
+    if (i16 < 16 * 64) {
+      const int i = i16 / 64, uu = i16 % 64, p = uu / 8, u = uu % 8;
+      int seg = 0, row = 0;
+      const bool valid = tile_row(a, t, i, seg, row);
+      const QTensor& w = seg == 0 ? a.seg[0] : seg == 1 ? a.seg[1] : a.seg[2];
+      const int kb = ks * GV_BYTES + p * 128 + u * 16;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (valid && kb < row_bytes) v = *reinterpret_cast<const uint4*>(w.q + (size_t)row * row_bytes + kb);
+      *reinterpret_cast<uint4*>(out + (i / 8) * GV_HALF_W + p * 1024 + (i % 8) * 128 + ((u ^ (i % 8)) << 4)) = v;
+    } else {
+      const int j = i16 - 16 * 64, i = j / 4, v4 = j % 4;
+      int seg = 0, row = 0;
+      const bool valid = tile_row(a, t, i, seg, row);
+      const QTensor& w = seg == 0 ? a.seg[0] : seg == 1 ? a.seg[1] : a.seg[2];
+      const int grp = ks * 32 + v4 * 8;  // 8 scales per 16 bytes
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (valid && grp < K / 32) v = *reinterpret_cast<const uint4*>(w.s + (size_t)row * (K / 32) + grp);
+      *reinterpret_cast<uint4*>(out + 2 * GV_HALF_W + (i / 8) * GV_HALF_S + (i % 8) * 64 + v4 * 16) = v;
+    }
+  }
+}
+
 template <int NT, bool Q8, bool NORM>
 __global__ void __launch_bounds__(GV_THREADS, 1)
-    gemv3_kernel(const __grid_constant__ GvMaps maps, const Gemv3Args a, int tiles, int nst) {
-  // [full | empty barriers][cross-warp sums][activation rows][nst-stage ring]
+    gemv3_kernel(const Gemv3Args a, int tiles, int nst) {
+  // [full | empty | tdone | tfree barriers][cross-warp sums][activation rows][nst-stage ring]
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
   uint64_t* empty = full + GV_MAX_STAGES;
-  float4* red = reinterpret_cast<float4*>(empty + GV_MAX_STAGES);  // [2][GV_WARPS][NT][32] partial sums
+  uint64_t* tdone = empty + GV_MAX_STAGES;  // [2] a tile's partial sums are written (GV_WARPS arrivals)
+  uint64_t* tfree = tdone + 2;              // [2] the epilogue has read them (1 arrival)
+  float4* red = reinterpret_cast<float4*>(tfree + 2);  // [2][GV_WARPS][NT][32] partial sums
   half* xs = reinterpret_cast<half*>(red + 2 * GV_WARPS * 32 * NT);
   uint8_t* ring = gsm + gv_ring_offset(a.nb, a.K, NT);
   __shared__ float nred[GV_WARPS][16];
@@ -230,40 +268,27 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], GV_WARPS);
     }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tdone[b], GV_WARPS);
+      mbar_init(&tfree[b], 1);
+    }
     mbar_fence_init();
   }
   __syncthreads();
 
   if (warp == GV_WARPS) {
-    // ---------------- producer: one thread, four TMA loads per stage (the
-    // two 8-row halves of the tile and their scales); rows past a matrix
-    // and K past its end arrive as zeros.
+    // ---------------- producer: one thread, one bulk copy per stage
     int stage = 0;
     uint32_t phase = 0;
-    const uint32_t tx = 2 * GV_HALF_W + (Q8 ? 2 * GV_HALF_S : 0);
-    if (lane == 0) {
-      for (int i = 0; i < 3; i++) {
-        tma_prefetch_desc(&maps.w[i]);
-        if (Q8) tma_prefetch_desc(&maps.s[i]);
-      }
-    }
+    const uint32_t sbytes = (uint32_t)gv_stage_bytes(Q8);
     for (int t = t0; t < t1; t++) {
-      int seg0 = 0, row0 = 0, seg1 = 0, row1 = 0;
-      tile_row(a, t, 0, seg0, row0);
-      tile_row(a, t, 8, seg1, row1);
       for (int ks = 0; ks < kstages; ks++) {
-        if (!mbar_wait(&empty[stage], phase ^ 1, budget)) {
+        if (!mbar_wait_sleep(&empty[stage], phase ^ 1, budget)) {
           if (lane == 0) atomicOr(a.err, 32u);
         }
         if (lane == 0) {
-          uint8_t* sb = ring + stage * GV_STAGE;
-          mbar_expect_tx(&full[stage], tx);
-          tma_load_3d(sb, &maps.w[seg0], &full[stage], 0, row0, ks * 8);
-          tma_load_3d(sb + GV_HALF_W, &maps.w[seg1], &full[stage], 0, row1, ks * 8);
-          if (Q8) {
-            tma_load_2d(sb + 2 * GV_HALF_W, &maps.s[seg0], &full[stage], ks * 32, row0);
-            tma_load_2d(sb + 2 * GV_HALF_W + GV_HALF_S, &maps.s[seg1], &full[stage], ks * 32, row1);
-          }
+          mbar_expect_tx(&full[stage], sbytes);
+          bulk_g2s(ring + stage * GV_STAGE, a.packed + ((size_t)t * kstages + ks) * sbytes, sbytes, &full[stage]);
         }
         __syncwarp();
         if (++stage == nst) {
@@ -283,8 +308,161 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
     return;
   }
 
-  // ---------------- compute warps
   const int g = lane >> 2, tq = lane & 3;
+  if (warp == GV_WARPS + 1) {
+    // ---------------- epilogue warp: sums the compute warps' partials and
+    // writes the outputs.  Each tile's global operands (residual, RoPE
+    // factors, bias) are loaded before waiting for its sums, so their
+    // latency overlaps the tile's K loop.  Lane (g, tq) holds rows g and g+8
+    // for batch rows n*8 + 2tq + e.
+    pdl_wait();
+    const int tqn = a.qd / 16, tkn = a.kd / 16;
+    int pos[NT][2], slot[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int b = n * 8 + 2 * tq + e;
+        pos[n][e] = (a.mode == GV_QKV && b < a.nb) ? a.pos[b] : 0;
+        slot[n][e] = (a.mode == GV_QKV && b < a.nb) ? a.slot[b] : 0;
+      }
+    unsigned long long best[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; n++) best[n][0] = best[n][1] = 0ull;
+    for (int t = t0; t < t1; t++) {
+      const int u = t - t0, buf = u & 1;
+      // operands of tile t
+      float yv[NT][2][2];
+      float2 cs[NT][2];
+      float bg = 0.f, bh = 0.f;
+      bool isk = false, isv = false;
+      int h = 0, j = 0, r0 = t * 16 + g;
+      if (a.mode == GV_QKV) {
+        isv = t >= tqn + tkn;
+        if (!isv) {
+          isk = t >= tqn;
+          const int tt = isk ? t - tqn : t, per = a.hd / 16;
+          h = tt / per;
+          j = 8 * (tt % per) + g;
+          const int col0 = (isk ? a.qd : 0) + h * a.hd + j;
+          if (a.bias) {
+            bg = __ldg(a.bias + col0);
+            bh = __ldg(a.bias + col0 + a.hd / 2);
+          }
+        } else {
+          r0 = (t - tqn - tkn) * 16 + g;
+          if (a.bias) {
+            bg = r0 < a.kd ? __ldg(a.bias + a.qd + a.kd + r0) : 0.f;
+            bh = r0 + 8 < a.kd ? __ldg(a.bias + a.qd + a.kd + r0 + 8) : 0.f;
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int b = n * 8 + 2 * tq + e;
+          yv[n][e][0] = yv[n][e][1] = 0.f;
+          cs[n][e] = make_float2(1.f, 0.f);
+          if (b >= a.nb) continue;
+          if (a.mode == GV_PLAIN && a.acc) {
+            const float* yb = a.y + (size_t)b * a.ldy;
+            if (r0 < a.seg[0].rows) yv[n][e][0] = yb[r0];
+            if (r0 + 8 < a.seg[0].rows) yv[n][e][1] = yb[r0 + 8];
+          } else if (a.mode == GV_QKV && !isv) {
+            cs[n][e] = __ldg(a.rope + (size_t)pos[n][e] * (a.hd / 2) + j);
+          }
+        }
+      if (!mbar_wait_sleep(&tdone[buf], (u >> 1) & 1, budget)) {
+        if (lane == 0) atomicOr(a.err, 512u);
+      }
+      const float4* rb = red + buf * (GV_WARPS * NT * 32);
+      float acc[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        float4 sum = rb[n * 32 + lane];
+#pragma unroll
+        for (int w = 1; w < GV_WARPS; w++) {
+          const float4 v = rb[(w * NT + n) * 32 + lane];
+          sum.x += v.x;
+          sum.y += v.y;
+          sum.z += v.z;
+          sum.w += v.w;
+        }
+        acc[n][0] = sum.x;
+        acc[n][1] = sum.y;
+        acc[n][2] = sum.z;
+        acc[n][3] = sum.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[buf]);
+#pragma unroll
+      for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int b = n * 8 + 2 * tq + e;
+          if (b >= a.nb) continue;
+          const float vg = acc[n][e], vh = acc[n][2 + e];
+          if (a.mode == GV_PLAIN) {
+            float* yb = a.y + (size_t)b * a.ldy;
+            if (r0 < a.seg[0].rows) yb[r0] = yv[n][e][0] + vg;  // yv is 0 unless accumulating
+            if (r0 + 8 < a.seg[0].rows) yb[r0 + 8] = yv[n][e][1] + vh;
+          } else if (a.mode == GV_ARGMAX) {
+            if (r0 < a.seg[0].rows) {
+              const unsigned long long kk = pack_logit(vg, r0);
+              best[n][e] = kk > best[n][e] ? kk : best[n][e];
+            }
+            if (r0 + 8 < a.seg[0].rows) {
+              const unsigned long long kk = pack_logit(vh, r0 + 8);
+              best[n][e] = kk > best[n][e] ? kk : best[n][e];
+            }
+          } else if (a.mode == GV_SWIGLU) {
+            const int c = 8 * t + g;
+            const int ffn = a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows;
+            if (c < ffn) a.act[(size_t)b * a.ld_act + c] = __float2half_rn(vg / (1.f + __expf(-vg)) * vh);
+          } else {  // GV_QKV
+            const int page = slot[n][e] / a.page_size, off = slot[n][e] % a.page_size;
+            if (!isv) {
+              // rotate-half RoPE (src/tensor.rs:158-171) after the bias
+              const float x0 = vg + bg, x1 = vh + bh;
+              const float y0 = x0 * cs[n][e].x - x1 * cs[n][e].y, y1 = x1 * cs[n][e].x + x0 * cs[n][e].y;
+              half* dst = isk ? a.kcache + (((size_t)page * a.kvh + h) * a.page_size + off) * a.hd
+                              : a.q + (size_t)b * a.qd + h * a.hd;
+              dst[j] = __float2half_rn(y0);
+              dst[j + a.hd / 2] = __float2half_rn(y1);
+            } else {
+#pragma unroll
+              for (int hh = 0; hh < 2; hh++) {
+                const int r = r0 + 8 * hh;
+                if (r >= a.kd) continue;
+                const float v = (hh ? vh : vg) + (hh ? bh : bg);
+                a.vcache[(((size_t)page * a.kvh + r / a.hd) * a.page_size + off) * a.hd + r % a.hd] =
+                    __float2half_rn(v);
+              }
+            }
+          }
+        }
+    }
+    if (a.mode == GV_ARGMAX) {
+      // lanes with the same tq hold the same batch rows: reduce over g
+#pragma unroll
+      for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          unsigned long long k = best[n][e];
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+            k = ok > k ? ok : k;
+          }
+          const int b = n * 8 + 2 * tq + e;
+          if (g == 0 && b < a.nb && k) atomicMax(a.best + b, k);
+        }
+    }
+    return;
+  }
+
+  // ---------------- compute warps
   const int tid = threadIdx.x;
   const int xpitch = K + 8;
   pdl_wait();
@@ -331,9 +509,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
   }
   pdl_trigger();
 
-  unsigned long long best[NT][2];
-#pragma unroll
-  for (int n = 0; n < NT; n++) best[n][0] = best[n][1] = 0ull;
   int stage = 0;
   uint32_t phase = 0;
   for (int t = t0; t < t1; t++) {
@@ -343,7 +518,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < 4; j++) acc[n][j] = 0.f;
     for (int ks = 0; ks < kstages; ks++) {
-      if (!mbar_wait(&full[stage], phase, budget)) {
+      if (!mbar_wait_sleep(&full[stage], phase, budget)) {
         if (lane == 0) atomicOr(a.err, 128u);
       }
       const uint8_t* sb = ring + stage * GV_STAGE;
@@ -368,110 +543,16 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
         phase ^= 1;
       }
     }
-    // Cross-warp sum: every warp holds partial sums over its share of K;
-    // warp 0 adds them up (one 16-byte load per warp) and runs the epilogue.
-    float4* rb = red + ((t - t0) & 1) * (GV_WARPS * NT * 32);
+    // Hand the partial sums (this warp's share of K) to the epilogue warp.
+    const int u = t - t0, buf = u & 1;
+    if (!mbar_wait_sleep(&tfree[buf], ((u >> 1) & 1) ^ 1, budget)) {
+      if (lane == 0) atomicOr(a.err, 256u);
+    }
+    float4* rb = red + buf * (GV_WARPS * NT * 32);
 #pragma unroll
     for (int n = 0; n < NT; n++) rb[(warp * NT + n) * 32 + lane] = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
-    named_sync();
-    if (warp != 0) continue;
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-      float4 sum = rb[n * 32 + lane];
-#pragma unroll
-      for (int w = 1; w < GV_WARPS; w++) {
-        const float4 v = rb[(w * NT + n) * 32 + lane];
-        sum.x += v.x;
-        sum.y += v.y;
-        sum.z += v.z;
-        sum.w += v.w;
-      }
-      acc[n][0] = sum.x;
-      acc[n][1] = sum.y;
-      acc[n][2] = sum.z;
-      acc[n][3] = sum.w;
-    }
-    // Epilogue.  Lane (g, tq) holds rows g and g+8 for batch rows
-    // n*8 + 2tq and n*8 + 2tq + 1.
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-      for (int e = 0; e < 2; e++) {
-        const int b = n * 8 + 2 * tq + e;
-        if (b >= a.nb) continue;
-        const float vg = acc[n][e], vh = acc[n][2 + e];
-        if (a.mode == GV_PLAIN || a.mode == GV_ARGMAX) {
-          const int r0 = t * 16 + g, r1 = r0 + 8;
-          if (a.mode == GV_PLAIN) {
-            float* yb = a.y + (size_t)b * a.ldy;
-            if (r0 < a.seg[0].rows) yb[r0] = a.acc ? yb[r0] + vg : vg;
-            if (r1 < a.seg[0].rows) yb[r1] = a.acc ? yb[r1] + vh : vh;
-          } else {
-            if (r0 < a.seg[0].rows) {
-              const unsigned long long kk = pack_logit(vg, r0);
-              best[n][e] = kk > best[n][e] ? kk : best[n][e];
-            }
-            if (r1 < a.seg[0].rows) {
-              const unsigned long long kk = pack_logit(vh, r1);
-              best[n][e] = kk > best[n][e] ? kk : best[n][e];
-            }
-          }
-        } else if (a.mode == GV_SWIGLU) {
-          const int c = 8 * t + g;
-          const int ffn = a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows;
-          if (c < ffn) a.act[(size_t)b * a.ld_act + c] = __float2half_rn(vg / (1.f + __expf(-vg)) * vh);
-        } else {  // GV_QKV
-          const int tqn = a.qd / 16, tkn = a.kd / 16;
-          const int slot = a.slot[b];
-          const int page = slot / a.page_size, off = slot % a.page_size;
-          if (t < tqn + tkn) {
-            const bool isk = t >= tqn;
-            const int tt = isk ? t - tqn : t;
-            const int per = a.hd / 16;
-            const int h = tt / per, j = 8 * (tt % per) + g;
-            const int col0 = (isk ? a.qd : 0) + h * a.hd + j;  // fused q|k|v column of row g
-            float x0 = vg, x1 = vh;
-            if (a.bias) {
-              x0 += a.bias[col0];
-              x1 += a.bias[col0 + a.hd / 2];
-            }
-            // rotate-half RoPE (src/tensor.rs:158-171)
-            const float2 cs = a.rope[(size_t)a.pos[b] * (a.hd / 2) + j];
-            const float y0 = x0 * cs.x - x1 * cs.y, y1 = x1 * cs.x + x0 * cs.y;
-            half* dst = isk ? a.kcache + (((size_t)page * a.kvh + h) * a.page_size + off) * a.hd
-                            : a.q + (size_t)b * a.qd + h * a.hd;
-            dst[j] = __float2half_rn(y0);
-            dst[j + a.hd / 2] = __float2half_rn(y1);
-          } else {
-            const int r0 = (t - tqn - tkn) * 16 + g;
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-              const int r = r0 + 8 * hh;
-              if (r >= a.kd) continue;
-              float v = hh ? vh : vg;
-              if (a.bias) v += a.bias[a.qd + a.kd + r];
-              const int h = r / a.hd, jj = r % a.hd;
-              a.vcache[(((size_t)page * a.kvh + h) * a.page_size + off) * a.hd + jj] = __float2half_rn(v);
-            }
-          }
-        }
-      }
-  }
-  if (a.mode == GV_ARGMAX && warp == 0) {
-    // lanes with the same tq hold the same batch rows: reduce over g
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-      for (int e = 0; e < 2; e++) {
-        unsigned long long k = best[n][e];
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
-          k = ok > k ? ok : k;
-        }
-        const int b = n * 8 + 2 * tq + e;
-        if (g == 0 && b < a.nb && k) atomicMax(a.best + b, k);
-      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tdone[buf]);
   }
 }
 
@@ -485,8 +566,9 @@ static int gemv3_stages(const Gemv3Args& a, int nt) {
   return (int)std::min<size_t>(GV_MAX_STAGES, (GV_SMEM_BUDGET - off) / GV_STAGE);
 }
 
-bool gemv3_supported(const Gemv3Args& a) {
-  if (a.nb < 1 || a.nb > 16 || a.K <= 0 || a.K % 256) return false;
+// Weight-side conditions (packing needs only these).
+static bool gemv3_weights_ok(const Gemv3Args& a) {
+  if (a.K <= 0 || a.K % 256) return false;
   const int nseg = a.mode == GV_QKV ? 3 : (a.mode == GV_SWIGLU && !a.interleaved) ? 2 : 1;
   for (int i = 0; i < nseg; i++) {
     const QTensor& w = a.seg[i];
@@ -494,7 +576,13 @@ bool gemv3_supported(const Gemv3Args& a) {
     if (reinterpret_cast<uintptr_t>(w.q) & 15) return false;
     if (w.kind == K_Q8_0 && (!w.s || (reinterpret_cast<uintptr_t>(w.s) & 15))) return false;
   }
-  if (a.mode == GV_QKV && (a.hd % 16 || a.qd % 16 || a.kd % 16 || !a.pos || !a.slot || !a.rope)) return false;
+  if (a.mode == GV_QKV && (a.hd % 16 || a.qd % 16 || a.kd % 16)) return false;
+  return true;
+}
+
+bool gemv3_supported(const Gemv3Args& a) {
+  if (a.nb < 1 || a.nb > 16 || !gemv3_weights_ok(a)) return false;
+  if (a.mode == GV_QKV && (!a.pos || !a.slot || !a.rope)) return false;
   if (gemv3_stages(a, a.nb <= 8 ? 1 : 2) < 2) return false;
   if (a.xres) {
     if (!a.norm_w) return false;
@@ -509,35 +597,6 @@ static cudaError_t gemv3_go(const Gemv3Args& a, int tiles, int num_sms, cudaStre
   auto kern = gemv3_kernel<NT, Q8, NORM>;
   const int nst = gemv3_stages(a, NT);
   const size_t smem = gv_ring_offset(a.nb, a.K, NT) + 1024 + (size_t)nst * GV_STAGE;
-  GvMaps maps;
-  std::memset(&maps, 0, sizeof(maps));
-  const int nseg = a.mode == GV_QKV ? 3 : (a.mode == GV_SWIGLU && !a.interleaved) ? 2 : 1;
-  for (int i = 0; i < nseg; i++) {
-    const QTensor& w = a.seg[i];
-    const uint64_t rows = (uint64_t)w.rows, K = (uint64_t)a.K;
-    const uint32_t wbox[3] = {Q8 ? 128u : 64u, 8u, 8u};
-    if (Q8) {
-      // [rows][K] int8 viewed as (128-byte span, row, 128-byte plane)
-      const uint64_t dims[3] = {128, rows, K / 128}, strides[2] = {K, 128};
-      if (!encode_tiled(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w.q, dims, strides, wbox,
-                        CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
-      const uint64_t sdims[2] = {K / 32, rows}, sstrides[1] = {K / 16};
-      const uint32_t sbox[2] = {32, 8};
-      if (!encode_tiled(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.s, sdims, sstrides, sbox,
-                        CU_TENSOR_MAP_SWIZZLE_NONE))
-        return cudaErrorInvalidValue;
-    } else {
-      const uint64_t dims[3] = {64, rows, K / 64}, strides[2] = {2 * K, 128};
-      if (!encode_tiled(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w.q, dims, strides, wbox,
-                        CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
-    }
-  }
-  for (int i = nseg; i < 3; i++) {
-    maps.w[i] = maps.w[0];
-    maps.s[i] = maps.s[0];
-  }
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -550,18 +609,36 @@ static cudaError_t gemv3_go(const Gemv3Args& a, int tiles, int num_sms, cudaStre
   }
   // one CTA per SM, each with a contiguous range of tiles
   const int grid = std::min(tiles, num_sms);
-  return launch_k(kern, dim3(grid), dim3(GV_THREADS), smem, st, true, maps, a, tiles, nst);
+  return launch_k(kern, dim3(grid), dim3(GV_THREADS), smem, st, true, a, tiles, nst);
+}
+
+static int gemv3_tiles(const Gemv3Args& a) {
+  if (a.mode == GV_QKV) return a.qd / 16 + a.kd / 16 + (a.kd + 15) / 16;
+  if (a.mode == GV_SWIGLU) return ((a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows) + 7) / 8;
+  return (a.seg[0].rows + 15) / 16;
+}
+
+static int gemv3_kstages(const Gemv3Args& a) {
+  const int row_bytes = a.seg[0].kind == K_Q8_0 ? a.K : 2 * a.K;
+  return (row_bytes + GV_BYTES - 1) / GV_BYTES;
+}
+
+size_t gemv3_packed_bytes(const Gemv3Args& a) {
+  if (!gemv3_weights_ok(a)) return 0;
+  return (size_t)gemv3_tiles(a) * gemv3_kstages(a) * gv_stage_bytes(a.seg[0].kind == K_Q8_0);
+}
+
+cudaError_t gemv3_pack(const Gemv3Args& a, uint8_t* dst, cudaStream_t st) {
+  if (!gemv3_weights_ok(a)) return cudaErrorInvalidValue;
+  const int blocks = gemv3_tiles(a) * gemv3_kstages(a);
+  if (blocks <= 0) return cudaSuccess;
+  gemv3_pack_kernel<<<blocks, 256, 0, st>>>(a, gemv3_kstages(a), dst);
+  return cudaGetLastError();
 }
 
 cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st) {
-  if (!gemv3_supported(a)) return cudaErrorInvalidValue;
-  int tiles = 0;
-  if (a.mode == GV_QKV)
-    tiles = a.qd / 16 + a.kd / 16 + (a.kd + 15) / 16;
-  else if (a.mode == GV_SWIGLU)
-    tiles = ((a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows) + 7) / 8;
-  else
-    tiles = (a.seg[0].rows + 15) / 16;
+  if (!gemv3_supported(a) || !a.packed || (reinterpret_cast<uintptr_t>(a.packed) & 15)) return cudaErrorInvalidValue;
+  const int tiles = gemv3_tiles(a);
   if (tiles <= 0) return cudaSuccess;
   const bool q8 = a.seg[0].kind == K_Q8_0;
   const bool norm = a.xres != nullptr;

@@ -48,6 +48,8 @@ struct Gemv3Args {
   half* kcache;
   half* vcache;       // [pages][kvh][page_size][hd]
   int page_size;
+  // packed weight image of the segments (gemv3_pack), required by gemv3_launch
+  const uint8_t* packed;
   // bounded waits
   unsigned* err;
   long long budget;
@@ -56,6 +58,11 @@ struct Gemv3Args {
 // True when gemv3_launch handles these operands (Q8_0 or F16, K a multiple
 // of 256, at most 16 batch rows, the staged activations fit).
 bool gemv3_supported(const Gemv3Args& a);
+// The segments' weights rearranged for streaming: per 16-row tile and per
+// 1 KB of K, one contiguous stage image.  Depends only on mode, segments and
+// K (not on the batch rows), so it is built once per model.
+size_t gemv3_packed_bytes(const Gemv3Args& a);
+cudaError_t gemv3_pack(const Gemv3Args& a, uint8_t* dst, cudaStream_t st);
 cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st);
 
 }  // namespace laya

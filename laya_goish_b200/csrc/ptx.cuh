@@ -47,6 +47,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint (ns): a waiting thread sleeps until the
+// phase completes or the hint expires instead of re-polling.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\tmbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, "
+      "P;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, long long budget) {
+  if (mbar_try_wait_sleep(bar, parity)) return true;
+  long long t0 = clock64();
+  while (!mbar_try_wait_sleep(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+
 // Bounded wait: false once `budget` SM clock cycles have passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long budget) {
   if (mbar_try_wait(bar, parity)) return true;
