@@ -430,37 +430,45 @@ __global__ void __launch_bounds__(128) attn_kernel(const half* __restrict__ q, i
         mma16816(s[nj + 1], qf[kk], b[2], b[3]);
       }
     }
+    // Scores stay unscaled until the exponent (the scale is positive, so
+    // the running maximum is the same).  Only blocks that reach past the
+    // CTA's first query position or past the last key need the causal mask.
+    if (kb * BKV + BKV - 1 > it.pos0 || kb * BKV + BKV > n_keys) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int key = kb * BKV + j * 8 + 2 * t;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          if (key + e > pos_a || key + e >= n_keys) s[j][e] = -INFINITY;
+          if (key + e > pos_b || key + e >= n_keys) s[j][2 + e] = -INFINITY;
+        }
+      }
+    }
     float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      const int key = kb * BKV + j * 8 + 2 * t;
-#pragma unroll
-      for (int e = 0; e < 2; e++) {
-        float va = s[j][e] * scale_log2, vb = s[j][2 + e] * scale_log2;
-        if (key + e > pos_a || key + e >= n_keys) va = -INFINITY;
-        if (key + e > pos_b || key + e >= n_keys) vb = -INFINITY;
-        s[j][e] = va;
-        s[j][2 + e] = vb;
-        mx_a = fmaxf(mx_a, va);
-        mx_b = fmaxf(mx_b, vb);
-      }
+      mx_a = fmaxf(mx_a, fmaxf(s[j][0], s[j][1]));
+      mx_b = fmaxf(mx_b, fmaxf(s[j][2], s[j][3]));
     }
 #pragma unroll
     for (int o2 = 1; o2 <= 2; o2 <<= 1) {
       mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffff, mx_a, o2));
       mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffff, mx_b, o2));
     }
+    // Block 0 always holds key 0 <= every query position, so the maxima are
+    // finite from the first block on.
     const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float ca = exp2f(m_a - mn_a), cb = exp2f(m_b - mn_b);
+    const float ca = exp2f((m_a - mn_a) * scale_log2), cb = exp2f((m_b - mn_b) * scale_log2);
     m_a = mn_a;
     m_b = mn_b;
+    const float oa = -mn_a * scale_log2, ob = -mn_b * scale_log2;
     float sum_a = 0.f, sum_b = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      s[j][0] = exp2f(s[j][0] - mn_a);
-      s[j][1] = exp2f(s[j][1] - mn_a);
-      s[j][2] = exp2f(s[j][2] - mn_b);
-      s[j][3] = exp2f(s[j][3] - mn_b);
+      s[j][0] = exp2f(fmaf(s[j][0], scale_log2, oa));
+      s[j][1] = exp2f(fmaf(s[j][1], scale_log2, oa));
+      s[j][2] = exp2f(fmaf(s[j][2], scale_log2, ob));
+      s[j][3] = exp2f(fmaf(s[j][3], scale_log2, ob));
       sum_a += s[j][0] + s[j][1];
       sum_b += s[j][2] + s[j][3];
     }
