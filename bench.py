@@ -292,6 +292,90 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+AUX = {
+    # name: (config, requests per GPU, prompt tokens, question builder, description)
+    "cfg0": ("cfg0", 1, 256, "check over 2 candidate ids",
+             "cfg0: Llama-16L F16 from seed, one 256-token request, one check question over 2 candidates"),
+    "cfg2": ("cfg2", 128, 768, "score over 5 criteria x 3-token continuations (full-vocabulary log-softmax)",
+             "cfg2: Llama-16L Q4_K_M (attn_v/ffn_down Q6_K) from seed, 128 requests x 768-token shared prefix, "
+             "one score question over 5 criteria of 3-token continuations"),
+    "cfg3": ("cfg3", 128, 1024, "3 check questions, each a 16-id suffix and 2 candidates",
+             "cfg3: Qwen2-28L F16 from seed (d 3584, 28/4 heads, FFN 18944, V 152064, QKV bias), 128 requests "
+             "per GPU (1024 over 8 GPUs) x 1024 tokens, 3 check questions with 16-id suffixes"),
+}
+
+
+def aux_questions(name, vocab):
+    from laya_goish_b200.engine import Question
+
+    rng = np.random.default_rng(7)
+    if name == "cfg0":
+        return [Question("noul", synth.candidates(rng, vocab, 2))], 0
+    if name == "cfg2":
+        return [Question("score", synth.token_ids(rng, vocab, 15).reshape(5, 3))], 15
+    return [Question("noul", synth.candidates(rng, vocab, 2), suffix=synth.token_ids(rng, vocab, 16))
+            for _ in range(3)], 48
+
+
+def run_aux(args):
+    """The other BASELINE configs on one GPU (auxiliary lines; the contract
+    line is the default cfg1 run).  Same timing as run_ours: W warm-up
+    steps, K timed steps, CUDA-event device time of the library's stream."""
+    import torch
+
+    _, _, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    from laya_goish_b200 import engine
+
+    cname, requests, tokens, qdesc, desc = AUX[args.workload]
+    cfg = synth.CONFIGS[cname]
+    path = synth.model_path(cname)
+    rng = np.random.default_rng(1000)
+    prompts = [synth.token_ids(rng, cfg.vocab, tokens) for _ in range(requests)]
+    qs, branch_tokens = aux_questions(args.workload, cfg.vocab)
+    e = engine.Engine(path, devices=[local])
+    clk = Clocks(local).start()
+    for _ in range(args.warmup):
+        e.decide_batch(prompts, qs)
+    e.profile(True)
+    e.profile_read()
+    torch.cuda.synchronize()
+    dev_ms, wall = 0.0, 0.0
+    clk.begin()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        e.decide_batch(prompts, qs)
+        wall += (time.perf_counter() - t0) * 1000.0
+        dev_ms += e.timing()["device_ms"]
+    torch.cuda.synchronize()
+    clk.end()
+    clk.stop()
+    prof = e.profile_read()
+    e.close()
+    gemm_ms = sum(v[1] for k, v in prof.items() if k.startswith("gemm_") and k != "gemm_head")
+    tok = requests * (tokens + branch_tokens)
+    gemm_flops = gemm_flops_per_token(cfg) * tok * args.steps
+    pk, pk_kind = peaks()
+    step_ms = dev_ms / args.steps
+    wbytes = os.path.getsize(path)  # every weight byte is read at least once per step
+    line = {
+        "metric": "decide requests/s", "value": requests * args.steps / (dev_ms / 1000.0), "unit": "req/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": desc, "requests": requests, "prompt_tokens": tokens, "questions": qdesc},
+        "prefill_tok_s": tok / (step_ms / 1000.0),
+        "gemm_tflops": gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None,
+        "gemm_frac": (gemm_flops / (gemm_ms / 1000.0) / 1e12) / pk["bf16_tflops_sustained"] if gemm_ms else None,
+        "weight_stream_frac": (wbytes / (step_ms / 1000.0) / 1e9) / pk["hbm_gbs"],
+        "weight_bytes": wbytes,
+        "peak_kind": pk_kind,
+        "e2e_req_s": requests * args.steps / (wall / 1000.0),
+        "kernel_shares": {k: round(v[1] / dev_ms, 4) for k, v in sorted(prof.items())} if dev_ms else {},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_decode(args):
     """cfg4: KV-cached greedy decode on the cfg1 Q8_0 decoder.  Context of
     `--ctx` seeded ids per sequence, `--gen` generated tokens, `--batch`
@@ -351,7 +435,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3"])
     ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
     ap.add_argument("--gen", type=int, default=128, help="decode: generated tokens")
@@ -362,6 +446,8 @@ def main():
         args.warmup = 3
     if args.workload == "decode":
         run_decode(args)
+    elif args.workload in AUX:
+        run_aux(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
