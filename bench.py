@@ -40,6 +40,13 @@ WORKLOAD = ("cfg1: Llama-16L (d 2048, 32/8 heads, FFN 8192, V 32000) Q8_0 from s
             f"{REQUESTS} requests x {TOKENS} tokens per GPU, one choose question over {OPTIONS} single-token options")
 
 
+# DRAM bytes (read + write) per GEMM launch at the benchmark size: in one ncu
+# capture of the 16-request case the layer's four GEMM launches moved
+# 1091 MB; every term grows with the token rows, so x4 for 64 requests,
+# averaged over the four launches.
+GEMM_TRAFFIC_BYTES = 1091e6 * 4 / 4
+
+
 def gemm_flops_per_token(cfg) -> float:
     """Algorithmic GEMM FLOPs per prompt token: 2 x the layer matrix parameters."""
     return 2.0 * cfg.matrix_params()
@@ -272,7 +279,8 @@ def run_ours(args):
         "prefill_tok_s": value * TOKENS,
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all prefill GEMMs)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "frac": (achieved / peak) if achieved else None, "traffic": GEMM_TRAFFIC_BYTES,
+                     "traffic_unit": "bytes per GEMM launch (ncu DRAM read+write, 16-request capture x 4)",
                      "peak_kind": f"{pk_kind} bf16 dense sustained", "launches": gemm_launches,
                      "share_of_step": round(gemm_ms / dev_ms, 4) if dev_ms else None,
                      "flops_per_step": gemm_flops / args.steps},

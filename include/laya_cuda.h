@@ -4,7 +4,7 @@
  * The library owns all device memory; callers own every host buffer they
  * pass.  Only C types cross this boundary (no CUDA or torch types), so the
  * reference engine's Rust side can bind it with plain `extern "C"`
- * declarations (see INTEGRATION.md).
+ * declarations.
  *
  * Status codes: 0 on success, a negative LAYA_E_* otherwise; the message of
  * the last failure on the calling thread is returned by laya_last_error().
