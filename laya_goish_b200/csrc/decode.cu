@@ -20,6 +20,8 @@
 #include "gemm.h"
 #include "gemv.h"
 #include "launch.h"
+#include "mma.cuh"
+#include "ptx.cuh"
 
 namespace laya {
 
@@ -732,6 +734,187 @@ __global__ void __launch_bounds__(128) attn_dec2_kernel(const half* __restrict__
   }
 }
 
+// Decode attention for a GQA group of G <= 8 query heads over whole 64-token
+// pages, one CTA per (sequence, kv head, split of pages).  A producer warp
+// streams each page's K and V blocks into a shared-memory ring with 2-D
+// tensor-map loads (64 rows x 128 B boxes, 128-byte swizzle); consumer warp
+// w takes pages w, w+4, ... of the split, each with its own online softmax
+// (src/models/openthai/model.rs:276-294), and the group's heads are the rows
+// of mma.sync m16n8k16 tiles (S = Q.K^T, then P.V).  The four warps' states
+// are merged in shared memory and written as one split partial in the form
+// attn_combine_kernel reads (max in log2 units, sum, unnormalised output).
+__device__ __forceinline__ int kv_off(int r, int c) {  // byte offset of 16-byte chunk c of page row r
+  return (c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+template <int HD>
+struct Dec3 {
+  static constexpr int NW = 4;                    // consumer warps
+  static constexpr int S = HD == 64 ? 8 : 4;      // ring stages (pages)
+  static constexpr int PAGE_BYTES = 64 * HD * 2;  // K or V of one page
+  static constexpr int STAGE = 2 * PAGE_BYTES;
+  static constexpr int SMEM = S * STAGE + 2 * S * 8 + NW * 8 * (HD + 2) * 4 + 1024;
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(160, 1)
+    attn_dec3_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                     const half* __restrict__ q, const int* __restrict__ tables, const DecSeq* __restrict__ seqs,
+                     int KV, float scale_log2, int split_pages, int splits, float* __restrict__ part,
+                     unsigned* err, long long budget) {
+  using C = Dec3<HD>;
+  extern __shared__ uint8_t d3_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(d3_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::S * C::STAGE);
+  uint64_t* empty = full + C::S;
+  float* comb = reinterpret_cast<float*>(empty + C::S);  // [NW][8][HD + 2]
+  const int b = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
+  const int H = KV * G;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::S; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the step's K/V rows were appended by the previous kernel
+  pdl_trigger();
+  const DecSeq s = seqs[b];
+  const int n_pages = (s.n_keys + PAGE - 1) / PAGE;
+  const int p0 = sp * split_pages, p1 = min(n_pages, p0 + split_pages);
+  const int np = max(0, p1 - p0);
+  const int g = lane >> 2, t = lane & 3;
+  if (warp == C::NW) {
+    if (lane == 0) {
+      for (int i = 0; i < np; i++) {
+        const int st = i % C::S;
+        if (!mbar_wait(&empty[st], ((i / C::S) & 1) ^ 1, budget)) atomicOr(err, 1024u);
+        const int row = (tables[s.table_off + p0 + i] * KV + kvh) * PAGE;
+        uint8_t* dst = sm + st * C::STAGE;
+        mbar_expect_tx(&full[st], C::STAGE);
+#pragma unroll
+        for (int hb = 0; hb < HD / 64; hb++) {
+          tma_load_2d(dst + hb * 8192, &tk, &full[st], hb * 64, row);
+          tma_load_2d(dst + C::PAGE_BYTES + hb * 8192, &tv, &full[st], hb * 64, row);
+        }
+      }
+    }
+  } else {
+    // Q of head g of the group as the A fragment (rows g + 8 are zero)
+    uint32_t qa[HD / 16][4];
+    const half* qg = q + ((size_t)b * H + kvh * G + (g < G ? g : 0)) * HD;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; kk++) {
+      qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qg + kk * 16 + 2 * t) : 0u;
+      qa[kk][1] = 0u;
+      qa[kk][2] = g < G ? *reinterpret_cast<const uint32_t*>(qg + kk * 16 + 8 + 2 * t) : 0u;
+      qa[kk][3] = 0u;
+    }
+    float m = -INFINITY, l = 0.f;  // m in raw score units
+    float acc[HD / 8][4];
+#pragma unroll
+    for (int i = 0; i < HD / 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (int i = warp; i < np; i += C::NW) {
+      const int st = i % C::S;
+      if (!mbar_wait(&full[st], (i / C::S) & 1, budget) && lane == 0) atomicOr(err, 2048u);
+      const uint8_t* sK = sm + st * C::STAGE;
+      const uint8_t* sV = sK + C::PAGE_BYTES;
+      float sc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; kk++) {
+#pragma unroll
+        for (int nj = 0; nj < 8; nj += 2) {
+          uint32_t bf[4];
+          const int mat = lane / 8;
+          ldsm_x4(bf, sK + kv_off(nj * 8 + (lane % 8) + (mat / 2) * 8, kk * 2 + (mat % 2)));
+          mma16816(sc[nj], qa[kk], bf[0], bf[1]);
+          mma16816(sc[nj + 1], qa[kk], bf[2], bf[3]);
+        }
+      }
+      const int key0 = (p0 + i) * PAGE;
+      if (key0 + PAGE > s.n_keys) {
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+          for (int e = 0; e < 2; e++)
+            if (key0 + j * 8 + 2 * t + e >= s.n_keys) sc[j][e] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; j++) mx = fmaxf(mx, fmaxf(sc[j][0], sc[j][1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      // every page of the split holds at least one key, so mn is finite
+      const float mn = fmaxf(m, mx);
+      const float corr = exp2f((m - mn) * scale_log2), off = -mn * scale_log2;
+      m = mn;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        sc[j][0] = exp2f(fmaf(sc[j][0], scale_log2, off));
+        sc[j][1] = exp2f(fmaf(sc[j][1], scale_log2, off));
+        sum += sc[j][0] + sc[j][1];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      l = l * corr + sum;
+#pragma unroll
+      for (int d = 0; d < HD / 8; d++) {
+        acc[d][0] *= corr;
+        acc[d][1] *= corr;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const uint32_t pa[4] = {pack_h2(sc[2 * kk][0], sc[2 * kk][1]), 0u, pack_h2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
+                                0u};
+#pragma unroll
+        for (int nd = 0; nd < HD / 8; nd += 2) {
+          uint32_t bf[4];
+          const int mat = lane / 8;
+          ldsm_x4_t(bf, sV + kv_off(kk * 16 + (lane % 8) + (mat % 2) * 8, nd + mat / 2));
+          mma16816(acc[nd], pa, bf[0], bf[1]);
+          mma16816(acc[nd + 1], pa, bf[2], bf[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (g < G) {
+      float* cw = comb + (warp * 8 + g) * (HD + 2);
+      if (t == 0) {
+        cw[0] = m == -INFINITY ? -INFINITY : m * scale_log2;
+        cw[1] = l;
+      }
+#pragma unroll
+      for (int d = 0; d < HD / 8; d++) {
+        cw[2 + d * 8 + 2 * t] = acc[d][0];
+        cw[2 + d * 8 + 2 * t + 1] = acc[d][1];
+      }
+    }
+  }
+  __syncthreads();
+  // merge the consumer warps: one split partial per head of the group
+  for (int idx = threadIdx.x; idx < G * (HD + 2); idx += blockDim.x) {
+    const int gg = idx / (HD + 2), c = idx % (HD + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < C::NW; w++) M = fmaxf(M, comb[(w * 8 + gg) * (HD + 2)]);
+    float v = c == 0 ? M : 0.f;
+    if (c > 0 && M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < C::NW; w++) {
+        const float mw = comb[(w * 8 + gg) * (HD + 2)];
+        if (mw != -INFINITY) v += exp2f(mw - M) * comb[(w * 8 + gg) * (HD + 2) + c];
+      }
+    }
+    part[(((size_t)b * H + kvh * G + gg) * splits + sp) * (HD + 2) + c] = v;
+  }
+}
+
 // Merges the key splits: o = sum_s 2^(m_s - M) acc_s / sum_s 2^(m_s - M) l_s.
 // The split weights are computed once into shared memory; then the threads
 // (dims x split subsets) sum independent, coalesced loads.
@@ -794,7 +977,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int H, int H
 // ---------------------------------------------------------------- host
 
 struct AttnShape {
-  int splits, split_pages;
+  int splits, split_pages;    // attn_dec2_kernel
+  int splits3, split_pages3;  // attn_dec3_kernel: one CTA per SM, so at most one wave of CTAs
 };
 
 static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_keys) {
@@ -802,7 +986,31 @@ static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_k
   int splits = std::max(1, (4 * r.num_sms + nb * c.KV - 1) / (nb * c.KV));
   splits = std::min(splits, pages);
   const int split_pages = (pages + splits - 1) / splits;
-  return {(pages + split_pages - 1) / split_pages, split_pages};
+  int s3 = std::max(1, std::min(r.num_sms / (nb * c.KV), (pages + 1) / 2));
+  const int sp3 = (pages + s3 - 1) / s3;
+  return {(pages + split_pages - 1) / split_pages, split_pages, (pages + sp3 - 1) / sp3, sp3};
+}
+
+static bool dec3_enabled() {
+  const char* e = std::getenv("LAYA_DEC_ATTN3");
+  return !(e && e[0] == '0');
+}
+
+template <int HD, int G>
+static cudaError_t launch_dec3(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
+                               const half* q, const int* tables, const DecSeq* seqs, int KV, float sl2,
+                               int split_pages, int splits, float* part, unsigned* err) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_dec3_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, Dec3<HD>::SMEM);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
+  }
+  return launch_k(attn_dec3_kernel<HD, G>, grid, dim3(160), (size_t)Dec3<HD>::SMEM, st, true, tk, tv, q, tables,
+                  seqs, KV, sl2, split_pages, splits, part, err, 4000000000ll);
 }
 
 template <int HD, int G>
@@ -827,15 +1035,41 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
   const Config& c = m.cfg;
   const float sl2 = (1.f / sqrtf((float)c.hd)) * 1.4426950408889634f;
   const int G = c.H / c.KV;
-  const dim3 grid(nb, c.KV, sh.splits);
   cudaEvent_t a;
   prof_begin(r, P_ATTN_DEC, &a);
   r.launches += 2;
   cudaError_t e = cudaErrorNotSupported;
   const int* tb = r.tables.as<int>();
   float* part = r.dpart.as<float>();
+  int splits = sh.splits;
+  if (dec3_enabled() && G <= 8 && (c.hd == 64 || c.hd == 128)) {
+    // K and V of this layer as [pages * kv_heads * 64 rows][hd] F16, 64 x 64 boxes
+    CUtensorMap tk, tv;
+    const uint64_t dims[2] = {(uint64_t)c.hd, (uint64_t)r.kv_pages * c.KV * PAGE}, strides[1] = {(uint64_t)c.hd * 2};
+    const uint32_t box[2] = {64, 64};
+    if (!encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(LAYA_E_CUDA, "KV tensor map");
+    const dim3 g3(nb, c.KV, sh.splits3);
+    splits = sh.splits3;
+#define LAYA_DEC3(HDV, GV)                                                                                 \
+  if (c.hd == HDV && G == GV)                                                                              \
+    e = launch_dec3<HDV, GV>(g3, r.stream, tk, tv, q, tb, seqs, c.KV, sl2, sh.split_pages3, sh.splits3, part, \
+                             r.err);
+    LAYA_DEC3(64, 1)
+    LAYA_DEC3(64, 2)
+    LAYA_DEC3(64, 4)
+    LAYA_DEC3(64, 8)
+    LAYA_DEC3(128, 1)
+    LAYA_DEC3(128, 2)
+    LAYA_DEC3(128, 4)
+    LAYA_DEC3(128, 7)
+    LAYA_DEC3(128, 8)
+#undef LAYA_DEC3
+  }
+  const dim3 grid(nb, c.KV, sh.splits);
 #define LAYA_DEC2(HDV, GV)                                                                                         \
-  if (c.hd == HDV && G == GV)                                                                                      \
+  if (e == cudaErrorNotSupported && c.hd == HDV && G == GV)                                                       \
     e = launch_dec2<HDV, GV>(grid, r.stream, q, kc, vc, tb, seqs, c.KV, sl2, sh.split_pages, sh.splits, part);
   LAYA_DEC2(64, 1)
   LAYA_DEC2(64, 2)
@@ -850,8 +1084,8 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
   if (e == cudaErrorNotSupported) return fail(LAYA_E_INVALID, "unsupported head grouping for decode");
   if (e != cudaSuccess) return cuda_fail(e, "attn_dec2_kernel");
   const int cthreads = c.hd <= 64 ? 256 : 256;
-  LAYA_CK(launch_k(attn_combine_kernel, dim3(nb, c.H), dim3(cthreads), (size_t)(sh.splits + cthreads) * 4, r.stream,
-                   true, (const float*)part, c.H, c.hd, sh.splits, out));
+  LAYA_CK(launch_k(attn_combine_kernel, dim3(nb, c.H), dim3(cthreads), (size_t)(splits + cthreads) * 4, r.stream,
+                   true, (const float*)part, c.H, c.hd, splits, out));
   prof_end(r, P_ATTN_DEC, a);
   return 0;
 }

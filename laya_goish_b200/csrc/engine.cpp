@@ -515,6 +515,11 @@ int ensure_kv(Model& m, Replica& r, int pages) {
   r.vc.release();
   if (int rc = r.kc.ensure(bytes)) return rc;
   if (int rc = r.vc.ensure(bytes)) return rc;
+  // Attention kernels read whole pages and weight the unused slots of a
+  // sequence's last page by zero: start from zeros so those slots hold no
+  // Inf/NaN bit patterns (0 x Inf would poison the sum).
+  LAYA_CK(cudaMemsetAsync(r.kc.p, 0, bytes, r.stream));
+  LAYA_CK(cudaMemsetAsync(r.vc.p, 0, bytes, r.stream));
   r.kv_pages = want;
   return 0;
 }
