@@ -189,7 +189,7 @@ int laya_forward(laya_model* h, const int32_t* ids, int n, const int32_t* read, 
     p.pos.push_back(t);
     p.slot.push_back(t);
   }
-  for (int t0 = 0; t0 < n; t0 += 64) p.items.push_back({t0, std::min(64, n - t0), t0, 0});
+  for (int t0 = 0; t0 < n; t0 += kAttnRows) p.items.push_back({t0, std::min(kAttnRows, n - t0), t0, 0});
   p.read_rows.assign(read, read + nread);
   int rc;
   if ((rc = ensure_kv(m, r, pages)) || (rc = r.hid32.ensure((size_t)nread * c.d * 4)) ||

@@ -1515,7 +1515,7 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
       pre.pos.push_back(t);
       pre.slot.push_back(tables[toff[i] + t / PAGE] * PAGE + t % PAGE);
     }
-    for (int t0 = 0; t0 < len; t0 += 64) pre.items.push_back({row0 + t0, std::min(64, len - t0), t0, toff[i]});
+    for (int t0 = 0; t0 < len; t0 += kAttnRows) pre.items.push_back({row0 + t0, std::min(kAttnRows, len - t0), t0, toff[i]});
     pre.read_rows.push_back(row0 + len - 1);
     max_keys = std::max(max_keys, len + steps);
   }

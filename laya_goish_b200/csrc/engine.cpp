@@ -660,6 +660,9 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       ap.KV = c.KV;
       ap.hd = c.hd;
       ap.scale_log2 = scale_log2;
+      ap.q_rows = M;
+      ap.kv_rows = r.kv_pages * c.KV * PAGE;
+      ap.err = r.err;
       ProfScope ps(r, P_ATTN);
       r.launches++;
       LAYA_CK(attention(ap, st));
@@ -869,7 +872,7 @@ int decide_shard(Model& m, Replica& r, const laya_batch& b, int r0, int r1, laya
         pre.pos.push_back(t);
         pre.slot.push_back(tables[toff + t / PAGE] * PAGE + t % PAGE);
       }
-      for (int t0 = 0; t0 < len; t0 += 64) pre.items.push_back({row0 + t0, std::min(64, len - t0), t0, toff});
+      for (int t0 = 0; t0 < len; t0 += kAttnRows) pre.items.push_back({row0 + t0, std::min(kAttnRows, len - t0), t0, toff});
       for (int qi = 0; qi < nq; qi++) {
         const laya_question& Q = b.questions[qi];
         if (Q.suffix_len) continue;
@@ -911,7 +914,7 @@ int decide_shard(Model& m, Replica& r, const laya_batch& b, int r0, int r1, laya
             br.pos.push_back(pos);
             br.slot.push_back(tables[toff + pos / PAGE] * PAGE + pos % PAGE);
           }
-          for (int u0 = 0; u0 < blen; u0 += 64) br.items.push_back({row0 + u0, std::min(64, blen - u0), plen + u0, toff});
+          for (int u0 = 0; u0 < blen; u0 += kAttnRows) br.items.push_back({row0 + u0, std::min(kAttnRows, blen - u0), plen + u0, toff});
           auto term = [&](int o) -> std::vector<Term>& {
             return terms[((size_t)ri * nq + qi) * LAYA_MAX_OPTIONS + o];
           };

@@ -1,6 +1,7 @@
 // Memory-bound kernels of the decision hot path and the paged causal GQA
 // attention.  Each cites the reference function it replaces.
 #include <cfloat>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -329,7 +330,13 @@ __global__ void __launch_bounds__(128) attn_kernel(const half* __restrict__ q, i
   half* sQ = reinterpret_cast<half*>(smem_attn);
   half* sK = sQ + BQ * HD;
   half* sV = sK + 2 * BKV * HD;
-  const AttnItem it = items[blockIdx.x];
+  // an item holds up to kAttnRows rows; this CTA takes the 64-row half blockIdx.z
+  AttnItem it = items[blockIdx.x];
+  it.q_row += 64 * blockIdx.z;
+  it.pos0 += 64 * blockIdx.z;
+  it.q_len -= 64 * blockIdx.z;
+  if (it.q_len <= 0) return;
+  if (it.q_len > 64) it.q_len = 64;
   const int h = blockIdx.y, kvh = h / (H / KV);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_keys = it.pos0 + it.q_len;
@@ -498,13 +505,23 @@ static cudaError_t attn_launch(const AttnParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured[dev & 63] = true;
   }
-  attn_kernel<HD><<<dim3(p.n_items, p.H), 128, smem, st>>>(p.q, p.ldq, p.o, p.ldo, p.kc, p.vc, p.tables, p.items, p.H,
-                                                             p.KV, p.scale_log2);
+  attn_kernel<HD><<<dim3(p.n_items, p.H, kAttnRows / 64), 128, smem, st>>>(p.q, p.ldq, p.o, p.ldo, p.kc, p.vc,
+                                                                            p.tables, p.items, p.H, p.KV,
+                                                                            p.scale_log2);
   return cudaGetLastError();
+}
+
+static bool attn_tc_enabled() {
+  const char* e = std::getenv("LAYA_ATTN_TC");
+  return !(e && e[0] == '0');
 }
 
 cudaError_t attention(const AttnParams& p, cudaStream_t st) {
   if (!p.n_items) return cudaSuccess;
+  if (attn_tc_enabled()) {
+    const cudaError_t e = attention_tc(p, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (p.hd == 64) return attn_launch<64>(p, st);
   if (p.hd == 128) return attn_launch<128>(p, st);
   return cudaErrorInvalidValue;

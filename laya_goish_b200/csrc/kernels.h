@@ -13,8 +13,11 @@ namespace laya {
 // One attention work unit: query rows [q_row, q_row + q_len) of one sequence
 // at absolute positions pos0.., attending keys 0 .. pos0+q_len-1 through the
 // page list tables[table_off ..] (one 64-token page per key block).
+// Query rows per attention work item (one sequence's consecutive rows).
+constexpr int kAttnRows = 128;
+
 struct AttnItem {
-  int q_row, q_len, pos0, table_off;
+  int q_row, q_len, pos0, table_off;  // q_len <= kAttnRows
 };
 
 struct AttnParams {
@@ -28,7 +31,14 @@ struct AttnParams {
   const AttnItem* items;
   int n_items, H, KV, hd;
   float scale_log2;
+  int q_rows;     // rows of q / o
+  int kv_rows;    // rows of kc / vc: pages * KV * 64
+  unsigned* err;  // device error word (bounded waits)
 };
+
+// tcgen05 attention (attn_tc.cu); cudaErrorNotSupported for head dims it
+// does not cover.
+cudaError_t attention_tc(const AttnParams& p, cudaStream_t st);
 
 cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st);
 cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstride, int goff, cudaStream_t st);
