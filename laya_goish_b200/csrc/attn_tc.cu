@@ -3,8 +3,8 @@
 // j <= i, then .v, with kv head = h / (H/KV)), flash-style over the paged
 // KV cache.
 //
-// One CTA = up to 128 query rows of one sequence x one query head,
-// 192 threads:
+// Work unit = up to 128 query rows of one sequence x one query head; a
+// persistent CTA (192 threads) runs a strided list of units:
 //   warp 0     : TMA producer: the Q tile once, then each 64-key page's K and
 //                V blocks into a ring (64 x 128 B boxes, 128-byte swizzle)
 //   warp 1     : allocates TMEM; one thread issues S_j = Q.K_j^T (M 128,
@@ -24,6 +24,8 @@
 // page j-1 unambiguously; the final read of O waits on its own barrier.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm.h"
 #include "kernels.h"
@@ -34,18 +36,30 @@ namespace laya {
 
 template <int HD>
 struct Atc {
-  static constexpr int NS = HD == 64 ? 3 : 3;      // K/V ring stages (pages)
+  // K pages are released as soon as their S MMA is done, V pages only after
+  // their P.V MMA, so the K ring is the deeper one.
+  static constexpr int NK = 3;
+  static constexpr int NV = HD == 64 ? 2 : 3;
   static constexpr int Q_BYTES = 128 * HD * 2;     // [HD/64 blocks][128 rows][128 B]
   static constexpr int KV_BYTES = 64 * HD * 2;     // K or V page: [HD/64 blocks][64 rows][128 B]
-  static constexpr int STAGE = 2 * KV_BYTES;
   static constexpr int P_BYTES = 128 * 64 * 2;     // [128 rows][64 keys] F16
-  static constexpr int OFF_KV = Q_BYTES;
-  static constexpr int OFF_P = OFF_KV + NS * STAGE;
+  static constexpr int OFF_K = 2 * Q_BYTES;        // two Q buffers
+  static constexpr int OFF_V = OFF_K + NK * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + NV * KV_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = 256;            // S buffers at 0 and 64, O at 128
+  static constexpr int TMEM_COLS = HD == 64 ? 256 : 512;  // S buffers at 0, 64; O buffers at 128, 128 + HD
   static constexpr int O_COL = 128;
+  static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
 };
+
+// 2^x with the SFU's approximate exponent (PTX ex2.approx.ftz: relative
+// error ~2^-22, far below the F16 rounding of P); 2^-inf = 0.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // K-major operand descriptor of k-step kk (16 elements) of a tile stored as
 // 64-element (128-byte) column blocks `block_bytes` apart.
@@ -53,46 +67,73 @@ __device__ __forceinline__ uint64_t kdesc(const uint8_t* base, int kk, int block
   return sw128_desc(smem_u32(base + (kk >> 2) * block_bytes + (kk & 3) * 32));
 }
 
+struct AtcUnit {
+  AttnItem it;
+  int h, kvh, n_keys, nblk;
+};
+
+__device__ __forceinline__ AtcUnit atc_unit(const AttnItem* items, int u, int H, int KV) {
+  AtcUnit w;
+  w.it = items[u / H];
+  w.h = u % H;
+  w.kvh = w.h / (H / KV);
+  w.n_keys = w.it.pos0 + w.it.q_len;
+  w.nblk = (w.n_keys + 63) / 64;
+  return w;
+}
+
+// Persistent: CTA c takes work units u = c, c + gridDim.x, ... with
+// u = item * H + head (CTAs running together share K/V pages in L2).  All
+// ring, buffer and barrier indices run over the CTA's global page count g
+// and unit count k, so the producer fetches the next unit's Q and pages
+// while the current unit is still being computed.
 template <int HD>
 __global__ void __launch_bounds__(192, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, half* __restrict__ o, int ldo,
-                   const int* __restrict__ tables, const AttnItem* __restrict__ items, int H, int KV,
+                   const int* __restrict__ tables, const AttnItem* __restrict__ items, int n_units, int H, int KV,
                    float scale_log2, unsigned* err, long long budget) {
   using C = Atc<HD>;
   extern __shared__ uint8_t at_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = sm;
-  uint8_t* sKV = sm + C::OFF_KV;
+  uint8_t* sK = sm + C::OFF_K;
+  uint8_t* sV = sm + C::OFF_V;
   uint8_t* sP = sm + C::OFF_P;
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + C::NS;
-  uint64_t* s_full = kv_empty + C::NS;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_done = p_full + 2;   // one phase per P.V page
-  uint64_t* o_final = o_done + 1;  // the last P.V
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);  // [2] Q of unit k in buffer k & 1
+  uint64_t* q_empty = q_full + 2;                                   // [2] the unit's last S MMA is done
+  uint64_t* k_full = q_empty + 2;                                   // [NK] K of page g in stage g % NK
+  uint64_t* k_empty = k_full + C::NK;                               // [NK] its S MMA is done
+  uint64_t* v_full = k_empty + C::NK;                               // [NV] V of page g in stage g % NV
+  uint64_t* v_empty = v_full + C::NV;                               // [NV] its P.V MMA is done
+  uint64_t* s_full = v_empty + C::NV;                               // [2] S of page g in buffer g & 1
+  uint64_t* s_empty = s_full + 2;                                   // [2] 4 softmax warps read it
+  uint64_t* p_full = s_empty + 2;                                   // [2] P of page g written (4 warps)
+  uint64_t* o_done = p_full + 2;                                    // one phase per P.V page
+  uint64_t* o_full = o_done + 1;                                    // [2] O of unit k complete
+  uint64_t* o_empty = o_full + 2;                                   // [2] O of unit k read (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
 
-  const AttnItem it = items[blockIdx.x];
-  const int h = blockIdx.y, kvh = h / (H / KV);
-  const int n_keys = it.pos0 + it.q_len;
-  const int nblk = (n_keys + 63) / 64;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < C::NS; s++) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
     for (int b = 0; b < 2; b++) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
       mbar_init(&s_full[b], 1);
       mbar_init(&s_empty[b], 4);
       mbar_init(&p_full[b], 4);
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_empty[b], 4);
+    }
+    for (int i = 0; i < C::NK; i++) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < C::NV; i++) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     mbar_init(o_done, 1);
-    mbar_init(o_final, 1);
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -106,164 +147,200 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, C::Q_BYTES);
+      int g = 0;
+      for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
+        const AtcUnit w = atc_unit(items, u, H, KV);
+        const int qb = k & 1;
+        if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
+        mbar_expect_tx(&q_full[qb], C::Q_BYTES);
 #pragma unroll
-      for (int hb = 0; hb < HD / 64; hb++) tma_load_2d(sQ + hb * 16384, &tq, q_full, h * HD + hb * 64, it.q_row);
-      for (int j = 0; j < nblk; j++) {
-        const int st = j % C::NS;
-        if (!mbar_wait(&kv_empty[st], ((j / C::NS) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
-        const int row = (tables[it.table_off + j] * KV + kvh) * 64;
-        uint8_t* dst = sKV + st * C::STAGE;
-        mbar_expect_tx(&kv_full[st], C::STAGE);
+        for (int hb = 0; hb < HD / 64; hb++)
+          tma_load_2d(sQ + qb * C::Q_BYTES + hb * 16384, &tq, &q_full[qb], w.h * HD + hb * 64, w.it.q_row);
+        for (int j = 0; j < w.nblk; j++, g++) {
+          const int row = (tables[w.it.table_off + j] * KV + w.kvh) * 64;
+          const int ks = g % C::NK, vs = g % C::NV;
+          if (!mbar_wait(&k_empty[ks], ((g / C::NK) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
+          mbar_expect_tx(&k_full[ks], C::KV_BYTES);
 #pragma unroll
-        for (int hb = 0; hb < HD / 64; hb++) {
-          tma_load_2d(dst + hb * 8192, &tk, &kv_full[st], hb * 64, row);
-          tma_load_2d(dst + C::KV_BYTES + hb * 8192, &tv, &kv_full[st], hb * 64, row);
+          for (int hb = 0; hb < HD / 64; hb++)
+            tma_load_2d(sK + ks * C::KV_BYTES + hb * 8192, &tk, &k_full[ks], hb * 64, row);
+          if (!mbar_wait(&v_empty[vs], ((g / C::NV) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
+          mbar_expect_tx(&v_full[vs], C::KV_BYTES);
+#pragma unroll
+          for (int hb = 0; hb < HD / 64; hb++)
+            tma_load_2d(sV + vs * C::KV_BYTES + hb * 8192, &tv, &v_full[vs], hb * 64, row);
         }
       }
-      // Drain: the last use of every stage is released (its P.V finished)
+      // Drain: the last use of every stage is released (its MMA finished)
       // before the CTA may exit, so no MMA completion arrives afterwards.
-      for (int j = nblk - 1; j >= 0 && j >= nblk - C::NS; j--)
-        if (!mbar_wait(&kv_empty[j % C::NS], (j / C::NS) & 1, budget)) atomicOr(err, 1u << 20);
+      for (int x = g - 1; x >= 0 && x >= g - C::NK; x--)
+        if (!mbar_wait(&k_empty[x % C::NK], (x / C::NK) & 1, budget)) atomicOr(err, 1u << 20);
+      for (int x = g - 1; x >= 0 && x >= g - C::NV; x--)
+        if (!mbar_wait(&v_empty[x % C::NV], (x / C::NV) & 1, budget)) atomicOr(err, 1u << 20);
     }
   } else if (warp == 1) {
     if (elect_one()) {
       const uint32_t idS = idesc_f16_f32(128, 64);
       const uint32_t idO = idesc_f16_f32(128, HD) | (1u << 16);  // B (V) MN-major
-      if (!mbar_wait(q_full, 0, budget)) atomicOr(err, 1u << 13);
-      tc_fence_after();
-      for (int j = 0; j <= nblk; j++) {
-        if (j < nblk) {
-          const int st = j % C::NS, sb = j & 1;
-          if (!mbar_wait(&kv_full[st], (j / C::NS) & 1, budget)) atomicOr(err, 1u << 14);
-          if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, budget)) atomicOr(err, 1u << 15);
+      // P.V of page pg (stage pst) into O buffer pob; first / last page of its unit
+      int pg = -1, pob = 0, pk = 0;
+      bool pfirst = false, plast = false;
+      auto issue_pv = [&]() {
+        const int pb = pg & 1;
+        if (pfirst && !mbar_wait(&o_empty[pob], ((pk >> 1) & 1) ^ 1, budget)) atomicOr(err, 1u << 16);
+        const int vs = pg % C::NV;
+        if (!mbar_wait(&p_full[pb], (pg >> 1) & 1, budget)) atomicOr(err, 1u << 16);
+        if (!mbar_wait(&v_full[vs], (pg / C::NV) & 1, budget)) atomicOr(err, 1u << 16);
+        tc_fence_after();
+        const uint8_t* v = sV + vs * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          umma_f16(tbase + C::O_COL + pob * HD, sw128_desc(smem_u32(sP + pb * C::P_BYTES + kk * 32)),
+                   sw128_mn_desc(smem_u32(v + kk * 2048), 8192, 1024), idO, (!pfirst || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[vs]);
+        umma_commit(o_done);
+        if (plast) umma_commit(&o_full[pob]);
+      };
+      int g = 0;
+      for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
+        const AtcUnit w = atc_unit(items, u, H, KV);
+        const int qb = k & 1;
+        if (!mbar_wait(&q_full[qb], (k >> 1) & 1, budget)) atomicOr(err, 1u << 13);
+        for (int j = 0; j < w.nblk; j++, g++) {
+          const int ks = g % C::NK, sb = g & 1;
+          if (!mbar_wait(&k_full[ks], (g / C::NK) & 1, budget)) atomicOr(err, 1u << 14);
+          if (!mbar_wait(&s_empty[sb], ((g >> 1) & 1) ^ 1, budget)) atomicOr(err, 1u << 15);
           tc_fence_after();
-          const uint8_t* sK = sKV + st * C::STAGE;
 #pragma unroll
           for (int kk = 0; kk < HD / 16; kk++)
-            umma_f16(tbase + sb * 64, kdesc(sQ, kk, 16384), kdesc(sK, kk, 8192), idS, kk > 0 ? 1u : 0u);
+            umma_f16(tbase + sb * 64, kdesc(sQ + qb * C::Q_BYTES, kk, 16384), kdesc(sK + ks * C::KV_BYTES, kk, 8192),
+                     idS, kk > 0 ? 1u : 0u);
           umma_commit(&s_full[sb]);
-        }
-        if (j >= 1) {
-          const int jj = j - 1, st = jj % C::NS, pb = jj & 1;
-          if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, budget)) atomicOr(err, 1u << 16);
-          tc_fence_after();
-          const uint8_t* sV = sKV + st * C::STAGE + C::KV_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            umma_f16(tbase + C::O_COL, sw128_desc(smem_u32(sP + pb * C::P_BYTES + kk * 32)),
-                     sw128_mn_desc(smem_u32(sV + kk * 2048), 8192, 1024), idO, (jj > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&kv_empty[st]);
-          umma_commit(o_done);
-          if (jj == nblk - 1) umma_commit(o_final);
+          umma_commit(&k_empty[ks]);
+          if (j == w.nblk - 1) umma_commit(&q_empty[qb]);
+          if (pg >= 0) issue_pv();
+          pg = g;
+          pob = k & 1;
+          pk = k;
+          pfirst = j == 0;
+          plast = j == w.nblk - 1;
         }
       }
+      if (pg >= 0) issue_pv();
     }
   } else {
     // softmax: thread = query row r = TMEM lane r
     const int quarter = warp % 4, r = quarter * 32 + lane;
-    const int pos = it.pos0 + r;
     const uint32_t tl = tbase + ((uint32_t)(quarter * 32) << 16);
-    float mref = -INFINITY, l = 0.f;  // reference maximum in log2 units
-    for (int j = 0; j < nblk; j++) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, budget) && lane == 0) atomicOr(err, 1u << 17);
+    int g = 0;
+    for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
+      const AtcUnit w = atc_unit(items, u, H, KV);
+      const int ob = k & 1;
+      const int pos = w.it.pos0 + r;
+      float mref = -INFINITY, l = 0.f;  // reference maximum in log2 units
+      for (int j = 0; j < w.nblk; j++, g++) {
+        const int sb = g & 1;
+        if (!mbar_wait(&s_full[sb], (g >> 1) & 1, budget) && lane == 0) atomicOr(err, 1u << 17);
+        tc_fence_after();
+        uint32_t v0[32], v1[32];
+        __syncwarp();
+        tmem_ld32(tl + sb * 64, v0);
+        tmem_ld32(tl + sb * 64 + 32, v1);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[sb]);
+        float s[64];
+#pragma unroll
+        for (int c = 0; c < 32; c++) {
+          s[c] = __uint_as_float(v0[c]);
+          s[32 + c] = __uint_as_float(v1[c]);
+        }
+        const int key0 = j * 64;
+        if (key0 + 63 > w.it.pos0 || key0 + 64 > w.n_keys) {
+          // keys key0 + c with c > lim are masked (causal, and past the last key)
+          const int lim = min(pos, w.n_keys - 1) - key0;
+#pragma unroll
+          for (int c = 0; c < 64; c++) s[c] = c > lim ? -INFINITY : s[c];
+        }
+        float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int c = 4; c < 64; c++) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+        // raw scores; the scale is positive, so the maximum commutes with it
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2;
+        // Page 0 holds key 0 <= every position, so mref is finite from j = 0
+        // on.  A row moves its reference when its maximum exceeds it by more
+        // than 8 (P stays <= 2^8); the warp rescales its rows of O together,
+        // because TMEM loads and stores are warp-wide.
+        const float nref = mx > mref + 8.f ? mx : mref;
+        const float corr = ex2(mref - nref);  // 1 when unchanged; unused at j = 0
+        if (j > 0 && __any_sync(0xffffffffu, nref != mref)) {
+          // O holds P.V of this unit's pages < j once page g-1's MMA is done
+          if (!mbar_wait(o_done, (g - 1) & 1, budget) && lane == 0) atomicOr(err, 1u << 18);
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 32; c++) {
+            uint32_t v[32];
+            __syncwarp();
+            tmem_ld32(tl + C::O_COL + ob * HD + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
+            tmem_st32(tl + C::O_COL + ob * HD + c * 32, v);
+          }
+          tmem_st_wait();
+          l *= corr;
+        }
+        mref = nref;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 64; c++) {
+          s[c] = ex2(fmaf(s[c], scale_log2, -mref));
+          l4[c & 3] += s[c];
+        }
+        l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        // P row r: [128 rows][64 keys] F16, 16-byte unit u of row r at u ^ (r % 8)
+        uint8_t* prow = sP + sb * C::P_BYTES + r * 128;
+#pragma unroll
+        for (int u8 = 0; u8 < 8; u8++) {
+          uint4 pw;
+          pw.x = pack_h2(s[8 * u8], s[8 * u8 + 1]);
+          pw.y = pack_h2(s[8 * u8 + 2], s[8 * u8 + 3]);
+          pw.z = pack_h2(s[8 * u8 + 4], s[8 * u8 + 5]);
+          pw.w = pack_h2(s[8 * u8 + 6], s[8 * u8 + 7]);
+          *reinterpret_cast<uint4*>(prow + ((u8 ^ (r & 7)) << 4)) = pw;
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
+      }
+      // O of this unit
+      if (!mbar_wait(&o_full[ob], (k >> 1) & 1, budget) && lane == 0) atomicOr(err, 1u << 19);
       tc_fence_after();
-      float s[64];
-      {
+      const float inv = 1.f / l;
+#pragma unroll
+      for (int c = 0; c < HD / 32; c++) {
         uint32_t v[32];
         __syncwarp();
-        tmem_ld32(tl + sb * 64, v);
+        tmem_ld32(tl + C::O_COL + ob * HD + c * 32, v);
         tmem_ld_wait();
+        if (r < w.it.q_len) {
+          half* dst = o + (size_t)(w.it.q_row + r) * ldo + w.h * HD + c * 32;
 #pragma unroll
-        for (int c = 0; c < 32; c++) s[c] = __uint_as_float(v[c]) * scale_log2;
-        tmem_ld32(tl + sb * 64 + 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; c++) s[32 + c] = __uint_as_float(v[c]) * scale_log2;
+          for (int u4 = 0; u4 < 4; u4++) {
+            uint4 ow;
+            ow.x = pack_h2(__uint_as_float(v[8 * u4]) * inv, __uint_as_float(v[8 * u4 + 1]) * inv);
+            ow.y = pack_h2(__uint_as_float(v[8 * u4 + 2]) * inv, __uint_as_float(v[8 * u4 + 3]) * inv);
+            ow.z = pack_h2(__uint_as_float(v[8 * u4 + 4]) * inv, __uint_as_float(v[8 * u4 + 5]) * inv);
+            ow.w = pack_h2(__uint_as_float(v[8 * u4 + 6]) * inv, __uint_as_float(v[8 * u4 + 7]) * inv);
+            reinterpret_cast<uint4*>(dst)[u4] = ow;
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);
-      const int key0 = j * 64;
-      if (key0 + 63 > it.pos0 || key0 + 64 > n_keys) {
-#pragma unroll
-        for (int c = 0; c < 64; c++)
-          if (key0 + c > pos || key0 + c >= n_keys) s[c] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 64; c++) mx = fmaxf(mx, s[c]);
-      // Page 0 holds key 0 <= every position, so mref is finite from j = 0 on.
-      // A row moves its reference when its maximum exceeds it by more than 8
-      // (P stays <= 2^8); the warp rescales its rows of O together, because
-      // TMEM loads and stores are warp-wide.
-      const float nref = mx > mref + 8.f ? mx : mref;
-      const float corr = exp2f(mref - nref);  // 1 when unchanged; unused at j = 0
-      if (j > 0 && __any_sync(0xffffffffu, nref != mref)) {
-        // O holds P.V of pages < j once page j-1's MMA is done
-        if (!mbar_wait(o_done, (j - 1) & 1, budget) && lane == 0) atomicOr(err, 1u << 18);
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < HD / 32; c++) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld32(tl + C::O_COL + c * 32, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
-          tmem_st32(tl + C::O_COL + c * 32, v);
-        }
-        tmem_st_wait();
-        l *= corr;
-      }
-      mref = nref;
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; c++) {
-        s[c] = exp2f(s[c] - mref);
-        sum += s[c];
-      }
-      l += sum;
-      // P row r: [128 rows][64 keys] F16, 16-byte unit u of row r at u ^ (r % 8)
-      uint8_t* prow = sP + sb * C::P_BYTES + r * 128;
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        uint4 w;
-        w.x = pack_h2(s[8 * u], s[8 * u + 1]);
-        w.y = pack_h2(s[8 * u + 2], s[8 * u + 3]);
-        w.z = pack_h2(s[8 * u + 4], s[8 * u + 5]);
-        w.w = pack_h2(s[8 * u + 6], s[8 * u + 7]);
-        *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = w;
-      }
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
-    }
-    // (o_done's parity cannot tell page nblk-1 from nblk-3 here: at this
-    // point only the P.V of page nblk-3 is known to be done)
-    if (!mbar_wait(o_final, 0, budget) && lane == 0) atomicOr(err, 1u << 19);
-    tc_fence_after();
-    const float inv = 1.f / l;
-#pragma unroll
-    for (int c = 0; c < HD / 32; c++) {
-      uint32_t v[32];
-      __syncwarp();
-      tmem_ld32(tl + C::O_COL + c * 32, v);
-      tmem_ld_wait();
-      if (r < it.q_len) {
-        half* dst = o + (size_t)(it.q_row + r) * ldo + h * HD + c * 32;
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          uint4 w;
-          w.x = pack_h2(__uint_as_float(v[8 * u]) * inv, __uint_as_float(v[8 * u + 1]) * inv);
-          w.y = pack_h2(__uint_as_float(v[8 * u + 2]) * inv, __uint_as_float(v[8 * u + 3]) * inv);
-          w.z = pack_h2(__uint_as_float(v[8 * u + 4]) * inv, __uint_as_float(v[8 * u + 5]) * inv);
-          w.w = pack_h2(__uint_as_float(v[8 * u + 6]) * inv, __uint_as_float(v[8 * u + 7]) * inv);
-          reinterpret_cast<uint4*>(dst)[u] = w;
-        }
-      }
+      if (lane == 0) mbar_arrive(&o_empty[ob]);
     }
   }
   tc_fence_before();
@@ -285,8 +362,15 @@ static cudaError_t attn_tc_go(const AttnParams& p, const CUtensorMap& tq, const 
     if (e != cudaSuccess) return e;
     configured[dev & 63] = true;
   }
-  attn_tc_kernel<HD><<<dim3(p.n_items, p.H), 192, Atc<HD>::SMEM, st>>>(
-      tq, tk, tv, p.o, p.ldo, p.tables, p.items, p.H, p.KV, p.scale_log2, p.err, 100000000ll);
+  static int sms[64] = {0};
+  if (!sms[dev & 63]) {
+    cudaError_t e = cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  const int units = p.n_items * p.H;
+  const int grid = std::min(units, Atc<HD>::CTAS_PER_SM * sms[dev & 63]);
+  attn_tc_kernel<HD><<<grid, 192, Atc<HD>::SMEM, st>>>(tq, tk, tv, p.o, p.ldo, p.tables, p.items, units, p.H, p.KV,
+                                                       p.scale_log2, p.err, 100000000ll);
   return cudaGetLastError();
 }
 
