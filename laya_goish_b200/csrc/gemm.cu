@@ -404,7 +404,54 @@ constexpr int PAIR_STAGES = 6;
 constexpr int PA_BYTES = 128 * BK * 2;  // this CTA's 128 rows of the 256-row A tile
 constexpr int PB_BYTES = 128 * BK * 2;  // this CTA's 128 rows of the 256-row B tile
 constexpr int PAIR_SMEM = PAIR_STAGES * (PA_BYTES + PB_BYTES) + 1024 + 256;
-static_assert(PAIR_SMEM <= 227 * 1024, "pair GEMM shared memory");
+// EPI_RESID stages each epilogue warp's 32x32 F32 chunks (two 4 KB buffers
+// per warp) for TMA reduce-add into the residual stream.
+constexpr int PAIR_STG = (PAIR_STAGES * (PA_BYTES + PB_BYTES) + 256 + 1023) / 1024 * 1024;
+constexpr int PAIR_SMEM_RESID = PAIR_STG + 4 * 2 * 4096 + 1024;
+static_assert(PAIR_SMEM <= 227 * 1024 && PAIR_SMEM_RESID <= 227 * 1024, "pair GEMM shared memory");
+
+// x[rows row_base .. +31][col0 ..] += acc through TMA reduce-add: the warp's
+// 32 rows x 32 columns at a time are written to a shared-memory buffer in the
+// tensor map's 128-byte swizzle (16-byte unit u of row r at u ^ (r % 8)) and
+// one lane issues the reduction.  Each residual element receives exactly one
+// addition, so the result does not depend on timing.
+__device__ __forceinline__ void resid_tma_tile(const GemmArgs& a, const CUtensorMap* tmR, uint32_t tbase,
+                                               int row_base, int col0, uint8_t* stg, int lane) {
+  for (int c = 0; c < BN / 32; c++) {
+    const int cb = col0 + c * 32;
+    if (cb >= a.N) break;
+    uint32_t r[32];
+    __syncwarp();
+    tmem_ld32(tbase + c * 32, r);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+    if (a.bias) {
+      const int n = min(32, a.N - cb);
+#pragma unroll
+      for (int i = 0; i < 32; i++)
+        if (i < n) v[i] += a.bias[cb + i];
+    }
+    uint8_t* buf = stg + (c & 1) * 4096;
+    if (c >= 2) {
+      if (lane == 0) bulk_wait_read<1>();  // the reduction issued from this buffer two chunks ago has read it
+      __syncwarp();
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_reduce_add_2d(tmR, buf, cb, row_base);
+      bulk_commit();
+    }
+  }
+  if (lane == 0) bulk_wait_read<0>();  // both buffers free for the next tile
+  __syncwarp();
+}
 
 // Launched in clusters of two CTAs.  Tile t of the cluster's sequence covers
 // output rows mt*256 .. +255 (rank r owns mt*256 + 128r ..) and columns
@@ -417,7 +464,7 @@ static_assert(PAIR_SMEM <= 227 * 1024, "pair GEMM shared memory");
 template <int EPI, int HD>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs a) {
+                     const __grid_constant__ CUtensorMap tmR, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -535,18 +582,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quarter = warp % 4;
+    uint8_t* stg = smem + PAIR_STG + quarter * 2 * 4096;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = cluster; tile < total; tile += nclusters) {
       const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
       const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
-      resid_prefetch<EPI>(a, row, nt);
       if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
         atomicOr(a.err, 8u);
         break;
       }
       tc_fence_after();
-      epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt);
+      if constexpr (EPI == EPI_RESID)
+        resid_tma_tile(a, &tmR, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row - lane, nt * BN, stg,
+                       lane);
+      else
+        epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
@@ -556,6 +607,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   }
+  if constexpr (EPI == EPI_RESID)
+    if (warp >= 2 && lane == 0) bulk_wait<0>();  // residual reductions complete before exit
   tc_fence_before();
   __syncwarp();
   __syncthreads();
@@ -630,8 +683,9 @@ static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, cons
 }
 
 template <int EPI, int HD>
-static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
-                               cudaStream_t st) {
+static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const GemmArgs& a,
+                               int num_sms, cudaStream_t st) {
+  constexpr int SMEM = EPI == EPI_RESID ? PAIR_SMEM_RESID : PAIR_SMEM;
   // Per device: the attribute is set once and the number of CTA pairs that
   // fit at once is queried once, so the persistent grid never exceeds what is
   // co-resident (a pair left for a second wave would double the time).
@@ -646,12 +700,12 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(GEMM_THREADS);
-  cfg.dynamicSmemBytes = PAIR_SMEM;
+  cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (clusters_fit[dev & 63] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(2 * (num_sms / 2));
     int n = 0;
@@ -665,7 +719,7 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   if (clusters > num_sms / 2) clusters = num_sms / 2;
   if (clusters > total) clusters = total;
   cfg.gridDim = dim3(2 * clusters);
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, a);
 }
 
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
@@ -677,16 +731,26 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
   if (a.M > BM && num_sms >= 2) {
     if (!make_map(&ta, A, a.M, a.K, lda, 128) || !make_map(&tb, B, a.N, a.K, ldb, 128))
       return cudaErrorInvalidValue;
+    CUtensorMap tr = ta;
+    if (epi == EPI_RESID) {
+      // residual F32 [M][ldo] in 32 x 32 boxes, 128-byte swizzle
+      if ((a.ldo % 4) || (reinterpret_cast<uintptr_t>(a.resid) & 15)) return cudaErrorInvalidValue;
+      const uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M}, strides[1] = {(uint64_t)a.ldo * 4};
+      const uint32_t box[2] = {32, 32};
+      if (!encode_tiled(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.resid, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    }
     a.m_tiles = (a.M + 255) / 256;
     a.n_tiles = (a.N + BN - 1) / BN;
     switch (epi) {
-      case EPI_F32: return launch_pair<EPI_F32, 64>(ta, tb, a, num_sms, st);
-      case EPI_F16: return launch_pair<EPI_F16, 64>(ta, tb, a, num_sms, st);
-      case EPI_RESID: return launch_pair<EPI_RESID, 64>(ta, tb, a, num_sms, st);
-      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU, 64>(ta, tb, a, num_sms, st);
+      case EPI_F32: return launch_pair<EPI_F32, 64>(ta, tb, tr, a, num_sms, st);
+      case EPI_F16: return launch_pair<EPI_F16, 64>(ta, tb, tr, a, num_sms, st);
+      case EPI_RESID: return launch_pair<EPI_RESID, 64>(ta, tb, tr, a, num_sms, st);
+      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU, 64>(ta, tb, tr, a, num_sms, st);
       case EPI_QKV:
-        if (a.hd == 64) return launch_pair<EPI_QKV, 64>(ta, tb, a, num_sms, st);
-        if (a.hd == 128) return launch_pair<EPI_QKV, 128>(ta, tb, a, num_sms, st);
+        if (a.hd == 64) return launch_pair<EPI_QKV, 64>(ta, tb, tr, a, num_sms, st);
+        if (a.hd == 128) return launch_pair<EPI_QKV, 128>(ta, tb, tr, a, num_sms, st);
         return cudaErrorInvalidValue;
     }
     return cudaErrorInvalidValue;
