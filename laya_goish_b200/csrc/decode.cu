@@ -573,11 +573,13 @@ struct DecSeq {
 __global__ void advance_kernel(int* counter, unsigned long long* __restrict__ best, int* __restrict__ toks,
                                const int* __restrict__ pos_all, const int* __restrict__ slot_all,
                                const DecSeq* __restrict__ seq_all, int nb, int* __restrict__ cur_tok,
-                               int* __restrict__ cur_pos, int* __restrict__ cur_slot, DecSeq* __restrict__ cur_seq) {
+                               int* __restrict__ cur_pos, int* __restrict__ cur_slot, DecSeq* __restrict__ cur_seq,
+                               unsigned* __restrict__ gbar, int n_gbar) {
   __shared__ int s;
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x == 0) s = *counter + 1;
+  for (int i = threadIdx.x; i < n_gbar; i += blockDim.x) gbar[i] = 0u;  // this step's grid barriers
   __syncthreads();
   for (int i = threadIdx.x; i < nb; i += blockDim.x) {
     const int tok = unpack_row(best[i]);
@@ -991,6 +993,11 @@ static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_k
   return {(pages + split_pages - 1) / split_pages, split_pages, (pages + sp3 - 1) / sp3, sp3};
 }
 
+static bool seq_enabled() {
+  const char* e = std::getenv("LAYA_DECODE_SEQ");
+  return !(e && e[0] == '0');
+}
+
 static bool dec3_enabled() {
   const char* e = std::getenv("LAYA_DEC_ATTN3");
   return !(e && e[0] == '0');
@@ -1221,6 +1228,8 @@ struct StepIO {
   const DecSeq* seq_all;
   int *cur_tok, *cur_pos, *cur_slot;
   DecSeq* cur_seq;
+  unsigned* gbar;  // [layers] grid barrier counters of the multi-phase GEMV launches
+  int n_gbar;
 };
 
 // One decode step for nb sequences; every pointer it uses is fixed, so the
@@ -1234,7 +1243,8 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
   int rc;
   r.launches++;
   LAYA_CK(launch_k(advance_kernel, dim3(1), dim3(256), 0, st, true, io.counter, io.best, io.toks, io.pos_all,
-                   io.slot_all, io.seq_all, nb, io.cur_tok, io.cur_pos, io.cur_slot, io.cur_seq));
+                   io.slot_all, io.seq_all, nb, io.cur_tok, io.cur_pos, io.cur_slot, io.cur_seq, io.gbar,
+                   io.n_gbar));
   float* x = r.x.as<float>();
   r.launches++;
   LAYA_CK(rows_f32(r.embd, io.cur_tok, nb, x, st, true));
@@ -1257,11 +1267,15 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     LAYA_CK(dequant_f16(t, out, ldo, grp, gstride, goff, st));
     return 0;
   };
-  for (int l = 0; l < c.L; l++) {
+  const bool packed_all = (int)r.gv_packed.size() == 4 * c.L + 1;
+  // The four streaming-GEMV operands of layer l: g[0] qkv, g[1] attention
+  // output, g[2] gate/up, g[3] down.  Returns whether all of them run on it.
+  auto layer_args = [&](int l, Gemv3Args* g) -> bool {
     const Layer& L = r.layers[l];
     half* kcl = r.kc.as<half>() + l * layer_elems;
     half* vcl = r.vc.as<half>() + l * layer_elems;
-    Gemv3Args gq = gv3_base(r, GV_QKV, nb, d);
+    Gemv3Args& gq = g[0];
+    gq = gv3_base(r, GV_QKV, nb, d);
     gq.seg[0] = L.wq;
     gq.seg[1] = L.wk;
     gq.seg[2] = L.wv;
@@ -1280,14 +1294,16 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     gq.kcache = kcl;
     gq.vcache = vcl;
     gq.page_size = PAGE;
-    Gemv3Args go = gv3_base(r, GV_PLAIN, nb, qd);
+    Gemv3Args& go = g[1];
+    go = gv3_base(r, GV_PLAIN, nb, qd);
     go.seg[0] = L.wo;
     go.x = r.att.as<half>();
     go.ldx = qd;
     go.y = x;  // residual add (tensor::add, src/tensor.rs:123-128)
     go.ldy = d;
     go.acc = 1;
-    Gemv3Args gg = gv3_base(r, GV_SWIGLU, nb, d);
+    Gemv3Args& gg = g[2];
+    gg = gv3_base(r, GV_SWIGLU, nb, d);
     gg.seg[0] = L.wg;
     gg.seg[1] = L.wu;
     gg.interleaved = L.wgu16 != nullptr;
@@ -1296,28 +1312,52 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     gg.eps = c.eps;
     gg.act = r.act.as<half>();
     gg.ld_act = ffn;
-    Gemv3Args gd = gv3_base(r, GV_PLAIN, nb, ffn);
+    Gemv3Args& gd = g[3];
+    gd = gv3_base(r, GV_PLAIN, nb, ffn);
     gd.seg[0] = L.wd;
     gd.x = r.act.as<half>();
     gd.ldx = ffn;
     gd.y = x;
     gd.ldy = d;
     gd.acc = 1;
-    // the streaming GEMV serves the whole layer when it supports every operand
-    bool v3 = small && gemv3_enabled() && (int)r.gv_packed.size() == 4 * c.L + 1;
-    if (v3) {
-      gq.packed = r.gv_packed[4 * l];
-      go.packed = r.gv_packed[4 * l + 1];
-      gg.packed = r.gv_packed[4 * l + 2];
-      gd.packed = r.gv_packed[4 * l + 3];
-      v3 = gq.packed && go.packed && gg.packed && gd.packed && gemv3_supported(gq) && gemv3_supported(go) &&
-           gemv3_supported(gg) && gemv3_supported(gd);
+    if (!(small && gemv3_enabled() && packed_all)) return false;
+    for (int i = 0; i < 4; i++) {
+      g[i].packed = r.gv_packed[4 * l + i];
+      if (!g[i].packed || !gemv3_supported(g[i])) return false;
     }
+    return true;
+  };
+  Gemv3Args gh = gv3_base(r, GV_ARGMAX, nb, d);
+  gh.seg[0] = r.head;
+  gh.xres = x;
+  gh.norm_w = r.out_norm;
+  gh.eps = c.eps;
+  gh.best = io.best;
+  gh.packed = packed_all ? r.gv_packed[4 * c.L] : nullptr;
+  const bool head3 = small && gemv3_enabled() && gh.packed && gemv3_supported(gh);
+  // Whole-model chaining: after layer l's attention, one cooperative launch
+  // runs attention output, gate/up, down and the next layer's qkv (the head
+  // after the last layer), so the weights stream without a launch gap.
+  std::vector<Gemv3Args> ga(4 * c.L);
+  bool seq = head3 && seq_enabled() && io.gbar && io.n_gbar >= c.L;
+  for (int l = 0; seq && l < c.L; l++) {
+    seq = layer_args(l, &ga[4 * l]);
+    for (int i = 0; seq && i < 4; i++) seq = ga[4 * l + i].seg[0].kind == gh.seg[0].kind;
+  }
+  for (int l = 0; l < c.L; l++) {
+    const Layer& L = r.layers[l];
+    half* kcl = r.kc.as<half>() + l * layer_elems;
+    half* vcl = r.vc.as<half>() + l * layer_elems;
+    Gemv3Args g4[4];
+    const bool v3 = layer_args(l, g4);
+    Gemv3Args &gq = g4[0], &go = g4[1], &gg = g4[2], &gd = g4[3];
     if (!small) {
       r.launches++;
       LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
     }
-    if (small && v3) {
+    if (seq) {
+      if (l == 0 && (rc = run_gemv3(r, gq))) return rc;  // later layers' qkv ran in the previous chain
+    } else if (small && v3) {
       if ((rc = run_gemv3(r, gq))) return rc;
     } else if (small) {
       GemvPlan p{};
@@ -1368,6 +1408,15 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       if ((rc = gemm_d(P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
     }
     if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, io.cur_seq, sh, r.att.as<half>()))) return rc;
+    if (seq) {
+      const Gemv3Args ph[4] = {go, gg, gd, l + 1 < c.L ? ga[4 * (l + 1)] : gh};
+      cudaEvent_t ev;
+      prof_begin(r, P_GEMV, &ev);
+      r.launches++;
+      LAYA_CK(gemv3_launch_seq(ph, 4, io.gbar + l, r.num_sms, st));
+      prof_end(r, P_GEMV, ev);
+      continue;
+    }
     if (small && v3) {
       if ((rc = run_gemv3(r, go))) return rc;
     } else if (small) {
@@ -1447,14 +1496,9 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     LAYA_CK(rmsnorm(x, nullptr, nb, r.out_norm, d, c.eps, h, nullptr, st));
   }
   float* logits = r.dlogits.as<float>();
-  Gemv3Args gh = gv3_base(r, GV_ARGMAX, nb, d);
-  gh.seg[0] = r.head;
-  gh.xres = x;
-  gh.norm_w = r.out_norm;
-  gh.eps = c.eps;
-  gh.best = io.best;
-  gh.packed = (int)r.gv_packed.size() == 4 * c.L + 1 ? r.gv_packed[4 * c.L] : nullptr;
-  if (small && gemv3_enabled() && gh.packed && gemv3_supported(gh)) {
+  if (seq) {
+    // the head ran at the end of the last layer's chain
+  } else if (head3) {
     // head GEMV with the final RMSNorm and the greedy argmax fused
     if ((rc = run_gemv3(r, gh))) return rc;
   } else if (small) {
@@ -1543,8 +1587,8 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
     return rc;
   // device state: [counter | best | toks | pos_all | slot_all | seq_all | cur_tok | cur_pos | cur_slot | cur_seq]
   const size_t best_bytes = ((size_t)n_seqs * 8 + 255) / 256 * 256;
-  const size_t meta_bytes =
-      256 + best_bytes + nmeta * 4 * 3 + nmeta * sizeof(DecSeq) + (size_t)n_seqs * (12 + sizeof(DecSeq)) + 256;
+  const size_t meta_bytes = 256 + best_bytes + nmeta * 4 * 3 + nmeta * sizeof(DecSeq) +
+                            (size_t)n_seqs * (12 + sizeof(DecSeq)) + 256 + (size_t)c.L * 4 + 256;
   if ((rc = r.dargmax.ensure(meta_bytes))) return rc;
   char* base = static_cast<char*>(r.dargmax.p);
   StepIO io;
@@ -1561,6 +1605,8 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   io.cur_pos = io.cur_tok + n_seqs;
   io.cur_slot = io.cur_pos + n_seqs;
   io.cur_seq = reinterpret_cast<DecSeq*>(io.cur_slot + n_seqs);
+  io.gbar = reinterpret_cast<unsigned*>(reinterpret_cast<uintptr_t>(io.cur_seq + n_seqs + 63) & ~uintptr_t(255));
+  io.n_gbar = c.L;
   LAYA_CK(cudaMemsetAsync(io.best, 0, best_bytes, r.stream));
   Gemv3Args gh0 = gv3_base(r, GV_ARGMAX, R, c.d);
   gh0.seg[0] = r.head;

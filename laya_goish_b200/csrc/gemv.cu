@@ -240,9 +240,32 @@ __global__ void gemv3_pack_kernel(const Gemv3Args a, int kstages, uint8_t* __res
   }
 }
 
-template <int NT, bool Q8, bool NORM>
-__global__ void __launch_bounds__(GV_THREADS, 1)
-    gemv3_kernel(const Gemv3Args a, int tiles, int nst) {
+// Two named barriers besides __syncthreads: 1 = the compute warps,
+// 2 = the compute warps and the epilogue warp.
+__device__ __forceinline__ void cta_epi_sync() { asm volatile("bar.sync 2, %0;" ::"n"((GV_WARPS + 1) * 32) : "memory"); }
+
+// Work of phase p of a GEMV sequence: this CTA's contiguous tile range.
+struct GvPhase {
+  int kstages, t0, t1;
+};
+
+__device__ __forceinline__ GvPhase gv_phase(const GemvSeq& q, int p, bool q8) {
+  const Gemv3Args& a = q.ph[p];
+  GvPhase r;
+  r.kstages = ((q8 ? a.K : 2 * a.K) + GV_BYTES - 1) / GV_BYTES;
+  r.t0 = (int)((long long)blockIdx.x * q.tiles[p] / gridDim.x);
+  r.t1 = (int)((long long)(blockIdx.x + 1) * q.tiles[p] / gridDim.x);
+  return r;
+}
+
+// One launch runs q.n GEMV phases in order (e.g. attention output, gate/up,
+// down, the next layer's QKV).  The producer streams every phase's weight
+// stages back to back, so the next phase's weights are already in flight
+// while the current phase finishes; between phases every CTA waits at a
+// grid-wide barrier (q.gbar, zeroed before the launch; the launch is
+// cooperative), because a phase reads the previous phase's outputs.
+template <int NT, bool Q8>
+__global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_constant__ GemvSeq q, int nst) {
   // [full | empty | tdone | tfree barriers][cross-warp sums][activation rows][nst-stage ring]
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -252,17 +275,13 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
   uint64_t* tfree = tdone + 2;              // [2] the epilogue has read them (1 arrival)
   float4* red = reinterpret_cast<float4*>(tfree + 2);  // [2][GV_WARPS][NT][32] partial sums
   half* xs = reinterpret_cast<half*>(red + 2 * GV_WARPS * 32 * NT);
-  uint8_t* ring = gsm + gv_ring_offset(a.nb, a.K, NT);
+  uint8_t* ring = gsm + gv_ring_offset(q.ph[0].nb, q.kmax, NT);
   __shared__ float nred[GV_WARPS][16];
   __shared__ float nscale[16];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int K = a.K;
-  const int row_bytes = Q8 ? K : 2 * K;
-  const int kstages = (row_bytes + GV_BYTES - 1) / GV_BYTES;
-  const int t0 = (int)((long long)blockIdx.x * tiles / gridDim.x);
-  const int t1 = (int)((long long)(blockIdx.x + 1) * tiles / gridDim.x);
-  const long long budget = a.budget;
+  const long long budget = q.ph[0].budget;
+  unsigned* err = q.ph[0].err;
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; s++) {
       mbar_init(&full[s], 1);
@@ -277,29 +296,33 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
   __syncthreads();
 
   if (warp == GV_WARPS) {
-    // ---------------- producer: one thread, one bulk copy per stage
+    // ---------------- producer: one thread, one bulk copy per stage, all phases
     int stage = 0;
     uint32_t phase = 0;
     const uint32_t sbytes = (uint32_t)gv_stage_bytes(Q8);
-    for (int t = t0; t < t1; t++) {
-      for (int ks = 0; ks < kstages; ks++) {
-        if (!mbar_wait_sleep(&empty[stage], phase ^ 1, budget)) {
-          if (lane == 0) atomicOr(a.err, 32u);
-        }
-        if (lane == 0) {
-          mbar_expect_tx(&full[stage], sbytes);
-          bulk_g2s(ring + stage * GV_STAGE, a.packed + ((size_t)t * kstages + ks) * sbytes, sbytes, &full[stage]);
-        }
-        __syncwarp();
-        if (++stage == nst) {
-          stage = 0;
-          phase ^= 1;
+    for (int p = 0; p < q.n; p++) {
+      const GvPhase w = gv_phase(q, p, Q8);
+      const uint8_t* src = q.ph[p].packed;
+      for (int t = w.t0; t < w.t1; t++) {
+        for (int ks = 0; ks < w.kstages; ks++) {
+          if (!mbar_wait_sleep(&empty[stage], phase ^ 1, budget)) {
+            if (lane == 0) atomicOr(err, 32u);
+          }
+          if (lane == 0) {
+            mbar_expect_tx(&full[stage], sbytes);
+            bulk_g2s(ring + stage * GV_STAGE, src + ((size_t)t * w.kstages + ks) * sbytes, sbytes, &full[stage]);
+          }
+          __syncwarp();
+          if (++stage == nst) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
       }
     }
     // Every fill is consumed before the CTA exits (no copy left in flight).
     for (int i = 0; i < nst; i++) {
-      if (!mbar_wait(&empty[stage], phase ^ 1, budget) && lane == 0) atomicOr(a.err, 64u);
+      if (!mbar_wait(&empty[stage], phase ^ 1, budget) && lane == 0) atomicOr(err, 64u);
       if (++stage == nst) {
         stage = 0;
         phase ^= 1;
@@ -309,6 +332,27 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
   }
 
   const int g = lane >> 2, tq = lane & 3;
+  // Barrier between phases p-1 and p: all of this CTA's outputs of phase p-1
+  // are written (compute and epilogue warps meet), then one thread joins
+  // the grid-wide count, then everyone proceeds.
+  auto grid_sync = [&](int p) {
+    cta_epi_sync();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(q.gbar, 1u);
+      const unsigned target = (unsigned)p * gridDim.x;
+      long long t0 = clock64();
+      while (atomicAdd(q.gbar, 0u) < target) {
+        if (clock64() - t0 > budget) {
+          atomicOr(err, 4096u);
+          break;
+        }
+      }
+      __threadfence();
+    }
+    cta_epi_sync();
+  };
+
   if (warp == GV_WARPS + 1) {
     // ---------------- epilogue warp: sums the compute warps' partials and
     // writes the outputs.  Each tile's global operands (residual, RoPE
@@ -316,243 +360,256 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
     // latency overlaps the tile's K loop.  Lane (g, tq) holds rows g and g+8
     // for batch rows n*8 + 2tq + e.
     pdl_wait();
-    const int tqn = a.qd / 16, tkn = a.kd / 16;
-    int pos[NT][2], slot[NT][2];
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-      for (int e = 0; e < 2; e++) {
-        const int b = n * 8 + 2 * tq + e;
-        pos[n][e] = (a.mode == GV_QKV && b < a.nb) ? a.pos[b] : 0;
-        slot[n][e] = (a.mode == GV_QKV && b < a.nb) ? a.slot[b] : 0;
-      }
-    unsigned long long best[NT][2];
-#pragma unroll
-    for (int n = 0; n < NT; n++) best[n][0] = best[n][1] = 0ull;
-    for (int t = t0; t < t1; t++) {
-      const int u = t - t0, buf = u & 1;
-      // operands of tile t
-      float yv[NT][2][2];
-      float2 cs[NT][2];
-      float bg = 0.f, bh = 0.f;
-      bool isk = false, isv = false;
-      int h = 0, j = 0, r0 = t * 16 + g;
-      if (a.mode == GV_QKV) {
-        isv = t >= tqn + tkn;
-        if (!isv) {
-          isk = t >= tqn;
-          const int tt = isk ? t - tqn : t, per = a.hd / 16;
-          h = tt / per;
-          j = 8 * (tt % per) + g;
-          const int col0 = (isk ? a.qd : 0) + h * a.hd + j;
-          if (a.bias) {
-            bg = __ldg(a.bias + col0);
-            bh = __ldg(a.bias + col0 + a.hd / 2);
-          }
-        } else {
-          r0 = (t - tqn - tkn) * 16 + g;
-          if (a.bias) {
-            bg = r0 < a.kd ? __ldg(a.bias + a.qd + a.kd + r0) : 0.f;
-            bh = r0 + 8 < a.kd ? __ldg(a.bias + a.qd + a.kd + r0 + 8) : 0.f;
-          }
-        }
-      }
+    int T = 0;  // tiles handed over so far (all phases)
+    for (int p = 0; p < q.n; p++) {
+      if (p > 0) grid_sync(p);
+      const Gemv3Args& a = q.ph[p];
+      const GvPhase w = gv_phase(q, p, Q8);
+      const int tqn = a.qd / 16, tkn = a.kd / 16;
+      int pos[NT][2], slot[NT][2];
 #pragma unroll
       for (int n = 0; n < NT; n++)
 #pragma unroll
         for (int e = 0; e < 2; e++) {
           const int b = n * 8 + 2 * tq + e;
-          yv[n][e][0] = yv[n][e][1] = 0.f;
-          cs[n][e] = make_float2(1.f, 0.f);
-          if (b >= a.nb) continue;
-          if (a.mode == GV_PLAIN && a.acc) {
-            const float* yb = a.y + (size_t)b * a.ldy;
-            if (r0 < a.seg[0].rows) yv[n][e][0] = yb[r0];
-            if (r0 + 8 < a.seg[0].rows) yv[n][e][1] = yb[r0 + 8];
-          } else if (a.mode == GV_QKV && !isv) {
-            cs[n][e] = __ldg(a.rope + (size_t)pos[n][e] * (a.hd / 2) + j);
+          pos[n][e] = (a.mode == GV_QKV && b < a.nb) ? a.pos[b] : 0;
+          slot[n][e] = (a.mode == GV_QKV && b < a.nb) ? a.slot[b] : 0;
+        }
+      unsigned long long best[NT][2];
+#pragma unroll
+      for (int n = 0; n < NT; n++) best[n][0] = best[n][1] = 0ull;
+      for (int t = w.t0; t < w.t1; t++, T++) {
+        const int buf = T & 1;
+        // operands of tile t
+        float yv[NT][2][2];
+        float2 cs[NT][2];
+        float bg = 0.f, bh = 0.f;
+        bool isk = false, isv = false;
+        int h = 0, j = 0, r0 = t * 16 + g;
+        if (a.mode == GV_QKV) {
+          isv = t >= tqn + tkn;
+          if (!isv) {
+            isk = t >= tqn;
+            const int tt = isk ? t - tqn : t, per = a.hd / 16;
+            h = tt / per;
+            j = 8 * (tt % per) + g;
+            const int col0 = (isk ? a.qd : 0) + h * a.hd + j;
+            if (a.bias) {
+              bg = __ldg(a.bias + col0);
+              bh = __ldg(a.bias + col0 + a.hd / 2);
+            }
+          } else {
+            r0 = (t - tqn - tkn) * 16 + g;
+            if (a.bias) {
+              bg = r0 < a.kd ? __ldg(a.bias + a.qd + a.kd + r0) : 0.f;
+              bh = r0 + 8 < a.kd ? __ldg(a.bias + a.qd + a.kd + r0 + 8) : 0.f;
+            }
           }
         }
-      if (!mbar_wait_sleep(&tdone[buf], (u >> 1) & 1, budget)) {
-        if (lane == 0) atomicOr(a.err, 512u);
-      }
-      const float4* rb = red + buf * (GV_WARPS * NT * 32);
-      float acc[NT][4];
 #pragma unroll
-      for (int n = 0; n < NT; n++) {
-        float4 sum = rb[n * 32 + lane];
+        for (int n = 0; n < NT; n++)
 #pragma unroll
-        for (int w = 1; w < GV_WARPS; w++) {
-          const float4 v = rb[(w * NT + n) * 32 + lane];
-          sum.x += v.x;
-          sum.y += v.y;
-          sum.z += v.z;
-          sum.w += v.w;
+          for (int e = 0; e < 2; e++) {
+            const int b = n * 8 + 2 * tq + e;
+            yv[n][e][0] = yv[n][e][1] = 0.f;
+            cs[n][e] = make_float2(1.f, 0.f);
+            if (b >= a.nb) continue;
+            if (a.mode == GV_PLAIN && a.acc) {
+              const float* yb = a.y + (size_t)b * a.ldy;
+              if (r0 < a.seg[0].rows) yv[n][e][0] = yb[r0];
+              if (r0 + 8 < a.seg[0].rows) yv[n][e][1] = yb[r0 + 8];
+            } else if (a.mode == GV_QKV && !isv) {
+              cs[n][e] = __ldg(a.rope + (size_t)pos[n][e] * (a.hd / 2) + j);
+            }
+          }
+        if (!mbar_wait_sleep(&tdone[buf], (T >> 1) & 1, budget)) {
+          if (lane == 0) atomicOr(err, 512u);
         }
-        acc[n][0] = sum.x;
-        acc[n][1] = sum.y;
-        acc[n][2] = sum.z;
-        acc[n][3] = sum.w;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tfree[buf]);
+        const float4* rb = red + buf * (GV_WARPS * NT * 32);
+        float acc[NT][4];
 #pragma unroll
-      for (int n = 0; n < NT; n++)
+        for (int n = 0; n < NT; n++) {
+          float4 sum = rb[n * 32 + lane];
 #pragma unroll
-        for (int e = 0; e < 2; e++) {
-          const int b = n * 8 + 2 * tq + e;
-          if (b >= a.nb) continue;
-          const float vg = acc[n][e], vh = acc[n][2 + e];
-          if (a.mode == GV_PLAIN) {
-            float* yb = a.y + (size_t)b * a.ldy;
-            if (r0 < a.seg[0].rows) yb[r0] = yv[n][e][0] + vg;  // yv is 0 unless accumulating
-            if (r0 + 8 < a.seg[0].rows) yb[r0 + 8] = yv[n][e][1] + vh;
-          } else if (a.mode == GV_ARGMAX) {
-            if (r0 < a.seg[0].rows) {
-              const unsigned long long kk = pack_logit(vg, r0);
-              best[n][e] = kk > best[n][e] ? kk : best[n][e];
-            }
-            if (r0 + 8 < a.seg[0].rows) {
-              const unsigned long long kk = pack_logit(vh, r0 + 8);
-              best[n][e] = kk > best[n][e] ? kk : best[n][e];
-            }
-          } else if (a.mode == GV_SWIGLU) {
-            const int c = 8 * t + g;
-            const int ffn = a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows;
-            if (c < ffn) a.act[(size_t)b * a.ld_act + c] = __float2half_rn(vg / (1.f + __expf(-vg)) * vh);
-          } else {  // GV_QKV
-            const int page = slot[n][e] / a.page_size, off = slot[n][e] % a.page_size;
-            if (!isv) {
-              // rotate-half RoPE (src/tensor.rs:158-171) after the bias
-              const float x0 = vg + bg, x1 = vh + bh;
-              const float y0 = x0 * cs[n][e].x - x1 * cs[n][e].y, y1 = x1 * cs[n][e].x + x0 * cs[n][e].y;
-              half* dst = isk ? a.kcache + (((size_t)page * a.kvh + h) * a.page_size + off) * a.hd
-                              : a.q + (size_t)b * a.qd + h * a.hd;
-              dst[j] = __float2half_rn(y0);
-              dst[j + a.hd / 2] = __float2half_rn(y1);
-            } else {
+          for (int ww = 1; ww < GV_WARPS; ww++) {
+            const float4 v = rb[(ww * NT + n) * 32 + lane];
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
+          }
+          acc[n][0] = sum.x;
+          acc[n][1] = sum.y;
+          acc[n][2] = sum.z;
+          acc[n][3] = sum.w;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tfree[buf]);
 #pragma unroll
-              for (int hh = 0; hh < 2; hh++) {
-                const int r = r0 + 8 * hh;
-                if (r >= a.kd) continue;
-                const float v = (hh ? vh : vg) + (hh ? bh : bg);
-                a.vcache[(((size_t)page * a.kvh + r / a.hd) * a.page_size + off) * a.hd + r % a.hd] =
-                    __float2half_rn(v);
+        for (int n = 0; n < NT; n++)
+#pragma unroll
+          for (int e = 0; e < 2; e++) {
+            const int b = n * 8 + 2 * tq + e;
+            if (b >= a.nb) continue;
+            const float vg = acc[n][e], vh = acc[n][2 + e];
+            if (a.mode == GV_PLAIN) {
+              float* yb = a.y + (size_t)b * a.ldy;
+              if (r0 < a.seg[0].rows) yb[r0] = yv[n][e][0] + vg;  // yv is 0 unless accumulating
+              if (r0 + 8 < a.seg[0].rows) yb[r0 + 8] = yv[n][e][1] + vh;
+            } else if (a.mode == GV_ARGMAX) {
+              if (r0 < a.seg[0].rows) {
+                const unsigned long long kk = pack_logit(vg, r0);
+                best[n][e] = kk > best[n][e] ? kk : best[n][e];
+              }
+              if (r0 + 8 < a.seg[0].rows) {
+                const unsigned long long kk = pack_logit(vh, r0 + 8);
+                best[n][e] = kk > best[n][e] ? kk : best[n][e];
+              }
+            } else if (a.mode == GV_SWIGLU) {
+              const int c = 8 * t + g;
+              const int ffn = a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows;
+              if (c < ffn) a.act[(size_t)b * a.ld_act + c] = __float2half_rn(vg / (1.f + __expf(-vg)) * vh);
+            } else {  // GV_QKV
+              const int page = slot[n][e] / a.page_size, off = slot[n][e] % a.page_size;
+              if (!isv) {
+                // rotate-half RoPE (src/tensor.rs:158-171) after the bias
+                const float x0 = vg + bg, x1 = vh + bh;
+                const float y0 = x0 * cs[n][e].x - x1 * cs[n][e].y, y1 = x1 * cs[n][e].x + x0 * cs[n][e].y;
+                half* dst = isk ? a.kcache + (((size_t)page * a.kvh + h) * a.page_size + off) * a.hd
+                                : a.q + (size_t)b * a.qd + h * a.hd;
+                dst[j] = __float2half_rn(y0);
+                dst[j + a.hd / 2] = __float2half_rn(y1);
+              } else {
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                  const int r = r0 + 8 * hh;
+                  if (r >= a.kd) continue;
+                  const float v = (hh ? vh : vg) + (hh ? bh : bg);
+                  a.vcache[(((size_t)page * a.kvh + r / a.hd) * a.page_size + off) * a.hd + r % a.hd] =
+                      __float2half_rn(v);
+                }
               }
             }
           }
-        }
-    }
-    if (a.mode == GV_ARGMAX) {
-      // lanes with the same tq hold the same batch rows: reduce over g
+      }
+      if (a.mode == GV_ARGMAX) {
+        // lanes with the same tq hold the same batch rows: reduce over g
 #pragma unroll
-      for (int n = 0; n < NT; n++)
+        for (int n = 0; n < NT; n++)
 #pragma unroll
-        for (int e = 0; e < 2; e++) {
-          unsigned long long k = best[n][e];
+          for (int e = 0; e < 2; e++) {
+            unsigned long long k = best[n][e];
 #pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
-            k = ok > k ? ok : k;
+            for (int o = 4; o < 32; o <<= 1) {
+              const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+              k = ok > k ? ok : k;
+            }
+            const int b = n * 8 + 2 * tq + e;
+            if (g == 0 && b < a.nb && k) atomicMax(a.best + b, k);
           }
-          const int b = n * 8 + 2 * tq + e;
-          if (g == 0 && b < a.nb && k) atomicMax(a.best + b, k);
-        }
+      }
     }
     return;
   }
 
   // ---------------- compute warps
   const int tid = threadIdx.x;
-  const int xpitch = K + 8;
   pdl_wait();
-  if constexpr (!NORM) {
-    // F16 activation rows -> shared memory
-    for (int b = 0; b < a.nb; b++)
-      for (int k = tid * 8; k < K; k += GV_WARPS * 32 * 8)
-        *reinterpret_cast<uint4*>(xs + (size_t)b * xpitch + k) =
-            *reinterpret_cast<const uint4*>(a.x + (size_t)b * a.ldx + k);
-    named_sync();
-  } else {
-    // x = rmsnorm(xres[b]) * norm_w  (src/models/openthai/model.rs:84-94), F16 rows in shared memory
-    for (int b = 0; b < a.nb; b++) {
-      float ss = 0.f;
-      for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) nred[warp][b] = ss;
-    }
-    named_sync();
-    if (tid < a.nb) {
-      float tsum = 0.f;
-      for (int i = 0; i < GV_WARPS; i++) tsum += nred[i][tid];
-      nscale[tid] = 1.f / sqrtf(tsum / (float)K + a.eps);
-    }
-    named_sync();
-    for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
-      const float4 wv = *reinterpret_cast<const float4*>(a.norm_w + k);
-      for (int b = 0; b < a.nb; b++) {
-        const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
-        const float sc = nscale[b];
-        half2 h0 = __floats2half2_rn(v.x * sc * wv.x, v.y * sc * wv.y);
-        half2 h1 = __floats2half2_rn(v.z * sc * wv.z, v.w * sc * wv.w);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t*>(&h0);
-        u.y = *reinterpret_cast<uint32_t*>(&h1);
-        *reinterpret_cast<uint2*>(xs + (size_t)b * xpitch + k) = u;
-      }
-    }
-    named_sync();
-  }
-  pdl_trigger();
-
-  int stage = 0;
+  int stage = 0, T = 0;
   uint32_t phase = 0;
-  for (int t = t0; t < t1; t++) {
-    float acc[NT][4];
+  for (int p = 0; p < q.n; p++) {
+    if (p > 0) grid_sync(p);
+    const Gemv3Args& a = q.ph[p];
+    const GvPhase w = gv_phase(q, p, Q8);
+    const int K = a.K;
+    const int row_bytes = Q8 ? K : 2 * K;
+    const int xpitch = K + 8;
+    if (!a.xres) {
+      // F16 activation rows -> shared memory
+      for (int b = 0; b < a.nb; b++)
+        for (int k = tid * 8; k < K; k += GV_WARPS * 32 * 8)
+          *reinterpret_cast<uint4*>(xs + (size_t)b * xpitch + k) =
+              *reinterpret_cast<const uint4*>(a.x + (size_t)b * a.ldx + k);
+      named_sync();
+    } else {
+      // x = rmsnorm(xres[b]) * norm_w  (src/models/openthai/model.rs:84-94), F16 rows in shared memory
+      for (int b = 0; b < a.nb; b++) {
+        float ss = 0.f;
+        for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
+          const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
 #pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-      for (int j = 0; j < 4; j++) acc[n][j] = 0.f;
-    for (int ks = 0; ks < kstages; ks++) {
-      if (!mbar_wait_sleep(&full[stage], phase, budget)) {
-        if (lane == 0) atomicOr(a.err, 128u);
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) nred[warp][b] = ss;
       }
-      const uint8_t* sb = ring + stage * GV_STAGE;
-      const int kb = ks * GV_BYTES;
-      const int nbytes = min(GV_BYTES, row_bytes - kb);
-      const int chunks = nbytes / (Q8 ? 32 : 64);  // 32-element groups in this stage
-      const int kel0 = Q8 ? kb : kb / 2;           // first K index of the stage
-      // A full stage has 32 (Q8_0) or 16 (F16) groups: warp w takes groups
-      // w and w + 16, all loads issued before the MMAs.
-      constexpr int CPW = Q8 ? 2 : 1;
-      Frag<NT> f[CPW];
+      named_sync();
+      if (tid < a.nb) {
+        float tsum = 0.f;
+        for (int i = 0; i < GV_WARPS; i++) tsum += nred[i][tid];
+        nscale[tid] = 1.f / sqrtf(tsum / (float)K + a.eps);
+      }
+      named_sync();
+      for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
+        const float4 wv = *reinterpret_cast<const float4*>(a.norm_w + k);
+        for (int b = 0; b < a.nb; b++) {
+          const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
+          const float sc = nscale[b];
+          half2 h0 = __floats2half2_rn(v.x * sc * wv.x, v.y * sc * wv.y);
+          half2 h1 = __floats2half2_rn(v.z * sc * wv.z, v.w * sc * wv.w);
+          uint2 u2;
+          u2.x = *reinterpret_cast<uint32_t*>(&h0);
+          u2.y = *reinterpret_cast<uint32_t*>(&h1);
+          *reinterpret_cast<uint2*>(xs + (size_t)b * xpitch + k) = u2;
+        }
+      }
+      named_sync();
+    }
+    // the next kernel may start once every CTA is past its last grid barrier
+    if (p == q.n - 1) pdl_trigger();
+    for (int t = w.t0; t < w.t1; t++, T++) {
+      float acc[NT][4];
 #pragma unroll
-      for (int i = 0; i < CPW; i++)
-        if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, warp + i * GV_WARPS, kel0, xs, xpitch, a.nb, g, tq);
+      for (int n = 0; n < NT; n++)
 #pragma unroll
-      for (int i = 0; i < CPW; i++)
-        if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
+        for (int j = 0; j < 4; j++) acc[n][j] = 0.f;
+      for (int ks = 0; ks < w.kstages; ks++) {
+        if (!mbar_wait_sleep(&full[stage], phase, budget)) {
+          if (lane == 0) atomicOr(err, 128u);
+        }
+        const uint8_t* sb = ring + stage * GV_STAGE;
+        const int kb = ks * GV_BYTES;
+        const int nbytes = min(GV_BYTES, row_bytes - kb);
+        const int chunks = nbytes / (Q8 ? 32 : 64);  // 32-element groups in this stage
+        const int kel0 = Q8 ? kb : kb / 2;           // first K index of the stage
+        // A full stage has 32 (Q8_0) or 16 (F16) groups: warp w takes groups
+        // w and w + 16, all loads issued before the MMAs.
+        constexpr int CPW = Q8 ? 2 : 1;
+        Frag<NT> f[CPW];
+#pragma unroll
+        for (int i = 0; i < CPW; i++)
+          if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, warp + i * GV_WARPS, kel0, xs, xpitch, a.nb, g, tq);
+#pragma unroll
+        for (int i = 0; i < CPW; i++)
+          if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == nst) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      // Hand the partial sums (this warp's share of K) to the epilogue warp.
+      const int buf = T & 1;
+      if (!mbar_wait_sleep(&tfree[buf], ((T >> 1) & 1) ^ 1, budget)) {
+        if (lane == 0) atomicOr(err, 256u);
+      }
+      float4* rb = red + buf * (GV_WARPS * NT * 32);
+#pragma unroll
+      for (int n = 0; n < NT; n++) rb[(warp * NT + n) * 32 + lane] = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == nst) {
-        stage = 0;
-        phase ^= 1;
-      }
+      if (lane == 0) mbar_arrive(&tdone[buf]);
     }
-    // Hand the partial sums (this warp's share of K) to the epilogue warp.
-    const int u = t - t0, buf = u & 1;
-    if (!mbar_wait_sleep(&tfree[buf], ((u >> 1) & 1) ^ 1, budget)) {
-      if (lane == 0) atomicOr(a.err, 256u);
-    }
-    float4* rb = red + buf * (GV_WARPS * NT * 32);
-#pragma unroll
-    for (int n = 0; n < NT; n++) rb[(warp * NT + n) * 32 + lane] = make_float4(acc[n][0], acc[n][1], acc[n][2], acc[n][3]);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&tdone[buf]);
   }
 }
 
@@ -560,11 +617,12 @@ constexpr size_t GV_SMEM_BUDGET = 225 * 1024;  // dynamic shared memory per CTA 
 
 // Ring stages that fit beside the staged activations: 2 .. GV_MAX_STAGES,
 // or 0 when even two do not fit.
-static int gemv3_stages(const Gemv3Args& a, int nt) {
-  const size_t off = gv_ring_offset(a.nb, a.K, nt) + 1024;  // + alignment slack
+static int stages_for(int nb, int K, int nt) {
+  const size_t off = gv_ring_offset(nb, K, nt) + 1024;  // + alignment slack
   if (off + 2 * GV_STAGE > GV_SMEM_BUDGET) return 0;
   return (int)std::min<size_t>(GV_MAX_STAGES, (GV_SMEM_BUDGET - off) / GV_STAGE);
 }
+static int gemv3_stages(const Gemv3Args& a, int nt) { return stages_for(a.nb, a.K, nt); }
 
 // Weight-side conditions (packing needs only these).
 static bool gemv3_weights_ok(const Gemv3Args& a) {
@@ -592,26 +650,6 @@ bool gemv3_supported(const Gemv3Args& a) {
   return true;
 }
 
-template <int NT, bool Q8, bool NORM>
-static cudaError_t gemv3_go(const Gemv3Args& a, int tiles, int num_sms, cudaStream_t st) {
-  auto kern = gemv3_kernel<NT, Q8, NORM>;
-  const int nst = gemv3_stages(a, NT);
-  const size_t smem = gv_ring_offset(a.nb, a.K, NT) + 1024 + (size_t)nst * GV_STAGE;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!configured[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GV_SMEM_BUDGET);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return e;
-    configured[dev & 63] = true;
-  }
-  // one CTA per SM, each with a contiguous range of tiles
-  const int grid = std::min(tiles, num_sms);
-  return launch_k(kern, dim3(grid), dim3(GV_THREADS), smem, st, true, a, tiles, nst);
-}
-
 static int gemv3_tiles(const Gemv3Args& a) {
   if (a.mode == GV_QKV) return a.qd / 16 + a.kd / 16 + (a.kd + 15) / 16;
   if (a.mode == GV_SWIGLU) return ((a.interleaved ? a.seg[0].rows / 2 : a.seg[0].rows) + 7) / 8;
@@ -636,18 +674,63 @@ cudaError_t gemv3_pack(const Gemv3Args& a, uint8_t* dst, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st) {
-  if (!gemv3_supported(a) || !a.packed || (reinterpret_cast<uintptr_t>(a.packed) & 15)) return cudaErrorInvalidValue;
-  const int tiles = gemv3_tiles(a);
-  if (tiles <= 0) return cudaSuccess;
-  const bool q8 = a.seg[0].kind == K_Q8_0;
-  const bool norm = a.xres != nullptr;
-  if (a.nb <= 8) {
-    if (q8) return norm ? gemv3_go<1, true, true>(a, tiles, num_sms, st) : gemv3_go<1, true, false>(a, tiles, num_sms, st);
-    return norm ? gemv3_go<1, false, true>(a, tiles, num_sms, st) : gemv3_go<1, false, false>(a, tiles, num_sms, st);
+template <int NT, bool Q8>
+static cudaError_t gemv3_go(const GemvSeq& q, int num_sms, cudaStream_t st) {
+  auto kern = gemv3_kernel<NT, Q8>;
+  const int nst = stages_for(q.ph[0].nb, q.kmax, NT);
+  if (nst < 2) return cudaErrorInvalidValue;
+  const size_t smem = gv_ring_offset(q.ph[0].nb, q.kmax, NT) + 1024 + (size_t)nst * GV_STAGE;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GV_SMEM_BUDGET);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    configured[dev & 63] = true;
   }
-  if (q8) return norm ? gemv3_go<2, true, true>(a, tiles, num_sms, st) : gemv3_go<2, true, false>(a, tiles, num_sms, st);
-  return norm ? gemv3_go<2, false, true>(a, tiles, num_sms, st) : gemv3_go<2, false, false>(a, tiles, num_sms, st);
+  // one CTA per SM, each with a contiguous range of every phase's tiles; a
+  // multi-phase launch is cooperative (its CTAs wait on one another)
+  const int grid = q.n == 1 ? std::min(q.tiles[0], num_sms) : num_sms;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GV_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = q.n > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, q, nst);
+}
+
+cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st) {
+  if (n < 1 || n > 4 || (n > 1 && !gbar)) return cudaErrorInvalidValue;
+  GemvSeq q{};
+  q.n = n;
+  q.gbar = gbar;
+  for (int i = 0; i < n; i++) {
+    const Gemv3Args& a = ph[i];
+    if (!gemv3_supported(a) || !a.packed || (reinterpret_cast<uintptr_t>(a.packed) & 15)) return cudaErrorInvalidValue;
+    if (a.nb != ph[0].nb || a.seg[0].kind != ph[0].seg[0].kind) return cudaErrorInvalidValue;
+    q.ph[i] = a;
+    q.tiles[i] = gemv3_tiles(a);
+    q.kmax = std::max(q.kmax, a.K);
+  }
+  const int nt = ph[0].nb <= 8 ? 1 : 2;
+  if (stages_for(ph[0].nb, q.kmax, nt) < 2) return cudaErrorInvalidValue;
+  const bool q8 = ph[0].seg[0].kind == K_Q8_0;
+  if (nt == 1) return q8 ? gemv3_go<1, true>(q, num_sms, st) : gemv3_go<1, false>(q, num_sms, st);
+  return q8 ? gemv3_go<2, true>(q, num_sms, st) : gemv3_go<2, false>(q, num_sms, st);
+}
+
+cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st) {
+  if (gemv3_tiles(a) <= 0) return cudaSuccess;
+  return gemv3_launch_seq(&a, 1, nullptr, num_sms, st);
 }
 
 }  // namespace laya

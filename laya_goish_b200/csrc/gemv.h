@@ -55,6 +55,17 @@ struct Gemv3Args {
   long long budget;
 };
 
+// Up to four GEMV phases run by one (cooperative) launch, in order, with a
+// grid-wide barrier between consecutive phases: a phase may read what the
+// previous phase wrote.  All phases share the batch rows and the block type.
+struct GemvSeq {
+  Gemv3Args ph[4];
+  int tiles[4];
+  int n;
+  int kmax;        // largest K of the phases (activation staging)
+  unsigned* gbar;  // grid barrier counter, zero at launch (n > 1)
+};
+
 // True when gemv3_launch handles these operands (Q8_0 or F16, K a multiple
 // of 256, at most 16 batch rows, the staged activations fit).
 bool gemv3_supported(const Gemv3Args& a);
@@ -64,5 +75,7 @@ bool gemv3_supported(const Gemv3Args& a);
 size_t gemv3_packed_bytes(const Gemv3Args& a);
 cudaError_t gemv3_pack(const Gemv3Args& a, uint8_t* dst, cudaStream_t st);
 cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st);
+// Runs ph[0..n-1] as one launch; gbar must be zero when the launch starts.
+cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st);
 
 }  // namespace laya
