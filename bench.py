@@ -436,6 +436,33 @@ def run_decode(args):
     print(json.dumps(out), flush=True)
 
 
+def run_load(args):
+    """Start-up cost: one laya_open of a synthetic GGUF onto GPUs 0..N-1 from
+    one process (the C ABI's multi-device model).  The file is opened once
+    untimed first, so the page cache holds it and the timed open measures the
+    upload path, not the disk.  Not the contract line."""
+    import torch
+
+    from laya_goish_b200 import engine
+
+    n = max(1, args.gpus)
+    if torch.cuda.device_count() < n:
+        raise SystemExit(f"--workload load needs {n} visible GPUs")
+    path = synth.model_path(args.load_cfg)
+    file_gb = os.path.getsize(path) / 1e9
+    engine.Engine(path, devices=[0]).close()  # page cache warm-up
+    t0 = time.perf_counter()
+    e = engine.Engine(path, devices=list(range(n)))
+    dt = time.perf_counter() - t0
+    info = e.info
+    e.close()
+    rep_gb = info["device_bytes"] / 1e9
+    out = {"workload": f"load {args.load_cfg} onto {n} GPU(s)", "open_s": dt, "file_gb": file_gb,
+           "replica_gb": rep_gb, "replicas_gb_per_s": n * rep_gb / dt,
+           "peer_copies": n > 1 and os.environ.get("LAYA_LOAD_PEER", "1") != "0"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -443,7 +470,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3", "load"])
+    ap.add_argument("--load-cfg", default="cfg3", help="load: synthetic model to open")
     ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
     ap.add_argument("--gen", type=int, default=128, help="decode: generated tokens")
@@ -454,6 +482,8 @@ def main():
         args.warmup = 3
     if args.workload == "decode":
         run_decode(args)
+    elif args.workload == "load":
+        run_load(args)
     elif args.workload in AUX:
         run_aux(args)
     elif args.impl == "reference":

@@ -1,5 +1,6 @@
 // extern "C" entry points of laya_cuda.h.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <thread>
@@ -34,8 +35,30 @@ static int open_common(Gguf& g, const int* devices, int n_devices, laya_model** 
   std::string e = read_config(g, &h->m.cfg);
   if (!e.empty()) return fail(LAYA_E_FORMAT, e);
   h->m.reps.resize(devs.size());
-  for (size_t i = 0; i < devs.size(); i++) {
+  {
+    // create the devices' contexts at once (a few hundred ms each)
+    std::vector<int> uniq(devs);
+    std::sort(uniq.begin(), uniq.end());
+    uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+    std::vector<std::thread> ts;
+    for (int d : uniq)
+      ts.emplace_back([d] {
+        if (cudaSetDevice(d) == cudaSuccess) cudaFree(nullptr);
+      });
+    for (auto& t : ts) t.join();
+  }
+  // One replica from the file; the others copied device to device over
+  // NVLink (LAYA_LOAD_PEER=0: every replica from the file).
+  const char* pe = std::getenv("LAYA_LOAD_PEER");
+  const bool peer = !(pe && pe[0] == '0');
+  for (size_t i = 0; i < (peer ? 1 : devs.size()); i++) {
     if (int rc = load_replica(h->m, g, devs[i], h->m.reps[i])) {
+      for (auto& r : h->m.reps) free_replica(r);
+      return rc;
+    }
+  }
+  if (peer && devs.size() > 1) {
+    if (int rc = mirror_replicas(h->m, devs)) {
       for (auto& r : h->m.reps) free_replica(r);
       return rc;
     }

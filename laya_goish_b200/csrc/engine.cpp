@@ -214,12 +214,22 @@ static int dmalloc(Replica& r, size_t bytes, void** p) {
   cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (weights)");
   r.allocs.push_back(*p);
+  if (r.loading) r.wmap.emplace_back(*p, bytes ? bytes : 16);
   r.weight_bytes += bytes;
   return 0;
 }
+
+// Host -> device weight copy.  The source is mostly the mmap'd GGUF file;
+// the driver's pageable copy pins and streams it (a pinned staging ring
+// filled by host threads measured no faster: the page faults on the mapping
+// bound both).
+static cudaError_t h2d(void* dst, const void* src, size_t n) {
+  return cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice);
+}
+
 static int upload(Replica& r, const void* src, size_t bytes, void** p) {
   if (int rc = dmalloc(r, bytes, p)) return rc;
-  LAYA_CK(cudaMemcpy(*p, src, bytes, cudaMemcpyHostToDevice));
+  LAYA_CK(h2d(*p, src, bytes));
   return 0;
 }
 
@@ -332,8 +342,7 @@ static int place_f16(const Gguf& g, const std::string& name, int rows, int cols,
   const int nblk = (rows + grp - 1) / grp;
   for (int bidx = 0; bidx < nblk; bidx++) {
     const int r0 = bidx * grp, cnt = std::min(grp, rows - r0);
-    LAYA_CK(cudaMemcpy(dst + ((size_t)bidx * gstride + goff) * cols, src + (size_t)r0 * cols, row_bytes * cnt,
-                       cudaMemcpyHostToDevice));
+    LAYA_CK(h2d(dst + ((size_t)bidx * gstride + goff) * cols, src + (size_t)r0 * cols, row_bytes * cnt));
   }
   return 0;
 }
@@ -359,8 +368,7 @@ static int upload_vector(Replica& r, const Gguf& g, const std::string& name, int
   return 0;
 }
 
-int load_replica(Model& m, const Gguf& g, int device, Replica& r) {
-  const Config& c = m.cfg;
+static int init_device(int device, Replica& r) {
   r.device = device;
   LAYA_CK(cudaSetDevice(device));
   cudaDeviceProp prop;
@@ -368,6 +376,24 @@ int load_replica(Model& m, const Gguf& g, int device, Replica& r) {
   if (prop.major != 10) return fail(LAYA_E_CUDA, std::string("device ") + prop.name + " is not an sm_100 GPU");
   r.num_sms = prop.multiProcessorCount;
   LAYA_CK(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking));
+  return 0;
+}
+
+static int load_weights(Model& m, const Gguf& g, Replica& r);
+
+int load_replica(Model& m, const Gguf& g, int device, Replica& r) {
+  if (int rc = init_device(device, r)) return rc;
+  r.loading = true;
+  const int rc = load_weights(m, g, r);
+  r.loading = false;
+  if (rc) return rc;
+  LAYA_CK(cudaMemsetAsync(r.err, 0, 16, r.stream));
+  LAYA_CK(cudaStreamSynchronize(r.stream));
+  return 0;
+}
+
+static int load_weights(Model& m, const Gguf& g, Replica& r) {
+  const Config& c = m.cfg;
   const int qd = c.H * c.hd, kd = c.KV * c.hd, d = c.d;
   int rc;
   r.layers.resize(c.L);
@@ -467,7 +493,114 @@ int load_replica(Model& m, const Gguf& g, int device, Replica& r) {
   void* e;
   if ((rc = dmalloc(r, 16, &e))) return rc;
   r.err = static_cast<unsigned*>(e);
-  LAYA_CK(cudaMemset(r.err, 0, 16));
+  return 0;
+}
+
+// Pointer relocation from a source replica's weight buffers to a copy's.
+class Reloc {
+ public:
+  Reloc(const std::vector<std::pair<void*, size_t>>& src, const std::vector<void*>& dst) {
+    for (size_t i = 0; i < src.size(); i++) map_.push_back({static_cast<char*>(src[i].first), src[i].second,
+                                                            static_cast<char*>(dst[i])});
+    std::sort(map_.begin(), map_.end(), [](const E& a, const E& b) { return a.s < b.s; });
+  }
+  bool ok = true;
+  template <class T>
+  T* operator()(T* p) {
+    if (!p) return p;
+    const char* c = reinterpret_cast<const char*>(p);
+    auto it = std::upper_bound(map_.begin(), map_.end(), c, [](const char* v, const E& e) { return v < e.s; });
+    if (it == map_.begin() || c >= (it - 1)->s + (it - 1)->n) {
+      ok = false;
+      return nullptr;
+    }
+    --it;
+    return reinterpret_cast<T*>(it->d + (c - it->s));
+  }
+  QTensor operator()(QTensor t) {
+    t.q = (*this)(t.q);
+    t.s = (*this)(t.s);
+    t.qh = (*this)(t.qh);
+    t.sc = (*this)(t.sc);
+    return t;
+  }
+
+ private:
+  struct E {
+    char* s;
+    size_t n;
+    char* d;
+  };
+  std::vector<E> map_;
+};
+
+// Allocates src's weight buffers on r's device and queues their copies on
+// r's stream; the pointers of r are src's, relocated.
+static int mirror_from(const Replica& src, Replica& r) {
+  LAYA_CK(cudaSetDevice(r.device));
+  std::vector<void*> dst(src.wmap.size());
+  r.loading = true;
+  for (size_t i = 0; i < src.wmap.size(); i++) {
+    if (int rc = dmalloc(r, src.wmap[i].second, &dst[i])) {
+      r.loading = false;
+      return rc;
+    }
+    LAYA_CK(cudaMemcpyPeerAsync(dst[i], r.device, src.wmap[i].first, src.device, src.wmap[i].second, r.stream));
+  }
+  r.loading = false;
+  Reloc rl(src.wmap, dst);
+  r.layers.resize(src.layers.size());
+  for (size_t l = 0; l < src.layers.size(); l++) {
+    const Layer& a = src.layers[l];
+    Layer& b = r.layers[l];
+    b.attn_norm = rl(a.attn_norm);
+    b.ffn_norm = rl(a.ffn_norm);
+    b.wq = rl(a.wq);
+    b.wk = rl(a.wk);
+    b.wv = rl(a.wv);
+    b.wo = rl(a.wo);
+    b.wg = rl(a.wg);
+    b.wu = rl(a.wu);
+    b.wd = rl(a.wd);
+    b.bqkv = rl(a.bqkv);
+    b.wqkv16 = rl(a.wqkv16);
+    b.wgu16 = rl(a.wgu16);
+    b.wo16 = rl(a.wo16);
+    b.wd16 = rl(a.wd16);
+  }
+  r.embd = rl(src.embd);
+  r.head = rl(src.head);
+  r.out_norm = rl(src.out_norm);
+  r.head16 = rl(src.head16);
+  r.rope = rl(src.rope);
+  r.err = rl(src.err);
+  for (const auto& kv : src.named) r.named[kv.first] = rl(kv.second);
+  if (!rl.ok) return fail(LAYA_E_CUDA, "replica copy: a weight pointer lies outside the loaded buffers");
+  LAYA_CK(cudaMemsetAsync(r.err, 0, 16, r.stream));
+  return 0;
+}
+
+int mirror_replicas(Model& m, const std::vector<int>& devices) {
+  std::vector<int> have = {0};
+  size_t next = 1;
+  while (next < devices.size()) {
+    std::vector<int> fresh;
+    for (int s : std::vector<int>(have)) {
+      if (next >= devices.size()) break;
+      Replica& r = m.reps[next];
+      if (int rc = init_device(devices[next], r)) return rc;
+      // the copy reads the source device's buffers: wait for them to be filled
+      LAYA_CK(cudaSetDevice(m.reps[s].device));
+      LAYA_CK(cudaStreamSynchronize(m.reps[s].stream));
+      if (int rc = mirror_from(m.reps[s], r)) return rc;
+      fresh.push_back((int)next++);
+    }
+    for (int i : fresh) {
+      LAYA_CK(cudaSetDevice(m.reps[i].device));
+      LAYA_CK(cudaStreamSynchronize(m.reps[i].stream));
+      have.push_back(i);
+    }
+  }
   return 0;
 }
 

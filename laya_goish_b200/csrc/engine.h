@@ -82,6 +82,11 @@ struct Replica {
   int device = 0, num_sms = 148;
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
+  // (address, bytes) of every weight allocation made while loading, in
+  // allocation order: another replica of the same model is these buffers
+  // copied device to device, with its pointers relocated
+  std::vector<std::pair<void*, size_t>> wmap;
+  bool loading = false;
   size_t weight_bytes = 0;
   std::vector<Layer> layers;
   QTensor embd{}, head{};
@@ -129,6 +134,11 @@ struct PassPlan {
 
 std::string read_config(const Gguf& g, Config* c);
 int load_replica(Model& m, const Gguf& g, int device, Replica& r);
+// Copies loaded replicas to the other devices over NVLink: replicas[0] is
+// loaded from the file, then every loaded replica copies itself to one
+// unloaded device per round (1 -> 2 -> 4 -> 8 replicas).  Devices without
+// peer access copy through the host (cudaMemcpyPeerAsync).
+int mirror_replicas(Model& m, const std::vector<int>& devices);
 void free_replica(Replica& r);
 int ensure_kv(Model& m, Replica& r, int pages);
 int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>& tables, int read_base,

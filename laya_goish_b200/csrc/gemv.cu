@@ -339,16 +339,18 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
     cta_epi_sync();
     if (threadIdx.x == 0) {
       __threadfence();
-      atomicAdd(q.gbar, 1u);
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(q.gbar) : "memory");
       const unsigned target = (unsigned)p * gridDim.x;
-      long long t0 = clock64();
-      while (atomicAdd(q.gbar, 0u) < target) {
+      const long long t0 = clock64();
+      unsigned v;
+      while (true) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(q.gbar) : "memory");
+        if (v >= target) break;
         if (clock64() - t0 > budget) {
           atomicOr(err, 4096u);
           break;
         }
       }
-      __threadfence();
     }
     cta_epi_sync();
   };

@@ -169,3 +169,26 @@ def test_multi_replica_sharding_matches_single(tiny_paths):
     for i in range(len(prompts)):
         for j in range(len(qs)):
             assert np.allclose(a[i][j]["probabilities"], b[i][j]["probabilities"], atol=1e-5), (i, j)
+
+
+@pytest.mark.parametrize("peer", ["1", "0"])
+def test_replicas_on_distinct_gpus(tiny_paths, monkeypatch, peer):
+    # Replicas on other GPUs are copied from the first over NVLink (or, with
+    # LAYA_LOAD_PEER=0, each read from the file); both give the one-GPU answers.
+    import torch
+
+    n = min(torch.cuda.device_count(), 4)
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    monkeypatch.setenv("LAYA_LOAD_PEER", peer)
+    path = tiny_paths["small-llama-q8_0"] if "small-llama-q8_0" in tiny_paths else tiny_paths["tiny-llama-q8_0"]
+    rng = np.random.default_rng(12)
+    prompts = [synth.token_ids(rng, 1000, int(n_)) for n_ in (40, 7, 300, 64, 90, 12, 128, 33)]
+    qs = [Question("choice", [10, 11, 12, 13])]
+    with engine.Engine(path, devices=[0]) as one, engine.Engine(path, devices=list(range(n))) as many:
+        assert many.info["n_devices"] == n
+        assert many.info["device_bytes"] == one.info["device_bytes"]
+        a = one.decide_batch(prompts, qs)
+        b = many.decide_batch(prompts, qs)
+    for i in range(len(prompts)):
+        assert np.allclose(a[i][0]["probabilities"], b[i][0]["probabilities"], atol=1e-5), i
