@@ -1,0 +1,334 @@
+"""Batch front end over the decision hot path: the request handling of the
+reference's HTTP server (`/v1/decide`, `/v1/decide/batch`,
+src/server.rs:65-332) and of its JSON-lines daemon (src/main.rs:139-151),
+calling one batched `Engine.decide_batch` (laya_decide_batch) per request.
+
+What is kept from the reference, in the same order:
+
+* routes and methods: unknown path -> 404 `not_found_error`; wrong method ->
+  405 with `Allow` (src/server.rs:82-95);
+* the body must parse as JSON (400) and be an object with a `state`
+  (422, src/server.rs:65-75, 221-227);
+* `/v1/decide/batch`: `states` is an array of 1..256 states sharing
+  `questions` (src/server.rs:235-258);
+* the whole batch is validated before any work starts, the first failure is
+  a 422, and at most 256 questions are counted over the batch
+  (src/server.rs:259-282);
+* one inference at a time: a second request while one runs gets 429
+  `busy_error` with `Retry-After: 1` (src/server.rs:283-297);
+* a canceled call maps to 408 `request_canceled`, any other failure to 500
+  `internal_error`; success is 200 with `X-Response-Time-Ms`, answers in
+  request order (src/server.rs:298-331);
+* the daemon answers each non-empty input line with one output line, the
+  result or `{"error": message}` (src/main.rs:139-151).
+
+Requests are token-level, because the tokenizer and prompt templates sit
+above this boundary: `state` is the prompt's token ids (a list, or an object
+with `ids`), and every option of a question is a token id or a list of ids
+(a continuation).  Question objects follow src/models/laya/decision.rs:19-98:
+
+    {"type": "choice", "criteria": {"label": id | [ids], ...}, "suffix": [ids]}
+    {"type": "score",  "criteria": [id | [ids], ...]}          (>= 2 levels)
+    {"type": "noul",   "criteria": {"false": id | [ids], "true": id | [ids]}}
+
+Answers follow src/models/laya/decision.rs:214-268 (`choice` label, `score`
+with its `legend`, `noul`, `confidence`, `probabilities` by label; `logits`
+when raw).  The Laya encoder's `action` head is not part of this path.
+Authentication, presets, the model registry and draining are not part of it
+either.
+"""
+from __future__ import annotations
+
+import json
+import sys
+import threading
+import time
+from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+from typing import Callable
+
+from ._lib import E_CANCELED, E_INVALID, LayaError
+
+MAX_STATES = 256
+MAX_QUESTIONS = 256
+MAX_OPTIONS = 16
+MAX_BODY = 1024 * 1024  # src/server.rs:22
+
+ROUTES = {"/health": "GET, HEAD", "/v1/decide": "POST", "/v1/decide/batch": "POST"}
+
+
+class RequestError(ValueError):
+    """A request that fails validation (422 over HTTP)."""
+
+
+def _ids(v, what: str) -> list[int]:
+    if isinstance(v, bool) or not isinstance(v, (int, list)):
+        raise RequestError(f"{what} must be a token id or a list of token ids")
+    ids = [v] if isinstance(v, int) else v
+    if not ids or any(isinstance(t, bool) or not isinstance(t, int) for t in ids):
+        raise RequestError(f"{what} must be a token id or a non-empty list of token ids")
+    return ids
+
+
+def state_ids(state) -> list[int]:
+    """The prompt of one request: a list of token ids, or {"ids": [...]}."""
+    if isinstance(state, dict):
+        state = state.get("ids")
+    if not isinstance(state, list) or not state:
+        raise RequestError("state must be a non-empty list of token ids (or an object with ids)")
+    return _ids(state, "state")
+
+
+class ParsedQuestion:
+    def __init__(self, qid: str, kind: str, labels: list[str], options: list[list[int]], suffix: list[int]):
+        self.id, self.kind, self.labels, self.options, self.suffix = qid, kind, labels, options, suffix
+
+
+def parse_questions(obj) -> list[ParsedQuestion]:
+    """src/models/laya/decision.rs:19-98 on token-level criteria."""
+    if not isinstance(obj, dict) or not obj or len(obj) > MAX_QUESTIONS:
+        raise RequestError("questions must contain 1..256 named questions")
+    out = []
+    for qid, q in obj.items():
+        if not isinstance(q, dict):
+            raise RequestError(f"{qid}: question must be an object")
+        kind = q.get("type")
+        if kind not in ("choice", "score", "noul"):
+            raise RequestError(f"{qid}: type must be choice, score, or noul")
+        c = q.get("criteria")
+        if kind == "choice":
+            if not isinstance(c, dict) or not c:
+                raise RequestError(f"{qid}: choice requires a criteria object")
+            labels = list(c)
+            opts = [_ids(c[k], f"{qid}.{k}") for k in labels]
+        elif kind == "score":
+            if not isinstance(c, list) or len(c) < 2:
+                raise RequestError(f"{qid}: score requires at least two ordered criteria")
+            labels = [str(i) for i in range(len(c))]
+            opts = [_ids(v, f"{qid}[{i}]") for i, v in enumerate(c)]
+        else:
+            if not isinstance(c, dict) or "false" not in c or "true" not in c:
+                raise RequestError(f"{qid}: noul requires criteria with false and true token ids")
+            labels = ["false", "true"]
+            opts = [_ids(c["false"], f"{qid}.false"), _ids(c["true"], f"{qid}.true")]
+        if not opts or len(opts) > MAX_OPTIONS:
+            raise RequestError(f"{qid}: requires 1..16 options")
+        if len({len(o) for o in opts}) != 1:
+            raise RequestError(f"{qid}: all options must have the same number of tokens")
+        suffix = q.get("suffix", [])
+        if suffix is None:
+            suffix = []
+        if not isinstance(suffix, list) or any(isinstance(t, bool) or not isinstance(t, int) for t in suffix):
+            raise RequestError(f"{qid}: suffix must be a list of token ids")
+        out.append(ParsedQuestion(str(qid), kind, labels, opts, suffix))
+    return out
+
+
+def _engine_questions(qs: list[ParsedQuestion]):
+    from .engine import Question
+
+    return [Question(q.kind, [o[0] for o in q.options] if len(q.options[0]) == 1 else q.options, q.suffix)
+            for q in qs]
+
+
+def answer_json(q: ParsedQuestion, a: dict, raw: bool) -> dict:
+    """src/models/laya/decision.rs:214-268 for one question."""
+    p = a["probabilities"]
+    out = {"type": q.kind}
+    if q.kind == "choice":
+        out["choice"] = q.labels[a["choice"]]
+    elif q.kind == "score":
+        out["score"] = a["score"]
+        out["legend"] = {str(i): o if len(o) > 1 else o[0] for i, o in enumerate(q.options)}
+    else:
+        out["noul"] = a["noul"]
+    out["confidence"] = a["confidence"]
+    out["probabilities"] = {lab: v for lab, v in zip(q.labels, p)}
+    if raw:
+        out["logits"] = a["logits"]
+    return out
+
+
+class Response:
+    def __init__(self, status: int, body: dict, headers: dict | None = None):
+        self.status, self.body, self.headers = status, body, headers or {}
+
+    def json(self) -> str:
+        return json.dumps(self.body) + "\n"
+
+
+def _error(status: int, kind: str, message: str, headers: dict | None = None) -> Response:
+    return Response(status, {"error": {"type": kind, "message": message}}, headers)
+
+
+class DecideService:
+    """The server's request handling around one loaded Engine (or any object
+    with the same `validate` / `decide_batch` / `info` interface)."""
+
+    def __init__(self, engine, raw: bool = False):
+        self.engine = engine
+        self.raw = raw
+        self._busy = threading.Lock()
+        self._requests = 0
+        self._count_lock = threading.Lock()
+
+    def _prepare(self, req) -> tuple[list[list[int]], list[ParsedQuestion]]:
+        if not isinstance(req, dict):
+            raise RequestError("request body must be a JSON object")
+        if req.get("state") is None:
+            raise RequestError("state is required")
+        return [state_ids(req["state"])], parse_questions(req.get("questions"))
+
+    def handle(self, method: str, path: str, body: bytes | str | None,
+               canceled: Callable[[], bool] | None = None) -> Response:
+        with self._count_lock:
+            self._requests += 1
+            rid = self._requests
+        r = self._handle(method, path, body, canceled)
+        r.headers.setdefault("X-Request-Id", f"laya-{rid}")
+        return r
+
+    def _handle(self, method, path, body, canceled) -> Response:
+        allowed = ROUTES.get(path)
+        if allowed is None:
+            return _error(404, "not_found_error", "Endpoint not found")
+        if (allowed == "POST") != (method == "POST") or (allowed != "POST" and method not in ("GET", "HEAD")):
+            return _error(405, "invalid_request_error", "Method not allowed", {"Allow": allowed})
+        if path == "/health":
+            return Response(200, {"status": "ok", "layers": self.engine.layers()})
+        if body is not None and len(body) > MAX_BODY:
+            return _error(413, "invalid_request_error", "request body too large")
+        try:
+            req = json.loads(body or b"")
+        except (ValueError, UnicodeDecodeError) as e:
+            return _error(400, "invalid_request_error", str(e))
+        batch = path == "/v1/decide/batch"
+        # Validate the whole batch before starting any expensive work.
+        try:
+            if batch:
+                if not isinstance(req, dict):
+                    raise RequestError("request body must be a JSON object")
+                states = req.get("states")
+                if not isinstance(states, list) or not 1 <= len(states) <= MAX_STATES:
+                    raise RequestError("states must be an array of 1..256 states")
+                prompts = [state_ids(s) for s in states]
+                qs = parse_questions(req.get("questions"))
+            else:
+                prompts, qs = self._prepare(req)
+            eqs = _engine_questions(qs)
+            self.engine.validate(prompts, eqs)
+            if len(qs) * len(prompts) > MAX_QUESTIONS:
+                raise RequestError("At most 256 total questions per request")
+        except RequestError as e:
+            return _error(422, "invalid_request_error", str(e))
+        except LayaError as e:
+            if e.code == E_INVALID:
+                return _error(422, "invalid_request_error", e.message)
+            return _error(500, "internal_error", e.message)
+        if not self._busy.acquire(blocking=False):
+            return _error(429, "busy_error", "An inference request is running; retry later", {"Retry-After": "1"})
+        try:
+            start = time.perf_counter()
+            try:
+                ans = self.engine.decide_batch(prompts, eqs, canceled=canceled)
+            except LayaError as e:
+                if e.code == E_CANCELED:
+                    return _error(408, "request_canceled", e.message)
+                return _error(500, "internal_error", e.message)
+            ms = int((time.perf_counter() - start) * 1000)
+        finally:
+            self._busy.release()
+        results = []
+        for prompt, row in zip(prompts, ans):
+            tokens = sum(len(prompt) + len(q.suffix) for q in qs)
+            results.append({"model": self.engine.info.get("architecture"),
+                            "answers": {q.id: answer_json(q, a, self.raw) for q, a in zip(qs, row)},
+                            "usage": {"tokens": tokens}})
+        body = {"results": results} if batch else results[0]
+        return Response(200, body, {"X-Response-Time-Ms": str(ms)})
+
+
+def run_daemon(service: DecideService, inp=None, out=None) -> None:
+    """JSON lines: each non-empty input line is one /v1/decide body; the
+    answer or {"error": message} is written as one line (src/main.rs:139-151)."""
+    inp = inp or sys.stdin
+    out = out or sys.stdout
+    for line in inp:
+        if not line.strip():
+            continue
+        r = service.handle("POST", "/v1/decide", line)
+        if r.status == 200:
+            out.write(r.json())
+        else:
+            out.write(json.dumps({"error": r.body["error"]["message"]}) + "\n")
+        out.flush()
+
+
+def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 8080) -> ThreadingHTTPServer:
+    """An HTTP server over `service` (serve with .serve_forever())."""
+
+    class Handler(BaseHTTPRequestHandler):
+        protocol_version = "HTTP/1.1"
+
+        def _go(self, method):
+            n = int(self.headers.get("Content-Length") or 0)
+            if n > MAX_BODY:
+                r = _error(413, "invalid_request_error", "request body too large")
+            else:
+                body = self.rfile.read(n) if n else b""
+                r = service.handle(method, self.path.split("?", 1)[0], body)
+            data = r.json().encode()
+            self.send_response(r.status)
+            self.send_header("Content-Type", "application/json; charset=utf-8")
+            self.send_header("Cache-Control", "no-store")
+            self.send_header("X-Content-Type-Options", "nosniff")
+            self.send_header("Content-Length", str(len(data)))
+            for k, v in r.headers.items():
+                self.send_header(k, v)
+            self.end_headers()
+            if method != "HEAD":
+                self.wfile.write(data)
+
+        def do_GET(self):
+            self._go("GET")
+
+        def do_HEAD(self):
+            self._go("HEAD")
+
+        def do_POST(self):
+            self._go("POST")
+
+        def log_message(self, *a):
+            pass
+
+    return ThreadingHTTPServer((host, port), Handler)
+
+
+def main(argv=None) -> int:
+    import argparse
+
+    from .engine import Engine
+
+    ap = argparse.ArgumentParser(prog="python -m laya_goish_b200.frontend")
+    ap.add_argument("model", help="GGUF file")
+    ap.add_argument("mode", choices=["daemon", "serve"])
+    ap.add_argument("--devices", default="0", help="comma-separated CUDA devices")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8080)
+    ap.add_argument("--raw", action="store_true")
+    a = ap.parse_args(argv)
+    eng = Engine(a.model, devices=[int(d) for d in a.devices.split(",")])
+    svc = DecideService(eng, raw=a.raw)
+    if a.mode == "daemon":
+        run_daemon(svc)
+    else:
+        srv = make_server(svc, a.host, a.port)
+        try:
+            srv.serve_forever()
+        finally:
+            srv.server_close()
+    eng.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,195 @@
+"""Host logic of the batch front end (src/server.rs:65-332, src/main.rs:139-151)
+against a fake engine: routes, validation order, busy, cancel, errors, order."""
+import io
+import json
+import threading
+
+import pytest
+
+from laya_goish_b200 import frontend
+from laya_goish_b200._lib import E_CANCELED, E_CUDA, E_INVALID, LayaError
+
+
+class FakeEngine:
+    """Answers choice with the option whose first token id is largest."""
+
+    info = {"architecture": "llama"}
+
+    def __init__(self, vocab=1000):
+        self.vocab = vocab
+        self.calls = []
+        self.gate = None
+        self.fail = None
+
+    def layers(self):
+        return 2
+
+    def validate(self, prompts, questions):
+        for p in prompts:
+            if any(t < 0 or t >= self.vocab for t in p):
+                raise LayaError(E_INVALID, "token id out of range")
+
+    def decide_batch(self, prompts, questions, canceled=None):
+        self.calls.append((len(prompts), len(questions)))
+        if self.gate:
+            self.gate.wait(5)
+        if canceled and canceled():
+            raise LayaError(E_CANCELED, "request canceled")
+        if self.fail:
+            raise LayaError(self.fail, "boom")
+        out = []
+        for p in prompts:
+            row = []
+            for q in questions:
+                _, opts, _ = q.arrays()
+                k = opts.shape[0]
+                best = int(max(range(k), key=lambda i: (opts[i, 0] + p[0]) % 7))
+                probs = [0.0] * k
+                probs[best] = 1.0
+                row.append({"type": q.kind, "probabilities": probs, "logits": [float(i) for i in range(k)],
+                            "confidence": 1.0, "choice": best, "score": float(best), "noul": probs[-1]})
+            out.append(row)
+        return out
+
+
+CHOICE = {"pick": {"type": "choice", "criteria": {"a": 5, "b": 6, "c": 7}}}
+
+
+def body(**kw):
+    return json.dumps(kw).encode()
+
+
+def test_routes_and_methods():
+    s = frontend.DecideService(FakeEngine())
+    assert s.handle("GET", "/nope", None).status == 404
+    r = s.handle("GET", "/v1/decide", None)
+    assert r.status == 405 and r.headers["Allow"] == "POST"
+    assert s.handle("POST", "/health", b"").status == 405
+    r = s.handle("GET", "/health", None)
+    assert r.status == 200 and r.body["status"] == "ok"
+    assert r.headers["X-Request-Id"].startswith("laya-")
+
+
+def test_bad_json_and_validation():
+    s = frontend.DecideService(FakeEngine())
+    assert s.handle("POST", "/v1/decide", b"{").status == 400
+    r = s.handle("POST", "/v1/decide", body(questions=CHOICE))
+    assert r.status == 422 and "state" in r.body["error"]["message"]
+    r = s.handle("POST", "/v1/decide", body(state=[1, 2], questions={"q": {"type": "bogus"}}))
+    assert r.status == 422 and "type must be" in r.body["error"]["message"]
+    r = s.handle("POST", "/v1/decide", body(state=[1, 2], questions={"q": {"type": "score", "criteria": [1]}}))
+    assert r.status == 422
+    r = s.handle("POST", "/v1/decide", body(state=[1, 2], questions={"q": {"type": "noul", "criteria": {"true": 3}}}))
+    assert r.status == 422
+    r = s.handle("POST", "/v1/decide", body(state=[1, 2],
+                                           questions={"q": {"type": "choice", "criteria": {"a": 1, "b": [2, 3]}}}))
+    assert r.status == 422 and "same number of tokens" in r.body["error"]["message"]
+    r = s.handle("POST", "/v1/decide", body(state=[1, 5000], questions=CHOICE))
+    assert r.status == 422 and "out of range" in r.body["error"]["message"]
+    many = {f"q{i}": {"type": "choice", "criteria": {"a": 1, "b": 2}} for i in range(257)}
+    assert s.handle("POST", "/v1/decide", body(state=[1], questions=many)).status == 422
+
+
+def test_batch_validates_everything_first():
+    eng = FakeEngine()
+    s = frontend.DecideService(eng)
+    assert s.handle("POST", "/v1/decide/batch", body(states=[], questions=CHOICE)).status == 422
+    assert s.handle("POST", "/v1/decide/batch", body(states=[[1]] * 257, questions=CHOICE)).status == 422
+    # one bad state anywhere fails the batch before any inference
+    r = s.handle("POST", "/v1/decide/batch", body(states=[[1, 2], [3], [9999]], questions=CHOICE))
+    assert r.status == 422 and eng.calls == []
+    # 2 questions x 129 states > 256
+    two = {"x": CHOICE["pick"], "y": CHOICE["pick"]}
+    r = s.handle("POST", "/v1/decide/batch", body(states=[[1]] * 129, questions=two))
+    assert r.status == 422 and "256" in r.body["error"]["message"] and eng.calls == []
+
+
+def test_batch_answers_in_order_one_call():
+    eng = FakeEngine()
+    s = frontend.DecideService(eng)
+    states = [[i, 2, 3] for i in range(10)]
+    r = s.handle("POST", "/v1/decide/batch", body(states=states, questions=CHOICE))
+    assert r.status == 200 and eng.calls == [(10, 1)]
+    assert "X-Response-Time-Ms" in r.headers
+    res = r.body["results"]
+    assert len(res) == 10
+    for i, st in enumerate(states):
+        want = max(range(3), key=lambda k: ([5, 6, 7][k] + st[0]) % 7)
+        a = res[i]["answers"]["pick"]
+        assert a["choice"] == "abc"[want]
+        assert set(a["probabilities"]) == {"a", "b", "c"}
+        assert res[i]["usage"]["tokens"] == 3
+
+
+def test_score_and_noul_shapes():
+    s = frontend.DecideService(FakeEngine(), raw=True)
+    q = {"s": {"type": "score", "criteria": [[4, 5], [6, 7], [8, 9]]},
+         "n": {"type": "noul", "criteria": {"false": 3, "true": 4}, "suffix": [1, 2]}}
+    r = s.handle("POST", "/v1/decide", body(state={"ids": [1, 2]}, questions=q))
+    assert r.status == 200
+    a = r.body["answers"]
+    assert set(a["s"]) >= {"score", "legend", "confidence", "probabilities", "logits"}
+    assert a["s"]["legend"] == {"0": [4, 5], "1": [6, 7], "2": [8, 9]}
+    assert set(a["n"]["probabilities"]) == {"false", "true"} and "noul" in a["n"]
+    assert r.body["usage"]["tokens"] == 2 + 4
+
+
+def test_busy_cancel_and_internal_errors():
+    eng = FakeEngine()
+    s = frontend.DecideService(eng)
+    eng.gate = threading.Event()
+    first = {}
+    t = threading.Thread(target=lambda: first.update(r=s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE))))
+    t.start()
+    for _ in range(500):
+        if eng.calls:
+            break
+        threading.Event().wait(0.01)
+    r = s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE))
+    assert r.status == 429 and r.headers["Retry-After"] == "1" and r.body["error"]["type"] == "busy_error"
+    eng.gate.set()
+    t.join()
+    assert first["r"].status == 200
+    eng.gate = None
+    r = s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE), canceled=lambda: True)
+    assert r.status == 408 and r.body["error"]["type"] == "request_canceled"
+    eng.fail = E_CUDA
+    r = s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE))
+    assert r.status == 500 and r.body["error"]["type"] == "internal_error"
+    eng.fail = None
+    assert s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE)).status == 200  # busy flag released
+
+
+def test_daemon_lines():
+    s = frontend.DecideService(FakeEngine())
+    inp = io.StringIO(json.dumps({"state": [1, 2], "questions": CHOICE}) + "\n\n{bad\n" +
+                      json.dumps({"state": [1], "questions": {"q": {"type": "x"}}}) + "\n")
+    out = io.StringIO()
+    frontend.run_daemon(s, inp, out)
+    lines = [json.loads(x) for x in out.getvalue().splitlines()]
+    assert len(lines) == 3
+    assert "answers" in lines[0]
+    assert "error" in lines[1] and "error" in lines[2]
+
+
+def test_http_round_trip():
+    import urllib.error
+    import urllib.request
+
+    srv = frontend.make_server(frontend.DecideService(FakeEngine()), "127.0.0.1", 0)
+    th = threading.Thread(target=srv.serve_forever, daemon=True)
+    th.start()
+    try:
+        url = f"http://127.0.0.1:{srv.server_address[1]}"
+        req = urllib.request.Request(url + "/v1/decide/batch", data=body(states=[[1], [2]], questions=CHOICE),
+                                     method="POST")
+        with urllib.request.urlopen(req, timeout=10) as r:
+            assert r.status == 200
+            assert r.headers["Content-Type"].startswith("application/json")
+            assert len(json.loads(r.read())["results"]) == 2
+        with pytest.raises(urllib.error.HTTPError) as e:
+            urllib.request.urlopen(url + "/missing", timeout=10)
+        assert e.value.code == 404
+    finally:
+        srv.shutdown()
+        srv.server_close()

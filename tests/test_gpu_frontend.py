@@ -1,0 +1,39 @@
+"""The batch front end over the real engine: a /v1/decide/batch body gives the
+answers of one direct decide_batch call, in request order."""
+import json
+
+import numpy as np
+import pytest
+
+from laya_goish_b200 import engine, frontend, synth
+from laya_goish_b200.engine import Question
+
+pytestmark = pytest.mark.gpu
+
+
+def test_batch_endpoint_matches_engine(tiny_paths):
+    path = tiny_paths["tiny-llama-q8_0"]
+    rng = np.random.default_rng(21)
+    states = [synth.token_ids(rng, 1000, int(n)).tolist() for n in (12, 70, 33, 5)]
+    q = {"pick": {"type": "choice", "criteria": {"x": 11, "y": 12, "z": 13}, "suffix": [7, 8]},
+         "lvl": {"type": "score", "criteria": [[3, 4], [5, 6], [7, 9]]},
+         "ok": {"type": "noul", "criteria": {"false": 21, "true": 22}}}
+    with engine.Engine(path) as e:
+        svc = frontend.DecideService(e, raw=True)
+        r = svc.handle("POST", "/v1/decide/batch", json.dumps({"states": states, "questions": q}).encode())
+        assert r.status == 200, r.body
+        direct = e.decide_batch(states, [Question("choice", [11, 12, 13], [7, 8]),
+                                         Question("score", [[3, 4], [5, 6], [7, 9]]),
+                                         Question("noul", [21, 22])])
+        bad = svc.handle("POST", "/v1/decide/batch", json.dumps({"states": states + [[1, 5000]], "questions": q}))
+        assert bad.status == 422
+    res = r.body["results"]
+    assert len(res) == len(states)
+    for i in range(len(states)):
+        a = res[i]["answers"]
+        d = direct[i]
+        assert a["pick"]["choice"] == "xyz"[d[0]["choice"]]
+        assert np.allclose(list(a["pick"]["probabilities"].values()), d[0]["probabilities"])
+        assert a["lvl"]["score"] == pytest.approx(d[1]["score"])
+        assert a["ok"]["noul"] == pytest.approx(d[2]["noul"])
+        assert a["ok"]["logits"] == pytest.approx(d[2]["logits"])
