@@ -613,7 +613,7 @@ void free_replica(Replica& r) {
   r.allocs.clear();
   for (DevBuf* b : {&r.ids, &r.pos, &r.slot, &r.x, &r.h, &r.qb, &r.att, &r.act, &r.items, &r.tables, &r.rows, &r.hid32,
                     &r.hid16, &r.cand, &r.row_of, &r.clog, &r.flog, &r.lse, &r.cow, &r.wqkv_s, &r.wo_s, &r.wgu_s,
-                    &r.wd_s, &r.kc, &r.vc, &r.dx16, &r.dlogits, &r.dargmax, &r.dpart})
+                    &r.wd_s, &r.kpart, &r.kc, &r.vc, &r.dx16, &r.dlogits, &r.dargmax, &r.dpart})
     b->release();
   r.pin.release();
   for (auto& e : r.prof_events) {
@@ -738,6 +738,21 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
   const size_t layer_elems = (size_t)r.kv_pages * c.KV * PAGE * c.hd;
   std::vector<cudaEvent_t> lev;
   const int big = 1 << 30;
+  // Residual GEMMs with few output tiles (small M) split K; their partial sums
+  // are merged, in split order, by the RMSNorm that next reads the residual.
+  const char* ke = std::getenv("LAYA_KSPLIT");
+  const bool ks_on = !(ke && ke[0] == '0');
+  const int ks_o = ks_on ? gemm_ksplit(M, d, qd, r.num_sms) : 1;
+  const int ks_d = ks_on ? gemm_ksplit(M, d, ffn, r.num_sms) : 1;
+  if (std::max(ks_o, ks_d) > 1 && (rc = r.kpart.ensure((size_t)std::max(ks_o, ks_d) * M * d * 4))) return rc;
+  int pend = 0;  // K splits of x not yet merged
+  auto norm = [&](const int* rows, int n, const float* w, half* o16, float* o32) -> cudaError_t {
+    r.launches++;
+    const int ns = pend;
+    pend = 0;
+    if (ns > 1) return rmsnorm_merge(x, rows, n, r.kpart.as<float>(), ns, (size_t)M * d, w, d, c.eps, o16, o32, st);
+    return rmsnorm(x, rows, n, w, d, c.eps, o16, o32, st);
+  };
   for (int l = 0; l < c.L; l++) {
     const Layer& L = r.layers[l];
     if (canceled) {
@@ -750,8 +765,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
         return fail(LAYA_E_CANCELED, "request canceled");
       }
     }
-    r.launches++;
-    LAYA_CK(rmsnorm(x, nullptr, M, L.attn_norm, d, c.eps, h, nullptr, st));
+    LAYA_CK(norm(nullptr, M, L.attn_norm, h, nullptr));
     const half* wqkv = L.wqkv16;
     if (!wqkv) {
       half* s = r.wqkv_s.as<half>();
@@ -811,9 +825,11 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     b.K = qd;
     b.resid = x;
     b.ldo = d;
+    b.ksplit = ks_o;
+    b.part = r.kpart.as<float>();
     if ((rc = gemm(r, P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
-    r.launches++;
-    LAYA_CK(rmsnorm(x, nullptr, M, L.ffn_norm, d, c.eps, h, nullptr, st));
+    pend = ks_o;
+    LAYA_CK(norm(nullptr, M, L.ffn_norm, h, nullptr));
     const half* wgu = L.wgu16;
     if (!wgu) {
       half* s = r.wgu_s.as<half>();
@@ -839,7 +855,10 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     dn.K = ffn;
     dn.resid = x;
     dn.ldo = d;
+    dn.ksplit = ks_d;
+    dn.part = r.kpart.as<float>();
     if ((rc = gemm(r, P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, wd, ffn, dn))) return rc;
+    pend = ks_d;
     if (canceled) {
       cudaEvent_t e;
       LAYA_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -849,9 +868,8 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
   }
   for (auto e : lev) cudaEventDestroy(e);
   const int R = (int)p.read_rows.size();
-  r.launches++;
-  LAYA_CK(rmsnorm(x, r.rows.as<int>(), R, r.out_norm, d, c.eps, r.hid16.as<half>() + (size_t)read_base * d,
-                  r.hid32.as<float>() + (size_t)read_base * d, st));
+  LAYA_CK(norm(r.rows.as<int>(), R, r.out_norm, r.hid16.as<half>() + (size_t)read_base * d,
+               r.hid32.as<float>() + (size_t)read_base * d));
   return 0;
 }
 

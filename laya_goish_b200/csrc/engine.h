@@ -102,6 +102,7 @@ struct Replica {
   // scratch
   DevBuf ids, pos, slot, x, h, qb, att, act, items, tables, rows, hid32, hid16, cand, row_of, clog, flog, lse, cow;
   DevBuf wqkv_s, wo_s, wgu_s, wd_s;  // F16 staging of one layer (quantised models)
+  DevBuf kpart;                      // K-split partial sums of the residual GEMMs (small M)
   DevBuf kc, vc;
   int kv_pages = 0;
   HostBuf pin;

@@ -25,6 +25,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm.h"
 #include "ptx.cuh"
@@ -415,8 +417,10 @@ static_assert(PAIR_SMEM <= 227 * 1024 && PAIR_SMEM_RESID <= 227 * 1024, "pair GE
 // tensor map's 128-byte swizzle (16-byte unit u of row r at u ^ (r % 8)) and
 // one lane issues the reduction.  Each residual element receives exactly one
 // addition, so the result does not depend on timing.
+// split >= 0: store the tile's partial sums to plane `split` of the 3-D map
+// over GemmArgs::part instead of adding them into the residual.
 __device__ __forceinline__ void resid_tma_tile(const GemmArgs& a, const CUtensorMap* tmR, uint32_t tbase,
-                                               int row_base, int col0, uint8_t* stg, int lane) {
+                                               int row_base, int col0, uint8_t* stg, int lane, int split) {
   for (int c = 0; c < BN / 32; c++) {
     const int cb = col0 + c * 32;
     if (cb >= a.N) break;
@@ -427,7 +431,7 @@ __device__ __forceinline__ void resid_tma_tile(const GemmArgs& a, const CUtensor
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-    if (a.bias) {
+    if (a.bias && split <= 0) {
       const int n = min(32, a.N - cb);
 #pragma unroll
       for (int i = 0; i < 32; i++)
@@ -445,7 +449,10 @@ __device__ __forceinline__ void resid_tma_tile(const GemmArgs& a, const CUtensor
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_reduce_add_2d(tmR, buf, cb, row_base);
+      if (split >= 0)
+        tma_store_3d(tmR, buf, cb, row_base, split);
+      else
+        tma_reduce_add_2d(tmR, buf, cb, row_base);
       bulk_commit();
     }
   }
@@ -503,8 +510,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total = a.m_tiles * a.n_tiles;
+  const int tiles = a.m_tiles * a.n_tiles;
   const int kblocks = (a.K + BK - 1) / BK;
+  // work unit u = tile u % tiles, K split u / tiles (one split unless EPI_RESID splits K)
+  const int nsplit = (EPI == EPI_RESID && a.ksplit > 1) ? a.ksplit : 1;
+  const int kbs = (kblocks + nsplit - 1) / nsplit;
+  const int total = tiles * nsplit;
   const long long budget = a.budget;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
 
@@ -513,9 +524,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = cluster; tile < total && ok; tile += nclusters) {
+      for (int unit = cluster; unit < total && ok; unit += nclusters) {
+        const int tile = unit % tiles, sp = unit / tiles;
         const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
-        for (int kb = 0; kb < kblocks; kb++) {
+        const int kb1 = min(kblocks, (sp + 1) * kbs);
+        for (int kb = sp * kbs; kb < kb1; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, budget)) {
             atomicOr(a.err, 1u);
             ok = false;
@@ -548,14 +561,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = cluster; tile < total && ok; tile += nclusters) {
+      for (int unit = cluster; unit < total && ok; unit += nclusters) {
+        const int sp = unit / tiles, kb0 = sp * kbs, kb1 = min(kblocks, kb0 + kbs);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, budget)) {
           atomicOr(a.err, 2u);
           break;
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
-        for (int kb = 0; kb < kblocks; kb++) {
+        for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait(&full[stage], phase, budget)) {
             atomicOr(a.err, 4u);
             ok = false;
@@ -566,7 +580,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint64_t bd = sw128_desc(smem_u32(sB + stage * PB_BYTES));
 #pragma unroll
           for (int k = 0; k < BK / 16; k++)
-            umma_f16_pair(tmem_d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(tmem_d, ad + 2 * k, bd + 2 * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == PAIR_STAGES) {
             stage = 0;
@@ -585,7 +599,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint8_t* stg = smem + PAIR_STG + quarter * 2 * 4096;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = cluster; tile < total; tile += nclusters) {
+    for (int unit = cluster; unit < total; unit += nclusters) {
+      const int tile = unit % tiles;
       const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
       const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
       if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
@@ -595,7 +610,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       if constexpr (EPI == EPI_RESID)
         resid_tma_tile(a, &tmR, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row - lane, nt * BN, stg,
-                       lane);
+                       lane, nsplit > 1 ? unit / tiles : -1);
       else
         epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt);
       tc_fence_before();
@@ -714,12 +729,24 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
     if (n <= 0) return cudaErrorInvalidConfiguration;
     clusters_fit[dev & 63] = n;
   }
-  const int total = a.m_tiles * a.n_tiles;
+  const int total = a.m_tiles * a.n_tiles * (a.ksplit > 1 ? a.ksplit : 1);
   int clusters = clusters_fit[dev & 63];
   if (clusters > num_sms / 2) clusters = num_sms / 2;
   if (clusters > total) clusters = total;
   cfg.gridDim = dim3(2 * clusters);
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, a);
+}
+
+int gemm_ksplit(int M, int N, int K, int num_sms) {
+  if (M <= BM || num_sms < 2) return 1;
+  const int tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
+  const int pairs = num_sms / 2, kblocks = (K + BK - 1) / BK;
+  if (2 * tiles >= pairs) return 1;
+  // at least 4 K blocks (256 columns of K) per split, at most 16 splits
+  int s = std::min(std::min(pairs / tiles, kblocks / 4), 16);
+  if (s < 2) return 1;
+  const int per = (kblocks + s - 1) / s;
+  return (kblocks + per - 1) / per;  // every split gets at least one K block
 }
 
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
@@ -732,7 +759,21 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
     if (!make_map(&ta, A, a.M, a.K, lda, 128) || !make_map(&tb, B, a.N, a.K, ldb, 128))
       return cudaErrorInvalidValue;
     CUtensorMap tr = ta;
-    if (epi == EPI_RESID) {
+    if (epi != EPI_RESID || a.ksplit < 2) a.ksplit = 1;
+    if (epi == EPI_RESID && a.ksplit > 1) {
+      // partial sums F32 [ksplit][M][ldo] in 32 x 32 x 1 boxes: rows past M
+      // of a plane are clipped, never written into the next plane
+      const int kblocks = (a.K + BK - 1) / BK;
+      if (!a.part || (a.ldo % 4) || (reinterpret_cast<uintptr_t>(a.part) & 15) || a.ksplit > kblocks ||
+          (a.ksplit - 1) * ((kblocks + a.ksplit - 1) / a.ksplit) >= kblocks)
+        return cudaErrorInvalidValue;
+      const uint64_t dims[3] = {(uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ksplit};
+      const uint64_t strides[2] = {(uint64_t)a.ldo * 4, (uint64_t)a.M * a.ldo * 4};
+      const uint32_t box[3] = {32, 32, 1};
+      if (!encode_tiled(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.part, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    } else if (epi == EPI_RESID) {
       // residual F32 [M][ldo] in 32 x 32 boxes, 128-byte swizzle
       if ((a.ldo % 4) || (reinterpret_cast<uintptr_t>(a.resid) & 15)) return cudaErrorInvalidValue;
       const uint64_t dims[2] = {(uint64_t)a.N, (uint64_t)a.M}, strides[1] = {(uint64_t)a.ldo * 4};
@@ -755,6 +796,7 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
     }
     return cudaErrorInvalidValue;
   }
+  if (epi == EPI_RESID && a.ksplit > 1) return cudaErrorInvalidValue;  // K splits need M > 128
   if (!make_map(&ta, A, a.M, a.K, lda, BM) || !make_map(&tb, B, a.N, a.K, ldb, BN)) return cudaErrorInvalidValue;
   a.m_tiles = (a.M + BM - 1) / BM;
   a.n_tiles = (a.N + BN - 1) / BN;

@@ -32,6 +32,11 @@ struct GemmArgs {
   int page_size;
   unsigned* err;          // device error word; nonzero after a timed-out wait
   long long budget;       // wait budget in SM clock cycles
+  // EPI_RESID split over K (gemm_ksplit): ksplit > 1 writes the partial sums
+  // of split s to part[s][M][ldo] instead of adding into resid; the consumer
+  // adds resid + part[0] + ... + part[ksplit-1] in that order.
+  int ksplit;
+  float* part;
 };
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point: `rank`
@@ -45,5 +50,8 @@ bool encode_tiled(CUtensorMap* m, int dtype, int rank, const void* base, const u
 // (K contiguous).  lda, ldb multiples of 8; A, B 16-byte aligned.
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
                         cudaStream_t st);
+// K splits for an EPI_RESID GEMM of this shape: more than 1 when its 256 x 256
+// output tiles would leave most CTA pairs idle (M > 128 only).
+int gemm_ksplit(int M, int N, int K, int num_sms);
 
 }  // namespace laya

@@ -170,16 +170,31 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // rms (src/models/openthai/model.rs:84-94), offset 0, eps from the GGUF:
 // y = x / sqrt(mean(x^2) + eps) * w.  One block per output row; optional
 // source-row gather (answer-position gather, model.rs:232-235).
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const int* __restrict__ rows, const float* __restrict__ w,
-                               int d, float eps, half* __restrict__ out16, float* __restrict__ out32) {
+// part (nsplit planes of split_stride floats, may be null): K-split partial
+// sums of the GEMM that produced x; they are added first, in plane order, and
+// the merged row is written back to x.
+__global__ void rmsnorm_kernel(float* __restrict__ x, const int* __restrict__ rows, const float* __restrict__ w,
+                               int d, float eps, half* __restrict__ out16, float* __restrict__ out32,
+                               const float* __restrict__ part, int nsplit, size_t split_stride) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.x;
-  const float* xr = x + (size_t)(rows ? rows[r] : r) * d;
+  const size_t roff = (size_t)(rows ? rows[r] : r) * d;
+  float* xr = x + roff;
   float ss = 0.f;
   for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
     float4 v = *reinterpret_cast<const float4*>(xr + i);
+    if (nsplit) {
+      for (int s = 0; s < nsplit; s++) {
+        const float4 p = *reinterpret_cast<const float4*>(part + s * split_stride + roff + i);
+        v.x += p.x;
+        v.y += p.y;
+        v.z += p.z;
+        v.w += p.w;
+      }
+      *reinterpret_cast<float4*>(xr + i) = v;
+    }
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   ss = block_sum(ss, red);
@@ -200,7 +215,15 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const int* __restric
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
                     float* out32, cudaStream_t st, bool pdl) {
   if (!nrows) return cudaSuccess;
-  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, x, rows, w, d, eps, out16, out32);
+  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, const_cast<float*>(x), rows, w, d, eps, out16,
+                  out32, (const float*)nullptr, 0, (size_t)0);
+}
+
+cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
+                          const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st) {
+  if (!nrows) return cudaSuccess;
+  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, false, x, rows, w, d, eps, out16, out32, part,
+                  part ? nsplit : 0, split_stride);
 }
 
 // ---------------------------------------------------------------- heads

@@ -89,10 +89,13 @@ def test_batch_invariance_and_determinism(models):
     a = e.decide_batch(prompts, qs)
     b = e.decide_batch(prompts, qs)
     assert a == b  # repeated requests are bit-identical (validation/smoke.py:25)
+    # Alone, a request runs with fewer token rows, so its residual GEMMs may
+    # split K (partial sums merged in split order): the same sums, associated
+    # differently in F32, hence a tolerance rather than bit equality.
     for i, p in enumerate(prompts):
         alone = e.decide_batch([p], qs)[0]
         for j in range(len(qs)):
-            assert np.allclose(alone[j]["probabilities"], a[i][j]["probabilities"], atol=1e-5), (i, j)
+            assert np.allclose(alone[j]["probabilities"], a[i][j]["probabilities"], atol=2e-4), (i, j)
 
 
 def test_waves_match_single_wave(models, monkeypatch):
@@ -101,10 +104,11 @@ def test_waves_match_single_wave(models, monkeypatch):
     prompts = [synth.token_ids(rng, o.vocab, n) for n in (90, 33, 140, 2, 77)]
     qs = [Question("noul", synth.candidates(rng, o.vocab, 2), suffix=[5, 6, 7])]
     one = e.decide_batch(prompts, qs)
+    # smaller waves may split the residual GEMMs' K differently (2e-4 below)
     monkeypatch.setenv("LAYA_WAVE_TOKENS", "100")
     many = e.decide_batch(prompts, qs)
     for i in range(len(prompts)):
-        assert np.allclose(one[i][0]["probabilities"], many[i][0]["probabilities"], atol=1e-5)
+        assert np.allclose(one[i][0]["probabilities"], many[i][0]["probabilities"], atol=2e-4)
 
 
 def test_validation_rejects_before_launch(models):
@@ -168,7 +172,7 @@ def test_multi_replica_sharding_matches_single(tiny_paths):
         b = two.decide_batch(prompts, qs)
     for i in range(len(prompts)):
         for j in range(len(qs)):
-            assert np.allclose(a[i][j]["probabilities"], b[i][j]["probabilities"], atol=1e-5), (i, j)
+            assert np.allclose(a[i][j]["probabilities"], b[i][j]["probabilities"], atol=2e-4), (i, j)
 
 
 @pytest.mark.parametrize("peer", ["1", "0"])
@@ -191,4 +195,4 @@ def test_replicas_on_distinct_gpus(tiny_paths, monkeypatch, peer):
         a = one.decide_batch(prompts, qs)
         b = many.decide_batch(prompts, qs)
     for i in range(len(prompts)):
-        assert np.allclose(a[i][0]["probabilities"], b[i][0]["probabilities"], atol=1e-5), i
+        assert np.allclose(a[i][0]["probabilities"], b[i][0]["probabilities"], atol=2e-4), i
