@@ -745,7 +745,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
   const int ks_o = ks_on ? gemm_ksplit(M, d, qd, r.num_sms) : 1;
   const int ks_d = ks_on ? gemm_ksplit(M, d, ffn, r.num_sms) : 1;
   if (std::max(ks_o, ks_d) > 1 && (rc = r.kpart.ensure((size_t)std::max(ks_o, ks_d) * M * d * 4))) return rc;
-  int pend = 0;  // K splits of x not yet merged
+  int pend = 0;  // K splits of x not yet merged (the gathered final norm merges without writing x back)
   auto norm = [&](const int* rows, int n, const float* w, half* o16, float* o32) -> cudaError_t {
     r.launches++;
     const int ns = pend;

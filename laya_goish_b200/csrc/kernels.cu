@@ -171,8 +171,23 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // y = x / sqrt(mean(x^2) + eps) * w.  One block per output row; optional
 // source-row gather (answer-position gather, model.rs:232-235).
 // part (nsplit planes of split_stride floats, may be null): K-split partial
-// sums of the GEMM that produced x; they are added first, in plane order, and
-// the merged row is written back to x.
+// sums of the GEMM that produced x; they are added first, in plane order.
+// Without a row gather the merged rows are also written back to x; with one
+// they are not (a gather may name a row more than once, and the residual is
+// not read again after the gathered final norm).
+__device__ __forceinline__ float4 merged_row4(const float* x, const float* part, int nsplit, size_t split_stride,
+                                              size_t off) {
+  float4 v = *reinterpret_cast<const float4*>(x + off);
+  for (int s = 0; s < nsplit; s++) {
+    const float4 p = *reinterpret_cast<const float4*>(part + s * split_stride + off);
+    v.x += p.x;
+    v.y += p.y;
+    v.z += p.z;
+    v.w += p.w;
+  }
+  return v;
+}
+
 __global__ void rmsnorm_kernel(float* __restrict__ x, const int* __restrict__ rows, const float* __restrict__ w,
                                int d, float eps, half* __restrict__ out16, float* __restrict__ out32,
                                const float* __restrict__ part, int nsplit, size_t split_stride) {
@@ -181,26 +196,18 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const int* __restrict__ ro
   pdl_trigger();
   const int r = blockIdx.x;
   const size_t roff = (size_t)(rows ? rows[r] : r) * d;
-  float* xr = x + roff;
+  const bool write_back = nsplit && !rows;
   float ss = 0.f;
   for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
-    float4 v = *reinterpret_cast<const float4*>(xr + i);
-    if (nsplit) {
-      for (int s = 0; s < nsplit; s++) {
-        const float4 p = *reinterpret_cast<const float4*>(part + s * split_stride + roff + i);
-        v.x += p.x;
-        v.y += p.y;
-        v.z += p.z;
-        v.w += p.w;
-      }
-      *reinterpret_cast<float4*>(xr + i) = v;
-    }
+    const float4 v = merged_row4(x, part, nsplit, split_stride, roff + i);
+    if (write_back) *reinterpret_cast<float4*>(x + roff + i) = v;
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   ss = block_sum(ss, red);
   const float scale = 1.f / sqrtf(ss / (float)d + eps);
   for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
-    float4 v = *reinterpret_cast<const float4*>(xr + i);
+    // the same thread wrote these elements back above, or re-merges them
+    const float4 v = merged_row4(x, part, write_back ? 0 : nsplit, split_stride, roff + i);
     float4 g = *reinterpret_cast<const float4*>(w + i);
     float y0 = v.x * scale * g.x, y1 = v.y * scale * g.y, y2 = v.z * scale * g.z, y3 = v.w * scale * g.w;
     if (out16) {

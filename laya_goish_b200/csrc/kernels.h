@@ -47,8 +47,8 @@ cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cu
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
                     float* out32, cudaStream_t st, bool pdl = false);
 // rmsnorm of x + part[0] + ... + part[nsplit-1] (K-split partial sums of the
-// GEMM that wrote x, planes split_stride floats apart), the merged rows also
-// written back to x.
+// GEMM that wrote x, planes split_stride floats apart); without a row gather
+// (rows null) the merged rows are also written back to x.
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,
