@@ -277,7 +277,7 @@ def run_ours(args):
                    "l2": "working set > L2 (weights 1.03 GB, activations 0.5 GB/layer); no flush needed",
                    "parallelism": f"request sharding x{world}, full replica per GPU, no collective"},
         "prefill_tok_s": value * TOKENS,
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all prefill GEMMs)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel + gemm_tc_kernel (tcgen05, all prefill GEMMs)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if achieved else None, "traffic": GEMM_TRAFFIC_BYTES,
                      "traffic_unit": "bytes per GEMM launch (ncu DRAM read+write, 16-request capture x 4)",

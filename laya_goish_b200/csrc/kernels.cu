@@ -188,6 +188,23 @@ __device__ __forceinline__ float4 merged_row4(const float* x, const float* part,
   return v;
 }
 
+__device__ __forceinline__ void rms_out(float4 v, float scale, const float* w, int i, size_t obase, half* out16,
+                                        float* out32) {
+  const float4 g = *reinterpret_cast<const float4*>(w + i);
+  const float y0 = v.x * scale * g.x, y1 = v.y * scale * g.y, y2 = v.z * scale * g.z, y3 = v.w * scale * g.w;
+  if (out16) {
+    half2 a = __floats2half2_rn(y0, y1), b = __floats2half2_rn(y2, y3);
+    uint2 u = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    *reinterpret_cast<uint2*>(out16 + obase + i) = u;
+  }
+  if (out32) *reinterpret_cast<float4*>(out32 + obase + i) = make_float4(y0, y1, y2, y3);
+}
+
+// One CTA per row.  Rows of up to RN_HELD x 4 x blockDim elements (4096 at
+// 256 threads) stay in registers between the sum of squares and the output
+// pass, so x is read once (6 B per element moved with an F16 output).
+constexpr int RN_HELD = 4;
+
 __global__ void rmsnorm_kernel(float* __restrict__ x, const int* __restrict__ rows, const float* __restrict__ w,
                                int d, float eps, half* __restrict__ out16, float* __restrict__ out32,
                                const float* __restrict__ part, int nsplit, size_t split_stride) {
@@ -195,27 +212,36 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const int* __restrict__ ro
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.x;
-  const size_t roff = (size_t)(rows ? rows[r] : r) * d;
+  const size_t roff = (size_t)(rows ? rows[r] : r) * d, obase = (size_t)r * d;
   const bool write_back = nsplit && !rows;
+  const int step = blockDim.x * 4, held_end = RN_HELD * step;
+  float4 v[RN_HELD];
   float ss = 0.f;
-  for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
-    const float4 v = merged_row4(x, part, nsplit, split_stride, roff + i);
-    if (write_back) *reinterpret_cast<float4*>(x + roff + i) = v;
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+  for (int u = 0; u < RN_HELD; u++) {
+    const int i = threadIdx.x * 4 + u * step;
+    if (i < d) {
+      v[u] = merged_row4(x, part, nsplit, split_stride, roff + i);
+      if (write_back) *reinterpret_cast<float4*>(x + roff + i) = v[u];
+      ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    }
+  }
+  for (int i = threadIdx.x * 4 + held_end; i < d; i += step) {  // rows wider than the register tile
+    const float4 t = merged_row4(x, part, nsplit, split_stride, roff + i);
+    if (write_back) *reinterpret_cast<float4*>(x + roff + i) = t;
+    ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
   }
   ss = block_sum(ss, red);
   const float scale = 1.f / sqrtf(ss / (float)d + eps);
-  for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+#pragma unroll
+  for (int u = 0; u < RN_HELD; u++) {
+    const int i = threadIdx.x * 4 + u * step;
+    if (i < d) rms_out(v[u], scale, w, i, obase, out16, out32);
+  }
+  for (int i = threadIdx.x * 4 + held_end; i < d; i += step) {
     // the same thread wrote these elements back above, or re-merges them
-    const float4 v = merged_row4(x, part, write_back ? 0 : nsplit, split_stride, roff + i);
-    float4 g = *reinterpret_cast<const float4*>(w + i);
-    float y0 = v.x * scale * g.x, y1 = v.y * scale * g.y, y2 = v.z * scale * g.z, y3 = v.w * scale * g.w;
-    if (out16) {
-      half2 a = __floats2half2_rn(y0, y1), b = __floats2half2_rn(y2, y3);
-      uint2 u = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-      *reinterpret_cast<uint2*>(out16 + (size_t)r * d + i) = u;
-    }
-    if (out32) *reinterpret_cast<float4*>(out32 + (size_t)r * d + i) = make_float4(y0, y1, y2, y3);
+    const float4 t = merged_row4(x, part, write_back ? 0 : nsplit, split_stride, roff + i);
+    rms_out(t, scale, w, i, obase, out16, out32);
   }
 }
 
