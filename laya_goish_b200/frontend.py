@@ -22,14 +22,18 @@ What is kept from the reference, in the same order:
 * the daemon answers each non-empty input line with one output line, the
   result or `{"error": message}` (src/main.rs:139-151).
 
-Requests are token-level, because the tokenizer and prompt templates sit
-above this boundary: `state` is the prompt's token ids (a list, or an object
-with `ids`), and every option of a question is a token id or a list of ids
-(a continuation).  Question objects follow src/models/laya/decision.rs:19-98:
+`state` is the prompt's token ids (a list, or an object with `ids`), or
+text when the service has a tokenizer (the model file's own BPE vocabulary,
+`tokenizer.Tokenizer`); every option of a question is a token id, a list of
+ids (a continuation) or, with a tokenizer, text.  Question objects follow
+src/models/laya/decision.rs:19-98:
 
-    {"type": "choice", "criteria": {"label": id | [ids], ...}, "suffix": [ids]}
-    {"type": "score",  "criteria": [id | [ids], ...]}          (>= 2 levels)
-    {"type": "noul",   "criteria": {"false": id | [ids], "true": id | [ids]}}
+    {"type": "choice", "criteria": {"label": option, ...}, "suffix": [ids] | text}
+    {"type": "score",  "criteria": [option, ...]}              (>= 2 levels)
+    {"type": "noul",   "criteria": {"false": option, "true": option}}
+
+Prompt templates (how a product phrases the question around the state) sit
+above this layer: the caller writes them into the state text or the suffix.
 
 Answers follow src/models/laya/decision.rs:214-268 (`choice` label, `score`
 with its `legend`, `noul`, `confidence`, `probabilities` by label; `logits`
@@ -60,7 +64,21 @@ class RequestError(ValueError):
     """A request that fails validation (422 over HTTP)."""
 
 
-def _ids(v, what: str) -> list[int]:
+def _encode(tok, text: str, what: str) -> list[int]:
+    if tok is None:
+        raise RequestError(f"{what}: text needs a model with a tokenizer; send token ids")
+    try:
+        ids = tok.encode(text)
+    except ValueError as e:
+        raise RequestError(f"{what}: {e}") from e
+    if not ids:
+        raise RequestError(f"{what}: text encodes to no tokens")
+    return ids
+
+
+def _ids(v, what: str, tok=None) -> list[int]:
+    if isinstance(v, str):
+        return _encode(tok, v, what)
     if isinstance(v, bool) or not isinstance(v, (int, list)):
         raise RequestError(f"{what} must be a token id or a list of token ids")
     ids = [v] if isinstance(v, int) else v
@@ -69,22 +87,26 @@ def _ids(v, what: str) -> list[int]:
     return ids
 
 
-def state_ids(state) -> list[int]:
-    """The prompt of one request: a list of token ids, or {"ids": [...]}."""
+def state_ids(state, tok=None) -> list[int]:
+    """The prompt of one request: a list of token ids, {"ids": [...]}, or text."""
     if isinstance(state, dict):
         state = state.get("ids")
+    if isinstance(state, str):
+        return _encode(tok, state, "state")
     if not isinstance(state, list) or not state:
         raise RequestError("state must be a non-empty list of token ids (or an object with ids)")
     return _ids(state, "state")
 
 
 class ParsedQuestion:
-    def __init__(self, qid: str, kind: str, labels: list[str], options: list[list[int]], suffix: list[int]):
+    def __init__(self, qid: str, kind: str, labels: list[str], options: list[list[int]], suffix: list[int],
+                 given=None):
         self.id, self.kind, self.labels, self.options, self.suffix = qid, kind, labels, options, suffix
+        self.given = given  # the criteria as sent (the score legend)
 
 
-def parse_questions(obj) -> list[ParsedQuestion]:
-    """src/models/laya/decision.rs:19-98 on token-level criteria."""
+def parse_questions(obj, tok=None) -> list[ParsedQuestion]:
+    """src/models/laya/decision.rs:19-98 on token-level (or tokenised) criteria."""
     if not isinstance(obj, dict) or not obj or len(obj) > MAX_QUESTIONS:
         raise RequestError("questions must contain 1..256 named questions")
     out = []
@@ -99,17 +121,17 @@ def parse_questions(obj) -> list[ParsedQuestion]:
             if not isinstance(c, dict) or not c:
                 raise RequestError(f"{qid}: choice requires a criteria object")
             labels = list(c)
-            opts = [_ids(c[k], f"{qid}.{k}") for k in labels]
+            opts = [_ids(c[k], f"{qid}.{k}", tok) for k in labels]
         elif kind == "score":
             if not isinstance(c, list) or len(c) < 2:
                 raise RequestError(f"{qid}: score requires at least two ordered criteria")
             labels = [str(i) for i in range(len(c))]
-            opts = [_ids(v, f"{qid}[{i}]") for i, v in enumerate(c)]
+            opts = [_ids(v, f"{qid}[{i}]", tok) for i, v in enumerate(c)]
         else:
             if not isinstance(c, dict) or "false" not in c or "true" not in c:
                 raise RequestError(f"{qid}: noul requires criteria with false and true token ids")
             labels = ["false", "true"]
-            opts = [_ids(c["false"], f"{qid}.false"), _ids(c["true"], f"{qid}.true")]
+            opts = [_ids(c["false"], f"{qid}.false", tok), _ids(c["true"], f"{qid}.true", tok)]
         if not opts or len(opts) > MAX_OPTIONS:
             raise RequestError(f"{qid}: requires 1..16 options")
         if len({len(o) for o in opts}) != 1:
@@ -117,9 +139,11 @@ def parse_questions(obj) -> list[ParsedQuestion]:
         suffix = q.get("suffix", [])
         if suffix is None:
             suffix = []
+        if isinstance(suffix, str):
+            suffix = _encode(tok, suffix, f"{qid}.suffix")
         if not isinstance(suffix, list) or any(isinstance(t, bool) or not isinstance(t, int) for t in suffix):
             raise RequestError(f"{qid}: suffix must be a list of token ids")
-        out.append(ParsedQuestion(str(qid), kind, labels, opts, suffix))
+        out.append(ParsedQuestion(str(qid), kind, labels, opts, suffix, c))
     return out
 
 
@@ -138,7 +162,7 @@ def answer_json(q: ParsedQuestion, a: dict, raw: bool) -> dict:
         out["choice"] = q.labels[a["choice"]]
     elif q.kind == "score":
         out["score"] = a["score"]
-        out["legend"] = {str(i): o if len(o) > 1 else o[0] for i, o in enumerate(q.options)}
+        out["legend"] = {str(i): v for i, v in enumerate(q.given)}
     else:
         out["noul"] = a["noul"]
     out["confidence"] = a["confidence"]
@@ -164,9 +188,10 @@ class DecideService:
     """The server's request handling around one loaded Engine (or any object
     with the same `validate` / `decide_batch` / `info` interface)."""
 
-    def __init__(self, engine, raw: bool = False):
+    def __init__(self, engine, raw: bool = False, tokenizer=None):
         self.engine = engine
         self.raw = raw
+        self.tokenizer = tokenizer
         self._busy = threading.Lock()
         self._requests = 0
         self._count_lock = threading.Lock()
@@ -176,7 +201,7 @@ class DecideService:
             raise RequestError("request body must be a JSON object")
         if req.get("state") is None:
             raise RequestError("state is required")
-        return [state_ids(req["state"])], parse_questions(req.get("questions"))
+        return [state_ids(req["state"], self.tokenizer)], parse_questions(req.get("questions"), self.tokenizer)
 
     def handle(self, method: str, path: str, body: bytes | str | None,
                canceled: Callable[[], bool] | None = None) -> Response:
@@ -210,8 +235,8 @@ class DecideService:
                 states = req.get("states")
                 if not isinstance(states, list) or not 1 <= len(states) <= MAX_STATES:
                     raise RequestError("states must be an array of 1..256 states")
-                prompts = [state_ids(s) for s in states]
-                qs = parse_questions(req.get("questions"))
+                prompts = [state_ids(s, self.tokenizer) for s in states]
+                qs = parse_questions(req.get("questions"), self.tokenizer)
             else:
                 prompts, qs = self._prepare(req)
             eqs = _engine_questions(qs)
@@ -316,8 +341,14 @@ def main(argv=None) -> int:
     ap.add_argument("--port", type=int, default=8080)
     ap.add_argument("--raw", action="store_true")
     a = ap.parse_args(argv)
+    from .tokenizer import Tokenizer
+
+    try:
+        tok = Tokenizer.from_gguf(a.model)
+    except ValueError:
+        tok = None  # no usable vocabulary in the file: token-id requests only
     eng = Engine(a.model, devices=[int(d) for d in a.devices.split(",")])
-    svc = DecideService(eng, raw=a.raw)
+    svc = DecideService(eng, raw=a.raw, tokenizer=tok)
     if a.mode == "daemon":
         run_daemon(svc)
     else:

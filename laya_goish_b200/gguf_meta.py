@@ -1,0 +1,96 @@
+"""GGUF v3 metadata reader (header and key/value section only).
+
+The device loader parses the container natively (csrc/gguf.cpp) and skips
+array values; the host tokenizer needs them (`tokenizer.ggml.tokens`,
+`.merges`, `.token_type`), so this reads the same layout in Python:
+magic "GGUF", version 3, tensor count, KV count, then per KV a string key,
+a u32 value type and the value (src/gguf.rs:48-79, 95-125).  Tensors are
+not read.
+"""
+from __future__ import annotations
+
+import mmap
+import struct
+
+_SCALARS = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
+MAX_ARRAY = 1 << 24
+
+
+class GGUFError(ValueError):
+    pass
+
+
+class _Reader:
+    def __init__(self, buf):
+        self.b = buf
+        self.p = 0
+
+    def take(self, n: int):
+        if n < 0 or self.p + n > len(self.b):
+            raise GGUFError("truncated GGUF")
+        v = self.b[self.p:self.p + n]
+        self.p += n
+        return v
+
+    def fmt(self, f: str):
+        return struct.unpack(f, self.take(struct.calcsize(f)))[0]
+
+    def string(self) -> str:
+        n = self.fmt("<Q")
+        if n > len(self.b):
+            raise GGUFError("GGUF string length overflow")
+        try:
+            return bytes(self.take(n)).decode("utf-8")
+        except UnicodeDecodeError as e:
+            raise GGUFError("invalid GGUF UTF-8") from e
+
+    def value(self, t: int, depth: int = 0):
+        if depth > 4:
+            raise GGUFError("GGUF metadata nesting too deep")
+        if t in _SCALARS:
+            return self.fmt(_SCALARS[t])
+        if t == 8:
+            return self.string()
+        if t == 9:
+            et, n = self.fmt("<I"), self.fmt("<Q")
+            if n > MAX_ARRAY:
+                raise GGUFError("GGUF array too large")
+            if et in _SCALARS:  # one unpack for the whole numeric array
+                f = _SCALARS[et]
+                size = struct.calcsize(f)
+                return list(struct.unpack("<%d%s" % (n, f[1]), self.take(n * size)))
+            return [self.value(et, depth + 1) for _ in range(n)]
+        raise GGUFError(f"unsupported GGUF metadata type {t}")
+
+
+def read_metadata(path_or_bytes) -> dict:
+    """All metadata key/values of a GGUF file (path) or image (bytes)."""
+    if isinstance(path_or_bytes, (bytes, bytearray, memoryview)):
+        return _parse(memoryview(path_or_bytes))
+    with open(path_or_bytes, "rb") as f:
+        with mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) as m:
+            mv = memoryview(m)
+            try:
+                return _parse(mv)
+            finally:
+                mv.release()
+
+
+def _parse(buf) -> dict:
+    r = _Reader(buf)
+    try:
+        if bytes(r.take(4)) != b"GGUF":
+            raise GGUFError("not a GGUF file")
+        if r.fmt("<I") != 3:
+            raise GGUFError("unsupported GGUF version")
+        r.fmt("<Q")  # tensor count
+        n_kv = r.fmt("<Q")
+        if n_kv > 1 << 20:
+            raise GGUFError("too many GGUF metadata entries")
+        out = {}
+        for _ in range(n_kv):
+            k = r.string()
+            out[k] = r.value(r.fmt("<I"))
+        return out
+    finally:
+        r.b = None

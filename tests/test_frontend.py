@@ -193,3 +193,26 @@ def test_http_round_trip():
     finally:
         srv.shutdown()
         srv.server_close()
+
+
+def test_text_requests_with_tokenizer():
+    from laya_goish_b200 import synth
+    from laya_goish_b200.tokenizer import Tokenizer
+
+    tok = Tokenizer(synth._meta(synth.TINY["tiny-llama-q8_0-tok"]))
+    eng = FakeEngine()
+    s = frontend.DecideService(eng, tokenizer=tok)
+    q = {"q": {"type": "choice", "criteria": {"yes": "yes", "no": "no"}, "suffix": " the answer"}}
+    r = s.handle("POST", "/v1/decide", body(state="hello world, is this spam?", questions=q))
+    assert r.status == 200, r.body
+    assert r.body["usage"]["tokens"] == len(tok.encode("hello world, is this spam?")) + len(tok.encode(" the answer"))
+    ids = s.handle("POST", "/v1/decide", body(state=tok.encode("hello world, is this spam?"),
+                                              questions={"q": {"type": "choice",
+                                                               "criteria": {"yes": tok.encode("yes"), "no": tok.encode("no")},
+                                                               "suffix": tok.encode(" the answer")}}))
+    assert ids.body["answers"] == r.body["answers"]
+    lv = s.handle("POST", "/v1/decide", body(state="x", questions={"s": {"type": "score", "criteria": ["bad", "good"]}}))
+    assert lv.status == 200 and lv.body["answers"]["s"]["legend"] == {"0": "bad", "1": "good"}
+    # without a tokenizer, text is a 422
+    r = frontend.DecideService(FakeEngine()).handle("POST", "/v1/decide", body(state="hello", questions=CHOICE))
+    assert r.status == 422 and "tokenizer" in r.body["error"]["message"]

@@ -37,3 +37,20 @@ def test_batch_endpoint_matches_engine(tiny_paths):
         assert a["lvl"]["score"] == pytest.approx(d[1]["score"])
         assert a["ok"]["noul"] == pytest.approx(d[2]["noul"])
         assert a["ok"]["logits"] == pytest.approx(d[2]["logits"])
+
+
+def test_text_state_matches_token_ids(tiny_paths):
+    from laya_goish_b200.tokenizer import Tokenizer
+
+    path = tiny_paths["tiny-llama-q8_0-tok"]
+    tok = Tokenizer.from_gguf(path)
+    text = "hello world, the email is urgent. answer yes or no"
+    q_text = {"ok": {"type": "noul", "criteria": {"false": "no", "true": "yes"}, "suffix": " answer"}}
+    q_ids = {"ok": {"type": "noul", "criteria": {"false": tok.encode("no"), "true": tok.encode("yes")},
+                    "suffix": tok.encode(" answer")}}
+    with engine.Engine(path) as e:
+        svc = frontend.DecideService(e, tokenizer=tok)
+        a = svc.handle("POST", "/v1/decide", json.dumps({"state": text, "questions": q_text}))
+        b = svc.handle("POST", "/v1/decide", json.dumps({"state": tok.encode(text), "questions": q_ids}))
+    assert a.status == 200 and b.status == 200
+    assert a.body["answers"] == b.body["answers"]
