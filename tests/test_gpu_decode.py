@@ -42,3 +42,17 @@ def test_greedy_decode_matches_oracle(tiny_paths, name, nseq):
                 break  # near-tie: F16 rounding may pick the other token; later steps diverge
             assert toks[i, s] == want[s], (name, i, s, toks[i], want)
     o.close()
+
+
+@pytest.mark.parametrize("name,nseq", [("small-llama-q8_0", 1), ("small-llama-q8_0", 8), ("tiny-llama-f16", 4)])
+def test_chained_gemv_step_matches_per_launch_step(tiny_paths, monkeypatch, name, nseq):
+    # One cooperative launch per layer (grid barriers between the GEMV phases)
+    # does the same arithmetic as one launch per GEMV: identical tokens.
+    path = tiny_paths[name]
+    rng = np.random.default_rng(100 + nseq)
+    ctxs = [synth.token_ids(rng, 1000, int(n)) for n in rng.integers(5, 90, size=nseq)]
+    with engine.Engine(path) as e:
+        chained, _ = e.decode(ctxs, 12)
+        monkeypatch.setenv("LAYA_DECODE_SEQ", "0")
+        separate, _ = e.decode(ctxs, 12)
+    assert np.array_equal(chained, separate)
