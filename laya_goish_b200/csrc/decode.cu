@@ -1380,7 +1380,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       LAYA_CK(launch_k(rope_append_kernel, dim3(nb), dim3(256), 0, st, true, (const float*)f, L.bqkv, qd, kd, c.hd,
                        c.KV, (const int*)io.cur_pos, (const int*)io.cur_slot, r.rope, r.qb.as<half>(), kcl, vcl));
     } else {
-      const half* wqkv = L.wqkv16;
+      const half* wqkv = L.wqkv16 ? L.wqkv16 : L.rqkv16;
       if (!wqkv) {
         half* s = r.wqkv_s.as<half>();
         if ((rc = stage(L.wq, s, d, big, 0, 0)) || (rc = stage(L.wk, s, d, big, 0, qd)) ||
@@ -1422,7 +1422,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     } else if (small) {
       if ((rc = run_gemv(r, plan1(L.wo, r.att.as<half>(), qd, x, d, 1), nbp))) return rc;
     } else {
-      const half* wo = L.wo16;
+      const half* wo = L.wo16 ? L.wo16 : L.ro16;
       if (!wo) {
         if ((rc = stage(L.wo, r.wo_s.as<half>(), qd, big, 0, 0))) return rc;
         wo = r.wo_s.as<half>();
@@ -1463,7 +1463,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       if ((rc = run_gemv(r, p, nbp))) return rc;
       if ((rc = run_gemv(r, plan1(L.wd, r.act.as<half>(), ffn, x, d, 1), nbp))) return rc;
     } else {
-      const half* wgu = L.wgu16;
+      const half* wgu = L.wgu16 ? L.wgu16 : L.rgu16;
       if (!wgu) {
         half* s = r.wgu_s.as<half>();
         if ((rc = stage(L.wg, s, d, 128, 256, 0)) || (rc = stage(L.wu, s, d, 128, 256, 128))) return rc;
@@ -1476,7 +1476,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       gu.out = r.act.p;
       gu.ldo = ffn;
       if ((rc = gemm_d(P_GEMM_GU, EPI_SWIGLU, h, d, wgu, d, gu))) return rc;
-      const half* wd = L.wd16;
+      const half* wd = L.wd16 ? L.wd16 : L.rd16;
       if (!wd) {
         if ((rc = stage(L.wd, r.wd_s.as<half>(), ffn, big, 0, 0))) return rc;
         wd = r.wd_s.as<half>();

@@ -639,6 +639,52 @@ int ensure_head16(Model& m, Replica& r) {
   return 0;
 }
 
+int ensure_f16_cache(Model& m, Replica& r) {
+  const Config& c = m.cfg;
+  const char* e = std::getenv("LAYA_F16_CACHE");
+  if (!c.quantized || (e && e[0] == '0') || r.layers.empty() || r.layers[0].rqkv16 || r.f16_cache_failed) return 0;
+  const int qd = c.H * c.hd, kd = c.KV * c.hd, d = c.d, ffn = c.ffn, big = 1 << 30;
+  const size_t sizes[4] = {(size_t)(qd + 2 * kd) * d * 2, (size_t)2 * ffn * d * 2, (size_t)d * qd * 2,
+                           (size_t)d * ffn * 2};
+  std::vector<void*> bufs;
+  for (int l = 0; l < c.L && !r.f16_cache_failed; l++)
+    for (int i = 0; i < 4; i++) {
+      void* p = nullptr;
+      if (cudaMalloc(&p, sizes[i]) != cudaSuccess) {
+        cudaGetLastError();
+        r.f16_cache_failed = true;  // keep staging before each GEMM
+        break;
+      }
+      bufs.push_back(p);
+    }
+  if (r.f16_cache_failed) {
+    for (void* p : bufs) cudaFree(p);
+    return 0;
+  }
+  for (int l = 0; l < c.L; l++) {
+    Layer& L = r.layers[l];
+    half* qkv = static_cast<half*>(bufs[4 * l]);
+    half* gu = static_cast<half*>(bufs[4 * l + 1]);
+    half* o = static_cast<half*>(bufs[4 * l + 2]);
+    half* dn = static_cast<half*>(bufs[4 * l + 3]);
+    // the layouts of the per-GEMM staging: q|k|v stacked, gate/up interleaved per 128 rows
+    LAYA_CK(dequant_f16(L.wq, qkv, d, big, 0, 0, r.stream));
+    LAYA_CK(dequant_f16(L.wk, qkv, d, big, 0, qd, r.stream));
+    LAYA_CK(dequant_f16(L.wv, qkv, d, big, 0, qd + kd, r.stream));
+    LAYA_CK(dequant_f16(L.wg, gu, d, 128, 256, 0, r.stream));
+    LAYA_CK(dequant_f16(L.wu, gu, d, 128, 256, 128, r.stream));
+    LAYA_CK(dequant_f16(L.wo, o, qd, big, 0, 0, r.stream));
+    LAYA_CK(dequant_f16(L.wd, dn, ffn, big, 0, 0, r.stream));
+    r.launches += 7;
+    L.rqkv16 = qkv;
+    L.rgu16 = gu;
+    L.ro16 = o;
+    L.rd16 = dn;
+  }
+  for (void* p : bufs) r.allocs.push_back(p);
+  return 0;
+}
+
 int ensure_kv(Model& m, Replica& r, int pages) {
   if (pages <= r.kv_pages) return 0;
   const Config& c = m.cfg;
@@ -724,7 +770,8 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       (rc = r.qb.ensure((size_t)M * qd * 2)) || (rc = r.att.ensure((size_t)M * qd * 2)) ||
       (rc = r.act.ensure((size_t)M * ffn * 2)))
     return rc;
-  if (c.quantized) {
+  if (c.quantized && (rc = ensure_f16_cache(m, r))) return rc;
+  if (c.quantized && !r.layers[0].rqkv16) {
     if ((rc = r.wqkv_s.ensure((size_t)(qd + 2 * kd) * d * 2)) || (rc = r.wo_s.ensure((size_t)d * qd * 2)) ||
         (rc = r.wgu_s.ensure((size_t)2 * ffn * d * 2)) || (rc = r.wd_s.ensure((size_t)d * ffn * 2)))
       return rc;
@@ -766,7 +813,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       }
     }
     LAYA_CK(norm(nullptr, M, L.attn_norm, h, nullptr));
-    const half* wqkv = L.wqkv16;
+    const half* wqkv = L.wqkv16 ? L.wqkv16 : L.rqkv16;
     if (!wqkv) {
       half* s = r.wqkv_s.as<half>();
       if ((rc = stage(r, P_DEQUANT, L.wq, s, d, big, 0, 0)) || (rc = stage(r, P_DEQUANT, L.wk, s, d, big, 0, qd)) ||
@@ -814,7 +861,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       r.launches++;
       LAYA_CK(attention(ap, st));
     }
-    const half* wo = L.wo16;
+    const half* wo = L.wo16 ? L.wo16 : L.ro16;
     if (!wo) {
       if ((rc = stage(r, P_DEQUANT, L.wo, r.wo_s.as<half>(), qd, big, 0, 0))) return rc;
       wo = r.wo_s.as<half>();
@@ -830,7 +877,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     if ((rc = gemm(r, P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
     pend = ks_o;
     LAYA_CK(norm(nullptr, M, L.ffn_norm, h, nullptr));
-    const half* wgu = L.wgu16;
+    const half* wgu = L.wgu16 ? L.wgu16 : L.rgu16;
     if (!wgu) {
       half* s = r.wgu_s.as<half>();
       if ((rc = stage(r, P_DEQUANT, L.wg, s, d, 128, 256, 0)) || (rc = stage(r, P_DEQUANT, L.wu, s, d, 128, 256, 128)))
@@ -844,7 +891,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     gu.out = r.act.p;
     gu.ldo = ffn;
     if ((rc = gemm(r, P_GEMM_GU, EPI_SWIGLU, h, d, wgu, d, gu))) return rc;
-    const half* wd = L.wd16;
+    const half* wd = L.wd16 ? L.wd16 : L.rd16;
     if (!wd) {
       if ((rc = stage(r, P_DEQUANT, L.wd, r.wd_s.as<half>(), ffn, big, 0, 0))) return rc;
       wd = r.wd_s.as<half>();

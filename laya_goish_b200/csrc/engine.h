@@ -71,6 +71,12 @@ struct Layer {
   const half* wgu16 = nullptr;  // gate/up rows interleaved per 128
   const half* wo16 = nullptr;
   const half* wd16 = nullptr;
+  // Quantised models: F16 images of the same four operands for the prefill
+  // GEMMs, decoded once (ensure_f16_cache) instead of before every GEMM.
+  const half* rqkv16 = nullptr;
+  const half* rgu16 = nullptr;
+  const half* ro16 = nullptr;
+  const half* rd16 = nullptr;
 };
 
 struct ProfEvent {
@@ -103,6 +109,7 @@ struct Replica {
   DevBuf ids, pos, slot, x, h, qb, att, act, items, tables, rows, hid32, hid16, cand, row_of, clog, flog, lse, cow;
   DevBuf wqkv_s, wo_s, wgu_s, wd_s;  // F16 staging of one layer (quantised models)
   DevBuf kpart;                      // K-split partial sums of the residual GEMMs (small M)
+  bool f16_cache_failed = false;     // no room for the F16 operand cache: stage per GEMM
   DevBuf kc, vc;
   int kv_pages = 0;
   HostBuf pin;
@@ -145,6 +152,10 @@ int ensure_kv(Model& m, Replica& r, int pages);
 int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>& tables, int read_base,
                 int (*canceled)(void*), void* user, std::mutex* cancel_mu);
 int ensure_head16(Model& m, Replica& r);
+// Quantised models: decodes every layer's GEMM operands to resident F16 once
+// (about 2 bytes per weight; skipped, and the per-GEMM staging kept, when the
+// memory is not there or LAYA_F16_CACHE=0).
+int ensure_f16_cache(Model& m, Replica& r);
 int decide_shard(Model& m, Replica& r, const laya_batch& b, int r0, int r1, laya_answer* out,
                  int (*canceled)(void*), void* user, std::mutex* cancel_mu);
 int validate_batch(const Config& c, const laya_batch* b);
