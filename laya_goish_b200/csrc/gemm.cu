@@ -91,8 +91,13 @@ __device__ __forceinline__ void resid_prefetch(const GemmArgs& a, int row, int n
   }
 }
 
+// stg (pair kernel, may be null): the warp's 8 KB staging buffer; with it the
+// QKV epilogue writes each head's 32 rows through shared memory so that every
+// store instruction covers whole 128-byte lines (a lane per row would touch 32
+// lines with 16 bytes each).
 template <int EPI, int HD>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase, int row, int nt) {
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase, int row, int nt,
+                                              uint8_t* stg = nullptr) {
   const bool live = row < a.M;
   const int col0 = nt * BN;
   if constexpr (EPI == EPI_RESID) {
@@ -195,6 +200,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
     // One head (hd columns) at a time: bias, rotate-half RoPE for q/k
     // (src/tensor.rs:158-171), then q -> Q rows, k/v -> paged KV cache.
     constexpr int hd = HD;
+    const int lane = threadIdx.x & 31;
     int pos = 0, slot = 0;
     if (live) {
       pos = a.pos[row];
@@ -202,7 +208,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
     }
     for (int hc = 0; hc < BN; hc += hd) {
       const int cb = col0 + hc;
-      if (cb >= a.N) break;
+      if (cb >= a.N) break;  // uniform across the warp
       float v[hd];
 #pragma unroll
       for (int c = 0; c < hd / 32; c++) {
@@ -213,7 +219,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
 #pragma unroll
         for (int i = 0; i < 32; i++) v[c * 32 + i] = __uint_as_float(r[i]);
       }
-      if (!live) continue;
+      if (!live && !stg) continue;
       if (a.bias) {
         const float4* b4 = reinterpret_cast<const float4*>(a.bias + cb);
 #pragma unroll
@@ -241,18 +247,48 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
           v[j + 1 + hd / 2] = y1 * t.z + y0 * t.w;
         }
       }
-      if (cb < a.qd) {
-        half* dst = reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb;
-#pragma unroll
-        for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
-      } else {
-        const int kvh = is_v ? (cb - a.qd - a.kd) / hd : (cb - a.qd) / hd;
-        const int page = slot / a.page_size, off = slot % a.page_size;
-        half* base = is_v ? a.vcache : a.kcache;
-        half* dst = base + (((size_t)page * a.kvh + kvh) * a.page_size + off) * hd;
-#pragma unroll
-        for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
+      half* dst = nullptr;
+      if (live) {
+        if (cb < a.qd) {
+          dst = reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + cb;
+        } else {
+          const int kvh = is_v ? (cb - a.qd - a.kd) / hd : (cb - a.qd) / hd;
+          const int page = slot / a.page_size, off = slot % a.page_size;
+          half* base = is_v ? a.vcache : a.kcache;
+          dst = base + (((size_t)page * a.kvh + kvh) * a.page_size + off) * hd;
+        }
       }
+      if (!stg) {
+#pragma unroll
+        for (int c = 0; c < hd / 32; c++) store_f16x32(dst + c * 32, v + c * 32, 32);
+        continue;
+      }
+      // Through shared memory: lane l's row as hd/8 16-byte chunks, chunk j
+      // at l * 2hd + (j ^ (l % 8)) * 16 (conflict-free writes and reads);
+      // then each store instruction moves 512 contiguous bytes of rows.
+      constexpr int CH = hd / 8;
+#pragma unroll
+      for (int j = 0; j < CH; j++) {
+        half2 h0 = __floats2half2_rn(v[8 * j], v[8 * j + 1]), h1 = __floats2half2_rn(v[8 * j + 2], v[8 * j + 3]);
+        half2 h2 = __floats2half2_rn(v[8 * j + 4], v[8 * j + 5]), h3 = __floats2half2_rn(v[8 * j + 6], v[8 * j + 7]);
+        uint4 u;
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        u.z = *reinterpret_cast<uint32_t*>(&h2);
+        u.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(stg + lane * (2 * hd) + ((j ^ (lane & 7)) << 4)) = u;
+      }
+      __syncwarp();
+      const unsigned long long dmine = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+      for (int i = 0; i < CH; i++) {
+        const int c = i * 32 + lane, r = c / CH, j = c % CH;
+        const unsigned long long dr = __shfl_sync(0xffffffffu, dmine, r);
+        if (dr)
+          *reinterpret_cast<uint4*>(dr + (unsigned long long)j * 16) =
+              *reinterpret_cast<const uint4*>(stg + r * (2 * hd) + ((j ^ (r & 7)) << 4));
+      }
+      __syncwarp();
     }
   }
 }
@@ -612,7 +648,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         resid_tma_tile(a, &tmR, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row - lane, nt * BN, stg,
                        lane, nsplit > 1 ? unit / tiles : -1);
       else
-        epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt);
+        epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt,
+                               EPI == EPI_QKV ? stg : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
@@ -700,7 +737,8 @@ static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, cons
 template <int EPI, int HD>
 static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const GemmArgs& a,
                                int num_sms, cudaStream_t st) {
-  constexpr int SMEM = EPI == EPI_RESID ? PAIR_SMEM_RESID : PAIR_SMEM;
+  // the residual and QKV epilogues stage through the per-warp buffers at PAIR_STG
+  constexpr int SMEM = (EPI == EPI_RESID || EPI == EPI_QKV) ? PAIR_SMEM_RESID : PAIR_SMEM;
   // Per device: the attribute is set once and the number of CTA pairs that
   // fit at once is queried once, so the persistent grid never exceeds what is
   // co-resident (a pair left for a second wave would double the time).
