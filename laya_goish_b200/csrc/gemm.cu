@@ -182,6 +182,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
   } else if constexpr (EPI == EPI_SWIGLU) {
     // B rows of tile nt: [0,128) gate rows, [128,256) up rows of FFN
     // columns nt*128 .. nt*128+127 (interleaved at load time).
+    // With a staging buffer and a whole tile (128 columns = 256 bytes per
+    // row), the rows go through shared memory (16-byte unit j of lane l at
+    // l * 256 + (j ^ (l % 8)) * 16) and each store instruction writes two
+    // rows' 256 contiguous bytes.
+    const int lane = threadIdx.x & 31;
+    const bool coop = stg != nullptr && nt * 128 + 128 <= a.N / 2 && (a.ldo % 8) == 0;
     for (int c = 0; c < 4; c++) {
       const int fc = nt * 128 + c * 32;
       if (fc >= a.N / 2) break;
@@ -193,7 +199,37 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; i++) v[i] = silu_f(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
-      if (live) store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + fc, v, min(32, a.N / 2 - fc));
+      if (coop) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const int j = 4 * c + q;
+          half2 h0 = __floats2half2_rn(v[8 * q], v[8 * q + 1]), h1 = __floats2half2_rn(v[8 * q + 2], v[8 * q + 3]);
+          half2 h2 = __floats2half2_rn(v[8 * q + 4], v[8 * q + 5]), h3 = __floats2half2_rn(v[8 * q + 6], v[8 * q + 7]);
+          uint4 u;
+          u.x = *reinterpret_cast<uint32_t*>(&h0);
+          u.y = *reinterpret_cast<uint32_t*>(&h1);
+          u.z = *reinterpret_cast<uint32_t*>(&h2);
+          u.w = *reinterpret_cast<uint32_t*>(&h3);
+          *reinterpret_cast<uint4*>(stg + lane * 256 + ((j ^ (lane & 7)) << 4)) = u;
+        }
+      } else if (live) {
+        store_f16x32(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + fc, v, min(32, a.N / 2 - fc));
+      }
+    }
+    if (coop) {
+      __syncwarp();
+      const unsigned long long dmine =
+          live ? reinterpret_cast<unsigned long long>(reinterpret_cast<half*>(a.out) + (size_t)row * a.ldo + nt * 128)
+               : 0ull;
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int ch = i * 32 + lane, r = ch / 16, j = ch % 16;
+        const unsigned long long dr = __shfl_sync(0xffffffffu, dmine, r);
+        if (dr)
+          *reinterpret_cast<uint4*>(dr + (unsigned long long)j * 16) =
+              *reinterpret_cast<const uint4*>(stg + r * 256 + ((j ^ (r & 7)) << 4));
+      }
+      __syncwarp();
     }
   } else if constexpr (EPI == EPI_QKV) {
     // Columns: [0,qd) q heads, [qd,qd+kd) k heads, [qd+kd,qd+2kd) v heads.
@@ -649,7 +685,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                        lane, nsplit > 1 ? unit / tiles : -1);
       else
         epilogue_tile<EPI, HD>(a, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, row, nt,
-                               EPI == EPI_QKV ? stg : nullptr);
+                               (EPI == EPI_QKV || EPI == EPI_SWIGLU) ? stg : nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(cluster_addr(&tempty[acc], 0));
@@ -737,8 +773,8 @@ static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, cons
 template <int EPI, int HD>
 static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const GemmArgs& a,
                                int num_sms, cudaStream_t st) {
-  // the residual and QKV epilogues stage through the per-warp buffers at PAIR_STG
-  constexpr int SMEM = (EPI == EPI_RESID || EPI == EPI_QKV) ? PAIR_SMEM_RESID : PAIR_SMEM;
+  // the residual, QKV and SwiGLU epilogues stage through the per-warp buffers at PAIR_STG
+  constexpr int SMEM = (EPI == EPI_RESID || EPI == EPI_QKV || EPI == EPI_SWIGLU) ? PAIR_SMEM_RESID : PAIR_SMEM;
   // Per device: the attribute is set once and the number of CTA pairs that
   // fit at once is queried once, so the persistent grid never exceeds what is
   // co-resident (a pair left for a second wave would double the time).
