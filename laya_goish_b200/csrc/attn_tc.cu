@@ -292,12 +292,29 @@ __global__ void __launch_bounds__(192, 1)
           l *= corr;
         }
         mref = nref;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        // Packed F32x2 FMA / add (one instruction per two scores, the same
+        // IEEE results as two fmaf / two adds); the sums keep the order of
+        // four running partials l[c % 4].
+        unsigned long long sc2, nm2, acc2[2];
+        asm("mov.b64 %0, {%1, %1};" : "=l"(sc2) : "f"(scale_log2));
+        asm("mov.b64 %0, {%1, %1};" : "=l"(nm2) : "f"(-mref));
+        asm("mov.b64 %0, {%1, %1};" : "=l"(acc2[0]) : "f"(0.f));
+        acc2[1] = acc2[0];
 #pragma unroll
-        for (int c = 0; c < 64; c++) {
-          s[c] = ex2(fmaf(s[c], scale_log2, -mref));
-          l4[c & 3] += s[c];
+        for (int c = 0; c < 64; c += 2) {
+          unsigned long long x2, e2, p2;
+          asm("mov.b64 %0, {%1, %2};" : "=l"(x2) : "f"(s[c]), "f"(s[c + 1]));
+          asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(e2) : "l"(x2), "l"(sc2), "l"(nm2));
+          float e0, e1;
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(e0), "=f"(e1) : "l"(e2));
+          s[c] = ex2(e0);
+          s[c + 1] = ex2(e1);
+          asm("mov.b64 %0, {%1, %2};" : "=l"(p2) : "f"(s[c]), "f"(s[c + 1]));
+          asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc2[(c >> 1) & 1]) : "l"(acc2[(c >> 1) & 1]), "l"(p2));
         }
+        float l4[4];
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(l4[0]), "=f"(l4[1]) : "l"(acc2[0]));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(l4[2]), "=f"(l4[3]) : "l"(acc2[1]));
         l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
         // P row r: [128 rows][64 keys] F16, 16-byte unit u of row r at u ^ (r % 8)
         uint8_t* prow = sP + sb * C::P_BYTES + r * 128;
