@@ -798,7 +798,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     const int ns = pend;
     pend = 0;
     if (ns > 1) return rmsnorm_merge(x, rows, n, r.kpart.as<float>(), ns, (size_t)M * d, w, d, c.eps, o16, o32, st);
-    return rmsnorm(x, rows, n, w, d, c.eps, o16, o32, st);
+    return rmsnorm(x, rows, n, w, d, c.eps, o16, o32, st, false, r.err);
   };
   for (int l = 0; l < c.L; l++) {
     const Layer& L = r.layers[l];

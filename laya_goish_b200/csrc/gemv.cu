@@ -53,13 +53,6 @@ constexpr int GV_MAX_STAGES = 8;     // ring depth: as many stages as shared mem
 constexpr int GV_WARPS = 16;                   // compute warps; warp GV_WARPS is the producer
 constexpr int GV_THREADS = (GV_WARPS + 2) * 32;  // + producer warp + epilogue warp
 
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
   asm volatile(

@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "mma.cuh"
+#include "ptx.cuh"
 #include "launch.h"
 
 namespace laya {
@@ -245,9 +246,84 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const int* __restrict__ ro
   }
 }
 
+// Plain rows (no gather, no K-split partials): one 128-thread CTA per row
+// fetches the whole F32 row with one bulk copy into shared memory, so up to
+// 16 rows per SM are in flight (the register-held kernel keeps 8 CTAs of 256
+// threads per SM, too few bytes in flight to reach HBM speed).
+constexpr int RNB_THREADS = 128;
+__global__ void __launch_bounds__(RNB_THREADS) rmsnorm_bulk_kernel(const float* __restrict__ x,
+                                                                   const float* __restrict__ w, int d, float eps,
+                                                                   half* __restrict__ out16, float* __restrict__ out32,
+                                                                   unsigned* err) {
+  extern __shared__ float4 rnb_row[];
+  __shared__ uint64_t bar;
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    mbar_expect_tx(&bar, (uint32_t)d * 4);
+    bulk_g2s(rnb_row, x + (size_t)r * d, (uint32_t)d * 4, &bar);
+  }
+  __syncthreads();
+  if (!mbar_wait(&bar, 0, 2000000000ll)) {
+    if (threadIdx.x == 0) atomicOr(err, 1u << 20);
+    mbar_wait(&bar, 0, 2000000000ll);  // give the copy in flight a second bounded wait before leaving
+    return;
+  }
+  // The sum of squares in exactly the order of rmsnorm_kernel's 256 threads
+  // (thread t sums float4 columns t, t + 256, ...; warps reduce by xor
+  // shuffles, then warp 0 over the 8 warp sums), so both kernels give the
+  // same bits: this thread plays threads t and t + 128 of that layout.
+  float sa = 0.f, sb = 0.f;
+  for (int i = threadIdx.x; i < d / 4; i += 256) {
+    const float4 v = rnb_row[i];
+    sa += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  for (int i = threadIdx.x + 128; i < d / 4; i += 256) {
+    const float4 v = rnb_row[i];
+    sb += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+  }
+  const int wq = threadIdx.x / 32, lq = threadIdx.x % 32;
+  if (lq == 0) {
+    red[wq] = sa;
+    red[wq + 4] = sb;
+  }
+  __syncthreads();
+  if (wq == 0) {
+    float t = lq < 8 ? red[lq] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lq == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float ss = red[0];
+  const float scale = 1.f / sqrtf(ss / (float)d + eps);
+  for (int i = threadIdx.x; i < d / 4; i += RNB_THREADS) rms_out(rnb_row[i], scale, w, 4 * i, (size_t)r * d, out16, out32);
+}
+
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
-                    float* out32, cudaStream_t st, bool pdl) {
+                    float* out32, cudaStream_t st, bool pdl, unsigned* err) {
   if (!nrows) return cudaSuccess;
+  if (!rows && err && d % 4 == 0 && d <= 12288 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+      cudaError_t e = cudaFuncSetAttribute(rmsnorm_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 48 * 1024);
+      if (e != cudaSuccess) return e;
+      configured[dev & 63] = true;
+    }
+    return launch_k(rmsnorm_bulk_kernel, dim3(nrows), dim3(RNB_THREADS), (size_t)d * 4, st, pdl, x, w, d, eps, out16,
+                    out32, err);
+  }
   return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, const_cast<float*>(x), rows, w, d, eps, out16,
                   out32, (const float*)nullptr, 0, (size_t)0);
 }

@@ -44,8 +44,10 @@ cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* 
 cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstride, int goff, cudaStream_t st);
 // pdl: launch with programmatic dependent launch allowed (decode graph).
 cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st, bool pdl = false);
+// err (may be null): device error word; with it, plain rows (rows null) take
+// the bulk-copy kernel, whose bounded wait reports there.
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
-                    float* out32, cudaStream_t st, bool pdl = false);
+                    float* out32, cudaStream_t st, bool pdl = false, unsigned* err = nullptr);
 // rmsnorm of x + part[0] + ... + part[nsplit-1] (K-split partial sums of the
 // GEMM that wrote x, planes split_stride floats apart); without a row gather
 // (rows null) the merged rows are also written back to x.
