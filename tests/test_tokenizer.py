@@ -127,3 +127,28 @@ def test_synthetic_model_vocabulary_round_trip(tmp_path):
     assert t.encode("the") == [t.vocab["the"]]
     with pytest.raises(GGUFError):
         read_metadata(b"GGUF" + b"\x02\x00\x00\x00")
+
+
+def test_gguf_metadata_reader_errors_and_types():
+    import struct
+
+    def kv_str(k, v):
+        kb, vb = k.encode(), v.encode()
+        return struct.pack("<Q", len(kb)) + kb + struct.pack("<IQ", 8, len(vb)) + vb
+
+    head = b"GGUF" + struct.pack("<IQQ", 3, 0, 3)
+    body = kv_str("general.name", "x")
+    body += struct.pack("<Q", 1) + b"f" + struct.pack("<Id", 12, 2.5)          # f64 scalar
+    body += struct.pack("<Q", 1) + b"a" + struct.pack("<IIQ", 9, 4, 3) + struct.pack("<3I", 7, 8, 9)  # u32 array
+    m = read_metadata(head + body)
+    assert m == {"general.name": "x", "f": 2.5, "a": [7, 8, 9]}
+    with pytest.raises(GGUFError):
+        read_metadata(b"GGUX" + head[4:] + body)  # bad magic
+    with pytest.raises(GGUFError):
+        read_metadata(head + body[:-3])  # truncated
+    bad_type = b"GGUF" + struct.pack("<IQQ", 3, 0, 1) + struct.pack("<Q", 1) + b"k" + struct.pack("<I", 13)
+    with pytest.raises(GGUFError):
+        read_metadata(bad_type)
+    bad_utf8 = b"GGUF" + struct.pack("<IQQ", 3, 0, 1) + struct.pack("<Q", 1) + b"k" + struct.pack("<IQ", 8, 2) + b"\xff\xfe"
+    with pytest.raises(GGUFError):
+        read_metadata(bad_utf8)
