@@ -41,7 +41,8 @@ _lib = None
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB) or os.path.getmtime(_LIB) < os.path.getmtime(os.path.join(_HERE, "oracle.c")):
+        srcs = [os.path.join(_HERE, f) for f in ("oracle.c", "openthai.c", "oracle.h")]
+        if not os.path.exists(_LIB) or os.path.getmtime(_LIB) < max(os.path.getmtime(f) for f in srcs):
             build()
         L = ctypes.CDLL(_LIB)
         P = ctypes.c_void_p
@@ -58,6 +59,9 @@ def lib() -> ctypes.CDLL:
         L.or_model_free.argtypes = [P]
         L.or_model_dim.argtypes = [P, ctypes.c_int]
         L.or_forward.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
+        i = ctypes.c_int
+        L.or_ot_full.argtypes = [P, i, i, i, i, i, i, ctypes.c_float, P, P, P, P, P, P, i, P]
+        L.or_ot_delta.argtypes = [P, i, i, i, i, P, P, P, P, P, P, P, P, P, i, P]
         L.or_head.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
         L.or_decide.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(Question), ctypes.POINTER(Answer)]
         _lib = L
@@ -172,3 +176,32 @@ class Model:
         return {"kind": a.kind, "choice": a.choice, "score": a.score, "noul": a.noul,
                 "confidence": a.confidence, "probabilities": list(a.probabilities[:k]),
                 "logits": list(a.logits[:k])}
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def ot_full(x, wq, wk, wv, wo, qn, kn, H, KV, hd, rot, theta, threads=4) -> np.ndarray:
+    """OpenThai gated full attention of one sequence x [s][d] (Full::run)."""
+    x = _f32(x)
+    s, d = x.shape
+    args = [_f32(a) for a in (wq, wk, wv, wo, qn, kn)]
+    out = np.zeros((s, d), np.float32)
+    rc = lib().or_ot_full(x.ctypes.data, s, d, H, KV, hd, rot, theta, *[a.ctypes.data for a in args], threads,
+                          out.ctypes.data)
+    if rc:
+        raise ValueError(f"or_ot_full failed ({rc})")
+    return out
+
+
+def ot_delta(x, wqkv, wz, wa, wb, wo, conv, dt, alog, normw, nh, hk, threads=4) -> np.ndarray:
+    """OpenThai gated DeltaNet mixer of one sequence x [s][d] (Delta::run)."""
+    x = _f32(x)
+    s, d = x.shape
+    args = [_f32(a) for a in (wqkv, wz, wa, wb, wo, conv, dt, alog, normw)]
+    out = np.zeros((s, d), np.float32)
+    rc = lib().or_ot_delta(x.ctypes.data, s, d, nh, hk, *[a.ctypes.data for a in args], threads, out.ctypes.data)
+    if rc:
+        raise ValueError(f"or_ot_delta failed ({rc})")
+    return out

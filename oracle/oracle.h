@@ -39,6 +39,17 @@ void or_matrix_apply(const float* w, int rows, int cols, const float* x, int m,
                      const float* bias, int threads, float* out);
 /* src/tensor.rs:132-140 */
 void or_softmax(const float* x, int n, float* p);
+
+/* OpenThai sequence mixers on one sequence x[s][d] -> out[s][d] (openthai.c):
+ * gated full attention (Full::run, src/models/openthai/model.rs:243-299) and
+ * the gated DeltaNet recurrence (Delta::run, model.rs:301-363).  Matrices are
+ * row-major [out rows][in cols] F32.  Return 0, or < 0 on bad shapes. */
+int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, float theta, const float* wq,
+               const float* wk, const float* wv, const float* wo, const float* qn, const float* kn, int threads,
+               float* out);
+int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,
+                const float* wb, const float* wo, const float* conv, const float* dt, const float* alog,
+                const float* normw, int threads, float* out);
 /* src/models/laya/decision.rs:155-167 */
 float or_confidence(const float* p, int n);
 
