@@ -131,6 +131,15 @@ int laya_matrix_apply(int device, uint32_t kind, const uint8_t* w, int rows, int
  * first device: final-normed hidden rows at `read` positions of one causal
  * sequence.  out: nread * d_model floats. */
 int laya_forward(laya_model* m, const int32_t* ids, int n, const int32_t* read, int nread, float* out);
+/* The gated DeltaNet recurrence of OpenThai's linear-attention layers
+ * (Delta::run, src/models/openthai/model.rs:322-355) for one sequence of s
+ * tokens on device `device`: qkv = s rows of [q | k | v] heads (3 * nh * hk
+ * floats, after the causal convolution and SiLU), a and b = s rows of nh
+ * gate projections, dt = dt_bias[nh], alog = A_log[nh]; out = s rows of
+ * nh * hk floats, before the per-head output norm.  hk is 64 or 128 (the
+ * reference uses 128).  Host buffers. */
+int laya_gated_delta(int device, const float* qkv, const float* a, const float* b, const float* dt,
+                     const float* alog, int s, int nh, int hk, float* out);
 /* Decodes a weight tensor of the model from its device layout back to F32
  * (for parity checks of the upload transcoding).  out: element count floats. */
 int laya_tensor_f32(laya_model* m, const char* name, float* out, size_t max_elems);

@@ -269,6 +269,31 @@ int laya_dequantize(int device, uint32_t kind, const uint8_t* blocks, size_t nby
   return 0;
 }
 
+int laya_gated_delta(int device, const float* qkv, const float* a, const float* b, const float* dt,
+                     const float* alog, int s, int nh, int hk, float* out) {
+  if (!qkv || !a || !b || !dt || !alog || !out || s < 0 || nh < 1 || (hk != 64 && hk != 128))
+    return fail(LAYA_E_INVALID, "invalid DeltaNet arguments (hk must be 64 or 128)");
+  if (s == 0) return 0;
+  LAYA_CK(cudaSetDevice(device));
+  const size_t w = (size_t)nh * hk, nq = (size_t)s * 3 * w, nab = (size_t)s * nh, no = (size_t)s * w;
+  DevBuf dq, da, db, dp, dout;
+  int rc;
+  if ((rc = dq.ensure(nq * 4)) || (rc = da.ensure(nab * 4)) || (rc = db.ensure(nab * 4)) ||
+      (rc = dp.ensure((size_t)2 * nh * 4)) || (rc = dout.ensure(no * 4)))
+    return rc;
+  float* dpar = dp.as<float>();
+  cudaError_t e = cudaMemcpy(dq.p, qkv, nq * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(da.p, a, nab * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(db.p, b, nab * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dpar, dt, (size_t)nh * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dpar + nh, alog, (size_t)nh * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = gated_delta(dq.as<float>(), da.as<float>(), db.as<float>(), dpar, dpar + nh, s, nh, hk, dout.as<float>(), 0);
+  if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, no * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "laya_gated_delta");
+  return 0;
+}
+
 int laya_matrix_apply(int device, uint32_t kind, const uint8_t* w, int rows, int cols, const float* x, int m,
                       const float* bias, float* out) {
   int block, size;

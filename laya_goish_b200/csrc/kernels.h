@@ -51,6 +51,11 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
 // rmsnorm of x + part[0] + ... + part[nsplit-1] (K-split partial sums of the
 // GEMM that wrote x, planes split_stride floats apart); without a row gather
 // (rows null) the merged rows are also written back to x.
+// Gated DeltaNet recurrence (deltanet.cu): qkv [s][3 nh hk] after the
+// convolution and SiLU, a / b [s][nh], dt / A_log [nh] -> out [s][nh hk]
+// (hk 64 or 128).  All device pointers.
+cudaError_t gated_delta(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
+                        int nh, int hk, float* out, cudaStream_t st);
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,

@@ -198,3 +198,17 @@ def matrix_apply(kind: int, w_bytes, rows: int, cols: int, x, bias=None, device:
                                        None if b is None else b.ctypes.data_as(ctypes.c_void_p),
                                        out.ctypes.data_as(ctypes.c_void_p)))
     return out
+
+
+def gated_delta(qkv, a, b, dt, alog, nh: int, hk: int, device: int = 0) -> np.ndarray:
+    """OpenThai's gated DeltaNet recurrence on the GPU (Delta::run,
+    src/models/openthai/model.rs:322-355): qkv [s][3 nh hk] after the
+    convolution and SiLU, a / b [s][nh], dt / A_log [nh] -> [s][nh hk]."""
+    q = np.ascontiguousarray(np.asarray(qkv, np.float32))
+    s = q.shape[0]
+    arrs = [np.ascontiguousarray(np.asarray(v, np.float32)) for v in (a, b, dt, alog)]
+    out = np.zeros((s, nh * hk), np.float32)
+    check(_lib.lib().laya_gated_delta(device, q.ctypes.data_as(ctypes.c_void_p),
+                                      *[v.ctypes.data_as(ctypes.c_void_p) for v in arrs], s, nh, hk,
+                                      out.ctypes.data_as(ctypes.c_void_p)))
+    return out

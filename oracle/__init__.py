@@ -62,6 +62,7 @@ def lib() -> ctypes.CDLL:
         i = ctypes.c_int
         L.or_ot_full.argtypes = [P, i, i, i, i, i, i, ctypes.c_float, P, P, P, P, P, P, i, P]
         L.or_ot_delta.argtypes = [P, i, i, i, i, P, P, P, P, P, P, P, P, P, i, P]
+        L.or_ot_delta_core.argtypes = [P, P, P, P, P, i, i, i, P]
         L.or_head.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
         L.or_decide.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(Question), ctypes.POINTER(Answer)]
         _lib = L
@@ -204,4 +205,17 @@ def ot_delta(x, wqkv, wz, wa, wb, wo, conv, dt, alog, normw, nh, hk, threads=4) 
     rc = lib().or_ot_delta(x.ctypes.data, s, d, nh, hk, *[a.ctypes.data for a in args], threads, out.ctypes.data)
     if rc:
         raise ValueError(f"or_ot_delta failed ({rc})")
+    return out
+
+
+def ot_delta_core(qkv, a, b, dt, alog, nh, hk) -> np.ndarray:
+    """The DeltaNet recurrence alone: qkv [s][3 nh hk] (after conv + SiLU),
+    a / b [s][nh], dt / A_log [nh] -> [s][nh hk] before the output norm."""
+    qkv = _f32(qkv)
+    s = qkv.shape[0]
+    args = [_f32(v) for v in (a, b, dt, alog)]
+    out = np.zeros((s, nh * hk), np.float32)
+    rc = lib().or_ot_delta_core(qkv.ctypes.data, *[v.ctypes.data for v in args], s, nh, hk, out.ctypes.data)
+    if rc:
+        raise ValueError(f"or_ot_delta_core failed ({rc})")
     return out

@@ -96,32 +96,17 @@ int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, flo
   return 0;
 }
 
-int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,
-                const float* wb, const float* wo, const float* conv, const float* dt, const float* alog,
-                const float* normw, int threads, float* out) {
+/* The DeltaNet recurrence alone (model.rs:322-355): qkv[s][3 nh hk] after
+ * the convolution and SiLU, a / b [s][nh] projections, dt / A_log [nh];
+ * out[s][nh hk] before the output norm and gate. */
+int or_ot_delta_core(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
+                     int nh, int hk, float* o) {
   if (s < 1 || nh < 1 || hk < 1) return -1;
   const int w = nh * hk, C = 3 * w;
-  float* raw = malloc(sizeof(float) * (size_t)s * C);
-  float* qkv = malloc(sizeof(float) * (size_t)s * C);
-  float* z = malloc(sizeof(float) * (size_t)s * w);
-  float* a = malloc(sizeof(float) * (size_t)s * nh);
-  float* b = malloc(sizeof(float) * (size_t)s * nh);
-  float* o = calloc((size_t)s * w, sizeof(float));
   float* state = malloc(sizeof(float) * (size_t)hk * hk);
   float* delta = malloc(sizeof(float) * (size_t)hk);
-  if (!raw || !qkv || !z || !a || !b || !o || !state || !delta) return -2;
-  or_matrix_apply(wqkv, C, d, x, s, NULL, threads, raw);
-  or_matrix_apply(wz, w, d, x, s, NULL, threads, z);
-  or_matrix_apply(wa, nh, d, x, s, NULL, threads, a);
-  or_matrix_apply(wb, nh, d, x, s, NULL, threads, b);
-  /* causal depthwise conv (width 4) + SiLU */
-  for (int i = 0; i < s; i++)
-    for (int c = 0; c < C; c++) {
-      float acc = 0.f;
-      for (int j = 0; j < 4; j++)
-        if (i + j >= 3) acc += raw[(size_t)(i + j - 3) * C + c] * conv[(size_t)c * 4 + j];
-      qkv[(size_t)i * C + c] = ot_silu(acc);
-    }
+  if (!state || !delta) return -2;
+  memset(o, 0, sizeof(float) * (size_t)s * w);
   for (int h = 0; h < nh; h++) {
     memset(state, 0, sizeof(float) * (size_t)hk * hk);
     for (int i = 0; i < s; i++) {
@@ -149,9 +134,38 @@ int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv,
       }
     }
   }
+  free(state), free(delta);
+  return 0;
+}
+
+int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,
+                const float* wb, const float* wo, const float* conv, const float* dt, const float* alog,
+                const float* normw, int threads, float* out) {
+  if (s < 1 || nh < 1 || hk < 1) return -1;
+  const int w = nh * hk, C = 3 * w;
+  float* raw = malloc(sizeof(float) * (size_t)s * C);
+  float* qkv = malloc(sizeof(float) * (size_t)s * C);
+  float* z = malloc(sizeof(float) * (size_t)s * w);
+  float* a = malloc(sizeof(float) * (size_t)s * nh);
+  float* b = malloc(sizeof(float) * (size_t)s * nh);
+  float* o = calloc((size_t)s * w, sizeof(float));
+  if (!raw || !qkv || !z || !a || !b || !o) return -2;
+  or_matrix_apply(wqkv, C, d, x, s, NULL, threads, raw);
+  or_matrix_apply(wz, w, d, x, s, NULL, threads, z);
+  or_matrix_apply(wa, nh, d, x, s, NULL, threads, a);
+  or_matrix_apply(wb, nh, d, x, s, NULL, threads, b);
+  /* causal depthwise conv (width 4) + SiLU */
+  for (int i = 0; i < s; i++)
+    for (int c = 0; c < C; c++) {
+      float acc = 0.f;
+      for (int j = 0; j < 4; j++)
+        if (i + j >= 3) acc += raw[(size_t)(i + j - 3) * C + c] * conv[(size_t)c * 4 + j];
+      qkv[(size_t)i * C + c] = ot_silu(acc);
+    }
+  or_ot_delta_core(qkv, a, b, dt, alog, s, nh, hk, o);
   ot_rms(o, normw, hk, s * nh, 0.f);
   for (size_t e = 0; e < (size_t)s * w; e++) o[e] *= ot_silu(z[e]);
   or_matrix_apply(wo, d, w, o, s, NULL, threads, out);
-  free(raw), free(qkv), free(z), free(a), free(b), free(o), free(state), free(delta);
+  free(raw), free(qkv), free(z), free(a), free(b), free(o);
   return 0;
 }
