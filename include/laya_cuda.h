@@ -140,6 +140,16 @@ int laya_forward(laya_model* m, const int32_t* ids, int n, const int32_t* read, 
  * reference uses 128).  Host buffers. */
 int laya_gated_delta(int device, const float* qkv, const float* a, const float* b, const float* dt,
                      const float* alog, int s, int nh, int hk, float* out);
+/* The gated full attention of OpenThai's attention layers after their
+ * projections (Full::run, src/models/openthai/model.rs:248-296) for one
+ * sequence of s tokens: qgate = s rows of H heads x [query hd | gate hd],
+ * k and v = s rows of KV x hd, qn / kn = the per-head q / k RMSNorm weights
+ * (applied with offset 1, eps 1e-6); RoPE on the first `rot` dimensions of a
+ * head with base theta (the reference: hd 256, rot 64, theta 1e7); out = s
+ * rows of H x hd, sigmoid(gate) x attention, before o_proj.  hd 64, 128 or
+ * 256; H a multiple of KV.  Host buffers. */
+int laya_gated_attention(int device, const float* qgate, const float* k, const float* v, const float* qn,
+                         const float* kn, int s, int H, int KV, int hd, int rot, float theta, float* out);
 /* Decodes a weight tensor of the model from its device layout back to F32
  * (for parity checks of the upload transcoding).  out: element count floats. */
 int laya_tensor_f32(laya_model* m, const char* name, float* out, size_t max_elems);

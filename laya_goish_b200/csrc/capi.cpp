@@ -294,6 +294,33 @@ int laya_gated_delta(int device, const float* qkv, const float* a, const float* 
   return 0;
 }
 
+int laya_gated_attention(int device, const float* qgate, const float* k, const float* v, const float* qn,
+                         const float* kn, int s, int H, int KV, int hd, int rot, float theta, float* out) {
+  if (!qgate || !k || !v || !qn || !kn || !out || s < 0 || H < 1 || KV < 1 || H % KV ||
+      (hd != 64 && hd != 128 && hd != 256) || rot < 0 || rot > hd || rot % 2)
+    return fail(LAYA_E_INVALID, "invalid gated-attention arguments");
+  if (s == 0) return 0;
+  LAYA_CK(cudaSetDevice(device));
+  const size_t nq = (size_t)s * H * 2 * hd, nk = (size_t)s * KV * hd, no = (size_t)s * H * hd;
+  DevBuf dq, dk, dv, dn, dsc, dout;
+  int rc;
+  if ((rc = dq.ensure(nq * 4)) || (rc = dk.ensure(nk * 4)) || (rc = dv.ensure(nk * 4)) ||
+      (rc = dn.ensure((size_t)2 * hd * 4)) || (rc = dsc.ensure((no + nk) * 4)) || (rc = dout.ensure(no * 4)))
+    return rc;
+  float* dnw = dn.as<float>();
+  cudaError_t e = cudaMemcpy(dq.p, qgate, nq * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dk.p, k, nk * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dv.p, v, nk * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dnw, qn, (size_t)hd * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dnw + hd, kn, (size_t)hd * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = gated_attention(dq.as<float>(), dk.as<float>(), dv.as<float>(), dnw, dnw + hd, s, H, KV, hd, rot, theta,
+                        dsc.as<float>(), dout.as<float>(), 0);
+  if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, no * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "laya_gated_attention");
+  return 0;
+}
+
 int laya_matrix_apply(int device, uint32_t kind, const uint8_t* w, int rows, int cols, const float* x, int m,
                       const float* bias, float* out) {
   int block, size;

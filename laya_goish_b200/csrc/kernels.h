@@ -56,6 +56,12 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
 // (hk 64 or 128).  All device pointers.
 cudaError_t gated_delta(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
                         int nh, int hk, float* out, cudaStream_t st);
+// Gated full attention after the projections (gated_attn.cu): qgate
+// [s][H][query hd | gate hd], k / v [s][KV][hd], q / k norm weights [hd] ->
+// out [s][H][hd]; scratch holds s * (H + KV) * hd floats.  hd 64/128/256.
+cudaError_t gated_attention(const float* qgate, const float* k, const float* v, const float* qn, const float* kn,
+                            int s, int H, int KV, int hd, int rot, float theta, float* scratch, float* out,
+                            cudaStream_t st);
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,

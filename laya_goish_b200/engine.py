@@ -212,3 +212,18 @@ def gated_delta(qkv, a, b, dt, alog, nh: int, hk: int, device: int = 0) -> np.nd
                                       *[v.ctypes.data_as(ctypes.c_void_p) for v in arrs], s, nh, hk,
                                       out.ctypes.data_as(ctypes.c_void_p)))
     return out
+
+
+def gated_attention(qgate, k, v, qn, kn, H: int, KV: int, hd: int, rot: int, theta: float,
+                    device: int = 0) -> np.ndarray:
+    """OpenThai's gated full attention after the projections on the GPU
+    (Full::run, src/models/openthai/model.rs:248-296): qgate [s][H 2hd], k / v
+    [s][KV hd], q / k norm weights [hd] -> [s][H hd] before o_proj."""
+    q = np.ascontiguousarray(np.asarray(qgate, np.float32))
+    s = q.shape[0]
+    arrs = [np.ascontiguousarray(np.asarray(a, np.float32)) for a in (k, v, qn, kn)]
+    out = np.zeros((s, H * hd), np.float32)
+    check(_lib.lib().laya_gated_attention(device, q.ctypes.data_as(ctypes.c_void_p),
+                                          *[a.ctypes.data_as(ctypes.c_void_p) for a in arrs], s, H, KV, hd, rot,
+                                          theta, out.ctypes.data_as(ctypes.c_void_p)))
+    return out

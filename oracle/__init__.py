@@ -63,6 +63,7 @@ def lib() -> ctypes.CDLL:
         L.or_ot_full.argtypes = [P, i, i, i, i, i, i, ctypes.c_float, P, P, P, P, P, P, i, P]
         L.or_ot_delta.argtypes = [P, i, i, i, i, P, P, P, P, P, P, P, P, P, i, P]
         L.or_ot_delta_core.argtypes = [P, P, P, P, P, i, i, i, P]
+        L.or_ot_full_core.argtypes = [P, P, P, P, P, i, i, i, i, i, ctypes.c_float, P]
         L.or_head.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
         L.or_decide.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(Question), ctypes.POINTER(Answer)]
         _lib = L
@@ -218,4 +219,18 @@ def ot_delta_core(qkv, a, b, dt, alog, nh, hk) -> np.ndarray:
     rc = lib().or_ot_delta_core(qkv.ctypes.data, *[v.ctypes.data for v in args], s, nh, hk, out.ctypes.data)
     if rc:
         raise ValueError(f"or_ot_delta_core failed ({rc})")
+    return out
+
+
+def ot_full_core(qgate, k, v, qn, kn, H, KV, hd, rot, theta) -> np.ndarray:
+    """Gated attention after the projections: qgate [s][H 2hd], k / v
+    [s][KV hd] -> [s][H hd] before o_proj."""
+    qgate = _f32(qgate)
+    s = qgate.shape[0]
+    args = [_f32(a) for a in (k, v, qn, kn)]
+    out = np.zeros((s, H * hd), np.float32)
+    rc = lib().or_ot_full_core(qgate.ctypes.data, *[a.ctypes.data for a in args], s, H, KV, hd, rot, theta,
+                               out.ctypes.data)
+    if rc:
+        raise ValueError(f"or_ot_full_core failed ({rc})")
     return out

@@ -41,30 +41,27 @@ static void ot_rms(float* x, const float* w, int d, int rows, float off) {
   }
 }
 
-int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, float theta, const float* wq,
-               const float* wk, const float* wv, const float* wo, const float* qn, const float* kn, int threads,
-               float* out) {
+/* Gated attention after the projections (model.rs:248-296): qgate [s][H *
+ * 2hd] (per head [query | gate]), k / v [s][KV * hd] -> out [s][H * hd],
+ * the gated attention output before o_proj. */
+int or_ot_full_core(const float* qgate, const float* kin, const float* v, const float* qn, const float* kn, int s,
+                    int H, int KV, int hd, int rot, float theta, float* att) {
   if (s < 1 || H < 1 || KV < 1 || H % KV || rot > hd || rot % 2) return -1;
   const int qd = H * hd, kd = KV * hd, grp = H / KV;
-  float* qgate = malloc(sizeof(float) * (size_t)s * 2 * qd);
   float* q = malloc(sizeof(float) * (size_t)s * qd);
   float* gate = malloc(sizeof(float) * (size_t)s * qd);
   float* k = malloc(sizeof(float) * (size_t)s * kd);
-  float* v = malloc(sizeof(float) * (size_t)s * kd);
-  float* att = calloc((size_t)s * qd, sizeof(float));
   float* sc = malloc(sizeof(float) * (size_t)s);
   float* p = malloc(sizeof(float) * (size_t)s);
-  if (!qgate || !q || !gate || !k || !v || !att || !sc || !p) return -2;
-  or_matrix_apply(wq, 2 * qd, d, x, s, NULL, threads, qgate);
+  if (!q || !gate || !k || !sc || !p) return -2;
   for (int i = 0; i < s; i++)
     for (int h = 0; h < H; h++) {
       memcpy(q + (size_t)i * qd + h * hd, qgate + (size_t)i * 2 * qd + h * 2 * hd, sizeof(float) * hd);
       memcpy(gate + (size_t)i * qd + h * hd, qgate + (size_t)i * 2 * qd + h * 2 * hd + hd, sizeof(float) * hd);
     }
   ot_rms(q, qn, hd, s * H, 1.f);
-  or_matrix_apply(wk, kd, d, x, s, NULL, threads, k);
+  memcpy(k, kin, sizeof(float) * (size_t)s * kd);
   ot_rms(k, kn, hd, s * KV, 1.f);
-  or_matrix_apply(wv, kd, d, x, s, NULL, threads, v);
   const int half = rot / 2;
   for (int pass = 0; pass < 2; pass++) {
     float* buf = pass == 0 ? q : k;
@@ -81,6 +78,7 @@ int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, flo
         }
   }
   const float root = sqrtf((float)hd);  /* the reference divides by 16 = sqrt(256) */
+  memset(att, 0, sizeof(float) * (size_t)s * qd);
   for (int i = 0; i < s; i++)
     for (int h = 0; h < H; h++) {
       const int kh = h / grp;
@@ -91,9 +89,27 @@ int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, flo
         for (int c = 0; c < hd; c++) att[(size_t)i * qd + h * hd + c] += p[j] * v[(size_t)j * kd + kh * hd + c];
     }
   for (size_t e = 0; e < (size_t)s * qd; e++) att[e] *= ot_sigmoid(gate[e]);
-  or_matrix_apply(wo, d, qd, att, s, NULL, threads, out);
-  free(qgate), free(q), free(gate), free(k), free(v), free(att), free(sc), free(p);
+  free(q), free(gate), free(k), free(sc), free(p);
   return 0;
+}
+
+int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, float theta, const float* wq,
+               const float* wk, const float* wv, const float* wo, const float* qn, const float* kn, int threads,
+               float* out) {
+  if (s < 1 || H < 1 || KV < 1 || H % KV || rot > hd || rot % 2) return -1;
+  const int qd = H * hd, kd = KV * hd;
+  float* qgate = malloc(sizeof(float) * (size_t)s * 2 * qd);
+  float* k = malloc(sizeof(float) * (size_t)s * kd);
+  float* v = malloc(sizeof(float) * (size_t)s * kd);
+  float* att = malloc(sizeof(float) * (size_t)s * qd);
+  if (!qgate || !k || !v || !att) return -2;
+  or_matrix_apply(wq, 2 * qd, d, x, s, NULL, threads, qgate);
+  or_matrix_apply(wk, kd, d, x, s, NULL, threads, k);
+  or_matrix_apply(wv, kd, d, x, s, NULL, threads, v);
+  int rc = or_ot_full_core(qgate, k, v, qn, kn, s, H, KV, hd, rot, theta, att);
+  if (!rc) or_matrix_apply(wo, d, qd, att, s, NULL, threads, out);
+  free(qgate), free(k), free(v), free(att);
+  return rc;
 }
 
 /* The DeltaNet recurrence alone (model.rs:322-355): qkv[s][3 nh hk] after

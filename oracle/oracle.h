@@ -47,6 +47,8 @@ void or_softmax(const float* x, int n, float* p);
 int or_ot_full(const float* x, int s, int d, int H, int KV, int hd, int rot, float theta, const float* wq,
                const float* wk, const float* wv, const float* wo, const float* qn, const float* kn, int threads,
                float* out);
+int or_ot_full_core(const float* qgate, const float* k, const float* v, const float* qn, const float* kn, int s,
+                    int H, int KV, int hd, int rot, float theta, float* out);
 int or_ot_delta_core(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
                      int nh, int hk, float* out);
 int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,

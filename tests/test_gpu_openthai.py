@@ -41,3 +41,23 @@ def test_gated_delta_rejects_bad_head_dim():
     with pytest.raises(LayaError) as e:
         engine.gated_delta(qkv, a, b, dt, alog, 2, 32)
     assert e.value.code == E_INVALID
+
+
+@pytest.mark.parametrize("s,H,KV,hd,rot", [(1, 8, 2, 256, 64), (23, 8, 2, 256, 64), (130, 8, 2, 256, 64),
+                                           (40, 4, 4, 128, 128), (17, 6, 2, 64, 16)])
+def test_gated_attention_matches_oracle(s, H, KV, hd, rot):
+    rng = np.random.default_rng(s + hd)
+    qgate = rng.normal(0, 1, (s, H * 2 * hd))
+    k = rng.normal(0, 1, (s, KV * hd))
+    v = rng.normal(0, 1, (s, KV * hd))
+    qn, kn = rng.normal(0, 0.1, hd), rng.normal(0, 0.1, hd)
+    got = engine.gated_attention(qgate, k, v, qn, kn, H, KV, hd, rot, 1e7)
+    want = oracle.ot_full_core(qgate, k, v, qn, kn, H, KV, hd, rot, 1e7)
+    assert np.allclose(got, want, atol=1e-4, rtol=1e-3), np.abs(got - want).max()
+
+
+def test_gated_attention_rejects_bad_shapes():
+    z = np.zeros((2, 512), np.float32)
+    with pytest.raises(LayaError) as e:
+        engine.gated_attention(z, z, z, np.zeros(256), np.zeros(256), H=3, KV=2, hd=256, rot=64, theta=1e7)
+    assert e.value.code == E_INVALID
