@@ -140,6 +140,15 @@ int laya_forward(laya_model* m, const int32_t* ids, int n, const int32_t* read, 
  * reference uses 128).  Host buffers. */
 int laya_gated_delta(int device, const float* qkv, const float* a, const float* b, const float* dt,
                      const float* alog, int s, int nh, int hk, float* out);
+/* OpenThai's whole DeltaNet mixer after its projections (Delta::run,
+ * src/models/openthai/model.rs:309-360) for one sequence: raw = s rows of
+ * in_proj_qkv output (3 * nh * hk), z = s rows of in_proj_z (nh * hk), a / b
+ * = s rows of nh, conv = the depthwise kernel [3 * nh * hk][4], dt, alog [nh],
+ * normw [hk]; out = s rows of nh * hk: causal convolution + SiLU, the
+ * recurrence, per-head RMSNorm and x SiLU(z), before out_proj.  Host buffers. */
+int laya_gated_delta_mixer(int device, const float* raw, const float* z, const float* a, const float* b,
+                           const float* conv, const float* dt, const float* alog, const float* normw, int s, int nh,
+                           int hk, float* out);
 /* The gated full attention of OpenThai's attention layers after their
  * projections (Full::run, src/models/openthai/model.rs:248-296) for one
  * sequence of s tokens: qgate = s rows of H heads x [query hd | gate hd],

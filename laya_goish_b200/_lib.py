@@ -96,6 +96,7 @@ def lib() -> ctypes.CDLL:
     L.laya_matrix_apply.argtypes = [I, ctypes.c_uint32, P, I, I, P, I, P, P]
     L.laya_gated_delta.argtypes = [I, P, P, P, P, P, I, I, I, P]
     L.laya_gated_attention.argtypes = [I, P, P, P, P, P, I, I, I, I, I, ctypes.c_float, P]
+    L.laya_gated_delta_mixer.argtypes = [I, P, P, P, P, P, P, P, P, I, I, I, P]
     L.laya_forward.argtypes = [P, P, I, P, I, P]
     L.laya_tensor_f32.argtypes = [P, ctypes.c_char_p, P, SZ]
     L.laya_matrix_apply_static.argtypes = [ctypes.c_uint32, P, I, I, P, I, P, P, P]

@@ -294,6 +294,37 @@ int laya_gated_delta(int device, const float* qkv, const float* a, const float* 
   return 0;
 }
 
+int laya_gated_delta_mixer(int device, const float* raw, const float* z, const float* a, const float* b,
+                           const float* conv, const float* dt, const float* alog, const float* normw, int s, int nh,
+                           int hk, float* out) {
+  if (!raw || !z || !a || !b || !conv || !dt || !alog || !normw || !out || s < 0 || nh < 1 || (hk != 64 && hk != 128))
+    return fail(LAYA_E_INVALID, "invalid DeltaNet mixer arguments (hk must be 64 or 128)");
+  if (s == 0) return 0;
+  LAYA_CK(cudaSetDevice(device));
+  const size_t w = (size_t)nh * hk, nr = (size_t)s * 3 * w, nz = (size_t)s * w, nab = (size_t)s * nh;
+  DevBuf draw, dz, da, db, dconv, dpar, dsc, dout;
+  int rc;
+  if ((rc = draw.ensure(nr * 4)) || (rc = dz.ensure(nz * 4)) || (rc = da.ensure(nab * 4)) ||
+      (rc = db.ensure(nab * 4)) || (rc = dconv.ensure(3 * w * 4 * 4)) || (rc = dpar.ensure(((size_t)2 * nh + hk) * 4)) ||
+      (rc = dsc.ensure(nr * 4)) || (rc = dout.ensure(nz * 4)))
+    return rc;
+  float* p = dpar.as<float>();
+  cudaError_t e = cudaMemcpy(draw.p, raw, nr * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dz.p, z, nz * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(da.p, a, nab * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(db.p, b, nab * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dconv.p, conv, 3 * w * 4 * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(p, dt, (size_t)nh * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(p + nh, alog, (size_t)nh * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(p + 2 * nh, normw, (size_t)hk * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = gated_delta_mixer(draw.as<float>(), dz.as<float>(), da.as<float>(), db.as<float>(), dconv.as<float>(), p,
+                          p + nh, p + 2 * nh, s, nh, hk, dsc.as<float>(), dout.as<float>(), 0);
+  if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, nz * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "laya_gated_delta_mixer");
+  return 0;
+}
+
 int laya_gated_attention(int device, const float* qgate, const float* k, const float* v, const float* qn,
                          const float* kn, int s, int H, int KV, int hd, int rot, float theta, float* out) {
   if (!qgate || !k || !v || !qn || !kn || !out || s < 0 || H < 1 || KV < 1 || H % KV ||

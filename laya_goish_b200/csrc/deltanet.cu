@@ -77,6 +77,64 @@ __global__ void __launch_bounds__(HK) gated_delta_kernel(const float* __restrict
   }
 }
 
+// Causal depthwise convolution of width 4 over the token axis, then SiLU
+// (model.rs:309-320): out[i][c] = silu(sum_j raw[i + j - 3][c] conv[c][j]),
+// terms before token 0 left out, summed in j order.
+__global__ void conv_silu_kernel(const float* __restrict__ raw, const float* __restrict__ conv, int s, int C,
+                                 float* __restrict__ out) {
+  const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (size_t)s * C) return;
+  const int i = (int)(e / C), c = (int)(e % C);
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; j++)
+    if (i + j >= 3) acc += raw[(size_t)(i + j - 3) * C + c] * conv[(size_t)c * 4 + j];
+  out[e] = acc / (1.f + expf(-acc));
+}
+
+// Per-head RMSNorm (weight offset 0, eps 1e-6) of the recurrence output,
+// then x SiLU(z) (model.rs:356-360); one warp per (token, head) row.
+template <int HK>
+__global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict__ z, const float* __restrict__ w,
+                                 int rows) {
+  constexpr int PL = HK / 32;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (gw >= rows) return;
+  float* r = o + (size_t)gw * HK;
+  const float* zr = z + (size_t)gw * HK;
+  float v[PL], ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < PL; u++) {
+    v[u] = r[lane + 32 * u];
+    ss += v[u] * v[u];
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float scale = 1.f / sqrtf(ss / (float)HK + 1e-6f);
+#pragma unroll
+  for (int u = 0; u < PL; u++) {
+    const float zz = zr[lane + 32 * u];
+    r[lane + 32 * u] = v[u] * scale * w[lane + 32 * u] * (zz / (1.f + expf(-zz)));
+  }
+}
+
+cudaError_t gated_delta_mixer(const float* raw, const float* z, const float* a, const float* b, const float* conv,
+                              const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
+                              float* qkv_scratch, float* out, cudaStream_t st) {
+  if (s <= 0) return cudaSuccess;
+  if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
+  const size_t C = (size_t)3 * nh * hk, n = (size_t)s * C;
+  conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, conv, s, (int)C, qkv_scratch);
+  cudaError_t e = gated_delta(qkv_scratch, a, b, dt, alog, s, nh, hk, out, st);
+  if (e != cudaSuccess) return e;
+  const int rows = s * nh;
+  if (hk == 128)
+    norm_gate_kernel<128><<<(rows + 7) / 8, 256, 0, st>>>(out, z, normw, rows);
+  else
+    norm_gate_kernel<64><<<(rows + 7) / 8, 256, 0, st>>>(out, z, normw, rows);
+  return cudaGetLastError();
+}
+
 cudaError_t gated_delta(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
                         int nh, int hk, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;

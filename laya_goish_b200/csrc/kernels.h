@@ -56,6 +56,13 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
 // (hk 64 or 128).  All device pointers.
 cudaError_t gated_delta(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
                         int nh, int hk, float* out, cudaStream_t st);
+// The DeltaNet mixer after its projections (deltanet.cu): raw [s][3 nh hk]
+// from in_proj_qkv, z [s][nh hk], a / b [s][nh], conv [3 nh hk][4], dt /
+// A_log [nh], norm weight [hk] -> out [s][nh hk] before out_proj;
+// qkv_scratch holds s * 3 * nh * hk floats.
+cudaError_t gated_delta_mixer(const float* raw, const float* z, const float* a, const float* b, const float* conv,
+                              const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
+                              float* qkv_scratch, float* out, cudaStream_t st);
 // Gated full attention after the projections (gated_attn.cu): qgate
 // [s][H][query hd | gate hd], k / v [s][KV][hd], q / k norm weights [hd] ->
 // out [s][H][hd]; scratch holds s * (H + KV) * hd floats.  hd 64/128/256.

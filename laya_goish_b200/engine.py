@@ -227,3 +227,18 @@ def gated_attention(qgate, k, v, qn, kn, H: int, KV: int, hd: int, rot: int, the
                                           *[a.ctypes.data_as(ctypes.c_void_p) for a in arrs], s, H, KV, hd, rot,
                                           theta, out.ctypes.data_as(ctypes.c_void_p)))
     return out
+
+
+def gated_delta_mixer(raw, z, a, b, conv, dt, alog, normw, nh: int, hk: int, device: int = 0) -> np.ndarray:
+    """OpenThai's DeltaNet mixer after its projections on the GPU (Delta::run,
+    src/models/openthai/model.rs:309-360): raw [s][3 nh hk], z [s][nh hk],
+    a / b [s][nh], conv [3 nh hk][4], dt / A_log [nh], norm [hk] -> [s][nh hk]
+    before out_proj."""
+    r = np.ascontiguousarray(np.asarray(raw, np.float32))
+    s = r.shape[0]
+    arrs = [np.ascontiguousarray(np.asarray(v, np.float32)) for v in (z, a, b, conv, dt, alog, normw)]
+    out = np.zeros((s, nh * hk), np.float32)
+    check(_lib.lib().laya_gated_delta_mixer(device, r.ctypes.data_as(ctypes.c_void_p),
+                                            *[v.ctypes.data_as(ctypes.c_void_p) for v in arrs], s, nh, hk,
+                                            out.ctypes.data_as(ctypes.c_void_p)))
+    return out

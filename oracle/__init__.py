@@ -64,6 +64,7 @@ def lib() -> ctypes.CDLL:
         L.or_ot_delta.argtypes = [P, i, i, i, i, P, P, P, P, P, P, P, P, P, i, P]
         L.or_ot_delta_core.argtypes = [P, P, P, P, P, i, i, i, P]
         L.or_ot_full_core.argtypes = [P, P, P, P, P, i, i, i, i, i, ctypes.c_float, P]
+        L.or_ot_delta_mid.argtypes = [P, P, P, P, P, P, P, P, i, i, i, P]
         L.or_head.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
         L.or_decide.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(Question), ctypes.POINTER(Answer)]
         _lib = L
@@ -233,4 +234,17 @@ def ot_full_core(qgate, k, v, qn, kn, H, KV, hd, rot, theta) -> np.ndarray:
                                out.ctypes.data)
     if rc:
         raise ValueError(f"or_ot_full_core failed ({rc})")
+    return out
+
+
+def ot_delta_mid(raw, z, a, b, conv, dt, alog, normw, nh, hk) -> np.ndarray:
+    """The DeltaNet mixer after its projections: raw [s][3 nh hk], z [s][nh hk],
+    a / b [s][nh] -> [s][nh hk] before out_proj."""
+    raw = _f32(raw)
+    s = raw.shape[0]
+    args = [_f32(v) for v in (z, a, b, conv, dt, alog, normw)]
+    out = np.zeros((s, nh * hk), np.float32)
+    rc = lib().or_ot_delta_mid(raw.ctypes.data, *[v.ctypes.data for v in args], s, nh, hk, out.ctypes.data)
+    if rc:
+        raise ValueError(f"or_ot_delta_mid failed ({rc})")
     return out

@@ -154,22 +154,16 @@ int or_ot_delta_core(const float* qkv, const float* a, const float* b, const flo
   return 0;
 }
 
-int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,
-                const float* wb, const float* wo, const float* conv, const float* dt, const float* alog,
-                const float* normw, int threads, float* out) {
+/* Delta::run after its projections (model.rs:309-360): raw [s][3w] from
+ * in_proj_qkv, z [s][w], a / b [s][nh] -> out [s][w] (w = nh hk) before
+ * out_proj: causal width-4 convolution + SiLU, the recurrence, per-head
+ * RMSNorm (offset 0) and x SiLU(z). */
+int or_ot_delta_mid(const float* raw, const float* z, const float* a, const float* b, const float* conv,
+                    const float* dt, const float* alog, const float* normw, int s, int nh, int hk, float* o) {
   if (s < 1 || nh < 1 || hk < 1) return -1;
   const int w = nh * hk, C = 3 * w;
-  float* raw = malloc(sizeof(float) * (size_t)s * C);
   float* qkv = malloc(sizeof(float) * (size_t)s * C);
-  float* z = malloc(sizeof(float) * (size_t)s * w);
-  float* a = malloc(sizeof(float) * (size_t)s * nh);
-  float* b = malloc(sizeof(float) * (size_t)s * nh);
-  float* o = calloc((size_t)s * w, sizeof(float));
-  if (!raw || !qkv || !z || !a || !b || !o) return -2;
-  or_matrix_apply(wqkv, C, d, x, s, NULL, threads, raw);
-  or_matrix_apply(wz, w, d, x, s, NULL, threads, z);
-  or_matrix_apply(wa, nh, d, x, s, NULL, threads, a);
-  or_matrix_apply(wb, nh, d, x, s, NULL, threads, b);
+  if (!qkv) return -2;
   /* causal depthwise conv (width 4) + SiLU */
   for (int i = 0; i < s; i++)
     for (int c = 0; c < C; c++) {
@@ -178,10 +172,31 @@ int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv,
         if (i + j >= 3) acc += raw[(size_t)(i + j - 3) * C + c] * conv[(size_t)c * 4 + j];
       qkv[(size_t)i * C + c] = ot_silu(acc);
     }
-  or_ot_delta_core(qkv, a, b, dt, alog, s, nh, hk, o);
+  int rc = or_ot_delta_core(qkv, a, b, dt, alog, s, nh, hk, o);
+  free(qkv);
+  if (rc) return rc;
   ot_rms(o, normw, hk, s * nh, 0.f);
   for (size_t e = 0; e < (size_t)s * w; e++) o[e] *= ot_silu(z[e]);
-  or_matrix_apply(wo, d, w, o, s, NULL, threads, out);
-  free(raw), free(qkv), free(z), free(a), free(b), free(o);
   return 0;
+}
+
+int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,
+                const float* wb, const float* wo, const float* conv, const float* dt, const float* alog,
+                const float* normw, int threads, float* out) {
+  if (s < 1 || nh < 1 || hk < 1) return -1;
+  const int w = nh * hk, C = 3 * w;
+  float* raw = malloc(sizeof(float) * (size_t)s * C);
+  float* z = malloc(sizeof(float) * (size_t)s * w);
+  float* a = malloc(sizeof(float) * (size_t)s * nh);
+  float* b = malloc(sizeof(float) * (size_t)s * nh);
+  float* o = malloc(sizeof(float) * (size_t)s * w);
+  if (!raw || !z || !a || !b || !o) return -2;
+  or_matrix_apply(wqkv, C, d, x, s, NULL, threads, raw);
+  or_matrix_apply(wz, w, d, x, s, NULL, threads, z);
+  or_matrix_apply(wa, nh, d, x, s, NULL, threads, a);
+  or_matrix_apply(wb, nh, d, x, s, NULL, threads, b);
+  int rc = or_ot_delta_mid(raw, z, a, b, conv, dt, alog, normw, s, nh, hk, o);
+  if (!rc) or_matrix_apply(wo, d, w, o, s, NULL, threads, out);
+  free(raw), free(z), free(a), free(b), free(o);
+  return rc;
 }

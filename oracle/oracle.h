@@ -51,6 +51,8 @@ int or_ot_full_core(const float* qgate, const float* k, const float* v, const fl
                     int H, int KV, int hd, int rot, float theta, float* out);
 int or_ot_delta_core(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
                      int nh, int hk, float* out);
+int or_ot_delta_mid(const float* raw, const float* z, const float* a, const float* b, const float* conv,
+                    const float* dt, const float* alog, const float* normw, int s, int nh, int hk, float* out);
 int or_ot_delta(const float* x, int s, int d, int nh, int hk, const float* wqkv, const float* wz, const float* wa,
                 const float* wb, const float* wo, const float* conv, const float* dt, const float* alog,
                 const float* normw, int threads, float* out);

@@ -61,3 +61,17 @@ def test_gated_attention_rejects_bad_shapes():
     with pytest.raises(LayaError) as e:
         engine.gated_attention(z, z, z, np.zeros(256), np.zeros(256), H=3, KV=2, hd=256, rot=64, theta=1e7)
     assert e.value.code == E_INVALID
+
+
+@pytest.mark.parametrize("s,nh,hk", [(3, 2, 128), (90, 16, 128), (33, 4, 64)])
+def test_gated_delta_mixer_matches_oracle(s, nh, hk):
+    rng = np.random.default_rng(1000 + s)
+    w = nh * hk
+    raw = rng.normal(0, 1, (s, 3 * w))
+    z = rng.normal(0, 1, (s, w))
+    a, b = rng.normal(0, 1, (s, nh)), rng.normal(0, 1, (s, nh))
+    conv = rng.normal(0, 0.5, (3 * w, 4))
+    dt, alog, normw = rng.normal(0, 0.5, nh), rng.normal(-1, 0.5, nh), rng.normal(1, 0.1, hk)
+    got = engine.gated_delta_mixer(raw, z, a, b, conv, dt, alog, normw, nh, hk)
+    want = oracle.ot_delta_mid(raw, z, a, b, conv, dt, alog, normw, nh, hk)
+    assert np.allclose(got, want, atol=1e-4, rtol=1e-3), np.abs(got - want).max()
