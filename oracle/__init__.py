@@ -248,3 +248,47 @@ def ot_delta_mid(raw, z, a, b, conv, dt, alog, normw, nh, hk) -> np.ndarray:
     if rc:
         raise ValueError(f"or_ot_delta_mid failed ({rc})")
     return out
+
+
+def _rms(x: np.ndarray, w: np.ndarray, off: float) -> np.ndarray:
+    """rms (src/models/openthai/model.rs:84-94) in F32: rows of len(w), eps 1e-6."""
+    d = w.shape[0]
+    r = x.reshape(-1, d).astype(np.float32)
+    dot = np.add.accumulate(r * r, axis=1, dtype=np.float32)[:, -1]  # sequential, as tensor::dot
+    scale = (np.float32(1) / np.sqrt(dot / np.float32(d) + np.float32(1e-6))).astype(np.float32)
+    return (r * scale[:, None] * (np.float32(off) + w.astype(np.float32))).reshape(x.shape).astype(np.float32)
+
+
+def ot_forward(m: dict, ids, positions, threads: int = 4) -> np.ndarray:
+    """OpenThai Model::forward (src/models/openthai/model.rs:192-241) on
+    weights given as a dict of F32 arrays under the OpenThai GGUF tensor
+    names, composed from the C mixers and Matrix::apply:
+    embedding rows; per layer x += mixer(rms(x, n1, 1)), x += down(silu(gate
+    h) * up h) with h = rms(x, n2, 1); the slot head (+ bias) on
+    rms(x[positions], norm, 1).  Returns [len(positions)][slots]."""
+    c = m["config"]
+    H, KV, hd, rot, theta = c["heads"], c["kv_heads"], c["head_dim"], c["rot"], c["theta"]
+    nh, hk = c["lin_heads"], c["lin_dim"]
+    x = m["model.embed_tokens.weight"][np.asarray(ids)].astype(np.float32)
+    for i, kind in enumerate(c["layer_types"]):
+        p = f"model.layers.{i}"
+        h = _rms(x, m[f"{p}.input_layernorm.weight"], 1.0)
+        if kind == "full_attention":
+            y = ot_full(h, m[f"{p}.self_attn.q_proj.weight"], m[f"{p}.self_attn.k_proj.weight"],
+                        m[f"{p}.self_attn.v_proj.weight"], m[f"{p}.self_attn.o_proj.weight"],
+                        m[f"{p}.self_attn.q_norm.weight"], m[f"{p}.self_attn.k_norm.weight"], H, KV, hd, rot, theta,
+                        threads)
+        else:
+            y = ot_delta(h, m[f"{p}.linear_attn.in_proj_qkv.weight"], m[f"{p}.linear_attn.in_proj_z.weight"],
+                         m[f"{p}.linear_attn.in_proj_a.weight"], m[f"{p}.linear_attn.in_proj_b.weight"],
+                         m[f"{p}.linear_attn.out_proj.weight"], m[f"{p}.linear_attn.conv1d.weight"],
+                         m[f"{p}.linear_attn.dt_bias"], m[f"{p}.linear_attn.A_log"],
+                         m[f"{p}.linear_attn.norm.weight"], nh, hk, threads)
+        x = (x + y).astype(np.float32)
+        h = _rms(x, m[f"{p}.post_attention_layernorm.weight"], 1.0)
+        g = matrix_apply(m[f"{p}.mlp.gate_proj.weight"], h, threads=threads)
+        u = matrix_apply(m[f"{p}.mlp.up_proj.weight"], h, threads=threads)
+        act = (g * (np.float32(1) / (np.float32(1) + np.exp(-g))) * u).astype(np.float32)
+        x = (x + matrix_apply(m[f"{p}.mlp.down_proj.weight"], act, threads=threads)).astype(np.float32)
+    ans = _rms(x[np.asarray(positions)], m["model.norm.weight"], 1.0)
+    return matrix_apply(m["slot_head.weight"], ans, m["slot_head.bias"], threads=threads)

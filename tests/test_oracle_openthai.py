@@ -1,9 +1,9 @@
-"""The oracle's OpenThai sequence mixers (oracle/openthai.c) against an
-independent float64 NumPy restatement of the same equations
-(src/models/openthai/model.rs:243-363), at the reference's head layouts on
-small widths, plus the properties the equations imply (causality, the gate
-at zero, the decay limit).  Parity with the reference itself is unpinned:
-its goldens need the real OpenThai weights."""
+"""The oracle's OpenThai sequence mixers (oracle/openthai.c) and the forward
+composed from them (oracle.ot_forward) against an independent float64 NumPy
+restatement of the same equations (src/models/openthai/model.rs:192-363),
+at the reference's head layouts on small widths, plus causality.  Parity
+with the reference itself is unpinned: its goldens need the real OpenThai
+weights."""
 import numpy as np
 import pytest
 
@@ -115,3 +115,72 @@ def test_bad_shapes_rejected():
     z = np.zeros(64, np.float32)
     with pytest.raises(ValueError):
         oracle.ot_full(x, z, z, z, z, z, z, H=3, KV=2, hd=4, rot=4, theta=1e7)  # H % KV != 0
+
+
+def ref_forward(m, ids, positions):
+    c = m["config"]
+    x = m["model.embed_tokens.weight"][np.asarray(ids)].astype(np.float64)
+    for i, kind in enumerate(c["layer_types"]):
+        p = f"model.layers.{i}"
+        h = rms(x, m[f"{p}.input_layernorm.weight"], 1).reshape(x.shape)
+        if kind == "full_attention":
+            y = ref_full(h, m[f"{p}.self_attn.q_proj.weight"], m[f"{p}.self_attn.k_proj.weight"],
+                         m[f"{p}.self_attn.v_proj.weight"], m[f"{p}.self_attn.o_proj.weight"],
+                         m[f"{p}.self_attn.q_norm.weight"], m[f"{p}.self_attn.k_norm.weight"], c["heads"],
+                         c["kv_heads"], c["head_dim"], c["rot"], c["theta"])
+        else:
+            y = ref_delta(h, m[f"{p}.linear_attn.in_proj_qkv.weight"], m[f"{p}.linear_attn.in_proj_z.weight"],
+                          m[f"{p}.linear_attn.in_proj_a.weight"], m[f"{p}.linear_attn.in_proj_b.weight"],
+                          m[f"{p}.linear_attn.out_proj.weight"], m[f"{p}.linear_attn.conv1d.weight"],
+                          m[f"{p}.linear_attn.dt_bias"], m[f"{p}.linear_attn.A_log"],
+                          m[f"{p}.linear_attn.norm.weight"], c["lin_heads"], c["lin_dim"])
+        x = x + y
+        h = rms(x, m[f"{p}.post_attention_layernorm.weight"], 1).reshape(x.shape)
+        g, u = h @ m[f"{p}.mlp.gate_proj.weight"].T, h @ m[f"{p}.mlp.up_proj.weight"].T
+        x = x + (g * sigmoid(g) * u) @ m[f"{p}.mlp.down_proj.weight"].T
+    ans = rms(x[np.asarray(positions)], m["model.norm.weight"], 1).reshape(len(positions), -1)
+    return ans @ m["slot_head.weight"].T + m["slot_head.bias"]
+
+
+def tiny_openthai(rng):
+    d, ffn, V, slots = 48, 96, 300, 16
+    c = {"heads": 4, "kv_heads": 2, "head_dim": 32, "rot": 8, "theta": 1e7, "lin_heads": 2, "lin_dim": 16,
+         "layer_types": ["linear_attention", "linear_attention", "full_attention", "linear_attention"]}
+    H, KV, hd, nh, hk = c["heads"], c["kv_heads"], c["head_dim"], c["lin_heads"], c["lin_dim"]
+    w = nh * hk
+    n = lambda *shape, sd=0.05: rng.normal(0, sd, shape).astype(np.float32)  # noqa: E731
+    m = {"config": c, "model.embed_tokens.weight": n(V, d, sd=1.0), "model.norm.weight": n(d),
+         "slot_head.weight": n(slots, d, sd=0.2), "slot_head.bias": n(slots)}
+    for i, kind in enumerate(c["layer_types"]):
+        p = f"model.layers.{i}"
+        m.update({f"{p}.input_layernorm.weight": n(d), f"{p}.post_attention_layernorm.weight": n(d),
+                  f"{p}.mlp.gate_proj.weight": n(ffn, d, sd=0.1), f"{p}.mlp.up_proj.weight": n(ffn, d, sd=0.1),
+                  f"{p}.mlp.down_proj.weight": n(d, ffn, sd=0.1)})
+        if kind == "full_attention":
+            m.update({f"{p}.self_attn.q_proj.weight": n(2 * H * hd, d, sd=0.1),
+                      f"{p}.self_attn.k_proj.weight": n(KV * hd, d, sd=0.1),
+                      f"{p}.self_attn.v_proj.weight": n(KV * hd, d, sd=0.1),
+                      f"{p}.self_attn.o_proj.weight": n(d, H * hd, sd=0.1),
+                      f"{p}.self_attn.q_norm.weight": n(hd), f"{p}.self_attn.k_norm.weight": n(hd)})
+        else:
+            m.update({f"{p}.linear_attn.in_proj_qkv.weight": n(3 * w, d, sd=0.2),
+                      f"{p}.linear_attn.in_proj_z.weight": n(w, d, sd=0.2),
+                      f"{p}.linear_attn.in_proj_a.weight": n(nh, d, sd=0.3),
+                      f"{p}.linear_attn.in_proj_b.weight": n(nh, d, sd=0.3),
+                      f"{p}.linear_attn.out_proj.weight": n(d, w, sd=0.1),
+                      f"{p}.linear_attn.conv1d.weight": n(3 * w, 4, sd=0.5),
+                      f"{p}.linear_attn.dt_bias": n(nh, sd=0.5), f"{p}.linear_attn.A_log": n(nh, sd=0.3) - 1,
+                      f"{p}.linear_attn.norm.weight": 1 + n(hk)})
+    return m
+
+
+@pytest.mark.parametrize("s", [1, 9, 40])
+def test_openthai_forward_matches_float64(s):
+    rng = np.random.default_rng(300 + s)
+    m = tiny_openthai(rng)
+    ids = rng.integers(0, 300, size=s)
+    pos = sorted({0, s // 2, s - 1})
+    got = oracle.ot_forward(m, ids, pos)
+    want = ref_forward(m, ids, pos)
+    assert got.shape == (len(pos), 16)
+    assert np.allclose(got, want, atol=2e-3, rtol=2e-3), np.abs(got - want).max()
