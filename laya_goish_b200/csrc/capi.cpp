@@ -4,6 +4,7 @@
 #include <cstring>
 #include <memory>
 #include <thread>
+#include <vector>
 
 #include "engine.h"
 #include "gemm.h"
@@ -269,6 +270,14 @@ int laya_dequantize(int device, uint32_t kind, const uint8_t* blocks, size_t nby
   return 0;
 }
 
+// Frees a call's temporary device buffers on every return path.
+struct ReleaseOnExit {
+  std::vector<DevBuf*> bufs;
+  ~ReleaseOnExit() {
+    for (DevBuf* b : bufs) b->release();
+  }
+};
+
 int laya_gated_delta(int device, const float* qkv, const float* a, const float* b, const float* dt,
                      const float* alog, int s, int nh, int hk, float* out) {
   if (!qkv || !a || !b || !dt || !alog || !out || s < 0 || nh < 1 || (hk != 64 && hk != 128))
@@ -277,6 +286,7 @@ int laya_gated_delta(int device, const float* qkv, const float* a, const float* 
   LAYA_CK(cudaSetDevice(device));
   const size_t w = (size_t)nh * hk, nq = (size_t)s * 3 * w, nab = (size_t)s * nh, no = (size_t)s * w;
   DevBuf dq, da, db, dp, dout;
+  ReleaseOnExit guard{{&dq, &da, &db, &dp, &dout}};
   int rc;
   if ((rc = dq.ensure(nq * 4)) || (rc = da.ensure(nab * 4)) || (rc = db.ensure(nab * 4)) ||
       (rc = dp.ensure((size_t)2 * nh * 4)) || (rc = dout.ensure(no * 4)))
@@ -303,6 +313,7 @@ int laya_gated_delta_mixer(int device, const float* raw, const float* z, const f
   LAYA_CK(cudaSetDevice(device));
   const size_t w = (size_t)nh * hk, nr = (size_t)s * 3 * w, nz = (size_t)s * w, nab = (size_t)s * nh;
   DevBuf draw, dz, da, db, dconv, dpar, dsc, dout;
+  ReleaseOnExit guard{{&draw, &dz, &da, &db, &dconv, &dpar, &dsc, &dout}};
   int rc;
   if ((rc = draw.ensure(nr * 4)) || (rc = dz.ensure(nz * 4)) || (rc = da.ensure(nab * 4)) ||
       (rc = db.ensure(nab * 4)) || (rc = dconv.ensure(3 * w * 4 * 4)) || (rc = dpar.ensure(((size_t)2 * nh + hk) * 4)) ||
@@ -334,6 +345,7 @@ int laya_gated_attention(int device, const float* qgate, const float* k, const f
   LAYA_CK(cudaSetDevice(device));
   const size_t nq = (size_t)s * H * 2 * hd, nk = (size_t)s * KV * hd, no = (size_t)s * H * hd;
   DevBuf dq, dk, dv, dn, dsc, dout;
+  ReleaseOnExit guard{{&dq, &dk, &dv, &dn, &dsc, &dout}};
   int rc;
   if ((rc = dq.ensure(nq * 4)) || (rc = dk.ensure(nk * 4)) || (rc = dv.ensure(nk * 4)) ||
       (rc = dn.ensure((size_t)2 * hd * 4)) || (rc = dsc.ensure((no + nk) * 4)) || (rc = dout.ensure(no * 4)))
