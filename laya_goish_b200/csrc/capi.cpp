@@ -251,6 +251,14 @@ int laya_tensor_f32(laya_model* h, const char* name, float* out, size_t max_elem
   return 0;
 }
 
+// Frees a call's temporary device buffers on every return path.
+struct ReleaseOnExit {
+  std::vector<DevBuf*> bufs;
+  ~ReleaseOnExit() {
+    for (DevBuf* b : bufs) b->release();
+  }
+};
+
 int laya_dequantize(int device, uint32_t kind, const uint8_t* blocks, size_t nbytes, float* out) {
   int block, size;
   if (!ggml_layout(kind, &block, &size)) return fail(LAYA_E_INVALID, "unsupported GGML tensor type");
@@ -259,24 +267,15 @@ int laya_dequantize(int device, uint32_t kind, const uint8_t* blocks, size_t nby
   if (!nb) return 0;
   LAYA_CK(cudaSetDevice(device));
   DevBuf din, dout;
+  ReleaseOnExit guard{{&din, &dout}};
   int rc;
   if ((rc = din.ensure(nb * size)) || (rc = dout.ensure(nb * block * 4))) return rc;
   cudaError_t e = cudaMemcpy(din.p, blocks, nb * size, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = dequant_raw((int)kind, din.as<uint8_t>(), nb, dout.as<float>(), 0);
   if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, nb * block * 4, cudaMemcpyDeviceToHost);
-  din.release();
-  dout.release();
   if (e != cudaSuccess) return cuda_fail(e, "laya_dequantize");
   return 0;
 }
-
-// Frees a call's temporary device buffers on every return path.
-struct ReleaseOnExit {
-  std::vector<DevBuf*> bufs;
-  ~ReleaseOnExit() {
-    for (DevBuf* b : bufs) b->release();
-  }
-};
 
 int laya_gated_delta(int device, const float* qkv, const float* a, const float* b, const float* dt,
                      const float* alog, int s, int nh, int hk, float* out) {
@@ -378,6 +377,7 @@ int laya_matrix_apply(int device, uint32_t kind, const uint8_t* w, int rows, int
   const int ld = (cols + 7) / 8 * 8;
   const size_t wbytes = (size_t)rows * cols / block * size;
   DevBuf dw, dwf, dw16, dx, dx16, db, dy, derr;
+  ReleaseOnExit guard{{&dw, &dwf, &dw16, &dx, &dx16, &db, &dy, &derr}};
   int rc;
   if ((rc = dw.ensure(wbytes)) || (rc = dwf.ensure((size_t)rows * cols * 4)) ||
       (rc = dw16.ensure((size_t)rows * ld * 2)) || (rc = dx.ensure((size_t)m * cols * 4)) ||
@@ -406,7 +406,6 @@ int laya_matrix_apply(int device, uint32_t kind, const uint8_t* w, int rows, int
   if (e == cudaSuccess) e = cudaMemcpy(out, dy.p, (size_t)m * rows * 4, cudaMemcpyDeviceToHost);
   unsigned err = 0;
   if (e == cudaSuccess) e = cudaMemcpy(&err, derr.p, 4, cudaMemcpyDeviceToHost);
-  for (DevBuf* b : {&dw, &dwf, &dw16, &dx, &dx16, &db, &dy, &derr}) b->release();
   if (e != cudaSuccess) return cuda_fail(e, "laya_matrix_apply");
   if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");
   return 0;
