@@ -1,0 +1,271 @@
+"""Host side of OpenThai decisions: the request rules, the control-token
+prompt, the option-order permutations and the calibrated slot decoding of
+src/models/openthai/decision.rs, restated for the GPU forward (the layers'
+mixers are `engine.gated_attention` / `engine.gated_delta_mixer`).
+
+A request's questions become text blocks
+
+    <|ts_q|><|ts_{choice|score|noul}|> {instructions}\\n
+    <|ts_opt_{slot}|> {name}[: {description}]\\n      (one per option, in pass order)
+    <|ts_answer|>\\n
+
+after a state block `<|ts_state|> {state}\\n` (decision.rs:169-233); the slot
+head's 256 logits at each block's answer token give, per question, a softmax
+over its k option slots and the abstain slot 255, scaled by the per-kind
+temperature; choice questions are asked in several cyclic option orders and
+the slot probabilities are averaged back onto the options (decision.rs:
+243-391).
+
+Where the reference leaves the exact text to its own JSON writer (numbers in
+non-string states), the standard library's JSON formatting is used; that
+corner is not pinned.
+"""
+from __future__ import annotations
+
+import json
+import math
+
+import numpy as np
+
+KINDS = ("choice", "score", "noul")
+ABSTAIN_SLOT = 255
+SLOTS = 256
+# Unicode White_Space (Rust's str::trim)
+_WS = frozenset([0x9, 0xA, 0xB, 0xC, 0xD, 0x20, 0x85, 0xA0, 0x1680, *range(0x2000, 0x200B), 0x2028, 0x2029,
+                 0x202F, 0x205F, 0x3000])
+
+
+class OpenThaiError(ValueError):
+    pass
+
+
+def trim(s: str) -> str:
+    i, j = 0, len(s)
+    while i < j and ord(s[i]) in _WS:
+        i += 1
+    while j > i and ord(s[j - 1]) in _WS:
+        j -= 1
+    return s[i:j]
+
+
+def clean(s: str) -> str:
+    """Control-token text inside user strings is broken with a zero-width
+    space (decision.rs:17-19)."""
+    return s.replace("<|ts_", "<\u200b|ts_")
+
+
+class Spec:
+    def __init__(self, qid, kind, ins, names, desc):
+        self.id, self.kind, self.ins, self.names, self.desc = qid, kind, ins, names, desc
+
+
+def questions(req: dict) -> list[Spec]:
+    """Request validation (decision.rs:20-109)."""
+    qs = req.get("questions")
+    if not isinstance(qs, dict) or not qs or len(qs) > 256:
+        raise OpenThaiError("questions must contain 1..256 named questions")
+    if not isinstance(req.get("state"), (str, dict, list)):
+        raise OpenThaiError("OpenThai state must be a string, object, or array")
+    out = []
+
+    def text(qid, v):
+        if isinstance(v, str):
+            return v
+        if v is None:
+            return ""
+        raise OpenThaiError(f"{qid}: descriptions must be strings or null")
+
+    for qid, q in qs.items():
+        q = q if isinstance(q, dict) else {}
+        kind = q.get("type")
+        if kind not in KINDS:
+            raise OpenThaiError(f"{qid}: invalid question type")
+        kind = KINDS.index(kind)
+        ins = q.get("instructions")
+        if not isinstance(ins, str):
+            raise OpenThaiError(f"{qid}: instructions must be a string")
+        c = q.get("criteria")
+        names, desc = [], []
+        if kind == 0:
+            if not isinstance(c, dict) or not 1 <= len(c) <= 255:
+                raise OpenThaiError(f"{qid}: choice requires 1..255 options")
+            for name, d in c.items():
+                if not trim(name):
+                    raise OpenThaiError(f"{qid}: option name is empty")
+                names.append(name)
+                desc.append(text(qid, d))
+        elif kind == 1:
+            if not isinstance(c, list) or not 2 <= len(c) <= 10:
+                raise OpenThaiError(f"{qid}: score requires 2..10 levels")
+            for i, d in enumerate(c):
+                if not isinstance(d, str):
+                    raise OpenThaiError(f"{qid}: score descriptions must be strings")
+                names.append(str(i))
+                desc.append(d)
+        else:
+            if not (c is None or isinstance(c, dict)) or (isinstance(c, dict) and any(k not in ("false", "true")
+                                                                                      for k in c)):
+                raise OpenThaiError(f"{qid}: noul criteria keys must be false/true")
+            c = c or {}
+            names = ["no", "yes"]
+            desc = [text(qid, c.get("false")), text(qid, c.get("true"))]
+        out.append(Spec(str(qid), kind, ins, names, desc))
+    oi = req.get("order_invariant")
+    if oi is not None and not isinstance(oi, bool):
+        raise OpenThaiError("order_invariant must be boolean")
+    p = req.get("permutations")
+    if p is not None:
+        if isinstance(p, bool) or not isinstance(p, (int, float)) or not 1 <= p <= 32 or p != int(p):
+            raise OpenThaiError("permutations must be 1..32")
+    return out
+
+
+def orders(k: int, n: int) -> list[list[int]]:
+    """The n cyclic option orders of a k-option question (decision.rs:120-135):
+    offsets j*k/n rounded half to even, deduplicated, ascending."""
+    n = max(1, min(n, k))
+    offs = set()
+    for j in range(n):
+        a = j * k
+        d, rem = a // n, a % n
+        offs.add((d + (1 if rem * 2 > n or (rem * 2 == n and d % 2 == 1) else 0)) % k)
+    return [[(i + off) % k for i in range(k)] for off in sorted(offs)]
+
+
+def permutation_count(req: dict, qs: list[Spec]) -> int:
+    """Passes over the prompt (decision.rs:136-162)."""
+    k = max([len(q.names) for q in qs if q.kind == 0], default=1)
+    p = req.get("permutations")
+    if p is not None:
+        n = int(p)
+    elif req.get("order_invariant") is False:
+        n = 1
+    elif req.get("order_invariant") is True:
+        n = 8
+    else:
+        n = 8 if k >= 11 else 1
+    return max(1, min(n, k))
+
+
+def py_state(v) -> str:
+    """A non-string state as text (decision.rs:110-119): strings JSON-quoted,
+    arrays `[a, b]`, objects `{"k": v}`, other values as JSON."""
+    if isinstance(v, str):
+        return json.dumps(v, ensure_ascii=False)
+    if isinstance(v, list):
+        return "[" + ", ".join(py_state(x) for x in v) + "]"
+    if isinstance(v, dict):
+        return "{" + ", ".join(f"{json.dumps(k, ensure_ascii=False)}: {py_state(x)}" for k, x in v.items()) + "}"
+    return json.dumps(v)
+
+
+class Encoded:
+    def __init__(self, ids, positions, order, truncated):
+        self.ids, self.positions, self.order, self.truncated = ids, positions, order, truncated
+
+
+def encode(tok, req: dict, qs: list[Spec], n: int, npass: int, answer_id: int, max_tokens: int = 4096,
+           max_state: int = 2048) -> Encoded:
+    """Pass `npass` of the prompt (decision.rs:169-233): question blocks in
+    that pass's option order, the state block truncated to its budget
+    (keeping its first token), answer positions at each block's last answer
+    token."""
+    blocks, order = [], []
+    for q in qs:
+        if q.kind == 0:
+            all_ = orders(len(q.names), n)
+            ordq = all_[npass % len(all_)]
+        else:
+            ordq = list(range(len(q.names)))
+        text = f"<|ts_q|><|ts_{KINDS[q.kind]}|> {trim(clean(q.ins))}\n"
+        for slot, i in enumerate(ordq):
+            text += f"<|ts_opt_{slot}|> {trim(clean(q.names[i]))}"
+            if q.desc[i]:
+                text += f": {trim(clean(q.desc[i]))}"
+            text += "\n"
+        text += "<|ts_answer|>\n"
+        blocks.append(tok.encode(text))
+        order.append(ordq)
+    total = sum(len(b) for b in blocks)
+    if total >= max_tokens:
+        raise OpenThaiError("question tokens exceed OpenThai context budget")
+    state = req["state"] if isinstance(req["state"], str) else py_state(req["state"])
+    ids = tok.encode(f"<|ts_state|> {trim(clean(state))}\n")
+    budget = min(max_state, max_tokens - total)
+    truncated = len(ids) > budget
+    if truncated:
+        ids = ids[:1] + ids[len(ids) - (budget - 1):]
+    positions = []
+    for b in blocks:
+        if answer_id not in b:
+            raise OpenThaiError("missing OpenThai answer token")
+        p = len(b) - 1 - b[::-1].index(answer_id)
+        positions.append(len(ids) + p)
+        ids = ids + b
+    return Encoded(ids, positions, order, truncated)
+
+
+def _softmax32(x: np.ndarray) -> np.ndarray:
+    """tensor::softmax (src/tensor.rs:132-140) in F32."""
+    x = x.astype(np.float32)
+    e = np.exp(x - x.max()).astype(np.float32)
+    s = np.float32(0)
+    for v in e:
+        s = np.float32(s + v)
+    return (e / s).astype(np.float32)
+
+
+def decide(qs: list[Spec], passes, temperature) -> dict:
+    """Calibrated slot decoding (decision.rs:264-380).  passes: one (logits,
+    order) per permutation pass, logits [len(qs)][256] slot-head rows at the
+    answer positions, order the pass's option order per question;
+    temperature[kind] from the model.  Returns {question id: answer}."""
+    n = len(passes)
+    probs = [np.zeros(len(q.names), np.float32) for q in qs]
+    abstain = [np.float32(0)] * len(qs)
+    for logits, order in passes:
+        for i, q in enumerate(qs):
+            k = len(q.names)
+            row = np.asarray(logits[i], np.float32)
+            t = np.float32(temperature[q.kind])
+            valid = np.concatenate([row[:k] / t, [row[ABSTAIN_SLOT] / t]]).astype(np.float32)
+            p = _softmax32(valid)
+            ssum = np.float32(0)
+            for v in p[:k]:
+                ssum = np.float32(ssum + v)
+            ssum = max(ssum, np.float32(1e-12))
+            for slot in range(k):
+                probs[i][order[i][slot]] += p[slot] / ssum / np.float32(n)
+            abstain[i] = np.float32(abstain[i] + p[k] / np.float32(n))
+    out = {}
+    for i, q in enumerate(qs):
+        p = probs[i]
+        s = np.float32(0)
+        for v in p:
+            s = np.float32(s + v)
+        p = (p / max(s, np.float32(1e-12))).astype(np.float32)
+        k = len(p)
+        ent = np.float32(0)
+        for v in p:
+            v = max(v, np.float32(1e-12))
+            ent = np.float32(ent + v * np.float32(math.log(v)))
+        ent = -ent
+        conf = 1.0 if k <= 1 else float(min(max(1 - ent / np.float32(math.log(k)), 0.0), 1.0))
+        a = {"type": KINDS[q.kind]}
+        if q.kind == 2:
+            a["noul"] = float(p[1])
+        else:
+            a["probabilities"] = {name: float(v) for name, v in zip(q.names, p)}
+            a["confidence"] = conf
+            if q.kind == 0:
+                best = 0
+                for j in range(1, k):
+                    if p[j] > p[best]:
+                        best = j
+                a["choice"] = q.names[best]
+                a["abstain"] = float(abstain[i])
+            else:
+                a["score"] = float(sum(np.float32(j) * v for j, v in enumerate(p)))
+                a["legend"] = {str(j): (d if d else str(j)) for j, d in enumerate(q.desc)}
+        out[q.id] = a
+    return out
