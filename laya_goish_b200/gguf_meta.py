@@ -76,21 +76,62 @@ def read_metadata(path_or_bytes) -> dict:
                 mv.release()
 
 
-def _parse(buf) -> dict:
+def _parse(buf, tensors: bool = False):
     r = _Reader(buf)
     try:
         if bytes(r.take(4)) != b"GGUF":
             raise GGUFError("not a GGUF file")
         if r.fmt("<I") != 3:
             raise GGUFError("unsupported GGUF version")
-        r.fmt("<Q")  # tensor count
+        n_t = r.fmt("<Q")
         n_kv = r.fmt("<Q")
-        if n_kv > 1 << 20:
-            raise GGUFError("too many GGUF metadata entries")
+        if n_kv > 1 << 20 or n_t > 1 << 20:
+            raise GGUFError("too many GGUF entries")
         out = {}
         for _ in range(n_kv):
             k = r.string()
             out[k] = r.value(r.fmt("<I"))
-        return out
+        if not tensors:
+            return out
+        infos = []
+        for _ in range(n_t):
+            name = r.string()
+            nd = r.fmt("<I")
+            if nd > 4:
+                raise GGUFError("GGUF tensor rank above 4")
+            dims = [r.fmt("<Q") for _ in range(nd)]
+            kind, off = r.fmt("<I"), r.fmt("<Q")
+            infos.append((name, dims, kind, off))
+        align = int(out.get("general.alignment", 32))
+        base = (r.p + align - 1) // align * align
+        return out, infos, base
     finally:
         r.b = None
+
+
+_ELEM = {0: (4, "<f4"), 1: (2, "<f2")}
+
+
+def read_tensors_f32(path: str) -> tuple[dict, dict]:
+    """Metadata and every F32 / F16 tensor of a GGUF file as F32 arrays of
+    shape dims reversed (GGUF dims are innermost first: a matrix [K, N] is N
+    rows of K).  Other tensor types raise GGUFError."""
+    import numpy as np
+
+    with open(path, "rb") as f:
+        data = f.read()
+    meta, infos, base = _parse(memoryview(data), tensors=True)
+    out = {}
+    for name, dims, kind, off in infos:
+        if kind not in _ELEM:
+            raise GGUFError(f"{name}: tensor type {kind} is not F32/F16")
+        size, dt = _ELEM[kind]
+        n = 1
+        for d in dims:
+            n *= d
+        start = base + off
+        if start + n * size > len(data):
+            raise GGUFError(f"{name}: tensor data out of range")
+        a = np.frombuffer(data, dtype=dt, count=n, offset=start).astype(np.float32)
+        out[name] = a.reshape(list(reversed(dims))) if dims else a
+    return meta, out

@@ -269,3 +269,64 @@ def decide(qs: list[Spec], passes, temperature) -> dict:
                 a["legend"] = {str(j): (d if d else str(j)) for j, d in enumerate(q.desc)}
         out[q.id] = a
     return out
+
+
+# Model::new's fixed text_config (src/models/openthai/model.rs:99-125)
+REFERENCE_CONFIG = {"hidden_size": 1024, "intermediate_size": 3584, "num_hidden_layers": 24, "head_dim": 256,
+                    "num_attention_heads": 8, "num_key_value_heads": 2, "linear_conv_kernel_dim": 4,
+                    "linear_key_head_dim": 128, "linear_value_head_dim": 128, "linear_num_key_heads": 16,
+                    "linear_num_value_heads": 16, "vocab_size": 248339}
+
+
+def load_config(meta: dict, strict: bool = True) -> dict:
+    """The model shape from a GGUF's `openthai.config` JSON
+    (src/models/openthai/model.rs:99-135).  strict: the reference's checks
+    (its one supported size, 256 slots with abstain slot 255, answer token
+    248082, eps 1e-6, rope theta 1e7 on a quarter of each head); otherwise any
+    consistent shape (small models for tests)."""
+    try:
+        cfg = json.loads(meta.get("openthai.config", ""))
+    except ValueError as e:
+        raise OpenThaiError(f"openthai.config: {e}") from e
+    c = cfg.get("text_config") or {}
+    if strict:
+        for k, n in REFERENCE_CONFIG.items():
+            if c.get(k) != n:
+                raise OpenThaiError(f"unsupported OpenThai config {k}")
+        rp = c.get("rope_parameters") or {}
+        if (cfg.get("n_slots") != 256 or cfg.get("abstain_slot") != 255 or cfg.get("answer_token_id") != 248082
+                or c.get("rms_norm_eps") != 1e-6 or rp.get("rope_theta") != 1e7
+                or rp.get("partial_rotary_factor") != 0.25 or rp.get("rope_type") != "default"):
+            raise OpenThaiError("unsupported OpenThai head/normalization/rotary configuration")
+    if c.get("linear_num_key_heads") != c.get("linear_num_value_heads") or \
+            c.get("linear_key_head_dim") != c.get("linear_value_head_dim"):
+        raise OpenThaiError("DeltaNet key and value heads must match")
+    rp = c.get("rope_parameters") or {}
+    hd = int(c["head_dim"])
+    types = list(c.get("layer_types") or [])
+    if len(types) != int(c["num_hidden_layers"]) or any(t not in ("full_attention", "linear_attention")
+                                                           for t in types):
+        raise OpenThaiError("unsupported OpenThai layer type")
+    max_tokens = int(meta.get("openthai.context_length", 4096))
+    max_state = int(meta.get("openthai.state_length", 2048))
+    if not 32 <= max_tokens <= 8192 or not 1 <= max_state <= max_tokens:
+        raise OpenThaiError("invalid OpenThai sequence budgets")
+    return {"d": int(c["hidden_size"]), "ffn": int(c["intermediate_size"]), "heads": int(c["num_attention_heads"]),
+            "kv_heads": int(c["num_key_value_heads"]), "head_dim": hd,
+            "rot": int(round(hd * float(rp.get("partial_rotary_factor", 0.25)))),
+            "theta": float(rp.get("rope_theta", 1e7)), "lin_heads": int(c["linear_num_key_heads"]),
+            "lin_dim": int(c["linear_key_head_dim"]), "vocab": int(c["vocab_size"]), "layer_types": types,
+            "slots": int(cfg.get("n_slots", 256)), "answer_token_id": int(cfg.get("answer_token_id", 248082)),
+            "max_tokens": max_tokens, "max_state": max_state}
+
+
+def load_weights(path: str, strict: bool = True) -> dict:
+    """Config and F32 weights of an OpenThai GGUF under its tensor names
+    (model.rs:103-174), with `temperature` = exp(log_temperature)."""
+    from .gguf_meta import read_tensors_f32
+
+    meta, t = read_tensors_f32(path)
+    cfg = load_config(meta, strict)
+    t["config"] = cfg
+    t["temperature"] = np.exp(t["log_temperature"].astype(np.float32)).astype(np.float32)
+    return t

@@ -184,3 +184,28 @@ def test_openthai_forward_matches_float64(s):
     want = ref_forward(m, ids, pos)
     assert got.shape == (len(pos), 16)
     assert np.allclose(got, want, atol=2e-3, rtol=2e-3), np.abs(got - want).max()
+
+
+def test_openthai_gguf_round_trip_and_forward(tmp_path):
+    from laya_goish_b200 import openthai, synth
+
+    path = synth.write_openthai(str(tmp_path / "ot.gguf"), seed=5)
+    with pytest.raises(openthai.OpenThaiError, match="unsupported OpenThai config"):
+        openthai.load_weights(path)  # the reference loads only its one size
+    m = openthai.load_weights(path, strict=False)
+    c = m["config"]
+    assert (c["d"], c["heads"], c["kv_heads"], c["head_dim"], c["rot"]) == (48, 4, 2, 32, 8)
+    assert c["layer_types"][2] == "full_attention" and c["max_state"] == 256
+    assert m["model.layers.0.linear_attn.in_proj_qkv.weight"].shape == (96, 48)
+    assert m["model.layers.0.linear_attn.conv1d.weight"].shape == (96 * 4,)
+    for i in (0, 1, 3):  # the [3w][4] view of the convolution kernel for the float64 restatement
+        k = f"model.layers.{i}.linear_attn.conv1d.weight"
+        m[k] = m[k].reshape(-1, 4)
+    rng = np.random.default_rng(9)
+    ids = rng.integers(0, 300, size=23)
+    pos = [0, 11, 22]
+    got = oracle.ot_forward(m, ids, pos)
+    want = ref_forward(m, ids, pos)
+    assert got.shape == (3, 256)
+    assert np.allclose(got, want, atol=2e-3, rtol=2e-3), np.abs(got - want).max()
+    assert np.allclose(m["temperature"], np.exp(m["log_temperature"]))
