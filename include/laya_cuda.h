@@ -159,6 +159,26 @@ int laya_gated_delta_mixer(int device, const float* raw, const float* z, const f
  * 256; H a multiple of KV.  Host buffers. */
 int laya_gated_attention(int device, const float* qgate, const float* k, const float* v, const float* qn,
                          const float* kn, int s, int H, int KV, int hd, int rot, float theta, float* out);
+/* OpenThai model on one GPU (Model::load / Model::forward,
+ * src/models/openthai/model.rs:99-241).  The shape comes parsed from the
+ * file's `openthai.config` by the host (its config checks, model.rs:99-135);
+ * layer_full[l] is nonzero for a full-attention layer, zero for a DeltaNet
+ * layer, and is read only during laya_openthai_open.  Weights are F32 or F16
+ * tensors under the reference's names; the GEMMs run on F16 operands with F32
+ * accumulation.  Constraints of the GPU forward: d a multiple of 32, ffn a
+ * multiple of 128, head_dim 64/128/256, lin_dim 64/128. */
+typedef struct laya_ot_config {
+  int d, ffn, heads, kv_heads, head_dim, rot, lin_heads, lin_dim, vocab, slots, n_layers;
+  float theta, eps;
+  const uint8_t* layer_full;
+} laya_ot_config;
+typedef struct laya_ot_model laya_ot_model;
+int laya_openthai_open(const char* path, int device, const laya_ot_config* cfg, laya_ot_model** out);
+/* Model::forward for one encoded pass: the slot logits (slot head + bias) at
+ * the given positions -> out [npos][slots] (host buffers). */
+int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int32_t* positions, int npos,
+                          float* out);
+void laya_openthai_close(laya_ot_model* m);
 /* Decodes a weight tensor of the model from its device layout back to F32
  * (for parity checks of the upload transcoding).  out: element count floats. */
 int laya_tensor_f32(laya_model* m, const char* name, float* out, size_t max_elems);

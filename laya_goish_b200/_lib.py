@@ -59,6 +59,12 @@ class Timing(ctypes.Structure):
                 ("d2h_bytes", ctypes.c_int64)]
 
 
+class OtConfig(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_int32) for k in ("d", "ffn", "heads", "kv_heads", "head_dim", "rot", "lin_heads",
+                                              "lin_dim", "vocab", "slots", "n_layers")] + \
+               [("theta", ctypes.c_float), ("eps", ctypes.c_float), ("layer_full", ctypes.c_void_p)]
+
+
 class ProfileEntry(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
 
@@ -103,6 +109,10 @@ def lib() -> ctypes.CDLL:
     L.laya_last_timing.argtypes = [P, ctypes.POINTER(Timing)]
     L.laya_profile_enable.argtypes = [P, I]
     L.laya_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I]
+    L.laya_openthai_open.argtypes = [ctypes.c_char_p, I, ctypes.POINTER(OtConfig), ctypes.POINTER(P)]
+    L.laya_openthai_forward.argtypes = [P, P, I, P, I, P]
+    L.laya_openthai_close.argtypes = [P]
+    L.laya_openthai_close.restype = None
     _lib = L
     return L
 

@@ -1,0 +1,335 @@
+// OpenThai forward on one GPU (Model::forward, src/models/openthai/model.rs:
+// 192-241): embedding rows; per layer x += mixer(rms(x, n1, 1)) with the
+// gated attention or the gated DeltaNet mixer, x += down(silu(gate h) * up h)
+// with h = rms(x, n2, 1); the slot head (+ bias) on rms(x[positions], norm, 1).
+//
+// Built from the decoder path's pieces: the tcgen05 GEMM for every
+// projection (F16 operands, F32 accumulation; the attention output, out_proj
+// and down GEMMs add into the F32 residual; gate/up interleaved per 128 rows
+// for the SwiGLU epilogue), the RMSNorm kernel with the offset-1 weights
+// stored as 1 + w, and the two mixer kernels (gated_attn.cu, deltanet.cu).
+// The model shape comes parsed from the file's `openthai.config` by the
+// caller (the host's config checks); tensors are read from the GGUF here.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "engine.h"
+#include "gemm.h"
+#include "gguf.h"
+#include "kernels.h"
+
+namespace laya {
+
+struct OtLayer {
+  bool full = false;
+  const float *n1 = nullptr, *n2 = nullptr;  // 1 + w
+  const half *gu = nullptr, *down = nullptr;
+  const half *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+  const float *qn = nullptr, *kn = nullptr;
+  const half *qkv = nullptr, *z = nullptr, *a = nullptr, *b = nullptr, *out = nullptr;
+  const float *conv = nullptr, *dt = nullptr, *alog = nullptr, *normw = nullptr;
+};
+
+}  // namespace laya
+
+struct laya_ot_model {
+  laya_ot_config cfg{};
+  int device = 0, num_sms = 148;
+  cudaStream_t st = nullptr;
+  std::vector<laya::OtLayer> layers;
+  laya::QTensor embd{};
+  const float* norm = nullptr;  // 1 + w
+  const half* head = nullptr;
+  const float* head_bias = nullptr;
+  unsigned* err = nullptr;
+  std::vector<void*> allocs;
+  std::mutex mu;
+};
+
+namespace laya {
+namespace {
+
+using Model = laya_ot_model;
+
+int dalloc(Model& m, size_t bytes, void** p) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (OpenThai weights)");
+  m.allocs.push_back(*p);
+  return 0;
+}
+
+// The tensor's elements as F32 on the host (F32 or F16 tensors).
+int host_f32(const Gguf& g, const std::string& name, size_t count, std::vector<float>* out) {
+  const TensorInfo* t = g.tensor(name);
+  if (!t) return fail(LAYA_E_FORMAT, "missing tensor " + name);
+  if (t->count() != count) return fail(LAYA_E_FORMAT, name + ": unexpected shape");
+  if (t->kind != K_F32 && t->kind != K_F16) return fail(LAYA_E_FORMAT, name + ": only F32/F16 OpenThai tensors");
+  out->resize(count);
+  const uint8_t* d = g.data(*t);
+  if (t->kind == K_F32) {
+    std::memcpy(out->data(), d, count * 4);
+  } else {
+    for (size_t i = 0; i < count; i++) (*out)[i] = half_bits((uint16_t)(d[2 * i] | (d[2 * i + 1] << 8)));
+  }
+  return 0;
+}
+
+int upload_vec(Model& m, const Gguf& g, const std::string& name, size_t n, float offset, const float** out) {
+  std::vector<float> v;
+  if (int rc = host_f32(g, name, n, &v)) return rc;
+  for (float& x : v) x = offset + x;
+  void* p;
+  if (int rc = dalloc(m, n * 4, &p)) return rc;
+  LAYA_CK(cudaMemcpy(p, v.data(), n * 4, cudaMemcpyHostToDevice));
+  *out = static_cast<const float*>(p);
+  return 0;
+}
+
+// Matrix [rows][cols] as F16 (GGUF dims [cols, rows]).
+int upload_mat(Model& m, const Gguf& g, const std::string& name, int rows, int cols, const half** out) {
+  const TensorInfo* t = g.tensor(name);
+  if (!t) return fail(LAYA_E_FORMAT, "missing tensor " + name);
+  if (t->dims.size() != 2 || t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)
+    return fail(LAYA_E_FORMAT, name + ": unexpected matrix shape");
+  std::vector<float> v;
+  if (int rc = host_f32(g, name, (size_t)rows * cols, &v)) return rc;
+  std::vector<half> h(v.size());
+  for (size_t i = 0; i < v.size(); i++) h[i] = __float2half_rn(v[i]);
+  void* p;
+  if (int rc = dalloc(m, h.size() * 2, &p)) return rc;
+  LAYA_CK(cudaMemcpy(p, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+  *out = static_cast<const half*>(p);
+  return 0;
+}
+
+// gate and up [ffn][d] interleaved per 128 rows into one [2 ffn][d] operand
+int upload_gate_up(Model& m, const Gguf& g, const std::string& p, int ffn, int d, const half** out) {
+  std::vector<float> gt, up;
+  if (int rc = host_f32(g, p + ".mlp.gate_proj.weight", (size_t)ffn * d, &gt)) return rc;
+  if (int rc = host_f32(g, p + ".mlp.up_proj.weight", (size_t)ffn * d, &up)) return rc;
+  std::vector<half> h((size_t)2 * ffn * d);
+  for (int r = 0; r < ffn; r++) {
+    const size_t blk = r / 128, off = r % 128;
+    for (int c = 0; c < d; c++) {
+      h[((blk * 256) + off) * d + c] = __float2half_rn(gt[(size_t)r * d + c]);
+      h[((blk * 256) + 128 + off) * d + c] = __float2half_rn(up[(size_t)r * d + c]);
+    }
+  }
+  void* q;
+  if (int rc = dalloc(m, h.size() * 2, &q)) return rc;
+  LAYA_CK(cudaMemcpy(q, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+  *out = static_cast<const half*>(q);
+  return 0;
+}
+
+int load(Model& m, const Gguf& g) {
+  const laya_ot_config& c = m.cfg;
+  const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
+  const int w = nh * hk;
+  const TensorInfo* e = g.tensor("model.embed_tokens.weight");
+  if (!e || e->dims.size() != 2 || e->dims[0] != (uint64_t)d || e->dims[1] != (uint64_t)c.vocab ||
+      (e->kind != K_F32 && e->kind != K_F16))
+    return fail(LAYA_E_FORMAT, "OpenThai embeddings must be F32/F16 with shape [vocab, hidden]");
+  void* pe;
+  if (int rc = dalloc(m, e->len, &pe)) return rc;
+  LAYA_CK(cudaMemcpy(pe, g.data(*e), e->len, cudaMemcpyHostToDevice));
+  m.embd = QTensor{};
+  m.embd.kind = (int)e->kind;
+  m.embd.rows = c.vocab;
+  m.embd.cols = d;
+  m.embd.q = static_cast<const uint8_t*>(pe);
+  m.layers.resize(c.n_layers);
+  int rc;
+  for (int l = 0; l < c.n_layers; l++) {
+    OtLayer& L = m.layers[l];
+    const std::string p = "model.layers." + std::to_string(l);
+    L.full = c.layer_full[l] != 0;
+    if ((rc = upload_vec(m, g, p + ".input_layernorm.weight", d, 1.f, &L.n1)) ||
+        (rc = upload_vec(m, g, p + ".post_attention_layernorm.weight", d, 1.f, &L.n2)) ||
+        (rc = upload_gate_up(m, g, p, c.ffn, d, &L.gu)) ||
+        (rc = upload_mat(m, g, p + ".mlp.down_proj.weight", d, c.ffn, &L.down)))
+      return rc;
+    if (L.full) {
+      if ((rc = upload_mat(m, g, p + ".self_attn.q_proj.weight", 2 * H * hd, d, &L.q)) ||
+          (rc = upload_mat(m, g, p + ".self_attn.k_proj.weight", KV * hd, d, &L.k)) ||
+          (rc = upload_mat(m, g, p + ".self_attn.v_proj.weight", KV * hd, d, &L.v)) ||
+          (rc = upload_mat(m, g, p + ".self_attn.o_proj.weight", d, H * hd, &L.o)) ||
+          (rc = upload_vec(m, g, p + ".self_attn.q_norm.weight", hd, 0.f, &L.qn)) ||
+          (rc = upload_vec(m, g, p + ".self_attn.k_norm.weight", hd, 0.f, &L.kn)))
+        return rc;
+    } else {
+      if ((rc = upload_mat(m, g, p + ".linear_attn.in_proj_qkv.weight", 3 * w, d, &L.qkv)) ||
+          (rc = upload_mat(m, g, p + ".linear_attn.in_proj_z.weight", w, d, &L.z)) ||
+          (rc = upload_mat(m, g, p + ".linear_attn.in_proj_a.weight", nh, d, &L.a)) ||
+          (rc = upload_mat(m, g, p + ".linear_attn.in_proj_b.weight", nh, d, &L.b)) ||
+          (rc = upload_mat(m, g, p + ".linear_attn.out_proj.weight", d, w, &L.out)) ||
+          (rc = upload_vec(m, g, p + ".linear_attn.conv1d.weight", (size_t)3 * w * 4, 0.f, &L.conv)) ||
+          (rc = upload_vec(m, g, p + ".linear_attn.dt_bias", nh, 0.f, &L.dt)) ||
+          (rc = upload_vec(m, g, p + ".linear_attn.A_log", nh, 0.f, &L.alog)) ||
+          (rc = upload_vec(m, g, p + ".linear_attn.norm.weight", hk, 0.f, &L.normw)))
+        return rc;
+    }
+  }
+  if ((rc = upload_vec(m, g, "model.norm.weight", d, 1.f, &m.norm)) ||
+      (rc = upload_mat(m, g, "slot_head.weight", c.slots, d, &m.head)) ||
+      (rc = upload_vec(m, g, "slot_head.bias", c.slots, 0.f, &m.head_bias)))
+    return rc;
+  void* pe2;
+  if ((rc = dalloc(m, 16, &pe2))) return rc;
+  m.err = static_cast<unsigned*>(pe2);
+  LAYA_CK(cudaMemset(m.err, 0, 16));
+  return 0;
+}
+
+int gemm(Model& m, int epi, const half* A, int lda, const half* B, int N, int K, int M, void* out, int ldo,
+         float* resid, const float* bias) {
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.out = out;
+  a.ldo = ldo;
+  a.resid = resid;
+  a.bias = bias;
+  a.err = m.err;
+  a.budget = 4000000000ll;
+  LAYA_CK(gemm_launch(epi, A, lda, B, K, a, m.num_sms, m.st));
+  return 0;
+}
+
+}  // namespace
+}  // namespace laya
+
+using namespace laya;
+
+extern "C" {
+
+int laya_openthai_open(const char* path, int device, const laya_ot_config* cfg, laya_ot_model** out) {
+  if (!path || !cfg || !out || !cfg->layer_full) return fail(LAYA_E_INVALID, "null argument");
+  *out = nullptr;
+  const laya_ot_config& c = *cfg;
+  if (c.d < 32 || c.d % 32 || c.ffn < 128 || c.ffn % 128 || c.heads < 1 || c.kv_heads < 1 || c.heads % c.kv_heads ||
+      (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) || c.rot < 0 || c.rot > c.head_dim ||
+      c.rot % 2 || c.lin_heads < 1 || (c.lin_dim != 64 && c.lin_dim != 128) || c.vocab < 1 || c.slots < 1 ||
+      c.n_layers < 1 || c.n_layers > 256)
+    return fail(LAYA_E_INVALID, "unsupported OpenThai shape for the GPU forward");
+  Gguf g;
+  std::string e = g.open_file(path);
+  if (!e.empty()) return fail(g.bytes() ? LAYA_E_FORMAT : LAYA_E_IO, e);
+  auto m = std::make_unique<laya_ot_model>();
+  m->cfg = c;
+  m->cfg.layer_full = nullptr;  // not kept: copied into the layers
+  m->device = device;
+  LAYA_CK(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  LAYA_CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(LAYA_E_CUDA, "not an sm_100 GPU");
+  m->num_sms = prop.multiProcessorCount;
+  LAYA_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
+  m->cfg.layer_full = c.layer_full;
+  int rc = load(*m, g);
+  m->cfg.layer_full = nullptr;
+  if (rc) {
+    laya_openthai_close(m.release());
+    return rc;
+  }
+  *out = m.release();
+  return 0;
+}
+
+int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int32_t* positions, int npos,
+                          float* out) {
+  if (!m || !ids || !positions || !out || s < 1 || npos < 1) return fail(LAYA_E_INVALID, "invalid forward arguments");
+  std::lock_guard<std::mutex> lk(m->mu);
+  const laya_ot_config& c = m->cfg;
+  for (int i = 0; i < s; i++)
+    if (ids[i] < 0 || ids[i] >= c.vocab) return fail(LAYA_E_INVALID, "invalid OpenThai token sequence");
+  for (int i = 0; i < npos; i++)
+    if (positions[i] < 0 || positions[i] >= s) return fail(LAYA_E_INVALID, "invalid OpenThai token sequence");
+  LAYA_CK(cudaSetDevice(m->device));
+  LAYA_CK(cudaMemsetAsync(m->err, 0, 4, m->st));
+  const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
+  const int w = nh * hk, qd = H * hd, ffn = c.ffn;
+  const size_t S = (size_t)s;
+  DevBuf dids, dpos, x, h, big, k, v, att, att16, act, logits;
+  struct Release {
+    std::vector<DevBuf*> b;
+    ~Release() {
+      for (DevBuf* p : b) p->release();
+    }
+  } rel{{&dids, &dpos, &x, &h, &big, &k, &v, &att, &att16, &act, &logits}};
+  // big: the largest projection output (2 qd, 3w) plus the mixers' scratch
+  const size_t bigf = S * (size_t)std::max(2 * qd, 3 * w) + S * (size_t)std::max(qd + KV * hd, 3 * w) + S * 2 * w;
+  int rc;
+  if ((rc = dids.ensure(S * 4)) || (rc = dpos.ensure((size_t)npos * 4)) || (rc = x.ensure(S * d * 4)) ||
+      (rc = h.ensure(std::max(S, (size_t)npos) * d * 2)) || (rc = big.ensure(bigf * 4)) || (rc = k.ensure(S * std::max(KV * hd, 2 * nh) * 4)) ||
+      (rc = v.ensure(S * std::max(KV * hd, w) * 4)) || (rc = att.ensure(S * std::max(qd, w) * 4)) ||
+      (rc = att16.ensure(S * std::max(qd, w) * 2)) || (rc = act.ensure(S * ffn * 2)) ||
+      (rc = logits.ensure((size_t)npos * c.slots * 4)))
+    return rc;
+  cudaStream_t st = m->st;
+  LAYA_CK(cudaMemcpyAsync(dids.p, ids, S * 4, cudaMemcpyHostToDevice, st));
+  LAYA_CK(cudaMemcpyAsync(dpos.p, positions, (size_t)npos * 4, cudaMemcpyHostToDevice, st));
+  float* X = x.as<float>();
+  half* Hh = h.as<half>();
+  float* P = big.as<float>();                                   // projection outputs
+  float* SCR = P + S * (size_t)std::max(2 * qd, 3 * w);        // mixer scratch
+  LAYA_CK(rows_f32(m->embd, dids.as<int>(), s, X, st));
+  for (int l = 0; l < c.n_layers; l++) {
+    const OtLayer& L = m->layers[l];
+    LAYA_CK(rmsnorm(X, nullptr, s, L.n1, d, c.eps, Hh, nullptr, st));
+    if (L.full) {
+      float* qg = P;
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.q, 2 * qd, d, s, qg, 2 * qd, nullptr, nullptr)) ||
+          (rc = gemm(*m, EPI_F32, Hh, d, L.k, KV * hd, d, s, k.p, KV * hd, nullptr, nullptr)) ||
+          (rc = gemm(*m, EPI_F32, Hh, d, L.v, KV * hd, d, s, v.p, KV * hd, nullptr, nullptr)))
+        return rc;
+      LAYA_CK(gated_attention(qg, k.as<float>(), v.as<float>(), L.qn, L.kn, s, H, KV, hd, c.rot, c.theta, SCR,
+                              att.as<float>(), st));
+      LAYA_CK(f32_to_f16_pad(att.as<float>(), s, qd, qd, att16.as<half>(), st));
+      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr))) return rc;
+    } else {
+      float* raw = P;
+      float* zz = v.as<float>();
+      float* ab = k.as<float>();  // a then b, [s][nh] each
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, 3 * w, d, s, raw, 3 * w, nullptr, nullptr)) ||
+          (rc = gemm(*m, EPI_F32, Hh, d, L.z, w, d, s, zz, w, nullptr, nullptr)) ||
+          (rc = gemm(*m, EPI_F32, Hh, d, L.a, nh, d, s, ab, nh, nullptr, nullptr)) ||
+          (rc = gemm(*m, EPI_F32, Hh, d, L.b, nh, d, s, ab + S * nh, nh, nullptr, nullptr)))
+        return rc;
+      LAYA_CK(gated_delta_mixer(raw, zz, ab, ab + S * nh, L.conv, L.dt, L.alog, L.normw, s, nh, hk, SCR,
+                                att.as<float>(), st));
+      LAYA_CK(f32_to_f16_pad(att.as<float>(), s, w, w, att16.as<half>(), st));
+      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), w, L.out, d, w, s, nullptr, d, X, nullptr))) return rc;
+    }
+    LAYA_CK(rmsnorm(X, nullptr, s, L.n2, d, c.eps, Hh, nullptr, st));
+    if ((rc = gemm(*m, EPI_SWIGLU, Hh, d, L.gu, 2 * ffn, d, s, act.p, ffn, nullptr, nullptr)) ||
+        (rc = gemm(*m, EPI_RESID, act.as<half>(), ffn, L.down, d, ffn, s, nullptr, d, X, nullptr)))
+      return rc;
+  }
+  LAYA_CK(rmsnorm(X, dpos.as<int>(), npos, m->norm, d, c.eps, Hh, nullptr, st));
+  if ((rc = gemm(*m, EPI_F32, Hh, d, m->head, c.slots, d, npos, logits.p, c.slots, nullptr, m->head_bias))) return rc;
+  LAYA_CK(cudaMemcpyAsync(out, logits.p, (size_t)npos * c.slots * 4, cudaMemcpyDeviceToHost, st));
+  LAYA_CK(cudaStreamSynchronize(st));
+  unsigned err = 0;
+  LAYA_CK(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost));
+  if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");
+  for (size_t i = 0; i < (size_t)npos * c.slots; i++)
+    if (!std::isfinite(out[i])) return fail(LAYA_E_NONFINITE, "non-finite model output");
+  return 0;
+}
+
+void laya_openthai_close(laya_ot_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->st) cudaStreamSynchronize(m->st);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->st) cudaStreamDestroy(m->st);
+  delete m;
+}
+
+}  // extern "C"

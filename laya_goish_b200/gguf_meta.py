@@ -112,26 +112,33 @@ def _parse(buf, tensors: bool = False):
 _ELEM = {0: (4, "<f4"), 1: (2, "<f2")}
 
 
-def read_tensors_f32(path: str) -> tuple[dict, dict]:
-    """Metadata and every F32 / F16 tensor of a GGUF file as F32 arrays of
-    shape dims reversed (GGUF dims are innermost first: a matrix [K, N] is N
-    rows of K).  Other tensor types raise GGUFError."""
+def read_tensors_f32(path: str, names=None) -> tuple[dict, dict]:
+    """Metadata and the F32 / F16 tensors of a GGUF file (all of them, or
+    those in `names`) as F32 arrays of shape dims reversed (GGUF dims are
+    innermost first: a matrix [K, N] is N rows of K).  Other tensor types
+    raise GGUFError."""
     import numpy as np
 
     with open(path, "rb") as f:
-        data = f.read()
-    meta, infos, base = _parse(memoryview(data), tensors=True)
-    out = {}
-    for name, dims, kind, off in infos:
-        if kind not in _ELEM:
-            raise GGUFError(f"{name}: tensor type {kind} is not F32/F16")
-        size, dt = _ELEM[kind]
-        n = 1
-        for d in dims:
-            n *= d
-        start = base + off
-        if start + n * size > len(data):
-            raise GGUFError(f"{name}: tensor data out of range")
-        a = np.frombuffer(data, dtype=dt, count=n, offset=start).astype(np.float32)
-        out[name] = a.reshape(list(reversed(dims))) if dims else a
+        with mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) as data:
+            mv = memoryview(data)
+            try:
+                meta, infos, base = _parse(mv, tensors=True)
+                out = {}
+                for name, dims, kind, off in infos:
+                    if names is not None and name not in names:
+                        continue
+                    if kind not in _ELEM:
+                        raise GGUFError(f"{name}: tensor type {kind} is not F32/F16")
+                    size, dt = _ELEM[kind]
+                    n = 1
+                    for d in dims:
+                        n *= d
+                    start = base + off
+                    if start + n * size > len(data):
+                        raise GGUFError(f"{name}: tensor data out of range")
+                    a = np.frombuffer(mv[start:start + n * size], dtype=dt, count=n).astype(np.float32)
+                    out[name] = a.reshape(list(reversed(dims))) if dims else a
+            finally:
+                mv.release()
     return meta, out

@@ -330,3 +330,78 @@ def load_weights(path: str, strict: bool = True) -> dict:
     t["config"] = cfg
     t["temperature"] = np.exp(t["log_temperature"].astype(np.float32)).astype(np.float32)
     return t
+
+
+class Model:
+    """An OpenThai GGUF on one GPU (laya_openthai_open / _forward / _close):
+    the config from the file's `openthai.config` (checked as `load_config`),
+    the per-kind temperatures from `log_temperature`, and `decide(tok, req)`
+    running every permutation pass of a request through the GPU forward and
+    the calibrated slot decoding (decision.rs:243-391)."""
+
+    def __init__(self, path: str, device: int = 0, strict: bool = True):
+        import ctypes
+
+        from . import _lib
+        from .gguf_meta import read_tensors_f32
+
+        meta, t = read_tensors_f32(path, names={"log_temperature"})
+        self.config = c = load_config(meta, strict)
+        if "log_temperature" not in t or t["log_temperature"].size != 3:
+            raise OpenThaiError("missing or invalid tensor log_temperature")
+        self.temperature = np.exp(t["log_temperature"].astype(np.float32)).astype(np.float32)
+        self._full = np.array([ty == "full_attention" for ty in c["layer_types"]], np.uint8)
+        eps = float(json.loads(meta["openthai.config"]).get("text_config", {}).get("rms_norm_eps", 1e-6))
+        cfg = _lib.OtConfig(c["d"], c["ffn"], c["heads"], c["kv_heads"], c["head_dim"], c["rot"], c["lin_heads"],
+                            c["lin_dim"], c["vocab"], c["slots"], len(c["layer_types"]), c["theta"], eps,
+                            self._full.ctypes.data_as(ctypes.c_void_p))
+        h = ctypes.c_void_p()
+        _lib.check(_lib.lib().laya_openthai_open(path.encode(), device, ctypes.byref(cfg), ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        from . import _lib
+
+        if self._h:
+            _lib.lib().laya_openthai_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, ids, positions) -> np.ndarray:
+        """Slot logits [len(positions)][slots] of one encoded pass."""
+        import ctypes
+
+        from . import _lib
+
+        if not self._h:
+            raise OpenThaiError("model is closed")
+        ids = np.ascontiguousarray(np.asarray(ids, np.int32))
+        pos = np.ascontiguousarray(np.asarray(positions, np.int32))
+        out = np.zeros((len(pos), self.config["slots"]), np.float32)
+        _lib.check(_lib.lib().laya_openthai_forward(self._h, ids.ctypes.data_as(ctypes.c_void_p), len(ids),
+                                                    pos.ctypes.data_as(ctypes.c_void_p), len(pos),
+                                                    out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def decide(self, tok, req: dict) -> dict:
+        """Model::decide (decision.rs:70-120): every permutation pass of the
+        request through the forward, then the calibrated slot decoding."""
+        qs = questions(req)
+        n = permutation_count(req, qs)
+        c = self.config
+        passes = []
+        for p in range(n):
+            e = encode(tok, req, qs, n, p, c["answer_token_id"], c["max_tokens"], c["max_state"])
+            passes.append((self.forward(e.ids, e.positions), e.order))
+        return decide(qs, passes, self.temperature)

@@ -40,3 +40,16 @@ def test_null_arguments_rejected():
     assert L.laya_layers(None) == _lib.E_INVALID
     assert L.laya_decide_batch(None, None, None, _lib.CANCEL_FN(), None) == _lib.E_INVALID
     assert b"null" in L.laya_last_error()
+
+
+def test_openthai_entry_points_reject_bad_arguments():
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    full = (ctypes.c_uint8 * 2)(1, 0)
+    cfg = _lib.OtConfig(128, 256, 4, 2, 96, 24, 2, 64, 300, 256, 2, 1e7, 1e-6,
+                        ctypes.cast(full, ctypes.c_void_p))
+    assert L.laya_openthai_open(b"/nonexistent.gguf", 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_INVALID
+    assert b"unsupported OpenThai shape" in L.laya_last_error() and not h.value
+    assert L.laya_openthai_open(b"x", 0, None, ctypes.byref(h)) == _lib.E_INVALID
+    assert L.laya_openthai_forward(None, None, 0, None, 0, None) == _lib.E_INVALID
+    L.laya_openthai_close(None)

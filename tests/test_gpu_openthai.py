@@ -75,3 +75,68 @@ def test_gated_delta_mixer_matches_oracle(s, nh, hk):
     got = engine.gated_delta_mixer(raw, z, a, b, conv, dt, alog, normw, nh, hk)
     want = oracle.ot_delta_mid(raw, z, a, b, conv, dt, alog, normw, nh, hk)
     assert np.allclose(got, want, atol=1e-4, rtol=1e-3), np.abs(got - want).max()
+
+
+@pytest.fixture(scope="module")
+def ot_model(tmp_path_factory):
+    from laya_goish_b200 import openthai, synth
+
+    path = synth.write_openthai(str(tmp_path_factory.mktemp("ot") / "ot.gguf"), d=128, ffn=256, heads=4, kv=2,
+                                hd=64, lin_heads=2, lin_dim=64, seed=11)
+    weights = openthai.load_weights(path, strict=False)
+    with openthai.Model(path, strict=False) as m:
+        yield m, weights
+
+
+def test_openthai_forward_matches_oracle(ot_model):
+    m, w = ot_model
+    rng = np.random.default_rng(3)
+    for s, pos in [(40, [0, 20, 39]), (1, [0]), (200, [7, 150, 199])]:
+        ids = rng.integers(0, 300, s)
+        got = m.forward(ids, pos)
+        want = oracle.ot_forward(w, ids, pos)
+        # F16 GEMM operands (activations rounded to 2^-11 relative) against F32;
+        # a NumPy emulation of that rounding lands near 1e-3 of the largest logit
+        tol = 5e-3 * np.abs(want).max()
+        assert got.shape == (len(pos), 256)
+        assert np.abs(got - want).max() < tol, (s, np.abs(got - want).max(), tol)
+    # causal: a prefix's last position gives the same logits as in the full pass
+    ids = rng.integers(0, 300, 40)
+    full = m.forward(ids, [20])
+    head = m.forward(ids[:21], [20])
+    assert np.allclose(full, head, atol=1e-4, rtol=1e-4)
+    with pytest.raises(LayaError):
+        m.forward([0, 1, 300], [0])
+    with pytest.raises(LayaError):
+        m.forward([0, 1, 2], [3])
+
+
+def test_openthai_decide_matches_oracle(ot_model):
+    from laya_goish_b200 import openthai
+    from laya_goish_b200.tokenizer import Tokenizer, byte_alphabet
+
+    m, w = ot_model
+    control = ["<|ts_q|>", "<|ts_choice|>", "<|ts_score|>", "<|ts_noul|>", "<|ts_answer|>", "<|ts_state|>"] + \
+              [f"<|ts_opt_{i}|>" for i in range(12)]
+    tok = Tokenizer({"tokenizer.ggml.pre": "gpt2", "tokenizer.ggml.tokens": byte_alphabet() + control,
+                     "tokenizer.ggml.merges": []})
+    m.config["answer_token_id"] = w["config"]["answer_token_id"] = tok.vocab["<|ts_answer|>"]
+    req = {"state": {"ticket": "refund please", "n": 3},
+           "questions": {"c": {"type": "choice", "instructions": "route", "criteria": {"a": "billing", "b": None,
+                                                                                       "c": "other"}},
+                         "s": {"type": "score", "instructions": "urgency", "criteria": ["low", "mid", "high"]},
+                         "n": {"type": "noul", "instructions": "spam?"}},
+           "order_invariant": True}
+    got = m.decide(tok, req)
+    qs = openthai.questions(req)
+    n = openthai.permutation_count(req, qs)
+    assert n == 3
+    passes = []
+    for p in range(n):
+        e = openthai.encode(tok, req, qs, n, p, w["config"]["answer_token_id"], 512, 256)
+        passes.append((oracle.ot_forward(w, e.ids, e.positions), e.order))
+    want = openthai.decide(qs, passes, w["temperature"])
+    for k in ("a", "b", "c"):
+        assert abs(got["c"]["probabilities"][k] - want["c"]["probabilities"][k]) < 1e-2
+    assert abs(got["s"]["score"] - want["s"]["score"]) < 5e-2
+    assert abs(got["n"]["noul"] - want["n"]["noul"]) < 1e-2
