@@ -463,6 +463,59 @@ def run_load(args):
     print(json.dumps(out), flush=True)
 
 
+def run_openthai(args):
+    """OpenThai forward on one GPU at the reference's widths (d 1024, FFN
+    3584, 24 layers: 18 gated DeltaNet layers of 16 x 128 heads and 6 gated
+    attention layers of 8/2 x 256 heads, one in four, a synthetic F16 model
+    from seed; vocabulary cut to 4096 rows, which only sizes the embedding
+    table).  One step = one `--ot-tokens`-token pass through the host API
+    (ids up, three answer rows of slot logits down), so the time includes
+    the copies.  Not the contract line."""
+    import tempfile
+
+    import torch
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    from laya_goish_b200 import openthai
+
+    d, ffn, H, KV, hd, nh, hk, L = 1024, 3584, 8, 2, 256, 16, 128, 24
+    types = tuple((["linear_attention"] * 3 + ["full_attention"]) * (L // 4))
+    s = args.ot_tokens
+    with tempfile.TemporaryDirectory() as tmp:
+        path = synth.write_openthai(os.path.join(tmp, "openthai.gguf"), d=d, ffn=ffn, vocab=4096, heads=H, kv=KV,
+                                    hd=hd, lin_heads=nh, lin_dim=hk, layer_types=types, seed=1, width_scaled=True)
+        t0 = time.perf_counter()
+        m = openthai.Model(path, device=local, strict=False)
+        open_s = time.perf_counter() - t0
+    ids = np.random.default_rng(2).integers(0, 4096, s)
+    pos = [s - 201, s - 101, s - 1] if s > 201 else [s - 1]
+    for _ in range(args.warmup):
+        m.forward(ids, pos)
+    clk = Clocks(local).start()
+    clk.begin()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = m.forward(ids, pos)
+    ms = (time.perf_counter() - t0) * 1000 / args.steps
+    clk.end()
+    clk.stop()
+    m.close()
+    w = nh * hk
+    per_delta = d * (3 * w + w + 2 * nh) + w * d
+    per_full = d * (2 * H * hd + 2 * KV * hd) + H * hd * d
+    mlp = 3 * d * ffn
+    gemm_flops = 2.0 * s * (L * mlp + (3 * L // 4) * per_delta + (L // 4) * per_full) + 2.0 * len(pos) * 256 * d
+    out_line = {"workload": f"OpenThai forward: d {d}, FFN {ffn}, {L} layers ({3 * L // 4} DeltaNet {nh}x{hk}, "
+                            f"{L // 4} gated attention {H}/{KV}x{hd}), synthetic F16, {s}-token pass, "
+                            f"{len(pos)} answer rows",
+                "ms_per_pass": ms, "tokens_per_s": s / (ms / 1000), "passes_per_s": 1000 / ms,
+                "gemm_tflops_incl_all_kernels": gemm_flops / (ms / 1000) / 1e12, "open_s": open_s,
+                "finite": bool(np.isfinite(out).all()), "timing": "host wall clock around the API call",
+                "clocks": clk.summary()}
+    print(json.dumps(out_line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -470,11 +523,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3", "load"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3", "load", "openthai"])
     ap.add_argument("--load-cfg", default="cfg3", help="load: synthetic model to open")
     ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
     ap.add_argument("--gen", type=int, default=128, help="decode: generated tokens")
+    ap.add_argument("--ot-tokens", type=int, default=1024, help="openthai: tokens per pass")
     ap.add_argument("--requests", type=int, default=REQUESTS,
                     help="requests per GPU (64 is the benchmark; smaller only for profiler captures)")
     args = ap.parse_args()
@@ -484,6 +538,8 @@ def main():
         run_decode(args)
     elif args.workload == "load":
         run_load(args)
+    elif args.workload == "openthai":
+        run_openthai(args)
     elif args.workload in AUX:
         run_aux(args)
     elif args.impl == "reference":
