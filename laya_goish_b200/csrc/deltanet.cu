@@ -5,75 +5,175 @@
 //   softplus(a + dt_bias)); beta = sigmoid(b)
 //   S = decay * S;  delta = beta * (v - k^T S);  S += k delta^T;  o = q^T S
 //
-// with a per-head state S [key hk][value hk] starting at zero.  One CTA per
-// head, one thread per value column: the thread keeps its column of S in
-// registers (hk floats), so a token costs two passes over the column plus
-// two block reductions (|q|^2, |k|^2).  Tokens are sequential; a chunked
-// (WY-form) scan that runs the token blocks on the tensor cores is the
-// faster form for long prompts.
+// with a per-head state S [key hk][value hk] starting at zero.
+//
+// Two kernels.  delta_prep_kernel does the per-token work that does not
+// depend on S in parallel over (token, head): the two L2 norms (in place in
+// qkv) and decay / beta (in place in a / b).  delta_scan_kernel then runs
+// the token-sequential part.  The value columns of S are independent of one
+// another (delta and o of column c read only column c), so a head's columns
+// are split over HK / 16 CTAs; inside a CTA eight lanes share one column,
+// each holding HK / 8 of its keys in registers, and a token's two key sums
+// are 3-step shuffle trees over those lanes.  Tokens are staged in chunks of
+// 16 in shared memory, double-buffered: the next chunk's loads are issued
+// into registers before the current chunk is processed.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace laya {
 
+namespace delta {
+constexpr int T = 16;   // tokens per staged chunk
+constexpr int CPB = 16; // value columns per CTA
+constexpr int G = 8;    // lanes per column (key groups)
+constexpr int THREADS = CPB * G;
+}  // namespace delta
+
 template <int HK>
-__global__ void __launch_bounds__(HK) gated_delta_kernel(const float* __restrict__ qkv, const float* __restrict__ a,
-                                                         const float* __restrict__ b, const float* __restrict__ dt,
-                                                         const float* __restrict__ alog, int s, int nh,
-                                                         float* __restrict__ out) {
-  constexpr int NW = HK / 32;
-  __shared__ float kk[HK], qq[HK];
-  __shared__ float red[2][NW];
-  const int h = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
-  const int w = nh * HK, C = 3 * w;
-  float S[HK];  // S[j] = state[j][c]
+__global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv, float* __restrict__ a,
+                                                         float* __restrict__ b, const float* __restrict__ dt,
+                                                         const float* __restrict__ alog, int s, int nh) {
+  constexpr int PL = HK / 32;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (gw >= s * nh) return;
+  const int i = gw / nh, h = gw % nh, w = nh * HK;
+  float* q = qkv + (size_t)i * 3 * w + h * HK;
+  float* k = q + w;
+  float qv[PL], kv[PL], q2 = 0.f, k2 = 0.f;
 #pragma unroll
-  for (int j = 0; j < HK; j++) S[j] = 0.f;
-  const float ea = expf(alog[h]), dth = dt[h];
-  for (int i = 0; i < s; i++) {
-    const float* row = qkv + (size_t)i * C;
-    const float q = row[h * HK + c], k = row[w + h * HK + c], v = row[2 * w + h * HK + c];
-    float q2 = q * q, k2 = k * k;
+  for (int u = 0; u < PL; u++) {
+    qv[u] = q[lane + 32 * u];
+    kv[u] = k[lane + 32 * u];
+    q2 += qv[u] * qv[u];
+    k2 += kv[u] * kv[u];
+  }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      q2 += __shfl_xor_sync(0xffffffffu, q2, o);
-      k2 += __shfl_xor_sync(0xffffffffu, k2, o);
-    }
-    if (lane == 0) {
-      red[0][warp] = q2;
-      red[1][warp] = k2;
-    }
-    __syncthreads();
-    float qsum = 0.f, ksum = 0.f;
+  for (int o = 16; o; o >>= 1) {
+    q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+    k2 += __shfl_xor_sync(0xffffffffu, k2, o);
+  }
+  const float qs = 1.f / sqrtf(q2 + 1e-6f) / sqrtf((float)HK);
+  const float ks = 1.f / sqrtf(k2 + 1e-6f);
 #pragma unroll
-    for (int u = 0; u < NW; u++) {
-      qsum += red[0][u];
-      ksum += red[1][u];
-    }
-    const float qs = 1.f / sqrtf(qsum + 1e-6f) / sqrtf((float)HK);
-    const float ks = 1.f / sqrtf(ksum + 1e-6f);
-    const float x = a[(size_t)i * nh + h] + dth;
+  for (int u = 0; u < PL; u++) {
+    q[lane + 32 * u] = qv[u] * qs;
+    k[lane + 32 * u] = kv[u] * ks;
+  }
+  if (lane == 0) {
+    const size_t e = (size_t)i * nh + h;
+    const float x = a[e] + dt[h];
     const float sp = x > 20.f ? x : log1pf(expf(x));
-    const float decay = expf(-ea * sp);
-    const float beta = 1.f / (1.f + expf(-b[(size_t)i * nh + h]));
-    kk[c] = k * ks;
-    qq[c] = q * qs;
+    a[e] = expf(-expf(alog[h]) * sp);
+    b[e] = 1.f / (1.f + expf(-b[e]));
+  }
+}
+
+// Thread (column cl = tid / 8, group g = tid % 8) of CTA (head, column block)
+// holds S[j][c] for its keys j = 32 m + 4 g + r (m < HK / 32, r < 4), so a
+// group's float4 reads of a staged key row are eight consecutive 16-byte
+// words (no bank conflicts).
+template <int HK>
+__global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float* __restrict__ qkv,
+                                                                   const float* __restrict__ dec,
+                                                                   const float* __restrict__ beta, int s, int nh,
+                                                                   float* __restrict__ out) {
+  using namespace delta;
+  constexpr int M = HK / 32;            // float4 words of keys per thread
+  constexpr int QW = T * HK / 4;        // float4 words of one staged q (or k) chunk
+  constexpr int QPT = QW / THREADS;     // ... per thread
+  static_assert(QW % THREADS == 0, "chunk words must divide over the block");
+  constexpr int VW = T * CPB / 4;       // float4 words of the staged v chunk
+  static_assert(VW <= THREADS, "v chunk must fit one word per thread");
+  __shared__ __align__(16) float Qs[2][T][HK];
+  __shared__ __align__(16) float Ks[2][T][HK];
+  __shared__ __align__(16) float Vs[2][T][CPB];
+  __shared__ float Ds[2][T], Bs[2][T];
+  const int tid = threadIdx.x, g = tid % G, cl = tid / G;
+  const int h = blockIdx.x, c0 = blockIdx.y * CPB, w = nh * HK;
+  const size_t C = (size_t)3 * w;
+  float S[4 * M];
+#pragma unroll
+  for (int j = 0; j < 4 * M; j++) S[j] = 0.f;
+
+  float4 rq[QPT], rk[QPT], rv = make_float4(0.f, 0.f, 0.f, 0.f);
+  float rd = 0.f;
+  auto fetch = [&](int i0) {
+#pragma unroll
+    for (int u = 0; u < QPT; u++) {
+      const int idx = tid + u * THREADS, t = idx / (HK / 4), x = idx % (HK / 4), i = i0 + t;
+      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float* row = qkv + (size_t)i * C + h * HK + 4 * x;
+      rq[u] = i < s ? *reinterpret_cast<const float4*>(row) : zero;
+      rk[u] = i < s ? *reinterpret_cast<const float4*>(row + w) : zero;
+    }
+    if (tid < VW) {
+      const int t = tid / (CPB / 4), x = tid % (CPB / 4), i = i0 + t;
+      rv = i < s ? *reinterpret_cast<const float4*>(qkv + (size_t)i * C + 2 * w + h * HK + c0 + 4 * x)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (tid < 2 * T) {
+      const int t = tid % T, i = i0 + t;
+      rd = i < s ? (tid < T ? dec : beta)[(size_t)i * nh + h] : 0.f;
+    }
+  };
+  auto stage = [&](int buf) {
+#pragma unroll
+    for (int u = 0; u < QPT; u++) {
+      const int idx = tid + u * THREADS, t = idx / (HK / 4), x = idx % (HK / 4);
+      reinterpret_cast<float4*>(&Qs[buf][t][0])[x] = rq[u];
+      reinterpret_cast<float4*>(&Ks[buf][t][0])[x] = rk[u];
+    }
+    if (tid < VW) reinterpret_cast<float4*>(&Vs[buf][tid / (CPB / 4)][0])[tid % (CPB / 4)] = rv;
+    if (tid < T) Ds[buf][tid] = rd;
+    else if (tid < 2 * T) Bs[buf][tid - T] = rd;
+  };
+
+  const int nch = (s + T - 1) / T;
+  fetch(0);
+  stage(0);
+  __syncthreads();
+  for (int ch = 0; ch < nch; ch++) {
+    const int buf = ch & 1, i0 = ch * T;
+    if (ch + 1 < nch) fetch(i0 + T);
+    const int tn = min(T, s - i0);
+    for (int t = 0; t < tn; t++) {
+      const float dcy = Ds[buf][t], bt = Bs[buf][t], v = Vs[buf][t][cl];
+      float kk[4 * M];
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float4 k4 = reinterpret_cast<const float4*>(&Ks[buf][t][0])[8 * m + g];
+        kk[4 * m] = k4.x, kk[4 * m + 1] = k4.y, kk[4 * m + 2] = k4.z, kk[4 * m + 3] = k4.w;
+      }
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4 * M; j += 2) {
+        S[j] *= dcy;
+        S[j + 1] *= dcy;
+        d0 += S[j] * kk[j];
+        d1 += S[j + 1] * kk[j + 1];
+      }
+      float dsum = d0 + d1;
+#pragma unroll
+      for (int o = 1; o < G; o <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+      const float delta = (v - dsum) * bt;
+      float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        const float4 q4 = reinterpret_cast<const float4*>(&Qs[buf][t][0])[8 * m + g];
+        S[4 * m] += kk[4 * m] * delta;
+        S[4 * m + 1] += kk[4 * m + 1] * delta;
+        S[4 * m + 2] += kk[4 * m + 2] * delta;
+        S[4 * m + 3] += kk[4 * m + 3] * delta;
+        o0 += S[4 * m] * q4.x + S[4 * m + 2] * q4.z;
+        o1 += S[4 * m + 1] * q4.y + S[4 * m + 3] * q4.w;
+      }
+      float osum = o0 + o1;
+#pragma unroll
+      for (int o = 1; o < G; o <<= 1) osum += __shfl_xor_sync(0xffffffffu, osum, o);
+      if (g == 0) out[(size_t)(i0 + t) * w + h * HK + c0 + cl] = osum;
+    }
+    if (ch + 1 < nch) stage(buf ^ 1);
     __syncthreads();
-    float delta = 0.f;
-#pragma unroll
-    for (int j = 0; j < HK; j++) {
-      S[j] *= decay;
-      delta += S[j] * kk[j];
-    }
-    delta = (v - delta) * beta;
-    float o = 0.f;
-#pragma unroll
-    for (int j = 0; j < HK; j++) {
-      S[j] += kk[j] * delta;
-      o += S[j] * qq[j];
-    }
-    out[(size_t)i * w + h * HK + c] = o;
-    __syncthreads();  // kk, qq and red are rewritten by the next token
   }
 }
 
@@ -118,7 +218,7 @@ __global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict_
   }
 }
 
-cudaError_t gated_delta_mixer(const float* raw, const float* z, const float* a, const float* b, const float* conv,
+cudaError_t gated_delta_mixer(const float* raw, const float* z, float* a, float* b, const float* conv,
                               const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
                               float* qkv_scratch, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
@@ -135,16 +235,19 @@ cudaError_t gated_delta_mixer(const float* raw, const float* z, const float* a, 
   return cudaGetLastError();
 }
 
-cudaError_t gated_delta(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
-                        int nh, int hk, float* out, cudaStream_t st) {
+cudaError_t gated_delta(float* qkv, float* a, float* b, const float* dt, const float* alog, int s, int nh, int hk,
+                        float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
-  if (nh < 1) return cudaErrorInvalidValue;
-  if (hk == 128)
-    gated_delta_kernel<128><<<nh, 128, 0, st>>>(qkv, a, b, dt, alog, s, nh, out);
-  else if (hk == 64)
-    gated_delta_kernel<64><<<nh, 64, 0, st>>>(qkv, a, b, dt, alog, s, nh, out);
-  else
-    return cudaErrorInvalidValue;
+  if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
+  const unsigned prep_blocks = (unsigned)(((size_t)s * nh + 7) / 8);
+  const dim3 grid(nh, hk / delta::CPB);
+  if (hk == 128) {
+    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, dt, alog, s, nh);
+    delta_scan_kernel<128><<<grid, delta::THREADS, 0, st>>>(qkv, a, b, s, nh, out);
+  } else {
+    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, dt, alog, s, nh);
+    delta_scan_kernel<64><<<grid, delta::THREADS, 0, st>>>(qkv, a, b, s, nh, out);
+  }
   return cudaGetLastError();
 }
 

@@ -53,14 +53,15 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
 // (rows null) the merged rows are also written back to x.
 // Gated DeltaNet recurrence (deltanet.cu): qkv [s][3 nh hk] after the
 // convolution and SiLU, a / b [s][nh], dt / A_log [nh] -> out [s][nh hk]
-// (hk 64 or 128).  All device pointers.
-cudaError_t gated_delta(const float* qkv, const float* a, const float* b, const float* dt, const float* alog, int s,
-                        int nh, int hk, float* out, cudaStream_t st);
+// (hk 64 or 128).  All device pointers.  Works in place: q and k of qkv are
+// overwritten with their normalised values, a with the decay and b with beta.
+cudaError_t gated_delta(float* qkv, float* a, float* b, const float* dt, const float* alog, int s, int nh, int hk,
+                        float* out, cudaStream_t st);
 // The DeltaNet mixer after its projections (deltanet.cu): raw [s][3 nh hk]
-// from in_proj_qkv, z [s][nh hk], a / b [s][nh], conv [3 nh hk][4], dt /
-// A_log [nh], norm weight [hk] -> out [s][nh hk] before out_proj;
-// qkv_scratch holds s * 3 * nh * hk floats.
-cudaError_t gated_delta_mixer(const float* raw, const float* z, const float* a, const float* b, const float* conv,
+// from in_proj_qkv, z [s][nh hk], a / b [s][nh] (overwritten, as above),
+// conv [3 nh hk][4], dt / A_log [nh], norm weight [hk] -> out [s][nh hk]
+// before out_proj; qkv_scratch holds s * 3 * nh * hk floats.
+cudaError_t gated_delta_mixer(const float* raw, const float* z, float* a, float* b, const float* conv,
                               const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
                               float* qkv_scratch, float* out, cudaStream_t st);
 // Gated full attention after the projections (gated_attn.cu): qgate
