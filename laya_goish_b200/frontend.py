@@ -40,6 +40,11 @@ with its `legend`, `noul`, `confidence`, `probabilities` by label; `logits`
 when raw).  The Laya encoder's `action` head is not part of this path.
 Authentication, presets, the model registry and draining are not part of it
 either.
+
+An OpenThai GGUF (`general.architecture` "openthai_systemone",
+src/models/mod.rs:64-70) is served by `OpenThaiService` over the same routes:
+its requests and answer objects are OpenThai's own
+(src/models/openthai/decision.rs), one `openthai.Model.respond` per state.
 """
 from __future__ import annotations
 
@@ -226,7 +231,9 @@ class DecideService:
             req = json.loads(body or b"")
         except (ValueError, UnicodeDecodeError) as e:
             return _error(400, "invalid_request_error", str(e))
-        batch = path == "/v1/decide/batch"
+        return self._decide(req, path == "/v1/decide/batch", canceled)
+
+    def _decide(self, req, batch: bool, canceled) -> Response:
         # Validate the whole batch before starting any expensive work.
         try:
             if batch:
@@ -270,6 +277,64 @@ class DecideService:
                             "usage": {"tokens": tokens}})
         body = {"results": results} if batch else results[0]
         return Response(200, body, {"X-Response-Time-Ms": str(ms)})
+
+
+class OpenThaiService(DecideService):
+    """The same routes over an OpenThai model (`openthai.Model`), whose
+    requests keep OpenThai's own shape (decision.rs:20-109): `state` is text
+    or any JSON object / array written into the prompt, questions carry
+    `instructions` and `criteria`, plus `order_invariant` / `permutations`.
+    Each request (each state of a batch, with the shared questions and
+    options, src/server.rs:235-258) is validated through every permutation
+    pass before any runs, then answered by one `Model.respond`; the answer
+    objects are the model's own (model, answers, usage, id, _raw)."""
+
+    def __init__(self, model, tokenizer, raw: bool = False):
+        if tokenizer is None:
+            raise ValueError("an OpenThai model needs its tokenizer")
+        super().__init__(model, raw=raw, tokenizer=tokenizer)
+
+    def _decide(self, req, batch: bool, canceled) -> Response:
+        from .openthai import OpenThaiError
+
+        try:
+            if not isinstance(req, dict):
+                raise RequestError("request body must be a JSON object")
+            if batch:
+                states = req.get("states")
+                if not isinstance(states, list) or not 1 <= len(states) <= MAX_STATES:
+                    raise RequestError("states must be an array of 1..256 states")
+                reqs = [{"state": st, "questions": req.get("questions"), "model": req.get("model"),
+                         "order_invariant": req.get("order_invariant"), "permutations": req.get("permutations")}
+                        for st in states]
+            else:
+                reqs = [req]
+            count = 0
+            for r in reqs:
+                if r.get("state") is None:
+                    raise RequestError("state is required")
+                self.engine.validate(self.tokenizer, r)
+                count += len(r["questions"])
+            if count > MAX_QUESTIONS:
+                raise RequestError("At most 256 total questions per request")
+        except (RequestError, OpenThaiError) as e:
+            return _error(422, "invalid_request_error", str(e))
+        if not self._busy.acquire(blocking=False):
+            return _error(429, "busy_error", "An inference request is running; retry later", {"Retry-After": "1"})
+        try:
+            start = time.perf_counter()
+            results = []
+            for r in reqs:
+                try:
+                    results.append(self.engine.respond(self.tokenizer, r, self.raw, canceled))
+                except LayaError as e:
+                    if e.code == E_CANCELED:
+                        return _error(408, "request_canceled", e.message)
+                    return _error(500, "internal_error", e.message)
+            ms = int((time.perf_counter() - start) * 1000)
+        finally:
+            self._busy.release()
+        return Response(200, {"results": results} if batch else results[0], {"X-Response-Time-Ms": str(ms)})
 
 
 def run_daemon(service: DecideService, inp=None, out=None) -> None:
@@ -343,12 +408,21 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     from .tokenizer import Tokenizer
 
+    from .gguf_meta import read_metadata
+
     try:
         tok = Tokenizer.from_gguf(a.model)
     except ValueError:
         tok = None  # no usable vocabulary in the file: token-id requests only
-    eng = Engine(a.model, devices=[int(d) for d in a.devices.split(",")])
-    svc = DecideService(eng, raw=a.raw, tokenizer=tok)
+    devices = [int(d) for d in a.devices.split(",")]
+    if read_metadata(a.model).get("general.architecture") == "openthai_systemone":
+        from .openthai import Model
+
+        eng = Model(a.model, device=devices[0])
+        svc = OpenThaiService(eng, tok, raw=a.raw)
+    else:
+        eng = Engine(a.model, devices=devices)
+        svc = DecideService(eng, raw=a.raw, tokenizer=tok)
     if a.mode == "daemon":
         run_daemon(svc)
     else:

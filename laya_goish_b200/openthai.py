@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import json
 import math
+import time
 
 import numpy as np
 
@@ -394,14 +395,58 @@ class Model:
                                                     out.ctypes.data_as(ctypes.c_void_p)))
         return out
 
-    def decide(self, tok, req: dict) -> dict:
-        """Model::decide (decision.rs:70-120): every permutation pass of the
-        request through the forward, then the calibrated slot decoding."""
+    info = {"architecture": "openthai_systemone"}
+
+    def layers(self) -> int:
+        return len(self.config["layer_types"])
+
+    def _encode(self, tok, req, qs, n, p) -> Encoded:
+        c = self.config
+        return encode(tok, req, qs, n, p, c["answer_token_id"], c["max_tokens"], c["max_state"])
+
+    def validate(self, tok, req: dict) -> None:
+        """validate (decision.rs:234-242): the questions, then every
+        permutation pass's prompt against the context budget (option order
+        can change the token count)."""
         qs = questions(req)
         n = permutation_count(req, qs)
-        c = self.config
-        passes = []
         for p in range(n):
-            e = encode(tok, req, qs, n, p, c["answer_token_id"], c["max_tokens"], c["max_state"])
-            passes.append((self.forward(e.ids, e.positions), e.order))
-        return decide(qs, passes, self.temperature)
+            self._encode(tok, req, qs, n, p)
+
+    def respond(self, tok, req: dict, raw: bool = False, canceled=None) -> dict:
+        """decide (decision.rs:243-390): every permutation pass through the
+        forward, the calibrated slot decoding, and the result object: model,
+        answers, usage (input tokens of the first pass, permutations, whether
+        the state was truncated, latency), the request's `id` if it has one,
+        and with `raw` each pass's input ids, answer positions and logits.
+        `canceled()` is polled before each pass (LayaError E_CANCELED)."""
+        from ._lib import E_CANCELED, LayaError
+
+        start = time.perf_counter()
+        qs = questions(req)
+        n = permutation_count(req, qs)
+        passes, debug, tokens, truncated = [], [], 0, False
+        for p in range(n):
+            if canceled is not None and canceled():
+                raise LayaError(E_CANCELED, "request canceled")
+            e = self._encode(tok, req, qs, n, p)
+            if p == 0:
+                tokens = len(e.ids)
+            truncated |= e.truncated
+            logits = self.forward(e.ids, e.positions)
+            passes.append((logits, e.order))
+            if raw:
+                debug.append({"input_ids": [int(v) for v in e.ids], "answer_positions": [int(v) for v in e.positions],
+                              "logits": [float(v) for v in logits.reshape(-1)]})
+        out = {"model": "openthai-systemone", "answers": decide(qs, passes, self.temperature),
+               "usage": {"input_tokens": tokens, "output_tokens": 0, "permutations": n,
+                         "truncated_state": truncated, "latency_ms": int((time.perf_counter() - start) * 1000)}}
+        if req.get("id") is not None:
+            out["id"] = req["id"]
+        if raw:
+            out["_raw"] = debug
+        return out
+
+    def decide(self, tok, req: dict) -> dict:
+        """The answers of `respond`: {question id: answer}."""
+        return self.respond(tok, req)["answers"]
