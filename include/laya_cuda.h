@@ -174,6 +174,10 @@ typedef struct laya_ot_config {
 } laya_ot_config;
 typedef struct laya_ot_model laya_ot_model;
 int laya_openthai_open(const char* path, int device, const laya_ot_config* cfg, laya_ot_model** out);
+/* The same from a GGUF image in memory (the bytes of the reference's mapped
+ * `Gguf`); the image is read during this call only. */
+int laya_openthai_open_memory(const uint8_t* gguf, size_t len, int device, const laya_ot_config* cfg,
+                              laya_ot_model** out);
 /* Model::forward for one encoded pass: the slot logits (slot head + bias) at
  * the given positions -> out [npos][slots] (host buffers). */
 int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int32_t* positions, int npos,

@@ -126,7 +126,7 @@ int upload_gate_up(Model& m, const Gguf& g, const std::string& p, int ffn, int d
   return 0;
 }
 
-int load(Model& m, const Gguf& g) {
+int load(Model& m, const Gguf& g, const uint8_t* layer_full) {
   const laya_ot_config& c = m.cfg;
   const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
   const int w = nh * hk;
@@ -147,7 +147,7 @@ int load(Model& m, const Gguf& g) {
   for (int l = 0; l < c.n_layers; l++) {
     OtLayer& L = m.layers[l];
     const std::string p = "model.layers." + std::to_string(l);
-    L.full = c.layer_full[l] != 0;
+    L.full = layer_full[l] != 0;
     if ((rc = upload_vec(m, g, p + ".input_layernorm.weight", d, 1.f, &L.n1)) ||
         (rc = upload_vec(m, g, p + ".post_attention_layernorm.weight", d, 1.f, &L.n2)) ||
         (rc = upload_gate_up(m, g, p, c.ffn, d, &L.gu)) ||
@@ -201,6 +201,36 @@ int gemm(Model& m, int epi, const half* A, int lda, const half* B, int N, int K,
   return 0;
 }
 
+int check_shape(const laya_ot_config& c) {
+  if (c.d < 32 || c.d % 32 || c.ffn < 128 || c.ffn % 128 || c.heads < 1 || c.kv_heads < 1 || c.heads % c.kv_heads ||
+      (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) || c.rot < 0 || c.rot > c.head_dim ||
+      c.rot % 2 || c.lin_heads < 1 || (c.lin_dim != 64 && c.lin_dim != 128) || c.vocab < 1 || c.slots < 1 ||
+      c.n_layers < 1 || c.n_layers > 256)
+    return fail(LAYA_E_INVALID, "unsupported OpenThai shape for the GPU forward");
+  return 0;
+}
+
+// The model on `device` from a parsed GGUF (the tensors are read from it
+// during this call only).
+int open_parsed(const Gguf& g, int device, const laya_ot_config& c, laya_ot_model** out) {
+  auto m = std::make_unique<laya_ot_model>();
+  m->cfg = c;
+  m->cfg.layer_full = nullptr;  // read only here: the flags go into the layers
+  m->device = device;
+  LAYA_CK(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  LAYA_CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(LAYA_E_CUDA, "not an sm_100 GPU");
+  m->num_sms = prop.multiProcessorCount;
+  LAYA_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
+  if (int rc = load(*m, g, c.layer_full)) {
+    laya_openthai_close(m.release());
+    return rc;
+  }
+  *out = m.release();
+  return 0;
+}
+
 }  // namespace
 }  // namespace laya
 
@@ -211,34 +241,22 @@ extern "C" {
 int laya_openthai_open(const char* path, int device, const laya_ot_config* cfg, laya_ot_model** out) {
   if (!path || !cfg || !out || !cfg->layer_full) return fail(LAYA_E_INVALID, "null argument");
   *out = nullptr;
-  const laya_ot_config& c = *cfg;
-  if (c.d < 32 || c.d % 32 || c.ffn < 128 || c.ffn % 128 || c.heads < 1 || c.kv_heads < 1 || c.heads % c.kv_heads ||
-      (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) || c.rot < 0 || c.rot > c.head_dim ||
-      c.rot % 2 || c.lin_heads < 1 || (c.lin_dim != 64 && c.lin_dim != 128) || c.vocab < 1 || c.slots < 1 ||
-      c.n_layers < 1 || c.n_layers > 256)
-    return fail(LAYA_E_INVALID, "unsupported OpenThai shape for the GPU forward");
+  if (int rc = check_shape(*cfg)) return rc;
   Gguf g;
   std::string e = g.open_file(path);
   if (!e.empty()) return fail(g.bytes() ? LAYA_E_FORMAT : LAYA_E_IO, e);
-  auto m = std::make_unique<laya_ot_model>();
-  m->cfg = c;
-  m->cfg.layer_full = nullptr;  // not kept: copied into the layers
-  m->device = device;
-  LAYA_CK(cudaSetDevice(device));
-  cudaDeviceProp prop;
-  LAYA_CK(cudaGetDeviceProperties(&prop, device));
-  if (prop.major != 10) return fail(LAYA_E_CUDA, "not an sm_100 GPU");
-  m->num_sms = prop.multiProcessorCount;
-  LAYA_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
-  m->cfg.layer_full = c.layer_full;
-  int rc = load(*m, g);
-  m->cfg.layer_full = nullptr;
-  if (rc) {
-    laya_openthai_close(m.release());
-    return rc;
-  }
-  *out = m.release();
-  return 0;
+  return open_parsed(g, device, *cfg, out);
+}
+
+int laya_openthai_open_memory(const uint8_t* gguf, size_t len, int device, const laya_ot_config* cfg,
+                              laya_ot_model** out) {
+  if (!gguf || !cfg || !out || !cfg->layer_full) return fail(LAYA_E_INVALID, "null argument");
+  *out = nullptr;
+  if (int rc = check_shape(*cfg)) return rc;
+  Gguf g;
+  std::string e = g.open_memory(gguf, len);
+  if (!e.empty()) return fail(LAYA_E_FORMAT, e);
+  return open_parsed(g, device, *cfg, out);
 }
 
 int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int32_t* positions, int npos,

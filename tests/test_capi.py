@@ -51,5 +51,10 @@ def test_openthai_entry_points_reject_bad_arguments():
     assert L.laya_openthai_open(b"/nonexistent.gguf", 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_INVALID
     assert b"unsupported OpenThai shape" in L.laya_last_error() and not h.value
     assert L.laya_openthai_open(b"x", 0, None, ctypes.byref(h)) == _lib.E_INVALID
+    img = b"GGUF" + bytes(60)
+    assert L.laya_openthai_open_memory(img, len(img), 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_INVALID
+    cfg.head_dim = 64
+    assert L.laya_openthai_open_memory(img, 8, 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_FORMAT
+    assert L.laya_openthai_open_memory(None, 0, 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_INVALID
     assert L.laya_openthai_forward(None, None, 0, None, 0, None) == _lib.E_INVALID
     L.laya_openthai_close(None)
