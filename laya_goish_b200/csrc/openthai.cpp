@@ -47,6 +47,8 @@ struct laya_ot_model {
   const float* head_bias = nullptr;
   unsigned* err = nullptr;
   std::vector<void*> allocs;
+  // forward scratch, grown on demand and kept between passes
+  laya::DevBuf dids, dpos, x, h, big, k, v, att, att16, act, logits;
   std::mutex mu;
 };
 
@@ -273,13 +275,8 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
   const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
   const int w = nh * hk, qd = H * hd, ffn = c.ffn;
   const size_t S = (size_t)s;
-  DevBuf dids, dpos, x, h, big, k, v, att, att16, act, logits;
-  struct Release {
-    std::vector<DevBuf*> b;
-    ~Release() {
-      for (DevBuf* p : b) p->release();
-    }
-  } rel{{&dids, &dpos, &x, &h, &big, &k, &v, &att, &att16, &act, &logits}};
+  DevBuf &dids = m->dids, &dpos = m->dpos, &x = m->x, &h = m->h, &big = m->big, &k = m->k, &v = m->v,
+         &att = m->att, &att16 = m->att16, &act = m->act, &logits = m->logits;
   // big: the largest projection output (2 qd, 3w) plus the mixers' scratch
   const size_t bigf = S * (size_t)std::max(2 * qd, 3 * w) + S * (size_t)std::max(qd + KV * hd, 3 * w) + S * 2 * w;
   int rc;
@@ -346,6 +343,8 @@ void laya_openthai_close(laya_ot_model* m) {
   cudaSetDevice(m->device);
   if (m->st) cudaStreamSynchronize(m->st);
   for (void* p : m->allocs) cudaFree(p);
+  for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->k, &m->v, &m->att, &m->att16, &m->act, &m->logits})
+    b->release();
   if (m->st) cudaStreamDestroy(m->st);
   delete m;
 }
