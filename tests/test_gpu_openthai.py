@@ -105,7 +105,7 @@ def test_openthai_forward_matches_oracle(ot_model):
     full = m.forward(ids, [20])
     head = m.forward(ids[:21], [20])
     assert np.allclose(full, head, atol=1e-4, rtol=1e-4)
-    # a repeated request after a different (longer) one is bitwise identical:
+    # a repeated request after a different one is bitwise identical:
     # no state survives a pass in the reused scratch (validation/openthai_edges.py)
     assert np.array_equal(m.forward(ids, [20]), full)
     with pytest.raises(LayaError):
