@@ -1,7 +1,10 @@
-"""OpenThai's gated DeltaNet recurrence on the GPU (laya_gated_delta) against
-the oracle's restatement of Delta::run (src/models/openthai/model.rs:322-355).
-Parity with the reference itself is unpinned (its goldens need the real
-OpenThai weights)."""
+"""OpenThai on the GPU against the oracle's restatement of
+src/models/openthai/model.rs: the gated DeltaNet recurrence
+(laya_gated_delta, Delta::run 322-355) and its whole mixer after the
+projections, the gated attention (Full::run 248-296), the native forward
+(laya_openthai_forward, Model::forward 192-241) and a whole decision through
+it.  Parity of the forward with the reference itself is unpinned (its
+goldens need the real OpenThai weights)."""
 import numpy as np
 import pytest
 
