@@ -463,6 +463,24 @@ def run_load(args):
     print(json.dumps(out), flush=True)
 
 
+def openthai_cpu_baseline(path: str, tokens: int) -> dict:
+    """The oracle's OpenThai forward (C mixers and Matrix::apply in the
+    reference's loop order, all host threads) on a bounded sample: one pass of
+    `tokens` tokens through the same model, timed once after reading the
+    weights."""
+    import oracle
+    from laya_goish_b200 import openthai
+
+    threads = os.cpu_count() or 1
+    w = openthai.load_weights(path, strict=False)
+    ids = np.random.default_rng(2).integers(0, 4096, tokens)
+    t0 = time.perf_counter()
+    oracle.ot_forward(w, ids, [tokens - 1], threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one {tokens}-token pass, {dt:.1f} s"}
+
+
 def run_openthai(args):
     """OpenThai forward on one GPU at the reference's widths (d 1024, FFN
     3584, 24 layers: 18 gated DeltaNet layers of 16 x 128 heads and 6 gated
@@ -488,6 +506,7 @@ def run_openthai(args):
         t0 = time.perf_counter()
         m = openthai.Model(path, device=local, strict=False)
         open_s = time.perf_counter() - t0
+        cpu = None if args.no_cpu_baseline else openthai_cpu_baseline(path, args.ot_cpu_tokens)
     ids = np.random.default_rng(2).integers(0, 4096, s)
     pos = [s - 201, s - 101, s - 1] if s > 201 else [s - 1]
     for _ in range(args.warmup):
@@ -512,7 +531,7 @@ def run_openthai(args):
                 "ms_per_pass": ms, "tokens_per_s": s / (ms / 1000), "passes_per_s": 1000 / ms,
                 "gemm_tflops_incl_all_kernels": gemm_flops / (ms / 1000) / 1e12, "open_s": open_s,
                 "finite": bool(np.isfinite(out).all()), "timing": "host wall clock around the API call",
-                "clocks": clk.summary()}
+                "cpu_baseline": cpu, "clocks": clk.summary()}
     print(json.dumps(out_line), flush=True)
 
 
@@ -529,6 +548,7 @@ def main():
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
     ap.add_argument("--gen", type=int, default=128, help="decode: generated tokens")
     ap.add_argument("--ot-tokens", type=int, default=1024, help="openthai: tokens per pass")
+    ap.add_argument("--ot-cpu-tokens", type=int, default=128, help="openthai: tokens of the CPU baseline pass")
     ap.add_argument("--requests", type=int, default=REQUESTS,
                     help="requests per GPU (64 is the benchmark; smaller only for profiler captures)")
     args = ap.parse_args()
