@@ -5,10 +5,14 @@ calling one batched `Engine.decide_batch` (laya_decide_batch) per request.
 
 What is kept from the reference, in the same order:
 
-* routes and methods: unknown path -> 404 `not_found_error`; wrong method ->
-  405 with `Allow` (src/server.rs:82-95);
-* the body must parse as JSON (400) and be an object with a `state`
-  (422, src/server.rs:65-75, 221-227);
+* routes and methods: `/`, `/health` (status, model, busy, layers),
+  `/v1/models` (the one loaded model), `/v1/systemone` = `/v1/decide`,
+  `/v1/decide/batch`; unknown path -> 404 `not_found_error`; wrong method ->
+  405 with `Allow` (src/server.rs:82-158);
+* POST bodies: Content-Type must be application/json (415), at most 1 MiB,
+  fixed-length or chunked (413), UTF-8 JSON without repeated object keys
+  (400), an object whose optional `model` names the loaded model and which
+  has a `state` (422, src/server.rs:65-75, 175-233, src/registry.rs:58-73);
 * `/v1/decide/batch`: `states` is an array of 1..256 states sharing
   `questions` (src/server.rs:235-258);
 * the whole batch is validated before any work starts, the first failure is
@@ -62,7 +66,31 @@ MAX_QUESTIONS = 256
 MAX_OPTIONS = 16
 MAX_BODY = 1024 * 1024  # src/server.rs:22
 
-ROUTES = {"/health": "GET, HEAD", "/v1/decide": "POST", "/v1/decide/batch": "POST"}
+# src/server.rs:82-89; /v1/systemone is the reference's other name for /v1/decide
+ROUTES = {"/": "GET, HEAD", "/health": "GET, HEAD", "/v1/models": "GET, HEAD", "/v1/systemone": "POST",
+          "/v1/decide": "POST", "/v1/decide/batch": "POST"}
+
+
+def _no_duplicate_keys(pairs):
+    """JSON objects with a repeated key are rejected (400), as the
+    reference's parser does."""
+    out = {}
+    for k, v in pairs:
+        if k in out:
+            raise ValueError(f"duplicate object key {k}")
+        out[k] = v
+    return out
+
+
+def parse_body(body: bytes | str | None):
+    """The request body as JSON: UTF-8 text, no repeated object keys
+    (src/server.rs:214-227); ValueError with the message of the 400."""
+    if isinstance(body, (bytes, bytearray)):
+        try:
+            body = bytes(body).decode("utf-8")
+        except UnicodeDecodeError:
+            raise ValueError("Request body is not UTF-8") from None
+    return json.loads(body or "", object_pairs_hook=_no_duplicate_keys)
 
 
 class RequestError(ValueError):
@@ -193,13 +221,40 @@ class DecideService:
     """The server's request handling around one loaded Engine (or any object
     with the same `validate` / `decide_batch` / `info` interface)."""
 
-    def __init__(self, engine, raw: bool = False, tokenizer=None):
+    def __init__(self, engine, raw: bool = False, tokenizer=None, name: str | None = None,
+                 family: str | None = None):
         self.engine = engine
         self.raw = raw
         self.tokenizer = tokenizer
+        self.name = name or str(engine.info.get("architecture"))
+        self.family = family or self.name
         self._busy = threading.Lock()
         self._requests = 0
         self._count_lock = threading.Lock()
+
+    def _select(self, req) -> None:
+        """The request's optional `model` must name the loaded model
+        (src/registry.rs:58-73, one model loaded)."""
+        if not isinstance(req, dict):
+            raise RequestError("request body must be a JSON object")
+        m = req.get("model")
+        if m is None:
+            return
+        if not isinstance(m, str):
+            raise RequestError("model must be a string naming a loaded model")
+        if m != self.name:
+            raise RequestError(f"unknown model {m}; see /v1/models")
+
+    def _info(self, path: str) -> Response:
+        if path == "/":
+            return Response(200, {"service": "laya-goish B200", "health": "/health", "decide": "/v1/systemone"})
+        if path == "/v1/models":
+            return Response(200, {"models": [{
+                "name": self.name, "canonical_name": self.name, "architecture": str(self.engine.info.get("architecture")),
+                "family": self.family, "default": True,
+                "description": f"Locally loaded {self.name} decision model on B200"}]})
+        return Response(200, {"status": "ok", "model": self.name, "family": self.family, "device": "cuda",
+                              "models": [self.name], "busy": self._busy.locked(), "layers": self.engine.layers()})
 
     def _prepare(self, req) -> tuple[list[list[int]], list[ParsedQuestion]]:
         if not isinstance(req, dict):
@@ -209,28 +264,37 @@ class DecideService:
         return [state_ids(req["state"], self.tokenizer)], parse_questions(req.get("questions"), self.tokenizer)
 
     def handle(self, method: str, path: str, body: bytes | str | None,
-               canceled: Callable[[], bool] | None = None) -> Response:
+               canceled: Callable[[], bool] | None = None,
+               content_type: str | None = "application/json") -> Response:
+        """One request.  `content_type` is the request's Content-Type header
+        (callers without headers, like the daemon, keep the default)."""
         with self._count_lock:
             self._requests += 1
             rid = self._requests
-        r = self._handle(method, path, body, canceled)
+        r = self._handle(method, path, body, canceled, content_type)
         r.headers.setdefault("X-Request-Id", f"laya-{rid}")
         return r
 
-    def _handle(self, method, path, body, canceled) -> Response:
+    def _handle(self, method, path, body, canceled, content_type) -> Response:
         allowed = ROUTES.get(path)
         if allowed is None:
             return _error(404, "not_found_error", "Endpoint not found")
         if (allowed == "POST") != (method == "POST") or (allowed != "POST" and method not in ("GET", "HEAD")):
             return _error(405, "invalid_request_error", "Method not allowed", {"Allow": allowed})
-        if path == "/health":
-            return Response(200, {"status": "ok", "layers": self.engine.layers()})
+        if allowed != "POST":
+            return self._info(path)
+        if (content_type or "").split(";")[0].strip().lower() != "application/json":
+            return _error(415, "invalid_request_error", "Content-Type must be application/json")
         if body is not None and len(body) > MAX_BODY:
-            return _error(413, "invalid_request_error", "request body too large")
+            return _error(413, "invalid_request_error", "Request body exceeds 1 MiB")
         try:
-            req = json.loads(body or b"")
-        except (ValueError, UnicodeDecodeError) as e:
+            req = parse_body(body)
+        except ValueError as e:
             return _error(400, "invalid_request_error", str(e))
+        try:
+            self._select(req)
+        except RequestError as e:
+            return _error(422, "invalid_request_error", str(e))
         return self._decide(req, path == "/v1/decide/batch", canceled)
 
     def _decide(self, req, batch: bool, canceled) -> Response:
@@ -292,7 +356,8 @@ class OpenThaiService(DecideService):
     def __init__(self, model, tokenizer, raw: bool = False):
         if tokenizer is None:
             raise ValueError("an OpenThai model needs its tokenizer")
-        super().__init__(model, raw=raw, tokenizer=tokenizer)
+        super().__init__(model, raw=raw, tokenizer=tokenizer, name="openthai-systemone",
+                         family="openthai-systemone")
 
     def _decide(self, req, batch: bool, canceled) -> Response:
         from .openthai import OpenThaiError
@@ -359,13 +424,38 @@ def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 808
     class Handler(BaseHTTPRequestHandler):
         protocol_version = "HTTP/1.1"
 
-        def _go(self, method):
+        def _body(self):
+            """The request body (Content-Length or chunked), None past 1 MiB
+            or when it cannot be read."""
+            if "chunked" in (self.headers.get("Transfer-Encoding") or "").lower():
+                out = bytearray()
+                while True:
+                    line = self.rfile.readline(64)
+                    try:
+                        n = int(line.split(b";")[0].strip() or b"x", 16)
+                    except ValueError:
+                        return None
+                    if n == 0:
+                        while self.rfile.readline(1024) not in (b"\r\n", b"\n", b""):
+                            pass  # trailers
+                        return bytes(out)
+                    if len(out) + n > MAX_BODY:
+                        return None
+                    out += self.rfile.read(n)
+                    self.rfile.readline(8)  # the chunk's CRLF
             n = int(self.headers.get("Content-Length") or 0)
             if n > MAX_BODY:
-                r = _error(413, "invalid_request_error", "request body too large")
+                return None
+            return self.rfile.read(n) if n else b""
+
+        def _go(self, method):
+            body = self._body() if method == "POST" else b""
+            if body is None:
+                self.close_connection = True
+                r = _error(413, "invalid_request_error", "Request body exceeds 1 MiB or could not be read")
             else:
-                body = self.rfile.read(n) if n else b""
-                r = service.handle(method, self.path.split("?", 1)[0], body)
+                r = service.handle(method, self.path.split("?", 1)[0], body,
+                                   content_type=self.headers.get("Content-Type"))
             data = r.json().encode()
             self.send_response(r.status)
             self.send_header("Content-Type", "application/json; charset=utf-8")

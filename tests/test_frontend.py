@@ -182,7 +182,7 @@ def test_http_round_trip():
     try:
         url = f"http://127.0.0.1:{srv.server_address[1]}"
         req = urllib.request.Request(url + "/v1/decide/batch", data=body(states=[[1], [2]], questions=CHOICE),
-                                     method="POST")
+                                     method="POST", headers={"Content-Type": "application/json; charset=utf-8"})
         with urllib.request.urlopen(req, timeout=10) as r:
             assert r.status == 200
             assert r.headers["Content-Type"].startswith("application/json")
@@ -190,9 +190,79 @@ def test_http_round_trip():
         with pytest.raises(urllib.error.HTTPError) as e:
             urllib.request.urlopen(url + "/missing", timeout=10)
         assert e.value.code == 404
+        # no JSON content type: 415 (src/server.rs:175-189)
+        with pytest.raises(urllib.error.HTTPError) as e:
+            urllib.request.urlopen(urllib.request.Request(url + "/v1/decide", data=b"{}", method="POST"), timeout=10)
+        assert e.value.code == 415
     finally:
         srv.shutdown()
         srv.server_close()
+
+
+def _raw_http(port, head: bytes, chunks) -> tuple[int, dict]:
+    import socket
+
+    with socket.create_connection(("127.0.0.1", port), timeout=10) as c:
+        c.sendall(head)
+        for ch in chunks:
+            c.sendall(b"%x\r\n" % len(ch) + ch + b"\r\n")
+        c.sendall(b"0\r\n\r\n")
+        data = b""
+        while b"\r\n\r\n" not in data:
+            data += c.recv(65536)
+        h, rest = data.split(b"\r\n\r\n", 1)
+        n = int([x for x in h.split(b"\r\n") if x.lower().startswith(b"content-length")][0].split(b":")[1])
+        while len(rest) < n:
+            rest += c.recv(65536)
+    return int(h.split(b" ")[1]), json.loads(rest[:n])
+
+
+def test_http_chunked_bodies():
+    srv = frontend.make_server(frontend.DecideService(FakeEngine()), "127.0.0.1", 0)
+    th = threading.Thread(target=srv.serve_forever, daemon=True)
+    th.start()
+    try:
+        port = srv.server_address[1]
+        head = (b"POST /v1/decide HTTP/1.1\r\nHost: x\r\nContent-Type: application/json\r\n"
+                b"Transfer-Encoding: chunked\r\nConnection: close\r\n\r\n")
+        b = body(state=[1, 2], questions=CHOICE)
+        status, out = _raw_http(port, head, [b[:17], b[17:]])
+        assert status == 200 and set(out["answers"]["pick"]["probabilities"]) == {"a", "b", "c"}
+        status, out = _raw_http(port, head, [b"x" * 600000, b"x" * 600000])
+        assert status == 413 and "1 MiB" in out["error"]["message"]
+    finally:
+        srv.shutdown()
+        srv.server_close()
+
+
+def test_reference_routes_and_request_checks():
+    eng = FakeEngine()
+    s = frontend.DecideService(eng)
+    h = s.handle("GET", "/health", None).body
+    assert h["model"] == "llama" and h["busy"] is False and h["models"] == ["llama"] and h["layers"] == 2
+    assert s.handle("GET", "/", None).body["decide"] == "/v1/systemone"
+    m = s.handle("GET", "/v1/models", None).body["models"]
+    assert [x["name"] for x in m] == ["llama"] and m[0]["default"] is True
+    assert s.handle("HEAD", "/v1/models", None).status == 200
+    assert s.handle("POST", "/v1/presets", b"{}").status == 404  # presets are not served
+    # /v1/systemone is /v1/decide
+    a = s.handle("POST", "/v1/systemone", body(state=[1, 2], questions=CHOICE))
+    b = s.handle("POST", "/v1/decide", body(state=[1, 2], questions=CHOICE))
+    assert a.status == b.status == 200 and a.body == b.body
+    # 415, 400 (not UTF-8, repeated key), 422 (model selection)
+    assert s.handle("POST", "/v1/decide", b"{}", content_type="text/plain").status == 415
+    assert s.handle("POST", "/v1/decide", b"{}", content_type=None).status == 415
+    r = s.handle("POST", "/v1/decide", b'{"state": "\xff"}')
+    assert r.status == 400 and "UTF-8" in r.body["error"]["message"]
+    r = s.handle("POST", "/v1/decide", b'{"x": 1, "x": 2}')
+    assert r.status == 400 and "duplicate" in r.body["error"]["message"]
+    r = s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE, model="missing"))
+    assert r.status == 422 and r.body["error"]["message"] == "unknown model missing; see /v1/models"
+    r = s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE, model=3))
+    assert r.status == 422 and "must be a string" in r.body["error"]["message"]
+    r = s.handle("POST", "/v1/decide", b"[]")
+    assert r.status == 422 and "JSON object" in r.body["error"]["message"]
+    assert s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE, model="llama")).status == 200
 
 
 def test_text_requests_with_tokenizer():

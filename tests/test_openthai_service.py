@@ -136,7 +136,13 @@ def test_cancel_busy_and_failures(served):
         assert r.status == 500 and r.body["error"]["message"] == "device lost"
     finally:
         m.forward = fwd
-    assert svc.handle("GET", "/health", None).body == {"status": "ok", "layers": 4}
+    h = svc.handle("GET", "/health", None).body
+    assert h["model"] == "openthai-systemone" and h["layers"] == 4 and h["busy"] is False
+    # the model key must name the loaded model (validation/test_openthai_http.py)
+    r = svc.handle("POST", "/v1/decide", json.dumps(dict(REQ, model="laya")))
+    assert r.status == 422 and r.body["error"]["message"] == "unknown model laya; see /v1/models"
+    r = svc.handle("POST", "/v1/systemone", json.dumps(dict(REQ, model="openthai-systemone")))
+    assert r.status == 200 and r.body["id"] == "r-1"
     with pytest.raises(ValueError, match="tokenizer"):
         frontend.OpenThaiService(m, None)
 
