@@ -20,9 +20,12 @@ What is kept from the reference, in the same order:
   (src/server.rs:259-282);
 * one inference at a time: a second request while one runs gets 429
   `busy_error` with `Retry-After: 1` (src/server.rs:283-297);
-* a canceled call maps to 408 `request_canceled`, any other failure to 500
+* a canceled call maps to 408 `request_canceled` (an HTTP client that
+  disconnects cancels its request), any other failure to 500
   `internal_error`; success is 200 with `X-Response-Time-Ms`, answers in
   request order (src/server.rs:298-331);
+* `serve` drains on SIGTERM / SIGINT: new requests get 503, `/health`
+  reports "draining", running requests are answered, then it returns;
 * the daemon answers each non-empty input line with one output line, the
   result or `{"error": message}` (src/main.rs:139-151).
 
@@ -53,6 +56,9 @@ its requests and answer objects are OpenThai's own
 from __future__ import annotations
 
 import json
+import select
+import signal
+import socket
 import sys
 import threading
 import time
@@ -231,6 +237,7 @@ class DecideService:
         self._busy = threading.Lock()
         self._requests = 0
         self._count_lock = threading.Lock()
+        self.draining = False  # set on SIGTERM: new work is refused, running work finishes
 
     def _select(self, req) -> None:
         """The request's optional `model` must name the loaded model
@@ -253,8 +260,10 @@ class DecideService:
                 "name": self.name, "canonical_name": self.name, "architecture": str(self.engine.info.get("architecture")),
                 "family": self.family, "default": True,
                 "description": f"Locally loaded {self.name} decision model on B200"}]})
-        return Response(200, {"status": "ok", "model": self.name, "family": self.family, "device": "cuda",
-                              "models": [self.name], "busy": self._busy.locked(), "layers": self.engine.layers()})
+        return Response(503 if self.draining else 200,
+                        {"status": "draining" if self.draining else "ok", "model": self.name, "family": self.family,
+                         "device": "cuda", "models": [self.name], "busy": self._busy.locked(),
+                         "layers": self.engine.layers()})
 
     def _prepare(self, req) -> tuple[list[list[int]], list[ParsedQuestion]]:
         if not isinstance(req, dict):
@@ -283,6 +292,8 @@ class DecideService:
             return _error(405, "invalid_request_error", "Method not allowed", {"Allow": allowed})
         if allowed != "POST":
             return self._info(path)
+        if self.draining:
+            return _error(503, "unavailable_error", "Server is shutting down")
         if (content_type or "").split(";")[0].strip().lower() != "application/json":
             return _error(415, "invalid_request_error", "Content-Type must be application/json")
         if body is not None and len(body) > MAX_BODY:
@@ -418,8 +429,32 @@ def run_daemon(service: DecideService, inp=None, out=None) -> None:
         out.flush()
 
 
+class _InFlight:
+    """Requests between their first byte and their last response byte."""
+
+    def __init__(self):
+        self.n = 0
+        self.cv = threading.Condition()
+
+    def __enter__(self):
+        with self.cv:
+            self.n += 1
+
+    def __exit__(self, *exc):
+        with self.cv:
+            self.n -= 1
+            self.cv.notify_all()
+
+    def wait_idle(self, timeout: float) -> bool:
+        with self.cv:
+            return self.cv.wait_for(lambda: self.n == 0, timeout)
+
+
 def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 8080) -> ThreadingHTTPServer:
-    """An HTTP server over `service` (serve with .serve_forever())."""
+    """An HTTP server over `service` (serve with .serve_forever(), or `serve`
+    for the signal handling).  `server.inflight` counts requests being
+    answered."""
+    inflight = _InFlight()
 
     class Handler(BaseHTTPRequestHandler):
         protocol_version = "HTTP/1.1"
@@ -448,25 +483,42 @@ def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 808
                 return None
             return self.rfile.read(n) if n else b""
 
+        def _client_gone(self) -> bool:
+            """True once the client has closed its side: the request is
+            canceled between steps (src/server.rs:297-313, the request
+            context ends on disconnect)."""
+            try:
+                readable, _, _ = select.select([self.connection], [], [], 0)
+                return bool(readable) and self.connection.recv(1, socket.MSG_PEEK) == b""
+            except OSError:
+                return True
+
         def _go(self, method):
+            with inflight:
+                self._answer(method)
+
+        def _answer(self, method):
             body = self._body() if method == "POST" else b""
             if body is None:
                 self.close_connection = True
                 r = _error(413, "invalid_request_error", "Request body exceeds 1 MiB or could not be read")
             else:
-                r = service.handle(method, self.path.split("?", 1)[0], body,
+                r = service.handle(method, self.path.split("?", 1)[0], body, canceled=self._client_gone,
                                    content_type=self.headers.get("Content-Type"))
             data = r.json().encode()
-            self.send_response(r.status)
-            self.send_header("Content-Type", "application/json; charset=utf-8")
-            self.send_header("Cache-Control", "no-store")
-            self.send_header("X-Content-Type-Options", "nosniff")
-            self.send_header("Content-Length", str(len(data)))
-            for k, v in r.headers.items():
-                self.send_header(k, v)
-            self.end_headers()
-            if method != "HEAD":
-                self.wfile.write(data)
+            try:
+                self.send_response(r.status)
+                self.send_header("Content-Type", "application/json; charset=utf-8")
+                self.send_header("Cache-Control", "no-store")
+                self.send_header("X-Content-Type-Options", "nosniff")
+                self.send_header("Content-Length", str(len(data)))
+                for k, v in r.headers.items():
+                    self.send_header(k, v)
+                self.end_headers()
+                if method != "HEAD":
+                    self.wfile.write(data)
+            except (BrokenPipeError, ConnectionResetError):
+                self.close_connection = True  # the client left (a canceled request)
 
         def do_GET(self):
             self._go("GET")
@@ -480,7 +532,33 @@ def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 808
         def log_message(self, *a):
             pass
 
-    return ThreadingHTTPServer((host, port), Handler)
+    srv = ThreadingHTTPServer((host, port), Handler)
+    srv.inflight = inflight
+    return srv
+
+
+def serve(service: DecideService, host: str = "127.0.0.1", port: int = 8080, ready=None,
+          drain_timeout: float = 600.0) -> None:
+    """Serves until SIGTERM or SIGINT, then drains (the reference's
+    shutdown): new requests get 503 and /health reports "draining", requests
+    already running finish and are answered, and the call returns.
+    `ready(server)` is called once the socket listens."""
+    srv = make_server(service, host, port)
+
+    def stop(*_):
+        service.draining = True
+        threading.Thread(target=srv.shutdown, daemon=True).start()
+
+    old = {sig: signal.signal(sig, stop) for sig in (signal.SIGTERM, signal.SIGINT)}
+    try:
+        if ready is not None:
+            ready(srv)
+        srv.serve_forever()
+        srv.inflight.wait_idle(drain_timeout)
+    finally:
+        srv.server_close()
+        for sig, h in old.items():
+            signal.signal(sig, h)
 
 
 def main(argv=None) -> int:
@@ -516,11 +594,7 @@ def main(argv=None) -> int:
     if a.mode == "daemon":
         run_daemon(svc)
     else:
-        srv = make_server(svc, a.host, a.port)
-        try:
-            srv.serve_forever()
-        finally:
-            srv.server_close()
+        serve(svc, a.host, a.port)
     eng.close()
     return 0
 

@@ -286,3 +286,118 @@ def test_text_requests_with_tokenizer():
     # without a tokenizer, text is a 422
     r = frontend.DecideService(FakeEngine()).handle("POST", "/v1/decide", body(state="hello", questions=CHOICE))
     assert r.status == 422 and "tokenizer" in r.body["error"]["message"]
+
+
+def test_draining_refuses_new_work():
+    s = frontend.DecideService(FakeEngine())
+    s.draining = True
+    h = s.handle("GET", "/health", None)
+    assert h.status == 503 and h.body["status"] == "draining"
+    r = s.handle("POST", "/v1/decide", body(state=[1], questions=CHOICE))
+    assert r.status == 503 and r.body["error"]["type"] == "unavailable_error"
+
+
+class SlowEngine(FakeEngine):
+    """Runs until canceled (or 5 s), recording whether it saw the cancel."""
+
+    def __init__(self):
+        super().__init__()
+        self.saw_cancel = threading.Event()
+        self.started = threading.Event()
+
+    def decide_batch(self, prompts, questions, canceled=None):
+        self.started.set()
+        import time
+
+        end = time.monotonic() + 5
+        while time.monotonic() < end:
+            if canceled and canceled():
+                self.saw_cancel.set()
+                raise LayaError(E_CANCELED, "request canceled")
+            time.sleep(0.01)
+        return super().decide_batch(prompts, questions)
+
+
+def test_client_disconnect_cancels_running_request():
+    import socket
+
+    eng = SlowEngine()
+    srv = frontend.make_server(frontend.DecideService(eng), "127.0.0.1", 0)
+    th = threading.Thread(target=srv.serve_forever, daemon=True)
+    th.start()
+    try:
+        b = body(state=[1, 2], questions=CHOICE)
+        c = socket.create_connection(("127.0.0.1", srv.server_address[1]), timeout=10)
+        c.sendall(b"POST /v1/decide HTTP/1.1\r\nHost: x\r\nContent-Type: application/json\r\n"
+                  b"Content-Length: %d\r\n\r\n" % len(b) + b)
+        assert eng.started.wait(5)
+        c.close()
+        assert eng.saw_cancel.wait(3)
+        assert srv.inflight.wait_idle(5)
+    finally:
+        srv.shutdown()
+        srv.server_close()
+
+
+CHILD = r"""
+import sys, time
+sys.path.insert(0, sys.argv[1])
+from laya_goish_b200 import frontend
+
+class Eng:
+    info = {"architecture": "llama"}
+    def layers(self): return 1
+    def validate(self, prompts, questions): pass
+    def decide_batch(self, prompts, questions, canceled=None):
+        time.sleep(1.5)
+        return [[{"type": 0, "probabilities": [1.0, 0.0], "logits": [1.0, 0.0], "confidence": 1.0, "choice": 0,
+                  "score": 0.0, "noul": 0.0} for _ in questions] for _ in prompts]
+
+def ready(srv):
+    print(srv.server_address[1], flush=True)
+
+frontend.serve(frontend.DecideService(Eng()), "127.0.0.1", 0, ready=ready)
+print("drained", flush=True)
+"""
+
+
+def test_sigterm_drains_running_request(tmp_path):
+    import os
+    import signal
+    import subprocess
+    import sys
+    import urllib.request
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    p = subprocess.Popen([sys.executable, "-c", CHILD, root], stdout=subprocess.PIPE, text=True)
+    try:
+        port = int(p.stdout.readline())
+        url = f"http://127.0.0.1:{port}"
+        out = {}
+
+        def call():
+            req = urllib.request.Request(url + "/v1/decide", method="POST",
+                                         data=body(state=[1], questions={"q": {"type": "choice",
+                                                                               "criteria": {"a": 1, "b": 2}}}),
+                                         headers={"Content-Type": "application/json"})
+            with urllib.request.urlopen(req, timeout=20) as r:
+                out["status"], out["body"] = r.status, json.loads(r.read())
+
+        t = threading.Thread(target=call)
+        t.start()
+        import time
+
+        for _ in range(200):  # until the request runs
+            with urllib.request.urlopen(url + "/health", timeout=5) as r:
+                if json.loads(r.read())["busy"]:
+                    break
+            time.sleep(0.01)
+        p.send_signal(signal.SIGTERM)
+        t.join(20)
+        assert out.get("status") == 200 and out["body"]["answers"]["q"]["choice"] == "a"
+        assert p.wait(timeout=20) == 0
+        assert p.stdout.read().strip() == "drained"
+    finally:
+        if p.poll() is None:
+            p.kill()
+            p.wait()
