@@ -4,8 +4,6 @@ synthetic GGUF decoders: the forward's hidden states, and decide answers
 choice / score / noul questions, single-token and multi-token options,
 suffixes over a shared prefix, ragged prompt lengths, batch invariance,
 waves, validation errors and cancellation."""
-import os
-
 import numpy as np
 import pytest
 
