@@ -362,13 +362,61 @@ class OpenThaiService(DecideService):
     Each request (each state of a batch, with the shared questions and
     options, src/server.rs:235-258) is validated through every permutation
     pass before any runs, then answered by one `Model.respond`; the answer
-    objects are the model's own (model, answers, usage, id, _raw)."""
+    objects are the model's own (model, answers, usage, id, _raw).
+
+    `model` may be a list with one model per GPU: the states of a batch are
+    then shared out over them (each device thread takes the next unanswered
+    state), answers stay in request order, and the first failure stops the
+    others before their next state and fails the batch."""
 
     def __init__(self, model, tokenizer, raw: bool = False):
         if tokenizer is None:
             raise ValueError("an OpenThai model needs its tokenizer")
-        super().__init__(model, raw=raw, tokenizer=tokenizer, name="openthai-systemone",
+        self.models = list(model) if isinstance(model, (list, tuple)) else [model]
+        if not self.models:
+            raise ValueError("no OpenThai model")
+        super().__init__(self.models[0], raw=raw, tokenizer=tokenizer, name="openthai-systemone",
                          family="openthai-systemone")
+
+    def _run(self, reqs, canceled):
+        """Answers of `reqs` in order, over every model; raises the first
+        LayaError (a cancel wins over later failures)."""
+        if len(self.models) == 1 or len(reqs) == 1:
+            return [self.engine.respond(self.tokenizer, r, self.raw, canceled) for r in reqs]
+        results = [None] * len(reqs)
+        errors = []
+        lock = threading.Lock()
+        nxt = [0]
+
+        def stop():
+            return bool(errors) or (canceled is not None and canceled())
+
+        def worker(m):
+            while True:
+                with lock:
+                    if errors or nxt[0] >= len(reqs):
+                        return
+                    i = nxt[0]
+                    nxt[0] += 1
+                try:
+                    results[i] = m.respond(self.tokenizer, reqs[i], self.raw, stop)
+                except LayaError as e:
+                    with lock:
+                        errors.append((i, e))
+                    return
+
+        threads = [threading.Thread(target=worker, args=(m,)) for m in self.models[:len(reqs)]]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            # the failure that stopped the others, not the cancels it caused
+            first = [e for _, e in errors if e.code != E_CANCELED] or [e for _, e in errors]
+            if canceled is not None and canceled():
+                raise LayaError(E_CANCELED, "request canceled")
+            raise first[0]
+        return results
 
     def _decide(self, req, batch: bool, canceled) -> Response:
         from .openthai import OpenThaiError
@@ -399,14 +447,12 @@ class OpenThaiService(DecideService):
             return _error(429, "busy_error", "An inference request is running; retry later", {"Retry-After": "1"})
         try:
             start = time.perf_counter()
-            results = []
-            for r in reqs:
-                try:
-                    results.append(self.engine.respond(self.tokenizer, r, self.raw, canceled))
-                except LayaError as e:
-                    if e.code == E_CANCELED:
-                        return _error(408, "request_canceled", e.message)
-                    return _error(500, "internal_error", e.message)
+            try:
+                results = self._run(reqs, canceled)
+            except LayaError as e:
+                if e.code == E_CANCELED:
+                    return _error(408, "request_canceled", e.message)
+                return _error(500, "internal_error", e.message)
             ms = int((time.perf_counter() - start) * 1000)
         finally:
             self._busy.release()
@@ -586,8 +632,8 @@ def main(argv=None) -> int:
     if read_metadata(a.model).get("general.architecture") == "openthai_systemone":
         from .openthai import Model
 
-        eng = Model(a.model, device=devices[0])
-        svc = OpenThaiService(eng, tok, raw=a.raw)
+        models = [Model(a.model, device=d) for d in devices]
+        svc = OpenThaiService(models, tok, raw=a.raw)
     else:
         eng = Engine(a.model, devices=devices)
         svc = DecideService(eng, raw=a.raw, tokenizer=tok)
@@ -595,7 +641,8 @@ def main(argv=None) -> int:
         run_daemon(svc)
     else:
         serve(svc, a.host, a.port)
-    eng.close()
+    for m in getattr(svc, "models", [svc.engine]):
+        m.close()
     return 0
 
 

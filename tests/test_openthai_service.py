@@ -155,3 +155,49 @@ def test_daemon_lines(served):
     lines = [json.loads(x) for x in out.getvalue().splitlines()]
     assert lines[0]["model"] == "openthai-systemone" and "error" in lines[1]
     assert np.isfinite(lines[0]["answers"]["s"]["score"])
+
+
+def _model_like(m, forward):
+    c = object.__new__(openthai.Model)
+    c._h = None
+    c.config, c.temperature = m.config, m.temperature
+    c.forward = forward
+    return c
+
+
+def test_batch_shared_over_several_models(served):
+    import threading
+    import time
+
+    m, tok, w, _ = served
+    used = {}
+
+    def on(k):
+        def forward(ids, positions):
+            used.setdefault(k, 0)
+            used[k] += 1
+            time.sleep(0.02)
+            return oracle.ot_forward(w, ids, positions)
+        return forward
+
+    models = [_model_like(m, on(0)), _model_like(m, on(1))]
+    batch = {"states": ["a", {"b": 1}, "ccc", "d d", ["e"]], "questions": REQ["questions"], "order_invariant": True}
+    one = frontend.OpenThaiService(m, tok).handle("POST", "/v1/decide/batch", json.dumps(batch))
+    two = frontend.OpenThaiService(models, tok).handle("POST", "/v1/decide/batch", json.dumps(batch))
+    assert one.status == two.status == 200
+    strip = [{k: v for k, v in r.items() if k != "usage"} for r in one.body["results"]]
+    assert strip == [{k: v for k, v in r.items() if k != "usage"} for r in two.body["results"]]
+    assert set(used) == {0, 1} and sum(used.values()) == 5 * 3
+    # a failure on one device fails the batch and stops the other
+    stop = threading.Event()
+
+    def broken(ids, positions):
+        stop.set()
+        raise LayaError(E_CUDA, "device lost")
+
+    r = frontend.OpenThaiService([_model_like(m, on(0)), _model_like(m, broken)], tok).handle(
+        "POST", "/v1/decide/batch", json.dumps(batch))
+    assert r.status == 500 and r.body["error"]["message"] == "device lost" and stop.is_set()
+    r = frontend.OpenThaiService(models, tok).handle("POST", "/v1/decide/batch", json.dumps(batch),
+                                                    canceled=lambda: True)
+    assert r.status == 408
