@@ -201,3 +201,18 @@ def test_batch_shared_over_several_models(served):
     r = frontend.OpenThaiService(models, tok).handle("POST", "/v1/decide/batch", json.dumps(batch),
                                                     canceled=lambda: True)
     assert r.status == 408
+
+
+def test_model_without_gpu_fails_cleanly(tmp_path):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    path = synth.write_openthai(str(tmp_path / "ot.gguf"), d=128, ffn=256, hd=64, lin_dim=64)
+    with pytest.raises(openthai.OpenThaiError, match="unsupported OpenThai config"):
+        openthai.Model(path)  # the reference's one size only, unless strict=False
+    with pytest.raises(LayaError):
+        openthai.Model(path, strict=False)
+    m = object.__new__(openthai.Model)
+    m._h = None
+    with pytest.raises(openthai.OpenThaiError, match="closed"):
+        openthai.Model.forward(m, [1, 2], [1])
