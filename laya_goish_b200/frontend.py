@@ -506,10 +506,14 @@ def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 808
         protocol_version = "HTTP/1.1"
 
         def _body(self):
-            """The request body (Content-Length or chunked), None past 1 MiB
-            or when it cannot be read."""
+            """The request body (Content-Length or chunked); None past 1 MiB
+            or when it cannot be read.  Bodies over 1 MiB are still read and
+            dropped up to 16 MiB (the reference's transport buffers that
+            much before dispatch), so the client gets the 413 instead of a
+            reset connection."""
+            hard = 16 * MAX_BODY
             if "chunked" in (self.headers.get("Transfer-Encoding") or "").lower():
-                out = bytearray()
+                out, total = bytearray(), 0
                 while True:
                     line = self.rfile.readline(64)
                     try:
@@ -519,13 +523,22 @@ def make_server(service: DecideService, host: str = "127.0.0.1", port: int = 808
                     if n == 0:
                         while self.rfile.readline(1024) not in (b"\r\n", b"\n", b""):
                             pass  # trailers
-                        return bytes(out)
-                    if len(out) + n > MAX_BODY:
+                        return bytes(out) if total <= MAX_BODY else None
+                    total += n
+                    if total > hard:
                         return None
-                    out += self.rfile.read(n)
+                    data = self.rfile.read(n)
+                    if total <= MAX_BODY:
+                        out += data
                     self.rfile.readline(8)  # the chunk's CRLF
             n = int(self.headers.get("Content-Length") or 0)
             if n > MAX_BODY:
+                if n <= hard:
+                    while n > 0:
+                        got = len(self.rfile.read(min(n, 1 << 16)))
+                        if not got:
+                            break
+                        n -= got
                 return None
             return self.rfile.read(n) if n else b""
 
@@ -607,43 +620,128 @@ def serve(service: DecideService, host: str = "127.0.0.1", port: int = 8080, rea
             signal.signal(sig, h)
 
 
+MODES = ("decide", "daemon", "serve", "tokenize", "info")
+
+
+def build_request(a) -> dict:
+    """The `decide` command's request (src/main.rs:155-189): the --request
+    file, or a state (--state as JSON, else as text; --state-file) and the
+    questions (--questions / --questions-file).  Presets are not served, so
+    the questions must be given."""
+    if a.request:
+        with open(a.request, encoding="utf-8") as f:
+            return parse_body(f.read())
+    if a.state is not None:
+        try:
+            state = parse_body(a.state)
+        except ValueError:
+            state = a.state
+    elif a.state_file:
+        with open(a.state_file, encoding="utf-8") as f:
+            state = parse_body(f.read())
+    else:
+        raise RequestError("--request, --state or --state-file is required")
+    if a.questions is not None:
+        questions = parse_body(a.questions)
+    elif a.questions_file:
+        with open(a.questions_file, encoding="utf-8") as f:
+            questions = parse_body(f.read())
+    else:
+        raise RequestError("--questions or --questions-file is required (presets are not served)")
+    return {"state": state, "questions": questions}
+
+
+def gguf_info(path: str) -> dict:
+    """The `info` command (Gguf::info, src/gguf.rs:204-224) for this build."""
+    from .gguf_meta import _parse
+
+    with open(path, "rb") as f:
+        meta, infos, _ = _parse(memoryview(f.read()), tensors=True)
+    arch = meta.get("general.architecture")
+    return {"name": meta.get("general.name"),
+            "model": "openthai-systemone" if arch == "openthai_systemone" else meta.get("laya.model_name", arch),
+            "architecture": arch, "checkpoint": meta.get("laya.checkpoint"),
+            "max_len": int(meta.get("openthai.context_length", meta.get("laya.max_len", 512))),
+            "tensors": len(infos), "runtime": "laya-goish B200 (CUDA, sm_100a)"}
+
+
 def main(argv=None) -> int:
+    """`python -m laya_goish_b200.frontend COMMAND MODEL [options]`, the
+    reference's command line (src/main.rs:33-192) for the commands on the
+    decision path: decide, daemon, serve, plus tokenize and info.  The older
+    `MODEL COMMAND` order is accepted too."""
     import argparse
 
-    from .engine import Engine
-
     ap = argparse.ArgumentParser(prog="python -m laya_goish_b200.frontend")
-    ap.add_argument("model", help="GGUF file")
-    ap.add_argument("mode", choices=["daemon", "serve"])
+    ap.add_argument("first", help="command (decide, daemon, serve, tokenize, info) or GGUF file")
+    ap.add_argument("second", help="GGUF file or command")
     ap.add_argument("--devices", default="0", help="comma-separated CUDA devices")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)
     ap.add_argument("--raw", action="store_true")
+    ap.add_argument("--request", help="decide: request JSON file")
+    ap.add_argument("--state", help="decide: state (JSON, or text)")
+    ap.add_argument("--state-file", help="decide: state JSON file")
+    ap.add_argument("--questions", help="decide: questions JSON")
+    ap.add_argument("--questions-file", help="decide: questions JSON file")
+    ap.add_argument("--text", help="tokenize: text")
+    ap.add_argument("--threads", type=int, help="accepted for compatibility; the GPU path ignores it")
     a = ap.parse_args(argv)
+    mode, model = (a.first, a.second) if a.first in MODES else (a.second, a.first)
+    if mode not in MODES:
+        ap.error(f"unknown command {mode}")
+    if not 1 <= a.port <= 65535:
+        ap.error("--port must be 1..65535")
+    from .gguf_meta import read_metadata
     from .tokenizer import Tokenizer
 
-    from .gguf_meta import read_metadata
-
+    if mode == "info":
+        print(json.dumps(gguf_info(model), ensure_ascii=False))
+        return 0
+    if mode == "tokenize":
+        if a.text is None:
+            ap.error("missing --text")
+        print(json.dumps(Tokenizer.from_gguf(model).encode(a.text)))
+        return 0
+    req = None
+    if mode == "decide":
+        try:
+            req = build_request(a)
+        except (RequestError, ValueError, OSError) as e:
+            print(str(e), file=sys.stderr)
+            return 1
     try:
-        tok = Tokenizer.from_gguf(a.model)
+        tok = Tokenizer.from_gguf(model)
     except ValueError:
         tok = None  # no usable vocabulary in the file: token-id requests only
     devices = [int(d) for d in a.devices.split(",")]
-    if read_metadata(a.model).get("general.architecture") == "openthai_systemone":
+    if read_metadata(model).get("general.architecture") == "openthai_systemone":
         from .openthai import Model
 
-        models = [Model(a.model, device=d) for d in devices]
+        models = [Model(model, device=d) for d in devices]
         svc = OpenThaiService(models, tok, raw=a.raw)
     else:
-        eng = Engine(a.model, devices=devices)
-        svc = DecideService(eng, raw=a.raw, tokenizer=tok)
-    if a.mode == "daemon":
-        run_daemon(svc)
-    else:
-        serve(svc, a.host, a.port)
-    for m in getattr(svc, "models", [svc.engine]):
-        m.close()
-    return 0
+        from .engine import Engine
+
+        models = [Engine(model, devices=devices)]
+        svc = DecideService(models[0], raw=a.raw, tokenizer=tok)
+    rc = 0
+    try:
+        if mode == "decide":
+            r = svc.handle("POST", "/v1/decide", json.dumps(req))
+            if r.status == 200:
+                print(json.dumps(r.body, ensure_ascii=False))
+            else:
+                print(r.body["error"]["message"], file=sys.stderr)
+                rc = 1
+        elif mode == "daemon":
+            run_daemon(svc)
+        else:
+            serve(svc, a.host, a.port)
+    finally:
+        for m in models:
+            m.close()
+    return rc
 
 
 if __name__ == "__main__":

@@ -401,3 +401,32 @@ def test_sigterm_drains_running_request(tmp_path):
         if p.poll() is None:
             p.kill()
             p.wait()
+
+
+def test_command_line_without_a_model_load(tmp_path, capsys):
+    import types
+
+    from laya_goish_b200 import synth
+
+    path = synth.write_openthai(str(tmp_path / "ot.gguf"), tokenizer=True)
+    assert frontend.main(["info", path]) == 0
+    info = json.loads(capsys.readouterr().out)
+    assert info["model"] == "openthai-systemone" and info["max_len"] == 512 and info["tensors"] > 0
+    assert frontend.main(["tokenize", path, "--text", "th<|ts_q|>"]) == 0
+    ids = json.loads(capsys.readouterr().out)
+    assert ids == [274, 256]  # the merge "t h", then <|ts_q|> (the first control token)
+    # decide needs a request, or a state and questions (no presets)
+    assert frontend.main(["decide", path, "--state", "hi"]) == 1
+    assert "presets are not served" in capsys.readouterr().err
+    with pytest.raises(SystemExit):
+        frontend.main(["bogus", path])
+    # the request builder (src/main.rs:155-189)
+    ns = dict(request=None, state=None, state_file=None, questions=None, questions_file=None)
+    q = '{"q": {"type": "noul", "instructions": "?"}}'
+    r = frontend.build_request(types.SimpleNamespace(**dict(ns, state="plain text", questions=q)))
+    assert r == {"state": "plain text", "questions": {"q": {"type": "noul", "instructions": "?"}}}
+    r = frontend.build_request(types.SimpleNamespace(**dict(ns, state='{"a": 1}', questions=q)))
+    assert r["state"] == {"a": 1}
+    f = tmp_path / "req.json"
+    f.write_text(json.dumps({"state": "s", "questions": {}}))
+    assert frontend.build_request(types.SimpleNamespace(**dict(ns, request=str(f))))["state"] == "s"
