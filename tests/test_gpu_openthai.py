@@ -117,6 +117,26 @@ def test_openthai_forward_matches_oracle(ot_model):
         m.forward([0, 1, 2], [3])
 
 
+def test_openthai_forward_reference_head_geometry(tmp_path):
+    """The reference's head layout (8/2 attention heads of 256 with a 64-wide
+    rotary part, 16 DeltaNet heads of 128) on a small width; a NumPy
+    emulation of the F16 operand rounding lands near 1.5e-3 of the largest
+    logit here."""
+    from laya_goish_b200 import openthai, synth
+
+    path = synth.write_openthai(str(tmp_path / "ot_ref.gguf"), d=256, ffn=256, heads=8, kv=2, hd=256,
+                                lin_heads=16, lin_dim=128, seed=12, width_scaled=True)
+    w = openthai.load_weights(path, strict=False)
+    rng = np.random.default_rng(5)
+    with openthai.Model(path, strict=False) as m:
+        for s, pos in [(40, [0, 39]), (200, [99, 199])]:
+            ids = rng.integers(0, 300, s)
+            got = m.forward(ids, pos)
+            want = oracle.ot_forward(w, ids, pos)
+            tol = 5e-3 * np.abs(want).max()
+            assert np.abs(got - want).max() < tol, (s, np.abs(got - want).max(), tol)
+
+
 def test_openthai_decide_matches_oracle(ot_model):
     from laya_goish_b200 import openthai
     from laya_goish_b200.tokenizer import Tokenizer, byte_alphabet
