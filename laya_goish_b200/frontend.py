@@ -460,14 +460,18 @@ class OpenThaiService(DecideService):
 
 
 def run_daemon(service: DecideService, inp=None, out=None) -> None:
-    """JSON lines: each non-empty input line is one /v1/decide body; the
+    """JSON lines: each non-empty input line is one decide request, given to
+    the model as it is (no route, content-type or `model` checks); the
     answer or {"error": message} is written as one line (src/main.rs:139-151)."""
     inp = inp or sys.stdin
     out = out or sys.stdout
     for line in inp:
         if not line.strip():
             continue
-        r = service.handle("POST", "/v1/decide", line)
+        try:
+            r = service._decide(parse_body(line), False, None)  # no HTTP checks: the line goes to decide
+        except ValueError as e:
+            r = _error(400, "invalid_request_error", str(e))
         if r.status == 200:
             out.write(r.json())
         else:

@@ -170,6 +170,10 @@ def test_daemon_lines():
     assert len(lines) == 3
     assert "answers" in lines[0]
     assert "error" in lines[1] and "error" in lines[2]
+    # the daemon hands each line to the model: a `model` key is not checked
+    out = io.StringIO()
+    frontend.run_daemon(s, io.StringIO(json.dumps({"state": [1, 2], "questions": CHOICE, "model": "x"}) + "\n"), out)
+    assert "answers" in json.loads(out.getvalue())
 
 
 def test_http_round_trip():
