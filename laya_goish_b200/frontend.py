@@ -275,8 +275,8 @@ class DecideService:
     def handle(self, method: str, path: str, body: bytes | str | None,
                canceled: Callable[[], bool] | None = None,
                content_type: str | None = "application/json") -> Response:
-        """One request.  `content_type` is the request's Content-Type header
-        (callers without headers, like the daemon, keep the default)."""
+        """One HTTP request.  `content_type` is its Content-Type header
+        (in-process callers without headers keep the default)."""
         with self._count_lock:
             self._requests += 1
             rid = self._requests
