@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 
   if (warp == GV_WARPS) {
     // ---------------- producer: one thread, one bulk copy per stage, all phases
-    int stage = 0;
+    int stage = 0, issued = 0;
     uint32_t phase = 0;
     const uint32_t sbytes = (uint32_t)gv_stage_bytes(Q8);
     for (int p = 0; p < q.n; p++) {
@@ -304,6 +304,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
           if (lane == 0) {
             mbar_expect_tx(&full[stage], sbytes);
             bulk_g2s(ring + stage * GV_STAGE, src + ((size_t)t * w.kstages + ks) * sbytes, sbytes, &full[stage]);
+            // the ring's first fills go out before the prefetches
+            if (++issued == nst) pf_issue(q.pf, blockIdx.x, gridDim.x);
           }
           __syncwarp();
           if (++stage == nst) {
@@ -313,6 +315,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
         }
       }
     }
+    if (lane == 0 && issued < nst) pf_issue(q.pf, blockIdx.x, gridDim.x);
     // Every fill is consumed before the CTA exits (no copy left in flight).
     for (int i = 0; i < nst; i++) {
       if (!mbar_wait(&empty[stage], phase ^ 1, budget) && lane == 0) atomicOr(err, 64u);
@@ -703,11 +706,18 @@ static cudaError_t gemv3_go(const GemvSeq& q, int num_sms, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, q, nst);
 }
 
-cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st) {
+cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st,
+                             const PfList* pf) {
   if (n < 1 || n > 4 || (n > 1 && !gbar)) return cudaErrorInvalidValue;
   GemvSeq q{};
   q.n = n;
   q.gbar = gbar;
+  if (pf) {
+    if (pf->count < 0 || pf->count > PF_MAX) return cudaErrorInvalidValue;
+    for (int i = 0; i < pf->count; i++)
+      if (reinterpret_cast<uintptr_t>(pf->p[i]) & 15) return cudaErrorInvalidValue;
+    q.pf = *pf;
+  }
   for (int i = 0; i < n; i++) {
     const Gemv3Args& a = ph[i];
     if (!gemv3_supported(a) || !a.packed || (reinterpret_cast<uintptr_t>(a.packed) & 15)) return cudaErrorInvalidValue;
@@ -723,9 +733,9 @@ cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num
   return q8 ? gemv3_go<2, true>(q, num_sms, st) : gemv3_go<2, false>(q, num_sms, st);
 }
 
-cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st) {
+cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st, const PfList* pf) {
   if (gemv3_tiles(a) <= 0) return cudaSuccess;
-  return gemv3_launch_seq(&a, 1, nullptr, num_sms, st);
+  return gemv3_launch_seq(&a, 1, nullptr, num_sms, st, pf);
 }
 
 }  // namespace laya

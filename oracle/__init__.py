@@ -59,6 +59,12 @@ def lib() -> ctypes.CDLL:
         L.or_model_free.argtypes = [P]
         L.or_model_dim.argtypes = [P, ctypes.c_int]
         L.or_forward.argtypes = [P, P, ctypes.c_int, P, ctypes.c_int, P]
+        L.or_cache_new.restype = P
+        L.or_cache_new.argtypes = [P, ctypes.c_int]
+        L.or_cache_free.argtypes = [P]
+        L.or_cache_len.argtypes = [P]
+        L.or_cache_truncate.argtypes = [P, ctypes.c_int]
+        L.or_cache_forward.argtypes = [P, P, P, ctypes.c_int, P, ctypes.c_int, P]
         i = ctypes.c_int
         L.or_ot_full.argtypes = [P, i, i, i, i, i, i, ctypes.c_float, P, P, P, P, P, P, i, P]
         L.or_ot_delta.argtypes = [P, i, i, i, i, P, P, P, P, P, P, P, P, P, i, P]
@@ -153,6 +159,27 @@ class Model:
             raise ValueError("invalid token sequence")
         return out
 
+    def cache(self, capacity: int) -> "Cache":
+        """A K/V cache over this model for up to `capacity` tokens."""
+        return Cache(self, capacity)
+
+    def greedy(self, ctx, steps: int):
+        """Greedy decode with the K/V cache: the context once, then one token
+        per step (argmax over the full vocabulary, ties to the lowest id).
+        Returns (tokens, top-2 logit margins)."""
+        c = self.cache(len(ctx) + steps)
+        h = c.forward(ctx, [len(ctx) - 1])
+        toks, margins = [], []
+        for s in range(steps):
+            logits = self.head(h)[0]
+            order = np.argsort(-logits, kind="stable")
+            toks.append(int(order[0]))
+            margins.append(float(logits[order[0]] - logits[order[1]]))
+            if s + 1 < steps:
+                h = c.forward([toks[-1]], [0])
+        c.close()
+        return toks, margins
+
     def head(self, hidden, cand=None) -> np.ndarray:
         hidden = np.ascontiguousarray(hidden, np.float32).reshape(-1, self.d)
         n = 0 if cand is None else len(cand)
@@ -179,6 +206,44 @@ class Model:
         return {"kind": a.kind, "choice": a.choice, "score": a.score, "noul": a.noul,
                 "confidence": a.confidence, "probabilities": list(a.probabilities[:k]),
                 "logits": list(a.logits[:k])}
+
+
+class Cache:
+    """Model::forward extended token by token: forward() appends ids at the
+    next positions and returns the final-normed hidden rows at `read`
+    (indices into the appended ids); truncate(n) drops positions >= n, so a
+    shared prefix is computed once and branched.  Same bits as one forward
+    over the whole sequence."""
+
+    def __init__(self, model: Model, capacity: int):
+        self.m = model
+        h = lib().or_cache_new(model.h, capacity)
+        if not h:
+            raise ValueError("cache capacity out of range")
+        self.h = ctypes.c_void_p(h)
+
+    def __len__(self):
+        return lib().or_cache_len(self.h)
+
+    def forward(self, ids, read) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        read = np.ascontiguousarray(read, np.int32)
+        out = np.zeros((len(read), self.m.d), np.float32)
+        if lib().or_cache_forward(self.m.h, self.h, _p(ids), len(ids), _p(read), len(read), _p(out)):
+            raise ValueError("invalid token sequence or cache overflow")
+        return out
+
+    def truncate(self, n: int) -> None:
+        if lib().or_cache_truncate(self.h, n):
+            raise ValueError("truncate past the cached length")
+
+    def close(self):
+        if self.h:
+            lib().or_cache_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 def _f32(a) -> np.ndarray:

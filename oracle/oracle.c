@@ -652,13 +652,90 @@ static void rms(const float* x, const float* w, int d, int rows, float eps, floa
 }
 
 /* Rotate-half RoPE over the full head (src/tensor.rs:158-171; angle formula
- * src/models/openthai/model.rs:264 with rotary dim = head_dim). */
-static void rope(float* buf, int s, int heads, int hd, float theta) {
+ * src/models/openthai/model.rs:264 with rotary dim = head_dim): rope_at. */
+static float silu(float x) { return x * (1.f / (1.f + expf(-x))); }
+
+/* K/V of every processed token per layer (post-RoPE K), so a sequence can
+ * be extended token by token.  Every row of the forward depends only on its
+ * own token and the keys at or before it, and Matrix::apply computes each
+ * token row on its own (src/tensor.rs:58-102: a row's lanes and sum order do
+ * not depend on which rows share its block), so extending a cached prefix
+ * gives the same bits as recomputing the whole sequence. */
+struct or_cache {
+  int cap, n;
+  float *k, *v; /* [L][cap][kd] */
+};
+
+or_cache* or_cache_new(const or_model* m, int cap) {
+  if (cap < 1 || cap > m->ctx) return NULL;
+  or_cache* c = (or_cache*)calloc(1, sizeof(or_cache));
+  size_t kd = (size_t)m->KV * m->hd;
+  c->cap = cap;
+  c->k = (float*)malloc(sizeof(float) * (size_t)m->L * cap * kd);
+  c->v = (float*)malloc(sizeof(float) * (size_t)m->L * cap * kd);
+  if (!c->k || !c->v) {
+    or_cache_free(c);
+    return NULL;
+  }
+  return c;
+}
+
+void or_cache_free(or_cache* c) {
+  if (!c) return;
+  free(c->k);
+  free(c->v);
+  free(c);
+}
+
+int or_cache_len(const or_cache* c) { return c->n; }
+
+int or_cache_truncate(or_cache* c, int n) {
+  if (n < 0 || n > c->n) return -1;
+  c->n = n;
+  return 0;
+}
+
+/* Causal GQA attention (src/models/openthai/model.rs:276-294) of s new rows
+ * at positions pos0..pos0+s-1 over keys 0..pos; the (row, head) items are
+ * independent and split across threads, each computed in the same order as
+ * a single-threaded loop. */
+typedef struct {
+  const float *q, *k, *v;
+  float* att;
+  int s, pos0, H, hd, qd, kd, grp, first, step;
+  float scale;
+} attn_job;
+
+static void* attn_worker(void* arg) {
+  attn_job* J = (attn_job*)arg;
+  int keys = J->pos0 + J->s;
+  float* sc = (float*)malloc(sizeof(float) * (size_t)keys);
+  float* p = (float*)malloc(sizeof(float) * (size_t)keys);
+  for (int it = J->first; it < J->s * J->H; it += J->step) {
+    int i = it / J->H, hh = it % J->H, kh = hh / J->grp, pos = J->pos0 + i;
+    for (int j = 0; j <= pos; j++)
+      sc[j] = dotf(J->q + (size_t)i * J->qd + (size_t)hh * J->hd, J->k + (size_t)j * J->kd + (size_t)kh * J->hd,
+                   J->hd) * J->scale;
+    or_softmax(sc, pos + 1, p);
+    float* o = J->att + (size_t)i * J->qd + (size_t)hh * J->hd;
+    for (int z = 0; z < J->hd; z++) o[z] = 0.f;
+    for (int j = 0; j <= pos; j++) {
+      const float* vv = J->v + (size_t)j * J->kd + (size_t)kh * J->hd;
+      for (int z = 0; z < J->hd; z++) o[z] += p[j] * vv[z];
+    }
+  }
+  free(sc);
+  free(p);
+  return NULL;
+}
+
+/* Rotate-half RoPE of s rows starting at position pos0. */
+static void rope_at(float* buf, int s, int pos0, int heads, int hd, float theta) {
   int half = hd / 2;
   for (int i = 0; i < s; i++)
     for (int h = 0; h < heads; h++)
       for (int j = 0; j < half; j++) {
-        float angle = (float)i / powf(theta, (float)(2 * j) / (float)hd);
+        float angle = (float)(pos0 + i) / powf(theta, (float)(2 * j) / (float)hd);
         float co = cosf(angle), si = sinf(angle);
         size_t p = (size_t)i * heads * hd + (size_t)h * hd + j;
         float a = buf[p], b = buf[p + half];
@@ -667,14 +744,13 @@ static void rope(float* buf, int s, int heads, int hd, float theta) {
       }
 }
 
-static float silu(float x) { return x * (1.f / (1.f + expf(-x))); }
-
-int or_forward(or_model* m, const int32_t* ids, int s, const int32_t* read, int nread, float* out) {
+int or_cache_forward(or_model* m, or_cache* c, const int32_t* ids, int s, const int32_t* read, int nread, float* out) {
   int d = m->d, H = m->H, KV = m->KV, hd = m->hd, ffn = m->ffn;
   int qd = H * hd, kd = KV * hd, grp = H / KV;
   int block, size;
+  int pos0 = c->n;
   /* Model::forward input validation (src/models/openthai/model.rs:198-204) */
-  if (s < 1 || s > m->ctx) return -1;
+  if (s < 1 || pos0 + s > c->cap || pos0 + s > m->ctx) return -1;
   for (int i = 0; i < s; i++)
     if (ids[i] < 0 || ids[i] >= m->V) return -1;
   for (int i = 0; i < nread; i++)
@@ -684,38 +760,33 @@ int or_forward(or_model* m, const int32_t* ids, int s, const int32_t* read, int 
   float* x = (float*)malloc(sizeof(float) * (size_t)s * d);
   float* h = (float*)malloc(sizeof(float) * (size_t)s * d);
   float* q = (float*)malloc(sizeof(float) * (size_t)s * qd);
-  float* k = (float*)malloc(sizeof(float) * (size_t)s * kd);
-  float* v = (float*)malloc(sizeof(float) * (size_t)s * kd);
   float* att = (float*)malloc(sizeof(float) * (size_t)s * qd);
   float* y = (float*)malloc(sizeof(float) * (size_t)s * (ffn > d ? ffn : d));
   float* u = (float*)malloc(sizeof(float) * (size_t)s * ffn);
-  float* sc = (float*)malloc(sizeof(float) * (size_t)s);
-  float* p = (float*)malloc(sizeof(float) * (size_t)s);
   /* embedding rows decoded per used id (src/models/openthai/model.rs:205-213) */
   for (int i = 0; i < s; i++) or_decode(m->embd_kind, m->embd + (size_t)ids[i] * rowb, rowb, x + (size_t)i * d);
   float scale = 1.f / sqrtf((float)hd); /* src/tensor.rs:174 */
+  int nth = m->threads < s * H ? m->threads : s * H;
+  if (nth > 256) nth = 256;
   for (int l = 0; l < m->L; l++) {
     or_layer* b = &m->layer[l];
+    float* kl = c->k + ((size_t)l * c->cap) * kd;
+    float* vl = c->v + ((size_t)l * c->cap) * kd;
+    float* k = kl + (size_t)pos0 * kd;
+    float* v = vl + (size_t)pos0 * kd;
     rms(x, b->attn_norm, d, s, m->eps, h);
     or_matrix_apply(b->wq, qd, d, h, s, b->bq, m->threads, q);
     or_matrix_apply(b->wk, kd, d, h, s, b->bk, m->threads, k);
     or_matrix_apply(b->wv, kd, d, h, s, b->bv, m->threads, v);
-    rope(q, s, H, hd, m->theta);
-    rope(k, s, KV, hd, m->theta);
-    /* causal GQA attention (src/models/openthai/model.rs:276-294) */
-    memset(att, 0, sizeof(float) * (size_t)s * qd);
-    for (int i = 0; i < s; i++)
-      for (int hh = 0; hh < H; hh++) {
-        int kh = hh / grp;
-        for (int j = 0; j <= i; j++)
-          sc[j] = dotf(q + (size_t)i * qd + (size_t)hh * hd, k + (size_t)j * kd + (size_t)kh * hd, hd) * scale;
-        or_softmax(sc, i + 1, p);
-        float* o = att + (size_t)i * qd + (size_t)hh * hd;
-        for (int j = 0; j <= i; j++) {
-          const float* vv = v + (size_t)j * kd + (size_t)kh * hd;
-          for (int z = 0; z < hd; z++) o[z] += p[j] * vv[z];
-        }
-      }
+    rope_at(q, s, pos0, H, hd, m->theta);
+    rope_at(k, s, pos0, KV, hd, m->theta);
+    attn_job jobs[256];
+    pthread_t th[256];
+    for (int t = 0; t < nth; t++)
+      jobs[t] = (attn_job){q, kl, vl, att, s, pos0, H, hd, qd, kd, grp, t, nth, scale};
+    for (int t = 1; t < nth; t++) pthread_create(&th[t], NULL, attn_worker, &jobs[t]);
+    attn_worker(&jobs[0]);
+    for (int t = 1; t < nth; t++) pthread_join(th[t], NULL);
     or_matrix_apply(b->wo, d, qd, att, s, NULL, m->threads, y);
     for (size_t i = 0; i < (size_t)s * d; i++) x[i] += y[i]; /* tensor::add (src/tensor.rs:123-128) */
     rms(x, b->ffn_norm, d, s, m->eps, h);
@@ -725,11 +796,21 @@ int or_forward(or_model* m, const int32_t* ids, int s, const int32_t* read, int 
     or_matrix_apply(b->wd, d, ffn, y, s, NULL, m->threads, u);
     for (size_t i = 0; i < (size_t)s * d; i++) x[i] += u[i];
   }
+  c->n = pos0 + s;
   /* answer-position gather + final norm (src/models/openthai/model.rs:232-240) */
   for (int r = 0; r < nread; r++) memcpy(h + (size_t)r * d, x + (size_t)read[r] * d, sizeof(float) * d);
   rms(h, m->out_norm, d, nread, m->eps, out);
-  free(x); free(h); free(q); free(k); free(v); free(att); free(y); free(u); free(sc); free(p);
+  free(x); free(h); free(q); free(att); free(y); free(u);
   return 0;
+}
+
+int or_forward(or_model* m, const int32_t* ids, int s, const int32_t* read, int nread, float* out) {
+  if (s < 1 || s > m->ctx) return -1;
+  or_cache* c = or_cache_new(m, s);
+  if (!c) return -1;
+  int rc = or_cache_forward(m, c, ids, s, read, nread, out);
+  or_cache_free(c);
+  return rc;
 }
 
 int or_head(or_model* m, const float* hidden, int rows, const int32_t* cand, int ncand, float* out) {
@@ -774,17 +855,26 @@ int or_decide(or_model* m, const int32_t* ids, int n, const or_question* q, or_a
     if (rc) { free(seq); return rc; }
   } else {
     /* each option is scored by the summed full-vocabulary log-probability
-     * of its tokens, one forward per option */
+     * of its tokens: the shared prefix seq[0..base-1) once, then per option
+     * the last prefix token and the option's first L-1 tokens appended to
+     * it (the same rows as one forward over the whole sequence) */
     float* hid = (float*)malloc(sizeof(float) * (size_t)L * d);
     float* row = (float*)malloc(sizeof(float) * (size_t)L * m->V);
     int32_t* rp = (int32_t*)malloc(sizeof(int32_t) * (size_t)L);
+    int32_t* tail = (int32_t*)malloc(sizeof(int32_t) * (size_t)L);
+    or_cache* c = total <= m->ctx ? or_cache_new(m, total) : NULL;
+    int rc0 = c ? 0 : -1;
+    if (!rc0 && base > 1) rc0 = or_cache_forward(m, c, seq, base - 1, NULL, 0, NULL);
+    if (rc0) { or_cache_free(c); free(hid); free(row); free(rp); free(tail); free(seq); return rc0; }
     for (int o = 0; o < k; o++) {
       const int32_t* opt = q->options + (size_t)o * L;
-      for (int t = 0; t < L - 1; t++) seq[base + t] = opt[t];
-      for (int t = 0; t < L; t++) rp[t] = base - 1 + t;
-      int rc = or_forward(m, seq, total, rp, L, hid);
+      tail[0] = seq[base - 1];
+      for (int t = 0; t < L - 1; t++) tail[t + 1] = opt[t];
+      for (int t = 0; t < L; t++) rp[t] = t;
+      or_cache_truncate(c, base - 1);
+      int rc = or_cache_forward(m, c, tail, L, rp, L, hid);
       if (!rc) rc = or_head(m, hid, L, NULL, 0, row);
-      if (rc) { free(hid); free(row); free(rp); free(seq); return rc; }
+      if (rc) { or_cache_free(c); free(hid); free(row); free(rp); free(tail); free(seq); return rc; }
       double sum = 0;
       for (int t = 0; t < L; t++) {
         const float* r = row + (size_t)t * m->V;
@@ -796,7 +886,8 @@ int or_decide(or_model* m, const int32_t* ids, int n, const or_question* q, or_a
       }
       logits[o] = (float)sum;
     }
-    free(hid); free(row); free(rp);
+    or_cache_free(c);
+    free(hid); free(row); free(rp); free(tail);
   }
   free(seq);
   for (int i = 0; i < k; i++)

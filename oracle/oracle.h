@@ -72,6 +72,19 @@ int or_model_dim(const or_model* m, int what); /* 0 d, 1 layers, 2 vocab, 3 head
  * conventions).  out: nread*d floats.  0 on success. */
 int or_forward(or_model* m, const int32_t* ids, int n, const int32_t* read, int nread, float* out);
 
+/* The same forward with a K/V cache, so a shared prefix is computed once
+ * and then extended (question suffixes, option continuations, greedy
+ * decode).  or_cache_forward appends ids[0..n) at positions len..len+n-1 and
+ * returns the final-normed hidden rows at read[] (indices into the n new
+ * tokens); or_cache_truncate(c, n) drops every token from position n on.  The
+ * rows are bit-identical to or_forward over the whole sequence. */
+typedef struct or_cache or_cache;
+or_cache* or_cache_new(const or_model* m, int capacity);
+void or_cache_free(or_cache* c);
+int or_cache_len(const or_cache* c);
+int or_cache_truncate(or_cache* c, int n);
+int or_cache_forward(or_model* m, or_cache* c, const int32_t* ids, int n, const int32_t* read, int nread, float* out);
+
 /* Head logits for hidden rows: for each row, the logits of cand ids
  * (ncand > 0) or of the whole vocabulary (ncand == 0).  out: rows*(ncand or V). */
 int or_head(or_model* m, const float* hidden, int rows, const int32_t* cand, int ncand, float* out);

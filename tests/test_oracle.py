@@ -136,3 +136,46 @@ def test_decision_rules(tiny_paths):
     c = m.decide(ids, 2, [20, 21], suffix=[30, 31])
     assert c["noul"] == c["probabilities"][1]
     assert abs(c["confidence"] - max(c["noul"], 1 - c["noul"])) < 1e-7
+
+
+@pytest.mark.parametrize("name", ["tiny-llama-q8_0", "tiny-qwen2-f16"])
+def test_cached_forward_bit_equal_to_whole_sequence(tiny_paths, name):
+    # Extending a cached prefix gives the same bits as one forward over the
+    # whole sequence: each row depends on its own token and earlier keys, and
+    # Matrix::apply computes every token row alone (src/tensor.rs:58-102).
+    m = oracle.Model(open(tiny_paths[name], "rb").read(), threads=3)
+    rng = np.random.default_rng(11)
+    ids = synth.token_ids(rng, m.vocab, 41)
+    whole = m.forward(ids, list(range(41)))
+    c = m.cache(60)
+    parts = [c.forward(ids[:17], list(range(17))), c.forward(ids[17:18], [0]), c.forward(ids[18:], list(range(23)))]
+    assert len(c) == 41
+    assert np.array_equal(np.concatenate(parts), whole)
+    # branch off the prefix: truncate and append a different tail
+    c.truncate(30)
+    tail = synth.token_ids(rng, m.vocab, 5)
+    got = c.forward(tail, [4])
+    want = m.forward(np.concatenate([ids[:30], tail]), [34])
+    assert np.array_equal(got, want)
+    with pytest.raises(ValueError):
+        c.truncate(40)
+    c.close()
+
+
+def test_cached_greedy_matches_recompute(tiny_paths):
+    m = oracle.Model(open(tiny_paths["tiny-llama-f16"], "rb").read(), threads=2)
+    ctx = list(synth.token_ids(np.random.default_rng(12), m.vocab, 25))
+    toks, margins = m.greedy(ctx, 5)
+    seq = list(ctx)
+    for s in range(5):
+        logits = m.head(m.forward(np.array(seq, np.int32), [len(seq) - 1]))[0]
+        assert toks[s] == int(np.argmax(logits))
+        seq.append(toks[s])
+    assert all(g >= 0 for g in margins)
+
+
+def test_attention_threads_bit_equal(tiny_paths):
+    blob = open(tiny_paths["tiny-qwen2-f16"], "rb").read()
+    ids = synth.token_ids(np.random.default_rng(13), 1000, 50)
+    outs = [oracle.Model(blob, threads=t).forward(ids, [0, 25, 49]) for t in (1, 4, 7)]
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
