@@ -194,16 +194,23 @@ int laya_tensor_f32(laya_model* m, const char* name, float* out, size_t max_elem
  * w (GGUF bytes of type `kind`), x [m][cols] F32, bias [rows] F32 (may be
  * NULL) and out [m][rows] F32 are DEVICE pointers the caller owns, and the
  * F16 staging of the GEMM lives in a fixed array of LAYA_STATIC_SCRATCH_BYTES
- * inside the library, which every GPU that loads the library holds until
- * the process exits.  Work runs on `stream` (a cudaStream_t, NULL for the
- * legacy default stream) on the current device; the call returns after it
- * finished.  Needing more than the limit — 256 B + rows*cols*4 +
- * (rows + m) * ceil8(cols) * 2 bytes, each part rounded up to 256 — is
- * rejected with LAYA_E_INVALID.  The first call on a device looks up the
- * array's device address; make that first call before any stream capture.
- * All calls on a device share the one array: calls that overlap on the GPU
- * (concurrent host threads or streams) race and must be serialised by the
- * caller.  It calls no cudaMalloc/cudaFree and no allocating library. */
+ * inside the library, which every GPU on which the library's module is
+ * loaded holds until the process exits.  Work runs on `stream` (a
+ * cudaStream_t, NULL for the legacy default stream) on the current device;
+ * the call returns after it finished.  Needing more than the limit — 256 B +
+ * rows * ceil8(cols) * 2 + m * ceil8(cols) * 2 bytes, each part rounded up to
+ * 256 (a 2048 x 2048 weight with m = 1024 fits) — is rejected with
+ * LAYA_E_INVALID.  The first call on a device is its set-up: it looks up the
+ * array's device address, and under CUDA's default lazy module loading that
+ * is also when the module, and the 16 MiB array with it, is created on the
+ * device.  So make the first call on each device early — before any stream
+ * capture, and before the caller's own pool claims the device's memory (or
+ * load modules eagerly, CUDA_MODULE_LOADING=EAGER).  A cudaDeviceReset in the
+ * process invalidates the looked-up address: do not call this entry point
+ * after one.  All calls on a device share the one array: calls that overlap
+ * on the GPU (concurrent host threads or streams) race and must be
+ * serialised by the caller.  It calls no cudaMalloc/cudaFree and no
+ * allocating library. */
 #define LAYA_STATIC_SCRATCH_BYTES (16u << 20)
 int laya_matrix_apply_static(uint32_t kind, const uint8_t* w, int rows, int cols, const float* x, int m,
                              const float* bias, float* out, void* stream);

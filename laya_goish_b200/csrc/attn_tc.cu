@@ -22,6 +22,7 @@
 // softmax warp sees S_j, P.V of page j-2 has finished: its P buffer may be
 // rewritten, and o_done is in phase j-1 or later, so its parity identifies
 // page j-1 unambiguously; the final read of O waits on its own barrier.
+#include <atomic>
 #include <cuda.h>
 
 #include <algorithm>
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(192, 1)
 template <int HD>
 static cudaError_t attn_tc_go(const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
                               const CUtensorMap& tv, cudaStream_t st) {
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {

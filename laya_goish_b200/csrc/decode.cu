@@ -10,6 +10,7 @@
 // All per-step inputs live at fixed device addresses, advanced by a
 // one-thread-block kernel, so the whole step is captured once as a CUDA
 // graph and replayed for every generated token.
+#include <atomic>
 #include <algorithm>
 #include <cfloat>
 #include <chrono>
@@ -448,7 +449,7 @@ __global__ void __launch_bounds__(256, (B <= 2 ? 3 : B <= 8 ? 2 : 1)) gemv2_kern
 
 template <int B, bool FAST, bool XS>
 static cudaError_t gemv2_bx(const GemvPlan& p, dim3 grid, size_t smem, cudaStream_t st) {
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
@@ -1013,7 +1014,7 @@ template <int HD, int G>
 static cudaError_t launch_dec3(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
                                const half* q, const int* tables, const DecSeq* seqs, int KV, float sl2,
                                int split_pages, int splits, float* part, unsigned* err, const PfList& pf) {
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
@@ -1031,7 +1032,7 @@ static cudaError_t launch_dec2(dim3 grid, cudaStream_t st, const half* q, const 
                                const int* tables, const DecSeq* seqs, int KV, float sl2, int split_pages, int splits,
                                float* part) {
   const int smem = (2 * 64 * (HD + 8) + 2 * 64 * HD) * 2 + (G * HD + G * 64) * 4;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {

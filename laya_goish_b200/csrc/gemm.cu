@@ -22,6 +22,7 @@
 // (src/models/openthai/model.rs:225-230) / QKV + RoPE + KV-cache write, then
 // stores to HBM.  Every TMA load reads this GPU's own memory into the issuing
 // CTA's own shared memory.
+#include <atomic>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -757,7 +758,7 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 template <int EPI, int HD>
 static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
                               cudaStream_t st) {
-  static bool configured[64] = {false};  // per device, per instantiation
+  static std::atomic<bool> configured[64];  // per device and instantiation; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
@@ -778,7 +779,7 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   // Per device: the attribute is set once and the number of CTA pairs that
   // fit at once is queried once, so the persistent grid never exceeds what is
   // co-resident (a pair left for a second wave would double the time).
-  static int clusters_fit[64] = {0};
+  static std::atomic<int> clusters_fit[64];
   int dev = 0;
   cudaGetDevice(&dev);
   auto kern = gemm_pair_kernel<EPI, HD>;

@@ -30,6 +30,7 @@
 // are partners: the RoPE pair (j, j + hd/2) of a q/k head, or the gate and
 // up rows of one FFN column.  RoPE + KV-cache append and SwiGLU are
 // therefore applied in registers in the epilogue.
+#include <atomic>
 #include <algorithm>
 #include <cstring>
 
@@ -678,7 +679,7 @@ static cudaError_t gemv3_go(const GemvSeq& q, int num_sms, cudaStream_t st) {
   const int nst = stages_for(q.ph[0].nb, q.kmax, NT);
   if (nst < 2) return cudaErrorInvalidValue;
   const size_t smem = gv_ring_offset(q.ph[0].nb, q.kmax, NT) + 1024 + (size_t)nst * GV_STAGE;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {

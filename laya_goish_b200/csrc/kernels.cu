@@ -1,9 +1,11 @@
 // Memory-bound kernels of the decision hot path and the paged causal GQA
 // attention.  Each cites the reference function it replaces.
+#include <atomic>
 #include <cfloat>
 #include <cstdlib>
 
 #include "common.cuh"
+#include "dequant.cuh"
 #include "kernels.h"
 #include "mma.cuh"
 #include "ptx.cuh"
@@ -14,79 +16,12 @@ namespace laya {
 // ---------------------------------------------------------------- dequant
 
 // gguf::decode (src/gguf.rs:250-336) on the original GGUF block bytes:
-// one thread per block (per element for F32/F16), same arithmetic order,
-// explicit round-to-nearest so the result is bit-identical.
+// one thread per block (per element for F32/F16), decode_raw_block's
+// arithmetic, written as F32.
 __global__ void dequant_raw_kernel(int kind, const uint8_t* __restrict__ b, size_t nblocks, float* __restrict__ out) {
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i >= nblocks) return;
-  switch (kind) {
-    case K_F32: {
-      const uint8_t* c = b + i * 4;
-      out[i] = bits_f32(c[0] | (c[1] << 8) | (c[2] << 16) | ((uint32_t)c[3] << 24));
-    } break;
-    case K_F16: {
-      const uint8_t* c = b + i * 2;
-      out[i] = half_bits(c[0] | (c[1] << 8));
-    } break;
-    case K_Q8_0: {
-      const uint8_t* c = b + i * 34;
-      float d = half_bits(c[0] | (c[1] << 8));
-      for (int j = 0; j < 32; j++) out[i * 32 + j] = __fmul_rn(d, (float)(int8_t)c[2 + j]);
-    } break;
-    case K_Q4_0: {
-      const uint8_t* c = b + i * 18;
-      float d = half_bits(c[0] | (c[1] << 8));
-      for (int j = 0; j < 16; j++) {
-        out[i * 32 + j] = __fmul_rn(d, __fsub_rn((float)(c[2 + j] & 15), 8.f));
-        out[i * 32 + j + 16] = __fmul_rn(d, __fsub_rn((float)(c[2 + j] >> 4), 8.f));
-      }
-    } break;
-    case K_Q4_K: {
-      const uint8_t* c = b + i * 144;
-      float d = half_bits(c[0] | (c[1] << 8)), dm = half_bits(c[2] | (c[3] << 8));
-      const uint8_t* sc = c + 4;
-      const uint8_t* qs = c + 16;
-      float* o = out + i * 256;
-      for (int g = 0; g < 4; g++) {
-        uint32_t s[2], m[2];
-        for (int t = 0; t < 2; t++) {
-          int j = g * 2 + t;
-          if (j < 4) {
-            s[t] = sc[j] & 63;
-            m[t] = sc[j + 4] & 63;
-          } else {
-            s[t] = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4);
-            m[t] = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-          }
-        }
-        for (int j = 0; j < 32; j++) {
-          uint32_t q = qs[g * 32 + j];
-          o[g * 64 + j] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s[0]), (float)(q & 15)), __fmul_rn(dm, (float)m[0]));
-          o[g * 64 + 32 + j] =
-              __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s[1]), (float)(q >> 4)), __fmul_rn(dm, (float)m[1]));
-        }
-      }
-    } break;
-    case K_Q6_K: {
-      const uint8_t* c = b + i * 210;
-      const uint8_t* ql = c;
-      const uint8_t* qh = c + 128;
-      const int8_t* sc = reinterpret_cast<const int8_t*>(c + 192);
-      float d = half_bits(c[208] | (c[209] << 8));
-      float* o = out + i * 256;
-      for (int n = 0; n < 2; n++)
-        for (int l = 0; l < 32; l++) {
-          int lo = n * 64 + l;
-          uint32_t hi = qh[n * 32 + l];
-          int si = n * 8 + l / 16;
-          uint32_t q[4] = {(ql[lo] & 15u) | ((hi & 3u) << 4), (ql[lo + 32] & 15u) | (((hi >> 2) & 3u) << 4),
-                           (uint32_t)(ql[lo] >> 4) | (((hi >> 4) & 3u) << 4),
-                           (uint32_t)(ql[lo + 32] >> 4) | (((hi >> 6) & 3u) << 4)};
-          for (int j = 0; j < 4; j++)
-            o[n * 128 + j * 32 + l] = __fmul_rn(__fmul_rn(d, (float)sc[si + j * 2]), __fsub_rn((float)q[j], 32.f));
-        }
-    } break;
-  }
+  decode_raw_block(kind, b, i, F32Sink{out});
 }
 
 cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st) {
@@ -313,7 +248,7 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
                     float* out32, cudaStream_t st, bool pdl, unsigned* err) {
   if (!nrows) return cudaSuccess;
   if (!rows && err && d % 4 == 0 && d <= 12288 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    static bool configured[64] = {false};
+    static std::atomic<bool> configured[64];  // per device; any host thread may launch
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
@@ -629,7 +564,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const half* __restrict__ q, i
 template <int HD>
 static cudaError_t attn_launch(const AttnParams& p, cudaStream_t st) {
   const int smem = 5 * 64 * HD * 2;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {

@@ -10,19 +10,35 @@
 // F16, the activations rounded to F16, an error word) lives in one fixed
 // array inside this library instead of in fresh allocations.
 //
-// The array is a file-scope __device__ object, so every GPU that loads the
-// library holds LAYA_STATIC_SCRATCH_BYTES of it until the process exits.
+// The array is a file-scope __device__ object: every GPU on which the
+// library's module is loaded holds LAYA_STATIC_SCRATCH_BYTES of it until the
+// process exits.  Under CUDA's lazy module loading (the default) the module,
+// and with it the array, is created on a device at the first call's set-up.
 // Host code never uses the symbol itself as a pointer: on the first call on
 // each device, with that device current, cudaGetSymbolAddress gives the
 // device address, which is cached per device and passed to the kernels.
+#include <algorithm>
 #include <mutex>
 
+#include "dequant.cuh"
 #include "engine.h"
 #include "gemm.h"
 #include "kernels.h"
 #include "laya_cuda.h"
 
 namespace {
+
+// GGUF blocks of a [rows][cols] weight -> the F16 [rows][ld] GEMM operand in
+// one pass (gguf::decode, src/gguf.rs:250-336, then round to nearest F16:
+// the same bits as decoding to F32 and rounding afterwards), with the pad
+// columns cols..ld-1 set to zero.
+__global__ void static_w16_kernel(int kind, const uint8_t* __restrict__ b, size_t nblocks, int rows, int cols,
+                                  int ld, half* __restrict__ y) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < nblocks) laya::decode_raw_block(kind, b, i, laya::F16PadSink{y, cols, ld});
+  const int pad = ld - cols;
+  if (i < (size_t)rows * pad) y[(i / pad) * ld + cols + i % pad] = __float2half_rn(0.f);
+}
 
 constexpr size_t kScratchBytes = LAYA_STATIC_SCRATCH_BYTES;
 __device__ __align__(256) unsigned char g_static_scratch[kScratchBytes];
@@ -59,9 +75,8 @@ extern "C" int laya_matrix_apply_static(uint32_t kind, const uint8_t* w, int row
     return fail(LAYA_E_INVALID, "invalid matrix arguments");
   if (m == 0) return 0;
   const int ld = (cols + 7) / 8 * 8;
-  // scratch layout: [error word | W decoded F32 | W F16 padded | x F16 padded]
-  const size_t off_wf = 256;
-  const size_t off_w16 = off_wf + align256((size_t)rows * cols * 4);
+  // scratch layout: [error word | W F16 padded | x F16 padded]
+  const size_t off_w16 = 256;
   const size_t off_x16 = off_w16 + align256((size_t)rows * ld * 2);
   const size_t need = off_x16 + align256((size_t)m * ld * 2);
   if (need > kScratchBytes)
@@ -77,15 +92,15 @@ extern "C" int laya_matrix_apply_static(uint32_t kind, const uint8_t* w, int row
   if (int rc = scratch_address(dev, &scratch)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned* err = reinterpret_cast<unsigned*>(scratch);
-  float* wf = reinterpret_cast<float*>(scratch + off_wf);
   half* w16 = reinterpret_cast<half*>(scratch + off_w16);
   half* x16 = reinterpret_cast<half*>(scratch + off_x16);
   // The error word is the only scratch that must start at zero; everything
   // else is fully rewritten before it is read.
   LAYA_CK(cudaMemsetAsync(err, 0, 4, st));
   const size_t wbytes = (size_t)rows * cols / block * size;
-  LAYA_CK(dequant_raw((int)kind, w, wbytes / size, wf, st));
-  LAYA_CK(f32_to_f16_pad(wf, rows, cols, ld, w16, st));
+  const size_t nblocks = wbytes / size, work = std::max(nblocks, (size_t)rows * (ld - cols));
+  static_w16_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>((int)kind, w, nblocks, rows, cols, ld, w16);
+  LAYA_CK(cudaGetLastError());
   LAYA_CK(f32_to_f16_pad(x, m, cols, ld, x16, st));
   GemmArgs a{};
   a.M = m;

@@ -400,7 +400,7 @@ class OpenThaiService(DecideService):
                     nxt[0] += 1
                 try:
                     results[i] = m.respond(self.tokenizer, reqs[i], self.raw, stop)
-                except LayaError as e:
+                except Exception as e:  # any failure stops the other workers and fails the batch
                     with lock:
                         errors.append((i, e))
                     return
@@ -412,7 +412,7 @@ class OpenThaiService(DecideService):
             t.join()
         if errors:
             # the failure that stopped the others, not the cancels it caused
-            first = [e for _, e in errors if e.code != E_CANCELED] or [e for _, e in errors]
+            first = [e for _, e in errors if getattr(e, "code", None) != E_CANCELED] or [e for _, e in errors]
             if canceled is not None and canceled():
                 raise LayaError(E_CANCELED, "request canceled")
             raise first[0]
@@ -453,6 +453,8 @@ class OpenThaiService(DecideService):
                 if e.code == E_CANCELED:
                     return _error(408, "request_canceled", e.message)
                 return _error(500, "internal_error", e.message)
+            except Exception as e:  # a failure outside the library (model wrapper, tokenizer) is a 500 too
+                return _error(500, "internal_error", str(e) or type(e).__name__)
             ms = int((time.perf_counter() - start) * 1000)
         finally:
             self._busy.release()

@@ -203,6 +203,31 @@ def test_batch_shared_over_several_models(served):
     assert r.status == 408
 
 
+def test_non_library_failure_on_one_device_fails_the_batch(served):
+    # A worker's exception that is not a LayaError (here a RuntimeError from
+    # one model's forward on the third state) still stops the other worker
+    # and maps to 500, never a 200 with missing results.
+    import threading
+
+    m, tok, w, _ = served
+    seen = []
+    lock = threading.Lock()
+
+    def flaky(ids, positions):
+        with lock:
+            seen.append(1)
+            n = len(seen)
+        if n == 3:
+            raise RuntimeError("numpy blew up")
+        return oracle.ot_forward(w, ids, positions)
+
+    batch = {"states": ["a", "b", "c", "d", "e", "f"], "questions": REQ["questions"], "order_invariant": True}
+    models = [_model_like(m, flaky), _model_like(m, flaky)]
+    r = frontend.OpenThaiService(models, tok).handle("POST", "/v1/decide/batch", json.dumps(batch))
+    assert r.status == 500 and "numpy blew up" in r.body["error"]["message"]
+    assert len(seen) < 6 * 3  # the batch stopped early
+
+
 def test_model_without_gpu_fails_cleanly(tmp_path):
     torch = pytest.importorskip("torch")
     if torch.cuda.is_available():
