@@ -1,13 +1,16 @@
 """Benchmark of the decision hot path (BASELINE.json metric: decide requests/s
-and prefill tok/s).
+and prefill tok/s at 1/2/4/8 GPUs, decode GEMV HBM GB/s against peak).
 
 Workload: Llama-16L decoder (d 2048, 32/8 heads, FFN 8192,
-V 32000) with Q8_0 weights written from seed; per GPU a batch of 64 decide
+V 32000) with Q8_0 weights written from seed; ONE batch of 64 decide
 requests of 512 uniform-random token ids sharing one "choose" question over
-4 single-token options.  One step = one laya_decide_batch call over that
-batch.  Scaling is weak: every rank runs its own 64-request batch on its own
-GPU (requests shard with no collective); value = all requests / max device
-time over ranks.
+4 single-token options, sharded by request across the N ranks (contiguous
+ranges, balanced by tokens, as laya_decide_batch shards across devices).
+One step = one laya_decide_batch call per rank over its share.  Scaling is
+strong: value = 64 requests / the slowest rank's time.  At N > 1 the line
+also carries the weak figure (64 requests on every rank).  The line's
+`decode` object is configs[4] on the same decoder: context 4096, greedy
+tokens at batch 1 and 8 per GPU, timed apart from the decide steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -36,8 +39,9 @@ from laya_goish_b200 import synth  # noqa: E402
 
 REQUESTS, TOKENS, OPTIONS = 64, 512, 4
 CFG = synth.CONFIGS["cfg1"]
-WORKLOAD = ("cfg1: Llama-16L (d 2048, 32/8 heads, FFN 8192, V 32000) Q8_0 from seed; "
-            f"{REQUESTS} requests x {TOKENS} tokens per GPU, one choose question over {OPTIONS} single-token options")
+WORKLOAD = ("cfg1: Llama-16L (d 2048, 32/8 heads, FFN 8192, V 32000) Q8_0 from seed; one batch of "
+            f"{REQUESTS} requests x {TOKENS} tokens sharded across the GPUs, one choose question over {OPTIONS} "
+            "single-token options")
 
 
 # DRAM bytes (read + write) per GEMM launch at the benchmark size: in one ncu
@@ -62,6 +66,23 @@ def inputs(rank: int, requests: int = REQUESTS):
     prompts = [synth.token_ids(rng, CFG.vocab, TOKENS) for _ in range(requests)]
     cand = synth.candidates(np.random.default_rng(1), CFG.vocab, OPTIONS)
     return prompts, cand
+
+
+def shard(lengths, world: int, rank: int):
+    """Contiguous request range [a, b) of `rank`: cuts placed where the
+    running token count crosses rank/world of the total (the split
+    laya_decide_batch makes across its devices)."""
+    total = float(sum(lengths))
+    csum = np.concatenate([[0], np.cumsum(lengths)])
+
+    def cut(r):
+        if r <= 0:
+            return 0
+        if r >= world:
+            return len(lengths)
+        return int(np.searchsorted(csum, total * r / world, side="left"))
+
+    return cut(rank), cut(rank + 1)
 
 
 def peaks():
@@ -198,13 +219,90 @@ def run_reference(args):
     value = len(times) / total
     line = {"impl": "reference", "metric": "decide requests/s", "value": value, "unit": "req/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000 * total / len(times), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": 1000 * total / len(times), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "step": f"one {TOKENS}-token request (bounded sample of the batch)"},
             "cpu_baseline": {"value": value, "unit": "req/s", "cores": threads, "kind": "port",
                              "sample": f"{len(times)} requests of {TOKENS} tokens, one per step"},
             "e2e": {"value": value, "unit": "req/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def timed_steps(e, prompts, qs, steps, dist):
+    """K decide steps between barriers: (device ms, wall ms, launches, h2d, d2h) summed."""
+    import torch
+
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev_ms, wall, launches, h2d, d2h = 0.0, 0.0, 0, 0, 0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        e.decide_batch(prompts, qs)
+        wall += (time.perf_counter() - t0) * 1000.0
+        t = e.timing()
+        dev_ms += t["device_ms"]
+        launches += t["launches"]
+        h2d += t["h2d_bytes"]
+        d2h += t["d2h_bytes"]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    return dev_ms, wall, launches, h2d, d2h
+
+
+def decode_bytes(batch: int, ctx: int, gen: int):
+    """Algorithmic HBM bytes of one decode step: the Q8_0 weights incl. the
+    lm_head once, plus every sequence's K and V read once (mean context)."""
+    qd, kd = CFG.heads * CFG.hd, CFG.kv * CFG.hd
+    per_layer = CFG.d * (qd + 2 * kd) + qd * CFG.d + 3 * CFG.d * CFG.ffn
+    wbytes = (per_layer * CFG.layers + CFG.vocab * CFG.d) * 34 / 32
+    kv_bytes = batch * CFG.layers * 2 * (ctx + gen / 2) * kd * 2
+    return wbytes, kv_bytes
+
+
+def decode_point(e, batch: int, ctx: int, gen: int, dist, device):
+    """One decode run: `batch` sequences of `ctx` seeded ids,
+    `gen` greedy tokens; device time of steps 1..gen-1 (CUDA events of the
+    library), max over ranks."""
+    rng = np.random.default_rng(4)
+    ctxs = [synth.token_ids(rng, CFG.vocab, ctx) for _ in range(batch)]
+    if dist:
+        dist.barrier()
+    _, st = e.decode(ctxs, gen)
+    t = e.timing()
+    ms, = reduce_max([t["device_ms"] / (gen - 1)], dist, device)
+    wbytes, kv_bytes = decode_bytes(batch, ctx, gen)
+    pk, pk_kind = peaks()
+    gbs = (wbytes + kv_bytes) / (ms / 1000) / 1e9
+    return {"batch_per_gpu": batch, "ms_per_token": ms, "tokens_per_s_per_gpu": batch / (ms / 1000),
+            "step_gbs": gbs, "step_frac": gbs / pk["hbm_gbs"], "weight_bytes": wbytes, "kv_bytes": kv_bytes,
+            "launches_per_step": t["launches"] / (gen - 1)}
+
+
+def decode_cpu_baseline(path: str, ctx: int, steps: int = 3) -> dict:
+    """The oracle on configs[4] at batch 1: a greedy decode step (the
+    reference's Matrix::apply with one token row, its single-threaded
+    attention over the cached keys, the full-vocabulary head) at context
+    `ctx`, all host threads for the matrices.  Bounded sample: the cache is
+    filled with arbitrary K/V for the timing (the work per step does not
+    depend on the values), then `steps` steps are timed."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    o = oracle.Model(open(path, "rb").read(), threads=threads)
+    c = o.cache(ctx + steps)
+    c.fill_for_timing(ctx)
+    tok = 5
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        h = c.forward([tok], [0])
+        tok = int(np.argmax(o.head(h)[0]))
+    dt = (time.perf_counter() - t0) / steps
+    c.close()
+    o.close()
+    return {"value": 1000 * dt, "unit": "ms/token", "cores": threads, "kind": "port",
+            "sample": f"{steps} greedy steps at context {ctx}, batch 1 (cache filled for timing)"}
 
 
 def run_ours(args):
@@ -227,7 +325,10 @@ def run_ours(args):
     from laya_goish_b200 import engine
     from laya_goish_b200.engine import Question
 
-    prompts, cand = inputs(rank, args.requests)
+    # one 64-request batch, this rank's contiguous share
+    batch, cand = inputs(0, args.requests)
+    a, b = shard([len(p) for p in batch], world, rank)
+    prompts = batch[a:b]
     qs = [Question("choice", cand)]
     e = engine.Engine(path, devices=[local])
     clk = Clocks(local).start()
@@ -235,61 +336,67 @@ def run_ours(args):
         e.decide_batch(prompts, qs)
     e.profile(True)
     e.profile_read()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    dev_ms, wall, launches, h2d, d2h = 0.0, 0.0, 0, 0, 0
     clk.begin()
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        e.decide_batch(prompts, qs)
-        wall += (time.perf_counter() - t0) * 1000.0
-        t = e.timing()
-        dev_ms += t["device_ms"]
-        launches += t["launches"]
-        h2d += t["h2d_bytes"]
-        d2h += t["d2h_bytes"]
-    torch.cuda.synchronize()
+    dev_ms, wall, launches, h2d, d2h = timed_steps(e, prompts, qs, args.steps, dist)
     clk.end()
-    if dist:
-        dist.barrier()
-    clk.stop()
     prof = e.profile_read()
     e.profile(False)
     dev_ms, wall = reduce_max([dev_ms, wall], dist, "cuda")
-    value = throughput(args.requests, world, args.steps, dev_ms)
-    e2e = throughput(args.requests, world, args.steps, wall)
-    # roofline of the dominant kernel class: the tcgen05 GEMMs
+    value = throughput(args.requests, 1, args.steps, dev_ms)
+    e2e = throughput(args.requests, 1, args.steps, wall)
+    # roofline of the dominant kernel class on this rank: the tcgen05 GEMMs
+    mine = b - a
     gemm_ms = sum(v[1] for k, v in prof.items() if k.startswith("gemm_"))
     gemm_launches = sum(v[0] for k, v in prof.items() if k.startswith("gemm_"))
-    gemm_flops = gemm_flops_per_token(CFG) * args.requests * TOKENS * args.steps
+    gemm_flops = gemm_flops_per_token(CFG) * mine * TOKENS * args.steps
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None
     pk, pk_kind = peaks()
     peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
     step_ms = dev_ms / args.steps
-    shares = {k: round(v[1] / dev_ms, 4) for k, v in sorted(prof.items())} if dev_ms else {}
+    rank_ms = sum(v[1] for v in prof.values())
+    shares = {k: round(v[1] / rank_ms, 4) for k, v in sorted(prof.items())} if rank_ms else {}
     line = {
         "metric": "decide requests/s", "value": value, "unit": "req/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "requests_per_gpu": args.requests, "prompt_tokens": TOKENS,
-                   "weights": "Q8_0 (RTN from seeded F16 N(0,0.02))", "compute": "F16 operands, F32 accumulation",
-                   "l2": "working set > L2 (weights 1.03 GB, activations 0.5 GB/layer); no flush needed",
-                   "parallelism": f"request sharding x{world}, full replica per GPU, no collective"},
+        "config": {"workload": WORKLOAD, "global_batch": args.requests, "requests_per_gpu": mine,
+                   "prompt_tokens": TOKENS, "weights": "Q8_0 (RTN from seeded F16 N(0,0.02))",
+                   "compute": "F16 operands, F32 accumulation",
+                   "l2": "working set > L2 (weights 1.03 GB, activations 0.5 GB/layer at 64 requests); no flush",
+                   "parallelism": f"request sharding x{world} (contiguous ranges balanced by tokens), full replica "
+                                  "per GPU, no collective"},
         "prefill_tok_s": value * TOKENS,
         "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel + gemm_tc_kernel (tcgen05, all prefill GEMMs)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if achieved else None, "traffic": GEMM_TRAFFIC_BYTES,
                      "traffic_unit": "bytes per GEMM launch (ncu DRAM read+write, 16-request capture x 4)",
                      "peak_kind": f"{pk_kind} bf16 dense sustained", "launches": gemm_launches,
-                     "share_of_step": round(gemm_ms / dev_ms, 4) if dev_ms else None,
-                     "flops_per_step": gemm_flops / args.steps},
+                     "share_of_step": round(gemm_ms / rank_ms, 4) if rank_ms else None,
+                     "flops_per_step": gemm_flops / args.steps, "rank": rank},
         "kernel_shares": shares,
         "e2e": {"value": e2e, "unit": "req/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
         "gpu_launches": launches,
-        "clocks": clk.summary(),
     }
+    if world > 1:
+        # weak scaling figure: every rank runs a whole 64-request batch
+        own, _ = inputs(1000 + rank, args.requests)
+        e.decide_batch(own, qs)
+        wsteps = max(1, min(args.steps, 3))
+        wms, _, _, _, _ = timed_steps(e, own, qs, wsteps, dist)
+        wms, = reduce_max([wms], dist, "cuda")
+        line["weak"] = {"value": throughput(args.requests, world, wsteps, wms), "unit": "req/s",
+                        "requests_per_gpu": args.requests, "steps": wsteps, "ms_per_step": wms / wsteps}
+    clk.stop()
+    line["clocks"] = clk.summary()
+    if not args.no_decode:
+        dec = {"workload": f"configs[4]: the same Q8_0 decoder, context {args.ctx}, {args.gen} greedy tokens, "
+                           "one CUDA graph per step; device time of the steps (CUDA events), max over ranks",
+               "points": [decode_point(e, bsz, args.ctx, args.gen, dist, "cuda") for bsz in (1, 8)],
+               "peak_gbs": pk["hbm_gbs"], "peak_kind": pk_kind}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            dec["cpu_baseline"] = decode_cpu_baseline(path, args.ctx)
+        line["decode"] = dec
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(path, prompts, cand)
     e.close()
@@ -323,6 +430,35 @@ def aux_questions(name, vocab):
         return [Question("score", synth.token_ids(rng, vocab, 15).reshape(5, 3))], 15
     return [Question("noul", synth.candidates(rng, vocab, 2), suffix=synth.token_ids(rng, vocab, 16))
             for _ in range(3)], 48
+
+
+def aux_cpu_baseline(name, path, prompts, qs) -> dict:
+    """The oracle on a bounded sample of an auxiliary configuration, all host
+    threads for the matrices and the reference's single-threaded attention.
+    cfg0 / cfg2: one whole request (cfg2's 5 continuations branch off its
+    768-token prefix, computed once).  cfg3: a 14 TFLOP request is hours of
+    CPU work, so one 128-token prefix is timed and scaled to the request's
+    1024 + 3 x 16 tokens by its matrix FLOPs (attention grows faster than
+    that, so the extrapolated CPU time is a lower bound)."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    o = oracle.Model(open(path, "rb").read(), threads=threads)
+    t0 = time.perf_counter()
+    if name == "cfg3":
+        n = 128
+        o.forward(prompts[0][:n], [n - 1])
+        dt = (time.perf_counter() - t0) * (len(prompts[0]) + 3 * 16) / n
+        sample = f"one {n}-token prefix of a cfg3 request, extrapolated by matrix FLOPs to 1024 + 3 x 16 tokens"
+    else:
+        for q in qs:
+            kind, opts, suf = q.arrays()
+            o.decide(prompts[0], kind, opts, suf)
+        dt = time.perf_counter() - t0
+        sample = f"1 request of {len(prompts[0])} tokens, {dt:.1f} s"
+    o.close()
+    return {"value": 1.0 / dt, "unit": "req/s", "cores": threads, "kind": "port", "sample": sample,
+            "extrapolated": name == "cfg3"}
 
 
 def run_aux(args):
@@ -381,6 +517,8 @@ def run_aux(args):
         "kernel_shares": {k: round(v[1] / dev_ms, 4) for k, v in sorted(prof.items())} if dev_ms else {},
         "clocks": clk.summary(),
     }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = aux_cpu_baseline(args.workload, path, prompts, qs)
     print(json.dumps(line), flush=True)
 
 
@@ -433,6 +571,8 @@ def run_decode(args):
     if out["gemv_gbs"]:
         out["gemv_frac"] = out["gemv_gbs"] / pk["hbm_gbs"]
     out["step_frac"] = out["step_gbs"] / pk["hbm_gbs"]
+    if not args.no_cpu_baseline and args.batch == 1:
+        out["cpu_baseline"] = decode_cpu_baseline(path, args.ctx)
     print(json.dumps(out), flush=True)
 
 
@@ -550,7 +690,8 @@ def main():
     ap.add_argument("--ot-tokens", type=int, default=1024, help="openthai: tokens per pass")
     ap.add_argument("--ot-cpu-tokens", type=int, default=128, help="openthai: tokens of the CPU baseline pass")
     ap.add_argument("--requests", type=int, default=REQUESTS,
-                    help="requests per GPU (64 is the benchmark; smaller only for profiler captures)")
+                    help="requests of the batch (64 is the benchmark; smaller only for profiler captures)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode object of the cfg1 line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

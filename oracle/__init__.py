@@ -65,6 +65,8 @@ def lib() -> ctypes.CDLL:
         L.or_cache_len.argtypes = [P]
         L.or_cache_truncate.argtypes = [P, ctypes.c_int]
         L.or_cache_forward.argtypes = [P, P, P, ctypes.c_int, P, ctypes.c_int, P]
+        L.or_cache_fill_timing.argtypes = [P, P, ctypes.c_int]
+        L.or_model_attn_threads.argtypes = [P, ctypes.c_int]
         i = ctypes.c_int
         L.or_ot_full.argtypes = [P, i, i, i, i, i, i, ctypes.c_float, P, P, P, P, P, P, i, P]
         L.or_ot_delta.argtypes = [P, i, i, i, i, P, P, P, P, P, P, P, P, P, i, P]
@@ -132,7 +134,10 @@ def confidence(p) -> float:
 class Model:
     """The oracle decoder: GGUF image → F32 weights (as the reference loads them)."""
 
-    def __init__(self, blob: bytes | np.ndarray, threads: int = 1):
+    def __init__(self, blob: bytes | np.ndarray, threads: int = 1, attn_threads: int = 1):
+        """threads: Matrix::apply workers.  attn_threads: workers of the
+        attention loop; 1 keeps the reference's single-threaded loop (the
+        timed baseline), more give the same bits sooner (the checkers)."""
         self._buf = np.frombuffer(blob, dtype=np.uint8) if not isinstance(blob, np.ndarray) else blob
         err = ctypes.create_string_buffer(256)
         h = lib().or_model_load(_p(self._buf), len(self._buf), threads, err, 256)
@@ -140,6 +145,7 @@ class Model:
             raise ValueError(err.value.decode())
         self.h = ctypes.c_void_p(h)
         L = lib()
+        L.or_model_attn_threads(self.h, attn_threads)
         self.d, self.layers, self.vocab, self.heads, self.kv, self.hd, self.ffn, self.ctx = (
             L.or_model_dim(self.h, i) for i in range(8))
 
@@ -232,6 +238,11 @@ class Cache:
         if lib().or_cache_forward(self.m.h, self.h, _p(ids), len(ids), _p(read), len(read), _p(out)):
             raise ValueError("invalid token sequence or cache overflow")
         return out
+
+    def fill_for_timing(self, n: int) -> None:
+        """Timing only: positions 0..n-1 hold arbitrary K/V values."""
+        if lib().or_cache_fill_timing(self.h, self.m.h, n):
+            raise ValueError("fill past the cache capacity")
 
     def truncate(self, n: int) -> None:
         if lib().or_cache_truncate(self.h, n):

@@ -465,6 +465,7 @@ typedef struct {
 struct or_model {
   or_gguf g;
   int d, L, V, H, KV, hd, ffn, threads, ctx;
+  int attn_threads; /* 1 = the reference's single-threaded attention loop */
   float eps, theta;
   const uint8_t* embd;
   uint32_t embd_kind;
@@ -551,6 +552,7 @@ or_model* or_model_load(const uint8_t* bytes, size_t n, int threads, char* err, 
   m->g.err = err;
   m->g.errlen = errlen;
   m->threads = threads < 1 ? 1 : threads;
+  m->attn_threads = 1;
   if (gguf_parse(&m->g)) goto bad;
   const or_kv* arch = gguf_kv(&m->g, "general.architecture");
   if (!arch || !arch->str || (strcmp(arch->str, "llama") && strcmp(arch->str, "qwen2"))) {
@@ -744,6 +746,27 @@ static void rope_at(float* buf, int s, int pos0, int heads, int hd, float theta)
       }
 }
 
+void or_model_attn_threads(or_model* m, int n) { m->attn_threads = n < 1 ? 1 : n; }
+
+/* Timing only: marks positions 0..n-1 as cached with arbitrary K/V values
+ * (a seeded pattern of small numbers), so a decode step at context n can be
+ * timed without first prefilling n tokens.  Attention does the same work
+ * whatever the values are; nothing computed from such a cache is checked. */
+int or_cache_fill_timing(or_cache* c, const or_model* m, int n) {
+  if (n < 0 || n > c->cap) return -1;
+  size_t kd = (size_t)m->KV * m->hd;
+  uint32_t st = 12345u;
+  for (int l = 0; l < m->L; l++)
+    for (size_t i = 0; i < (size_t)n * kd; i++) {
+      st = st * 1664525u + 1013904223u;
+      float v = (float)((st >> 9) & 1023) / 1024.f - 0.5f;
+      c->k[(size_t)l * c->cap * kd + i] = v;
+      c->v[(size_t)l * c->cap * kd + i] = -v;
+    }
+  c->n = n;
+  return 0;
+}
+
 int or_cache_forward(or_model* m, or_cache* c, const int32_t* ids, int s, const int32_t* read, int nread, float* out) {
   int d = m->d, H = m->H, KV = m->KV, hd = m->hd, ffn = m->ffn;
   int qd = H * hd, kd = KV * hd, grp = H / KV;
@@ -766,7 +789,7 @@ int or_cache_forward(or_model* m, or_cache* c, const int32_t* ids, int s, const 
   /* embedding rows decoded per used id (src/models/openthai/model.rs:205-213) */
   for (int i = 0; i < s; i++) or_decode(m->embd_kind, m->embd + (size_t)ids[i] * rowb, rowb, x + (size_t)i * d);
   float scale = 1.f / sqrtf((float)hd); /* src/tensor.rs:174 */
-  int nth = m->threads < s * H ? m->threads : s * H;
+  int nth = m->attn_threads < s * H ? m->attn_threads : s * H;
   if (nth > 256) nth = 256;
   for (int l = 0; l < m->L; l++) {
     or_layer* b = &m->layer[l];

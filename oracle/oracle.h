@@ -84,6 +84,11 @@ void or_cache_free(or_cache* c);
 int or_cache_len(const or_cache* c);
 int or_cache_truncate(or_cache* c, int n);
 int or_cache_forward(or_model* m, or_cache* c, const int32_t* ids, int n, const int32_t* read, int nread, float* out);
+/* Timing only: positions 0..n-1 cached with arbitrary values. */
+int or_cache_fill_timing(or_cache* c, const or_model* m, int n);
+/* Threads of the attention loop (default 1, as in the reference, whose
+ * attention is single-threaded; more threads give the same bits). */
+void or_model_attn_threads(or_model* m, int n);
 
 /* Head logits for hidden rows: for each row, the logits of cand ids
  * (ncand > 0) or of the whole vocabulary (ncand == 0).  out: rows*(ncand or V). */

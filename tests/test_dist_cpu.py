@@ -1,6 +1,7 @@
 """The N>1 bench path on CPU: two gloo ranks reduce their timings with MAX
-(the slowest rank sets the time) and the whole-job throughput counts every
-rank's requests (weak scaling, no data-path collective)."""
+(the slowest rank sets the time); the strong-scaling line splits one batch
+into contiguous per-rank ranges balanced by tokens, and the weak figure
+counts every rank's whole batch (no data-path collective)."""
 import os
 import socket
 
@@ -25,7 +26,8 @@ def _worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         dev_ms, wall = bench.reduce_max([100.0 + 50 * rank, 300.0 - rank], dist, "cpu")
-        q.put((rank, dev_ms, wall, bench.throughput(64, world, 10, dev_ms)))
+        a, b = bench.shard([512] * 64, world, rank)
+        q.put((rank, dev_ms, wall, bench.throughput(64, world, 10, dev_ms), (a, b)))
     finally:
         dist.destroy_process_group()
 
@@ -41,9 +43,10 @@ def test_two_rank_max_reduction_and_weak_throughput():
         p.join(120)
         assert p.exitcode == 0
     got = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, dev_ms, wall, tput in got:
+    for rank, dev_ms, wall, tput, _ in got:
         assert dev_ms == 150.0 and wall == 300.0  # max over ranks on every rank
         assert tput == pytest.approx(64 * 2 * 10 / 0.150)
+    assert [g[4] for g in got] == [(0, 32), (32, 64)]  # one 64-request batch, split
 
 
 def test_single_process_reduction_is_identity():
@@ -51,3 +54,18 @@ def test_single_process_reduction_is_identity():
 
     assert bench.reduce_max([1.5, 2.5], None, "cpu") == [1.5, 2.5]
     assert bench.throughput(64, 1, 10, 1000.0) == pytest.approx(640.0)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8, 3])
+def test_shard_ranges_cover_the_batch_in_order(world):
+    import bench
+
+    lengths = [512] * 64
+    ranges = [bench.shard(lengths, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == 64
+    assert all(ranges[i][1] == ranges[i + 1][0] for i in range(world - 1))
+    if 64 % world == 0:
+        assert all(b - a == 64 // world for a, b in ranges)
+    # ragged lengths: balanced by tokens, not by count
+    ragged = [1000] + [100] * 10
+    assert bench.shard(ragged, 2, 0) == (0, 1) and bench.shard(ragged, 2, 1) == (1, 11)

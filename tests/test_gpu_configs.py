@@ -52,7 +52,7 @@ def test_cfg3_geometry_matches_oracle():
     with engine.Engine(path) as e:
         assert e.info["heads"] // e.info["kv_heads"] == 7
         got = e.decide(prompt, qs)
-    o = oracle.Model(open(path, "rb").read(), threads=THREADS)
+    o = oracle.Model(open(path, "rb").read(), threads=THREADS, attn_threads=THREADS)
     c = o.cache(1024 + 16)
     c.forward(prompt, [])
     worst = 0.0
@@ -75,7 +75,7 @@ def test_cfg2_full_request_matches_oracle():
     q = Question("score", opts)
     with engine.Engine(path) as e:
         got = e.decide(prompt, [q])[0]
-    o = oracle.Model(open(path, "rb").read(), threads=THREADS)
+    o = oracle.Model(open(path, "rb").read(), threads=THREADS, attn_threads=THREADS)
     want = o.decide(prompt, 1, opts)
     o.close()
     _check("cfg2 score over 5 x 3-token continuations", got, want["probabilities"], "score")
@@ -91,7 +91,7 @@ def test_cfg1_batch_requests_match_oracle():
     q = Question("choice", synth.candidates(np.random.default_rng(1), 32000, 4))
     with engine.Engine(path) as e:
         got = e.decide_batch(prompts, [q])
-    o = oracle.Model(open(path, "rb").read(), threads=THREADS)
+    o = oracle.Model(open(path, "rb").read(), threads=THREADS, attn_threads=THREADS)
     worst = 0.0
     for i in (0, 21, 42, 63):
         want = o.decide(prompts[i], 0, np.asarray(q.options).reshape(-1, 1))
@@ -112,7 +112,7 @@ def test_long_context_decode_matches_oracle(nseq):
     steps = 32
     with engine.Engine(path) as e:
         toks, _ = e.decode(ctxs, steps)
-    o = oracle.Model(open(path, "rb").read(), threads=THREADS)
+    o = oracle.Model(open(path, "rb").read(), threads=THREADS, attn_threads=THREADS)
     worst, exact = 0.0, 0
     for i, ctx in enumerate(ctxs):
         c = o.cache(len(ctx) + steps)

@@ -19,7 +19,7 @@ ATOL, RTOL = 1e-3, 1e-2
 def models(tiny_paths):
     out = {}
     for name, path in tiny_paths.items():
-        out[name] = (engine.Engine(path), oracle.Model(open(path, "rb").read(), threads=8))
+        out[name] = (engine.Engine(path), oracle.Model(open(path, "rb").read(), threads=8, attn_threads=8))
     yield out
     for e, o in out.values():
         e.close()

@@ -28,7 +28,7 @@ def oracle_greedy(o, ctx, steps):
                                        ("small-llama-q8_0", 16), ("tiny-llama-q8_0", 9), ("tiny-llama-f16", 12)])
 def test_greedy_decode_matches_oracle(tiny_paths, name, nseq):
     path = tiny_paths[name]
-    o = oracle.Model(open(path, "rb").read(), threads=8)
+    o = oracle.Model(open(path, "rb").read(), threads=8, attn_threads=8)
     rng = np.random.default_rng(nseq)
     ctxs = [synth.token_ids(rng, o.vocab, int(n)) for n in rng.integers(5, 140, size=nseq)]
     steps = 6

@@ -29,7 +29,7 @@ def test_full_config_decide_matches_oracle(full):
     prompt = synth.token_ids(rng, V, n)
     q = Question(kind, synth.candidates(rng, V, k))
     got = e.decide(prompt, [q])[0]
-    o = oracle.Model(open(path, "rb").read(), threads=16)
+    o = oracle.Model(open(path, "rb").read(), threads=16, attn_threads=16)
     kind_i, opts, suf = q.arrays()
     want = o.decide(prompt, kind_i, opts, suf)
     o.close()

@@ -143,7 +143,7 @@ def test_cached_forward_bit_equal_to_whole_sequence(tiny_paths, name):
     # Extending a cached prefix gives the same bits as one forward over the
     # whole sequence: each row depends on its own token and earlier keys, and
     # Matrix::apply computes every token row alone (src/tensor.rs:58-102).
-    m = oracle.Model(open(tiny_paths[name], "rb").read(), threads=3)
+    m = oracle.Model(open(tiny_paths[name], "rb").read(), threads=3, attn_threads=3)
     rng = np.random.default_rng(11)
     ids = synth.token_ids(rng, m.vocab, 41)
     whole = m.forward(ids, list(range(41)))
@@ -177,5 +177,5 @@ def test_cached_greedy_matches_recompute(tiny_paths):
 def test_attention_threads_bit_equal(tiny_paths):
     blob = open(tiny_paths["tiny-qwen2-f16"], "rb").read()
     ids = synth.token_ids(np.random.default_rng(13), 1000, 50)
-    outs = [oracle.Model(blob, threads=t).forward(ids, [0, 25, 49]) for t in (1, 4, 7)]
+    outs = [oracle.Model(blob, threads=t, attn_threads=t).forward(ids, [0, 25, 49]) for t in (1, 4, 7)]
     assert all(np.array_equal(outs[0], o) for o in outs[1:])
