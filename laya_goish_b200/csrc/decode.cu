@@ -1241,63 +1241,13 @@ struct StepIO {
   int kv_used;     // KV pages in use per layer (pages 0 .. kv_used - 1)
 };
 
-// L2 prefetch plan of a chained decode step.  The step reads HBM in launch
-// order: the first layer's qkv GEMV, then per layer the attention (its K and
-// V pages) and the chained GEMV launch (attention output, gate/up, down, the
-// next layer's qkv or the head).  Each launch asks for the stream's bytes
-// from where the previous launch's request ended (never before its own data
-// past what it loads at once) up to `window` bytes past the end of its own
-// data, wrapping into the next step, so HBM keeps streaming while grid
-// barriers and launch boundaries pass.  window 0 turns prefetching off.
-struct PfRange {
-  const uint8_t* p;
-  size_t n;
-};
-struct PfKernel {
-  std::vector<PfRange> own;  // this launch's reads, in order
-  size_t direct;             // leading bytes of `own` the launch loads at once (not prefetched)
-};
-
-static std::vector<PfList> pf_plan(const std::vector<PfKernel>& ks, size_t window) {
-  std::vector<PfList> out(ks.size(), PfList{});
-  std::vector<PfRange> flat;
-  std::vector<size_t> flat_at, start(ks.size()), end(ks.size());
-  size_t total = 0;
-  for (size_t k = 0; k < ks.size(); k++) {
-    start[k] = total;
-    for (const PfRange& r : ks[k].own) {
-      if (!r.n) continue;
-      flat.push_back(r);
-      flat_at.push_back(total);
-      total += r.n;
-    }
-    end[k] = total;
-  }
-  if (!window || !total) return out;
-  size_t cursor = 0;
-  for (size_t k = 0; k < ks.size(); k++) {
-    size_t a = std::max(cursor, start[k] + ks[k].direct);
-    a = (a + 15) & ~size_t(15);
-    const size_t b = std::min(end[k] + window, start[k] + total);
-    PfList& L = out[k];
-    while (a < b && L.count < PF_MAX) {
-      const size_t pos = a % total;
-      size_t i = std::upper_bound(flat_at.begin(), flat_at.end(), pos) - flat_at.begin() - 1;
-      const size_t in = pos - flat_at[i];
-      const size_t len = std::min(flat[i].n - in, b - a);
-      L.p[L.count] = flat[i].p + in;
-      L.n[L.count] = len;
-      L.count++;
-      a += len;
-    }
-    cursor = std::max(cursor, a);
-  }
-  return out;
-}
-
+// L2 prefetch plan of a chained decode step (pf_plan): the step reads HBM in
+// launch order: the first layer's qkv GEMV, then per layer the attention (its
+// K and V pages) and the chained GEMV launch (attention output, gate/up,
+// down, the next layer's qkv or the head).
 static size_t pf_window() {
   const char* e = std::getenv("LAYA_PF_MB");
-  const long v = e ? std::atol(e) : 48;
+  const long v = e ? std::atol(e) : 0;
   return v > 0 ? (size_t)v << 20 : 0;
 }
 

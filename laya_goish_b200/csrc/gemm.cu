@@ -375,7 +375,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      int stage = 0;
+      // The weights never depend on the previous kernel: the first tile's
+      // are pulled into L2 before waiting for it (programmatic launch).
+      if ((int)blockIdx.x < total)
+        for (int kb = 0; kb < min(kblocks, 2 * STAGES); kb++)
+          tma_prefetch_2d(&tmB, kb * BK, (int)(blockIdx.x % a.n_tiles) * BN);
+      pdl_wait();
+      pdl_trigger();
+      int stage = 0, filled = 0;
       uint32_t phase = 0;
       bool ok = true;
       int issued[STAGES];
@@ -392,12 +399,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
           tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
+          // the ring's first fills go out before the next launches' weights
+          if (++filled == STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      if (filled < STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
       // On a timeout, leave no copy in flight: wait (bounded) for every
       // stage this thread filled to land before the CTA exits.
       if (!ok)
@@ -444,6 +454,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     // Epilogue: warp w may read TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    pdl_wait();  // outputs and residual rows may be in use by the previous kernel until it ends
     const int quarter = warp % 4;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -594,7 +605,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      int stage = 0;
+      // The weights never depend on the previous kernel: this CTA's rows of
+      // the first unit's B tile are pulled into L2 before waiting for it.
+      if (cluster < total) {
+        const int tile = cluster % tiles, sp = cluster / tiles;
+        const int kb0 = sp * kbs, kb1 = min(kblocks, kb0 + min(kbs, 2 * PAIR_STAGES));
+        for (int kb = kb0; kb < kb1; kb++)
+          tma_prefetch_2d(&tmB, kb * BK, (tile % a.n_tiles) * 256 + (int)rank * 128);
+      }
+      pdl_wait();
+      pdl_trigger();
+      int stage = 0, filled = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int unit = cluster; unit < total && ok; unit += nclusters) {
@@ -611,12 +632,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (leader) mbar_expect_tx(&full[stage], 2 * (PA_BYTES + PB_BYTES));
           tma_load_2d_pair(sA + stage * PA_BYTES, &tmA, fbar, kb * BK, mt * 256 + rank * 128);
           tma_load_2d_pair(sB + stage * PB_BYTES, &tmB, fbar, kb * BK, nt * 256 + rank * 128);
+          // the ring's first fills go out before the next launches' weights
+          if (++filled == PAIR_STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
           if (++stage == PAIR_STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      if (filled < PAIR_STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
       // Drain: every stage's last fill is consumed (its empty barrier
       // completes) before this CTA may exit, so no MMA still reads this
       // CTA's shared memory and no commit arrives here after exit.
@@ -668,6 +692,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
+    pdl_wait();  // outputs and residual rows may be in use by the previous kernel until it ends
     const int quarter = warp % 4;
     uint8_t* stg = smem + PAIR_STG + quarter * 2 * 4096;
     int acc = 0;
@@ -757,7 +782,7 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 
 template <int EPI, int HD>
 static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
-                              cudaStream_t st) {
+                              cudaStream_t st, bool pdl) {
   static std::atomic<bool> configured[64];  // per device and instantiation; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
@@ -767,13 +792,22 @@ static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, cons
     if (e != cudaSuccess) return e;
     configured[dev & 63] = true;
   }
-  gemm_tc_kernel<EPI, HD><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = GEMM_SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EPI, HD>, ta, tb, a);
 }
 
 template <int EPI, int HD>
 static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const GemmArgs& a,
-                               int num_sms, cudaStream_t st) {
+                               int num_sms, cudaStream_t st, bool pdl) {
   // the residual, QKV and SwiGLU epilogues stage through the per-warp buffers at PAIR_STG
   constexpr int SMEM = (EPI == EPI_RESID || EPI == EPI_QKV || EPI == EPI_SWIGLU) ? PAIR_SMEM_RESID : PAIR_SMEM;
   // Per device: the attribute is set once and the number of CTA pairs that
@@ -784,11 +818,13 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   cudaGetDevice(&dev);
   auto kern = gemm_pair_kernel<EPI, HD>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
@@ -809,6 +845,7 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   if (clusters > num_sms / 2) clusters = num_sms / 2;
   if (clusters > total) clusters = total;
   cfg.gridDim = dim3(2 * clusters);
+  cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, a);
 }
 
@@ -825,7 +862,10 @@ int gemm_ksplit(int M, int N, int K, int num_sms) {
 }
 
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool pdl) {
+  if (a.pf.count < 0 || a.pf.count > PF_MAX) return cudaErrorInvalidValue;
+  for (int i = 0; i < a.pf.count; i++)
+    if (reinterpret_cast<uintptr_t>(a.pf.p[i]) & 15) return cudaErrorInvalidValue;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaSuccess;
   if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;
@@ -860,13 +900,13 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
     a.m_tiles = (a.M + 255) / 256;
     a.n_tiles = (a.N + BN - 1) / BN;
     switch (epi) {
-      case EPI_F32: return launch_pair<EPI_F32, 64>(ta, tb, tr, a, num_sms, st);
-      case EPI_F16: return launch_pair<EPI_F16, 64>(ta, tb, tr, a, num_sms, st);
-      case EPI_RESID: return launch_pair<EPI_RESID, 64>(ta, tb, tr, a, num_sms, st);
-      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU, 64>(ta, tb, tr, a, num_sms, st);
+      case EPI_F32: return launch_pair<EPI_F32, 64>(ta, tb, tr, a, num_sms, st, pdl);
+      case EPI_F16: return launch_pair<EPI_F16, 64>(ta, tb, tr, a, num_sms, st, pdl);
+      case EPI_RESID: return launch_pair<EPI_RESID, 64>(ta, tb, tr, a, num_sms, st, pdl);
+      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU, 64>(ta, tb, tr, a, num_sms, st, pdl);
       case EPI_QKV:
-        if (a.hd == 64) return launch_pair<EPI_QKV, 64>(ta, tb, tr, a, num_sms, st);
-        if (a.hd == 128) return launch_pair<EPI_QKV, 128>(ta, tb, tr, a, num_sms, st);
+        if (a.hd == 64) return launch_pair<EPI_QKV, 64>(ta, tb, tr, a, num_sms, st, pdl);
+        if (a.hd == 128) return launch_pair<EPI_QKV, 128>(ta, tb, tr, a, num_sms, st, pdl);
         return cudaErrorInvalidValue;
     }
     return cudaErrorInvalidValue;
@@ -878,13 +918,13 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
   const int total = a.m_tiles * a.n_tiles;
   const int grid = total < num_sms ? total : num_sms;
   switch (epi) {
-    case EPI_F32: return launch_epi<EPI_F32, 64>(ta, tb, a, grid, st);
-    case EPI_F16: return launch_epi<EPI_F16, 64>(ta, tb, a, grid, st);
-    case EPI_RESID: return launch_epi<EPI_RESID, 64>(ta, tb, a, grid, st);
-    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU, 64>(ta, tb, a, grid, st);
+    case EPI_F32: return launch_epi<EPI_F32, 64>(ta, tb, a, grid, st, pdl);
+    case EPI_F16: return launch_epi<EPI_F16, 64>(ta, tb, a, grid, st, pdl);
+    case EPI_RESID: return launch_epi<EPI_RESID, 64>(ta, tb, a, grid, st, pdl);
+    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU, 64>(ta, tb, a, grid, st, pdl);
     case EPI_QKV:
-      if (a.hd == 64) return launch_epi<EPI_QKV, 64>(ta, tb, a, grid, st);
-      if (a.hd == 128) return launch_epi<EPI_QKV, 128>(ta, tb, a, grid, st);
+      if (a.hd == 64) return launch_epi<EPI_QKV, 64>(ta, tb, a, grid, st, pdl);
+      if (a.hd == 128) return launch_epi<EPI_QKV, 128>(ta, tb, a, grid, st, pdl);
       return cudaErrorInvalidValue;
   }
   return cudaErrorInvalidValue;

@@ -4,6 +4,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "prefetch.h"
+
 namespace laya {
 
 // Epilogues fused into the GEMM.
@@ -37,6 +39,9 @@ struct GemmArgs {
   // adds resid + part[0] + ... + part[ksplit-1] in that order.
   int ksplit;
   float* part;
+  // Ranges to bring into L2 once the producer's ring is first full (the next
+  // launches' weights; prefetch.h), or count 0.
+  PfList pf;
 };
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point: `rank`
@@ -48,8 +53,11 @@ bool encode_tiled(CUtensorMap* m, int dtype, int rank, const void* base, const u
 
 // A: [M][lda] F16 row-major activations, B: [N][ldb] F16 row-major weights
 // (K contiguous).  lda, ldb multiples of 8; A, B 16-byte aligned.
+// pdl: launch with programmatic dependent launch; the kernel then prefetches
+// its first weight tiles into L2 while the previous kernel drains and waits
+// for it (griddepcontrol.wait) before touching anything that kernel wrote.
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
-                        cudaStream_t st);
+                        cudaStream_t st, bool pdl = false);
 // K splits for an EPI_RESID GEMM of this shape: more than 1 when its 256 x 256
 // output tiles would leave most CTA pairs idle (M > 128 only).
 int gemm_ksplit(int M, int N, int K, int num_sms);

@@ -32,6 +32,7 @@
 // therefore applied in registers in the epilogue.
 #include <atomic>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 
@@ -50,7 +51,7 @@ constexpr int GV_HALF_W = 8 * 8 * 128;
 constexpr int GV_HALF_S = 8 * 64;
 constexpr int GV_STAGE = 18 * 1024;  // shared-memory stride of a stage (1024-byte aligned)
 __host__ __device__ constexpr int gv_stage_bytes(bool q8) { return 2 * GV_HALF_W + (q8 ? 2 * GV_HALF_S : 0); }
-constexpr int GV_MAX_STAGES = 8;     // ring depth: as many stages as shared memory holds
+constexpr int GV_MAX_STAGES = 12;    // ring depth: as many stages as shared memory holds
 constexpr int GV_WARPS = 16;                   // compute warps; warp GV_WARPS is the producer
 constexpr int GV_THREADS = (GV_WARPS + 2) * 32;  // + producer warp + epilogue warp
 
@@ -294,6 +295,17 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
     int stage = 0, issued = 0;
     uint32_t phase = 0;
     const uint32_t sbytes = (uint32_t)gv_stage_bytes(Q8);
+    // Source of this CTA's j-th stage over all phases (a phase's stages of
+    // one CTA are one contiguous range of its packed image), or null.
+    auto stage_src = [&](int j) -> const uint8_t* {
+      for (int p = 0; p < q.n; p++) {
+        const GvPhase w = gv_phase(q, p, Q8);
+        const int cnt = (w.t1 - w.t0) * w.kstages;
+        if (j < cnt) return q.ph[p].packed + ((size_t)w.t0 * w.kstages + j) * sbytes;
+        j -= cnt;
+      }
+      return nullptr;
+    };
     for (int p = 0; p < q.n; p++) {
       const GvPhase w = gv_phase(q, p, Q8);
       const uint8_t* src = q.ph[p].packed;
@@ -305,6 +317,13 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
           if (lane == 0) {
             mbar_expect_tx(&full[stage], sbytes);
             bulk_g2s(ring + stage * GV_STAGE, src + ((size_t)t * w.kstages + ks) * sbytes, sbytes, &full[stage]);
+            if (q.pfd > 0) {
+              // keep the stages up to pfd ahead requested from HBM (into L2)
+              if (issued == 0)
+                for (int j = nst; j < q.pfd; j++)
+                  if (const uint8_t* s2 = stage_src(j)) l2_prefetch_bulk(s2, sbytes);
+              if (const uint8_t* s2 = stage_src(issued + max(q.pfd, nst))) l2_prefetch_bulk(s2, sbytes);
+            }
             // the ring's first fills go out before the prefetches
             if (++issued == nst) pf_issue(q.pf, blockIdx.x, gridDim.x);
           }
@@ -588,11 +607,18 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 #pragma unroll
         for (int i = 0; i < CPW; i++)
           if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, warp + i * GV_WARPS, kel0, xs, xpitch, a.nb, g, tq);
+        if (q.early) {
+          // the stage's bytes are in registers: hand the slot back to the producer
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
+        }
 #pragma unroll
         for (int i = 0; i < CPW; i++)
           if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (!q.early) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
+        }
         if (++stage == nst) {
           stage = 0;
           phase ^= 1;
@@ -616,10 +642,16 @@ constexpr size_t GV_SMEM_BUDGET = 225 * 1024;  // dynamic shared memory per CTA 
 
 // Ring stages that fit beside the staged activations: 2 .. GV_MAX_STAGES,
 // or 0 when even two do not fit.
+static int env_int(const char* name, int def) {
+  const char* e = std::getenv(name);
+  return e && e[0] ? std::atoi(e) : def;
+}
+
 static int stages_for(int nb, int K, int nt) {
   const size_t off = gv_ring_offset(nb, K, nt) + 1024;  // + alignment slack
   if (off + 2 * GV_STAGE > GV_SMEM_BUDGET) return 0;
-  return (int)std::min<size_t>(GV_MAX_STAGES, (GV_SMEM_BUDGET - off) / GV_STAGE);
+  static const int cap = std::max(2, std::min(GV_MAX_STAGES, env_int("LAYA_GV_STAGES", GV_MAX_STAGES)));
+  return (int)std::min<size_t>(cap, (GV_SMEM_BUDGET - off) / GV_STAGE);
 }
 static int gemv3_stages(const Gemv3Args& a, int nt) { return stages_for(a.nb, a.K, nt); }
 
@@ -719,6 +751,9 @@ cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num
       if (reinterpret_cast<uintptr_t>(pf->p[i]) & 15) return cudaErrorInvalidValue;
     q.pf = *pf;
   }
+  static const int pfd = env_int("LAYA_GV_PFD", 0), early = env_int("LAYA_GV_EARLY", 1);
+  q.pfd = pfd;
+  q.early = early;
   for (int i = 0; i < n; i++) {
     const Gemv3Args& a = ph[i];
     if (!gemv3_supported(a) || !a.packed || (reinterpret_cast<uintptr_t>(a.packed) & 15)) return cudaErrorInvalidValue;

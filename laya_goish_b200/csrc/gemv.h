@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "prefetch.h"
 
 namespace laya {
 
@@ -55,33 +56,6 @@ struct Gemv3Args {
   long long budget;
 };
 
-// Byte ranges a launch asks HBM for ahead of their use (by its own later
-// phases or by the next launches of the decode step), so the weight and KV
-// stream keeps going across grid barriers and kernel boundaries.  Each CTA
-// prefetches its slice of every range, ranges in order; the data lands in
-// L2 (cp.async.bulk.prefetch.L2) and the later bulk copies hit there.
-// Starts are 16-byte aligned; a range's length is used rounded down to 16.
-constexpr int PF_MAX = 8;
-struct PfList {
-  const uint8_t* p[PF_MAX];
-  unsigned long long n[PF_MAX];
-  int count;
-};
-
-// Slice `part` of `parts` of every range, in chunks of at most 32 KB.
-__device__ __forceinline__ void pf_issue(const PfList& pf, int part, int parts) {
-  for (int i = 0; i < pf.count; i++) {
-    const unsigned long long n = pf.n[i] & ~15ull;
-    unsigned long long a = (n * part / parts) & ~15ull;
-    const unsigned long long b = part + 1 == parts ? n : (n * (part + 1) / parts) & ~15ull;
-    while (a < b) {
-      const unsigned c = (unsigned)(b - a < 32768ull ? b - a : 32768ull);
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.p[i] + a), "r"(c) : "memory");
-      a += c;
-    }
-  }
-}
-
 // Up to four GEMV phases run by one (cooperative) launch, in order, with a
 // grid-wide barrier between consecutive phases: a phase may read what the
 // previous phase wrote.  All phases share the batch rows and the block type.
@@ -92,6 +66,8 @@ struct GemvSeq {
   int kmax;        // largest K of the phases (activation staging)
   unsigned* gbar;  // grid barrier counter, zero at launch (n > 1)
   PfList pf;       // prefetched once the producer's ring is first full
+  int pfd;         // > 0: each stage copy also brings the stage this many ahead into L2
+  int early;       // compute warps release a stage once its fragments are in registers
 };
 
 // True when gemv3_launch handles these operands (Q8_0 or F16, K a multiple

@@ -10,6 +10,8 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 
+#include "prefetch.h"
+
 namespace laya {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -92,6 +94,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// Brings the box of a tiled tensor map at (x, y) into L2 without a
+// destination in shared memory (no barrier, nothing to wait for).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y) : "memory");
+}
+
 // 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
 // aligned) from global into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -105,6 +113,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // without waiting for it.
 __device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Slice `part` of `parts` of every range of a prefetch list (prefetch.h),
+// in chunks of at most 32 KB.
+__device__ __forceinline__ void pf_issue(const PfList& pf, int part, int parts) {
+  for (int i = 0; i < pf.count; i++) {
+    const unsigned long long n = pf.n[i] & ~15ull;
+    unsigned long long a = (n * part / parts) & ~15ull;
+    const unsigned long long b = part + 1 == parts ? n : (n * (part + 1) / parts) & ~15ull;
+    while (a < b) {
+      const unsigned c = (unsigned)(b - a < 32768ull ? b - a : 32768ull);
+      l2_prefetch_bulk(pf.p[i] + a, c);
+      a += c;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- clusters
