@@ -764,7 +764,7 @@ __global__ void __launch_bounds__(160, 1)
     attn_dec3_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                      const half* __restrict__ q, const int* __restrict__ tables, const DecSeq* __restrict__ seqs,
                      int KV, float scale_log2, int split_pages, int splits, float* __restrict__ part,
-                     unsigned* err, long long budget, const PfList pf) {
+                     unsigned* err, long long budget) {
   using C = Dec3<HD>;
   extern __shared__ uint8_t d3_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(d3_raw) + 1023) & ~uintptr_t(1023));
@@ -802,13 +802,7 @@ __global__ void __launch_bounds__(160, 1)
           tma_load_2d(dst + hb * 8192, &tk, &full[st], hb * 64, row);
           tma_load_2d(dst + C::PAGE_BYTES + hb * 8192, &tv, &full[st], hb * 64, row);
         }
-        // the first pages go out before the prefetches of the next launches' data
-        if (i + 1 == min(np, C::S))
-          pf_issue(pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
-                   gridDim.x * gridDim.y * gridDim.z);
       }
-      if (np == 0)
-        pf_issue(pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x, gridDim.x * gridDim.y * gridDim.z);
     }
   } else {
     // Q of head g of the group as the A fragment (rows g + 8 are zero)
@@ -1013,7 +1007,7 @@ static bool dec3_enabled() {
 template <int HD, int G>
 static cudaError_t launch_dec3(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
                                const half* q, const int* tables, const DecSeq* seqs, int KV, float sl2,
-                               int split_pages, int splits, float* part, unsigned* err, const PfList& pf) {
+                               int split_pages, int splits, float* part, unsigned* err) {
   static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1024,7 +1018,7 @@ static cudaError_t launch_dec3(dim3 grid, cudaStream_t st, const CUtensorMap& tk
     configured[dev & 63] = true;
   }
   return launch_k(attn_dec3_kernel<HD, G>, grid, dim3(160), (size_t)Dec3<HD>::SMEM, st, true, tk, tv, q, tables,
-                  seqs, KV, sl2, split_pages, splits, part, err, 4000000000ll, pf);
+                  seqs, KV, sl2, split_pages, splits, part, err, 4000000000ll);
 }
 
 template <int HD, int G>
@@ -1045,8 +1039,7 @@ static cudaError_t launch_dec2(dim3 grid, cudaStream_t st, const half* q, const 
 }
 
 static int decode_attention(Model& m, Replica& r, int nb, const half* q, const half* kc, const half* vc,
-                            const DecSeq* seqs, const AttnShape& sh, half* out, const PfList* pf = nullptr) {
-  const PfList nopf{};
+                            const DecSeq* seqs, const AttnShape& sh, half* out) {
   const Config& c = m.cfg;
   const float sl2 = (1.f / sqrtf((float)c.hd)) * 1.4426950408889634f;
   const int G = c.H / c.KV;
@@ -1070,7 +1063,7 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
 #define LAYA_DEC3(HDV, GV)                                                                                 \
   if (c.hd == HDV && G == GV)                                                                              \
     e = launch_dec3<HDV, GV>(g3, r.stream, tk, tv, q, tb, seqs, c.KV, sl2, sh.split_pages3, sh.splits3, part, \
-                             r.err, pf ? *pf : nopf);
+                             r.err);
     LAYA_DEC3(64, 1)
     LAYA_DEC3(64, 2)
     LAYA_DEC3(64, 4)
@@ -1124,11 +1117,11 @@ static Gemv3Args gv3_base(Replica& r, int mode, int nb, int K) {
   return a;
 }
 
-static int run_gemv3(Replica& r, const Gemv3Args& a, const PfList* pf = nullptr) {
+static int run_gemv3(Replica& r, const Gemv3Args& a) {
   cudaEvent_t ev;
   prof_begin(r, P_GEMV, &ev);
   r.launches++;
-  LAYA_CK(gemv3_launch(a, r.num_sms, r.stream, pf));
+  LAYA_CK(gemv3_launch(a, r.num_sms, r.stream));
   prof_end(r, P_GEMV, ev);
   return 0;
 }
@@ -1238,18 +1231,7 @@ struct StepIO {
   DecSeq* cur_seq;
   unsigned* gbar;  // [layers] grid barrier counters of the multi-phase GEMV launches
   int n_gbar;
-  int kv_used;     // KV pages in use per layer (pages 0 .. kv_used - 1)
 };
-
-// L2 prefetch plan of a chained decode step (pf_plan): the step reads HBM in
-// launch order: the first layer's qkv GEMV, then per layer the attention (its
-// K and V pages) and the chained GEMV launch (attention output, gate/up,
-// down, the next layer's qkv or the head).
-static size_t pf_window() {
-  const char* e = std::getenv("LAYA_PF_MB");
-  const long v = e ? std::atol(e) : 0;
-  return v > 0 ? (size_t)v << 20 : 0;
-}
 
 // One decode step for nb sequences; every pointer it uses is fixed, so the
 // launch sequence can be captured once and replayed.
@@ -1363,27 +1345,6 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     seq = layer_args(l, &ga[4 * l]);
     for (int i = 0; seq && i < 4; i++) seq = ga[4 * l + i].seg[0].kind == gh.seg[0].kind;
   }
-  // prefetch lists: [0] the first qkv GEMV, then per layer [1 + 2l] the
-  // attention and [2 + 2l] the chained GEMV launch
-  std::vector<PfList> pf;
-  if (seq) {
-    std::vector<PfKernel> ks(1 + 2 * c.L);
-    const size_t kvb = (size_t)io.kv_used * c.KV * PAGE * c.hd * 2;
-    auto packed = [&](const Gemv3Args& a) { return PfRange{a.packed, gemv3_packed_bytes(a)}; };
-    ks[0].own = {packed(ga[0])};
-    ks[0].direct = ks[0].own[0].n;
-    for (int l = 0; l < c.L; l++) {
-      PfKernel& at = ks[1 + 2 * l];
-      at.own = {{reinterpret_cast<const uint8_t*>(r.kc.as<half>() + l * layer_elems), kvb},
-                {reinterpret_cast<const uint8_t*>(r.vc.as<half>() + l * layer_elems), kvb}};
-      at.direct = 2 * kvb;
-      PfKernel& ch = ks[2 + 2 * l];
-      ch.own = {packed(ga[4 * l + 1]), packed(ga[4 * l + 2]), packed(ga[4 * l + 3]),
-                packed(l + 1 < c.L ? ga[4 * (l + 1)] : gh)};
-      ch.direct = ch.own[0].n;
-    }
-    pf = pf_plan(ks, pf_window());
-  }
   for (int l = 0; l < c.L; l++) {
     const Layer& L = r.layers[l];
     half* kcl = r.kc.as<half>() + l * layer_elems;
@@ -1396,7 +1357,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
     }
     if (seq) {
-      if (l == 0 && (rc = run_gemv3(r, gq, &pf[0]))) return rc;  // later layers' qkv ran in the previous chain
+      if (l == 0 && (rc = run_gemv3(r, gq))) return rc;  // later layers' qkv ran in the previous chain
     } else if (small && v3) {
       if ((rc = run_gemv3(r, gq))) return rc;
     } else if (small) {
@@ -1447,15 +1408,13 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       a.page_size = PAGE;
       if ((rc = gemm_d(P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
     }
-    if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, io.cur_seq, sh, r.att.as<half>(),
-                               seq ? &pf[1 + 2 * l] : nullptr)))
-      return rc;
+    if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, io.cur_seq, sh, r.att.as<half>()))) return rc;
     if (seq) {
       const Gemv3Args ph[4] = {go, gg, gd, l + 1 < c.L ? ga[4 * (l + 1)] : gh};
       cudaEvent_t ev;
       prof_begin(r, P_GEMV, &ev);
       r.launches++;
-      LAYA_CK(gemv3_launch_seq(ph, 4, io.gbar + l, r.num_sms, st, &pf[2 + 2 * l]));
+      LAYA_CK(gemv3_launch_seq(ph, 4, io.gbar + l, r.num_sms, st));
       prof_end(r, P_GEMV, ev);
       continue;
     }
@@ -1649,7 +1608,6 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   io.cur_seq = reinterpret_cast<DecSeq*>(io.cur_slot + n_seqs);
   io.gbar = reinterpret_cast<unsigned*>(reinterpret_cast<uintptr_t>(io.cur_seq + n_seqs + 63) & ~uintptr_t(255));
   io.n_gbar = c.L;
-  io.kv_used = pages;
   LAYA_CK(cudaMemsetAsync(io.best, 0, best_bytes, r.stream));
   Gemv3Args gh0 = gv3_base(r, GV_ARGMAX, R, c.d);
   gh0.seg[0] = r.head;

@@ -705,70 +705,24 @@ int ensure_kv(Model& m, Replica& r, int pages) {
 
 // ---------------------------------------------------------------- forward
 
-std::vector<PfList> pf_plan(const std::vector<PfKernel>& ks, size_t window) {
-  std::vector<PfList> out(ks.size(), PfList{});
-  std::vector<PfRange> flat;
-  std::vector<size_t> flat_at, start(ks.size()), end(ks.size());
-  size_t total = 0;
-  for (size_t k = 0; k < ks.size(); k++) {
-    start[k] = total;
-    for (const PfRange& r : ks[k].own) {
-      if (!r.n) continue;
-      flat.push_back(r);
-      flat_at.push_back(total);
-      total += r.n;
-    }
-    end[k] = total;
-  }
-  if (!window || !total) return out;
-  size_t cursor = 0;
-  for (size_t k = 0; k < ks.size(); k++) {
-    size_t a = std::max(cursor, start[k] + ks[k].direct);
-    a = (a + 15) & ~size_t(15);
-    const size_t b = std::min(end[k] + window, start[k] + total);
-    PfList& L = out[k];
-    while (a < b && L.count < PF_MAX) {
-      const size_t pos = a % total;
-      size_t i = std::upper_bound(flat_at.begin(), flat_at.end(), pos) - flat_at.begin() - 1;
-      const size_t in = pos - flat_at[i];
-      const size_t len = std::min(flat[i].n - in, b - a);
-      L.p[L.count] = flat[i].p + in;
-      L.n[L.count] = len;
-      L.count++;
-      a += len;
-    }
-    cursor = std::max(cursor, a);
-  }
-  return out;
+// Prefill GEMMs launch with programmatic dependent launch (their first
+// weight tiles come into L2 while the previous kernel drains) unless
+// LAYA_GEMM_PDL=0.
+static bool gemm_pdl() {
+  static const bool on = [] {
+    const char* e = std::getenv("LAYA_GEMM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
-
-static int gemm(Replica& r, int cat, int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a,
-                bool pdl = false) {
+static int gemm(Replica& r, int cat, int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a) {
   a.err = r.err;
   a.budget = kWaitBudget;
   ProfScope ps(r, cat);
   r.launches++;
-  LAYA_CK(gemm_launch(epi, A, lda, B, ldb, a, r.num_sms, r.stream, pdl));
+  LAYA_CK(gemm_launch(epi, A, lda, B, ldb, a, r.num_sms, r.stream, gemm_pdl()));
   return 0;
-}
-
-static bool env_on(const char* name) {
-  const char* e = std::getenv(name);
-  return !(e && e[0] == '0');
-}
-
-// Prefill passes of at most this many token rows stream every weight about
-// once (few output tiles per weight tile), so their GEMMs prefetch the next
-// GEMMs' weights into L2; larger passes reuse each weight tile across many
-// row tiles and are bound by the tensor cores.
-static constexpr int kPfMaxRows = 1024;
-
-static size_t prefill_pf_window(int M) {
-  if (M > kPfMaxRows) return 0;
-  const char* e = std::getenv("LAYA_PF_PREFILL_MB");
-  const long v = e ? std::atol(e) : 32;
-  return v > 0 ? (size_t)v << 20 : 0;
 }
 
 static int stage(Replica& r, int cat, const QTensor& t, half* out, int ldo, int grp, int gstride, int goff) {
@@ -849,28 +803,6 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
   const int ks_o = ks_on ? gemm_ksplit(M, d, qd, r.num_sms) : 1;
   const int ks_d = ks_on ? gemm_ksplit(M, d, ffn, r.num_sms) : 1;
   if (std::max(ks_o, ks_d) > 1 && (rc = r.kpart.ensure((size_t)std::max(ks_o, ks_d) * M * d * 4))) return rc;
-  // L2 prefetch lists of the GEMMs (four per layer, in launch order) when
-  // the pass is small enough to be bound by the weight stream.
-  std::vector<PfList> pfl;
-  if (const size_t pfw = prefill_pf_window(M)) {
-    std::vector<PfKernel> ks(4 * c.L);
-    bool all = true;
-    for (int l = 0; l < c.L && all; l++) {
-      const Layer& L = r.layers[l];
-      const half* w4[4] = {L.wqkv16 ? L.wqkv16 : L.rqkv16, L.wo16 ? L.wo16 : L.ro16,
-                           L.wgu16 ? L.wgu16 : L.rgu16, L.wd16 ? L.wd16 : L.rd16};
-      const size_t n4[4] = {(size_t)(qd + 2 * kd) * d * 2, (size_t)d * qd * 2, (size_t)2 * ffn * d * 2,
-                            (size_t)d * ffn * 2};
-      for (int i = 0; i < 4; i++) {
-        all &= w4[i] != nullptr;
-        ks[4 * l + i].own = {{reinterpret_cast<const uint8_t*>(w4[i]), n4[i]}};
-        ks[4 * l + i].direct = 0;
-      }
-    }
-    if (all) pfl = pf_plan(ks, pfw);
-  }
-  auto pf_of = [&](int l, int i) { return pfl.empty() ? PfList{} : pfl[4 * l + i]; };
-  const bool pdl = env_on("LAYA_GEMM_PDL");
   int pend = 0;  // K splits of x not yet merged (the gathered final norm merges without writing x back)
   auto norm = [&](const int* rows, int n, const float* w, half* o16, float* o32) -> cudaError_t {
     r.launches++;
@@ -917,8 +849,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     a.kcache = r.kc.as<half>() + l * layer_elems;
     a.vcache = r.vc.as<half>() + l * layer_elems;
     a.page_size = PAGE;
-    a.pf = pf_of(l, 0);
-    if ((rc = gemm(r, P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a, pdl))) return rc;
+    if ((rc = gemm(r, P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
     {
       AttnParams ap{};
       ap.q = r.qb.as<half>();
@@ -954,8 +885,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     b.ldo = d;
     b.ksplit = ks_o;
     b.part = r.kpart.as<float>();
-    b.pf = pf_of(l, 1);
-    if ((rc = gemm(r, P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b, pdl))) return rc;
+    if ((rc = gemm(r, P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
     pend = ks_o;
     LAYA_CK(norm(nullptr, M, L.ffn_norm, h, nullptr));
     const half* wgu = L.wgu16 ? L.wgu16 : L.rgu16;
@@ -971,8 +901,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     gu.K = d;
     gu.out = r.act.p;
     gu.ldo = ffn;
-    gu.pf = pf_of(l, 2);
-    if ((rc = gemm(r, P_GEMM_GU, EPI_SWIGLU, h, d, wgu, d, gu, pdl))) return rc;
+    if ((rc = gemm(r, P_GEMM_GU, EPI_SWIGLU, h, d, wgu, d, gu))) return rc;
     const half* wd = L.wd16 ? L.wd16 : L.rd16;
     if (!wd) {
       if ((rc = stage(r, P_DEQUANT, L.wd, r.wd_s.as<half>(), ffn, big, 0, 0))) return rc;
@@ -986,8 +915,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     dn.ldo = d;
     dn.ksplit = ks_d;
     dn.part = r.kpart.as<float>();
-    dn.pf = pf_of(l, 3);
-    if ((rc = gemm(r, P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, wd, ffn, dn, pdl))) return rc;
+    if ((rc = gemm(r, P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, wd, ffn, dn))) return rc;
     pend = ks_d;
     if (canceled) {
       cudaEvent_t e;

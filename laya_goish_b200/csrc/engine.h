@@ -15,7 +15,6 @@
 #include "gguf.h"
 #include "kernels.h"
 #include "laya_cuda.h"
-#include "prefetch.h"
 
 namespace laya {
 
@@ -150,23 +149,6 @@ int load_replica(Model& m, const Gguf& g, int device, Replica& r);
 int mirror_replicas(Model& m, const std::vector<int>& devices);
 void free_replica(Replica& r);
 int ensure_kv(Model& m, Replica& r, int pages);
-// L2 prefetch plan of a sequence of launches (prefetch.h).  The launches
-// read HBM in order; each asks for the stream's bytes from where the
-// previous launch's request ended (never before its own data past what it
-// loads at once) up to `window` bytes past the end of its own data,
-// wrapping into the next repetition of the sequence, so HBM keeps
-// streaming while grid barriers and launch boundaries pass.  window 0
-// turns prefetching off (every list empty).
-struct PfRange {
-  const uint8_t* p;
-  size_t n;
-};
-struct PfKernel {
-  std::vector<PfRange> own;  // this launch's reads, in order
-  size_t direct;             // leading bytes of `own` the launch loads at once (not prefetched)
-};
-std::vector<PfList> pf_plan(const std::vector<PfKernel>& ks, size_t window);
-
 int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>& tables, int read_base,
                 int (*canceled)(void*), void* user, std::mutex* cancel_mu);
 int ensure_head16(Model& m, Replica& r);

@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tma_prefetch_2d(&tmB, kb * BK, (int)(blockIdx.x % a.n_tiles) * BN);
       pdl_wait();
       pdl_trigger();
-      int stage = 0, filled = 0;
+      int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       int issued[STAGES];
@@ -399,15 +399,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mt * BM);
           tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nt * BN);
-          // the ring's first fills go out before the next launches' weights
-          if (++filled == STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (filled < STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
       // On a timeout, leave no copy in flight: wait (bounded) for every
       // stage this thread filled to land before the CTA exits.
       if (!ok)
@@ -615,7 +612,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       pdl_wait();
       pdl_trigger();
-      int stage = 0, filled = 0;
+      int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int unit = cluster; unit < total && ok; unit += nclusters) {
@@ -632,15 +629,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (leader) mbar_expect_tx(&full[stage], 2 * (PA_BYTES + PB_BYTES));
           tma_load_2d_pair(sA + stage * PA_BYTES, &tmA, fbar, kb * BK, mt * 256 + rank * 128);
           tma_load_2d_pair(sB + stage * PB_BYTES, &tmB, fbar, kb * BK, nt * 256 + rank * 128);
-          // the ring's first fills go out before the next launches' weights
-          if (++filled == PAIR_STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
           if (++stage == PAIR_STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (filled < PAIR_STAGES) pf_issue(a.pf, blockIdx.x, gridDim.x);
       // Drain: every stage's last fill is consumed (its empty barrier
       // completes) before this CTA may exit, so no MMA still reads this
       // CTA's shared memory and no commit arrives here after exit.
@@ -863,9 +857,6 @@ int gemm_ksplit(int M, int N, int K, int num_sms) {
 
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
                         cudaStream_t st, bool pdl) {
-  if (a.pf.count < 0 || a.pf.count > PF_MAX) return cudaErrorInvalidValue;
-  for (int i = 0; i < a.pf.count; i++)
-    if (reinterpret_cast<uintptr_t>(a.pf.p[i]) & 15) return cudaErrorInvalidValue;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return cudaSuccess;
   if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;

@@ -4,8 +4,6 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
-#include "prefetch.h"
-
 namespace laya {
 
 // Epilogues fused into the GEMM.
@@ -39,9 +37,6 @@ struct GemmArgs {
   // adds resid + part[0] + ... + part[ksplit-1] in that order.
   int ksplit;
   float* part;
-  // Ranges to bring into L2 once the producer's ring is first full (the next
-  // launches' weights; prefetch.h), or count 0.
-  PfList pf;
 };
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point: `rank`

@@ -32,7 +32,6 @@
 // therefore applied in registers in the epilogue.
 #include <atomic>
 #include <algorithm>
-#include <cstdlib>
 #include <cstring>
 
 
@@ -51,7 +50,7 @@ constexpr int GV_HALF_W = 8 * 8 * 128;
 constexpr int GV_HALF_S = 8 * 64;
 constexpr int GV_STAGE = 18 * 1024;  // shared-memory stride of a stage (1024-byte aligned)
 __host__ __device__ constexpr int gv_stage_bytes(bool q8) { return 2 * GV_HALF_W + (q8 ? 2 * GV_HALF_S : 0); }
-constexpr int GV_MAX_STAGES = 12;    // ring depth: as many stages as shared memory holds
+constexpr int GV_MAX_STAGES = 8;     // ring depth: as many stages as shared memory holds
 constexpr int GV_WARPS = 16;                   // compute warps; warp GV_WARPS is the producer
 constexpr int GV_THREADS = (GV_WARPS + 2) * 32;  // + producer warp + epilogue warp
 
@@ -292,20 +291,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 
   if (warp == GV_WARPS) {
     // ---------------- producer: one thread, one bulk copy per stage, all phases
-    int stage = 0, issued = 0;
+    int stage = 0;
     uint32_t phase = 0;
     const uint32_t sbytes = (uint32_t)gv_stage_bytes(Q8);
-    // Source of this CTA's j-th stage over all phases (a phase's stages of
-    // one CTA are one contiguous range of its packed image), or null.
-    auto stage_src = [&](int j) -> const uint8_t* {
-      for (int p = 0; p < q.n; p++) {
-        const GvPhase w = gv_phase(q, p, Q8);
-        const int cnt = (w.t1 - w.t0) * w.kstages;
-        if (j < cnt) return q.ph[p].packed + ((size_t)w.t0 * w.kstages + j) * sbytes;
-        j -= cnt;
-      }
-      return nullptr;
-    };
     for (int p = 0; p < q.n; p++) {
       const GvPhase w = gv_phase(q, p, Q8);
       const uint8_t* src = q.ph[p].packed;
@@ -317,15 +305,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
           if (lane == 0) {
             mbar_expect_tx(&full[stage], sbytes);
             bulk_g2s(ring + stage * GV_STAGE, src + ((size_t)t * w.kstages + ks) * sbytes, sbytes, &full[stage]);
-            if (q.pfd > 0) {
-              // keep the stages up to pfd ahead requested from HBM (into L2)
-              if (issued == 0)
-                for (int j = nst; j < q.pfd; j++)
-                  if (const uint8_t* s2 = stage_src(j)) l2_prefetch_bulk(s2, sbytes);
-              if (const uint8_t* s2 = stage_src(issued + max(q.pfd, nst))) l2_prefetch_bulk(s2, sbytes);
-            }
-            // the ring's first fills go out before the prefetches
-            if (++issued == nst) pf_issue(q.pf, blockIdx.x, gridDim.x);
           }
           __syncwarp();
           if (++stage == nst) {
@@ -335,7 +314,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
         }
       }
     }
-    if (lane == 0 && issued < nst) pf_issue(q.pf, blockIdx.x, gridDim.x);
     // Every fill is consumed before the CTA exits (no copy left in flight).
     for (int i = 0; i < nst; i++) {
       if (!mbar_wait(&empty[stage], phase ^ 1, budget) && lane == 0) atomicOr(err, 64u);
@@ -607,18 +585,11 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 #pragma unroll
         for (int i = 0; i < CPW; i++)
           if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, warp + i * GV_WARPS, kel0, xs, xpitch, a.nb, g, tq);
-        if (q.early) {
-          // the stage's bytes are in registers: hand the slot back to the producer
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[stage]);
-        }
 #pragma unroll
         for (int i = 0; i < CPW; i++)
           if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
-        if (!q.early) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[stage]);
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
         if (++stage == nst) {
           stage = 0;
           phase ^= 1;
@@ -642,16 +613,10 @@ constexpr size_t GV_SMEM_BUDGET = 225 * 1024;  // dynamic shared memory per CTA 
 
 // Ring stages that fit beside the staged activations: 2 .. GV_MAX_STAGES,
 // or 0 when even two do not fit.
-static int env_int(const char* name, int def) {
-  const char* e = std::getenv(name);
-  return e && e[0] ? std::atoi(e) : def;
-}
-
 static int stages_for(int nb, int K, int nt) {
   const size_t off = gv_ring_offset(nb, K, nt) + 1024;  // + alignment slack
   if (off + 2 * GV_STAGE > GV_SMEM_BUDGET) return 0;
-  static const int cap = std::max(2, std::min(GV_MAX_STAGES, env_int("LAYA_GV_STAGES", GV_MAX_STAGES)));
-  return (int)std::min<size_t>(cap, (GV_SMEM_BUDGET - off) / GV_STAGE);
+  return (int)std::min<size_t>(GV_MAX_STAGES, (GV_SMEM_BUDGET - off) / GV_STAGE);
 }
 static int gemv3_stages(const Gemv3Args& a, int nt) { return stages_for(a.nb, a.K, nt); }
 
@@ -739,21 +704,11 @@ static cudaError_t gemv3_go(const GemvSeq& q, int num_sms, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, q, nst);
 }
 
-cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st,
-                             const PfList* pf) {
+cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st) {
   if (n < 1 || n > 4 || (n > 1 && !gbar)) return cudaErrorInvalidValue;
   GemvSeq q{};
   q.n = n;
   q.gbar = gbar;
-  if (pf) {
-    if (pf->count < 0 || pf->count > PF_MAX) return cudaErrorInvalidValue;
-    for (int i = 0; i < pf->count; i++)
-      if (reinterpret_cast<uintptr_t>(pf->p[i]) & 15) return cudaErrorInvalidValue;
-    q.pf = *pf;
-  }
-  static const int pfd = env_int("LAYA_GV_PFD", 0), early = env_int("LAYA_GV_EARLY", 1);
-  q.pfd = pfd;
-  q.early = early;
   for (int i = 0; i < n; i++) {
     const Gemv3Args& a = ph[i];
     if (!gemv3_supported(a) || !a.packed || (reinterpret_cast<uintptr_t>(a.packed) & 15)) return cudaErrorInvalidValue;
@@ -769,9 +724,9 @@ cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num
   return q8 ? gemv3_go<2, true>(q, num_sms, st) : gemv3_go<2, false>(q, num_sms, st);
 }
 
-cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st, const PfList* pf) {
+cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st) {
   if (gemv3_tiles(a) <= 0) return cudaSuccess;
-  return gemv3_launch_seq(&a, 1, nullptr, num_sms, st, pf);
+  return gemv3_launch_seq(&a, 1, nullptr, num_sms, st);
 }
 
 }  // namespace laya

@@ -4,7 +4,6 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
-#include "prefetch.h"
 
 namespace laya {
 
@@ -65,9 +64,6 @@ struct GemvSeq {
   int n;
   int kmax;        // largest K of the phases (activation staging)
   unsigned* gbar;  // grid barrier counter, zero at launch (n > 1)
-  PfList pf;       // prefetched once the producer's ring is first full
-  int pfd;         // > 0: each stage copy also brings the stage this many ahead into L2
-  int early;       // compute warps release a stage once its fragments are in registers
 };
 
 // True when gemv3_launch handles these operands (Q8_0 or F16, K a multiple
@@ -78,10 +74,8 @@ bool gemv3_supported(const Gemv3Args& a);
 // K (not on the batch rows), so it is built once per model.
 size_t gemv3_packed_bytes(const Gemv3Args& a);
 cudaError_t gemv3_pack(const Gemv3Args& a, uint8_t* dst, cudaStream_t st);
-cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st, const PfList* pf = nullptr);
+cudaError_t gemv3_launch(const Gemv3Args& a, int num_sms, cudaStream_t st);
 // Runs ph[0..n-1] as one launch; gbar must be zero when the launch starts.
-// pf (may be null): ranges to prefetch into L2 (PfList).
-cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st,
-                             const PfList* pf = nullptr);
+cudaError_t gemv3_launch_seq(const Gemv3Args* ph, int n, unsigned* gbar, int num_sms, cudaStream_t st);
 
 }  // namespace laya

@@ -10,8 +10,6 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 
-#include "prefetch.h"
-
 namespace laya {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -113,21 +111,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // without waiting for it.
 __device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// Slice `part` of `parts` of every range of a prefetch list (prefetch.h),
-// in chunks of at most 32 KB.
-__device__ __forceinline__ void pf_issue(const PfList& pf, int part, int parts) {
-  for (int i = 0; i < pf.count; i++) {
-    const unsigned long long n = pf.n[i] & ~15ull;
-    unsigned long long a = (n * part / parts) & ~15ull;
-    const unsigned long long b = part + 1 == parts ? n : (n * (part + 1) / parts) & ~15ull;
-    while (a < b) {
-      const unsigned c = (unsigned)(b - a < 32768ull ? b - a : 32768ull);
-      l2_prefetch_bulk(pf.p[i] + a, c);
-      a += c;
-    }
-  }
 }
 
 // ---------------------------------------------------------------- clusters
