@@ -74,11 +74,10 @@ __device__ __forceinline__ void mma16816_z(float (&c)[4], uint32_t a0, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
 
-// Four int8 (two's complement) -> two half2, exactly: the biased byte b =
-// q + 128 becomes the F16 1024 + b (exponent 0x64, b in the mantissa), and
-// 1024 + 128 is subtracted.
-__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t b = w ^ 0x80808080u;
+// Four biased bytes b = q + 128 (the packed image stores Q8_0 quants with
+// their sign bit flipped) -> two half2 holding q, exactly: b becomes the F16
+// 1024 + b (exponent 0x64, b in the mantissa), and 1024 + 128 is subtracted.
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t b, uint32_t& lo, uint32_t& hi) {
   uint32_t l = __byte_perm(b, 0x64646464u, 0x4140);
   uint32_t h = __byte_perm(b, 0x64646464u, 0x4342);
   const half2 off = __float2half2_rn(1152.f);
@@ -143,29 +142,48 @@ struct Frag {
   uint4 xv[NT];
 };
 
-template <int NT, bool Q8>
-__device__ __forceinline__ void load_frag(Frag<NT>& f, const uint8_t* sb, int c, int kel0, const half* xs,
-                                          int xpitch, int nb, int g, int tq) {
+// Per-lane shared-memory offsets of chunk c of a stage (chunk = one 32-element
+// group: 32 bytes of each row for Q8_0, 64 for F16): the lane's 8 (Q8_0) or
+// 16 (F16) bytes of row g in the first half, its F16 scale of row g (Q8_0),
+// and its first K index relative to the stage.
+struct ChunkOff {
+  int w, s, k;
+};
+template <bool Q8>
+__device__ __forceinline__ ChunkOff chunk_off(int c, int g, int tq) {
+  ChunkOff o;
   if constexpr (Q8) {
-    // chunk c = bytes [32c, 32c + 32) of each row; lane takes 8 of them
     const int p = c >> 2, u = ((c & 3) << 1) | (tq >> 1);
-    const int off = p * 1024 + g * 128 + ((u ^ g) << 4) + ((tq & 1) << 3);
-    const uint2 wg = *reinterpret_cast<const uint2*>(sb + off);
-    const uint2 wh = *reinterpret_cast<const uint2*>(sb + GV_HALF_W + off);
+    o.w = p * 1024 + g * 128 + ((u ^ g) << 4) + ((tq & 1) << 3);
+    o.s = 2 * GV_HALF_W + g * 64 + 2 * c;
+  } else {
+    const int p = c >> 1, u = ((c & 1) << 2) | tq;
+    o.w = p * 1024 + g * 128 + ((u ^ g) << 4);
+    o.s = 0;
+  }
+  o.k = c * 32 + 8 * tq;
+  return o;
+}
+
+// One chunk of stage `sb` (shared memory) as MMA fragments: rows g and g+8
+// of the tile, and the activation rows n*8 + g (rows past the batch repeat
+// the last real row; their output columns are never read).
+template <int NT, bool Q8>
+__device__ __forceinline__ void load_frag(Frag<NT>& f, const uint8_t* sb, const ChunkOff& o, const half* const (&xr)[NT],
+                                          int kel0) {
+  if constexpr (Q8) {
+    const uint2 wg = *reinterpret_cast<const uint2*>(sb + o.w);
+    const uint2 wh = *reinterpret_cast<const uint2*>(sb + GV_HALF_W + o.w);
     i8x4_to_h2x2(wg.x, f.ag[0], f.ag[1]);
     i8x4_to_h2x2(wg.y, f.ag[2], f.ag[3]);
     i8x4_to_h2x2(wh.x, f.ah[0], f.ah[1]);
     i8x4_to_h2x2(wh.y, f.ah[2], f.ah[3]);
     // F16 -> F32 is exact for every finite scale
-    const uint8_t* sc = sb + 2 * GV_HALF_W;
-    f.dg = __half2float(*reinterpret_cast<const half*>(sc + g * 64 + 2 * c));
-    f.dh = __half2float(*reinterpret_cast<const half*>(sc + GV_HALF_S + g * 64 + 2 * c));
+    f.dg = __half2float(*reinterpret_cast<const half*>(sb + o.s));
+    f.dh = __half2float(*reinterpret_cast<const half*>(sb + o.s + GV_HALF_S));
   } else {
-    // chunk c = bytes [64c, 64c + 64) of each row; lane takes 16 of them
-    const int p = c >> 1, u = ((c & 1) << 2) | tq;
-    const int off = p * 1024 + g * 128 + ((u ^ g) << 4);
-    const uint4 wg = *reinterpret_cast<const uint4*>(sb + off);
-    const uint4 wh = *reinterpret_cast<const uint4*>(sb + GV_HALF_W + off);
+    const uint4 wg = *reinterpret_cast<const uint4*>(sb + o.w);
+    const uint4 wh = *reinterpret_cast<const uint4*>(sb + GV_HALF_W + o.w);
     f.ag[0] = wg.x;
     f.ag[1] = wg.y;
     f.ag[2] = wg.z;
@@ -176,12 +194,8 @@ __device__ __forceinline__ void load_frag(Frag<NT>& f, const uint8_t* sb, int c,
     f.ah[3] = wh.w;
     f.dg = f.dh = 1.f;
   }
-  const int k = kel0 + c * 32 + 8 * tq;
 #pragma unroll
-  for (int n = 0; n < NT; n++) {
-    const int b = n * 8 + g;
-    f.xv[n] = b < nb ? *reinterpret_cast<const uint4*>(xs + (size_t)b * xpitch + k) : make_uint4(0u, 0u, 0u, 0u);
-  }
+  for (int n = 0; n < NT; n++) f.xv[n] = *reinterpret_cast<const uint4*>(xr[n] + kel0 + o.k);
 }
 
 template <int NT, bool Q8>
@@ -220,6 +234,12 @@ __global__ void gemv3_pack_kernel(const Gemv3Args a, int kstages, uint8_t* __res
       const int kb = ks * GV_BYTES + p * 128 + u * 16;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (valid && kb < row_bytes) v = *reinterpret_cast<const uint4*>(w.q + (size_t)row * row_bytes + kb);
+      if (q8) {  // quants stored biased (q + 128); padding becomes q = 0
+        v.x ^= 0x80808080u;
+        v.y ^= 0x80808080u;
+        v.z ^= 0x80808080u;
+        v.w ^= 0x80808080u;
+      }
       *reinterpret_cast<uint4*>(out + (i / 8) * GV_HALF_W + p * 1024 + (i % 8) * 128 + ((u ^ (i % 8)) << 4)) = v;
     } else {
       const int j = i16 - 16 * 64, i = j / 4, v4 = j % 4;
@@ -262,7 +282,9 @@ template <int NT, bool Q8>
 __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_constant__ GemvSeq q, int nst) {
   // [full | empty | tdone | tfree barriers][cross-warp sums][activation rows][nst-stage ring]
   extern __shared__ uint8_t gsm_raw[];
-  uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned by an integer offset from the shared array, so every
+  // pointer below stays a known shared-memory address (shared loads)
+  uint8_t* gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
   uint64_t* empty = full + GV_MAX_STAGES;
   uint64_t* tdone = empty + GV_MAX_STAGES;  // [2] a tile's partial sums are written (GV_WARPS arrivals)
@@ -291,32 +313,27 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 
   if (warp == GV_WARPS) {
     // ---------------- producer: one thread, one bulk copy per stage, all phases
+    if (lane != 0) return;
     int stage = 0;
     uint32_t phase = 0;
     const uint32_t sbytes = (uint32_t)gv_stage_bytes(Q8);
     for (int p = 0; p < q.n; p++) {
       const GvPhase w = gv_phase(q, p, Q8);
-      const uint8_t* src = q.ph[p].packed;
-      for (int t = w.t0; t < w.t1; t++) {
-        for (int ks = 0; ks < w.kstages; ks++) {
-          if (!mbar_wait_sleep(&empty[stage], phase ^ 1, budget)) {
-            if (lane == 0) atomicOr(err, 32u);
-          }
-          if (lane == 0) {
-            mbar_expect_tx(&full[stage], sbytes);
-            bulk_g2s(ring + stage * GV_STAGE, src + ((size_t)t * w.kstages + ks) * sbytes, sbytes, &full[stage]);
-          }
-          __syncwarp();
-          if (++stage == nst) {
-            stage = 0;
-            phase ^= 1;
-          }
+      const uint8_t* src = q.ph[p].packed + (size_t)w.t0 * w.kstages * sbytes;
+      const int nstg = (w.t1 - w.t0) * w.kstages;  // this CTA's stages of the phase: one contiguous range
+      for (int j = 0; j < nstg; j++) {
+        if (!mbar_wait_sleep(&empty[stage], phase ^ 1, budget)) atomicOr(err, 32u);
+        mbar_expect_tx(&full[stage], sbytes);
+        bulk_g2s(ring + stage * GV_STAGE, src + (size_t)j * sbytes, sbytes, &full[stage]);
+        if (++stage == nst) {
+          stage = 0;
+          phase ^= 1;
         }
       }
     }
     // Every fill is consumed before the CTA exits (no copy left in flight).
     for (int i = 0; i < nst; i++) {
-      if (!mbar_wait(&empty[stage], phase ^ 1, budget) && lane == 0) atomicOr(err, 64u);
+      if (!mbar_wait(&empty[stage], phase ^ 1, budget)) atomicOr(err, 64u);
       if (++stage == nst) {
         stage = 0;
         phase ^= 1;
@@ -510,6 +527,10 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 
   // ---------------- compute warps
   const int tid = threadIdx.x;
+  constexpr int CPW = Q8 ? 2 : 1;  // chunks per warp in a full stage
+  ChunkOff co[CPW];
+#pragma unroll
+  for (int i = 0; i < CPW; i++) co[i] = chunk_off<Q8>(warp + i * GV_WARPS, g, tq);
   pdl_wait();
   int stage = 0, T = 0;
   uint32_t phase = 0;
@@ -563,6 +584,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
     }
     // the next kernel may start once every CTA is past its last grid barrier
     if (p == q.n - 1) pdl_trigger();
+    const half* xr[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) xr[n] = xs + (size_t)min(n * 8 + g, a.nb - 1) * xpitch;
     for (int t = w.t0; t < w.t1; t++, T++) {
       float acc[NT][4];
 #pragma unroll
@@ -570,26 +594,36 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[n][j] = 0.f;
       for (int ks = 0; ks < w.kstages; ks++) {
-        if (!mbar_wait_sleep(&full[stage], phase, budget)) {
+        if (!mbar_wait_spin(&full[stage], phase, budget)) {
           if (lane == 0) atomicOr(err, 128u);
         }
         const uint8_t* sb = ring + stage * GV_STAGE;
         const int kb = ks * GV_BYTES;
         const int nbytes = min(GV_BYTES, row_bytes - kb);
-        const int chunks = nbytes / (Q8 ? 32 : 64);  // 32-element groups in this stage
-        const int kel0 = Q8 ? kb : kb / 2;           // first K index of the stage
+        const int kel0 = Q8 ? kb : kb / 2;  // first K index of the stage
         // A full stage has 32 (Q8_0) or 16 (F16) groups: warp w takes groups
         // w and w + 16, all loads issued before the MMAs.
-        constexpr int CPW = Q8 ? 2 : 1;
         Frag<NT> f[CPW];
+        if (nbytes == GV_BYTES) {
 #pragma unroll
-        for (int i = 0; i < CPW; i++)
-          if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, warp + i * GV_WARPS, kel0, xs, xpitch, a.nb, g, tq);
+          for (int i = 0; i < CPW; i++) load_frag<NT, Q8>(f[i], sb, co[i], xr, kel0);
+          // the stage's bytes are in registers: hand the slot back to the producer
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
 #pragma unroll
-        for (int i = 0; i < CPW; i++)
-          if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
+          for (int i = 0; i < CPW; i++) mma_frag<NT, Q8>(f[i], acc);
+        } else {
+          // the last stage of a row whose bytes are not a multiple of 1 KB
+          const int chunks = nbytes / (Q8 ? 32 : 64);
+#pragma unroll
+          for (int i = 0; i < CPW; i++)
+            if (warp + i * GV_WARPS < chunks) load_frag<NT, Q8>(f[i], sb, co[i], xr, kel0);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
+#pragma unroll
+          for (int i = 0; i < CPW; i++)
+            if (warp + i * GV_WARPS < chunks) mma_frag<NT, Q8>(f[i], acc);
+        }
         if (++stage == nst) {
           stage = 0;
           phase ^= 1;

@@ -68,6 +68,18 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   return true;
 }
 
+// Bounded wait that polls without a suspend hint and reads the clock only
+// every 64 polls: a cheap loop for waits that usually end within a few
+// hundred cycles.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, long long budget) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (unsigned i = 1;; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0 && clock64() - t0 > budget) return false;
+  }
+}
+
 // Bounded wait: false once `budget` SM clock cycles have passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long budget) {
   if (mbar_try_wait(bar, parity)) return true;
