@@ -576,6 +576,45 @@ def run_decode(args):
     print(json.dumps(out), flush=True)
 
 
+def run_inproc(args):
+    """configs[1] through the product's own multi-device sharding: ONE
+    process opens the model on GPUs 0..N-1 (the first replica read from the
+    file, the others copied over NVLink) and each step is one
+    laya_decide_batch over the 64-request batch, which the library splits
+    into contiguous token-balanced ranges, one host thread per device.
+    value = 64 requests / the step's device time (CUDA events, max over
+    devices); e2e = the same over the wall time of the call.  Not the
+    contract line (that one runs one process per GPU under torchrun)."""
+    import torch
+
+    from laya_goish_b200 import engine
+    from laya_goish_b200.engine import Question
+
+    n = max(1, args.gpus)
+    if torch.cuda.device_count() < n:
+        raise SystemExit(f"--workload inproc needs {n} visible GPUs")
+    path = synth.model_path("cfg1")
+    batch, cand = inputs(0, args.requests)
+    qs = [Question("choice", cand)]
+    t0 = time.perf_counter()
+    e = engine.Engine(path, devices=list(range(n)))
+    open_s = time.perf_counter() - t0
+    for _ in range(args.warmup):
+        e.decide_batch(batch, qs)
+    dev_ms, wall = 0.0, 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        e.decide_batch(batch, qs)
+        wall += (time.perf_counter() - t0) * 1000.0
+        dev_ms += e.timing()["device_ms"]
+    e.close()
+    out = {"workload": f"inproc: {WORKLOAD}; one process, Engine(devices=0..{n - 1})", "n_gpus": n,
+           "value": args.requests * args.steps / (dev_ms / 1000.0), "unit": "req/s",
+           "ms_per_step": dev_ms / args.steps, "e2e_req_s": args.requests * args.steps / (wall / 1000.0),
+           "open_s": open_s, "steps": args.steps, "warmup": args.warmup}
+    print(json.dumps(out), flush=True)
+
+
 def run_load(args):
     """Start-up cost: one laya_open of a synthetic GGUF onto GPUs 0..N-1 from
     one process (the C ABI's multi-device model).  The file is opened once
@@ -682,7 +721,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3", "load", "openthai"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3", "load", "openthai", "inproc"])
     ap.add_argument("--load-cfg", default="cfg3", help="load: synthetic model to open")
     ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
@@ -699,6 +738,8 @@ def main():
         run_decode(args)
     elif args.workload == "load":
         run_load(args)
+    elif args.workload == "inproc":
+        run_inproc(args)
     elif args.workload == "openthai":
         run_openthai(args)
     elif args.workload in AUX:

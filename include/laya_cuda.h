@@ -215,6 +215,14 @@ int laya_tensor_f32(laya_model* m, const char* name, float* out, size_t max_elem
 int laya_matrix_apply_static(uint32_t kind, const uint8_t* w, int rows, int cols, const float* x, int m,
                              const float* bias, float* out, void* stream);
 
+/* Failure-detection self-test; no counterpart in the reference.  Launches
+ * one device-side wait that nothing completes, bounded by budget_cycles SM
+ * clock cycles (1 .. 4e9) through the same helper as every pipeline wait of
+ * the library, and returns what a real expiry returns: LAYA_E_TIMEOUT, with
+ * the context still usable for the next call.  LAYA_OK would mean the wait
+ * ended without its budget running out. */
+int laya_wait_selftest(int device, long long budget_cycles);
+
 /* ---- timing of the last laya_decide_batch / laya_decode call ---- */
 typedef struct laya_timing {
   double device_ms;   /* CUDA-event time on the device stream(s), inputs already in HBM; max over devices */

@@ -106,6 +106,7 @@ def lib() -> ctypes.CDLL:
     L.laya_forward.argtypes = [P, P, I, P, I, P]
     L.laya_tensor_f32.argtypes = [P, ctypes.c_char_p, P, SZ]
     L.laya_matrix_apply_static.argtypes = [ctypes.c_uint32, P, I, I, P, I, P, P, P]
+    L.laya_wait_selftest.argtypes = [I, ctypes.c_longlong]
     L.laya_last_timing.argtypes = [P, ctypes.POINTER(Timing)]
     L.laya_profile_enable.argtypes = [P, I]
     L.laya_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I]

@@ -259,6 +259,21 @@ struct ReleaseOnExit {
   }
 };
 
+int laya_wait_selftest(int device, long long budget_cycles) {
+  if (budget_cycles < 1 || budget_cycles > 4000000000ll) return fail(LAYA_E_INVALID, "budget out of range");
+  LAYA_CK(cudaSetDevice(device));
+  DevBuf derr;
+  ReleaseOnExit guard{{&derr}};
+  if (int rc = derr.ensure(16)) return rc;
+  cudaError_t e = cudaMemset(derr.p, 0, 16);
+  if (e == cudaSuccess) e = wait_probe(derr.as<unsigned>(), budget_cycles, 0);
+  unsigned err = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&err, derr.p, 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "laya_wait_selftest");
+  if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");
+  return 0;
+}
+
 int laya_dequantize(int device, uint32_t kind, const uint8_t* blocks, size_t nbytes, float* out) {
   int block, size;
   if (!ggml_layout(kind, &block, &size)) return fail(LAYA_E_INVALID, "unsupported GGML tensor type");

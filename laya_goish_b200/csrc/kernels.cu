@@ -24,6 +24,24 @@ __global__ void dequant_raw_kernel(int kind, const uint8_t* __restrict__ b, size
   decode_raw_block(kind, b, i, F32Sink{out});
 }
 
+// A device-side wait that nothing completes: one thread waits on a fresh
+// mbarrier (one expected arrival, none ever made) with the same bounded
+// helper as every pipeline wait of the library, records the expiry in the
+// error word when the budget runs out, and returns; the other threads leave
+// at once.  Nothing is in flight when it ends, so the context stays usable.
+__global__ void wait_probe_kernel(unsigned* err, long long budget) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  if (!mbar_wait(&bar, 0, budget)) atomicOr(err, 1u << 20);
+}
+
+cudaError_t wait_probe(unsigned* err, long long budget, cudaStream_t st) {
+  wait_probe_kernel<<<1, 32, 0, st>>>(err, budget);
+  return cudaGetLastError();
+}
+
 cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st) {
   if (!nblocks) return cudaSuccess;
   dequant_raw_kernel<<<(unsigned)((nblocks + 255) / 256), 256, 0, st>>>(kind, blocks, nblocks, out);

@@ -41,6 +41,8 @@ struct AttnParams {
 cudaError_t attention_tc(const AttnParams& p, cudaStream_t st);
 
 cudaError_t dequant_raw(int kind, const uint8_t* blocks, size_t nblocks, float* out, cudaStream_t st);
+// One bounded wait that nothing completes (laya_wait_selftest).
+cudaError_t wait_probe(unsigned* err, long long budget, cudaStream_t st);
 cudaError_t dequant_f16(const QTensor& t, half* out, int ldo, int grp, int gstride, int goff, cudaStream_t st);
 // pdl: launch with programmatic dependent launch allowed (decode graph).
 cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cudaStream_t st, bool pdl = false);

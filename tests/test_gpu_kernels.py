@@ -82,3 +82,21 @@ def test_upload_transcoding_bit_exact(tiny_paths, name):
             if int(t.tensor_type) in (0, 1) or int(t.tensor_type) in (2, 8, 12, 14):
                 assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), t.name
     om.close()
+
+
+def test_device_wait_that_runs_out_reports_timeout_and_context_survives():
+    # A device-side wait that nothing completes (a fresh mbarrier nobody
+    # arrives at), bounded by ~1 ms of SM cycles: the kernel records the
+    # expiry and returns, the host maps it to LAYA_E_TIMEOUT, and the next
+    # call on the same context succeeds.  No fault, trap or hang is involved.
+    from laya_goish_b200 import _lib
+
+    L = _lib.lib()
+    assert L.laya_wait_selftest(0, 2_000_000) == _lib.E_TIMEOUT
+    assert b"budget" in L.laya_last_error()
+    assert L.laya_wait_selftest(0, 0) == _lib.E_INVALID
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((64, 256), dtype=np.float32) * 0.02).astype(np.float16).astype(np.float32)
+    x = rng.standard_normal((5, 256), dtype=np.float32).astype(np.float16).astype(np.float32)
+    got = engine.matrix_apply(1, synth.encode(1, w), 64, 256, x)
+    assert np.abs(got - x @ w.T).max() < 1e-3
