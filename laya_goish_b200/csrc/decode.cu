@@ -1218,6 +1218,19 @@ static GemvPlan plan1(const QTensor& w, const half* x, int ldx, float* y, int ld
 // Batches above this size run the linear layers on the tcgen05 GEMM.
 static constexpr int kGemvMaxBatch = 16;
 
+static int pad_batch(int nb);
+
+// Whether a decode batch of nb sequences runs its linear layers as GEMVs:
+// at most kGemvMaxBatch rows, and, with the streaming GEMV, only when its
+// staged activation rows (the widest K of the layer) fit beside its ring;
+// otherwise the tcgen05 GEMM takes them (e.g. 16 rows of the 8192-wide
+// down projection would need 262 KB of shared memory).
+static bool gemv_batch(const Config& c, int nb) {
+  if (nb > kGemvMaxBatch) return false;
+  if (!gemv3_enabled()) return true;
+  return gemv3_fits(pad_batch(nb), std::max(c.d, std::max(c.ffn, c.H * c.hd)));
+}
+
 static int pad_batch(int nb) { return nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : nb <= 8 ? 8 : 16; }
 
 // Fixed device addresses of the per-step inputs.
@@ -1239,7 +1252,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
   const Config& c = m.cfg;
   const int qd = c.H * c.hd, kd = c.KV * c.hd, d = c.d, ffn = c.ffn;
   cudaStream_t st = r.stream;
-  const bool small = nb <= kGemvMaxBatch;
+  const bool small = gemv_batch(c, nb);
   const int nbp = small ? pad_batch(nb) : nb;  // GEMV batch (padded rows are zero)
   int rc;
   r.launches++;
@@ -1542,7 +1555,7 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   }
   int rc;
   if ((rc = timing_begin_call(r))) return rc;
-  const bool small = n_seqs <= kGemvMaxBatch;
+  const bool small = gemv_batch(c, n_seqs);
   if (!small && (rc = ensure_head16(m, r))) return rc;
   if (small && gemv3_enabled() && (rc = ensure_gv_packed(m, r))) return rc;
   // pages: context + generated tokens per sequence

@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -549,6 +550,20 @@ __device__ __forceinline__ void resid_tma_tile(const GemmArgs& a, const CUtensor
 //   empty[s]  each CTA; arrived by the leader's MMA commit to both CTAs
 //   tfull[b]  each CTA; arrived by the leader's commit to both CTAs
 //   tempty[b] leader only; 8 arrivals, one per epilogue warp of either CTA
+// Output tile of tile index t in the pair kernel's walk.  Consecutive
+// indices run down a group of `group` row bands before moving to the next
+// column tile, so the CTA pairs working at once share a few row bands of A
+// and a few column tiles of the weights (group 1: row band by row band).
+__device__ __forceinline__ void pair_tile(const GemmArgs& a, int t, int& mt, int& nt) {
+  const int G = a.group > 1 ? a.group : 1;
+  const int per = G * a.n_tiles;
+  const int g0 = (t / per) * G;
+  const int gm = min(G, a.m_tiles - g0);
+  const int i = t - (t / per) * per;
+  nt = i / gm;
+  mt = g0 + i % gm;
+}
+
 template <int EPI, int HD>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -606,9 +621,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // the first unit's B tile are pulled into L2 before waiting for it.
       if (cluster < total) {
         const int tile = cluster % tiles, sp = cluster / tiles;
+        int mt0, nt0;
+        pair_tile(a, tile, mt0, nt0);
         const int kb0 = sp * kbs, kb1 = min(kblocks, kb0 + min(kbs, 2 * PAIR_STAGES));
-        for (int kb = kb0; kb < kb1; kb++)
-          tma_prefetch_2d(&tmB, kb * BK, (tile % a.n_tiles) * 256 + (int)rank * 128);
+        for (int kb = kb0; kb < kb1; kb++) tma_prefetch_2d(&tmB, kb * BK, nt0 * 256 + (int)rank * 128);
       }
       pdl_wait();
       pdl_trigger();
@@ -617,7 +633,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int unit = cluster; unit < total && ok; unit += nclusters) {
         const int tile = unit % tiles, sp = unit / tiles;
-        const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+        int mt, nt;
+        pair_tile(a, tile, mt, nt);
         const int kb1 = min(kblocks, (sp + 1) * kbs);
         for (int kb = sp * kbs; kb < kb1; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, budget)) {
@@ -693,7 +710,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint32_t acc_phase = 0;
     for (int unit = cluster; unit < total; unit += nclusters) {
       const int tile = unit % tiles;
-      const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+      int mt, nt;
+      pair_tile(a, tile, mt, nt);
       const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
       if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
         atomicOr(a.err, 8u);
@@ -843,6 +861,16 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, a);
 }
 
+// Row bands per group of the pair kernel's tile walk (pair_tile).
+static int pair_group() {
+  static const int g = [] {
+    const char* e = std::getenv("LAYA_GEMM_GROUP");
+    const int v = e ? std::atoi(e) : 1;
+    return v >= 1 ? v : 1;
+  }();
+  return g;
+}
+
 int gemm_ksplit(int M, int N, int K, int num_sms) {
   if (M <= BM || num_sms < 2) return 1;
   const int tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
@@ -890,6 +918,7 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
     }
     a.m_tiles = (a.M + 255) / 256;
     a.n_tiles = (a.N + BN - 1) / BN;
+    a.group = pair_group();
     switch (epi) {
       case EPI_F32: return launch_pair<EPI_F32, 64>(ta, tb, tr, a, num_sms, st, pdl);
       case EPI_F16: return launch_pair<EPI_F16, 64>(ta, tb, tr, a, num_sms, st, pdl);

@@ -18,6 +18,7 @@ enum Epi : int {
 struct GemmArgs {
   int M, N, K;
   int m_tiles, n_tiles;   // filled by gemm_launch
+  int group;              // row bands per group of the CTA-pair tile walk (filled by gemm_launch)
   const float* bias;      // [N] or null
   void* out;
   int ldo;

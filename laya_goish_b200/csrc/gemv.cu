@@ -654,6 +654,8 @@ static int stages_for(int nb, int K, int nt) {
 }
 static int gemv3_stages(const Gemv3Args& a, int nt) { return stages_for(a.nb, a.K, nt); }
 
+bool gemv3_fits(int nb, int kmax) { return nb >= 1 && nb <= 16 && stages_for(nb, kmax, nb <= 8 ? 1 : 2) >= 2; }
+
 // Weight-side conditions (packing needs only these).
 static bool gemv3_weights_ok(const Gemv3Args& a) {
   if (a.K <= 0 || a.K % 256) return false;

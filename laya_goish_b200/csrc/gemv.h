@@ -69,6 +69,9 @@ struct GemvSeq {
 // True when gemv3_launch handles these operands (Q8_0 or F16, K a multiple
 // of 256, at most 16 batch rows, the staged activations fit).
 bool gemv3_supported(const Gemv3Args& a);
+// True when nb activation rows of up to kmax columns can be staged beside a
+// ring of at least two stages.
+bool gemv3_fits(int nb, int kmax);
 // The segments' weights rearranged for streaming: per 16-row tile and per
 // 1 KB of K, one contiguous stage image.  Depends only on mode, segments and
 // K (not on the batch rows), so it is built once per model.
