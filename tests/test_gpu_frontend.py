@@ -54,3 +54,32 @@ def test_text_state_matches_token_ids(tiny_paths):
         b = svc.handle("POST", "/v1/decide", json.dumps({"state": tok.encode(text), "questions": q_ids}))
     assert a.status == 200 and b.status == 200
     assert a.body["answers"] == b.body["answers"]
+
+
+def test_batch_endpoint_matches_oracle(tiny_paths):
+    # The served answers against the oracle's decide (the reference's
+    # decision rules on its CPU forward), not only against the same engine.
+    import oracle
+
+    path = tiny_paths["tiny-llama-q4_k_m"]
+    rng = np.random.default_rng(22)
+    states = [synth.token_ids(rng, 1000, int(n)).tolist() for n in (9, 64, 130)]
+    q = {"pick": {"type": "choice", "criteria": {"a": 31, "b": 32, "c": 33, "d": 34}},
+         "lvl": {"type": "score", "criteria": [[3, 4, 5], [6, 7, 8]], "suffix": [40, 41]},
+         "ok": {"type": "noul", "criteria": {"false": 51, "true": 52}, "suffix": [9]}}
+    with engine.Engine(path) as e:
+        svc = frontend.DecideService(e)
+        r = svc.handle("POST", "/v1/decide/batch", json.dumps({"states": states, "questions": q}))
+    assert r.status == 200, r.body
+    o = oracle.Model(open(path, "rb").read(), threads=4, attn_threads=4)
+    for st, res in zip(states, r.body["results"]):
+        a = res["answers"]
+        pick = o.decide(st, 0, [31, 32, 33, 34])
+        lvl = o.decide(st, 1, [[3, 4, 5], [6, 7, 8]], suffix=[40, 41])
+        ok = o.decide(st, 2, [51, 52], suffix=[9])
+        assert np.allclose(list(a["pick"]["probabilities"].values()), pick["probabilities"], atol=1e-3, rtol=1e-2)
+        if sorted(pick["probabilities"])[-1] - sorted(pick["probabilities"])[-2] > 2e-3:
+            assert a["pick"]["choice"] == "abcd"[pick["choice"]]
+        assert a["lvl"]["score"] == pytest.approx(lvl["score"], abs=2e-3)
+        assert a["ok"]["noul"] == pytest.approx(ok["noul"], abs=1e-3, rel=1e-2)
+    o.close()
