@@ -156,7 +156,9 @@ int laya_gated_delta_mixer(int device, const float* raw, const float* z, const f
  * (applied with offset 1, eps 1e-6); RoPE on the first `rot` dimensions of a
  * head with base theta (the reference: hd 256, rot 64, theta 1e7); out = s
  * rows of H x hd, sigmoid(gate) x attention, before o_proj.  hd 64, 128 or
- * 256; H a multiple of KV.  Host buffers. */
+ * 256; H a multiple of KV.  Host buffers.  Runs on the tcgen05 attention:
+ * the normalised, rotated q and k and v are rounded to F16 (the tensor-core
+ * operand type), scores and sums stay F32, the output is rounded to F16. */
 int laya_gated_attention(int device, const float* qgate, const float* k, const float* v, const float* qn,
                          const float* kn, int s, int H, int KV, int hd, int rot, float theta, float* out);
 /* OpenThai model on one GPU (Model::load / Model::forward,

@@ -38,20 +38,27 @@ namespace laya {
 template <int HD>
 struct Atc {
   // K pages are released as soon as their S MMA is done, V pages only after
-  // their P.V MMA, so the K ring is the deeper one.
-  static constexpr int NK = 3;
-  static constexpr int NV = HD == 64 ? 2 : 3;
+  // their P.V MMA, so the K ring is the deeper one.  Head dim 256 (OpenThai's
+  // gated attention) keeps one Q buffer and one O accumulator so that its
+  // 64 KB Q tile and 32 KB pages fit: the next unit's P.V then waits for the
+  // previous unit's O to be read.
+  static constexpr int NQ = HD == 256 ? 1 : 2;     // Q buffers
+  static constexpr int NO = HD == 256 ? 1 : 2;     // O accumulators in TMEM
+  static constexpr int NK = HD == 256 ? 2 : 3;
+  static constexpr int NV = HD == 128 ? 3 : 2;
   static constexpr int Q_BYTES = 128 * HD * 2;     // [HD/64 blocks][128 rows][128 B]
   static constexpr int KV_BYTES = 64 * HD * 2;     // K or V page: [HD/64 blocks][64 rows][128 B]
   static constexpr int P_BYTES = 128 * 64 * 2;     // [128 rows][64 keys] F16
-  static constexpr int OFF_K = 2 * Q_BYTES;        // two Q buffers
+  static constexpr int OFF_K = NQ * Q_BYTES;
   static constexpr int OFF_V = OFF_K + NK * KV_BYTES;
   static constexpr int OFF_P = OFF_V + NV * KV_BYTES;
   static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = HD == 64 ? 256 : 512;  // S buffers at 0, 64; O buffers at 128, 128 + HD
+  static constexpr int TMEM_COLS = HD == 64 ? 256 : 512;  // S buffers at 0, 64; O buffers at 128 (+ HD)
   static constexpr int O_COL = 128;
   static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
+  static_assert(O_COL + NO * HD <= TMEM_COLS, "TMEM columns");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 // 2^x with the SFU's approximate exponent (PTX ex2.approx.ftz: relative
@@ -93,7 +100,8 @@ __global__ void __launch_bounds__(192, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, half* __restrict__ o, int ldo,
                    const int* __restrict__ tables, const AttnItem* __restrict__ items, int n_units, int H, int KV,
-                   float scale_log2, unsigned* err, long long budget) {
+                   float scale_log2, const float* __restrict__ gate, int ldg, int ghs, unsigned* err,
+                   long long budget) {
   using C = Atc<HD>;
   extern __shared__ uint8_t at_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_raw) + 1023) & ~uintptr_t(1023));
@@ -101,7 +109,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sK = sm + C::OFF_K;
   uint8_t* sV = sm + C::OFF_V;
   uint8_t* sP = sm + C::OFF_P;
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);  // [2] Q of unit k in buffer k & 1
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);  // [2] Q of unit k in buffer k % NQ
   uint64_t* q_empty = q_full + 2;                                   // [2] the unit's last S MMA is done
   uint64_t* k_full = q_empty + 2;                                   // [NK] K of page g in stage g % NK
   uint64_t* k_empty = k_full + C::NK;                               // [NK] its S MMA is done
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_empty = s_full + 2;                                   // [2] 4 softmax warps read it
   uint64_t* p_full = s_empty + 2;                                   // [2] P of page g written (4 warps)
   uint64_t* o_done = p_full + 2;                                    // one phase per P.V page
-  uint64_t* o_full = o_done + 1;                                    // [2] O of unit k complete
+  uint64_t* o_full = o_done + 1;                                    // [2] O of unit k (buffer k % NO) complete
   uint64_t* o_empty = o_full + 2;                                   // [2] O of unit k read (4 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
 
@@ -151,8 +159,8 @@ __global__ void __launch_bounds__(192, 1)
       int g = 0;
       for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
         const AtcUnit w = atc_unit(items, u, H, KV);
-        const int qb = k & 1;
-        if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
+        const int qb = k % C::NQ;
+        if (!mbar_wait(&q_empty[qb], ((k / C::NQ) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
         mbar_expect_tx(&q_full[qb], C::Q_BYTES);
 #pragma unroll
         for (int hb = 0; hb < HD / 64; hb++)
@@ -188,7 +196,7 @@ __global__ void __launch_bounds__(192, 1)
       bool pfirst = false, plast = false;
       auto issue_pv = [&]() {
         const int pb = pg & 1;
-        if (pfirst && !mbar_wait(&o_empty[pob], ((pk >> 1) & 1) ^ 1, budget)) atomicOr(err, 1u << 16);
+        if (pfirst && !mbar_wait(&o_empty[pob], ((pk / C::NO) & 1) ^ 1, budget)) atomicOr(err, 1u << 16);
         const int vs = pg % C::NV;
         if (!mbar_wait(&p_full[pb], (pg >> 1) & 1, budget)) atomicOr(err, 1u << 16);
         if (!mbar_wait(&v_full[vs], (pg / C::NV) & 1, budget)) atomicOr(err, 1u << 16);
@@ -205,8 +213,8 @@ __global__ void __launch_bounds__(192, 1)
       int g = 0;
       for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
         const AtcUnit w = atc_unit(items, u, H, KV);
-        const int qb = k & 1;
-        if (!mbar_wait(&q_full[qb], (k >> 1) & 1, budget)) atomicOr(err, 1u << 13);
+        const int qb = k % C::NQ;
+        if (!mbar_wait(&q_full[qb], (k / C::NQ) & 1, budget)) atomicOr(err, 1u << 13);
         for (int j = 0; j < w.nblk; j++, g++) {
           const int ks = g % C::NK, sb = g & 1;
           if (!mbar_wait(&k_full[ks], (g / C::NK) & 1, budget)) atomicOr(err, 1u << 14);
@@ -221,7 +229,7 @@ __global__ void __launch_bounds__(192, 1)
           if (j == w.nblk - 1) umma_commit(&q_empty[qb]);
           if (pg >= 0) issue_pv();
           pg = g;
-          pob = k & 1;
+          pob = k % C::NO;
           pk = k;
           pfirst = j == 0;
           plast = j == w.nblk - 1;
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(192, 1)
     int g = 0;
     for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
       const AtcUnit w = atc_unit(items, u, H, KV);
-      const int ob = k & 1;
+      const int ob = k % C::NO;
       const int pos = w.it.pos0 + r;
       float mref = -INFINITY, l = 0.f;  // reference maximum in log2 units
       for (int j = 0; j < w.nblk; j++, g++) {
@@ -334,7 +342,7 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) mbar_arrive(&p_full[sb]);
       }
       // O of this unit
-      if (!mbar_wait(&o_full[ob], (k >> 1) & 1, budget) && lane == 0) atomicOr(err, 1u << 19);
+      if (!mbar_wait(&o_full[ob], (k / C::NO) & 1, budget) && lane == 0) atomicOr(err, 1u << 19);
       tc_fence_after();
       const float inv = 1.f / l;
 #pragma unroll
@@ -345,13 +353,25 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_wait();
         if (r < w.it.q_len) {
           half* dst = o + (size_t)(w.it.q_row + r) * ldo + w.h * HD + c * 32;
+          if (gate) {
+            // OpenThai's output gate: o * sigmoid(gate) (src/models/openthai/model.rs:293-295)
+            const float* gr = gate + (size_t)(w.it.q_row + r) * ldg + w.h * ghs + c * 32;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              const float gv = gr[i];
+              v[i] = __float_as_uint(__uint_as_float(v[i]) * inv * (1.f / (1.f + expf(-gv))));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * inv);
+          }
 #pragma unroll
           for (int u4 = 0; u4 < 4; u4++) {
             uint4 ow;
-            ow.x = pack_h2(__uint_as_float(v[8 * u4]) * inv, __uint_as_float(v[8 * u4 + 1]) * inv);
-            ow.y = pack_h2(__uint_as_float(v[8 * u4 + 2]) * inv, __uint_as_float(v[8 * u4 + 3]) * inv);
-            ow.z = pack_h2(__uint_as_float(v[8 * u4 + 4]) * inv, __uint_as_float(v[8 * u4 + 5]) * inv);
-            ow.w = pack_h2(__uint_as_float(v[8 * u4 + 6]) * inv, __uint_as_float(v[8 * u4 + 7]) * inv);
+            ow.x = pack_h2(__uint_as_float(v[8 * u4]), __uint_as_float(v[8 * u4 + 1]));
+            ow.y = pack_h2(__uint_as_float(v[8 * u4 + 2]), __uint_as_float(v[8 * u4 + 3]));
+            ow.z = pack_h2(__uint_as_float(v[8 * u4 + 4]), __uint_as_float(v[8 * u4 + 5]));
+            ow.w = pack_h2(__uint_as_float(v[8 * u4 + 6]), __uint_as_float(v[8 * u4 + 7]));
             reinterpret_cast<uint4*>(dst)[u4] = ow;
           }
         }
@@ -388,13 +408,14 @@ static cudaError_t attn_tc_go(const AttnParams& p, const CUtensorMap& tq, const 
   const int units = p.n_items * p.H;
   const int grid = std::min(units, Atc<HD>::CTAS_PER_SM * sms[dev & 63]);
   attn_tc_kernel<HD><<<grid, 192, Atc<HD>::SMEM, st>>>(tq, tk, tv, p.o, p.ldo, p.tables, p.items, units, p.H, p.KV,
-                                                       p.scale_log2, p.err, 100000000ll);
+                                                       p.scale_log2, p.gate, p.ldg, p.ghs, p.err, 100000000ll);
   return cudaGetLastError();
 }
 
 cudaError_t attention_tc(const AttnParams& p, cudaStream_t st) {
   if (!p.n_items) return cudaSuccess;
-  if ((p.hd != 64 && p.hd != 128) || !p.err || p.q_rows <= 0 || p.kv_rows <= 0 || (p.ldq % 8)) return cudaErrorNotSupported;
+  if ((p.hd != 64 && p.hd != 128 && p.hd != 256) || !p.err || p.q_rows <= 0 || p.kv_rows <= 0 || (p.ldq % 8))
+    return cudaErrorNotSupported;
   CUtensorMap tq, tk, tv;
   const uint64_t qdims[2] = {(uint64_t)p.ldq, (uint64_t)p.q_rows}, qstr[1] = {(uint64_t)p.ldq * 2};
   const uint32_t qbox[2] = {64, 128};
@@ -405,7 +426,8 @@ cudaError_t attention_tc(const AttnParams& p, cudaStream_t st) {
       !encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.vc, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if (p.hd == 64) return attn_tc_go<64>(p, tq, tk, tv, st);
-  return attn_tc_go<128>(p, tq, tk, tv, st);
+  if (p.hd == 128) return attn_tc_go<128>(p, tq, tk, tv, st);
+  return attn_tc_go<256>(p, tq, tk, tv, st);
 }
 
 }  // namespace laya

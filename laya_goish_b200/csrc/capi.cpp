@@ -358,11 +358,12 @@ int laya_gated_attention(int device, const float* qgate, const float* k, const f
   if (s == 0) return 0;
   LAYA_CK(cudaSetDevice(device));
   const size_t nq = (size_t)s * H * 2 * hd, nk = (size_t)s * KV * hd, no = (size_t)s * H * hd;
-  DevBuf dq, dk, dv, dn, dsc, dout;
-  ReleaseOnExit guard{{&dq, &dk, &dv, &dn, &dsc, &dout}};
+  DevBuf dq, dk, dv, dn, dsc, dout, derr;
+  ReleaseOnExit guard{{&dq, &dk, &dv, &dn, &dsc, &dout, &derr}};
   int rc;
   if ((rc = dq.ensure(nq * 4)) || (rc = dk.ensure(nk * 4)) || (rc = dv.ensure(nk * 4)) ||
-      (rc = dn.ensure((size_t)2 * hd * 4)) || (rc = dsc.ensure((no + nk) * 4)) || (rc = dout.ensure(no * 4)))
+      (rc = dn.ensure((size_t)2 * hd * 4)) || (rc = dsc.ensure(gated_attention_scratch(s, H, KV, hd))) ||
+      (rc = dout.ensure(no * 2)) || (rc = derr.ensure(16)))
     return rc;
   float* dnw = dn.as<float>();
   cudaError_t e = cudaMemcpy(dq.p, qgate, nq * 4, cudaMemcpyHostToDevice);
@@ -370,11 +371,17 @@ int laya_gated_attention(int device, const float* qgate, const float* k, const f
   if (e == cudaSuccess) e = cudaMemcpy(dv.p, v, nk * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(dnw, qn, (size_t)hd * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(dnw + hd, kn, (size_t)hd * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(derr.p, 0, 16);
   if (e == cudaSuccess)
     e = gated_attention(dq.as<float>(), dk.as<float>(), dv.as<float>(), dnw, dnw + hd, s, H, KV, hd, rot, theta,
-                        dsc.as<float>(), dout.as<float>(), 0);
-  if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, no * 4, cudaMemcpyDeviceToHost);
+                        dsc.p, dout.as<half>(), derr.as<unsigned>(), 0);
+  std::vector<uint16_t> o16(no);
+  if (e == cudaSuccess) e = cudaMemcpy(o16.data(), dout.p, no * 2, cudaMemcpyDeviceToHost);
+  unsigned err = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&err, derr.p, 4, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "laya_gated_attention");
+  if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");
+  for (size_t i = 0; i < no; i++) out[i] = half_bits(o16[i]);
   return 0;
 }
 

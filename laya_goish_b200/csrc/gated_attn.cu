@@ -6,137 +6,166 @@
 //          pos / theta^(2j/rot));
 //   out[i, h] = sigmoid(gate[i, h]) * softmax_j<=i(q_i . k_j / sqrt(hd)) v_j,
 //          GQA: query head h reads KV head h / (H / KV).
-// Two kernels: gattn_prep_kernel normalises and rotates every query and key
-// head once (one warp per head row); gattn_kernel runs one CTA of 8 warps
-// per (token, query head), each warp an online softmax over every 8th key
-// with the row's hd/32 dimensions per lane, merged in shared memory.  A
-// first, correct form on CUDA cores; the head-dim-256 tcgen05 version is the
-// fast one.
+// gattn_prep_kernel normalises and rotates every query and key head once
+// (one warp per head row) and writes the F16 operands of the tensor-core
+// attention: Q as [s][H * hd] rows, K and V as 64-token pages
+// [pages][KV][64][hd] (the paged layout of the decoder's KV cache, one
+// sequence, page p = tokens 64p .. 64p + 63, rows past the sequence zero),
+// plus the attention's work list.  The causal attention itself is the
+// tcgen05 kernel of attn_tc.cu (S and O in TMEM; head dim 256 keeps one Q
+// buffer and one O accumulator), which applies the sigmoid gate in its
+// epilogue and writes F16 rows, the operand of the output projection.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace laya {
 
-// One warp per (token, head) row of q (heads 0..H-1, read from qgate) or k
-// (heads H..H+KV-1): RMSNorm (offset 1) and the partial rotation, written to
-// qr [s][H][hd] / kr [s][KV][hd].
+namespace {
+
+constexpr int kUnitRows = 128;  // query rows per attention work item
+constexpr int kPage = 64;
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+struct GaLayout {
+  size_t q16, k16, v16, items, tables, total;
+};
+
+GaLayout ga_layout(int s, int H, int KV, int hd) {
+  const size_t pages = ((size_t)s + kPage - 1) / kPage, units = ((size_t)s + kUnitRows - 1) / kUnitRows;
+  GaLayout L;
+  L.q16 = 0;
+  L.k16 = L.q16 + align256((size_t)s * H * hd * 2);
+  L.v16 = L.k16 + align256(pages * kPage * KV * hd * 2);
+  L.items = L.v16 + align256(pages * kPage * KV * hd * 2);
+  L.tables = L.items + align256(units * sizeof(AttnItem));
+  L.total = L.tables + align256(pages * 4);
+  return L;
+}
+
+}  // namespace
+
+// One warp per (token, head) row of q (heads 0..H-1, read from qgate), of k
+// (heads H..H+KV-1) or of v (heads H+KV..H+2KV-1), for tokens 0 .. pages*64-1
+// (rows past s are zero).  q and k: RMSNorm (offset 1) and the partial
+// rotation in F32 in the warp's shared row, then rounded to F16.
 template <int HD>
-__global__ void gattn_prep_kernel(const float* __restrict__ qgate, const float* __restrict__ k,
-                                  const float* __restrict__ qn, const float* __restrict__ kn, int s, int H, int KV,
-                                  int rot, float theta, float* __restrict__ qr, float* __restrict__ kr) {
+__global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict__ qgate, const float* __restrict__ k,
+                                                         const float* __restrict__ v, const float* __restrict__ qn,
+                                                         const float* __restrict__ kn, int s, int H, int KV, int rot,
+                                                         float theta, half* __restrict__ q16, half* __restrict__ k16,
+                                                         half* __restrict__ v16, AttnItem* __restrict__ items,
+                                                         int* __restrict__ tables) {
   constexpr int PL = HD / 32;  // dimensions per lane: lane l holds l, l + 32, ...
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  const int rows = s * (H + KV);
-  if (gw >= rows) return;
-  const int i = gw / (H + KV), hh = gw % (H + KV);
+  __shared__ float rowbuf[8][HD];
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32, wib = threadIdx.x / 32;
+  const int pages = (s + kPage - 1) / kPage;
+  // the work list: item u = query rows 128u .. of the one sequence, all pages in order
+  const int gt = blockIdx.x * blockDim.x + threadIdx.x;
+  if (gt < (s + kUnitRows - 1) / kUnitRows) items[gt] = {gt * kUnitRows, min(kUnitRows, s - gt * kUnitRows), gt * kUnitRows, 0};
+  if (gt < pages) tables[gt] = gt;
+  const int per = H + 2 * KV;
+  if (gw >= pages * kPage * per) return;
+  const int i = gw / per, hh = gw % per;
+  const int pg = i / kPage, r = i % kPage;
+  if (hh >= H + KV) {  // v row
+    const int kh = hh - H - KV;
+    half* dst = v16 + (((size_t)pg * KV + kh) * kPage + r) * HD;
+#pragma unroll
+    for (int u = 0; u < PL; u++) dst[lane + 32 * u] = __float2half_rn(i < s ? v[((size_t)i * KV + kh) * HD + lane + 32 * u] : 0.f);
+    return;
+  }
   const bool isq = hh < H;
+  half* dst = isq ? q16 + ((size_t)i * H + hh) * HD : k16 + (((size_t)pg * KV + (hh - H)) * kPage + r) * HD;
+  if (i >= s) {
+    if (!isq)
+#pragma unroll
+      for (int u = 0; u < PL; u++) dst[lane + 32 * u] = __float2half_rn(0.f);
+    return;
+  }
   const float* src = isq ? qgate + ((size_t)i * H + hh) * 2 * HD : k + ((size_t)i * KV + (hh - H)) * HD;
   const float* wn = isq ? qn : kn;
-  float* dst = isq ? qr + ((size_t)i * H + hh) * HD : kr + ((size_t)i * KV + (hh - H)) * HD;
-  float v[PL];
+  float* row = rowbuf[wib];
+  float x[PL];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < PL; u++) {
-    v[u] = src[lane + 32 * u];
-    ss += v[u] * v[u];
+    x[u] = src[lane + 32 * u];
+    ss += x[u] * x[u];
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float scale = 1.f / sqrtf(ss / (float)HD + 1e-6f);
 #pragma unroll
-  for (int u = 0; u < PL; u++) v[u] = v[u] * scale * (1.f + wn[lane + 32 * u]);
-  // rotation: write the normalised row, then each lane rotates its pairs
-#pragma unroll
-  for (int u = 0; u < PL; u++) dst[lane + 32 * u] = v[u];
+  for (int u = 0; u < PL; u++) row[lane + 32 * u] = x[u] * scale * (1.f + wn[lane + 32 * u]);
   __syncwarp();
-  const int half = rot / 2;
-  for (int j = lane; j < half; j += 32) {
+  // rotate-half on the first rot dimensions (pairs j, j + rot/2)
+  const int half_rot = rot / 2;
+  for (int j = lane; j < half_rot; j += 32) {
     const float angle = (float)i / powf(theta, (float)(2 * j) / (float)rot);
     const float co = cosf(angle), si = sinf(angle);
-    const float a = dst[j], b = dst[j + half];
-    dst[j] = a * co - b * si;
-    dst[j + half] = b * co + a * si;
+    const float a = row[j], b = row[j + half_rot];
+    row[j] = a * co - b * si;
+    row[j + half_rot] = b * co + a * si;
   }
+  __syncwarp();
+#pragma unroll
+  for (int u = 0; u < PL; u++) dst[lane + 32 * u] = __float2half_rn(row[lane + 32 * u]);
 }
 
-template <int HD>
-__global__ void __launch_bounds__(256) gattn_kernel(const float* __restrict__ qr, const float* __restrict__ kr,
-                                                    const float* __restrict__ v, const float* __restrict__ qgate,
-                                                    int s, int H, int KV, float* __restrict__ out) {
-  constexpr int PL = HD / 32, NW = 8;
-  __shared__ float wm[NW], wl[NW];
-  __shared__ float wacc[NW][HD];
-  const int i = blockIdx.x / H, h = blockIdx.x % H;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int kh = h / (H / KV);
-  const float root = sqrtf((float)HD);
-  float q[PL];
-#pragma unroll
-  for (int u = 0; u < PL; u++) q[u] = qr[((size_t)i * H + h) * HD + lane + 32 * u];
-  float m = -INFINITY, l = 0.f, acc[PL];
-#pragma unroll
-  for (int u = 0; u < PL; u++) acc[u] = 0.f;
-  for (int j = warp; j <= i; j += NW) {
-    const float* kj = kr + ((size_t)j * KV + kh) * HD;
-    const float* vj = v + ((size_t)j * KV + kh) * HD;
-    float dot = 0.f;
-#pragma unroll
-    for (int u = 0; u < PL; u++) dot += q[u] * kj[lane + 32 * u];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const float sc = dot / root;
-    const float mn = fmaxf(m, sc);
-    const float corr = expf(m - mn), p = expf(sc - mn);  // corr = 0 on the first key (m = -inf)
-    l = l * corr + p;
-#pragma unroll
-    for (int u = 0; u < PL; u++) acc[u] = acc[u] * corr + p * vj[lane + 32 * u];
-    m = mn;
-  }
-  if (lane == 0) {
-    wm[warp] = m;
-    wl[warp] = l;
-  }
-#pragma unroll
-  for (int u = 0; u < PL; u++) wacc[warp][lane + 32 * u] = acc[u];
-  __syncthreads();
-  float M = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w]);
-  float L = 0.f;
-#pragma unroll
-  for (int w = 0; w < NW; w++)
-    if (wm[w] != -INFINITY) L += expf(wm[w] - M) * wl[w];
-  for (int c = threadIdx.x; c < HD; c += blockDim.x) {
-    float o = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; w++)
-      if (wm[w] != -INFINITY) o += expf(wm[w] - M) * wacc[w][c];
-    const float g = qgate[((size_t)i * H + h) * 2 * HD + HD + c];
-    out[((size_t)i * H + h) * HD + c] = o / L * (1.f / (1.f + expf(-g)));
-  }
-}
-
-template <int HD>
-static cudaError_t gattn_go(const float* qgate, const float* k, const float* v, const float* qn, const float* kn,
-                            int s, int H, int KV, int rot, float theta, float* qr, float* kr, float* out,
-                            cudaStream_t st) {
-  const int rows = s * (H + KV);
-  gattn_prep_kernel<HD><<<(rows + 7) / 8, 256, 0, st>>>(qgate, k, qn, kn, s, H, KV, rot, theta, qr, kr);
-  gattn_kernel<HD><<<s * H, 256, 0, st>>>(qr, kr, v, qgate, s, H, KV, out);
-  return cudaGetLastError();
-}
+size_t gated_attention_scratch(int s, int H, int KV, int hd) { return s > 0 ? ga_layout(s, H, KV, hd).total : 0; }
 
 cudaError_t gated_attention(const float* qgate, const float* k, const float* v, const float* qn, const float* kn,
-                            int s, int H, int KV, int hd, int rot, float theta, float* scratch, float* out,
-                            cudaStream_t st) {
+                            int s, int H, int KV, int hd, int rot, float theta, void* scratch, half* out16,
+                            unsigned* err, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
-  if (H < 1 || KV < 1 || H % KV || rot < 0 || rot > hd || rot % 2) return cudaErrorInvalidValue;
-  float* qr = scratch;
-  float* kr = scratch + (size_t)s * H * hd;
-  if (hd == 256) return gattn_go<256>(qgate, k, v, qn, kn, s, H, KV, rot, theta, qr, kr, out, st);
-  if (hd == 128) return gattn_go<128>(qgate, k, v, qn, kn, s, H, KV, rot, theta, qr, kr, out, st);
-  if (hd == 64) return gattn_go<64>(qgate, k, v, qn, kn, s, H, KV, rot, theta, qr, kr, out, st);
-  return cudaErrorInvalidValue;
+  if (H < 1 || KV < 1 || H % KV || rot < 0 || rot > hd || rot % 2 || !err) return cudaErrorInvalidValue;
+  if ((hd != 64 && hd != 128 && hd != 256) || (reinterpret_cast<uintptr_t>(scratch) & 255)) return cudaErrorInvalidValue;
+  const GaLayout L = ga_layout(s, H, KV, hd);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  half* q16 = reinterpret_cast<half*>(base + L.q16);
+  half* k16 = reinterpret_cast<half*>(base + L.k16);
+  half* v16 = reinterpret_cast<half*>(base + L.v16);
+  AttnItem* items = reinterpret_cast<AttnItem*>(base + L.items);
+  int* tables = reinterpret_cast<int*>(base + L.tables);
+  const int pages = (s + kPage - 1) / kPage;
+  const size_t rows = (size_t)pages * kPage * (H + 2 * KV);
+  const unsigned blocks = (unsigned)std::max<size_t>((rows + 7) / 8, ((size_t)pages + 255) / 256);
+#define LAYA_GA_PREP(HDV)                                                                                    \
+  gattn_prep_kernel<HDV><<<blocks, 256, 0, st>>>(qgate, k, v, qn, kn, s, H, KV, rot, theta, q16, k16, v16, \
+                                                  items, tables)
+  if (hd == 256)
+    LAYA_GA_PREP(256);
+  else if (hd == 128)
+    LAYA_GA_PREP(128);
+  else
+    LAYA_GA_PREP(64);
+#undef LAYA_GA_PREP
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  AttnParams p{};
+  p.q = q16;
+  p.ldq = H * hd;
+  p.o = out16;
+  p.ldo = H * hd;
+  p.kc = k16;
+  p.vc = v16;
+  p.tables = tables;
+  p.items = items;
+  p.n_items = (s + kUnitRows - 1) / kUnitRows;
+  p.H = H;
+  p.KV = KV;
+  p.hd = hd;
+  p.scale_log2 = (1.f / sqrtf((float)hd)) * 1.4426950408889634f;
+  p.q_rows = s;
+  p.kv_rows = pages * KV * kPage;
+  p.err = err;
+  p.gate = qgate + hd;  // the gate half of each head's [query hd | gate hd]
+  p.ldg = 2 * H * hd;
+  p.ghs = 2 * hd;
+  return attention_tc(p, st);
 }
 
 }  // namespace laya

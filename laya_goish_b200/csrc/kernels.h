@@ -34,6 +34,9 @@ struct AttnParams {
   int q_rows;     // rows of q / o
   int kv_rows;    // rows of kc / vc: pages * KV * 64
   unsigned* err;  // device error word (bounded waits)
+  // optional output gate (OpenThai): o *= sigmoid(gate[row * ldg + head * ghs + c])
+  const float* gate;
+  int ldg, ghs;
 };
 
 // tcgen05 attention (attn_tc.cu); cudaErrorNotSupported for head dims it
@@ -66,12 +69,15 @@ cudaError_t gated_delta(float* qkv, float* a, float* b, const float* dt, const f
 cudaError_t gated_delta_mixer(const float* raw, const float* z, float* a, float* b, const float* conv,
                               const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
                               float* qkv_scratch, float* out, cudaStream_t st);
-// Gated full attention after the projections (gated_attn.cu): qgate
-// [s][H][query hd | gate hd], k / v [s][KV][hd], q / k norm weights [hd] ->
-// out [s][H][hd]; scratch holds s * (H + KV) * hd floats.  hd 64/128/256.
+// OpenThai gated attention after the projections (gated_attn.cu): qgate
+// [s][H][query hd | gate hd], k / v [s][KV][hd] F32, q / k norm weights [hd]
+// -> out16 [s][H * hd] F16 (the output projection's operand), on the tcgen05
+// attention.  scratch: gated_attention_scratch(...) bytes, 256-byte aligned.
+// hd 64/128/256.
+size_t gated_attention_scratch(int s, int H, int KV, int hd);
 cudaError_t gated_attention(const float* qgate, const float* k, const float* v, const float* qn, const float* kn,
-                            int s, int H, int KV, int hd, int rot, float theta, float* scratch, float* out,
-                            cudaStream_t st);
+                            int s, int H, int KV, int hd, int rot, float theta, void* scratch, half* out16,
+                            unsigned* err, cudaStream_t st);
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,

@@ -48,7 +48,7 @@ struct laya_ot_model {
   unsigned* err = nullptr;
   std::vector<void*> allocs;
   // forward scratch, grown on demand and kept between passes
-  laya::DevBuf dids, dpos, x, h, big, k, v, att, att16, act, logits;
+  laya::DevBuf dids, dpos, x, h, big, k, v, att, att16, act, logits, gscr;
   std::mutex mu;
 };
 
@@ -284,7 +284,8 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
       (rc = h.ensure(std::max(S, (size_t)npos) * d * 2)) || (rc = big.ensure(bigf * 4)) || (rc = k.ensure(S * std::max(KV * hd, 2 * nh) * 4)) ||
       (rc = v.ensure(S * std::max(KV * hd, w) * 4)) || (rc = att.ensure(S * std::max(qd, w) * 4)) ||
       (rc = att16.ensure(S * std::max(qd, w) * 2)) || (rc = act.ensure(S * ffn * 2)) ||
-      (rc = logits.ensure((size_t)npos * c.slots * 4)))
+      (rc = logits.ensure((size_t)npos * c.slots * 4)) ||
+      (rc = m->gscr.ensure(std::max<size_t>(16, gated_attention_scratch(s, H, KV, hd)))))
     return rc;
   cudaStream_t st = m->st;
   LAYA_CK(cudaMemcpyAsync(dids.p, ids, S * 4, cudaMemcpyHostToDevice, st));
@@ -303,9 +304,8 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
           (rc = gemm(*m, EPI_F32, Hh, d, L.k, KV * hd, d, s, k.p, KV * hd, nullptr, nullptr)) ||
           (rc = gemm(*m, EPI_F32, Hh, d, L.v, KV * hd, d, s, v.p, KV * hd, nullptr, nullptr)))
         return rc;
-      LAYA_CK(gated_attention(qg, k.as<float>(), v.as<float>(), L.qn, L.kn, s, H, KV, hd, c.rot, c.theta, SCR,
-                              att.as<float>(), st));
-      LAYA_CK(f32_to_f16_pad(att.as<float>(), s, qd, qd, att16.as<half>(), st));
+      LAYA_CK(gated_attention(qg, k.as<float>(), v.as<float>(), L.qn, L.kn, s, H, KV, hd, c.rot, c.theta,
+                              m->gscr.p, att16.as<half>(), m->err, st));
       if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr))) return rc;
     } else {
       float* raw = P;
@@ -343,7 +343,8 @@ void laya_openthai_close(laya_ot_model* m) {
   cudaSetDevice(m->device);
   if (m->st) cudaStreamSynchronize(m->st);
   for (void* p : m->allocs) cudaFree(p);
-  for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->k, &m->v, &m->att, &m->att16, &m->act, &m->logits})
+  for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->k, &m->v, &m->att, &m->att16, &m->act, &m->logits,
+                     &m->gscr})
     b->release();
   if (m->st) cudaStreamDestroy(m->st);
   delete m;

@@ -56,7 +56,11 @@ def test_gated_attention_matches_oracle(s, H, KV, hd, rot):
     qn, kn = rng.normal(0, 0.1, hd), rng.normal(0, 0.1, hd)
     got = engine.gated_attention(qgate, k, v, qn, kn, H, KV, hd, rot, 1e7)
     want = oracle.ot_full_core(qgate, k, v, qn, kn, H, KV, hd, rot, 1e7)
-    assert np.allclose(got, want, atol=1e-4, rtol=1e-3), np.abs(got - want).max()
+    # tensor-core operands: q, k, v, the softmax weights and the output are
+    # rounded to F16 (relative 2^-11 each), scores and sums are F32
+    err = np.abs(got - want).max()
+    print(f"[parity] gated attention s={s} H={H}/{KV} hd={hd}: max |d| = {err:.2e}")
+    assert np.allclose(got, want, atol=5e-3, rtol=2e-2), err
 
 
 def test_gated_attention_rejects_bad_shapes():
