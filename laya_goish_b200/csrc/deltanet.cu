@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
   __shared__ __align__(16) float Ks[2][T][HK];
   __shared__ __align__(16) float Vs[2][T][CPB];
   __shared__ float Ds[2][T], Bs[2][T];
+  __shared__ float Op[T][CPB][G + 1];  // the chunk's per-lane output partials (padded row)
   const int tid = threadIdx.x, g = tid % G, cl = tid / G;
   const int h = blockIdx.x, c0 = blockIdx.y * CPB, w = nh * HK;
   const size_t C = (size_t)3 * w;
@@ -136,6 +137,10 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
     const int buf = ch & 1, i0 = ch * T;
     if (ch + 1 < nch) fetch(i0 + T);
     const int tn = min(T, s - i0);
+    // Per token the critical path is decay, the key sum k . S (four partial
+    // sums, then the 3-step shuffle tree over the column's lanes), delta and
+    // the rank-1 update; the output q . S of the token is this lane's
+    // partial only, parked in shared memory and reduced once per chunk.
     for (int t = 0; t < tn; t++) {
       const float dcy = Ds[buf][t], bt = Bs[buf][t], v = Vs[buf][t][cl];
       float kk[4 * M];
@@ -144,19 +149,17 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
         const float4 k4 = reinterpret_cast<const float4*>(&Ks[buf][t][0])[8 * m + g];
         kk[4 * m] = k4.x, kk[4 * m + 1] = k4.y, kk[4 * m + 2] = k4.z, kk[4 * m + 3] = k4.w;
       }
-      float d0 = 0.f, d1 = 0.f;
+      float dp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 4 * M; j += 2) {
+      for (int j = 0; j < 4 * M; j++) {
         S[j] *= dcy;
-        S[j + 1] *= dcy;
-        d0 += S[j] * kk[j];
-        d1 += S[j + 1] * kk[j + 1];
+        dp[j & 3] += S[j] * kk[j];
       }
-      float dsum = d0 + d1;
+      float dsum = (dp[0] + dp[1]) + (dp[2] + dp[3]);
 #pragma unroll
       for (int o = 1; o < G; o <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
       const float delta = (v - dsum) * bt;
-      float o0 = 0.f, o1 = 0.f;
+      float op[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int m = 0; m < M; m++) {
         const float4 q4 = reinterpret_cast<const float4*>(&Qs[buf][t][0])[8 * m + g];
@@ -164,13 +167,21 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
         S[4 * m + 1] += kk[4 * m + 1] * delta;
         S[4 * m + 2] += kk[4 * m + 2] * delta;
         S[4 * m + 3] += kk[4 * m + 3] * delta;
-        o0 += S[4 * m] * q4.x + S[4 * m + 2] * q4.z;
-        o1 += S[4 * m + 1] * q4.y + S[4 * m + 3] * q4.w;
+        op[0] += S[4 * m] * q4.x;
+        op[1] += S[4 * m + 1] * q4.y;
+        op[2] += S[4 * m + 2] * q4.z;
+        op[3] += S[4 * m + 3] * q4.w;
       }
-      float osum = o0 + o1;
+      Op[t][cl][g] = (op[0] + op[1]) + (op[2] + op[3]);
+    }
+    __syncthreads();
+    // the chunk's outputs: thread (token, column) sums its 8 lane partials
+    for (int e = tid; e < tn * CPB; e += THREADS) {
+      const int t = e / CPB, c = e % CPB;
+      float o = 0.f;
 #pragma unroll
-      for (int o = 1; o < G; o <<= 1) osum += __shfl_xor_sync(0xffffffffu, osum, o);
-      if (g == 0) out[(size_t)(i0 + t) * w + h * HK + c0 + cl] = osum;
+      for (int j = 0; j < G; j++) o += Op[t][c][j];
+      out[(size_t)(i0 + t) * w + h * HK + c0 + c] = o;
     }
     if (ch + 1 < nch) stage(buf ^ 1);
     __syncthreads();
