@@ -312,7 +312,8 @@ int laya_gated_delta(int device, const float* qkv, const float* a, const float* 
   if (e == cudaSuccess) e = cudaMemcpy(dpar, dt, (size_t)nh * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(dpar + nh, alog, (size_t)nh * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
-    e = gated_delta(dq.as<float>(), da.as<float>(), db.as<float>(), dpar, dpar + nh, s, nh, hk, dout.as<float>(), 0);
+    e = gated_delta(dq.as<float>(), da.as<float>(), db.as<float>(), nh, dpar, dpar + nh, s, nh, hk, da.as<float>(),
+                    db.as<float>(), dout.as<float>(), 0);
   if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, no * 4, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "laya_gated_delta");
   return 0;
@@ -331,7 +332,7 @@ int laya_gated_delta_mixer(int device, const float* raw, const float* z, const f
   int rc;
   if ((rc = draw.ensure(nr * 4)) || (rc = dz.ensure(nz * 4)) || (rc = da.ensure(nab * 4)) ||
       (rc = db.ensure(nab * 4)) || (rc = dconv.ensure(3 * w * 4 * 4)) || (rc = dpar.ensure(((size_t)2 * nh + hk) * 4)) ||
-      (rc = dsc.ensure(nr * 4)) || (rc = dout.ensure(nz * 4)))
+      (rc = dsc.ensure(gated_delta_mixer_scratch(s, nh, hk))) || (rc = dout.ensure(nz * 4)))
     return rc;
   float* p = dpar.as<float>();
   cudaError_t e = cudaMemcpy(draw.p, raw, nr * 4, cudaMemcpyHostToDevice);
@@ -343,8 +344,8 @@ int laya_gated_delta_mixer(int device, const float* raw, const float* z, const f
   if (e == cudaSuccess) e = cudaMemcpy(p + nh, alog, (size_t)nh * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(p + 2 * nh, normw, (size_t)hk * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
-    e = gated_delta_mixer(draw.as<float>(), dz.as<float>(), da.as<float>(), db.as<float>(), dconv.as<float>(), p,
-                          p + nh, p + 2 * nh, s, nh, hk, dsc.as<float>(), dout.as<float>(), 0);
+    e = gated_delta_mixer(draw.as<float>(), (int)(3 * w), dz.as<float>(), (int)w, da.as<float>(), db.as<float>(), nh,
+                          dconv.as<float>(), p, p + nh, p + 2 * nh, s, nh, hk, dsc.as<float>(), dout.as<float>(), 0);
   if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, nz * 4, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "laya_gated_delta_mixer");
   return 0;
@@ -373,8 +374,8 @@ int laya_gated_attention(int device, const float* qgate, const float* k, const f
   if (e == cudaSuccess) e = cudaMemcpy(dnw + hd, kn, (size_t)hd * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(derr.p, 0, 16);
   if (e == cudaSuccess)
-    e = gated_attention(dq.as<float>(), dk.as<float>(), dv.as<float>(), dnw, dnw + hd, s, H, KV, hd, rot, theta,
-                        dsc.p, dout.as<half>(), derr.as<unsigned>(), 0);
+    e = gated_attention(dq.as<float>(), 2 * H * hd, dk.as<float>(), dv.as<float>(), KV * hd, dnw, dnw + hd, s, H, KV,
+                        hd, rot, theta, dsc.p, dout.as<half>(), derr.as<unsigned>(), 0);
   std::vector<uint16_t> o16(no);
   if (e == cudaSuccess) e = cudaMemcpy(o16.data(), dout.p, no * 2, cudaMemcpyDeviceToHost);
   unsigned err = 0;

@@ -29,10 +29,14 @@ constexpr int G = 8;    // lanes per column (key groups)
 constexpr int THREADS = CPB * G;
 }  // namespace delta
 
+// a / b: the gate projections of token i, head h at a[i * ldab + h] and
+// b[i * ldab + h]; decay / beta go to dec / beta [s][nh] (may alias a / b
+// when ldab == nh).
 template <int HK>
-__global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv, float* __restrict__ a,
-                                                         float* __restrict__ b, const float* __restrict__ dt,
-                                                         const float* __restrict__ alog, int s, int nh) {
+__global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv, const float* a, const float* b,
+                                                         int ldab, const float* __restrict__ dt,
+                                                         const float* __restrict__ alog, int s, int nh, float* dec,
+                                                         float* beta) {
   constexpr int PL = HK / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (gw >= s * nh) return;
@@ -60,11 +64,12 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv
     k[lane + 32 * u] = kv[u] * ks;
   }
   if (lane == 0) {
-    const size_t e = (size_t)i * nh + h;
-    const float x = a[e] + dt[h];
+    const size_t e = (size_t)i * nh + h, src = (size_t)i * ldab + h;
+    const float x = a[src] + dt[h];
+    const float bv = b[src];
     const float sp = x > 20.f ? x : log1pf(expf(x));
-    a[e] = expf(-expf(alog[h]) * sp);
-    b[e] = 1.f / (1.f + expf(-b[e]));
+    dec[e] = expf(-expf(alog[h]) * sp);
+    beta[e] = 1.f / (1.f + expf(-bv));
   }
 }
 
@@ -191,28 +196,28 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
 // Causal depthwise convolution of width 4 over the token axis, then SiLU
 // (model.rs:309-320): out[i][c] = silu(sum_j raw[i + j - 3][c] conv[c][j]),
 // terms before token 0 left out, summed in j order.
-__global__ void conv_silu_kernel(const float* __restrict__ raw, const float* __restrict__ conv, int s, int C,
-                                 float* __restrict__ out) {
+__global__ void conv_silu_kernel(const float* __restrict__ raw, int ldraw, const float* __restrict__ conv, int s,
+                                 int C, float* __restrict__ out) {
   const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= (size_t)s * C) return;
   const int i = (int)(e / C), c = (int)(e % C);
   float acc = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; j++)
-    if (i + j >= 3) acc += raw[(size_t)(i + j - 3) * C + c] * conv[(size_t)c * 4 + j];
+    if (i + j >= 3) acc += raw[(size_t)(i + j - 3) * ldraw + c] * conv[(size_t)c * 4 + j];
   out[e] = acc / (1.f + expf(-acc));
 }
 
 // Per-head RMSNorm (weight offset 0, eps 1e-6) of the recurrence output,
 // then x SiLU(z) (model.rs:356-360); one warp per (token, head) row.
 template <int HK>
-__global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict__ z, const float* __restrict__ w,
-                                 int rows) {
+__global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict__ z, int ldz, int nh,
+                                 const float* __restrict__ w, int rows) {
   constexpr int PL = HK / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (gw >= rows) return;
   float* r = o + (size_t)gw * HK;
-  const float* zr = z + (size_t)gw * HK;
+  const float* zr = z + (size_t)(gw / nh) * ldz + (size_t)(gw % nh) * HK;
   float v[PL], ss = 0.f;
 #pragma unroll
   for (int u = 0; u < PL; u++) {
@@ -229,35 +234,40 @@ __global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict_
   }
 }
 
-cudaError_t gated_delta_mixer(const float* raw, const float* z, float* a, float* b, const float* conv,
-                              const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
-                              float* qkv_scratch, float* out, cudaStream_t st) {
+cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int ldz, const float* a, const float* b,
+                              int ldab, const float* conv, const float* dt, const float* alog, const float* normw,
+                              int s, int nh, int hk, float* scratch, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
   if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
   const size_t C = (size_t)3 * nh * hk, n = (size_t)s * C;
-  conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, conv, s, (int)C, qkv_scratch);
-  cudaError_t e = gated_delta(qkv_scratch, a, b, dt, alog, s, nh, hk, out, st);
+  float* qkv = scratch;
+  float* dec = scratch + n;
+  float* beta = dec + (size_t)s * nh;
+  conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, ldraw, conv, s, (int)C, qkv);
+  cudaError_t e = gated_delta(qkv, a, b, ldab, dt, alog, s, nh, hk, dec, beta, out, st);
   if (e != cudaSuccess) return e;
   const int rows = s * nh;
   if (hk == 128)
-    norm_gate_kernel<128><<<(rows + 7) / 8, 256, 0, st>>>(out, z, normw, rows);
+    norm_gate_kernel<128><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows);
   else
-    norm_gate_kernel<64><<<(rows + 7) / 8, 256, 0, st>>>(out, z, normw, rows);
+    norm_gate_kernel<64><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows);
   return cudaGetLastError();
 }
 
-cudaError_t gated_delta(float* qkv, float* a, float* b, const float* dt, const float* alog, int s, int nh, int hk,
-                        float* out, cudaStream_t st) {
+size_t gated_delta_mixer_scratch(int s, int nh, int hk) { return (size_t)s * (3 * nh * hk + 2 * nh) * 4; }
+
+cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, const float* dt, const float* alog,
+                        int s, int nh, int hk, float* dec, float* beta, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
   if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
   const unsigned prep_blocks = (unsigned)(((size_t)s * nh + 7) / 8);
   const dim3 grid(nh, hk / delta::CPB);
   if (hk == 128) {
-    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, dt, alog, s, nh);
-    delta_scan_kernel<128><<<grid, delta::THREADS, 0, st>>>(qkv, a, b, s, nh, out);
+    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta);
+    delta_scan_kernel<128><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, s, nh, out);
   } else {
-    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, dt, alog, s, nh);
-    delta_scan_kernel<64><<<grid, delta::THREADS, 0, st>>>(qkv, a, b, s, nh, out);
+    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta);
+    delta_scan_kernel<64><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, s, nh, out);
   }
   return cudaGetLastError();
 }

@@ -52,8 +52,9 @@ GaLayout ga_layout(int s, int H, int KV, int hd) {
 // (rows past s are zero).  q and k: RMSNorm (offset 1) and the partial
 // rotation in F32 in the warp's shared row, then rounded to F16.
 template <int HD>
-__global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict__ qgate, const float* __restrict__ k,
-                                                         const float* __restrict__ v, const float* __restrict__ qn,
+__global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict__ qgate, int ldqg,
+                                                         const float* __restrict__ k, const float* __restrict__ v,
+                                                         int ldkv, const float* __restrict__ qn,
                                                          const float* __restrict__ kn, int s, int H, int KV, int rot,
                                                          float theta, half* __restrict__ q16, half* __restrict__ k16,
                                                          half* __restrict__ v16, AttnItem* __restrict__ items,
@@ -74,7 +75,8 @@ __global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict
     const int kh = hh - H - KV;
     half* dst = v16 + (((size_t)pg * KV + kh) * kPage + r) * HD;
 #pragma unroll
-    for (int u = 0; u < PL; u++) dst[lane + 32 * u] = __float2half_rn(i < s ? v[((size_t)i * KV + kh) * HD + lane + 32 * u] : 0.f);
+    for (int u = 0; u < PL; u++)
+      dst[lane + 32 * u] = __float2half_rn(i < s ? v[(size_t)i * ldkv + (size_t)kh * HD + lane + 32 * u] : 0.f);
     return;
   }
   const bool isq = hh < H;
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict
       for (int u = 0; u < PL; u++) dst[lane + 32 * u] = __float2half_rn(0.f);
     return;
   }
-  const float* src = isq ? qgate + ((size_t)i * H + hh) * 2 * HD : k + ((size_t)i * KV + (hh - H)) * HD;
+  const float* src = isq ? qgate + (size_t)i * ldqg + (size_t)hh * 2 * HD : k + (size_t)i * ldkv + (size_t)(hh - H) * HD;
   const float* wn = isq ? qn : kn;
   float* row = rowbuf[wib];
   float x[PL];
@@ -117,11 +119,12 @@ __global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict
 
 size_t gated_attention_scratch(int s, int H, int KV, int hd) { return s > 0 ? ga_layout(s, H, KV, hd).total : 0; }
 
-cudaError_t gated_attention(const float* qgate, const float* k, const float* v, const float* qn, const float* kn,
-                            int s, int H, int KV, int hd, int rot, float theta, void* scratch, half* out16,
-                            unsigned* err, cudaStream_t st) {
+cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const float* v, int ldkv, const float* qn,
+                            const float* kn, int s, int H, int KV, int hd, int rot, float theta, void* scratch,
+                            half* out16, unsigned* err, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
-  if (H < 1 || KV < 1 || H % KV || rot < 0 || rot > hd || rot % 2 || !err) return cudaErrorInvalidValue;
+  if (H < 1 || KV < 1 || H % KV || rot < 0 || rot > hd || rot % 2 || !err || ldqg < 2 * H * hd || ldkv < KV * hd)
+    return cudaErrorInvalidValue;
   if ((hd != 64 && hd != 128 && hd != 256) || (reinterpret_cast<uintptr_t>(scratch) & 255)) return cudaErrorInvalidValue;
   const GaLayout L = ga_layout(s, H, KV, hd);
   uint8_t* base = static_cast<uint8_t*>(scratch);
@@ -134,8 +137,8 @@ cudaError_t gated_attention(const float* qgate, const float* k, const float* v, 
   const size_t rows = (size_t)pages * kPage * (H + 2 * KV);
   const unsigned blocks = (unsigned)std::max<size_t>((rows + 7) / 8, ((size_t)pages + 255) / 256);
 #define LAYA_GA_PREP(HDV)                                                                                    \
-  gattn_prep_kernel<HDV><<<blocks, 256, 0, st>>>(qgate, k, v, qn, kn, s, H, KV, rot, theta, q16, k16, v16, \
-                                                  items, tables)
+  gattn_prep_kernel<HDV><<<blocks, 256, 0, st>>>(qgate, ldqg, k, v, ldkv, qn, kn, s, H, KV, rot, theta, q16, \
+                                                  k16, v16, items, tables)
   if (hd == 256)
     LAYA_GA_PREP(256);
   else if (hd == 128)
@@ -163,7 +166,7 @@ cudaError_t gated_attention(const float* qgate, const float* k, const float* v, 
   p.kv_rows = pages * KV * kPage;
   p.err = err;
   p.gate = qgate + hd;  // the gate half of each head's [query hd | gate hd]
-  p.ldg = 2 * H * hd;
+  p.ldg = ldqg;
   p.ghs = 2 * hd;
   return attention_tc(p, st);
 }

@@ -53,31 +53,32 @@ cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cu
 // the bulk-copy kernel, whose bounded wait reports there.
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
                     float* out32, cudaStream_t st, bool pdl = false, unsigned* err = nullptr);
+// OpenThai's gated DeltaNet recurrence (deltanet.cu), one sequence: qkv
+// [s][3 nh hk] after the convolution (q / k normalised in place); the gate
+// projections of token i, head h at a / b[i * ldab + h]; decay / beta are
+// written to dec / beta [s][nh] (they may alias a / b when ldab == nh);
+// out [s][nh hk] before the output norm.
+cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, const float* dt, const float* alog,
+                        int s, int nh, int hk, float* dec, float* beta, float* out, cudaStream_t st);
+// The whole mixer after its projections: raw rows (stride ldraw) [3 nh hk],
+// z rows (stride ldz) [nh hk], a / b as above; scratch holds
+// gated_delta_mixer_scratch(s, nh, hk) bytes.
+size_t gated_delta_mixer_scratch(int s, int nh, int hk);
+cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int ldz, const float* a, const float* b,
+                              int ldab, const float* conv, const float* dt, const float* alog, const float* normw,
+                              int s, int nh, int hk, float* scratch, float* out, cudaStream_t st);
+// OpenThai gated attention after the projections (gated_attn.cu): rows of
+// qgate [H][query hd | gate hd] (row stride ldqg), of k and v [KV][hd] (row
+// stride ldkv), F32; q / k norm weights [hd] -> out16 [s][H * hd] F16 (the
+// output projection's operand), on the tcgen05 attention.  scratch:
+// gated_attention_scratch(...) bytes, 256-byte aligned.  hd 64/128/256.
+size_t gated_attention_scratch(int s, int H, int KV, int hd);
+cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const float* v, int ldkv, const float* qn,
+                            const float* kn, int s, int H, int KV, int hd, int rot, float theta, void* scratch,
+                            half* out16, unsigned* err, cudaStream_t st);
 // rmsnorm of x + part[0] + ... + part[nsplit-1] (K-split partial sums of the
 // GEMM that wrote x, planes split_stride floats apart); without a row gather
 // (rows null) the merged rows are also written back to x.
-// Gated DeltaNet recurrence (deltanet.cu): qkv [s][3 nh hk] after the
-// convolution and SiLU, a / b [s][nh], dt / A_log [nh] -> out [s][nh hk]
-// (hk 64 or 128).  All device pointers.  Works in place: q and k of qkv are
-// overwritten with their normalised values, a with the decay and b with beta.
-cudaError_t gated_delta(float* qkv, float* a, float* b, const float* dt, const float* alog, int s, int nh, int hk,
-                        float* out, cudaStream_t st);
-// The DeltaNet mixer after its projections (deltanet.cu): raw [s][3 nh hk]
-// from in_proj_qkv, z [s][nh hk], a / b [s][nh] (overwritten, as above),
-// conv [3 nh hk][4], dt / A_log [nh], norm weight [hk] -> out [s][nh hk]
-// before out_proj; qkv_scratch holds s * 3 * nh * hk floats.
-cudaError_t gated_delta_mixer(const float* raw, const float* z, float* a, float* b, const float* conv,
-                              const float* dt, const float* alog, const float* normw, int s, int nh, int hk,
-                              float* qkv_scratch, float* out, cudaStream_t st);
-// OpenThai gated attention after the projections (gated_attn.cu): qgate
-// [s][H][query hd | gate hd], k / v [s][KV][hd] F32, q / k norm weights [hd]
-// -> out16 [s][H * hd] F16 (the output projection's operand), on the tcgen05
-// attention.  scratch: gated_attention_scratch(...) bytes, 256-byte aligned.
-// hd 64/128/256.
-size_t gated_attention_scratch(int s, int H, int KV, int hd);
-cudaError_t gated_attention(const float* qgate, const float* k, const float* v, const float* qn, const float* kn,
-                            int s, int H, int KV, int hd, int rot, float theta, void* scratch, half* out16,
-                            unsigned* err, cudaStream_t st);
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,

@@ -28,9 +28,9 @@ struct OtLayer {
   bool full = false;
   const float *n1 = nullptr, *n2 = nullptr;  // 1 + w
   const half *gu = nullptr, *down = nullptr;
-  const half *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+  const half *q = nullptr, *o = nullptr;  // q: [q | gate] rows, then k, then v rows, stacked
   const float *qn = nullptr, *kn = nullptr;
-  const half *qkv = nullptr, *z = nullptr, *a = nullptr, *b = nullptr, *out = nullptr;
+  const half *qkv = nullptr, *out = nullptr;  // qkv: in_proj_qkv, z, a, b rows, stacked
   const float *conv = nullptr, *dt = nullptr, *alog = nullptr, *normw = nullptr;
 };
 
@@ -48,7 +48,7 @@ struct laya_ot_model {
   unsigned* err = nullptr;
   std::vector<void*> allocs;
   // forward scratch, grown on demand and kept between passes
-  laya::DevBuf dids, dpos, x, h, big, k, v, att, att16, act, logits, gscr;
+  laya::DevBuf dids, dpos, x, h, big, att, att16, act, logits, gscr;
   std::mutex mu;
 };
 
@@ -108,6 +108,31 @@ int upload_mat(Model& m, const Gguf& g, const std::string& name, int rows, int c
   return 0;
 }
 
+// Several matrices [rows_i][cols] stacked row-wise into one F16 operand, so
+// the projections that read the same normed rows run as one GEMM.
+int upload_stack(Model& m, const Gguf& g, const std::vector<std::pair<std::string, int>>& parts, int cols,
+                 const half** out) {
+  size_t total = 0;
+  for (const auto& pr : parts) total += (size_t)pr.second * cols;
+  std::vector<half> h(total);
+  size_t at = 0;
+  for (const auto& pr : parts) {
+    const TensorInfo* t = g.tensor(pr.first);
+    if (!t) return fail(LAYA_E_FORMAT, "missing tensor " + pr.first);
+    if (t->dims.size() != 2 || t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)pr.second)
+      return fail(LAYA_E_FORMAT, pr.first + ": unexpected matrix shape");
+    std::vector<float> v;
+    if (int rc = host_f32(g, pr.first, (size_t)pr.second * cols, &v)) return rc;
+    for (size_t i = 0; i < v.size(); i++) h[at + i] = __float2half_rn(v[i]);
+    at += v.size();
+  }
+  void* p;
+  if (int rc = dalloc(m, h.size() * 2, &p)) return rc;
+  LAYA_CK(cudaMemcpy(p, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+  *out = static_cast<const half*>(p);
+  return 0;
+}
+
 // gate and up [ffn][d] interleaved per 128 rows into one [2 ffn][d] operand
 int upload_gate_up(Model& m, const Gguf& g, const std::string& p, int ffn, int d, const half** out) {
   std::vector<float> gt, up;
@@ -156,18 +181,18 @@ int load(Model& m, const Gguf& g, const uint8_t* layer_full) {
         (rc = upload_mat(m, g, p + ".mlp.down_proj.weight", d, c.ffn, &L.down)))
       return rc;
     if (L.full) {
-      if ((rc = upload_mat(m, g, p + ".self_attn.q_proj.weight", 2 * H * hd, d, &L.q)) ||
-          (rc = upload_mat(m, g, p + ".self_attn.k_proj.weight", KV * hd, d, &L.k)) ||
-          (rc = upload_mat(m, g, p + ".self_attn.v_proj.weight", KV * hd, d, &L.v)) ||
+      // q | k | v stacked: one projection GEMM
+      if ((rc = upload_stack(m, g, {{p + ".self_attn.q_proj.weight", 2 * H * hd}, {p + ".self_attn.k_proj.weight", KV * hd},
+                                    {p + ".self_attn.v_proj.weight", KV * hd}}, d, &L.q)) ||
           (rc = upload_mat(m, g, p + ".self_attn.o_proj.weight", d, H * hd, &L.o)) ||
           (rc = upload_vec(m, g, p + ".self_attn.q_norm.weight", hd, 0.f, &L.qn)) ||
           (rc = upload_vec(m, g, p + ".self_attn.k_norm.weight", hd, 0.f, &L.kn)))
         return rc;
     } else {
-      if ((rc = upload_mat(m, g, p + ".linear_attn.in_proj_qkv.weight", 3 * w, d, &L.qkv)) ||
-          (rc = upload_mat(m, g, p + ".linear_attn.in_proj_z.weight", w, d, &L.z)) ||
-          (rc = upload_mat(m, g, p + ".linear_attn.in_proj_a.weight", nh, d, &L.a)) ||
-          (rc = upload_mat(m, g, p + ".linear_attn.in_proj_b.weight", nh, d, &L.b)) ||
+      // qkv | z | a | b stacked: one projection GEMM
+      if ((rc = upload_stack(m, g, {{p + ".linear_attn.in_proj_qkv.weight", 3 * w}, {p + ".linear_attn.in_proj_z.weight", w},
+                                    {p + ".linear_attn.in_proj_a.weight", nh}, {p + ".linear_attn.in_proj_b.weight", nh}},
+                             d, &L.qkv)) ||
           (rc = upload_mat(m, g, p + ".linear_attn.out_proj.weight", d, w, &L.out)) ||
           (rc = upload_vec(m, g, p + ".linear_attn.conv1d.weight", (size_t)3 * w * 4, 0.f, &L.conv)) ||
           (rc = upload_vec(m, g, p + ".linear_attn.dt_bias", nh, 0.f, &L.dt)) ||
@@ -275,14 +300,17 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
   const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
   const int w = nh * hk, qd = H * hd, ffn = c.ffn;
   const size_t S = (size_t)s;
-  DevBuf &dids = m->dids, &dpos = m->dpos, &x = m->x, &h = m->h, &big = m->big, &k = m->k, &v = m->v,
+  DevBuf &dids = m->dids, &dpos = m->dpos, &x = m->x, &h = m->h, &big = m->big,
          &att = m->att, &att16 = m->att16, &act = m->act, &logits = m->logits;
-  // big: the largest projection output (2 qd, 3w) plus the mixers' scratch
-  const size_t bigf = S * (size_t)std::max(2 * qd, 3 * w) + S * (size_t)std::max(qd + KV * hd, 3 * w) + S * 2 * w;
+  // big: the stacked projection output of either layer kind, then the
+  // DeltaNet mixer's scratch
+  const int nfull = 2 * qd + 2 * KV * hd, ndelta = 4 * w + 2 * nh;
+  const size_t pw = ((size_t)std::max(nfull, ndelta) + 63) / 64 * 64;
+  const size_t bigf = S * pw + gated_delta_mixer_scratch(s, nh, hk) / 4 + 64;
   int rc;
   if ((rc = dids.ensure(S * 4)) || (rc = dpos.ensure((size_t)npos * 4)) || (rc = x.ensure(S * d * 4)) ||
-      (rc = h.ensure(std::max(S, (size_t)npos) * d * 2)) || (rc = big.ensure(bigf * 4)) || (rc = k.ensure(S * std::max(KV * hd, 2 * nh) * 4)) ||
-      (rc = v.ensure(S * std::max(KV * hd, w) * 4)) || (rc = att.ensure(S * std::max(qd, w) * 4)) ||
+      (rc = h.ensure(std::max(S, (size_t)npos) * d * 2)) || (rc = big.ensure(bigf * 4)) ||
+      (rc = att.ensure(S * std::max(qd, w) * 4)) ||
       (rc = att16.ensure(S * std::max(qd, w) * 2)) || (rc = act.ensure(S * ffn * 2)) ||
       (rc = logits.ensure((size_t)npos * c.slots * 4)) ||
       (rc = m->gscr.ensure(std::max<size_t>(16, gated_attention_scratch(s, H, KV, hd)))))
@@ -292,32 +320,23 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
   LAYA_CK(cudaMemcpyAsync(dpos.p, positions, (size_t)npos * 4, cudaMemcpyHostToDevice, st));
   float* X = x.as<float>();
   half* Hh = h.as<half>();
-  float* P = big.as<float>();                                   // projection outputs
-  float* SCR = P + S * (size_t)std::max(2 * qd, 3 * w);        // mixer scratch
+  float* P = big.as<float>();  // stacked projection outputs, rows of nfull / ndelta
+  float* SCR = P + S * pw;     // DeltaNet mixer scratch
   LAYA_CK(rows_f32(m->embd, dids.as<int>(), s, X, st));
   for (int l = 0; l < c.n_layers; l++) {
     const OtLayer& L = m->layers[l];
     LAYA_CK(rmsnorm(X, nullptr, s, L.n1, d, c.eps, Hh, nullptr, st));
     if (L.full) {
-      float* qg = P;
-      if ((rc = gemm(*m, EPI_F32, Hh, d, L.q, 2 * qd, d, s, qg, 2 * qd, nullptr, nullptr)) ||
-          (rc = gemm(*m, EPI_F32, Hh, d, L.k, KV * hd, d, s, k.p, KV * hd, nullptr, nullptr)) ||
-          (rc = gemm(*m, EPI_F32, Hh, d, L.v, KV * hd, d, s, v.p, KV * hd, nullptr, nullptr)))
-        return rc;
-      LAYA_CK(gated_attention(qg, k.as<float>(), v.as<float>(), L.qn, L.kn, s, H, KV, hd, c.rot, c.theta,
-                              m->gscr.p, att16.as<half>(), m->err, st));
+      // one GEMM: rows [q | gate per head] (2 qd), k (KV hd), v (KV hd)
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.q, nfull, d, s, P, nfull, nullptr, nullptr))) return rc;
+      LAYA_CK(gated_attention(P, nfull, P + 2 * qd, P + 2 * qd + KV * hd, nfull, L.qn, L.kn, s, H, KV, hd, c.rot,
+                              c.theta, m->gscr.p, att16.as<half>(), m->err, st));
       if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr))) return rc;
     } else {
-      float* raw = P;
-      float* zz = v.as<float>();
-      float* ab = k.as<float>();  // a then b, [s][nh] each
-      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, 3 * w, d, s, raw, 3 * w, nullptr, nullptr)) ||
-          (rc = gemm(*m, EPI_F32, Hh, d, L.z, w, d, s, zz, w, nullptr, nullptr)) ||
-          (rc = gemm(*m, EPI_F32, Hh, d, L.a, nh, d, s, ab, nh, nullptr, nullptr)) ||
-          (rc = gemm(*m, EPI_F32, Hh, d, L.b, nh, d, s, ab + S * nh, nh, nullptr, nullptr)))
-        return rc;
-      LAYA_CK(gated_delta_mixer(raw, zz, ab, ab + S * nh, L.conv, L.dt, L.alog, L.normw, s, nh, hk, SCR,
-                                att.as<float>(), st));
+      // one GEMM: rows in_proj_qkv (3w), z (w), a (nh), b (nh)
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, ndelta, d, s, P, ndelta, nullptr, nullptr))) return rc;
+      LAYA_CK(gated_delta_mixer(P, ndelta, P + 3 * w, ndelta, P + 4 * w, P + 4 * w + nh, ndelta, L.conv, L.dt, L.alog,
+                                L.normw, s, nh, hk, SCR, att.as<float>(), st));
       LAYA_CK(f32_to_f16_pad(att.as<float>(), s, w, w, att16.as<half>(), st));
       if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), w, L.out, d, w, s, nullptr, d, X, nullptr))) return rc;
     }
@@ -343,7 +362,7 @@ void laya_openthai_close(laya_ot_model* m) {
   cudaSetDevice(m->device);
   if (m->st) cudaStreamSynchronize(m->st);
   for (void* p : m->allocs) cudaFree(p);
-  for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->k, &m->v, &m->att, &m->att16, &m->act, &m->logits,
+  for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->att, &m->att16, &m->act, &m->logits,
                      &m->gscr})
     b->release();
   if (m->st) cudaStreamDestroy(m->st);
