@@ -299,11 +299,11 @@ int laya_gated_delta(int device, const float* qkv, const float* a, const float* 
   if (s == 0) return 0;
   LAYA_CK(cudaSetDevice(device));
   const size_t w = (size_t)nh * hk, nq = (size_t)s * 3 * w, nab = (size_t)s * nh, no = (size_t)s * w;
-  DevBuf dq, da, db, dp, dch, dout;
-  ReleaseOnExit guard{{&dq, &da, &db, &dp, &dch, &dout}};
+  DevBuf dq, da, db, dp, dkq, dout;
+  ReleaseOnExit guard{{&dq, &da, &db, &dp, &dkq, &dout}};
   int rc;
   if ((rc = dq.ensure(nq * 4)) || (rc = da.ensure(nab * 4)) || (rc = db.ensure(nab * 4)) ||
-      (rc = dp.ensure((size_t)2 * nh * 4)) || (rc = dch.ensure(gated_delta_scratch(s, nh, hk))) ||
+      (rc = dp.ensure((size_t)2 * nh * 4)) || (rc = dkq.ensure(gated_delta_scratch(s, nh))) ||
       (rc = dout.ensure(no * 4)))
     return rc;
   float* dpar = dp.as<float>();
@@ -314,7 +314,7 @@ int laya_gated_delta(int device, const float* qkv, const float* a, const float* 
   if (e == cudaSuccess) e = cudaMemcpy(dpar + nh, alog, (size_t)nh * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = gated_delta(dq.as<float>(), da.as<float>(), db.as<float>(), nh, dpar, dpar + nh, s, nh, hk, da.as<float>(),
-                    db.as<float>(), dch.as<float>(), dout.as<float>(), 0);
+                    db.as<float>(), dkq.as<float>(), dout.as<float>(), 0);
   if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, no * 4, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "laya_gated_delta");
   return 0;

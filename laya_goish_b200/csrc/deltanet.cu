@@ -7,45 +7,44 @@
 //
 // with a per-head state S [key hk][value hk] starting at zero.
 //
-// Chunked form (chunks of C = 64 tokens, per head; g_t = the running sum of
-// log decays inside the chunk, gamma_t = exp(g_t)): with S0 the state at the
-// chunk start,
-//   S_t   = gamma_t S0 + sum_{i<=t} (gamma_t / gamma_i) k_i delta_i^T
-//   Delta = U0 - W S0,   W = T diag(beta gamma) K,  U0 = T diag(beta) V,
-//           T = (I + A)^-1, A_ti = beta_t (gamma_t / gamma_i) k_t . k_i (i < t)
-//   O     = (Gamma Q) S0 + Pm Delta,   Pm_ti = (gamma_t / gamma_i) q_t . k_i (i <= t)
-//   S_C   = gamma_C S0 + Kd^T Delta,   Kd_i = (gamma_C / gamma_i) k_i
-// which is the token recurrence above, reassociated (every ratio
-// gamma_t / gamma_i <= 1 is formed from the log sums, so nothing overflows).
-//
-// Three kernels.  delta_prep_kernel does the per-token work in parallel over
-// (token, head): the two L2 norms (in place in qkv), the log decay and beta.
-// delta_chunk_kernel builds every chunk's W, U0, Gamma Q, Kd and Pm in
-// parallel over (chunk, head), with T from a forward substitution.
-// delta_state_kernel then walks the chunks in order for one head and a block
-// of 16 value columns (the columns of S are independent), the state held in
-// registers, key-group partial sums reduced through shared memory.
-#include <atomic>
-
+// Three kernels.  delta_prep_kernel does the per-token work that does not
+// depend on S in parallel over (token, head): the two L2 norms (in place in
+// qkv) and decay / beta.  delta_quad_kernel forms, per group of four tokens
+// and head, the key-key products k_m . k_i (i < m) and query-key products
+// q_m . k_i (i <= m).  delta_scan_kernel then runs the sequential part four
+// tokens at a time: with S0 the state before the group and a_m the decays,
+//   r_m = k_m . S0,  p_m = q_m . S0                 (eight independent sums)
+//   delta_m = beta_m (v_m - A_m r_m - sum_{i<m} a_{i+1..m} (k_m . k_i) delta_i)
+//   o_m = A_m p_m + sum_{i<=m} a_{i+1..m} (q_m . k_i) delta_i
+//   S  <- A_3 S0 + sum_i a_{i+1..3} k_i delta_i^T
+// (A_m = a_0 ... a_m, a_{i+1..m} the product of the decays after token i), the
+// token recurrence reassociated, so the four key sums share one pass of
+// shuffle trees.  The value columns of S are independent of one
+// another (delta and o of column c read only column c), so a head's columns
+// are split over HK / 16 CTAs; inside a CTA eight lanes share one column,
+// each holding HK / 8 of its keys in registers, and a token's two key sums
+// are 3-step shuffle trees over those lanes.  Tokens are staged in chunks of
+// 16 in shared memory, double-buffered: the next chunk's loads are issued
+// into registers before the current chunk is processed.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace laya {
 
 namespace delta {
-constexpr int C = 64;        // tokens per chunk
-constexpr int CB = 16;       // value columns per state CTA
-constexpr int KG = 16;       // key groups per state CTA (thread = key group x column)
-constexpr int THREADS = 256;
+constexpr int T = 16;   // tokens per staged chunk
+constexpr int CPB = 16; // value columns per CTA
+constexpr int G = 8;    // lanes per column (key groups)
+constexpr int THREADS = CPB * G;
 }  // namespace delta
 
 // a / b: the gate projections of token i, head h at a[i * ldab + h] and
-// b[i * ldab + h]; the log decay -exp(A_log) softplus(a + dt) and beta go to
-// ldec / beta [s][nh] (may alias a / b when ldab == nh).
+// b[i * ldab + h]; decay / beta go to dec / beta [s][nh] (may alias a / b
+// when ldab == nh).
 template <int HK>
 __global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv, const float* a, const float* b,
                                                          int ldab, const float* __restrict__ dt,
-                                                         const float* __restrict__ alog, int s, int nh, float* ldec,
+                                                         const float* __restrict__ alog, int s, int nh, float* dec,
                                                          float* beta) {
   constexpr int PL = HK / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
@@ -78,213 +77,214 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv
     const float x = a[src] + dt[h];
     const float bv = b[src];
     const float sp = x > 20.f ? x : log1pf(expf(x));
-    ldec[e] = -expf(alog[h]) * sp;
+    dec[e] = expf(-expf(alog[h]) * sp);
     beta[e] = 1.f / (1.f + expf(-bv));
   }
 }
 
-// One (chunk, head): stage the chunk's normalised q and k, v, beta and log
-// decay (rows past s are zero, so padded tokens add nothing), then
-//   g   = running sums of the log decays,
-//   KK  = K K^T and QK = Q K^T as 4 x 4 register tiles per thread,
-//   A   (strictly lower) and Pm (lower, diagonal included) from them,
-//   T   = (I + A)^-1 by forward substitution, one column per thread,
-//   W   = T diag(beta gamma) K and U0 = T diag(beta) V (4 x 8 tiles),
-// and write W, U0, Gamma Q, Kd [C][HK], Pm [C][C] and gamma_C.
-// Shared rows are padded to HK + 1 floats (no bank conflicts on columns).
+// One warp per (group of four tokens, head): the 6 key-key and 10
+// query-key products of the group, from the normalised q and k (tokens past
+// s read as zero), stored as kq[(quad * nh + h) * 16 + ...]: k1k0, k2k0,
+// k2k1, k3k0, k3k1, k3k2, then q0k0, q1k0, q1k1, q2k0, q2k1, q2k2, q3k0, q3k1,
+// q3k2, q3k3.
 template <int HK>
-__global__ void __launch_bounds__(delta::THREADS) delta_chunk_kernel(const float* __restrict__ qkv,
-                                                                    const float* __restrict__ ldec,
-                                                                    const float* __restrict__ beta, int s, int nh,
-                                                                    float* __restrict__ wout, float* __restrict__ uout,
-                                                                    float* __restrict__ qgout, float* __restrict__ kdout,
-                                                                    float* __restrict__ pmout, float* __restrict__ gcout) {
-  using namespace delta;
-  constexpr int LD = HK + 1, LDC = C + 1;
-  extern __shared__ float dsm[];
-  float* Ks = dsm;                // [C][LD]
-  float* Qs = Ks + C * LD;        // [C][LD]
-  float* Vs = Qs + C * LD;        // [C][LD]
-  float* As = Vs + C * LD;        // [C][LDC]  A
-  float* Ts = As + C * LDC;       // [C][LDC]  T
-  float* gs = Ts + C * LDC;       // [C]
-  float* bs = gs + C;             // [C]
-  const int ch = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int w = nh * HK, t0 = ch * C;
-  const size_t slot = (size_t)ch * nh + h;
-  for (int e = tid; e < C * HK; e += THREADS) {
-    const int t = e / HK, j = e % HK, i = t0 + t;
-    const bool live = i < s;
-    const float* row = qkv + (size_t)i * 3 * w + h * HK + j;
-    Qs[t * LD + j] = live ? row[0] : 0.f;
-    Ks[t * LD + j] = live ? row[w] : 0.f;
-    Vs[t * LD + j] = live ? row[2 * w] : 0.f;
-  }
-  if (tid < C) {
-    const int i = t0 + tid;
-    gs[tid] = i < s ? ldec[(size_t)i * nh + h] : 0.f;
-    bs[tid] = i < s ? beta[(size_t)i * nh + h] : 0.f;
-  }
-  __syncthreads();
-  if (tid == 0)
-    for (int t = 1; t < C; t++) gs[t] += gs[t - 1];  // in token order
-  __syncthreads();
-  {
-    // KK and QK: thread (rt, ri) owns rows t = 4 rt .. 4 rt + 3, columns i = 4 ri .. 4 ri + 3
-    const int rt = tid / 16, ri = tid % 16;
-    float kk[4][4] = {}, qk[4][4] = {};
-    for (int j = 0; j < HK; j++) {
-      float kt[4], qt[4], ki[4];
+__global__ void __launch_bounds__(256) delta_quad_kernel(const float* __restrict__ qkv, int s, int nh,
+                                                         float* __restrict__ kq) {
+  constexpr int PL = HK / 32;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  const int nq = (s + 3) / 4;
+  if (gw >= nq * nh) return;
+  const int qd = gw / nh, h = gw % nh, w = nh * HK;
+  float qv[4][PL], kv[4][PL];
 #pragma unroll
-      for (int r = 0; r < 4; r++) {
-        kt[r] = Ks[(4 * rt + r) * LD + j];
-        qt[r] = Qs[(4 * rt + r) * LD + j];
-        ki[r] = Ks[(4 * ri + r) * LD + j];
-      }
+  for (int m = 0; m < 4; m++) {
+    const int i = 4 * qd + m;
+    const float* row = qkv + (size_t)i * 3 * w + h * HK;
 #pragma unroll
-      for (int r = 0; r < 4; r++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          kk[r][c] = fmaf(kt[r], ki[c], kk[r][c]);
-          qk[r][c] = fmaf(qt[r], ki[c], qk[r][c]);
-        }
-    }
-    float* pm = pmout + slot * C * C;
-#pragma unroll
-    for (int r = 0; r < 4; r++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const int t = 4 * rt + r, i = 4 * ri + c;
-        const float ratio = i <= t ? expf(gs[t] - gs[i]) : 0.f;
-        As[t * LDC + i] = i < t ? bs[t] * ratio * kk[r][c] : 0.f;
-        pm[t * C + i] = ratio * qk[r][c];
-      }
-  }
-  __syncthreads();
-  // T = (I + A)^-1, lower triangular with a unit diagonal: row t is
-  // e_t - sum_{i<t} A[t][i] T[i][:]; thread c keeps column c
-  if (tid < C) {
-    const int c = tid;
-    for (int t = 0; t < C; t++) {
-      float v = t == c ? 1.f : 0.f;
-      for (int i = c; i < t; i++) v = fmaf(-As[t * LDC + i], Ts[i * LDC + c], v);
-      Ts[t * LDC + c] = t >= c ? v : 0.f;
+    for (int u = 0; u < PL; u++) {
+      qv[m][u] = i < s ? row[lane + 32 * u] : 0.f;
+      kv[m][u] = i < s ? row[w + lane + 32 * u] : 0.f;
     }
   }
-  __syncthreads();
-  {
-    // W and U0: thread (rt, rj) owns rows t = 4 rt .. + 3, columns j = rj, rj + 16, ... (HK / 16 of them)
-    constexpr int NJ = HK / 16;
-    const int rt = tid / 16, rj = tid % 16;
-    float wa[4][NJ] = {}, ua[4][NJ] = {};
-    for (int i = 0; i <= 4 * rt + 3; i++) {
-      const float sb = bs[i], sg = bs[i] * expf(gs[i]);
-      float tt[4];
+  float d[16];
+  int n = 0;
+  for (int m = 1; m < 4; m++)
+    for (int i = 0; i < m; i++) {
+      float x = 0.f;
 #pragma unroll
-      for (int r = 0; r < 4; r++) tt[r] = Ts[(4 * rt + r) * LDC + i];
-#pragma unroll
-      for (int q = 0; q < NJ; q++) {
-        const float kv = Ks[i * LD + rj + 16 * q] * sg, vv = Vs[i * LD + rj + 16 * q] * sb;
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-          wa[r][q] = fmaf(tt[r], kv, wa[r][q]);
-          ua[r][q] = fmaf(tt[r], vv, ua[r][q]);
-        }
-      }
+      for (int u = 0; u < PL; u++) x += kv[m][u] * kv[i][u];
+      d[n++] = x;
     }
-    const float gC = gs[C - 1];
+  for (int m = 0; m < 4; m++)
+    for (int i = 0; i <= m; i++) {
+      float x = 0.f;
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-      const int t = 4 * rt + r;
-      const float eg = expf(gs[t]), ed = expf(gC - gs[t]);
-#pragma unroll
-      for (int q = 0; q < NJ; q++) {
-        const int j = rj + 16 * q;
-        const size_t o = (slot * C + t) * HK + j;
-        wout[o] = wa[r][q];
-        uout[o] = ua[r][q];
-        qgout[o] = eg * Qs[t * LD + j];
-        kdout[o] = ed * Ks[t * LD + j];
-      }
+      for (int u = 0; u < PL; u++) x += qv[m][u] * kv[i][u];
+      d[n++] = x;
     }
-    if (tid == 0) gcout[slot] = expf(gC);
+#pragma unroll
+  for (int e = 0; e < 16; e++)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) d[e] += __shfl_xor_sync(0xffffffffu, d[e], o);
+  if (lane < 16) {
+    float v = d[0];
+#pragma unroll
+    for (int e = 1; e < 16; e++) v = lane == e ? d[e] : v;
+    kq[(size_t)gw * 16 + lane] = v;
   }
 }
 
-// One head, value columns c0 .. c0 + 15: the chunks in order.  Thread (kg,
-// c) holds S[j][c] for its HK / 16 keys j = kg * HK / 16 + r in registers.
-// Per chunk: Delta = U0 - W S0 and the Gamma Q S0 part of O as key-group
-// partials reduced in shared memory, O += Pm Delta, S = gamma_C S0 + Kd^T
-// Delta.
+// Thread (column cl = tid / 8, group g = tid % 8) of CTA (head, column block)
+// holds S[j][c] for its keys j = 32 m + 4 g + r (m < HK / 32, r < 4), so a
+// group's float4 reads of a staged key row are eight consecutive 16-byte
+// words (no bank conflicts).
 template <int HK>
-__global__ void __launch_bounds__(delta::THREADS) delta_state_kernel(const float* __restrict__ wk,
-                                                                    const float* __restrict__ uk,
-                                                                    const float* __restrict__ qgk,
-                                                                    const float* __restrict__ kdk,
-                                                                    const float* __restrict__ pmk,
-                                                                    const float* __restrict__ gck, int s, int nh,
-                                                                    float* __restrict__ out) {
+__global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float* __restrict__ qkv,
+                                                                   const float* __restrict__ dec,
+                                                                   const float* __restrict__ beta,
+                                                                   const float* __restrict__ kq, int s, int nh,
+                                                                   float* __restrict__ out) {
   using namespace delta;
-  constexpr int NK = HK / KG;  // keys per thread
-  extern __shared__ float ssm[];
-  float* R1 = ssm;                  // [KG][C][CB] partials of W S0
-  float* R2 = R1 + KG * C * CB;     // [KG][C][CB] partials of Gamma Q S0
-  float* Dl = R2 + KG * C * CB;     // [C][CB] Delta
-  const int h = blockIdx.x, c0 = blockIdx.y * CB, tid = threadIdx.x;
-  const int kg = tid / CB, c = tid % CB, w = nh * HK;
-  const int nch = (s + C - 1) / C;
-  float S[NK];
+  constexpr int M = HK / 32;            // float4 words of keys per thread
+  constexpr int QW = T * HK / 4;        // float4 words of one staged q (or k) chunk
+  constexpr int QPT = QW / THREADS;     // ... per thread
+  static_assert(QW % THREADS == 0, "chunk words must divide over the block");
+  constexpr int VW = T * CPB / 4;       // float4 words of the staged v chunk
+  static_assert(VW <= THREADS, "v chunk must fit one word per thread");
+  __shared__ __align__(16) float Qs[2][T][HK];
+  __shared__ __align__(16) float Ks[2][T][HK];
+  __shared__ __align__(16) float Vs[2][T][CPB];
+  __shared__ float Ds[2][T], Bs[2][T];
+  __shared__ float KQ[2][T / 4][16];   // the chunk's groups' key-key / query-key products
+  __shared__ float Op[T][CPB][G + 1];  // the chunk's per-lane output partials (padded row)
+  const int tid = threadIdx.x, g = tid % G, cl = tid / G;
+  const int h = blockIdx.x, c0 = blockIdx.y * CPB, w = nh * HK;
+  const size_t C = (size_t)3 * w;
+  float S[4 * M];
 #pragma unroll
-  for (int r = 0; r < NK; r++) S[r] = 0.f;
+  for (int j = 0; j < 4 * M; j++) S[j] = 0.f;
+
+  float4 rq[QPT], rk[QPT], rv = make_float4(0.f, 0.f, 0.f, 0.f);
+  float rd = 0.f, rkq = 0.f;
+  auto fetch = [&](int i0) {
+#pragma unroll
+    for (int u = 0; u < QPT; u++) {
+      const int idx = tid + u * THREADS, t = idx / (HK / 4), x = idx % (HK / 4), i = i0 + t;
+      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float* row = qkv + (size_t)i * C + h * HK + 4 * x;
+      rq[u] = i < s ? *reinterpret_cast<const float4*>(row) : zero;
+      rk[u] = i < s ? *reinterpret_cast<const float4*>(row + w) : zero;
+    }
+    if (tid < VW) {
+      const int t = tid / (CPB / 4), x = tid % (CPB / 4), i = i0 + t;
+      rv = i < s ? *reinterpret_cast<const float4*>(qkv + (size_t)i * C + 2 * w + h * HK + c0 + 4 * x)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (tid < 2 * T) {
+      const int t = tid % T, i = i0 + t;
+      rd = i < s ? (tid < T ? dec : beta)[(size_t)i * nh + h] : 0.f;
+    }
+    if (tid >= 64 && tid < 64 + 4 * T) {
+      const int e = tid - 64, qd = i0 / 4 + e / 16;
+      rkq = qd < (s + 3) / 4 ? kq[((size_t)qd * nh + h) * 16 + e % 16] : 0.f;
+    }
+  };
+  auto stage = [&](int buf) {
+#pragma unroll
+    for (int u = 0; u < QPT; u++) {
+      const int idx = tid + u * THREADS, t = idx / (HK / 4), x = idx % (HK / 4);
+      reinterpret_cast<float4*>(&Qs[buf][t][0])[x] = rq[u];
+      reinterpret_cast<float4*>(&Ks[buf][t][0])[x] = rk[u];
+    }
+    if (tid < VW) reinterpret_cast<float4*>(&Vs[buf][tid / (CPB / 4)][0])[tid % (CPB / 4)] = rv;
+    if (tid < T) Ds[buf][tid] = rd;
+    else if (tid < 2 * T) Bs[buf][tid - T] = rd;
+    if (tid >= 64 && tid < 64 + 4 * T) KQ[buf][(tid - 64) / 16][(tid - 64) % 16] = rkq;
+  };
+
+  const int nch = (s + T - 1) / T;
+  fetch(0);
+  stage(0);
+  __syncthreads();
   for (int ch = 0; ch < nch; ch++) {
-    const size_t slot = (size_t)ch * nh + h;
-    const float* W = wk + slot * C * HK;
-    const float* QG = qgk + slot * C * HK;
-    const float* KD = kdk + slot * C * HK;
-    const float* PM = pmk + slot * C * C;
-    const float* U0 = uk + slot * C * HK;
-    for (int t = 0; t < C; t++) {
-      float p1 = 0.f, p2 = 0.f;
+    const int buf = ch & 1, i0 = ch * T;
+    if (ch + 1 < nch) fetch(i0 + T);
+    const int tn = min(T, s - i0);
+    // Four tokens at a time: the eight sums k_m . S0 and q_m . S0 over this
+    // lane's keys, the key sums reduced over the column's lanes together,
+    // then the per-column solve for delta_0..3 (every lane of the column
+    // computes the same values) and one state update for the group.
+    for (int t = 0; t < tn; t += 4) {
+      const float* kqg = KQ[buf][t / 4];
+      float r[4], pp[4];
 #pragma unroll
-      for (int r = 0; r < NK; r++) {
-        const int j = kg * NK + r;
-        p1 = fmaf(__ldg(W + t * HK + j), S[r], p1);
-        p2 = fmaf(__ldg(QG + t * HK + j), S[r], p2);
+      for (int m = 0; m < 4; m++) {
+        float rr[4] = {0.f, 0.f, 0.f, 0.f}, qq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int mm = 0; mm < M; mm++) {
+          const float4 k4 = reinterpret_cast<const float4*>(&Ks[buf][t + m][0])[8 * mm + g];
+          const float4 q4 = reinterpret_cast<const float4*>(&Qs[buf][t + m][0])[8 * mm + g];
+          rr[0] = fmaf(S[4 * mm], k4.x, rr[0]);
+          rr[1] = fmaf(S[4 * mm + 1], k4.y, rr[1]);
+          rr[2] = fmaf(S[4 * mm + 2], k4.z, rr[2]);
+          rr[3] = fmaf(S[4 * mm + 3], k4.w, rr[3]);
+          qq[0] = fmaf(S[4 * mm], q4.x, qq[0]);
+          qq[1] = fmaf(S[4 * mm + 1], q4.y, qq[1]);
+          qq[2] = fmaf(S[4 * mm + 2], q4.z, qq[2]);
+          qq[3] = fmaf(S[4 * mm + 3], q4.w, qq[3]);
+        }
+        r[m] = (rr[0] + rr[1]) + (rr[2] + rr[3]);
+        pp[m] = (qq[0] + qq[1]) + (qq[2] + qq[3]);
       }
-      R1[(kg * C + t) * CB + c] = p1;
-      R2[(kg * C + t) * CB + c] = p2;
+#pragma unroll
+      for (int o = 1; o < G; o <<= 1)
+#pragma unroll
+        for (int m = 0; m < 4; m++) r[m] += __shfl_xor_sync(0xffffffffu, r[m], o);
+      float a[4], bt[4], v[4];
+#pragma unroll
+      for (int m = 0; m < 4; m++) {
+        a[m] = Ds[buf][t + m];
+        bt[m] = Bs[buf][t + m];
+        v[m] = Vs[buf][t + m][cl];
+      }
+      // A_m = a_0 .. a_m; x_mi = a_{i+1} .. a_m (products of later decays)
+      const float A0 = a[0], A1 = A0 * a[1], A2 = A1 * a[2], A3 = A2 * a[3];
+      const float x10 = a[1], x21 = a[2], x20 = a[2] * a[1], x32 = a[3], x31 = a[3] * a[2], x30 = x31 * a[1];
+      const float d0 = bt[0] * (v[0] - A0 * r[0]);
+      const float d1 = bt[1] * (v[1] - (A1 * r[1] + x10 * kqg[0] * d0));
+      const float d2 = bt[2] * (v[2] - (A2 * r[2] + x20 * kqg[1] * d0 + x21 * kqg[2] * d1));
+      const float d3 = bt[3] * (v[3] - (A3 * r[3] + x30 * kqg[3] * d0 + x31 * kqg[4] * d1 + x32 * kqg[5] * d2));
+      // outputs: this lane's share of A_m p_m, plus (lane 0) the delta terms
+      const bool l0 = g == 0;
+      Op[t][cl][g] = A0 * pp[0] + (l0 ? kqg[6] * d0 : 0.f);
+      Op[t + 1][cl][g] = A1 * pp[1] + (l0 ? x10 * kqg[7] * d0 + kqg[8] * d1 : 0.f);
+      Op[t + 2][cl][g] = A2 * pp[2] + (l0 ? x20 * kqg[9] * d0 + x21 * kqg[10] * d1 + kqg[11] * d2 : 0.f);
+      Op[t + 3][cl][g] =
+          A3 * pp[3] + (l0 ? x30 * kqg[12] * d0 + x31 * kqg[13] * d1 + x32 * kqg[14] * d2 + kqg[15] * d3 : 0.f);
+      // S <- A_3 S0 + x30 k0 d0 + x31 k1 d1 + x32 k2 d2 + k3 d3
+      const float w0 = x30 * d0, w1 = x31 * d1, w2 = x32 * d2;
+#pragma unroll
+      for (int mm = 0; mm < M; mm++) {
+        const float4 k0 = reinterpret_cast<const float4*>(&Ks[buf][t][0])[8 * mm + g];
+        const float4 k1 = reinterpret_cast<const float4*>(&Ks[buf][t + 1][0])[8 * mm + g];
+        const float4 k2 = reinterpret_cast<const float4*>(&Ks[buf][t + 2][0])[8 * mm + g];
+        const float4 k3 = reinterpret_cast<const float4*>(&Ks[buf][t + 3][0])[8 * mm + g];
+        S[4 * mm] = fmaf(k3.x, d3, fmaf(k2.x, w2, fmaf(k1.x, w1, fmaf(k0.x, w0, A3 * S[4 * mm]))));
+        S[4 * mm + 1] = fmaf(k3.y, d3, fmaf(k2.y, w2, fmaf(k1.y, w1, fmaf(k0.y, w0, A3 * S[4 * mm + 1]))));
+        S[4 * mm + 2] = fmaf(k3.z, d3, fmaf(k2.z, w2, fmaf(k1.z, w1, fmaf(k0.z, w0, A3 * S[4 * mm + 2]))));
+        S[4 * mm + 3] = fmaf(k3.w, d3, fmaf(k2.w, w2, fmaf(k1.w, w1, fmaf(k0.w, w0, A3 * S[4 * mm + 3]))));
+      }
     }
     __syncthreads();
-    for (int e = tid; e < C * CB; e += THREADS) {
-      const int t = e / CB, cc = e % CB;
-      float a = 0.f, q = 0.f;
+    // the chunk's outputs: thread (token, column) sums its 8 lane partials
+    for (int e = tid; e < tn * CPB; e += THREADS) {
+      const int t = e / CPB, c = e % CPB;
+      float o = 0.f;
 #pragma unroll
-      for (int g = 0; g < KG; g++) {
-        a += R1[(g * C + t) * CB + cc];
-        q += R2[(g * C + t) * CB + cc];
-      }
-      Dl[t * CB + cc] = __ldg(U0 + t * HK + c0 + cc) - a;
-      R2[t * CB + cc] = q;  // group 0's slot of R2 now holds the full Gamma Q S0 sum
+      for (int j = 0; j < G; j++) o += Op[t][c][j];
+      out[(size_t)(i0 + t) * w + h * HK + c0 + c] = o;
     }
-    __syncthreads();
-    for (int e = tid; e < C * CB; e += THREADS) {
-      const int t = e / CB, cc = e % CB;
-      float o = R2[t * CB + cc];
-      for (int i = 0; i <= t; i++) o = fmaf(__ldg(PM + t * C + i), Dl[i * CB + cc], o);
-      const int tok = ch * C + t;
-      if (tok < s) out[(size_t)tok * w + h * HK + c0 + cc] = o;
-    }
-    const float gC = __ldg(gck + slot);
-    float acc[NK];
-#pragma unroll
-    for (int r = 0; r < NK; r++) acc[r] = gC * S[r];
-    for (int i = 0; i < C; i++) {
-      const float d = Dl[i * CB + c];
-#pragma unroll
-      for (int r = 0; r < NK; r++) acc[r] = fmaf(__ldg(KD + i * HK + kg * NK + r), d, acc[r]);
-    }
-#pragma unroll
-    for (int r = 0; r < NK; r++) S[r] = acc[r];
+    if (ch + 1 < nch) stage(buf ^ 1);
     __syncthreads();
   }
 }
@@ -337,11 +337,11 @@ cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int l
   if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
   const size_t C = (size_t)3 * nh * hk, n = (size_t)s * C;
   float* qkv = scratch;
-  float* ldec = scratch + n;
-  float* beta = ldec + (size_t)s * nh;
-  float* chunks = beta + ((size_t)s * nh + 63) / 64 * 64;
+  float* dec = scratch + n;
+  float* beta = dec + (size_t)s * nh;
+  float* kq = beta + (size_t)s * nh;
   conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, ldraw, conv, s, (int)C, qkv);
-  cudaError_t e = gated_delta(qkv, a, b, ldab, dt, alog, s, nh, hk, ldec, beta, chunks, out, st);
+  cudaError_t e = gated_delta(qkv, a, b, ldab, dt, alog, s, nh, hk, dec, beta, kq, out, st);
   if (e != cudaSuccess) return e;
   const int rows = s * nh;
   if (hk == 128)
@@ -352,52 +352,28 @@ cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int l
 }
 
 size_t gated_delta_mixer_scratch(int s, int nh, int hk) {
-  return ((size_t)s * (3 * nh * hk + nh) + ((size_t)s * nh + 63) / 64 * 64) * 4 + gated_delta_scratch(s, nh, hk);
+  return (size_t)s * (3 * nh * hk + 2 * nh) * 4 + gated_delta_scratch(s, nh);
 }
 
-size_t gated_delta_scratch(int s, int nh, int hk) {
-  const size_t slots = (size_t)((s + delta::C - 1) / delta::C) * nh;
-  return (slots * (4 * delta::C * hk + delta::C * delta::C + 1) + 64) * 4;
-}
-
-template <int HK>
-static cudaError_t gated_delta_go(float* qkv, const float* a, const float* b, int ldab, const float* dt,
-                                  const float* alog, int s, int nh, float* ldec, float* beta, float* chunks,
-                                  float* out, cudaStream_t st) {
-  using namespace delta;
-  const unsigned prep_blocks = (unsigned)(((size_t)s * nh + 7) / 8);
-  delta_prep_kernel<HK><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, ldec, beta);
-  const int nch = (s + C - 1) / C;
-  const size_t slots = (size_t)nch * nh, mat = (size_t)C * HK;
-  float* W = chunks;
-  float* U = W + slots * mat;
-  float* QG = U + slots * mat;
-  float* KD = QG + slots * mat;
-  float* PM = KD + slots * mat;
-  float* GC = PM + slots * C * C;
-  constexpr int smem1 = (3 * C * (HK + 1) + 2 * C * (C + 1) + 2 * C) * 4;
-  constexpr int smem2 = (2 * KG * C * CB + C * CB) * 4;
-  static std::atomic<bool> configured[64];  // per device; any host thread may launch
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!configured[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(delta_chunk_kernel<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(delta_state_kernel<HK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
-    if (e != cudaSuccess) return e;
-    configured[dev & 63] = true;
-  }
-  delta_chunk_kernel<HK><<<dim3(nch, nh), THREADS, smem1, st>>>(qkv, ldec, beta, s, nh, W, U, QG, KD, PM, GC);
-  delta_state_kernel<HK><<<dim3(nh, HK / CB), THREADS, smem2, st>>>(W, U, QG, KD, PM, GC, s, nh, out);
-  return cudaGetLastError();
-}
+size_t gated_delta_scratch(int s, int nh) { return (size_t)((s + 3) / 4) * nh * 16 * 4; }
 
 cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, const float* dt, const float* alog,
-                        int s, int nh, int hk, float* ldec, float* beta, float* chunks, float* out, cudaStream_t st) {
+                        int s, int nh, int hk, float* dec, float* beta, float* kq, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
-  if (nh < 1 || (hk != 64 && hk != 128) || !chunks) return cudaErrorInvalidValue;
-  if (hk == 128) return gated_delta_go<128>(qkv, a, b, ldab, dt, alog, s, nh, ldec, beta, chunks, out, st);
-  return gated_delta_go<64>(qkv, a, b, ldab, dt, alog, s, nh, ldec, beta, chunks, out, st);
+  if (nh < 1 || (hk != 64 && hk != 128) || !kq) return cudaErrorInvalidValue;
+  const unsigned prep_blocks = (unsigned)(((size_t)s * nh + 7) / 8);
+  const unsigned quad_blocks = (unsigned)(((size_t)((s + 3) / 4) * nh + 7) / 8);
+  const dim3 grid(nh, hk / delta::CPB);
+  if (hk == 128) {
+    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta);
+    delta_quad_kernel<128><<<quad_blocks, 256, 0, st>>>(qkv, s, nh, kq);
+    delta_scan_kernel<128><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, kq, s, nh, out);
+  } else {
+    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta);
+    delta_quad_kernel<64><<<quad_blocks, 256, 0, st>>>(qkv, s, nh, kq);
+    delta_scan_kernel<64><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, kq, s, nh, out);
+  }
+  return cudaGetLastError();
 }
 
 }  // namespace laya

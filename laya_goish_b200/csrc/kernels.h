@@ -53,15 +53,15 @@ cudaError_t rows_f32(const QTensor& t, const int* ids, int nrows, float* out, cu
 // the bulk-copy kernel, whose bounded wait reports there.
 cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, int d, float eps, half* out16,
                     float* out32, cudaStream_t st, bool pdl = false, unsigned* err = nullptr);
-// OpenThai's gated DeltaNet recurrence (deltanet.cu), one sequence, in
-// chunks of 64 tokens: qkv [s][3 nh hk] after the convolution (q / k
-// normalised in place); the gate projections of token i, head h at a /
-// b[i * ldab + h]; the log decay / beta are written to ldec / beta [s][nh]
-// (they may alias a / b when ldab == nh); chunks: gated_delta_scratch(s,
-// nh, hk) bytes of per-chunk matrices; out [s][nh hk] before the output norm.
-size_t gated_delta_scratch(int s, int nh, int hk);
+// OpenThai's gated DeltaNet recurrence (deltanet.cu), one sequence: qkv
+// [s][3 nh hk] after the convolution (q / k normalised in place); the gate
+// projections of token i, head h at a / b[i * ldab + h]; decay / beta are
+// written to dec / beta [s][nh] (they may alias a / b when ldab == nh);
+// out [s][nh hk] before the output norm.
+// kq: gated_delta_scratch(s, nh) bytes (the four-token groups' products).
+size_t gated_delta_scratch(int s, int nh);
 cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, const float* dt, const float* alog,
-                        int s, int nh, int hk, float* ldec, float* beta, float* chunks, float* out, cudaStream_t st);
+                        int s, int nh, int hk, float* dec, float* beta, float* kq, float* out, cudaStream_t st);
 // The whole mixer after its projections: raw rows (stride ldraw) [3 nh hk],
 // z rows (stride ldz) [nh hk], a / b as above; scratch holds
 // gated_delta_mixer_scratch(s, nh, hk) bytes.
