@@ -354,12 +354,16 @@ __global__ void __launch_bounds__(192, 1)
         if (r < w.it.q_len) {
           half* dst = o + (size_t)(w.it.q_row + r) * ldo + w.h * HD + c * 32;
           if (gate) {
-            // OpenThai's output gate: o * sigmoid(gate) (src/models/openthai/model.rs:293-295)
-            const float* gr = gate + (size_t)(w.it.q_row + r) * ldg + w.h * ghs + c * 32;
+            // OpenThai's output gate: o * sigmoid(gate) (src/models/openthai/model.rs:293-295);
+            // the row's 32 gate values as eight 16-byte loads (rows are 16-byte aligned)
+            const float4* gr = reinterpret_cast<const float4*>(gate + (size_t)(w.it.q_row + r) * ldg + w.h * ghs + c * 32);
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-              const float gv = gr[i];
-              v[i] = __float_as_uint(__uint_as_float(v[i]) * inv * (1.f / (1.f + expf(-gv))));
+            for (int i4 = 0; i4 < 8; i4++) {
+              const float4 gv = __ldg(gr + i4);
+              const float gg[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+              for (int e = 0; e < 4; e++)
+                v[4 * i4 + e] = __float_as_uint(__uint_as_float(v[4 * i4 + e]) * inv * (1.f / (1.f + expf(-gg[e]))));
             }
           } else {
 #pragma unroll
@@ -416,6 +420,7 @@ cudaError_t attention_tc(const AttnParams& p, cudaStream_t st) {
   if (!p.n_items) return cudaSuccess;
   if ((p.hd != 64 && p.hd != 128 && p.hd != 256) || !p.err || p.q_rows <= 0 || p.kv_rows <= 0 || (p.ldq % 8))
     return cudaErrorNotSupported;
+  if (p.gate && ((reinterpret_cast<uintptr_t>(p.gate) & 15) || (p.ldg % 4) || (p.ghs % 4))) return cudaErrorInvalidValue;
   CUtensorMap tq, tk, tv;
   const uint64_t qdims[2] = {(uint64_t)p.ldq, (uint64_t)p.q_rows}, qstr[1] = {(uint64_t)p.ldq * 2};
   const uint32_t qbox[2] = {64, 128};
