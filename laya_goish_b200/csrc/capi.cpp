@@ -346,7 +346,8 @@ int laya_gated_delta_mixer(int device, const float* raw, const float* z, const f
   if (e == cudaSuccess) e = cudaMemcpy(p + 2 * nh, normw, (size_t)hk * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = gated_delta_mixer(draw.as<float>(), (int)(3 * w), dz.as<float>(), (int)w, da.as<float>(), db.as<float>(), nh,
-                          dconv.as<float>(), p, p + nh, p + 2 * nh, s, nh, hk, dsc.as<float>(), dout.as<float>(), 0);
+                          dconv.as<float>(), p, p + nh, p + 2 * nh, s, nh, hk, dsc.as<float>(), dout.as<float>(),
+                          nullptr, 0);
   if (e == cudaSuccess) e = cudaMemcpy(out, dout.p, nz * 4, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "laya_gated_delta_mixer");
   return 0;

@@ -304,11 +304,43 @@ __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldraw, const
   out[e] = acc / (1.f + expf(-acc));
 }
 
+// The same on four channels per thread with 16-byte loads and stores (raw
+// and out 16-byte aligned, ldraw and C multiples of 4): grid.y = token,
+// grid.x over channel quads; the four taps of each channel are one float4.
+__global__ void conv_silu4_kernel(const float* __restrict__ raw, int ldraw, const float* __restrict__ conv, int C,
+                                  float* __restrict__ out) {
+  const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x), i = blockIdx.y;
+  if (c >= C) return;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float4 w[4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) w[u] = __ldg(reinterpret_cast<const float4*>(conv + (size_t)(c + u) * 4));
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    if (i + j < 3) continue;
+    const float4 x = __ldg(reinterpret_cast<const float4*>(raw + (size_t)(i + j - 3) * ldraw + c));
+    const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const float wj = j == 0 ? w[u].x : j == 1 ? w[u].y : j == 2 ? w[u].z : w[u].w;
+      acc[u] += xs[u] * wj;
+    }
+  }
+  float4 r;
+  r.x = acc[0] / (1.f + expf(-acc[0]));
+  r.y = acc[1] / (1.f + expf(-acc[1]));
+  r.z = acc[2] / (1.f + expf(-acc[2]));
+  r.w = acc[3] / (1.f + expf(-acc[3]));
+  *reinterpret_cast<float4*>(out + (size_t)i * C + c) = r;
+}
+
 // Per-head RMSNorm (weight offset 0, eps 1e-6) of the recurrence output,
-// then x SiLU(z) (model.rs:356-360); one warp per (token, head) row.
+// then x SiLU(z) (model.rs:356-360); one warp per (token, head) row.  The
+// result goes to o (F32, in place) or, when out16 is set, to out16 as F16
+// rows [s][nh HK] (the output projection's operand) with o left as it was.
 template <int HK>
 __global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict__ z, int ldz, int nh,
-                                 const float* __restrict__ w, int rows) {
+                                 const float* __restrict__ w, int rows, half* __restrict__ out16) {
   constexpr int PL = HK / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (gw >= rows) return;
@@ -326,13 +358,17 @@ __global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict_
 #pragma unroll
   for (int u = 0; u < PL; u++) {
     const float zz = zr[lane + 32 * u];
-    r[lane + 32 * u] = v[u] * scale * w[lane + 32 * u] * (zz / (1.f + expf(-zz)));
+    const float y = v[u] * scale * w[lane + 32 * u] * (zz / (1.f + expf(-zz)));
+    if (out16)
+      out16[(size_t)gw * HK + lane + 32 * u] = __float2half_rn(y);
+    else
+      r[lane + 32 * u] = y;
   }
 }
 
 cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int ldz, const float* a, const float* b,
                               int ldab, const float* conv, const float* dt, const float* alog, const float* normw,
-                              int s, int nh, int hk, float* scratch, float* out, cudaStream_t st) {
+                              int s, int nh, int hk, float* scratch, float* out, half* out16, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
   if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
   const size_t C = (size_t)3 * nh * hk, n = (size_t)s * C;
@@ -340,14 +376,19 @@ cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int l
   float* dec = scratch + n;
   float* beta = dec + (size_t)s * nh;
   float* kq = beta + (size_t)s * nh;
-  conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, ldraw, conv, s, (int)C, qkv);
+  if (ldraw % 4 == 0 && (reinterpret_cast<uintptr_t>(raw) & 15) == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
+      s <= 65535)
+    conv_silu4_kernel<<<dim3((unsigned)((C / 4 + 127) / 128), (unsigned)s), 128, 0, st>>>(raw, ldraw, conv, (int)C,
+                                                                                          qkv);
+  else
+    conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, ldraw, conv, s, (int)C, qkv);
   cudaError_t e = gated_delta(qkv, a, b, ldab, dt, alog, s, nh, hk, dec, beta, kq, out, st);
   if (e != cudaSuccess) return e;
   const int rows = s * nh;
   if (hk == 128)
-    norm_gate_kernel<128><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows);
+    norm_gate_kernel<128><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows, out16);
   else
-    norm_gate_kernel<64><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows);
+    norm_gate_kernel<64><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows, out16);
   return cudaGetLastError();
 }
 

@@ -64,11 +64,13 @@ cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, co
                         int s, int nh, int hk, float* dec, float* beta, float* kq, float* out, cudaStream_t st);
 // The whole mixer after its projections: raw rows (stride ldraw) [3 nh hk],
 // z rows (stride ldz) [nh hk], a / b as above; scratch holds
-// gated_delta_mixer_scratch(s, nh, hk) bytes.
+// gated_delta_mixer_scratch(s, nh, hk) bytes (16-byte aligned).  The result
+// rows [s][nh hk] go to out (F32) or, when out16 is set, to out16 as F16
+// (out is then the recurrence's scratch output).
 size_t gated_delta_mixer_scratch(int s, int nh, int hk);
 cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int ldz, const float* a, const float* b,
                               int ldab, const float* conv, const float* dt, const float* alog, const float* normw,
-                              int s, int nh, int hk, float* scratch, float* out, cudaStream_t st);
+                              int s, int nh, int hk, float* scratch, float* out, half* out16, cudaStream_t st);
 // OpenThai gated attention after the projections (gated_attn.cu): rows of
 // qgate [H][query hd | gate hd] (row stride ldqg), of k and v [KV][hd] (row
 // stride ldkv), F32; q / k norm weights [hd] -> out16 [s][H * hd] F16 (the

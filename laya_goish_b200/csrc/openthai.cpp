@@ -12,6 +12,7 @@
 // caller (the host's config checks); tensors are read from the GGUF here.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -48,7 +49,7 @@ struct laya_ot_model {
   unsigned* err = nullptr;
   std::vector<void*> allocs;
   // forward scratch, grown on demand and kept between passes
-  laya::DevBuf dids, dpos, x, h, big, att, att16, act, logits, gscr;
+  laya::DevBuf dids, dpos, x, h, big, att, att16, act, logits, gscr, kpart;
   std::mutex mu;
 };
 
@@ -212,8 +213,21 @@ int load(Model& m, const Gguf& g, const uint8_t* layer_full) {
   return 0;
 }
 
+// Prefill GEMMs launch with programmatic dependent launch unless
+// LAYA_GEMM_PDL=0 (their first weight tiles come into L2 while the previous
+// kernel drains).
+bool gemm_pdl() {
+  static const bool on = [] {
+    const char* e = std::getenv("LAYA_GEMM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// ksplit > 1 (residual GEMMs only): partial sums into planes of `part`,
+// merged by the RMSNorm that next reads the residual.
 int gemm(Model& m, int epi, const half* A, int lda, const half* B, int N, int K, int M, void* out, int ldo,
-         float* resid, const float* bias) {
+         float* resid, const float* bias, int ksplit = 1, float* part = nullptr) {
   GemmArgs a{};
   a.M = M;
   a.N = N;
@@ -222,9 +236,11 @@ int gemm(Model& m, int epi, const half* A, int lda, const half* B, int N, int K,
   a.ldo = ldo;
   a.resid = resid;
   a.bias = bias;
+  a.ksplit = ksplit;
+  a.part = part;
   a.err = m.err;
   a.budget = 4000000000ll;
-  LAYA_CK(gemm_launch(epi, A, lda, B, K, a, m.num_sms, m.st));
+  LAYA_CK(gemm_launch(epi, A, lda, B, K, a, m.num_sms, m.st, gemm_pdl()));
   return 0;
 }
 
@@ -315,6 +331,23 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
       (rc = logits.ensure((size_t)npos * c.slots * 4)) ||
       (rc = m->gscr.ensure(std::max<size_t>(16, gated_attention_scratch(s, H, KV, hd)))))
     return rc;
+  // Residual GEMMs with few output tiles split K (as in the decoder forward);
+  // the RMSNorm that next reads the residual adds the planes in split order.
+  const char* ke = std::getenv("LAYA_KSPLIT");
+  const bool ks_on = !(ke && ke[0] == '0');
+  const int ks_full = ks_on ? gemm_ksplit(s, d, qd, m->num_sms) : 1;
+  const int ks_delta = ks_on ? gemm_ksplit(s, d, w, m->num_sms) : 1;
+  const int ks_down = ks_on ? gemm_ksplit(s, d, ffn, m->num_sms) : 1;
+  const int ks_max = std::max(std::max(ks_full, ks_delta), ks_down);
+  if (ks_max > 1 && (rc = m->kpart.ensure((size_t)ks_max * S * d * 4))) return rc;
+  float* PART = ks_max > 1 ? m->kpart.as<float>() : nullptr;
+  int pend = 0;  // K splits of X not yet merged
+  auto norm = [&](const int* rows, int n, const float* wn) -> cudaError_t {
+    const int ns = pend;
+    pend = 0;
+    if (ns > 1) return rmsnorm_merge(x.as<float>(), rows, n, PART, ns, S * d, wn, d, c.eps, h.as<half>(), nullptr, m->st);
+    return rmsnorm(x.as<float>(), rows, n, wn, d, c.eps, h.as<half>(), nullptr, m->st, false, m->err);
+  };
   cudaStream_t st = m->st;
   LAYA_CK(cudaMemcpyAsync(dids.p, ids, S * 4, cudaMemcpyHostToDevice, st));
   LAYA_CK(cudaMemcpyAsync(dpos.p, positions, (size_t)npos * 4, cudaMemcpyHostToDevice, st));
@@ -325,27 +358,33 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
   LAYA_CK(rows_f32(m->embd, dids.as<int>(), s, X, st));
   for (int l = 0; l < c.n_layers; l++) {
     const OtLayer& L = m->layers[l];
-    LAYA_CK(rmsnorm(X, nullptr, s, L.n1, d, c.eps, Hh, nullptr, st));
+    LAYA_CK(norm(nullptr, s, L.n1));
     if (L.full) {
       // one GEMM: rows [q | gate per head] (2 qd), k (KV hd), v (KV hd)
       if ((rc = gemm(*m, EPI_F32, Hh, d, L.q, nfull, d, s, P, nfull, nullptr, nullptr))) return rc;
       LAYA_CK(gated_attention(P, nfull, P + 2 * qd, P + 2 * qd + KV * hd, nfull, L.qn, L.kn, s, H, KV, hd, c.rot,
                               c.theta, m->gscr.p, att16.as<half>(), m->err, st));
-      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr))) return rc;
+      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr, ks_full, PART)))
+        return rc;
+      pend = ks_full;
     } else {
       // one GEMM: rows in_proj_qkv (3w), z (w), a (nh), b (nh)
       if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, ndelta, d, s, P, ndelta, nullptr, nullptr))) return rc;
+      // the mixer writes its normalised, gated rows as F16 straight into
+      // the output projection's operand
       LAYA_CK(gated_delta_mixer(P, ndelta, P + 3 * w, ndelta, P + 4 * w, P + 4 * w + nh, ndelta, L.conv, L.dt, L.alog,
-                                L.normw, s, nh, hk, SCR, att.as<float>(), st));
-      LAYA_CK(f32_to_f16_pad(att.as<float>(), s, w, w, att16.as<half>(), st));
-      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), w, L.out, d, w, s, nullptr, d, X, nullptr))) return rc;
+                                L.normw, s, nh, hk, SCR, att.as<float>(), att16.as<half>(), st));
+      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), w, L.out, d, w, s, nullptr, d, X, nullptr, ks_delta, PART)))
+        return rc;
+      pend = ks_delta;
     }
-    LAYA_CK(rmsnorm(X, nullptr, s, L.n2, d, c.eps, Hh, nullptr, st));
+    LAYA_CK(norm(nullptr, s, L.n2));
     if ((rc = gemm(*m, EPI_SWIGLU, Hh, d, L.gu, 2 * ffn, d, s, act.p, ffn, nullptr, nullptr)) ||
-        (rc = gemm(*m, EPI_RESID, act.as<half>(), ffn, L.down, d, ffn, s, nullptr, d, X, nullptr)))
+        (rc = gemm(*m, EPI_RESID, act.as<half>(), ffn, L.down, d, ffn, s, nullptr, d, X, nullptr, ks_down, PART)))
       return rc;
+    pend = ks_down;
   }
-  LAYA_CK(rmsnorm(X, dpos.as<int>(), npos, m->norm, d, c.eps, Hh, nullptr, st));
+  LAYA_CK(norm(dpos.as<int>(), npos, m->norm));
   if ((rc = gemm(*m, EPI_F32, Hh, d, m->head, c.slots, d, npos, logits.p, c.slots, nullptr, m->head_bias))) return rc;
   LAYA_CK(cudaMemcpyAsync(out, logits.p, (size_t)npos * c.slots * 4, cudaMemcpyDeviceToHost, st));
   LAYA_CK(cudaStreamSynchronize(st));
@@ -363,7 +402,7 @@ void laya_openthai_close(laya_ot_model* m) {
   if (m->st) cudaStreamSynchronize(m->st);
   for (void* p : m->allocs) cudaFree(p);
   for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->att, &m->att16, &m->act, &m->logits,
-                     &m->gscr})
+                     &m->gscr, &m->kpart})
     b->release();
   if (m->st) cudaStreamDestroy(m->st);
   delete m;

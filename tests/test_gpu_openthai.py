@@ -170,3 +170,31 @@ def test_openthai_decide_matches_oracle(ot_model):
         assert abs(got["c"]["probabilities"][k] - want["c"]["probabilities"][k]) < 1e-2
     assert abs(got["s"]["score"] - want["s"]["score"]) < 5e-2
     assert abs(got["n"]["noul"] - want["n"]["noul"]) < 1e-2
+
+
+def test_openthai_batch_over_two_gpus(tmp_path):
+    """A batch of states shared over one model per GPU (OpenThaiService with
+    a model list) gives the one-GPU answers, in request order."""
+    import json
+
+    import torch
+
+    from laya_goish_b200 import frontend, openthai, synth
+    from laya_goish_b200.tokenizer import Tokenizer
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    path = synth.write_openthai(str(tmp_path / "ot2.gguf"), d=128, ffn=256, heads=4, kv=2, hd=64, lin_heads=2,
+                                lin_dim=64, seed=13, tokenizer=True)
+    tok = Tokenizer.from_gguf(path)
+    batch = {"states": ["a", {"b": 1}, "ccc", "d d", ["e"], "ff"],
+             "questions": {"c": {"type": "choice", "instructions": "route",
+                                 "criteria": {"a": "billing", "b": None, "c": "other"}},
+                           "n": {"type": "noul", "instructions": "spam?"}},
+             "order_invariant": True}
+    with openthai.Model(path, device=0, strict=False) as m0, openthai.Model(path, device=1, strict=False) as m1:
+        one = frontend.OpenThaiService(m0, tok).handle("POST", "/v1/decide/batch", json.dumps(batch))
+        two = frontend.OpenThaiService([m0, m1], tok).handle("POST", "/v1/decide/batch", json.dumps(batch))
+    assert one.status == two.status == 200
+    strip = lambda b: [{k: v for k, v in r.items() if k not in ("usage", "id")} for r in b["results"]]
+    assert strip(one.body) == strip(two.body)
