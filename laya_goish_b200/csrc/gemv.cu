@@ -349,7 +349,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
   auto grid_sync = [&](int p) {
     cta_epi_sync();
     if (threadIdx.x == 0) {
-      __threadfence();
+      // the release is cumulative: the CTA's output stores, ordered before
+      // it by the named barrier above, are visible to every CTA whose
+      // acquire load below reads the completed count
       asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(q.gbar) : "memory");
       const unsigned target = (unsigned)p * gridDim.x;
       const long long t0 = clock64();
@@ -547,6 +549,44 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv3_kernel(const __grid_const
         for (int k = tid * 8; k < K; k += GV_WARPS * 32 * 8)
           *reinterpret_cast<uint4*>(xs + (size_t)b * xpitch + k) =
               *reinterpret_cast<const uint4*>(a.x + (size_t)b * a.ldx + k);
+      named_sync();
+    } else if ((size_t)a.nb * K <= (size_t)2 * GV_WARPS * 32 * NT * 4) {
+      // x = rmsnorm(xres[b]) * norm_w with one pass over global memory: the
+      // residual and the norm weights are loaded together and x * w is
+      // kept in F32 in the (idle) partial-sum buffer until the scale is known.
+      float* xw = reinterpret_cast<float*>(red);
+      for (int b = 0; b < a.nb; b++) {
+        float ss = 0.f;
+        for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
+          const float4 v = *reinterpret_cast<const float4*>(a.xres + (size_t)b * K + k);
+          const float4 wv = *reinterpret_cast<const float4*>(a.norm_w + k);
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+          *reinterpret_cast<float4*>(xw + (size_t)b * K + k) =
+              make_float4(v.x * wv.x, v.y * wv.y, v.z * wv.z, v.w * wv.w);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) nred[warp][b] = ss;
+      }
+      named_sync();
+      if (tid < a.nb) {
+        float tsum = 0.f;
+        for (int i = 0; i < GV_WARPS; i++) tsum += nred[i][tid];
+        nscale[tid] = 1.f / sqrtf(tsum / (float)K + a.eps);
+      }
+      named_sync();
+      for (int b = 0; b < a.nb; b++) {
+        const float sc = nscale[b];
+        for (int k = tid * 4; k < K; k += GV_WARPS * 32 * 4) {
+          const float4 t = *reinterpret_cast<const float4*>(xw + (size_t)b * K + k);
+          half2 h0 = __floats2half2_rn(t.x * sc, t.y * sc);
+          half2 h1 = __floats2half2_rn(t.z * sc, t.w * sc);
+          uint2 u2;
+          u2.x = *reinterpret_cast<uint32_t*>(&h0);
+          u2.y = *reinterpret_cast<uint32_t*>(&h1);
+          *reinterpret_cast<uint2*>(xs + (size_t)b * xpitch + k) = u2;
+        }
+      }
       named_sync();
     } else {
       // x = rmsnorm(xres[b]) * norm_w  (src/models/openthai/model.rs:84-94), F16 rows in shared memory
