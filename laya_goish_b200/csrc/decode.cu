@@ -782,28 +782,39 @@ __global__ void __launch_bounds__(160, 1)
     mbar_fence_init();
   }
   __syncthreads();
-  pdl_wait();  // the step's K/V rows were appended by the previous kernel
-  pdl_trigger();
+  // The sequence table (written by the step's first kernel), the page table
+  // and every K/V page except the one that holds this step's new key row
+  // (written by the kernel just before this one) were written two or more
+  // kernels back, which had completed before the previous kernel passed its
+  // own griddepcontrol.wait and let this one start: the first pages' loads
+  // are issued before waiting on the previous kernel.
   const DecSeq s = seqs[b];
   const int n_pages = (s.n_keys + PAGE - 1) / PAGE;
   const int p0 = sp * split_pages, p1 = min(n_pages, p0 + split_pages);
   const int np = max(0, p1 - p0);
   const int g = lane >> 2, t = lane & 3;
-  if (warp == C::NW) {
-    if (lane == 0) {
-      for (int i = 0; i < np; i++) {
-        const int st = i % C::S;
-        if (!mbar_wait(&empty[st], ((i / C::S) & 1) ^ 1, budget)) atomicOr(err, 1024u);
-        const int row = (tables[s.table_off + p0 + i] * KV + kvh) * PAGE;
-        uint8_t* dst = sm + st * C::STAGE;
-        mbar_expect_tx(&full[st], C::STAGE);
+  auto load_page = [&](int i) {
+    const int st = i % C::S;
+    if (!mbar_wait(&empty[st], ((i / C::S) & 1) ^ 1, budget)) atomicOr(err, 1024u);
+    const int row = (tables[s.table_off + p0 + i] * KV + kvh) * PAGE;
+    uint8_t* dst = sm + st * C::STAGE;
+    mbar_expect_tx(&full[st], C::STAGE);
 #pragma unroll
-        for (int hb = 0; hb < HD / 64; hb++) {
-          tma_load_2d(dst + hb * 8192, &tk, &full[st], hb * 64, row);
-          tma_load_2d(dst + C::PAGE_BYTES + hb * 8192, &tv, &full[st], hb * 64, row);
-        }
-      }
+    for (int hb = 0; hb < HD / 64; hb++) {
+      tma_load_2d(dst + hb * 8192, &tk, &full[st], hb * 64, row);
+      tma_load_2d(dst + C::PAGE_BYTES + hb * 8192, &tv, &full[st], hb * 64, row);
     }
+  };
+  // split-local index of the page holding the new row (np when it is not in this split)
+  const int last = min(np, (s.n_keys - 1) / PAGE - p0);
+  const int pre = max(0, min(min(np, C::S), last));
+  if (warp == C::NW && lane == 0)
+    for (int i = 0; i < pre; i++) load_page(i);
+  pdl_wait();  // q and the new K/V row were written by the previous kernel
+  pdl_trigger();
+  if (warp == C::NW) {
+    if (lane == 0)
+      for (int i = pre; i < np; i++) load_page(i);
   } else {
     // Q of head g of the group as the A fragment (rows g + 8 are zero)
     uint32_t qa[HD / 16][4];
