@@ -267,6 +267,7 @@ def decode_point(e, batch: int, ctx: int, gen: int, dist, device):
     library), max over ranks."""
     rng = np.random.default_rng(4)
     ctxs = [synth.token_ids(rng, CFG.vocab, ctx) for _ in range(batch)]
+    e.decode(ctxs, 4)  # warm-up: packed GEMV images, graph capture, first launches
     if dist:
         dist.barrier()
     _, st = e.decode(ctxs, gen)

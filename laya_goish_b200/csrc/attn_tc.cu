@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "gemm.h"
 #include "kernels.h"
+#include "launch.h"
 #include "mma.cuh"
 #include "ptx.cuh"
 
@@ -151,6 +152,10 @@ __global__ void __launch_bounds__(192, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // Launched early behind the previous kernel: everything above is set-up;
+  // every global read below waits for that kernel's output.
+  pdl_wait();
+  pdl_trigger();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
@@ -404,16 +409,19 @@ static cudaError_t attn_tc_go(const AttnParams& p, const CUtensorMap& tq, const 
     if (e != cudaSuccess) return e;
     configured[dev & 63] = true;
   }
-  static int sms[64] = {0};
+  static std::atomic<int> sms[64];
   if (!sms[dev & 63]) {
-    cudaError_t e = cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+    int n = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
+    sms[dev & 63] = n;
   }
   const int units = p.n_items * p.H;
   const int grid = std::min(units, Atc<HD>::CTAS_PER_SM * sms[dev & 63]);
-  attn_tc_kernel<HD><<<grid, 192, Atc<HD>::SMEM, st>>>(tq, tk, tv, p.o, p.ldo, p.tables, p.items, units, p.H, p.KV,
-                                                       p.scale_log2, p.gate, p.ldg, p.ghs, p.err, 100000000ll);
-  return cudaGetLastError();
+  // programmatic dependent launch: the CTAs set up their barriers and TMEM
+  // while the previous kernel drains
+  return launch_k(attn_tc_kernel<HD>, dim3(grid), dim3(192), (size_t)Atc<HD>::SMEM, st, true, tq, tk, tv, p.o, p.ldo,
+                  p.tables, p.items, units, p.H, p.KV, p.scale_log2, p.gate, p.ldg, p.ghs, p.err, 100000000ll);
 }
 
 cudaError_t attention_tc(const AttnParams& p, cudaStream_t st) {

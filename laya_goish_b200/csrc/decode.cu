@@ -757,14 +757,22 @@ struct Dec3 {
   static constexpr int PAGE_BYTES = 64 * HD * 2;  // K or V of one page
   static constexpr int STAGE = 2 * PAGE_BYTES;
   static constexpr int SMEM = S * STAGE + 2 * S * 8 + NW * 8 * (HD + 2) * 4 + 1024;
+  // cluster form: the leader also holds every split's partial [CLS][8][HD + 2]
+  // and the merge weights [8][CLS + 1]
+  static constexpr int CLS = 8;  // CTAs (key splits) per cluster
+  static constexpr int SMEM_CL = SMEM + CLS * 8 * (HD + 2) * 4 + 8 * (CLS + 1) * 4;
 };
 
-template <int HD, int G>
+// CL: the CLS key splits of one (sequence, kv head) form a cluster; each
+// CTA stores its split partial into the leader's shared memory (DSMEM), and
+// after one cluster barrier the leader merges them and writes the heads'
+// F16 output rows, so no separate merge launch is needed.
+template <int HD, int G, bool CL>
 __global__ void __launch_bounds__(160, 1)
     attn_dec3_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                      const half* __restrict__ q, const int* __restrict__ tables, const DecSeq* __restrict__ seqs,
                      int KV, float scale_log2, int split_pages, int splits, float* __restrict__ part,
-                     unsigned* err, long long budget) {
+                     half* __restrict__ out, unsigned* err, long long budget) {
   using C = Dec3<HD>;
   extern __shared__ uint8_t d3_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(d3_raw) + 1023) & ~uintptr_t(1023));
@@ -782,6 +790,9 @@ __global__ void __launch_bounds__(160, 1)
     mbar_fence_init();
   }
   __syncthreads();
+  // CL: every CTA of the cluster must be running before any stores into the
+  // leader's shared memory; this arrival is waited on just before them.
+  if constexpr (CL) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   // The sequence table (written by the step's first kernel), the page table
   // and every K/V page except the one that holds this step's new key row
   // (written by the kernel just before this one) were written two or more
@@ -912,6 +923,8 @@ __global__ void __launch_bounds__(160, 1)
   }
   __syncthreads();
   // merge the consumer warps: one split partial per head of the group
+  float* cp = comb + C::NW * 8 * (HD + 2);  // CL: the leader's [CLS][G][HD + 2]
+  if constexpr (CL) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   for (int idx = threadIdx.x; idx < G * (HD + 2); idx += blockDim.x) {
     const int gg = idx / (HD + 2), c = idx % (HD + 2);
     float M = -INFINITY;
@@ -925,7 +938,39 @@ __global__ void __launch_bounds__(160, 1)
         if (mw != -INFINITY) v += exp2f(mw - M) * comb[(w * 8 + gg) * (HD + 2) + c];
       }
     }
-    part[(((size_t)b * H + kvh * G + gg) * splits + sp) * (HD + 2) + c] = v;
+    if constexpr (CL) {
+      const uint32_t dst = cluster_addr(cp + ((size_t)sp * G + gg) * (HD + 2) + c, 0);
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(v) : "memory");
+    } else {
+      part[(((size_t)b * H + kvh * G + gg) * splits + sp) * (HD + 2) + c] = v;
+    }
+  }
+  if constexpr (CL) {
+    // o = sum_s 2^(m_s - M) acc_s / sum_s 2^(m_s - M) l_s over the cluster's splits
+    cluster_sync();
+    if (sp != 0) return;
+    float* wts = cp + C::CLS * G * (HD + 2);  // [G][CLS + 1]: split weights, then 1 / l
+    if (threadIdx.x < G) {
+      const int gg = threadIdx.x;
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < C::CLS; s2++) M = fmaxf(M, cp[(s2 * G + gg) * (HD + 2)]);
+      float l = 0.f;
+      for (int s2 = 0; s2 < C::CLS; s2++) {
+        const float ms = cp[(s2 * G + gg) * (HD + 2)];
+        const float wgt = ms == -INFINITY ? 0.f : exp2f(ms - M);
+        wts[gg * (C::CLS + 1) + s2] = wgt;
+        l += wgt * cp[(s2 * G + gg) * (HD + 2) + 1];
+      }
+      wts[gg * (C::CLS + 1) + C::CLS] = 1.f / l;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+      const int gg = idx / HD, d = idx % HD;
+      float v = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < C::CLS; s2++) v += wts[gg * (C::CLS + 1) + s2] * cp[(s2 * G + gg) * (HD + 2) + 2 + d];
+      out[((size_t)b * H + kvh * G + gg) * HD + d] = __float2half_rn(v * wts[gg * (C::CLS + 1) + C::CLS]);
+    }
   }
 }
 
@@ -993,7 +1038,14 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int H, int H
 struct AttnShape {
   int splits, split_pages;    // attn_dec2_kernel
   int splits3, split_pages3;  // attn_dec3_kernel: one CTA per SM, so at most one wave of CTAs
+  bool cluster;               // attn_dec3_kernel in clusters of CLS splits
+  int split_pages_cl;
 };
+
+static bool dec3_cluster_enabled() {
+  const char* e = std::getenv("LAYA_DEC_CLUSTER");
+  return !(e && e[0] == '0');
+}
 
 static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_keys) {
   const int pages = (max_keys + PAGE - 1) / PAGE;
@@ -1002,7 +1054,10 @@ static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_k
   const int split_pages = (pages + splits - 1) / splits;
   int s3 = std::max(1, std::min(r.num_sms / (nb * c.KV), (pages + 1) / 2));
   const int sp3 = (pages + s3 - 1) / s3;
-  return {(pages + split_pages - 1) / split_pages, split_pages, (pages + sp3 - 1) / sp3, sp3};
+  constexpr int CLS = Dec3<64>::CLS;
+  const bool cl = dec3_cluster_enabled() && nb * c.KV * CLS <= r.num_sms && pages >= CLS;
+  return {(pages + split_pages - 1) / split_pages, split_pages, (pages + sp3 - 1) / sp3, sp3, cl,
+          (pages + CLS - 1) / CLS};
 }
 
 static bool seq_enabled() {
@@ -1018,18 +1073,38 @@ static bool dec3_enabled() {
 template <int HD, int G>
 static cudaError_t launch_dec3(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
                                const half* q, const int* tables, const DecSeq* seqs, int KV, float sl2,
-                               int split_pages, int splits, float* part, unsigned* err) {
+                               int split_pages, int splits, float* part, half* out, bool cl, unsigned* err) {
   static std::atomic<bool> configured[64];  // per device; any host thread may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
     cudaError_t e =
-        cudaFuncSetAttribute(attn_dec3_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, Dec3<HD>::SMEM);
+        cudaFuncSetAttribute(attn_dec3_kernel<HD, G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Dec3<HD>::SMEM);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_dec3_kernel<HD, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Dec3<HD>::SMEM_CL);
     if (e != cudaSuccess) return e;
     configured[dev & 63] = true;
   }
-  return launch_k(attn_dec3_kernel<HD, G>, grid, dim3(160), (size_t)Dec3<HD>::SMEM, st, true, tk, tv, q, tables,
-                  seqs, KV, sl2, split_pages, splits, part, err, 4000000000ll);
+  if (!cl)
+    return launch_k(attn_dec3_kernel<HD, G, false>, grid, dim3(160), (size_t)Dec3<HD>::SMEM, st, true, tk, tv, q,
+                    tables, seqs, KV, sl2, split_pages, splits, part, out, err, 4000000000ll);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(160);
+  cfg.dynamicSmemBytes = Dec3<HD>::SMEM_CL;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = Dec3<HD>::CLS;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, attn_dec3_kernel<HD, G, true>, tk, tv, q, tables, seqs, KV, sl2, split_pages,
+                            splits, part, out, err, 4000000000ll);
 }
 
 template <int HD, int G>
@@ -1061,6 +1136,7 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
   const int* tb = r.tables.as<int>();
   float* part = r.dpart.as<float>();
   int splits = sh.splits;
+  bool cl = false;
   if (dec3_enabled() && G <= 8 && (c.hd == 64 || c.hd == 128)) {
     // K and V of this layer as [pages * kv_heads * 64 rows][hd] F16, 64 x 64 boxes
     CUtensorMap tk, tv;
@@ -1069,12 +1145,15 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
     if (!encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(LAYA_E_CUDA, "KV tensor map");
-    const dim3 g3(nb, c.KV, sh.splits3);
-    splits = sh.splits3;
-#define LAYA_DEC3(HDV, GV)                                                                                 \
-  if (c.hd == HDV && G == GV)                                                                              \
-    e = launch_dec3<HDV, GV>(g3, r.stream, tk, tv, q, tb, seqs, c.KV, sl2, sh.split_pages3, sh.splits3, part, \
-                             r.err);
+    // Few (sequence, kv head) pairs: eight key splits per pair as one
+    // cluster that merges its partials itself (no merge launch).
+    cl = sh.cluster;
+    const int sp3 = cl ? sh.split_pages_cl : sh.split_pages3;
+    splits = cl ? Dec3<64>::CLS : sh.splits3;
+    const dim3 g3(nb, c.KV, splits);
+#define LAYA_DEC3(HDV, GV)                                                                                    \
+  if (c.hd == HDV && G == GV)                                                                                 \
+    e = launch_dec3<HDV, GV>(g3, r.stream, tk, tv, q, tb, seqs, c.KV, sl2, sp3, splits, part, out, cl, r.err);
     LAYA_DEC3(64, 1)
     LAYA_DEC3(64, 2)
     LAYA_DEC3(64, 4)
@@ -1085,6 +1164,10 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
     LAYA_DEC3(128, 7)
     LAYA_DEC3(128, 8)
 #undef LAYA_DEC3
+    if (e == cudaErrorNotSupported) {  // the split-merge form below
+      cl = false;
+      splits = sh.splits;
+    }
   }
   const dim3 grid(nb, c.KV, sh.splits);
 #define LAYA_DEC2(HDV, GV)                                                                                         \
@@ -1102,9 +1185,13 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
 #undef LAYA_DEC2
   if (e == cudaErrorNotSupported) return fail(LAYA_E_INVALID, "unsupported head grouping for decode");
   if (e != cudaSuccess) return cuda_fail(e, "attn_dec2_kernel");
-  const int cthreads = c.hd <= 64 ? 256 : 256;
-  LAYA_CK(launch_k(attn_combine_kernel, dim3(nb, c.H), dim3(cthreads), (size_t)(splits + cthreads) * 4, r.stream,
-                   true, (const float*)part, c.H, c.hd, splits, out));
+  if (cl) {
+    r.launches--;
+  } else {
+    const int cthreads = 256;
+    LAYA_CK(launch_k(attn_combine_kernel, dim3(nb, c.H), dim3(cthreads), (size_t)(splits + cthreads) * 4, r.stream,
+                     true, (const float*)part, c.H, c.hd, splits, out));
+  }
   prof_end(r, P_ATTN_DEC, a);
   return 0;
 }

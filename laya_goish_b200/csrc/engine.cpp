@@ -808,8 +808,11 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     r.launches++;
     const int ns = pend;
     pend = 0;
-    if (ns > 1) return rmsnorm_merge(x, rows, n, r.kpart.as<float>(), ns, (size_t)M * d, w, d, c.eps, o16, o32, st);
-    return rmsnorm(x, rows, n, w, d, c.eps, o16, o32, st, false, r.err);
+    // launched early behind the previous kernel (it waits for that kernel's
+    // output before reading), so its launch overlaps the GEMM's tail
+    if (ns > 1)
+      return rmsnorm_merge(x, rows, n, r.kpart.as<float>(), ns, (size_t)M * d, w, d, c.eps, o16, o32, st, gemm_pdl());
+    return rmsnorm(x, rows, n, w, d, c.eps, o16, o32, st, gemm_pdl(), r.err);
   };
   for (int l = 0; l < c.L; l++) {
     const Layer& L = r.layers[l];

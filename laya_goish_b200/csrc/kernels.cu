@@ -282,9 +282,9 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
 }
 
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
-                          const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st) {
+                          const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st, bool pdl) {
   if (!nrows) return cudaSuccess;
-  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, false, x, rows, w, d, eps, out16, out32, part,
+  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, x, rows, w, d, eps, out16, out32, part,
                   part ? nsplit : 0, split_stride);
 }
 

@@ -84,7 +84,8 @@ cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const 
 // GEMM that wrote x, planes split_stride floats apart); without a row gather
 // (rows null) the merged rows are also written back to x.
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
-                          const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st);
+                          const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st,
+                          bool pdl = false);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,
                             cudaStream_t st);
 cudaError_t lse_rows(const float* logits, int V, int n, float* out, cudaStream_t st);

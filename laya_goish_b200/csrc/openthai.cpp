@@ -345,8 +345,10 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
   auto norm = [&](const int* rows, int n, const float* wn) -> cudaError_t {
     const int ns = pend;
     pend = 0;
-    if (ns > 1) return rmsnorm_merge(x.as<float>(), rows, n, PART, ns, S * d, wn, d, c.eps, h.as<half>(), nullptr, m->st);
-    return rmsnorm(x.as<float>(), rows, n, wn, d, c.eps, h.as<half>(), nullptr, m->st, false, m->err);
+    if (ns > 1)
+      return rmsnorm_merge(x.as<float>(), rows, n, PART, ns, S * d, wn, d, c.eps, h.as<half>(), nullptr, m->st,
+                           gemm_pdl());
+    return rmsnorm(x.as<float>(), rows, n, wn, d, c.eps, h.as<half>(), nullptr, m->st, gemm_pdl(), m->err);
   };
   cudaStream_t st = m->st;
   LAYA_CK(cudaMemcpyAsync(dids.p, ids, S * 4, cudaMemcpyHostToDevice, st));

@@ -100,12 +100,15 @@ def test_cfg1_batch_requests_match_oracle():
     print(f"[parity] cfg1 worst |dp| over 4 of 64 requests = {worst:.3e}")
 
 
-@pytest.mark.parametrize("nseq", [1, 4])
-def test_long_context_decode_matches_oracle(nseq):
+@pytest.mark.parametrize("nseq,cluster", [(1, "1"), (4, "1"), (1, "0")])
+def test_long_context_decode_matches_oracle(nseq, cluster, monkeypatch):
     # Teacher-forced on the GPU's own tokens: at every step the oracle, given
     # the same history, must rank the GPU's token within 2e-2 (logit units)
     # of its own maximum.  A free-running comparison would stop at the first
-    # near-tie, after which the sequences legitimately diverge.
+    # near-tie, after which the sequences legitimately diverge.  cluster "1":
+    # few sequences take the attention whose key splits merge inside one
+    # cluster; "0" forces the separate merge launch.
+    monkeypatch.setenv("LAYA_DEC_CLUSTER", cluster)
     path = synth.model_path("small-llama-q8_0")
     rng = np.random.default_rng(40 + nseq)
     ctxs = [synth.token_ids(rng, 4000, int(n)) for n in rng.integers(4090, 4200, size=nseq)]
@@ -127,5 +130,6 @@ def test_long_context_decode_matches_oracle(nseq):
                 h = c.forward([int(toks[i, s])], [0])
         c.close()
     o.close()
-    print(f"[parity] decode ctx ~4096 x {nseq}: {exact}/{nseq * steps} tokens are the oracle's argmax, "
+    print(f"[parity] decode ctx ~4096 x {nseq} (cluster merge {cluster}): {exact}/{nseq * steps} tokens are the "
+          f"oracle's argmax, "
           f"worst logit gap {worst:.3e}")
