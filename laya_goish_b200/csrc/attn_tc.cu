@@ -26,6 +26,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -77,30 +78,45 @@ __device__ __forceinline__ uint64_t kdesc(const uint8_t* base, int kk, int block
 }
 
 struct AtcUnit {
-  AttnItem it;
-  int h, kvh, n_keys, nblk;
+  int q_row, rows, pos0, table_off;  // query tokens q_row .. q_row + rows - 1 at positions pos0 ..
+  int hg, n_keys, nblk;              // head group: query heads hg * gp .. hg * gp + gp - 1
 };
 
-__device__ __forceinline__ AtcUnit atc_unit(const AttnItem* items, int u, int H, int KV) {
+// Rows of the 128-row tile per query head when gp heads share a unit: the
+// packed form puts the gp = H / KV heads of one KV head in one tile (row =
+// g * RT + t), so each K/V page is loaded and multiplied once for the group;
+// gp = 1 is one head per unit over 128 tokens.  A multiple of 8 (whole
+// swizzle atoms).
+__host__ __device__ __forceinline__ int atc_rt(int gp) { return (128 / gp) & ~7; }
+
+// Unit u = (item, block sb of RT tokens, head group hg of NHG).  Items hold
+// up to 128 tokens, so an item has ceil(128 / RT) blocks; a block past the
+// item's tokens is an empty unit (rows <= 0) that every role skips.
+__device__ __forceinline__ AtcUnit atc_unit(const AttnItem* items, int u, int SB, int NHG, int RT) {
   AtcUnit w;
-  w.it = items[u / H];
-  w.h = u % H;
-  w.kvh = w.h / (H / KV);
-  w.n_keys = w.it.pos0 + w.it.q_len;
+  const AttnItem it = items[u / (SB * NHG)];
+  const int rem = u % (SB * NHG), t0 = (rem / NHG) * RT;
+  w.hg = rem % NHG;
+  w.rows = min(RT, it.q_len - t0);
+  w.q_row = it.q_row + t0;
+  w.pos0 = it.pos0 + t0;
+  w.table_off = it.table_off;
+  w.n_keys = w.pos0 + max(w.rows, 0);
   w.nblk = (w.n_keys + 63) / 64;
   return w;
 }
 
-// Persistent: CTA c takes work units u = c, c + gridDim.x, ... with
-// u = item * H + head (CTAs running together share K/V pages in L2).  All
+// Persistent: CTA c takes work units u = c, c + gridDim.x, ... (see
+// atc_unit; CTAs running together share K/V pages in L2).  All
 // ring, buffer and barrier indices run over the CTA's global page count g
 // and unit count k, so the producer fetches the next unit's Q and pages
 // while the current unit is still being computed.
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, Atc<HD>::CTAS_PER_SM)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, half* __restrict__ o, int ldo,
                    const int* __restrict__ tables, const AttnItem* __restrict__ items, int n_units, int H, int KV,
+                   int gp,
                    float scale_log2, const float* __restrict__ gate, int ldg, int ghs, unsigned* err,
                    long long budget) {
   using C = Atc<HD>;
@@ -125,6 +141,15 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // G heads per unit (gp), NHG head groups, GQ query heads per KV head
+  const int G = gp, NHG = H / gp, GQ = H / KV, RT = atc_rt(G), SB = (128 + RT - 1) / RT;
+  // Q rows G * RT .. 127 are never loaded (G not a power of two): zero, so
+  // their scores stay finite; they are never written out.
+  for (int i = threadIdx.x; i < C::NQ * (HD / 64) * (128 - G * RT) * 8; i += blockDim.x) {
+    const int per = (128 - G * RT) * 8, blk = i / per, e = i % per;
+    reinterpret_cast<uint4*>(sQ + blk * 16384 + G * RT * 128)[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_async_smem();
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; b++) {
       mbar_init(&q_full[b], 1);
@@ -162,16 +187,21 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0) {
       int g = 0;
-      for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
-        const AtcUnit w = atc_unit(items, u, H, KV);
+      for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x) {
+        const AtcUnit w = atc_unit(items, u, SB, NHG, RT);
+        if (w.rows <= 0) continue;
         const int qb = k % C::NQ;
         if (!mbar_wait(&q_empty[qb], ((k / C::NQ) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
-        mbar_expect_tx(&q_full[qb], C::Q_BYTES);
+        mbar_expect_tx(&q_full[qb], (uint32_t)(G * RT * 128 * (HD / 64)));
+        // head g of the group: RT token rows into tile rows g * RT ..
 #pragma unroll
         for (int hb = 0; hb < HD / 64; hb++)
-          tma_load_2d(sQ + qb * C::Q_BYTES + hb * 16384, &tq, &q_full[qb], w.h * HD + hb * 64, w.it.q_row);
+          for (int gg = 0; gg < G; gg++)
+            tma_load_2d(sQ + qb * C::Q_BYTES + hb * 16384 + gg * RT * 128, &tq, &q_full[qb],
+                        (w.hg * G + gg) * HD + hb * 64, w.q_row);
+        k++;
         for (int j = 0; j < w.nblk; j++, g++) {
-          const int row = (tables[w.it.table_off + j] * KV + w.kvh) * 64;
+          const int row = (tables[w.table_off + j] * KV + w.hg * G / GQ) * 64;
           const int ks = g % C::NK, vs = g % C::NV;
           if (!mbar_wait(&k_empty[ks], ((g / C::NK) & 1) ^ 1, budget)) atomicOr(err, 1u << 12);
           mbar_expect_tx(&k_full[ks], C::KV_BYTES);
@@ -216,8 +246,10 @@ __global__ void __launch_bounds__(192, 1)
         if (plast) umma_commit(&o_full[pob]);
       };
       int g = 0;
-      for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
-        const AtcUnit w = atc_unit(items, u, H, KV);
+      for (int u = blockIdx.x, k = -1; u < n_units; u += gridDim.x) {
+        const AtcUnit w = atc_unit(items, u, SB, NHG, RT);
+        if (w.rows <= 0) continue;
+        k++;
         const int qb = k % C::NQ;
         if (!mbar_wait(&q_full[qb], (k / C::NQ) & 1, budget)) atomicOr(err, 1u << 13);
         for (int j = 0; j < w.nblk; j++, g++) {
@@ -247,10 +279,13 @@ __global__ void __launch_bounds__(192, 1)
     const int quarter = warp % 4, r = quarter * 32 + lane;
     const uint32_t tl = tbase + ((uint32_t)(quarter * 32) << 16);
     int g = 0;
-    for (int u = blockIdx.x, k = 0; u < n_units; u += gridDim.x, k++) {
-      const AtcUnit w = atc_unit(items, u, H, KV);
+    const int rg = r / RT, rt = r % RT;  // this row's head in the group and token in the block
+    for (int u = blockIdx.x, k = -1; u < n_units; u += gridDim.x) {
+      const AtcUnit w = atc_unit(items, u, SB, NHG, RT);
+      if (w.rows <= 0) continue;
+      k++;
       const int ob = k % C::NO;
-      const int pos = w.it.pos0 + r;
+      const int pos = w.pos0 + rt;
       float mref = -INFINITY, l = 0.f;  // reference maximum in log2 units
       for (int j = 0; j < w.nblk; j++, g++) {
         const int sb = g & 1;
@@ -271,7 +306,7 @@ __global__ void __launch_bounds__(192, 1)
           s[32 + c] = __uint_as_float(v1[c]);
         }
         const int key0 = j * 64;
-        if (key0 + 63 > w.it.pos0 || key0 + 64 > w.n_keys) {
+        if (key0 + 63 > w.pos0 || key0 + 64 > w.n_keys) {
           // keys key0 + c with c > lim are masked (causal, and past the last key)
           const int lim = min(pos, w.n_keys - 1) - key0;
 #pragma unroll
@@ -356,12 +391,13 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
         tmem_ld32(tl + C::O_COL + ob * HD + c * 32, v);
         tmem_ld_wait();
-        if (r < w.it.q_len) {
-          half* dst = o + (size_t)(w.it.q_row + r) * ldo + w.h * HD + c * 32;
+        if (rg < G && rt < w.rows) {
+          const int h = w.hg * G + rg;
+          half* dst = o + (size_t)(w.q_row + rt) * ldo + h * HD + c * 32;
           if (gate) {
             // OpenThai's output gate: o * sigmoid(gate) (src/models/openthai/model.rs:293-295);
             // the row's 32 gate values as eight 16-byte loads (rows are 16-byte aligned)
-            const float4* gr = reinterpret_cast<const float4*>(gate + (size_t)(w.it.q_row + r) * ldg + w.h * ghs + c * 32);
+            const float4* gr = reinterpret_cast<const float4*>(gate + (size_t)(w.q_row + rt) * ldg + h * ghs + c * 32);
 #pragma unroll
             for (int i4 = 0; i4 < 8; i4++) {
               const float4 gv = __ldg(gr + i4);
@@ -398,6 +434,15 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// LAYA_ATTN_PACK=0 / 1 overrides the caller's choice of packed units.
+static int attn_pack_forced() {
+  static const int forced = [] {
+    const char* e = std::getenv("LAYA_ATTN_PACK");
+    return e ? std::atoi(e) : -1;
+  }();
+  return forced;
+}
+
 template <int HD>
 static cudaError_t attn_tc_go(const AttnParams& p, const CUtensorMap& tq, const CUtensorMap& tk,
                               const CUtensorMap& tv, cudaStream_t st) {
@@ -416,12 +461,13 @@ static cudaError_t attn_tc_go(const AttnParams& p, const CUtensorMap& tq, const 
     if (e != cudaSuccess) return e;
     sms[dev & 63] = n;
   }
-  const int units = p.n_items * p.H;
+  const int gp = (attn_pack_forced() >= 0 ? attn_pack_forced() : p.pack) ? p.H / p.KV : 1;
+  const int RT = atc_rt(gp), units = p.n_items * ((128 + RT - 1) / RT) * (p.H / gp);
   const int grid = std::min(units, Atc<HD>::CTAS_PER_SM * sms[dev & 63]);
   // programmatic dependent launch: the CTAs set up their barriers and TMEM
   // while the previous kernel drains
   return launch_k(attn_tc_kernel<HD>, dim3(grid), dim3(192), (size_t)Atc<HD>::SMEM, st, true, tq, tk, tv, p.o, p.ldo,
-                  p.tables, p.items, units, p.H, p.KV, p.scale_log2, p.gate, p.ldg, p.ghs, p.err, 100000000ll);
+                  p.tables, p.items, units, p.H, p.KV, gp, p.scale_log2, p.gate, p.ldg, p.ghs, p.err, 100000000ll);
 }
 
 cudaError_t attention_tc(const AttnParams& p, cudaStream_t st) {
@@ -431,7 +477,9 @@ cudaError_t attention_tc(const AttnParams& p, cudaStream_t st) {
   if (p.gate && ((reinterpret_cast<uintptr_t>(p.gate) & 15) || (p.ldg % 4) || (p.ghs % 4))) return cudaErrorInvalidValue;
   CUtensorMap tq, tk, tv;
   const uint64_t qdims[2] = {(uint64_t)p.ldq, (uint64_t)p.q_rows}, qstr[1] = {(uint64_t)p.ldq * 2};
-  const uint32_t qbox[2] = {64, 128};
+  if (p.H % p.KV || p.H / p.KV > 16) return cudaErrorNotSupported;
+  const int gp = (attn_pack_forced() >= 0 ? attn_pack_forced() : p.pack) ? p.H / p.KV : 1;
+  const uint32_t qbox[2] = {64, (uint32_t)atc_rt(gp)};  // one head's block of query rows
   const uint64_t kdims[2] = {(uint64_t)p.hd, (uint64_t)p.kv_rows}, kstr[1] = {(uint64_t)p.hd * 2};
   const uint32_t kbox[2] = {64, 64};
   if (!encode_tiled(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.q, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||

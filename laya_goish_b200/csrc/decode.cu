@@ -759,11 +759,11 @@ struct Dec3 {
   static constexpr int SMEM = S * STAGE + 2 * S * 8 + NW * 8 * (HD + 2) * 4 + 1024;
   // cluster form: the leader also holds every split's partial [CLS][8][HD + 2]
   // and the merge weights [8][CLS + 1]
-  static constexpr int CLS = 8;  // CTAs (key splits) per cluster
+  static constexpr int CLS = 8;  // most CTAs (key splits) per cluster
   static constexpr int SMEM_CL = SMEM + CLS * 8 * (HD + 2) * 4 + 8 * (CLS + 1) * 4;
 };
 
-// CL: the CLS key splits of one (sequence, kv head) form a cluster; each
+// CL: the key splits (2..CLS) of one (sequence, kv head) form a cluster; each
 // CTA stores its split partial into the leader's shared memory (DSMEM), and
 // after one cluster barrier the leader merges them and writes the heads'
 // F16 output rows, so no separate merge launch is needed.
@@ -953,9 +953,9 @@ __global__ void __launch_bounds__(160, 1)
     if (threadIdx.x < G) {
       const int gg = threadIdx.x;
       float M = -INFINITY;
-      for (int s2 = 0; s2 < C::CLS; s2++) M = fmaxf(M, cp[(s2 * G + gg) * (HD + 2)]);
+      for (int s2 = 0; s2 < splits; s2++) M = fmaxf(M, cp[(s2 * G + gg) * (HD + 2)]);
       float l = 0.f;
-      for (int s2 = 0; s2 < C::CLS; s2++) {
+      for (int s2 = 0; s2 < splits; s2++) {
         const float ms = cp[(s2 * G + gg) * (HD + 2)];
         const float wgt = ms == -INFINITY ? 0.f : exp2f(ms - M);
         wts[gg * (C::CLS + 1) + s2] = wgt;
@@ -967,8 +967,7 @@ __global__ void __launch_bounds__(160, 1)
     for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
       const int gg = idx / HD, d = idx % HD;
       float v = 0.f;
-#pragma unroll
-      for (int s2 = 0; s2 < C::CLS; s2++) v += wts[gg * (C::CLS + 1) + s2] * cp[(s2 * G + gg) * (HD + 2) + 2 + d];
+      for (int s2 = 0; s2 < splits; s2++) v += wts[gg * (C::CLS + 1) + s2] * cp[(s2 * G + gg) * (HD + 2) + 2 + d];
       out[((size_t)b * H + kvh * G + gg) * HD + d] = __float2half_rn(v * wts[gg * (C::CLS + 1) + C::CLS]);
     }
   }
@@ -1038,8 +1037,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int H, int H
 struct AttnShape {
   int splits, split_pages;    // attn_dec2_kernel
   int splits3, split_pages3;  // attn_dec3_kernel: one CTA per SM, so at most one wave of CTAs
-  bool cluster;               // attn_dec3_kernel in clusters of CLS splits
-  int split_pages_cl;
+  bool cluster;               // attn_dec3_kernel with its splits as one cluster
+  int splits_cl, split_pages_cl;
 };
 
 static bool dec3_cluster_enabled() {
@@ -1054,10 +1053,15 @@ static AttnShape attn_shape(const Replica& r, const Config& c, int nb, int max_k
   const int split_pages = (pages + splits - 1) / splits;
   int s3 = std::max(1, std::min(r.num_sms / (nb * c.KV), (pages + 1) / 2));
   const int sp3 = (pages + s3 - 1) / s3;
+  // clusters of a power of two of splits (2..CLS) within one wave of CTAs;
+  // trailing splits may hold no page (their partial has weight 0)
   constexpr int CLS = Dec3<64>::CLS;
-  const bool cl = dec3_cluster_enabled() && nb * c.KV * CLS <= r.num_sms && pages >= CLS;
-  return {(pages + split_pages - 1) / split_pages, split_pages, (pages + sp3 - 1) / sp3, sp3, cl,
-          (pages + CLS - 1) / CLS};
+  const int n3 = (pages + sp3 - 1) / sp3;
+  int cls = CLS;
+  while (cls > 1 && (nb * c.KV * cls > r.num_sms || cls > pages)) cls /= 2;
+  const int spcl = (pages + cls - 1) / cls;
+  const bool cl = dec3_cluster_enabled() && cls >= 2;
+  return {(pages + split_pages - 1) / split_pages, split_pages, n3, sp3, cl, cl ? cls : 0, spcl};
 }
 
 static bool seq_enabled() {
@@ -1098,7 +1102,7 @@ static cudaError_t launch_dec3(dim3 grid, cudaStream_t st, const CUtensorMap& tk
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = Dec3<HD>::CLS;
+  attr[0].val.clusterDim.z = splits;  // one cluster per (sequence, kv head)
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
@@ -1149,7 +1153,7 @@ static int decode_attention(Model& m, Replica& r, int nb, const half* q, const h
     // cluster that merges its partials itself (no merge launch).
     cl = sh.cluster;
     const int sp3 = cl ? sh.split_pages_cl : sh.split_pages3;
-    splits = cl ? Dec3<64>::CLS : sh.splits3;
+    splits = cl ? sh.splits_cl : sh.splits3;
     const dim3 g3(nb, c.KV, splits);
 #define LAYA_DEC3(HDV, GV)                                                                                    \
   if (c.hd == HDV && G == GV)                                                                                 \

@@ -38,6 +38,27 @@ constexpr int G = 8;    // lanes per column (key groups)
 constexpr int THREADS = CPB * G;
 }  // namespace delta
 
+// Two F32 lanes in one 64-bit register pair (low word first) and the packed
+// F32x2 arithmetic of sm_100 (each lane an ordinary IEEE fma / mul, so the
+// results equal the scalar forms bit for bit, at one instruction per pair).
+using f32x2 = unsigned long long;
+__device__ __forceinline__ f32x2 pk2(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpk2(f32x2 v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // a / b: the gate projections of token i, head h at a[i * ldab + h] and
 // b[i * ldab + h]; decay / beta go to dec / beta [s][nh] (may alias a / b
 // when ldab == nh).
@@ -160,10 +181,10 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
   const int tid = threadIdx.x, g = tid % G, cl = tid / G;
   const int h = blockIdx.x, c0 = blockIdx.y * CPB, w = nh * HK;
   const size_t C = (size_t)3 * w;
-  float S[4 * M];
+  // S[j][c] of this thread's keys as pairs: S2[2 mm + e] = keys 4 (G mm + g) + 2 e, + 1
+  f32x2 S2[2 * M];
 #pragma unroll
-  for (int j = 0; j < 4 * M; j++) S[j] = 0.f;
-
+  for (int j = 0; j < 2 * M; j++) S2[j] = pk2(0.f, 0.f);
   float4 rq[QPT], rk[QPT], rv = make_float4(0.f, 0.f, 0.f, 0.f);
   float rd = 0.f, rkq = 0.f;
   auto fetch = [&](int i0) {
@@ -219,22 +240,24 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
       float r[4], pp[4];
 #pragma unroll
       for (int m = 0; m < 4; m++) {
-        float rr[4] = {0.f, 0.f, 0.f, 0.f}, qq[4] = {0.f, 0.f, 0.f, 0.f};
+        // running partials (rr[0], rr[1]) and (rr[2], rr[3]) as two pairs
+        f32x2 rr[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)}, qq[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
 #pragma unroll
         for (int mm = 0; mm < M; mm++) {
-          const float4 k4 = reinterpret_cast<const float4*>(&Ks[buf][t + m][0])[8 * mm + g];
-          const float4 q4 = reinterpret_cast<const float4*>(&Qs[buf][t + m][0])[8 * mm + g];
-          rr[0] = fmaf(S[4 * mm], k4.x, rr[0]);
-          rr[1] = fmaf(S[4 * mm + 1], k4.y, rr[1]);
-          rr[2] = fmaf(S[4 * mm + 2], k4.z, rr[2]);
-          rr[3] = fmaf(S[4 * mm + 3], k4.w, rr[3]);
-          qq[0] = fmaf(S[4 * mm], q4.x, qq[0]);
-          qq[1] = fmaf(S[4 * mm + 1], q4.y, qq[1]);
-          qq[2] = fmaf(S[4 * mm + 2], q4.z, qq[2]);
-          qq[3] = fmaf(S[4 * mm + 3], q4.w, qq[3]);
+          const ulonglong2 k4 = reinterpret_cast<const ulonglong2*>(&Ks[buf][t + m][0])[G * mm + g];
+          const ulonglong2 q4 = reinterpret_cast<const ulonglong2*>(&Qs[buf][t + m][0])[G * mm + g];
+          rr[0] = fma2(S2[2 * mm], k4.x, rr[0]);
+          rr[1] = fma2(S2[2 * mm + 1], k4.y, rr[1]);
+          qq[0] = fma2(S2[2 * mm], q4.x, qq[0]);
+          qq[1] = fma2(S2[2 * mm + 1], q4.y, qq[1]);
         }
-        r[m] = (rr[0] + rr[1]) + (rr[2] + rr[3]);
-        pp[m] = (qq[0] + qq[1]) + (qq[2] + qq[3]);
+        float a0, a1, a2, a3;
+        unpk2(rr[0], a0, a1);
+        unpk2(rr[1], a2, a3);
+        r[m] = (a0 + a1) + (a2 + a3);
+        unpk2(qq[0], a0, a1);
+        unpk2(qq[1], a2, a3);
+        pp[m] = (a0 + a1) + (a2 + a3);
       }
 #pragma unroll
       for (int o = 1; o < G; o <<= 1)
@@ -262,17 +285,17 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
       Op[t + 3][cl][g] =
           A3 * pp[3] + (l0 ? x30 * kqg[12] * d0 + x31 * kqg[13] * d1 + x32 * kqg[14] * d2 + kqg[15] * d3 : 0.f);
       // S <- A_3 S0 + x30 k0 d0 + x31 k1 d1 + x32 k2 d2 + k3 d3
-      const float w0 = x30 * d0, w1 = x31 * d1, w2 = x32 * d2;
+      const f32x2 A3p = pk2(A3, A3), w0p = pk2(x30 * d0, x30 * d0), w1p = pk2(x31 * d1, x31 * d1),
+                  w2p = pk2(x32 * d2, x32 * d2), d3p = pk2(d3, d3);
 #pragma unroll
       for (int mm = 0; mm < M; mm++) {
-        const float4 k0 = reinterpret_cast<const float4*>(&Ks[buf][t][0])[8 * mm + g];
-        const float4 k1 = reinterpret_cast<const float4*>(&Ks[buf][t + 1][0])[8 * mm + g];
-        const float4 k2 = reinterpret_cast<const float4*>(&Ks[buf][t + 2][0])[8 * mm + g];
-        const float4 k3 = reinterpret_cast<const float4*>(&Ks[buf][t + 3][0])[8 * mm + g];
-        S[4 * mm] = fmaf(k3.x, d3, fmaf(k2.x, w2, fmaf(k1.x, w1, fmaf(k0.x, w0, A3 * S[4 * mm]))));
-        S[4 * mm + 1] = fmaf(k3.y, d3, fmaf(k2.y, w2, fmaf(k1.y, w1, fmaf(k0.y, w0, A3 * S[4 * mm + 1]))));
-        S[4 * mm + 2] = fmaf(k3.z, d3, fmaf(k2.z, w2, fmaf(k1.z, w1, fmaf(k0.z, w0, A3 * S[4 * mm + 2]))));
-        S[4 * mm + 3] = fmaf(k3.w, d3, fmaf(k2.w, w2, fmaf(k1.w, w1, fmaf(k0.w, w0, A3 * S[4 * mm + 3]))));
+        const ulonglong2 k0 = reinterpret_cast<const ulonglong2*>(&Ks[buf][t][0])[G * mm + g];
+        const ulonglong2 k1 = reinterpret_cast<const ulonglong2*>(&Ks[buf][t + 1][0])[G * mm + g];
+        const ulonglong2 k2 = reinterpret_cast<const ulonglong2*>(&Ks[buf][t + 2][0])[G * mm + g];
+        const ulonglong2 k3 = reinterpret_cast<const ulonglong2*>(&Ks[buf][t + 3][0])[G * mm + g];
+        S2[2 * mm] = fma2(k3.x, d3p, fma2(k2.x, w2p, fma2(k1.x, w1p, fma2(k0.x, w0p, mul2(A3p, S2[2 * mm])))));
+        S2[2 * mm + 1] =
+            fma2(k3.y, d3p, fma2(k2.y, w2p, fma2(k1.y, w1p, fma2(k0.y, w0p, mul2(A3p, S2[2 * mm + 1])))));
       }
     }
     __syncthreads();

@@ -871,6 +871,10 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       ap.q_rows = M;
       ap.kv_rows = r.kv_pages * c.KV * PAGE;
       ap.err = r.err;
+      // the KV head's query heads share each unit, so its pages are loaded
+      // and multiplied once for the group instead of once per head (4x fewer
+      // page visits for question suffixes and option continuations)
+      ap.pack = 1;
       ProfScope ps(r, P_ATTN);
       r.launches++;
       LAYA_CK(attention(ap, st));

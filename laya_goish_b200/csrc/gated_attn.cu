@@ -168,6 +168,7 @@ cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const 
   p.gate = qgate + hd;  // the gate half of each head's [query hd | gate hd]
   p.ldg = ldqg;
   p.ghs = 2 * hd;
+  p.pack = 1;  // the query heads of a KV head share each unit
   return attention_tc(p, st);
 }
 

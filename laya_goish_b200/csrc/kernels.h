@@ -37,6 +37,10 @@ struct AttnParams {
   // optional output gate (OpenThai): o *= sigmoid(gate[row * ldg + head * ghs + c])
   const float* gate;
   int ldg, ghs;
+  // tcgen05 form: 1 = the H / KV query heads of a KV head share each unit
+  // (K/V pages loaded and multiplied once per group), 0 = one head per unit
+  // over up to 128 query rows
+  int pack;
 };
 
 // tcgen05 attention (attn_tc.cu); cudaErrorNotSupported for head dims it
