@@ -335,11 +335,16 @@ def run_ours(args):
     clk = Clocks(local).start()
     for _ in range(args.warmup):
         e.decide_batch(prompts, qs)
-    e.profile(True)
-    e.profile_read()
     clk.begin()
     dev_ms, wall, launches, h2d, d2h = timed_steps(e, prompts, qs, args.steps, dist)
     clk.end()
+    # Per-kernel CUDA events (roofline, shares) from separate untimed steps:
+    # an event between two kernels stops the second from starting early
+    # (programmatic dependent launch), so the timed steps run without them.
+    psteps = max(1, min(args.steps, 3))
+    e.profile(True)
+    e.profile_read()
+    timed_steps(e, prompts, qs, psteps, dist)
     prof = e.profile_read()
     e.profile(False)
     dev_ms, wall = reduce_max([dev_ms, wall], dist, "cuda")
@@ -348,8 +353,8 @@ def run_ours(args):
     # roofline of the dominant kernel class on this rank: the tcgen05 GEMMs
     mine = b - a
     gemm_ms = sum(v[1] for k, v in prof.items() if k.startswith("gemm_"))
-    gemm_launches = sum(v[0] for k, v in prof.items() if k.startswith("gemm_"))
-    gemm_flops = gemm_flops_per_token(CFG) * mine * TOKENS * args.steps
+    gemm_launches = sum(v[0] for k, v in prof.items() if k.startswith("gemm_")) // psteps * args.steps
+    gemm_flops = gemm_flops_per_token(CFG) * mine * TOKENS * psteps
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None
     pk, pk_kind = peaks()
     peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
@@ -373,7 +378,8 @@ def run_ours(args):
                      "traffic_unit": "bytes per GEMM launch (ncu DRAM read+write, 16-request capture x 4)",
                      "peak_kind": f"{pk_kind} bf16 dense sustained", "launches": gemm_launches,
                      "share_of_step": round(gemm_ms / rank_ms, 4) if rank_ms else None,
-                     "flops_per_step": gemm_flops / args.steps, "rank": rank},
+                     "flops_per_step": gemm_flops / psteps, "rank": rank,
+                     "timing": f"per-GEMM CUDA events over {psteps} separate profiled steps"},
         "kernel_shares": shares,
         "e2e": {"value": e2e, "unit": "req/s", "h2d_bytes_per_step": h2d // args.steps,
                 "d2h_bytes_per_step": d2h // args.steps},
@@ -482,8 +488,6 @@ def run_aux(args):
     clk = Clocks(local).start()
     for _ in range(args.warmup):
         e.decide_batch(prompts, qs)
-    e.profile(True)
-    e.profile_read()
     torch.cuda.synchronize()
     dev_ms, wall = 0.0, 0.0
     clk.begin()
@@ -495,11 +499,20 @@ def run_aux(args):
     torch.cuda.synchronize()
     clk.end()
     clk.stop()
+    # per-kernel events from separate untimed steps (they would stop the
+    # timed kernels from starting early behind their predecessors)
+    psteps = max(1, min(args.steps, 3))
+    e.profile(True)
+    e.profile_read()
+    prof_ms = 0.0
+    for _ in range(psteps):
+        e.decide_batch(prompts, qs)
+        prof_ms += e.timing()["device_ms"]
     prof = e.profile_read()
     e.close()
     gemm_ms = sum(v[1] for k, v in prof.items() if k.startswith("gemm_") and k != "gemm_head")
     tok = requests * (tokens + branch_tokens)
-    gemm_flops = gemm_flops_per_token(cfg) * tok * args.steps
+    gemm_flops = gemm_flops_per_token(cfg) * tok * psteps  # over the profiled steps
     pk, pk_kind = peaks()
     step_ms = dev_ms / args.steps
     wbytes = os.path.getsize(path)  # every weight byte is read at least once per step
@@ -515,7 +528,8 @@ def run_aux(args):
         "weight_bytes": wbytes,
         "peak_kind": pk_kind,
         "e2e_req_s": requests * args.steps / (wall / 1000.0),
-        "kernel_shares": {k: round(v[1] / dev_ms, 4) for k, v in sorted(prof.items())} if dev_ms else {},
+        "kernel_shares": {k: round(v[1] / prof_ms, 4) for k, v in sorted(prof.items())} if prof_ms else {},
+        "profiled_ms_per_step": prof_ms / psteps,
         "clocks": clk.summary(),
     }
     if not args.no_cpu_baseline:
@@ -541,14 +555,17 @@ def run_decode(args):
     ctxs = [synth.token_ids(rng, CFG.vocab, args.ctx) for _ in range(args.batch)]
     e = engine.Engine(path, devices=[local])
     e.decode(ctxs[:1], 4)  # warm-up
-    e.profile(True)
-    e.profile_read()
     clk = Clocks(local).start()
     clk.begin()
     toks, st = e.decode(ctxs, args.gen)
     clk.end()
     clk.stop()
     t = e.timing()
+    # per-kernel CUDA events of one step from a separate short decode (events
+    # between kernels would stop the timed ones from starting early)
+    e.profile(True)
+    e.profile_read()
+    e.decode(ctxs, 2)
     prof = e.profile_read()
     e.close()
     steps = args.gen - 1

@@ -34,6 +34,7 @@ def test_full_config_decide_matches_oracle(full):
     want = o.decide(prompt, kind_i, opts, suf)
     o.close()
     p, w = np.array(got["probabilities"]), np.array(want["probabilities"])
+    print(f"[parity] {cfg} full-size request: max |dp| = {np.abs(p - w).max():.3e}")
     assert np.allclose(p, w, atol=1e-3, rtol=1e-2), (p, w)
     if kind == "choice":
         assert got["choice"] == want["choice"]
