@@ -802,7 +802,12 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
   const bool ks_on = !(ke && ke[0] == '0');
   const int ks_o = ks_on ? gemm_ksplit(M, d, qd, r.num_sms) : 1;
   const int ks_d = ks_on ? gemm_ksplit(M, d, ffn, r.num_sms) : 1;
-  if (std::max(ks_o, ks_d) > 1 && (rc = r.kpart.ensure((size_t)std::max(ks_o, ks_d) * M * d * 4))) return rc;
+  // the QKV GEMM splits K the same way when it has few tiles; its partial
+  // planes (consumed by qkv_merge before the attention) share the buffer
+  const int nqkv = qd + 2 * kd;
+  const int ks_q = ks_on ? gemm_ksplit(M, nqkv, d, r.num_sms) : 1;
+  const size_t kpart_f = std::max((size_t)std::max(ks_o, ks_d) * M * d, (size_t)ks_q * M * nqkv);
+  if (std::max(std::max(ks_o, ks_d), ks_q) > 1 && (rc = r.kpart.ensure(kpart_f * 4))) return rc;
   int pend = 0;  // K splits of x not yet merged (the gathered final norm merges without writing x back)
   auto norm = [&](const int* rows, int n, const float* w, half* o16, float* o32) -> cudaError_t {
     r.launches++;
@@ -852,7 +857,23 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     a.kcache = r.kc.as<half>() + l * layer_elems;
     a.vcache = r.vc.as<half>() + l * layer_elems;
     a.page_size = PAGE;
-    if ((rc = gemm(r, P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
+    if (ks_q > 1) {
+      // raw partial sums of each K split, then bias / RoPE / q rows / KV cache
+      GemmArgs sp{};
+      sp.M = M;
+      sp.N = nqkv;
+      sp.K = d;
+      sp.ldo = nqkv;
+      sp.ksplit = ks_q;
+      sp.part = r.kpart.as<float>();
+      if ((rc = gemm(r, P_GEMM_QKV, EPI_RESID, h, d, wqkv, d, sp))) return rc;
+      ProfScope ps(r, P_GEMM_QKV);
+      r.launches++;
+      LAYA_CK(qkv_merge(r.kpart.as<float>(), ks_q, (size_t)M * nqkv, M, L.bqkv, qd, kd, c.hd, c.KV, a.pos, a.slot,
+                        r.rope, PAGE, r.qb.as<half>(), qd, a.kcache, a.vcache, st, gemm_pdl()));
+    } else if ((rc = gemm(r, P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) {
+      return rc;
+    }
     {
       AttnParams ap{};
       ap.q = r.qb.as<half>();

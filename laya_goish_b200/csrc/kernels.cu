@@ -132,6 +132,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __device__ __forceinline__ float4 merged_row4(const float* x, const float* part, int nsplit, size_t split_stride,
                                               size_t off) {
   float4 v = *reinterpret_cast<const float4*>(x + off);
+  // unrolled so several planes' loads are in flight; the adds keep split order
+#pragma unroll 4
   for (int s = 0; s < nsplit; s++) {
     const float4 p = *reinterpret_cast<const float4*>(part + s * split_stride + off);
     v.x += p.x;
@@ -279,6 +281,94 @@ cudaError_t rmsnorm(const float* x, const int* rows, int nrows, const float* w, 
   }
   return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, const_cast<float*>(x), rows, w, d, eps, out16,
                   out32, (const float*)nullptr, 0, (size_t)0);
+}
+
+// The QKV epilogue of a QKV GEMM split over K (few output tiles): x =
+// part[0] + ... + part[nsplit-1] (planes split_stride floats apart, rows of
+// n = qd + 2 kd) + bias, then rotate-half RoPE on the q and k heads
+// (src/tensor.rs:158-171, the (cos, sin) table of the fused epilogue), q ->
+// F16 rows q[m * ldq + c], k / v -> the paged KV cache at slot[m].  One CTA
+// per token row; a thread takes four (j, j + hd/2) pairs of a q / k head or
+// four v columns, as 16-byte loads from every plane.
+__device__ __forceinline__ float4 qkv_sum4(const float* row, int nsplit, size_t split_stride, const float* bias,
+                                           int c) {
+  float4 x = *reinterpret_cast<const float4*>(row + c);
+#pragma unroll 4
+  for (int s2 = 1; s2 < nsplit; s2++) {
+    const float4 y = *reinterpret_cast<const float4*>(row + (size_t)s2 * split_stride + c);
+    x.x += y.x;
+    x.y += y.y;
+    x.z += y.z;
+    x.w += y.w;
+  }
+  if (bias) {
+    const float4 b = *reinterpret_cast<const float4*>(bias + c);
+    x.x += b.x;
+    x.y += b.y;
+    x.z += b.z;
+    x.w += b.w;
+  }
+  return x;
+}
+
+__global__ void qkv_merge_kernel(const float* __restrict__ part, int nsplit, size_t split_stride,
+                                 const float* __restrict__ bias, int qd, int kd, int hd, int kvh,
+                                 const int* __restrict__ pos, const int* __restrict__ slot,
+                                 const float2* __restrict__ rope, int page_size, half* __restrict__ q, int ldq,
+                                 half* __restrict__ kc, half* __restrict__ vc) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x, n = qd + 2 * kd, half_hd = hd / 2;
+  const float* row = part + (size_t)m * n;
+  const int p = pos[m], sl = slot[m];
+  const int page = sl / page_size, off = sl % page_size;
+  const int nrot = (qd + kd) / 8, nv = kd / 4;  // four-pair groups of q / k, four-column groups of v
+  for (int i = threadIdx.x; i < nrot + nv; i += blockDim.x) {
+    if (i < nrot) {
+      const bool isq = i < qd / 8;
+      const int j = 4 * (isq ? i : i - qd / 8);  // first of four pairs
+      const int head = j / half_hd, jj = j % half_hd;
+      const int c0 = (isq ? 0 : qd) + head * hd + jj, c1 = c0 + half_hd;
+      const float4 a = qkv_sum4(row, nsplit, split_stride, bias, c0);
+      const float4 b = qkv_sum4(row, nsplit, split_stride, bias, c1);
+      const float4* cs4 = reinterpret_cast<const float4*>(rope + (size_t)p * half_hd + jj);
+      const float4 t0 = cs4[0], t1 = cs4[1];  // (cos, sin) of pairs jj .. jj + 3
+      const float xa[4] = {a.x, a.y, a.z, a.w}, xb[4] = {b.x, b.y, b.z, b.w};
+      const float co[4] = {t0.x, t0.z, t1.x, t1.z}, si[4] = {t0.y, t0.w, t1.y, t1.w};
+      __align__(8) half y0[4], y1[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        y0[e] = __float2half_rn(xa[e] * co[e] - xb[e] * si[e]);
+        y1[e] = __float2half_rn(xb[e] * co[e] + xa[e] * si[e]);
+      }
+      half* dst = isq ? q + (size_t)m * ldq + c0 - jj
+                      : kc + (((size_t)page * kvh + head) * page_size + off) * hd;
+      *reinterpret_cast<uint2*>(dst + jj) = *reinterpret_cast<const uint2*>(y0);
+      *reinterpret_cast<uint2*>(dst + jj + half_hd) = *reinterpret_cast<const uint2*>(y1);
+    } else {
+      const int j = 4 * (i - nrot), c = qd + kd + j;
+      const int head = j / hd, jj = j % hd;
+      const float4 v = qkv_sum4(row, nsplit, split_stride, bias, c);
+      __align__(8) half y[4] = {__float2half_rn(v.x), __float2half_rn(v.y), __float2half_rn(v.z),
+                                __float2half_rn(v.w)};
+      *reinterpret_cast<uint2*>(vc + (((size_t)page * kvh + head) * page_size + off) * hd + jj) =
+          *reinterpret_cast<const uint2*>(y);
+    }
+  }
+}
+
+cudaError_t qkv_merge(const float* part, int nsplit, size_t split_stride, int M, const float* bias, int qd, int kd,
+                      int hd, int kvh, const int* pos, const int* slot, const float2* rope, int page_size, half* q,
+                      int ldq, half* kc, half* vc, cudaStream_t st, bool pdl) {
+  if (M <= 0) return cudaSuccess;
+  // 16-byte loads of the planes and 8-byte stores: rows, bias and the
+  // (cos, sin) table in four-column steps
+  if (hd % 8 || qd % 8 || kd % 8 || (split_stride % 4) || (ldq % 4) ||
+      (reinterpret_cast<uintptr_t>(part) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15) ||
+      (reinterpret_cast<uintptr_t>(rope) & 15))
+    return cudaErrorInvalidValue;
+  return launch_k(qkv_merge_kernel, dim3(M), dim3(128), 0, st, pdl, part, nsplit, split_stride, bias, qd, kd, hd, kvh,
+                  pos, slot, rope, page_size, q, ldq, kc, vc);
 }
 
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,

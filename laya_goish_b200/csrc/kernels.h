@@ -90,6 +90,11 @@ cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const 
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st,
                           bool pdl = false);
+// The QKV epilogue (bias, RoPE, q rows, paged K/V) of a QKV GEMM whose K
+// was split: part holds nsplit planes [M][qd + 2 kd], split_stride floats apart.
+cudaError_t qkv_merge(const float* part, int nsplit, size_t split_stride, int M, const float* bias, int qd, int kd,
+                      int hd, int kvh, const int* pos, const int* slot, const float2* rope, int page_size, half* q,
+                      int ldq, half* kc, half* vc, cudaStream_t st, bool pdl = false);
 cudaError_t head_restricted(const QTensor& w, const float* hid, const int* cand, const int* row_of, int n, float* out,
                             cudaStream_t st);
 cudaError_t lse_rows(const float* logits, int V, int n, float* out, cudaStream_t st);
