@@ -327,34 +327,48 @@ __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldraw, const
   out[e] = acc / (1.f + expf(-acc));
 }
 
-// The same on four channels per thread with 16-byte loads and stores (raw
-// and out 16-byte aligned, ldraw and C multiples of 4): grid.y = token,
-// grid.x over channel quads; the four taps of each channel are one float4.
-__global__ void conv_silu4_kernel(const float* __restrict__ raw, int ldraw, const float* __restrict__ conv, int C,
-                                  float* __restrict__ out) {
-  const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x), i = blockIdx.y;
+// The same on four channels x eight consecutive tokens per thread with
+// 16-byte loads and stores (raw and out 16-byte aligned, ldraw and C
+// multiples of 4): the eleven input rows of the window are loaded once,
+// the four taps of each channel are one float4.  grid.y = token block.
+__global__ void conv_silu4_kernel(const float* __restrict__ raw, int ldraw, const float* __restrict__ conv, int s,
+                                  int C, float* __restrict__ out) {
+  constexpr int TT = 8;  // tokens per thread
+  const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x), i0 = blockIdx.y * TT;
   if (c >= C) return;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float4 w[4];
 #pragma unroll
   for (int u = 0; u < 4; u++) w[u] = __ldg(reinterpret_cast<const float4*>(conv + (size_t)(c + u) * 4));
+  float4 x[TT + 3];
 #pragma unroll
-  for (int j = 0; j < 4; j++) {
-    if (i + j < 3) continue;
-    const float4 x = __ldg(reinterpret_cast<const float4*>(raw + (size_t)(i + j - 3) * ldraw + c));
-    const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const float wj = j == 0 ? w[u].x : j == 1 ? w[u].y : j == 2 ? w[u].z : w[u].w;
-      acc[u] += xs[u] * wj;
-    }
+  for (int r = 0; r < TT + 3; r++) {
+    const int i = i0 + r - 3;
+    x[r] = (i >= 0 && i < s) ? __ldg(reinterpret_cast<const float4*>(raw + (size_t)i * ldraw + c))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float4 r;
-  r.x = acc[0] / (1.f + expf(-acc[0]));
-  r.y = acc[1] / (1.f + expf(-acc[1]));
-  r.z = acc[2] / (1.f + expf(-acc[2]));
-  r.w = acc[3] / (1.f + expf(-acc[3]));
-  *reinterpret_cast<float4*>(out + (size_t)i * C + c) = r;
+#pragma unroll
+  for (int t = 0; t < TT; t++) {
+    const int i = i0 + t;
+    if (i >= s) break;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (i + j < 3) continue;  // terms before token 0 are left out
+      const float4 xv = x[t + j];
+      const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float wj = j == 0 ? w[u].x : j == 1 ? w[u].y : j == 2 ? w[u].z : w[u].w;
+        acc[u] += xs[u] * wj;
+      }
+    }
+    float4 r;
+    r.x = acc[0] / (1.f + expf(-acc[0]));
+    r.y = acc[1] / (1.f + expf(-acc[1]));
+    r.z = acc[2] / (1.f + expf(-acc[2]));
+    r.w = acc[3] / (1.f + expf(-acc[3]));
+    *reinterpret_cast<float4*>(out + (size_t)i * C + c) = r;
+  }
 }
 
 // Per-head RMSNorm (weight offset 0, eps 1e-6) of the recurrence output,
@@ -400,9 +414,9 @@ cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int l
   float* beta = dec + (size_t)s * nh;
   float* kq = beta + (size_t)s * nh;
   if (ldraw % 4 == 0 && (reinterpret_cast<uintptr_t>(raw) & 15) == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
-      s <= 65535)
-    conv_silu4_kernel<<<dim3((unsigned)((C / 4 + 127) / 128), (unsigned)s), 128, 0, st>>>(raw, ldraw, conv, (int)C,
-                                                                                          qkv);
+      (s + 7) / 8 <= 65535)
+    conv_silu4_kernel<<<dim3((unsigned)((C / 4 + 127) / 128), (unsigned)((s + 7) / 8)), 128, 0, st>>>(
+        raw, ldraw, conv, s, (int)C, qkv);
   else
     conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, ldraw, conv, s, (int)C, qkv);
   cudaError_t e = gated_delta(qkv, a, b, ldab, dt, alog, s, nh, hk, dec, beta, kq, out, st);

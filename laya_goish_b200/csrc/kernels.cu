@@ -323,7 +323,8 @@ __global__ void qkv_merge_kernel(const float* __restrict__ part, int nsplit, siz
   const int p = pos[m], sl = slot[m];
   const int page = sl / page_size, off = sl % page_size;
   const int nrot = (qd + kd) / 8, nv = kd / 4;  // four-pair groups of q / k, four-column groups of v
-  for (int i = threadIdx.x; i < nrot + nv; i += blockDim.x) {
+  // grid.y CTAs share a row, so many rows' loads are in flight at once
+  for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < nrot + nv; i += gridDim.y * blockDim.x) {
     if (i < nrot) {
       const bool isq = i < qd / 8;
       const int j = 4 * (isq ? i : i - qd / 8);  // first of four pairs
@@ -367,7 +368,9 @@ cudaError_t qkv_merge(const float* part, int nsplit, size_t split_stride, int M,
       (reinterpret_cast<uintptr_t>(part) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15) ||
       (reinterpret_cast<uintptr_t>(rope) & 15))
     return cudaErrorInvalidValue;
-  return launch_k(qkv_merge_kernel, dim3(M), dim3(128), 0, st, pdl, part, nsplit, split_stride, bias, qd, kd, hd, kvh,
+  const int groups = (qd + kd) / 8 + kd / 4;  // work items of one row
+  return launch_k(qkv_merge_kernel, dim3(M, (groups + 63) / 64), dim3(64), 0, st, pdl, part, nsplit, split_stride,
+                  bias, qd, kd, hd, kvh,
                   pos, slot, rope, page_size, q, ldq, kc, vc);
 }
 
