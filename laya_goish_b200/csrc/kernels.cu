@@ -1,5 +1,6 @@
 // Memory-bound kernels of the decision hot path and the paged causal GQA
 // attention.  Each cites the reference function it replaces.
+#include <algorithm>
 #include <atomic>
 #include <cfloat>
 #include <cstdlib>
@@ -377,7 +378,10 @@ cudaError_t qkv_merge(const float* part, int nsplit, size_t split_stride, int M,
 cudaError_t rmsnorm_merge(float* x, const int* rows, int nrows, const float* part, int nsplit, size_t split_stride,
                           const float* w, int d, float eps, half* out16, float* out32, cudaStream_t st, bool pdl) {
   if (!nrows) return cudaSuccess;
-  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(256), 0, st, pdl, x, rows, w, d, eps, out16, out32, part,
+  // one float4 of the row per thread (up to 1024 threads): every plane's
+  // load of a column is in flight at once across the row
+  const int threads = std::min(1024, std::max(128, (d / 4 + 31) / 32 * 32));
+  return launch_k(rmsnorm_kernel, dim3(nrows), dim3(threads), 0, st, pdl, x, rows, w, d, eps, out16, out32, part,
                   part ? nsplit : 0, split_stride);
 }
 
