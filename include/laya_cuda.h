@@ -184,6 +184,15 @@ int laya_openthai_open_memory(const uint8_t* gguf, size_t len, int device, const
  * the given positions -> out [npos][slots] (host buffers). */
 int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int32_t* positions, int npos,
                           float* out);
+/* Several passes in one forward (the permutation passes of a request,
+ * src/models/openthai/decision.rs:258-262, which the reference runs one at a
+ * time): nseq (1..256) sequences of lens[i] tokens concatenated in ids, each
+ * causal on its own; positions index the concatenated rows -> out
+ * [npos][slots].  Row-wise work (norms, projections, MLP, head) runs once
+ * over all rows; each sequence's DeltaNet recurrence runs on its own stream,
+ * so the sequences' recurrences overlap. */
+int laya_openthai_forward_batch(laya_ot_model* m, const int32_t* ids, const int32_t* lens, int nseq,
+                                const int32_t* positions, int npos, float* out);
 void laya_openthai_close(laya_ot_model* m);
 /* Decodes a weight tensor of the model from its device layout back to F32
  * (for parity checks of the upload transcoding).  out: element count floats. */

@@ -113,6 +113,7 @@ def lib() -> ctypes.CDLL:
     L.laya_openthai_open.argtypes = [ctypes.c_char_p, I, ctypes.POINTER(OtConfig), ctypes.POINTER(P)]
     L.laya_openthai_open_memory.argtypes = [P, SZ, I, ctypes.POINTER(OtConfig), ctypes.POINTER(P)]
     L.laya_openthai_forward.argtypes = [P, P, I, P, I, P]
+    L.laya_openthai_forward_batch.argtypes = [P, P, P, I, P, I, P]
     L.laya_openthai_close.argtypes = [P]
     L.laya_openthai_close.restype = None
     _lib = L

@@ -50,6 +50,11 @@ struct laya_ot_model {
   std::vector<void*> allocs;
   // forward scratch, grown on demand and kept between passes
   laya::DevBuf dids, dpos, x, h, big, att, att16, act, logits, gscr, kpart;
+  // several sequences per forward: each one's DeltaNet mixer runs on a side
+  // stream, so the token-sequential recurrences of the sequences overlap
+  static constexpr int kSide = 4;
+  cudaStream_t side[kSide] = {};
+  cudaEvent_t fork = nullptr, join[kSide] = {};
   std::mutex mu;
 };
 
@@ -277,6 +282,148 @@ int open_parsed(const Gguf& g, int device, const laya_ot_config& c, laya_ot_mode
 }  // namespace
 }  // namespace laya
 
+namespace laya {
+namespace {
+
+// The forward of nseq sequences of lens[i] tokens, concatenated in ids;
+// positions index the concatenated rows.  Every row-wise step (norms,
+// projections, MLP, head) runs once over all rows; the sequence mixers run
+// per sequence (causal within it).
+int forward_seqs(laya_ot_model* m, const int32_t* ids, const int* lens, int nseq, const int32_t* positions, int npos,
+                 float* out) {
+  const laya_ot_config& c = m->cfg;
+  int s = 0;
+  for (int i = 0; i < nseq; i++) {
+    if (lens[i] < 1) return fail(LAYA_E_INVALID, "invalid forward arguments");
+    s += lens[i];
+  }
+  for (int i = 0; i < s; i++)
+    if (ids[i] < 0 || ids[i] >= c.vocab) return fail(LAYA_E_INVALID, "invalid OpenThai token sequence");
+  for (int i = 0; i < npos; i++)
+    if (positions[i] < 0 || positions[i] >= s) return fail(LAYA_E_INVALID, "invalid OpenThai token sequence");
+  LAYA_CK(cudaSetDevice(m->device));
+  LAYA_CK(cudaMemsetAsync(m->err, 0, 4, m->st));
+  const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
+  const int w = nh * hk, qd = H * hd, ffn = c.ffn;
+  const size_t S = (size_t)s;
+  DevBuf &dids = m->dids, &dpos = m->dpos, &x = m->x, &h = m->h, &big = m->big,
+         &att = m->att, &att16 = m->att16, &act = m->act, &logits = m->logits;
+  // big: the stacked projection output of either layer kind, then each
+  // sequence's DeltaNet mixer scratch (16-byte aligned)
+  const int nfull = 2 * qd + 2 * KV * hd, ndelta = 4 * w + 2 * nh;
+  const size_t pw = ((size_t)std::max(nfull, ndelta) + 63) / 64 * 64;
+  std::vector<size_t> scr_off(nseq);
+  size_t scr_f = 0, gscr_b = 16;
+  for (int i = 0; i < nseq; i++) {
+    scr_off[i] = scr_f;
+    scr_f += (gated_delta_mixer_scratch(lens[i], nh, hk) / 4 + 63) / 64 * 64;
+    gscr_b = std::max(gscr_b, gated_attention_scratch(lens[i], H, KV, hd));
+  }
+  const size_t bigf = S * pw + scr_f + 64;
+  int rc;
+  if ((rc = dids.ensure(S * 4)) || (rc = dpos.ensure((size_t)npos * 4)) || (rc = x.ensure(S * d * 4)) ||
+      (rc = h.ensure(std::max(S, (size_t)npos) * d * 2)) || (rc = big.ensure(bigf * 4)) ||
+      (rc = att.ensure(S * std::max(qd, w) * 4)) ||
+      (rc = att16.ensure(S * std::max(qd, w) * 2)) || (rc = act.ensure(S * ffn * 2)) ||
+      (rc = logits.ensure((size_t)npos * c.slots * 4)) || (rc = m->gscr.ensure(gscr_b)))
+    return rc;
+  if (nseq > 1 && !m->fork) {
+    LAYA_CK(cudaEventCreateWithFlags(&m->fork, cudaEventDisableTiming));
+    for (int i = 0; i < laya_ot_model::kSide; i++) {
+      LAYA_CK(cudaStreamCreateWithFlags(&m->side[i], cudaStreamNonBlocking));
+      LAYA_CK(cudaEventCreateWithFlags(&m->join[i], cudaEventDisableTiming));
+    }
+  }
+  // Residual GEMMs with few output tiles split K (as in the decoder forward);
+  // the RMSNorm that next reads the residual adds the planes in split order.
+  const char* ke = std::getenv("LAYA_KSPLIT");
+  const bool ks_on = !(ke && ke[0] == '0');
+  const int ks_full = ks_on ? gemm_ksplit(s, d, qd, m->num_sms) : 1;
+  const int ks_delta = ks_on ? gemm_ksplit(s, d, w, m->num_sms) : 1;
+  const int ks_down = ks_on ? gemm_ksplit(s, d, ffn, m->num_sms) : 1;
+  const int ks_max = std::max(std::max(ks_full, ks_delta), ks_down);
+  if (ks_max > 1 && (rc = m->kpart.ensure((size_t)ks_max * S * d * 4))) return rc;
+  float* PART = ks_max > 1 ? m->kpart.as<float>() : nullptr;
+  int pend = 0;  // K splits of X not yet merged
+  auto norm = [&](const int* rows, int n, const float* wn) -> cudaError_t {
+    const int ns = pend;
+    pend = 0;
+    if (ns > 1)
+      return rmsnorm_merge(x.as<float>(), rows, n, PART, ns, S * d, wn, d, c.eps, h.as<half>(), nullptr, m->st,
+                           gemm_pdl());
+    return rmsnorm(x.as<float>(), rows, n, wn, d, c.eps, h.as<half>(), nullptr, m->st, gemm_pdl(), m->err);
+  };
+  cudaStream_t st = m->st;
+  LAYA_CK(cudaMemcpyAsync(dids.p, ids, S * 4, cudaMemcpyHostToDevice, st));
+  LAYA_CK(cudaMemcpyAsync(dpos.p, positions, (size_t)npos * 4, cudaMemcpyHostToDevice, st));
+  float* X = x.as<float>();
+  half* Hh = h.as<half>();
+  float* P = big.as<float>();  // stacked projection outputs, rows of nfull / ndelta
+  float* SCR = P + S * pw;     // DeltaNet mixer scratch, one region per sequence
+  LAYA_CK(rows_f32(m->embd, dids.as<int>(), s, X, st));
+  for (int l = 0; l < c.n_layers; l++) {
+    const OtLayer& L = m->layers[l];
+    LAYA_CK(norm(nullptr, s, L.n1));
+    if (L.full) {
+      // one GEMM: rows [q | gate per head] (2 qd), k (KV hd), v (KV hd)
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.q, nfull, d, s, P, nfull, nullptr, nullptr))) return rc;
+      for (int i = 0, r0 = 0; i < nseq; r0 += lens[i], i++) {
+        const float* Pi = P + (size_t)r0 * nfull;
+        LAYA_CK(gated_attention(Pi, nfull, Pi + 2 * qd, Pi + 2 * qd + KV * hd, nfull, L.qn, L.kn, lens[i], H, KV, hd,
+                                c.rot, c.theta, m->gscr.p, att16.as<half>() + (size_t)r0 * qd, m->err, st));
+      }
+      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr, ks_full, PART)))
+        return rc;
+      pend = ks_full;
+    } else {
+      // one GEMM: rows in_proj_qkv (3w), z (w), a (nh), b (nh)
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, ndelta, d, s, P, ndelta, nullptr, nullptr))) return rc;
+      // the mixer writes its normalised, gated rows as F16 straight into
+      // the output projection's operand; with several sequences each one's
+      // mixer runs on a side stream (fork after the projection, join before
+      // the output projection)
+      if (nseq > 1) LAYA_CK(cudaEventRecord(m->fork, st));
+      for (int i = 0, r0 = 0; i < nseq; r0 += lens[i], i++) {
+        cudaStream_t ms = st;
+        if (nseq > 1) {
+          ms = m->side[i % laya_ot_model::kSide];
+          LAYA_CK(cudaStreamWaitEvent(ms, m->fork, 0));
+        }
+        const float* Pi = P + (size_t)r0 * ndelta;
+        LAYA_CK(gated_delta_mixer(Pi, ndelta, Pi + 3 * w, ndelta, Pi + 4 * w, Pi + 4 * w + nh, ndelta, L.conv, L.dt,
+                                  L.alog, L.normw, lens[i], nh, hk, SCR + scr_off[i],
+                                  att.as<float>() + (size_t)r0 * w, att16.as<half>() + (size_t)r0 * w, ms));
+      }
+      if (nseq > 1)
+        for (int k = 0; k < std::min(nseq, laya_ot_model::kSide); k++) {
+          LAYA_CK(cudaEventRecord(m->join[k], m->side[k]));
+          LAYA_CK(cudaStreamWaitEvent(st, m->join[k], 0));
+        }
+      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), w, L.out, d, w, s, nullptr, d, X, nullptr, ks_delta, PART)))
+        return rc;
+      pend = ks_delta;
+    }
+    LAYA_CK(norm(nullptr, s, L.n2));
+    if ((rc = gemm(*m, EPI_SWIGLU, Hh, d, L.gu, 2 * ffn, d, s, act.p, ffn, nullptr, nullptr)) ||
+        (rc = gemm(*m, EPI_RESID, act.as<half>(), ffn, L.down, d, ffn, s, nullptr, d, X, nullptr, ks_down, PART)))
+      return rc;
+    pend = ks_down;
+  }
+  LAYA_CK(norm(dpos.as<int>(), npos, m->norm));
+  if ((rc = gemm(*m, EPI_F32, Hh, d, m->head, c.slots, d, npos, logits.p, c.slots, nullptr, m->head_bias))) return rc;
+  LAYA_CK(cudaMemcpyAsync(out, logits.p, (size_t)npos * c.slots * 4, cudaMemcpyDeviceToHost, st));
+  LAYA_CK(cudaStreamSynchronize(st));
+  unsigned err = 0;
+  LAYA_CK(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost));
+  if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");
+  for (size_t i = 0; i < (size_t)npos * c.slots; i++)
+    if (!std::isfinite(out[i])) return fail(LAYA_E_NONFINITE, "non-finite model output");
+  return 0;
+}
+
+}  // namespace
+}  // namespace laya
+
 using namespace laya;
 
 extern "C" {
@@ -306,96 +453,15 @@ int laya_openthai_forward(laya_ot_model* m, const int32_t* ids, int s, const int
                           float* out) {
   if (!m || !ids || !positions || !out || s < 1 || npos < 1) return fail(LAYA_E_INVALID, "invalid forward arguments");
   std::lock_guard<std::mutex> lk(m->mu);
-  const laya_ot_config& c = m->cfg;
-  for (int i = 0; i < s; i++)
-    if (ids[i] < 0 || ids[i] >= c.vocab) return fail(LAYA_E_INVALID, "invalid OpenThai token sequence");
-  for (int i = 0; i < npos; i++)
-    if (positions[i] < 0 || positions[i] >= s) return fail(LAYA_E_INVALID, "invalid OpenThai token sequence");
-  LAYA_CK(cudaSetDevice(m->device));
-  LAYA_CK(cudaMemsetAsync(m->err, 0, 4, m->st));
-  const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
-  const int w = nh * hk, qd = H * hd, ffn = c.ffn;
-  const size_t S = (size_t)s;
-  DevBuf &dids = m->dids, &dpos = m->dpos, &x = m->x, &h = m->h, &big = m->big,
-         &att = m->att, &att16 = m->att16, &act = m->act, &logits = m->logits;
-  // big: the stacked projection output of either layer kind, then the
-  // DeltaNet mixer's scratch
-  const int nfull = 2 * qd + 2 * KV * hd, ndelta = 4 * w + 2 * nh;
-  const size_t pw = ((size_t)std::max(nfull, ndelta) + 63) / 64 * 64;
-  const size_t bigf = S * pw + gated_delta_mixer_scratch(s, nh, hk) / 4 + 64;
-  int rc;
-  if ((rc = dids.ensure(S * 4)) || (rc = dpos.ensure((size_t)npos * 4)) || (rc = x.ensure(S * d * 4)) ||
-      (rc = h.ensure(std::max(S, (size_t)npos) * d * 2)) || (rc = big.ensure(bigf * 4)) ||
-      (rc = att.ensure(S * std::max(qd, w) * 4)) ||
-      (rc = att16.ensure(S * std::max(qd, w) * 2)) || (rc = act.ensure(S * ffn * 2)) ||
-      (rc = logits.ensure((size_t)npos * c.slots * 4)) ||
-      (rc = m->gscr.ensure(std::max<size_t>(16, gated_attention_scratch(s, H, KV, hd)))))
-    return rc;
-  // Residual GEMMs with few output tiles split K (as in the decoder forward);
-  // the RMSNorm that next reads the residual adds the planes in split order.
-  const char* ke = std::getenv("LAYA_KSPLIT");
-  const bool ks_on = !(ke && ke[0] == '0');
-  const int ks_full = ks_on ? gemm_ksplit(s, d, qd, m->num_sms) : 1;
-  const int ks_delta = ks_on ? gemm_ksplit(s, d, w, m->num_sms) : 1;
-  const int ks_down = ks_on ? gemm_ksplit(s, d, ffn, m->num_sms) : 1;
-  const int ks_max = std::max(std::max(ks_full, ks_delta), ks_down);
-  if (ks_max > 1 && (rc = m->kpart.ensure((size_t)ks_max * S * d * 4))) return rc;
-  float* PART = ks_max > 1 ? m->kpart.as<float>() : nullptr;
-  int pend = 0;  // K splits of X not yet merged
-  auto norm = [&](const int* rows, int n, const float* wn) -> cudaError_t {
-    const int ns = pend;
-    pend = 0;
-    if (ns > 1)
-      return rmsnorm_merge(x.as<float>(), rows, n, PART, ns, S * d, wn, d, c.eps, h.as<half>(), nullptr, m->st,
-                           gemm_pdl());
-    return rmsnorm(x.as<float>(), rows, n, wn, d, c.eps, h.as<half>(), nullptr, m->st, gemm_pdl(), m->err);
-  };
-  cudaStream_t st = m->st;
-  LAYA_CK(cudaMemcpyAsync(dids.p, ids, S * 4, cudaMemcpyHostToDevice, st));
-  LAYA_CK(cudaMemcpyAsync(dpos.p, positions, (size_t)npos * 4, cudaMemcpyHostToDevice, st));
-  float* X = x.as<float>();
-  half* Hh = h.as<half>();
-  float* P = big.as<float>();  // stacked projection outputs, rows of nfull / ndelta
-  float* SCR = P + S * pw;     // DeltaNet mixer scratch
-  LAYA_CK(rows_f32(m->embd, dids.as<int>(), s, X, st));
-  for (int l = 0; l < c.n_layers; l++) {
-    const OtLayer& L = m->layers[l];
-    LAYA_CK(norm(nullptr, s, L.n1));
-    if (L.full) {
-      // one GEMM: rows [q | gate per head] (2 qd), k (KV hd), v (KV hd)
-      if ((rc = gemm(*m, EPI_F32, Hh, d, L.q, nfull, d, s, P, nfull, nullptr, nullptr))) return rc;
-      LAYA_CK(gated_attention(P, nfull, P + 2 * qd, P + 2 * qd + KV * hd, nfull, L.qn, L.kn, s, H, KV, hd, c.rot,
-                              c.theta, m->gscr.p, att16.as<half>(), m->err, st));
-      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), qd, L.o, d, qd, s, nullptr, d, X, nullptr, ks_full, PART)))
-        return rc;
-      pend = ks_full;
-    } else {
-      // one GEMM: rows in_proj_qkv (3w), z (w), a (nh), b (nh)
-      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, ndelta, d, s, P, ndelta, nullptr, nullptr))) return rc;
-      // the mixer writes its normalised, gated rows as F16 straight into
-      // the output projection's operand
-      LAYA_CK(gated_delta_mixer(P, ndelta, P + 3 * w, ndelta, P + 4 * w, P + 4 * w + nh, ndelta, L.conv, L.dt, L.alog,
-                                L.normw, s, nh, hk, SCR, att.as<float>(), att16.as<half>(), st));
-      if ((rc = gemm(*m, EPI_RESID, att16.as<half>(), w, L.out, d, w, s, nullptr, d, X, nullptr, ks_delta, PART)))
-        return rc;
-      pend = ks_delta;
-    }
-    LAYA_CK(norm(nullptr, s, L.n2));
-    if ((rc = gemm(*m, EPI_SWIGLU, Hh, d, L.gu, 2 * ffn, d, s, act.p, ffn, nullptr, nullptr)) ||
-        (rc = gemm(*m, EPI_RESID, act.as<half>(), ffn, L.down, d, ffn, s, nullptr, d, X, nullptr, ks_down, PART)))
-      return rc;
-    pend = ks_down;
-  }
-  LAYA_CK(norm(dpos.as<int>(), npos, m->norm));
-  if ((rc = gemm(*m, EPI_F32, Hh, d, m->head, c.slots, d, npos, logits.p, c.slots, nullptr, m->head_bias))) return rc;
-  LAYA_CK(cudaMemcpyAsync(out, logits.p, (size_t)npos * c.slots * 4, cudaMemcpyDeviceToHost, st));
-  LAYA_CK(cudaStreamSynchronize(st));
-  unsigned err = 0;
-  LAYA_CK(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost));
-  if (err) return fail(LAYA_E_TIMEOUT, "a device-side wait ran out of its budget");
-  for (size_t i = 0; i < (size_t)npos * c.slots; i++)
-    if (!std::isfinite(out[i])) return fail(LAYA_E_NONFINITE, "non-finite model output");
-  return 0;
+  return forward_seqs(m, ids, &s, 1, positions, npos, out);
+}
+
+int laya_openthai_forward_batch(laya_ot_model* m, const int32_t* ids, const int32_t* lens, int nseq,
+                                const int32_t* positions, int npos, float* out) {
+  if (!m || !ids || !lens || !positions || !out || nseq < 1 || nseq > 256 || npos < 1)
+    return fail(LAYA_E_INVALID, "invalid forward arguments");
+  std::lock_guard<std::mutex> lk(m->mu);
+  return forward_seqs(m, ids, lens, nseq, positions, npos, out);
 }
 
 void laya_openthai_close(laya_ot_model* m) {
@@ -406,6 +472,11 @@ void laya_openthai_close(laya_ot_model* m) {
   for (DevBuf* b : {&m->dids, &m->dpos, &m->x, &m->h, &m->big, &m->att, &m->att16, &m->act, &m->logits,
                      &m->gscr, &m->kpart})
     b->release();
+  for (int i = 0; i < laya_ot_model::kSide; i++) {
+    if (m->side[i]) cudaStreamDestroy(m->side[i]);
+    if (m->join[i]) cudaEventDestroy(m->join[i]);
+  }
+  if (m->fork) cudaEventDestroy(m->fork);
   if (m->st) cudaStreamDestroy(m->st);
   delete m;
 }

@@ -395,6 +395,32 @@ class Model:
                                                     out.ctypes.data_as(ctypes.c_void_p)))
         return out
 
+    def forward_batch(self, passes) -> list:
+        """Slot logits of several encoded passes [(ids, positions), ...] in
+        one forward (laya_openthai_forward_batch): each pass is its own causal
+        sequence.  A model without a native handle (a forward stood in by
+        another implementation) runs the passes one at a time."""
+        import ctypes
+
+        from . import _lib
+
+        if not self._h:
+            return [self.forward(ids, pos) for ids, pos in passes]
+        if len(passes) == 1:
+            return [self.forward(*passes[0])]
+        ids = [np.asarray(i, np.int32) for i, _ in passes]
+        lens = np.ascontiguousarray([len(i) for i in ids], np.int32)
+        offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+        allids = np.ascontiguousarray(np.concatenate(ids))
+        pos = [np.asarray(p, np.int64) for _, p in passes]
+        allpos = np.ascontiguousarray(np.concatenate([p + o for p, o in zip(pos, offs)]).astype(np.int32))
+        out = np.zeros((len(allpos), self.config["slots"]), np.float32)
+        _lib.check(_lib.lib().laya_openthai_forward_batch(
+            self._h, allids.ctypes.data_as(ctypes.c_void_p), lens.ctypes.data_as(ctypes.c_void_p), len(lens),
+            allpos.ctypes.data_as(ctypes.c_void_p), len(allpos), out.ctypes.data_as(ctypes.c_void_p)))
+        bounds = np.cumsum([0] + [len(p) for p in pos])
+        return [out[bounds[i]:bounds[i + 1]] for i in range(len(passes))]
+
     info = {"architecture": "openthai_systemone"}
 
     def layers(self) -> int:
@@ -419,21 +445,31 @@ class Model:
         answers, usage (input tokens of the first pass, permutations, whether
         the state was truncated, latency), the request's `id` if it has one,
         and with `raw` each pass's input ids, answer positions and logits.
-        `canceled()` is polled before each pass (LayaError E_CANCELED)."""
+        `canceled()` is polled before the passes run (LayaError E_CANCELED):
+        once before the single batched GPU forward of all passes, or before
+        each pass when the forward is another implementation's."""
         from ._lib import E_CANCELED, LayaError
 
         start = time.perf_counter()
         qs = questions(req)
         n = permutation_count(req, qs)
         passes, debug, tokens, truncated = [], [], 0, False
-        for p in range(n):
-            if canceled is not None and canceled():
-                raise LayaError(E_CANCELED, "request canceled")
-            e = self._encode(tok, req, qs, n, p)
-            if p == 0:
-                tokens = len(e.ids)
+        if canceled is not None and canceled():
+            raise LayaError(E_CANCELED, "request canceled")
+        enc = [self._encode(tok, req, qs, n, p) for p in range(n)]
+        tokens = len(enc[0].ids)
+        # every permutation pass in one forward on the GPU (one at a time
+        # when the forward is another implementation's)
+        if self._h:
+            all_logits = self.forward_batch([(e.ids, e.positions) for e in enc])
+        else:
+            all_logits = []
+            for e in enc:
+                if canceled is not None and canceled():
+                    raise LayaError(E_CANCELED, "request canceled")
+                all_logits.append(self.forward(e.ids, e.positions))
+        for e, logits in zip(enc, all_logits):
             truncated |= e.truncated
-            logits = self.forward(e.ids, e.positions)
             passes.append((logits, e.order))
             if raw:
                 debug.append({"input_ids": [int(v) for v in e.ids], "answer_positions": [int(v) for v in e.positions],

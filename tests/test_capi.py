@@ -57,4 +57,5 @@ def test_openthai_entry_points_reject_bad_arguments():
     assert L.laya_openthai_open_memory(img, 8, 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_FORMAT
     assert L.laya_openthai_open_memory(None, 0, 0, ctypes.byref(cfg), ctypes.byref(h)) == _lib.E_INVALID
     assert L.laya_openthai_forward(None, None, 0, None, 0, None) == _lib.E_INVALID
+    assert L.laya_openthai_forward_batch(None, None, None, 0, None, 0, None) == _lib.E_INVALID
     L.laya_openthai_close(None)

@@ -121,6 +121,28 @@ def test_openthai_forward_matches_oracle(ot_model):
         m.forward([0, 1, 2], [3])
 
 
+def test_openthai_forward_batch_matches_single_passes(ot_model):
+    """Several passes in one forward (laya_openthai_forward_batch): each
+    sequence causal on its own, mixers on side streams (five sequences: more
+    than the four side streams), the same logits as one pass at a time and
+    the oracle's."""
+    m, w = ot_model
+    rng = np.random.default_rng(21)
+    shapes = [(40, [0, 39]), (1, [0]), (200, [7, 150, 199]), (65, [64]), (130, [3, 129])]
+    passes = [(rng.integers(0, 300, s), pos) for s, pos in shapes]
+    got = m.forward_batch(passes)
+    assert len(got) == len(passes)
+    for (ids, pos), g in zip(passes, got):
+        one = m.forward(ids, pos)
+        want = oracle.ot_forward(w, ids, pos)
+        assert g.shape == one.shape == (len(pos), 256)
+        # the batch's GEMMs may split K differently from one pass's
+        assert np.allclose(g, one, atol=1e-3 * np.abs(one).max() + 1e-5), np.abs(g - one).max()
+        assert np.abs(g - want).max() < 5e-3 * np.abs(want).max()
+    with pytest.raises(LayaError):
+        m.forward_batch([([0, 1, 2], [0]), ([0, 1], [2])])  # a position past its own pass
+
+
 def test_openthai_forward_reference_head_geometry(tmp_path):
     """The reference's head layout (8/2 attention heads of 256 with a 64-wide
     rotary part, 16 DeltaNet heads of 128) on a small width; a NumPy
