@@ -44,6 +44,27 @@ def test_greedy_decode_matches_oracle(tiny_paths, name, nseq):
     o.close()
 
 
+@pytest.mark.parametrize("name,nseq,lo,hi", [("tiny-llama-q8_0", 2, 250, 400), ("tiny-qwen2-f16", 3, 450, 520),
+                                            ("small-llama-q8_0", 2, 700, 900)])
+def test_greedy_decode_mid_contexts_match_oracle(tiny_paths, name, nseq, lo, hi):
+    # 4-15 pages per sequence: the decode attention's key splits run as
+    # clusters of 4 or 8 CTAs that merge in the leader's shared memory
+    path = tiny_paths[name]
+    o = oracle.Model(open(path, "rb").read(), threads=8, attn_threads=8)
+    rng = np.random.default_rng(77 + nseq)
+    ctxs = [synth.token_ids(rng, o.vocab, int(n)) for n in rng.integers(lo, hi, size=nseq)]
+    steps = 4
+    with engine.Engine(path) as e:
+        toks, _ = e.decode(ctxs, steps)
+    for i, c in enumerate(ctxs):
+        want, margins = oracle_greedy(o, c, steps)
+        for s in range(steps):
+            if margins[s] < 2e-2:
+                break
+            assert toks[i, s] == want[s], (name, i, s, toks[i], want)
+    o.close()
+
+
 @pytest.mark.parametrize("name,nseq", [("small-llama-q8_0", 1), ("small-llama-q8_0", 8), ("tiny-llama-f16", 4)])
 def test_chained_gemv_step_matches_per_launch_step(tiny_paths, monkeypatch, name, nseq):
     # One cooperative launch per layer (grid barriers between the GEMV phases)
