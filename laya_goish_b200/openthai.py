@@ -409,6 +409,10 @@ class Model:
         if len(passes) == 1:
             return [self.forward(*passes[0])]
         ids = [np.asarray(i, np.int32) for i, _ in passes]
+        for (i, p) in zip(ids, (p for _, p in passes)):
+            if len(i) == 0 or any(not 0 <= int(x) < len(i) for x in p):
+                # a position past its own pass would read the next pass's row
+                raise _lib.LayaError(_lib.E_INVALID, "invalid OpenThai token sequence")
         lens = np.ascontiguousarray([len(i) for i in ids], np.int32)
         offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         allids = np.ascontiguousarray(np.concatenate(ids))

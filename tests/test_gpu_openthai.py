@@ -141,6 +141,8 @@ def test_openthai_forward_batch_matches_single_passes(ot_model):
         assert np.abs(g - want).max() < 5e-3 * np.abs(want).max()
     with pytest.raises(LayaError):
         m.forward_batch([([0, 1, 2], [0]), ([0, 1], [2])])  # a position past its own pass
+    with pytest.raises(LayaError):
+        m.forward_batch([([0, 1, 2], [3]), ([0, 1], [1])])  # ... that would land in the next pass
 
 
 def test_openthai_forward_reference_head_geometry(tmp_path):
