@@ -7,11 +7,11 @@
 //
 // with a per-head state S [key hk][value hk] starting at zero.
 //
-// Three kernels.  delta_prep_kernel does the per-token work that does not
-// depend on S in parallel over (token, head): the two L2 norms (in place in
-// qkv) and decay / beta.  delta_quad_kernel forms, per group of four tokens
-// and head, the key-key products k_m . k_i (i < m) and query-key products
-// q_m . k_i (i <= m).  delta_scan_kernel then runs the sequential part four
+// Two kernels.  delta_prep_kernel does the work that does not depend on S
+// in parallel over (group of four tokens, head): the two L2 norms (in place
+// in qkv), decay / beta, and the group's key-key products k_m . k_i (i < m)
+// and query-key products q_m . k_i (i <= m).  delta_scan_kernel then runs
+// the sequential part four
 // tokens at a time: with S0 the state before the group and a_m the decays,
 //   r_m = k_m . S0,  p_m = q_m . S0                 (eight independent sums)
 //   delta_m = beta_m (v_m - A_m r_m - sum_{i<m} a_{i+1..m} (k_m . k_i) delta_i)
@@ -26,6 +26,8 @@
 // are 3-step shuffle trees over those lanes.  Tokens are staged in chunks of
 // 16 in shared memory, double-buffered: the next chunk's loads are issued
 // into registers before the current chunk is processed.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -59,58 +61,20 @@ __device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
   return r;
 }
 
-// a / b: the gate projections of token i, head h at a[i * ldab + h] and
-// b[i * ldab + h]; decay / beta go to dec / beta [s][nh] (may alias a / b
-// when ldab == nh).
+// One warp per (group of four tokens, head), the per-token work that does
+// not depend on the state: the two L2 norms of q and k (written back in
+// place), decay and beta (a / b: the gate projections of token i, head h at
+// a[i * ldab + h] and b[i * ldab + h]; decay / beta go to dec / beta [s][nh],
+// which may alias a / b when ldab == nh), then from the normalised rows the
+// group's 6 key-key and 10 query-key products, stored as
+// kq[(quad * nh + h) * 16 + ...]: k1k0, k2k0, k2k1, k3k0, k3k1, k3k2, then
+// q0k0, q1k0, q1k1, q2k0, q2k1, q2k2, q3k0, q3k1, q3k2, q3k3 (tokens past s
+// count as zero).
 template <int HK>
 __global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv, const float* a, const float* b,
                                                          int ldab, const float* __restrict__ dt,
                                                          const float* __restrict__ alog, int s, int nh, float* dec,
-                                                         float* beta) {
-  constexpr int PL = HK / 32;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  if (gw >= s * nh) return;
-  const int i = gw / nh, h = gw % nh, w = nh * HK;
-  float* q = qkv + (size_t)i * 3 * w + h * HK;
-  float* k = q + w;
-  float qv[PL], kv[PL], q2 = 0.f, k2 = 0.f;
-#pragma unroll
-  for (int u = 0; u < PL; u++) {
-    qv[u] = q[lane + 32 * u];
-    kv[u] = k[lane + 32 * u];
-    q2 += qv[u] * qv[u];
-    k2 += kv[u] * kv[u];
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    q2 += __shfl_xor_sync(0xffffffffu, q2, o);
-    k2 += __shfl_xor_sync(0xffffffffu, k2, o);
-  }
-  const float qs = 1.f / sqrtf(q2 + 1e-6f) / sqrtf((float)HK);
-  const float ks = 1.f / sqrtf(k2 + 1e-6f);
-#pragma unroll
-  for (int u = 0; u < PL; u++) {
-    q[lane + 32 * u] = qv[u] * qs;
-    k[lane + 32 * u] = kv[u] * ks;
-  }
-  if (lane == 0) {
-    const size_t e = (size_t)i * nh + h, src = (size_t)i * ldab + h;
-    const float x = a[src] + dt[h];
-    const float bv = b[src];
-    const float sp = x > 20.f ? x : log1pf(expf(x));
-    dec[e] = expf(-expf(alog[h]) * sp);
-    beta[e] = 1.f / (1.f + expf(-bv));
-  }
-}
-
-// One warp per (group of four tokens, head): the 6 key-key and 10
-// query-key products of the group, from the normalised q and k (tokens past
-// s read as zero), stored as kq[(quad * nh + h) * 16 + ...]: k1k0, k2k0,
-// k2k1, k3k0, k3k1, k3k2, then q0k0, q1k0, q1k1, q2k0, q2k1, q2k2, q3k0, q3k1,
-// q3k2, q3k3.
-template <int HK>
-__global__ void __launch_bounds__(256) delta_quad_kernel(const float* __restrict__ qkv, int s, int nh,
-                                                         float* __restrict__ kq) {
+                                                         float* beta, float* __restrict__ kq) {
   constexpr int PL = HK / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   const int nq = (s + 3) / 4;
@@ -120,12 +84,41 @@ __global__ void __launch_bounds__(256) delta_quad_kernel(const float* __restrict
 #pragma unroll
   for (int m = 0; m < 4; m++) {
     const int i = 4 * qd + m;
-    const float* row = qkv + (size_t)i * 3 * w + h * HK;
+    float* q = qkv + (size_t)i * 3 * w + h * HK;
+    float* k = q + w;
+    float q2 = 0.f, k2 = 0.f;
 #pragma unroll
     for (int u = 0; u < PL; u++) {
-      qv[m][u] = i < s ? row[lane + 32 * u] : 0.f;
-      kv[m][u] = i < s ? row[w + lane + 32 * u] : 0.f;
+      qv[m][u] = i < s ? q[lane + 32 * u] : 0.f;
+      kv[m][u] = i < s ? k[lane + 32 * u] : 0.f;
+      q2 += qv[m][u] * qv[m][u];
+      k2 += kv[m][u] * kv[m][u];
     }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+      k2 += __shfl_xor_sync(0xffffffffu, k2, o);
+    }
+    const float qs = 1.f / sqrtf(q2 + 1e-6f) / sqrtf((float)HK);
+    const float ks = 1.f / sqrtf(k2 + 1e-6f);
+#pragma unroll
+    for (int u = 0; u < PL; u++) {
+      qv[m][u] *= qs;
+      kv[m][u] *= ks;
+      if (i < s) {
+        q[lane + 32 * u] = qv[m][u];
+        k[lane + 32 * u] = kv[m][u];
+      }
+    }
+  }
+  if (lane < 4 && 4 * qd + lane < s) {
+    const int i = 4 * qd + lane;
+    const size_t e = (size_t)i * nh + h, src = (size_t)i * ldab + h;
+    const float x = a[src] + dt[h];
+    const float bv = b[src];
+    const float sp = x > 20.f ? x : log1pf(expf(x));
+    dec[e] = expf(-expf(alog[h]) * sp);
+    beta[e] = 1.f / (1.f + expf(-bv));
   }
   float d[16];
   int n = 0;
@@ -372,34 +365,57 @@ __global__ void conv_silu4_kernel(const float* __restrict__ raw, int ldraw, cons
 }
 
 // Per-head RMSNorm (weight offset 0, eps 1e-6) of the recurrence output,
-// then x SiLU(z) (model.rs:356-360); one warp per (token, head) row.  The
-// result goes to o (F32, in place) or, when out16 is set, to out16 as F16
-// rows [s][nh HK] (the output projection's operand) with o left as it was.
+// then x SiLU(z) (model.rs:356-360); one warp per (token, head) row, each
+// lane HK / 32 consecutive elements as one vector load of o and of z (rows
+// 16-byte aligned, ldz a multiple of 4).  The result goes to o (F32, in
+// place) or, when out16 is set, to out16 as F16 rows [s][nh HK] (the output
+// projection's operand) with o left as it was.
 template <int HK>
 __global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict__ z, int ldz, int nh,
                                  const float* __restrict__ w, int rows, half* __restrict__ out16) {
-  constexpr int PL = HK / 32;
+  constexpr int PL = HK / 32;  // consecutive elements per lane (4 or 2), one vector load each
+  using VecF = typename std::conditional<PL == 4, float4, float2>::type;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (gw >= rows) return;
-  float* r = o + (size_t)gw * HK;
-  const float* zr = z + (size_t)(gw / nh) * ldz + (size_t)(gw % nh) * HK;
-  float v[PL], ss = 0.f;
+  float* r = o + (size_t)gw * HK + lane * PL;
+  const float* zr = z + (size_t)(gw / nh) * ldz + (size_t)(gw % nh) * HK + lane * PL;
+  float v[PL], zz[PL], wv[PL];
+  {
+    const VecF a = *reinterpret_cast<const VecF*>(r);
+    const VecF b = *reinterpret_cast<const VecF*>(zr);
+    const float* pa = reinterpret_cast<const float*>(&a);
+    const float* pb = reinterpret_cast<const float*>(&b);
 #pragma unroll
-  for (int u = 0; u < PL; u++) {
-    v[u] = r[lane + 32 * u];
-    ss += v[u] * v[u];
+    for (int u = 0; u < PL; u++) {
+      v[u] = pa[u];
+      zz[u] = pb[u];
+      wv[u] = __ldg(w + lane * PL + u);  // the norm weights need no alignment
+    }
   }
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < PL; u++) ss += v[u] * v[u];
 #pragma unroll
   for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float scale = 1.f / sqrtf(ss / (float)HK + 1e-6f);
+  float y[PL];
 #pragma unroll
-  for (int u = 0; u < PL; u++) {
-    const float zz = zr[lane + 32 * u];
-    const float y = v[u] * scale * w[lane + 32 * u] * (zz / (1.f + expf(-zz)));
-    if (out16)
-      out16[(size_t)gw * HK + lane + 32 * u] = __float2half_rn(y);
+  for (int u = 0; u < PL; u++) y[u] = v[u] * scale * wv[u] * (zz[u] / (1.f + expf(-zz[u])));
+  if (out16) {
+    __align__(8) half hv[PL];
+#pragma unroll
+    for (int u = 0; u < PL; u++) hv[u] = __float2half_rn(y[u]);
+    half* dst = out16 + (size_t)gw * HK + lane * PL;
+    if constexpr (PL == 4)
+      *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(hv);
     else
-      r[lane + 32 * u] = y;
+      *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(hv);
+  } else {
+    VecF t;
+    float* pt = reinterpret_cast<float*>(&t);
+#pragma unroll
+    for (int u = 0; u < PL; u++) pt[u] = y[u];
+    *reinterpret_cast<VecF*>(r) = t;
   }
 }
 
@@ -408,6 +424,10 @@ cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int l
                               int s, int nh, int hk, float* scratch, float* out, half* out16, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
   if (nh < 1 || (hk != 64 && hk != 128)) return cudaErrorInvalidValue;
+  // vector loads of the recurrence output and of z in the output norm
+  if ((ldz % 4) || (reinterpret_cast<uintptr_t>(z) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(out16) & 15))
+    return cudaErrorInvalidValue;
   const size_t C = (size_t)3 * nh * hk, n = (size_t)s * C;
   float* qkv = scratch;
   float* dec = scratch + n;
@@ -439,16 +459,13 @@ cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, co
                         int s, int nh, int hk, float* dec, float* beta, float* kq, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
   if (nh < 1 || (hk != 64 && hk != 128) || !kq) return cudaErrorInvalidValue;
-  const unsigned prep_blocks = (unsigned)(((size_t)s * nh + 7) / 8);
-  const unsigned quad_blocks = (unsigned)(((size_t)((s + 3) / 4) * nh + 7) / 8);
+  const unsigned prep_blocks = (unsigned)(((size_t)((s + 3) / 4) * nh + 7) / 8);
   const dim3 grid(nh, hk / delta::CPB);
   if (hk == 128) {
-    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta);
-    delta_quad_kernel<128><<<quad_blocks, 256, 0, st>>>(qkv, s, nh, kq);
+    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta, kq);
     delta_scan_kernel<128><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, kq, s, nh, out);
   } else {
-    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta);
-    delta_quad_kernel<64><<<quad_blocks, 256, 0, st>>>(qkv, s, nh, kq);
+    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta, kq);
     delta_scan_kernel<64><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, kq, s, nh, out);
   }
   return cudaGetLastError();

@@ -311,7 +311,8 @@ int forward_seqs(laya_ot_model* m, const int32_t* ids, const int* lens, int nseq
   // big: the stacked projection output of either layer kind, then each
   // sequence's DeltaNet mixer scratch (16-byte aligned)
   const int nfull = 2 * qd + 2 * KV * hd, ndelta = 4 * w + 2 * nh;
-  const size_t pw = ((size_t)std::max(nfull, ndelta) + 63) / 64 * 64;
+  const int ldd = (ndelta + 3) / 4 * 4;  // DeltaNet projection rows padded to 16 bytes (vector loads)
+  const size_t pw = ((size_t)std::max(nfull, ldd) + 63) / 64 * 64;
   std::vector<size_t> scr_off(nseq);
   size_t scr_f = 0, gscr_b = 16;
   for (int i = 0; i < nseq; i++) {
@@ -377,7 +378,7 @@ int forward_seqs(laya_ot_model* m, const int32_t* ids, const int* lens, int nseq
       pend = ks_full;
     } else {
       // one GEMM: rows in_proj_qkv (3w), z (w), a (nh), b (nh)
-      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, ndelta, d, s, P, ndelta, nullptr, nullptr))) return rc;
+      if ((rc = gemm(*m, EPI_F32, Hh, d, L.qkv, ndelta, d, s, P, ldd, nullptr, nullptr))) return rc;
       // the mixer writes its normalised, gated rows as F16 straight into
       // the output projection's operand; with several sequences each one's
       // mixer runs on a side stream (fork after the projection, join before
@@ -389,8 +390,8 @@ int forward_seqs(laya_ot_model* m, const int32_t* ids, const int* lens, int nseq
           ms = m->side[i % laya_ot_model::kSide];
           LAYA_CK(cudaStreamWaitEvent(ms, m->fork, 0));
         }
-        const float* Pi = P + (size_t)r0 * ndelta;
-        LAYA_CK(gated_delta_mixer(Pi, ndelta, Pi + 3 * w, ndelta, Pi + 4 * w, Pi + 4 * w + nh, ndelta, L.conv, L.dt,
+        const float* Pi = P + (size_t)r0 * ldd;
+        LAYA_CK(gated_delta_mixer(Pi, ldd, Pi + 3 * w, ldd, Pi + 4 * w, Pi + 4 * w + nh, ldd, L.conv, L.dt,
                                   L.alog, L.normw, lens[i], nh, hk, SCR + scr_off[i],
                                   att.as<float>() + (size_t)r0 * w, att16.as<half>() + (size_t)r0 * w, ms));
       }
