@@ -30,6 +30,13 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
+
+#define LAYA_DN_CK(x)                     \
+  do {                                    \
+    const cudaError_t e_ = (x);           \
+    if (e_ != cudaSuccess) return e_;     \
+  } while (0)
 
 namespace laya {
 
@@ -75,6 +82,8 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(float* __restrict__ qkv
                                                          int ldab, const float* __restrict__ dt,
                                                          const float* __restrict__ alog, int s, int nh, float* dec,
                                                          float* beta, float* __restrict__ kq) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int PL = HK / 32;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   const int nq = (s + 3) / 4;
@@ -310,6 +319,8 @@ __global__ void __launch_bounds__(delta::THREADS) delta_scan_kernel(const float*
 // terms before token 0 left out, summed in j order.
 __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldraw, const float* __restrict__ conv, int s,
                                  int C, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= (size_t)s * C) return;
   const int i = (int)(e / C), c = (int)(e % C);
@@ -326,6 +337,8 @@ __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldraw, const
 // the four taps of each channel are one float4.  grid.y = token block.
 __global__ void conv_silu4_kernel(const float* __restrict__ raw, int ldraw, const float* __restrict__ conv, int s,
                                   int C, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int TT = 8;  // tokens per thread
   const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x), i0 = blockIdx.y * TT;
   if (c >= C) return;
@@ -373,6 +386,8 @@ __global__ void conv_silu4_kernel(const float* __restrict__ raw, int ldraw, cons
 template <int HK>
 __global__ void norm_gate_kernel(float* __restrict__ o, const float* __restrict__ z, int ldz, int nh,
                                  const float* __restrict__ w, int rows, half* __restrict__ out16) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int PL = HK / 32;  // consecutive elements per lane (4 or 2), one vector load each
   using VecF = typename std::conditional<PL == 4, float4, float2>::type;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
@@ -429,23 +444,29 @@ cudaError_t gated_delta_mixer(const float* raw, int ldraw, const float* z, int l
       (reinterpret_cast<uintptr_t>(out16) & 15))
     return cudaErrorInvalidValue;
   const size_t C = (size_t)3 * nh * hk, n = (size_t)s * C;
+  // programmatic dependent launch on a created stream (each kernel waits for
+  // its predecessor's output before reading); plain launches on stream 0
+  const bool pdl = st != nullptr;
   float* qkv = scratch;
   float* dec = scratch + n;
   float* beta = dec + (size_t)s * nh;
   float* kq = beta + (size_t)s * nh;
   if (ldraw % 4 == 0 && (reinterpret_cast<uintptr_t>(raw) & 15) == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
       (s + 7) / 8 <= 65535)
-    conv_silu4_kernel<<<dim3((unsigned)((C / 4 + 127) / 128), (unsigned)((s + 7) / 8)), 128, 0, st>>>(
-        raw, ldraw, conv, s, (int)C, qkv);
+    LAYA_DN_CK(launch_k(conv_silu4_kernel, dim3((unsigned)((C / 4 + 127) / 128), (unsigned)((s + 7) / 8)), dim3(128),
+                        0, st, pdl, raw, ldraw, conv, s, (int)C, qkv));
   else
-    conv_silu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, ldraw, conv, s, (int)C, qkv);
+    LAYA_DN_CK(launch_k(conv_silu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, pdl, raw, ldraw, conv, s,
+                        (int)C, qkv));
   cudaError_t e = gated_delta(qkv, a, b, ldab, dt, alog, s, nh, hk, dec, beta, kq, out, st);
   if (e != cudaSuccess) return e;
   const int rows = s * nh;
   if (hk == 128)
-    norm_gate_kernel<128><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows, out16);
+    LAYA_DN_CK(launch_k(norm_gate_kernel<128>, dim3((rows + 7) / 8), dim3(256), 0, st, pdl, out, z, ldz, nh, normw, rows,
+                        out16));
   else
-    norm_gate_kernel<64><<<(rows + 7) / 8, 256, 0, st>>>(out, z, ldz, nh, normw, rows, out16);
+    LAYA_DN_CK(launch_k(norm_gate_kernel<64>, dim3((rows + 7) / 8), dim3(256), 0, st, pdl, out, z, ldz, nh, normw, rows,
+                        out16));
   return cudaGetLastError();
 }
 
@@ -459,14 +480,23 @@ cudaError_t gated_delta(float* qkv, const float* a, const float* b, int ldab, co
                         int s, int nh, int hk, float* dec, float* beta, float* kq, float* out, cudaStream_t st) {
   if (s <= 0) return cudaSuccess;
   if (nh < 1 || (hk != 64 && hk != 128) || !kq) return cudaErrorInvalidValue;
+  const bool pdl = st != nullptr;
   const unsigned prep_blocks = (unsigned)(((size_t)((s + 3) / 4) * nh + 7) / 8);
   const dim3 grid(nh, hk / delta::CPB);
   if (hk == 128) {
-    delta_prep_kernel<128><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta, kq);
-    delta_scan_kernel<128><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, kq, s, nh, out);
+    // The scan launches only once the prep is done (no programmatic early
+    // launch): launched early, its 128 CTAs were placed wherever the prep
+    // left room, several to an SM, and the latency-bound scan took twice as
+    // long.
+    LAYA_DN_CK(launch_k(delta_prep_kernel<128>, dim3(prep_blocks), dim3(256), 0, st, pdl, qkv, a, b, ldab, dt, alog, s, nh,
+                        dec, beta, kq));
+    LAYA_DN_CK(launch_k(delta_scan_kernel<128>, grid, dim3(delta::THREADS), 0, st, false, (const float*)qkv,
+                        (const float*)dec, (const float*)beta, (const float*)kq, s, nh, out));
   } else {
-    delta_prep_kernel<64><<<prep_blocks, 256, 0, st>>>(qkv, a, b, ldab, dt, alog, s, nh, dec, beta, kq);
-    delta_scan_kernel<64><<<grid, delta::THREADS, 0, st>>>(qkv, dec, beta, kq, s, nh, out);
+    LAYA_DN_CK(launch_k(delta_prep_kernel<64>, dim3(prep_blocks), dim3(256), 0, st, pdl, qkv, a, b, ldab, dt, alog, s, nh,
+                        dec, beta, kq));
+    LAYA_DN_CK(launch_k(delta_scan_kernel<64>, grid, dim3(delta::THREADS), 0, st, false, (const float*)qkv,
+                        (const float*)dec, (const float*)beta, (const float*)kq, s, nh, out));
   }
   return cudaGetLastError();
 }

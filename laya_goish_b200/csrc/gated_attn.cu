@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 
 namespace laya {
 
@@ -61,6 +62,8 @@ __global__ void __launch_bounds__(256) gattn_prep_kernel(const float* __restrict
                                                          int* __restrict__ tables) {
   constexpr int PL = HD / 32;  // dimensions per lane: lane l holds l, l + 32, ...
   __shared__ float rowbuf[8][HD];
+  pdl_wait();  // the projections were written by the previous kernel
+  pdl_trigger();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32, wib = threadIdx.x / 32;
   const int pages = (s + kPage - 1) / kPage;
   // the work list: item u = query rows 128u .. of the one sequence, all pages in order
@@ -136,9 +139,10 @@ cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const 
   const int pages = (s + kPage - 1) / kPage;
   const size_t rows = (size_t)pages * kPage * (H + 2 * KV);
   const unsigned blocks = (unsigned)std::max<size_t>((rows + 7) / 8, ((size_t)pages + 255) / 256);
-#define LAYA_GA_PREP(HDV)                                                                                    \
-  gattn_prep_kernel<HDV><<<blocks, 256, 0, st>>>(qgate, ldqg, k, v, ldkv, qn, kn, s, H, KV, rot, theta, q16, \
-                                                  k16, v16, items, tables)
+  cudaError_t e = cudaSuccess;
+#define LAYA_GA_PREP(HDV)                                                                                   \
+  e = launch_k(gattn_prep_kernel<HDV>, dim3(blocks), dim3(256), 0, st, st != nullptr, qgate, ldqg, k, v, ldkv, qn, kn, \
+               s, H, KV, rot, theta, q16, k16, v16, items, tables)
   if (hd == 256)
     LAYA_GA_PREP(256);
   else if (hd == 128)
@@ -146,7 +150,6 @@ cudaError_t gated_attention(const float* qgate, int ldqg, const float* k, const 
   else
     LAYA_GA_PREP(64);
 #undef LAYA_GA_PREP
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   AttnParams p{};
   p.q = q16;
