@@ -1356,6 +1356,15 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
   cudaStream_t st = r.stream;
   const bool small = gemv_batch(c, nb);
   const int nbp = small ? pad_batch(nb) : nb;  // GEMV batch (padded rows are zero)
+  // Batches past the GEMV run the layer GEMMs on the Q8_0 blocks where the
+  // model allows (scales and split planes were prepared by decode_run): the
+  // residual and QKV GEMMs split K when their output tiles are few, and the
+  // next RMSNorm / qkv_merge adds the partial planes in split order.
+  const bool q8 = !small && use_q8_gemm(m, r, nb) && r.layers.back().sqkv_t;
+  const int ks_q = q8 ? gemm_q8_ksplit(nb, qd + 2 * kd, d, r.num_sms) : 1;
+  const int ks_o = q8 ? gemm_q8_ksplit(nb, d, qd, r.num_sms) : 1;
+  const int ks_d = q8 ? gemm_q8_ksplit(nb, d, ffn, r.num_sms) : 1;
+  int pend = 0;  // K splits of x not yet merged
   int rc;
   r.launches++;
   LAYA_CK(launch_k(advance_kernel, dim3(1), dim3(256), 0, st, true, io.counter, io.best, io.toks, io.pos_all,
@@ -1376,6 +1385,27 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     r.launches++;
     LAYA_CK(gemm_launch(epi, A, lda, B, ldb, a, r.num_sms, st));
     prof_end(r, cat, ev);
+    return 0;
+  };
+  auto gemm_q8d = [&](int cat, int epi, const half* A, int lda, const Q8Weights& w, GemmArgs a) -> int {
+    a.err = r.err;
+    a.budget = 4000000000ll;
+    cudaEvent_t ev;
+    prof_begin(r, cat, &ev);
+    r.launches++;
+    LAYA_CK(gemm_q8_launch(epi, A, lda, w, a, r.num_sms, st));
+    prof_end(r, cat, ev);
+    return 0;
+  };
+  // RMSNorm of the residual rows into h, adding pending K-split planes first
+  auto dnorm = [&](const float* w) -> int {
+    r.launches++;
+    const int ns = pend;
+    pend = 0;
+    if (ns > 1)
+      LAYA_CK(rmsnorm_merge(x, nullptr, nb, r.kpart.as<float>(), ns, (size_t)nb * d, w, d, c.eps, h, nullptr, st));
+    else
+      LAYA_CK(rmsnorm(x, nullptr, nb, w, d, c.eps, h, nullptr, st));
     return 0;
   };
   auto stage = [&](const QTensor& t, half* out, int ldo, int grp, int gstride, int goff) -> int {
@@ -1467,10 +1497,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     Gemv3Args g4[4];
     const bool v3 = layer_args(l, g4);
     Gemv3Args &gq = g4[0], &go = g4[1], &gg = g4[2], &gd = g4[3];
-    if (!small) {
-      r.launches++;
-      LAYA_CK(rmsnorm(x, nullptr, nb, L.attn_norm, d, c.eps, h, nullptr, st));
-    }
+    if (!small && (rc = dnorm(L.attn_norm))) return rc;
     if (seq) {
       if (l == 0 && (rc = run_gemv3(r, gq))) return rc;  // later layers' qkv ran in the previous chain
     } else if (small && v3) {
@@ -1495,6 +1522,39 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       r.launches++;
       LAYA_CK(launch_k(rope_append_kernel, dim3(nb), dim3(256), 0, st, true, (const float*)f, L.bqkv, qd, kd, c.hd,
                        c.KV, (const int*)io.cur_pos, (const int*)io.cur_slot, r.rope, r.qb.as<half>(), kcl, vcl));
+    } else if (q8) {
+      if (ks_q > 1) {
+        GemmArgs sp{};
+        sp.M = nb;
+        sp.N = qd + 2 * kd;
+        sp.K = d;
+        sp.ldo = qd + 2 * kd;
+        sp.ksplit = ks_q;
+        sp.part = r.kpart.as<float>();
+        if ((rc = gemm_q8d(P_GEMM_QKV, EPI_RESID, h, d, q8_qkv(c, L), sp))) return rc;
+        r.launches++;
+        LAYA_CK(qkv_merge(r.kpart.as<float>(), ks_q, (size_t)nb * (qd + 2 * kd), nb, L.bqkv, qd, kd, c.hd, c.KV,
+                          io.cur_pos, io.cur_slot, r.rope, PAGE, r.qb.as<half>(), qd, kcl, vcl, st));
+      } else {
+        GemmArgs a{};
+        a.M = nb;
+        a.N = qd + 2 * kd;
+        a.K = d;
+        a.bias = L.bqkv;
+        a.out = r.qb.p;
+        a.ldo = qd;
+        a.qd = qd;
+        a.kd = kd;
+        a.hd = c.hd;
+        a.kvh = c.KV;
+        a.pos = io.cur_pos;
+        a.slot = io.cur_slot;
+        a.rope = r.rope;
+        a.kcache = kcl;
+        a.vcache = vcl;
+        a.page_size = PAGE;
+        if ((rc = gemm_q8d(P_GEMM_QKV, EPI_QKV, h, d, q8_qkv(c, L), a))) return rc;
+      }
     } else {
       const half* wqkv = L.wqkv16 ? L.wqkv16 : L.rqkv16;
       if (!wqkv) {
@@ -1537,6 +1597,17 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       if ((rc = run_gemv3(r, go))) return rc;
     } else if (small) {
       if ((rc = run_gemv(r, plan1(L.wo, r.att.as<half>(), qd, x, d, 1), nbp))) return rc;
+    } else if (q8) {
+      GemmArgs b{};
+      b.M = nb;
+      b.N = d;
+      b.K = qd;
+      b.resid = x;
+      b.ldo = d;
+      b.ksplit = ks_o;
+      b.part = r.kpart.as<float>();
+      if ((rc = gemm_q8d(P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, q8_o(c, L), b))) return rc;
+      pend = ks_o;
     } else {
       const half* wo = L.wo16 ? L.wo16 : L.ro16;
       if (!wo) {
@@ -1551,10 +1622,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       b.ldo = d;
       if ((rc = gemm_d(P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
     }
-    if (!small) {
-      r.launches++;
-      LAYA_CK(rmsnorm(x, nullptr, nb, L.ffn_norm, d, c.eps, h, nullptr, st));
-    }
+    if (!small && (rc = dnorm(L.ffn_norm))) return rc;
     if (small && v3) {
       if ((rc = run_gemv3(r, gg))) return rc;
       if ((rc = run_gemv3(r, gd))) return rc;
@@ -1578,6 +1646,24 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       }
       if ((rc = run_gemv(r, p, nbp))) return rc;
       if ((rc = run_gemv(r, plan1(L.wd, r.act.as<half>(), ffn, x, d, 1), nbp))) return rc;
+    } else if (q8) {
+      GemmArgs gu{};
+      gu.M = nb;
+      gu.N = 2 * ffn;
+      gu.K = d;
+      gu.out = r.act.p;
+      gu.ldo = ffn;
+      if ((rc = gemm_q8d(P_GEMM_GU, EPI_SWIGLU, h, d, q8_gu(c, L), gu))) return rc;
+      GemmArgs dn{};
+      dn.M = nb;
+      dn.N = d;
+      dn.K = ffn;
+      dn.resid = x;
+      dn.ldo = d;
+      dn.ksplit = ks_d;
+      dn.part = r.kpart.as<float>();
+      if ((rc = gemm_q8d(P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, q8_down(c, L), dn))) return rc;
+      pend = ks_d;
     } else {
       const half* wgu = L.wgu16 ? L.wgu16 : L.rgu16;
       if (!wgu) {
@@ -1607,10 +1693,7 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     }
   }
   // final norm + full-vocabulary logits + greedy argmax
-  if (!small) {
-    r.launches++;
-    LAYA_CK(rmsnorm(x, nullptr, nb, r.out_norm, d, c.eps, h, nullptr, st));
-  }
+  if (!small && (rc = dnorm(r.out_norm))) return rc;
   float* logits = r.dlogits.as<float>();
   if (seq) {
     // the head ran at the end of the last layer's chain
@@ -1632,7 +1715,11 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
     a.K = d;
     a.out = logits;
     a.ldo = c.V;
-    if ((rc = gemm_d(P_GEMM_HEAD, EPI_F32, h, d, r.head16, d, a))) return rc;
+    if (q8 && r.head_st) {
+      if ((rc = gemm_q8d(P_GEMM_HEAD, EPI_F32, h, d, q8_head(r), a))) return rc;
+    } else if ((rc = gemm_d(P_GEMM_HEAD, EPI_F32, h, d, r.head16, d, a))) {
+      return rc;
+    }
     r.launches++;
     LAYA_CK(launch_k(argmax_best_kernel, dim3(nb), dim3(256), 0, st, false, (const float*)logits, c.V, io.best));
   }
@@ -1658,7 +1745,11 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
   int rc;
   if ((rc = timing_begin_call(r))) return rc;
   const bool small = gemv_batch(c, n_seqs);
-  if (!small && (rc = ensure_head16(m, r))) return rc;
+  // batched steps on the Q8_0 blocks: their transposed scales exist before
+  // the step is captured into a graph
+  const bool q8 = !small && use_q8_gemm(m, r, n_seqs);
+  if (q8 && (rc = ensure_q8_scales(m, r))) return rc;
+  if (!small && !(q8 && r.head_st) && (rc = ensure_head16(m, r))) return rc;
   if (small && gemv3_enabled() && (rc = ensure_gv_packed(m, r))) return rc;
   // pages: context + generated tokens per sequence
   std::vector<int> tables, toff(n_seqs), clen(n_seqs);
@@ -1750,7 +1841,10 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
     a.err = r.err;
     a.budget = 4000000000ll;
     r.launches++;
-    LAYA_CK(gemm_launch(EPI_F32, r.hid16.as<half>(), c.d, r.head16, c.d, a, r.num_sms, r.stream));
+    if (q8 && r.head_st)
+      LAYA_CK(gemm_q8_launch(EPI_F32, r.hid16.as<half>(), c.d, q8_head(r), a, r.num_sms, r.stream));
+    else
+      LAYA_CK(gemm_launch(EPI_F32, r.hid16.as<half>(), c.d, r.head16, c.d, a, r.num_sms, r.stream));
     r.launches++;
     argmax_best_kernel<<<R, 256, 0, r.stream>>>(r.dlogits.as<float>(), c.V, io.best);
     LAYA_CK(cudaGetLastError());
@@ -1760,6 +1854,13 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
       (rc = r.qb.ensure((size_t)nbp * qd * 2)) || (rc = r.att.ensure((size_t)nbp * qd * 2)) ||
       (rc = r.act.ensure((size_t)nbp * c.ffn * 2)))
     return rc;
+  if (q8) {
+    // K-split partial planes of the step's Q8_0 GEMMs (allocated before any capture)
+    const int sq = gemm_q8_ksplit(n_seqs, qd + 2 * kd, c.d, r.num_sms);
+    const int so = std::max(gemm_q8_ksplit(n_seqs, c.d, qd, r.num_sms), gemm_q8_ksplit(n_seqs, c.d, c.ffn, r.num_sms));
+    const size_t f = std::max((size_t)sq * n_seqs * (qd + 2 * kd), (size_t)so * n_seqs * c.d);
+    if (std::max(sq, so) > 1 && (rc = r.kpart.ensure(f * 4))) return rc;
+  }
   const AttnShape sh = attn_shape(r, c, n_seqs, max_keys);
   if ((rc = r.dpart.ensure((size_t)n_seqs * c.H * sh.splits * (c.hd + 2) * 4)) ||
       (rc = r.tables.ensure(tables.size() * 4)))

@@ -685,6 +685,99 @@ int ensure_f16_cache(Model& m, Replica& r) {
   return 0;
 }
 
+bool use_q8_gemm(const Model& m, const Replica& r, int M) {
+  const Config& c = m.cfg;
+  if (!c.quantized || r.layers.empty() || M < 1) return false;
+  const char* on = std::getenv("LAYA_Q8_FUSED");
+  if (on && on[0] == '0') return false;
+  const char* mx = std::getenv("LAYA_Q8_FUSED_MAX_M");
+  const int max_m = mx ? std::atoi(mx) : 256;
+  if (M > max_m) return false;
+  const int qd = c.H * c.hd, kd = c.KV * c.hd;
+  if (c.d % 128 || qd % 128 || kd % 128 || c.ffn % 128) return false;
+  for (const Layer& L : r.layers)
+    for (const QTensor* t : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd})
+      if (t->kind != K_Q8_0) return false;
+  return true;
+}
+
+int ensure_q8_scales(Model& m, Replica& r) {
+  const Config& c = m.cfg;
+  if (r.layers.empty() || r.layers.back().sqkv_t) return 0;  // the last layer is built last
+  const int qd = c.H * c.hd, kd = c.KV * c.hd, d = c.d, ffn = c.ffn, big = 1 << 30;
+  const int nqkv = qd + 2 * kd;
+  // [K/32][N] F16 per operand
+  const size_t sizes[4] = {(size_t)(d / 32) * nqkv * 2, (size_t)(d / 32) * 2 * ffn * 2, (size_t)(qd / 32) * d * 2,
+                           (size_t)(ffn / 32) * d * 2};
+  for (int l = 0; l < c.L; l++) {
+    Layer& L = r.layers[l];
+    half* p[4];
+    for (int i = 0; i < 4; i++) {
+      void* v = nullptr;
+      LAYA_CK(cudaMalloc(&v, sizes[i]));
+      r.allocs.push_back(v);
+      p[i] = static_cast<half*>(v);
+    }
+    LAYA_CK(q8_scales_t(L.wq, p[0], nqkv, big, 0, 0, r.stream));
+    LAYA_CK(q8_scales_t(L.wk, p[0], nqkv, big, 0, qd, r.stream));
+    LAYA_CK(q8_scales_t(L.wv, p[0], nqkv, big, 0, qd + kd, r.stream));
+    LAYA_CK(q8_scales_t(L.wg, p[1], 2 * ffn, 128, 256, 0, r.stream));
+    LAYA_CK(q8_scales_t(L.wu, p[1], 2 * ffn, 128, 256, 128, r.stream));
+    LAYA_CK(q8_scales_t(L.wo, p[2], d, big, 0, 0, r.stream));
+    LAYA_CK(q8_scales_t(L.wd, p[3], d, big, 0, 0, r.stream));
+    r.launches += 7;
+    L.sqkv_t = p[0];
+    L.sgu_t = p[1];
+    L.so_t = p[2];
+    L.sd_t = p[3];
+  }
+  if (r.head.kind == K_Q8_0 && c.V % 8 == 0 && d % 128 == 0 && !r.head_st) {
+    void* v = nullptr;
+    LAYA_CK(cudaMalloc(&v, (size_t)(d / 32) * c.V * 2));
+    r.allocs.push_back(v);
+    LAYA_CK(q8_scales_t(r.head, static_cast<half*>(v), c.V, big, 0, 0, r.stream));
+    r.launches++;
+    r.head_st = static_cast<const half*>(v);
+  }
+  return 0;
+}
+
+static Q8Weights q8_one(const QTensor& t, const half* st) {
+  Q8Weights w{};
+  w.q[0] = reinterpret_cast<const int8_t*>(t.q);
+  w.rows[0] = t.rows;
+  w.nseg = 1;
+  w.st = st;
+  return w;
+}
+
+Q8Weights q8_qkv(const Config& c, const Layer& L) {
+  Q8Weights w{};
+  const QTensor* t[3] = {&L.wq, &L.wk, &L.wv};
+  for (int i = 0; i < 3; i++) {
+    w.q[i] = reinterpret_cast<const int8_t*>(t[i]->q);
+    w.rows[i] = t[i]->rows;
+  }
+  w.nseg = 3;
+  w.st = L.sqkv_t;
+  return w;
+}
+
+Q8Weights q8_gu(const Config& c, const Layer& L) {
+  Q8Weights w{};
+  w.q[0] = reinterpret_cast<const int8_t*>(L.wg.q);
+  w.q[1] = reinterpret_cast<const int8_t*>(L.wu.q);
+  w.rows[0] = w.rows[1] = c.ffn;
+  w.nseg = 2;
+  w.interleave = 1;
+  w.st = L.sgu_t;
+  return w;
+}
+
+Q8Weights q8_o(const Config& c, const Layer& L) { return q8_one(L.wo, L.so_t); }
+Q8Weights q8_down(const Config& c, const Layer& L) { return q8_one(L.wd, L.sd_t); }
+Q8Weights q8_head(const Replica& r) { return q8_one(r.head, r.head_st); }
+
 int ensure_kv(Model& m, Replica& r, int pages) {
   if (pages <= r.kv_pages) return 0;
   const Config& c = m.cfg;
@@ -722,6 +815,15 @@ static int gemm(Replica& r, int cat, int epi, const half* A, int lda, const half
   ProfScope ps(r, cat);
   r.launches++;
   LAYA_CK(gemm_launch(epi, A, lda, B, ldb, a, r.num_sms, r.stream, gemm_pdl()));
+  return 0;
+}
+
+static int gemm_q8(Replica& r, int cat, int epi, const half* A, int lda, const Q8Weights& w, GemmArgs a) {
+  a.err = r.err;
+  a.budget = kWaitBudget;
+  ProfScope ps(r, cat);
+  r.launches++;
+  LAYA_CK(gemm_q8_launch(epi, A, lda, w, a, r.num_sms, r.stream, gemm_pdl()));
   return 0;
 }
 
@@ -781,8 +883,11 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       (rc = r.qb.ensure((size_t)M * qd * 2)) || (rc = r.att.ensure((size_t)M * qd * 2)) ||
       (rc = r.act.ensure((size_t)M * ffn * 2)))
     return rc;
-  if (c.quantized && (rc = ensure_f16_cache(m, r))) return rc;
-  if (c.quantized && !r.layers[0].rqkv16) {
+  // short passes over Q8_0 weights decode the quants inside the GEMMs
+  const bool q8 = use_q8_gemm(m, r, M);
+  if (q8 && (rc = ensure_q8_scales(m, r))) return rc;
+  if (c.quantized && !q8 && (rc = ensure_f16_cache(m, r))) return rc;
+  if (c.quantized && !q8 && !r.layers[0].rqkv16) {
     if ((rc = r.wqkv_s.ensure((size_t)(qd + 2 * kd) * d * 2)) || (rc = r.wo_s.ensure((size_t)d * qd * 2)) ||
         (rc = r.wgu_s.ensure((size_t)2 * ffn * d * 2)) || (rc = r.wd_s.ensure((size_t)d * ffn * 2)))
       return rc;
@@ -800,12 +905,21 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
   // are merged, in split order, by the RMSNorm that next reads the residual.
   const char* ke = std::getenv("LAYA_KSPLIT");
   const bool ks_on = !(ke && ke[0] == '0');
-  const int ks_o = ks_on ? gemm_ksplit(M, d, qd, r.num_sms) : 1;
-  const int ks_d = ks_on ? gemm_ksplit(M, d, ffn, r.num_sms) : 1;
+  auto ksplit = [&](int N, int K) {
+    return !ks_on ? 1 : q8 ? gemm_q8_ksplit(M, N, K, r.num_sms) : gemm_ksplit(M, N, K, r.num_sms);
+  };
+  const int ks_o = ksplit(d, qd);
+  const int ks_d = ksplit(d, ffn);
   // the QKV GEMM splits K the same way when it has few tiles; its partial
   // planes (consumed by qkv_merge before the attention) share the buffer
   const int nqkv = qd + 2 * kd;
-  const int ks_q = ks_on ? gemm_ksplit(M, nqkv, d, r.num_sms) : 1;
+  const int ks_q = ksplit(nqkv, d);
+  // one layer GEMM: on the Q8_0 blocks (q8) or on the F16 operand B16
+  auto lgemm = [&](int cat, int epi, const half* A, int lda, const half* B16, const Q8Weights& w,
+                   const GemmArgs& a) -> int {
+    if (!q8) return gemm(r, cat, epi, A, lda, B16, lda, a);
+    return gemm_q8(r, cat, epi, A, lda, w, a);
+  };
   const size_t kpart_f = std::max((size_t)std::max(ks_o, ks_d) * M * d, (size_t)ks_q * M * nqkv);
   if (std::max(std::max(ks_o, ks_d), ks_q) > 1 && (rc = r.kpart.ensure(kpart_f * 4))) return rc;
   int pend = 0;  // K splits of x not yet merged (the gathered final norm merges without writing x back)
@@ -833,7 +947,8 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     }
     LAYA_CK(norm(nullptr, M, L.attn_norm, h, nullptr));
     const half* wqkv = L.wqkv16 ? L.wqkv16 : L.rqkv16;
-    if (!wqkv) {
+    const Q8Weights w_qkv = q8 ? q8_qkv(c, L) : Q8Weights{};
+    if (!wqkv && !q8) {
       half* s = r.wqkv_s.as<half>();
       if ((rc = stage(r, P_DEQUANT, L.wq, s, d, big, 0, 0)) || (rc = stage(r, P_DEQUANT, L.wk, s, d, big, 0, qd)) ||
           (rc = stage(r, P_DEQUANT, L.wv, s, d, big, 0, qd + kd)))
@@ -866,12 +981,12 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       sp.ldo = nqkv;
       sp.ksplit = ks_q;
       sp.part = r.kpart.as<float>();
-      if ((rc = gemm(r, P_GEMM_QKV, EPI_RESID, h, d, wqkv, d, sp))) return rc;
+      if ((rc = lgemm(P_GEMM_QKV, EPI_RESID, h, d, wqkv, w_qkv, sp))) return rc;
       ProfScope ps(r, P_GEMM_QKV);
       r.launches++;
       LAYA_CK(qkv_merge(r.kpart.as<float>(), ks_q, (size_t)M * nqkv, M, L.bqkv, qd, kd, c.hd, c.KV, a.pos, a.slot,
                         r.rope, PAGE, r.qb.as<half>(), qd, a.kcache, a.vcache, st, gemm_pdl()));
-    } else if ((rc = gemm(r, P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) {
+    } else if ((rc = lgemm(P_GEMM_QKV, EPI_QKV, h, d, wqkv, w_qkv, a))) {
       return rc;
     }
     {
@@ -901,7 +1016,7 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
       LAYA_CK(attention(ap, st));
     }
     const half* wo = L.wo16 ? L.wo16 : L.ro16;
-    if (!wo) {
+    if (!wo && !q8) {
       if ((rc = stage(r, P_DEQUANT, L.wo, r.wo_s.as<half>(), qd, big, 0, 0))) return rc;
       wo = r.wo_s.as<half>();
     }
@@ -913,11 +1028,11 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     b.ldo = d;
     b.ksplit = ks_o;
     b.part = r.kpart.as<float>();
-    if ((rc = gemm(r, P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
+    if ((rc = lgemm(P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, q8 ? q8_o(c, L) : Q8Weights{}, b))) return rc;
     pend = ks_o;
     LAYA_CK(norm(nullptr, M, L.ffn_norm, h, nullptr));
     const half* wgu = L.wgu16 ? L.wgu16 : L.rgu16;
-    if (!wgu) {
+    if (!wgu && !q8) {
       half* s = r.wgu_s.as<half>();
       if ((rc = stage(r, P_DEQUANT, L.wg, s, d, 128, 256, 0)) || (rc = stage(r, P_DEQUANT, L.wu, s, d, 128, 256, 128)))
         return rc;
@@ -929,9 +1044,9 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     gu.K = d;
     gu.out = r.act.p;
     gu.ldo = ffn;
-    if ((rc = gemm(r, P_GEMM_GU, EPI_SWIGLU, h, d, wgu, d, gu))) return rc;
+    if ((rc = lgemm(P_GEMM_GU, EPI_SWIGLU, h, d, wgu, q8 ? q8_gu(c, L) : Q8Weights{}, gu))) return rc;
     const half* wd = L.wd16 ? L.wd16 : L.rd16;
-    if (!wd) {
+    if (!wd && !q8) {
       if ((rc = stage(r, P_DEQUANT, L.wd, r.wd_s.as<half>(), ffn, big, 0, 0))) return rc;
       wd = r.wd_s.as<half>();
     }
@@ -943,7 +1058,8 @@ int run_forward(Model& m, Replica& r, const PassPlan& p, const std::vector<int>&
     dn.ldo = d;
     dn.ksplit = ks_d;
     dn.part = r.kpart.as<float>();
-    if ((rc = gemm(r, P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, wd, ffn, dn))) return rc;
+    if ((rc = lgemm(P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, wd, q8 ? q8_down(c, L) : Q8Weights{}, dn)))
+      return rc;
     pend = ks_d;
     if (canceled) {
       cudaEvent_t e;

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm.h"
 #include "gguf.h"
 #include "kernels.h"
 #include "laya_cuda.h"
@@ -77,6 +78,13 @@ struct Layer {
   const half* rgu16 = nullptr;
   const half* ro16 = nullptr;
   const half* rd16 = nullptr;
+  // Q8_0 models: the block scales of the same four operands transposed to
+  // [K/32][N] in the operands' row order, for the GEMM that decodes the int8
+  // quants in shared memory (gemm_q8_launch); built by ensure_q8_scales.
+  const half* sqkv_t = nullptr;
+  const half* sgu_t = nullptr;
+  const half* so_t = nullptr;
+  const half* sd_t = nullptr;
 };
 
 struct ProfEvent {
@@ -98,6 +106,7 @@ struct Replica {
   QTensor embd{}, head{};
   const float* out_norm = nullptr;
   const half* head16 = nullptr;  // F16 lm_head for full-vocabulary rows (lazy for quantised models)
+  const half* head_st = nullptr;  // Q8_0 lm_head: block scales as [d/32][V] (ensure_q8_scales)
   // Packed streaming images of the decode GEMV operands (gemv3_pack), built
   // on the first small-batch decode: per layer qkv, o, gate/up, down, then
   // the head; null where the streaming GEMV does not apply.
@@ -156,6 +165,21 @@ int ensure_head16(Model& m, Replica& r);
 // (about 2 bytes per weight; skipped, and the per-GEMM staging kept, when the
 // memory is not there or LAYA_F16_CACHE=0).
 int ensure_f16_cache(Model& m, Replica& r);
+// Whether a pass of M token rows runs its layer GEMMs on the Q8_0 blocks
+// themselves (gemm_q8_launch): every layer matrix Q8_0, every GEMM's K and
+// the q / k widths multiples of 128, and M at most LAYA_Q8_FUSED_MAX_M
+// (default 256, where the weight bytes bound the pass); LAYA_Q8_FUSED=0
+// turns it off.  The variables are read at every call.
+bool use_q8_gemm(const Model& m, const Replica& r, int M);
+// Builds the transposed block scales of every layer (and of a Q8_0 lm_head
+// with V % 8 == 0) once: 1/16 byte per weight.
+int ensure_q8_scales(Model& m, Replica& r);
+// The four GEMM operands of layer L, and a Q8_0 lm_head, as Q8_0 blocks.
+Q8Weights q8_qkv(const Config& c, const Layer& L);
+Q8Weights q8_gu(const Config& c, const Layer& L);
+Q8Weights q8_o(const Config& c, const Layer& L);
+Q8Weights q8_down(const Config& c, const Layer& L);
+Q8Weights q8_head(const Replica& r);
 int decide_shard(Model& m, Replica& r, const laya_batch& b, int r0, int r1, laya_answer* out,
                  int (*canceled)(void*), void* user, std::mutex* cancel_mu);
 int validate_batch(const Config& c, const laya_batch* b);
