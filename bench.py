@@ -418,6 +418,9 @@ AUX = {
     # name: (config, requests per GPU, prompt tokens, question builder, description)
     "cfg0": ("cfg0", 1, 256, "check over 2 candidate ids",
              "cfg0: Llama-16L F16 from seed, one 256-token request, one check question over 2 candidates"),
+    "cfg0q8": ("cfg1", 1, 256, "check over 2 candidate ids",
+               "cfg0's request (one 256-token check over 2 candidates) on the cfg1 Llama-16L Q8_0 decoder: the "
+               "layer GEMMs decode the Q8_0 blocks in their shared-memory staging"),
     "cfg2": ("cfg2", 128, 768, "score over 5 criteria x 3-token continuations (full-vocabulary log-softmax)",
              "cfg2: Llama-16L Q4_K_M (attn_v/ffn_down Q6_K) from seed, 128 requests x 768-token shared prefix, "
              "one score question over 5 criteria of 3-token continuations"),
@@ -431,7 +434,7 @@ def aux_questions(name, vocab):
     from laya_goish_b200.engine import Question
 
     rng = np.random.default_rng(7)
-    if name == "cfg0":
+    if name in ("cfg0", "cfg0q8"):
         return [Question("noul", synth.candidates(rng, vocab, 2))], 0
     if name == "cfg2":
         return [Question("score", synth.token_ids(rng, vocab, 15).reshape(5, 3))], 15
@@ -751,7 +754,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg2", "cfg3", "load", "openthai", "inproc"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg0q8", "cfg2", "cfg3", "load", "openthai", "inproc"])
     ap.add_argument("--load-cfg", default="cfg3", help="load: synthetic model to open")
     ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
