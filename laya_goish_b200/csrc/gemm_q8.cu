@@ -13,10 +13,9 @@
 //
 // Per CTA of a pair (tile 256 x 256; this CTA owns 128 rows of X and 128
 // rows of W):
-//   warp 0      TMA producer: per 128-column K block one int8 box (128 rows
+//   warp 0      weight stream: per 128-column K block one int8 box (128 rows
 //               x 128 B, 128-byte swizzle) and one scale box (4 blocks x 128
-//               rows) into a raw stage; per 64-column half the X box into an
-//               operand stage (pair form, counted on the leader's barrier)
+//               rows) into a raw stage, up to Q8_RS stages ahead
 //   warp 1      TMEM allocation; on the leader one thread issues
 //               tcgen05.mma.cta_group::2 per operand stage
 //   warps 2..5  epilogue (the F16 GEMM's: bias, residual TMA reduce-add or
@@ -24,7 +23,9 @@
 //   warps 6..9  converters: thread t decodes row t of the raw stage into row t
 //               of the operand stage's W half in the UMMA 128-byte swizzle
 //               (16-byte unit j of row r at (j ^ r % 8) * 16) and arrives on
-//               the leader's barrier of that stage
+//               the leader's barrier of that stage; converter thread 0 also
+//               loads the stage's X box (pair form, counted on the leader's
+//               barrier) as soon as the stage is free
 // Barriers:
 //   full[s]    leader only; 1 arrival (leader's expect_tx of both CTAs' X
 //              boxes) + 8 converter-warp arrivals (4 per CTA) + X bytes
@@ -44,8 +45,13 @@
 
 namespace laya {
 
-constexpr int Q8_FS = 4;               // operand stages, 64 K columns each
-constexpr int Q8_RS = 3;               // raw stages, 128 K columns each
+// The raw ring holds the HBM stream in flight: at small M a CTA streams its
+// weight rows as fast as it keeps boxes outstanding (a few microseconds of
+// loaded DRAM latency each), so shared memory goes to 7 raw stages (119 KB of
+// quants) and 2 operand stages, which the converters refill while the MMAs
+// read the other.
+constexpr int Q8_FS = 2;               // operand stages, 64 K columns each
+constexpr int Q8_RS = 7;               // raw stages, 128 K columns each
 constexpr int Q8_THREADS = 320;
 constexpr int Q8_PA = 128 * BK * 2;    // this CTA's 128 X rows of a stage
 constexpr int Q8_PB = 128 * BK * 2;    // this CTA's 128 W rows of a stage, as F16
@@ -168,21 +174,11 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      // The weights never depend on the previous kernel: this CTA's first
-      // int8 boxes come into L2 before waiting for it.
-      if (cluster < total) {
-        const int tile = cluster % tiles, sp = cluster / tiles;
-        int mt0, nt0, mi, lr;
-        pair_tile(a, tile, mt0, nt0);
-        q8_rows(seg, nt0 * 256 + (int)rank * 128, mi, lr);
-        const CUtensorMap* tq = mi == 0 ? &tmQ0 : mi == 1 ? &tmQ1 : &tmQ2;
-        const int k0 = sp * kqs, k1 = min(kqn, k0 + min(kqs, 2 * Q8_RS));
-        for (int kq = k0; kq < k1; kq++) tma_prefetch_2d(tq, kq * 128, lr);
-      }
-      pdl_wait();
-      pdl_trigger();
-      int fs = 0, rs = 0;
-      uint32_t fph = 0, rph = 0;
+      // Weight stream: the quants never depend on the previous kernel, so
+      // this thread starts at once (no griddepcontrol.wait) and keeps up to
+      // Q8_RS raw boxes in flight ahead of the converters.
+      int rs = 0;
+      uint32_t rph = 0;
       int rissued[Q8_RS];
       for (int s = 0; s < Q8_RS; s++) rissued[s] = -1;
       bool ok = true;
@@ -194,7 +190,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         q8_rows(seg, R0, mi, lr);
         const CUtensorMap* tq = mi == 0 ? &tmQ0 : mi == 1 ? &tmQ1 : &tmQ2;
         const int k1 = min(kqn, (sp + 1) * kqs);
-        for (int kq = sp * kqs; kq < k1 && ok; kq++) {
+        for (int kq = sp * kqs; kq < k1; kq++) {
           if (!mbar_wait(&rempty[rs], rph ^ 1, budget)) {
             atomicOr(a.err, 1u);
             ok = false;
@@ -208,32 +204,9 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
             rs = 0;
             rph ^= 1;
           }
-          for (int h = 0; h < 2; h++) {
-            if (!mbar_wait(&empty[fs], fph ^ 1, budget)) {
-              atomicOr(a.err, 1u);
-              ok = false;
-              break;
-            }
-            const uint32_t fbar = cluster_addr(&full[fs], 0);
-            if (leader) mbar_expect_tx(&full[fs], 2 * Q8_PA);
-            tma_load_2d_pair(sA + fs * Q8_PA, &tmA, fbar, kq * 128 + h * 64, mt * 256 + (int)rank * 128);
-            if (++fs == Q8_FS) {
-              fs = 0;
-              fph ^= 1;
-            }
-          }
         }
       }
-      // Drain: every operand stage's last fill is consumed before this CTA
-      // may exit (no MMA still reads its shared memory, no commit arrives
-      // after exit), and no raw box is still in flight.
-      for (int i = 0; i < Q8_FS; i++) {
-        if (!mbar_wait(&empty[fs], fph ^ 1, budget)) atomicOr(a.err, 16u);
-        if (++fs == Q8_FS) {
-          fs = 0;
-          fph ^= 1;
-        }
-      }
+      // no raw box is still in flight when the CTA exits
       for (int s = 0; s < Q8_RS; s++)
         if (rissued[s] >= 0 && !mbar_wait(&rfull[s], (uint32_t)rissued[s], budget)) atomicOr(a.err, 16u);
     }
@@ -309,13 +282,19 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     }
   } else {
     // Converters: thread t owns W row t of this CTA's half of every stage.
+    // Thread 0 also issues the stage's X box (X is the previous kernel's
+    // output: it waits for that kernel once, before its first X load).
     const int t = threadIdx.x - 192;
     const int sw = t & 7;
+    const bool xload = t == 0;
+    bool waited = false;
     int fs = 0, rs = 0;
     uint32_t fph = 0, rph = 0;
     bool ok = true;
     for (int unit = cluster; unit < total && ok; unit += nclusters) {
-      const int sp = unit / tiles;
+      const int tile = unit % tiles, sp = unit / tiles;
+      int mt, nt;
+      pair_tile(a, tile, mt, nt);
       const int k1 = min(kqn, (sp + 1) * kqs);
       for (int kq = sp * kqs; kq < k1 && ok; kq++) {
         // the lanes agree on the outcome of a wait, so a timeout never splits the warp
@@ -331,6 +310,16 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
             if (lane == 0) atomicOr(a.err, 32u);
             ok = false;
             break;
+          }
+          if (xload) {
+            if (!waited) {
+              pdl_wait();
+              pdl_trigger();
+              waited = true;
+            }
+            if (leader) mbar_expect_tx(&full[fs], 2 * Q8_PA);
+            tma_load_2d_pair(sA + fs * Q8_PA, &tmA, cluster_addr(&full[fs], 0), kq * 128 + h * 64,
+                             mt * 256 + (int)rank * 128);
           }
           uint8_t* dst = sB + fs * Q8_PB + t * 128;
 #pragma unroll
@@ -355,6 +344,22 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         if (++rs == Q8_RS) {
           rs = 0;
           rph ^= 1;
+        }
+      }
+    }
+    if (xload) {
+      if (!waited) {
+        pdl_wait();
+        pdl_trigger();
+      }
+      // Drain: every operand stage's last fill is consumed before this CTA
+      // may exit (no MMA still reads its shared memory, no commit arrives
+      // after exit).
+      for (int i = 0; i < Q8_FS; i++) {
+        if (!mbar_wait(&empty[fs], fph ^ 1, budget)) atomicOr(a.err, 16u);
+        if (++fs == Q8_FS) {
+          fs = 0;
+          fph ^= 1;
         }
       }
     }
