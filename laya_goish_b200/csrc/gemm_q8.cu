@@ -16,6 +16,8 @@
 //   warp 0      weight stream: per 128-column K block one int8 box (128 rows
 //               x 128 B, 128-byte swizzle) and one scale box (4 blocks x 128
 //               rows) into a raw stage, up to Q8_RS stages ahead
+//   warp 10     X stream: per 64-column K block the X box (pair form, counted
+//               on the leader's barrier), up to Q8_XS stages ahead
 //   warp 1      TMEM allocation; on the leader one thread issues
 //               tcgen05.mma.cta_group::2 per operand stage
 //   warps 2..5  epilogue (the F16 GEMM's: bias, residual TMA reduce-add or
@@ -23,13 +25,11 @@
 //   warps 6..9  converters: thread t decodes row t of the raw stage into row t
 //               of the operand stage's W half in the UMMA 128-byte swizzle
 //               (16-byte unit j of row r at (j ^ r % 8) * 16) and arrives on
-//               the leader's barrier of that stage; converter thread 0 also
-//               loads the stage's X box (pair form, counted on the leader's
-//               barrier) as soon as the stage is free
+//               the leader's barrier of that stage
 // Barriers:
-//   full[s]    leader only; 1 arrival (leader's expect_tx of both CTAs' X
-//              boxes) + 8 converter-warp arrivals (4 per CTA) + X bytes
-//   empty[s]   each CTA; the leader's MMA commit to both CTAs
+//   xfull[s]   leader only; 1 arrival (leader's expect_tx) + both CTAs' X bytes
+//   bfull[s]   leader only; 8 converter-warp arrivals (4 per CTA)
+//   x/bempty   each CTA; the leader's MMA commits to both CTAs
 //   rfull[r]   each CTA; its producer's expect_tx + the raw boxes' bytes
 //   rempty[r]  each CTA; 4 converter-warp arrivals
 //   tfull/tempty as in the F16 pair kernel
@@ -45,19 +45,20 @@
 
 namespace laya {
 
-// The raw ring holds the HBM stream in flight: at small M a CTA streams its
-// weight rows as fast as it keeps boxes outstanding (a few microseconds of
-// loaded DRAM latency each), so shared memory goes to 7 raw stages (119 KB of
-// quants) and 2 operand stages, which the converters refill while the MMAs
-// read the other.
-constexpr int Q8_FS = 2;               // operand stages, 64 K columns each
-constexpr int Q8_RS = 7;               // raw stages, 128 K columns each
-constexpr int Q8_THREADS = 320;
+// Shared memory: three rings.  The raw ring holds the HBM weight stream in
+// flight (a CTA streams its weight rows only as fast as it keeps boxes
+// outstanding); the X ring runs ahead of the MMAs by its own depth, since X
+// comes from L2 at about a microsecond per round trip; the converted W ring
+// needs only two stages (the converters fill one while the MMAs read the other).
+constexpr int Q8_XS = 4;               // X stages, 64 K columns each
+constexpr int Q8_FS = 2;               // converted W stages, 64 K columns each
+constexpr int Q8_RS = 5;               // raw stages, 128 K columns each
+constexpr int Q8_THREADS = 352;
 constexpr int Q8_PA = 128 * BK * 2;    // this CTA's 128 X rows of a stage
 constexpr int Q8_PB = 128 * BK * 2;    // this CTA's 128 W rows of a stage, as F16
 constexpr int Q8_RAW = 128 * 128;      // 128 rows x 128 int8 quants
 constexpr int Q8_SCL = 4 * 128 * 2;    // [4 blocks][128 rows] F16 scales
-constexpr int Q8_OFF_B = Q8_FS * Q8_PA;
+constexpr int Q8_OFF_B = Q8_XS * Q8_PA;
 constexpr int Q8_OFF_RAW = Q8_OFF_B + Q8_FS * Q8_PB;
 constexpr int Q8_OFF_SCL = Q8_OFF_RAW + Q8_RS * Q8_RAW;
 constexpr int Q8_OFF_STG = (Q8_OFF_SCL + Q8_RS * Q8_SCL + 1023) / 1024 * 1024;
@@ -65,6 +66,7 @@ constexpr int Q8_OFF_BAR = Q8_OFF_STG + 4 * 2 * 4096;
 constexpr int Q8_SMEM = Q8_OFF_BAR + 256 + 1024;
 static_assert(Q8_SMEM <= 227 * 1024, "Q8_0 pair GEMM shared memory");
 static_assert((Q8_OFF_B | Q8_OFF_RAW | Q8_OFF_STG) % 1024 == 0, "swizzled stages must be 1024-byte aligned");
+static_assert(2 * (Q8_XS + Q8_FS + Q8_RS + 4) * 8 + 4 <= 256, "Q8_0 pair GEMM barriers");
 
 // Row layout of the W operand across its tensors (see Q8Weights).
 struct Q8Seg {
@@ -111,6 +113,15 @@ __device__ __forceinline__ void q8_decode16(uint4 v, __half2 d, uint4& lo, uint4
   hi = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
+// Advances a ring position and flips its phase bit on wrap-around.
+template <int N>
+__device__ __forceinline__ void ring_next(int& s, uint32_t& ph) {
+  if (++s == N) {
+    s = 0;
+    ph ^= 1;
+  }
+}
+
 template <int EPI, int HD>
 __global__ void __launch_bounds__(Q8_THREADS, 1)
     gemm_q8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ0,
@@ -123,9 +134,11 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
   uint8_t* sB = smem + Q8_OFF_B;
   uint8_t* sRaw = smem + Q8_OFF_RAW;
   uint8_t* sScl = smem + Q8_OFF_SCL;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Q8_OFF_BAR);
-  uint64_t* empty = full + Q8_FS;
-  uint64_t* rfull = empty + Q8_FS;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + Q8_OFF_BAR);
+  uint64_t* xempty = xfull + Q8_XS;
+  uint64_t* bfull = xempty + Q8_XS;
+  uint64_t* bempty = bfull + Q8_FS;
+  uint64_t* rfull = bempty + Q8_FS;
   uint64_t* rempty = rfull + Q8_RS;
   uint64_t* tfull = rempty + Q8_RS;
   uint64_t* tempty = tfull + 2;
@@ -135,9 +148,13 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   if (threadIdx.x == 0) {
+    for (int s = 0; s < Q8_XS; s++) {
+      mbar_init(&xfull[s], 1);  // leader: its expect_tx of both CTAs' X boxes
+      mbar_init(&xempty[s], 1);
+    }
     for (int s = 0; s < Q8_FS; s++) {
-      mbar_init(&full[s], 1 + 8);
-      mbar_init(&empty[s], 1);
+      mbar_init(&bfull[s], 8);  // leader: 4 converter warps of each CTA
+      mbar_init(&bempty[s], 1);
     }
     for (int s = 0; s < Q8_RS; s++) {
       mbar_init(&rfull[s], 1);
@@ -200,21 +217,50 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
           mbar_expect_tx(&rfull[rs], Q8_RAW + Q8_SCL);
           tma_load_2d(sRaw + rs * Q8_RAW, tq, &rfull[rs], kq * 128, lr);
           tma_load_2d(sScl + rs * Q8_SCL, &tmS, &rfull[rs], R0, kq * 4);
-          if (++rs == Q8_RS) {
-            rs = 0;
-            rph ^= 1;
-          }
+          ring_next<Q8_RS>(rs, rph);
         }
       }
       // no raw box is still in flight when the CTA exits
       for (int s = 0; s < Q8_RS; s++)
         if (rissued[s] >= 0 && !mbar_wait(&rfull[s], (uint32_t)rissued[s], budget)) atomicOr(a.err, 16u);
     }
+  } else if (warp == 10) {
+    if (elect_one()) {
+      // X stream (the previous kernel's output): one box per 64 K columns,
+      // counted on the leader's barrier, up to Q8_XS stages ahead of the MMAs.
+      pdl_wait();
+      pdl_trigger();
+      int xs = 0;
+      uint32_t xph = 0;
+      bool ok = true;
+      for (int unit = cluster; unit < total && ok; unit += nclusters) {
+        const int tile = unit % tiles, sp = unit / tiles;
+        int mt, nt;
+        pair_tile(a, tile, mt, nt);
+        const int k1 = min(kqn, (sp + 1) * kqs);
+        for (int kb = 2 * sp * kqs; kb < 2 * k1; kb++) {
+          if (!mbar_wait(&xempty[xs], xph ^ 1, budget)) {
+            atomicOr(a.err, 1u);
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&xfull[xs], 2 * Q8_PA);
+          tma_load_2d_pair(sA + xs * Q8_PA, &tmA, cluster_addr(&xfull[xs], 0), kb * 64, mt * 256 + (int)rank * 128);
+          ring_next<Q8_XS>(xs, xph);
+        }
+      }
+      // Drain: every X stage's last fill is consumed before this CTA may exit
+      // (no MMA still reads its shared memory, no commit arrives after exit).
+      for (int i = 0; i < Q8_XS; i++) {
+        if (!mbar_wait(&xempty[xs], xph ^ 1, budget)) atomicOr(a.err, 16u);
+        ring_next<Q8_XS>(xs, xph);
+      }
+    }
   } else if (warp == 1) {
     if (leader && elect_one()) {
       const uint32_t idesc = idesc_f16_f32(256, BN);
-      int fs = 0, acc = 0;
-      uint32_t fph = 0, acc_phase = 0;
+      int xs = 0, fs = 0, acc = 0;
+      uint32_t xph = 0, fph = 0, acc_phase = 0;
       bool ok = true;
       for (int unit = cluster; unit < total && ok; unit += nclusters) {
         const int sp = unit / tiles, k0 = sp * kqs, k1 = min(kqn, k0 + kqs);
@@ -225,23 +271,22 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
         for (int kb = 2 * k0; kb < 2 * k1; kb++) {
-          // converters of both CTAs release their W halves at cluster scope
-          if (!mbar_wait_cluster(&full[fs], fph, budget)) {
+          // X by TMA; W halves released by both CTAs' converters at cluster scope
+          if (!mbar_wait(&xfull[xs], xph, budget) || !mbar_poll_cluster(&bfull[fs], fph, budget)) {
             atomicOr(a.err, 4u);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sw128_desc(smem_u32(sA + fs * Q8_PA));
+          const uint64_t ad = sw128_desc(smem_u32(sA + xs * Q8_PA));
           const uint64_t bd = sw128_desc(smem_u32(sB + fs * Q8_PB));
 #pragma unroll
           for (int k = 0; k < BK / 16; k++)
             umma_f16_pair(tmem_d, ad + 2 * k, bd + 2 * k, idesc, (kb != 2 * k0 || k != 0) ? 1u : 0u);
-          umma_commit_pair(&empty[fs], 0x3);
-          if (++fs == Q8_FS) {
-            fs = 0;
-            fph ^= 1;
-          }
+          umma_commit_pair(&xempty[xs], 0x3);
+          umma_commit_pair(&bempty[fs], 0x3);
+          ring_next<Q8_XS>(xs, xph);
+          ring_next<Q8_FS>(fs, fph);
         }
         umma_commit_pair(&tfull[acc], 0x3);
         if (++acc == 2) {
@@ -281,20 +326,15 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
       }
     }
   } else {
-    // Converters: thread t owns W row t of this CTA's half of every stage.
-    // Thread 0 also issues the stage's X box (X is the previous kernel's
-    // output: it waits for that kernel once, before its first X load).
+    // Converters (warps 6..9): thread t owns W row t of this CTA's half of
+    // every stage.
     const int t = threadIdx.x - 192;
     const int sw = t & 7;
-    const bool xload = t == 0;
-    bool waited = false;
     int fs = 0, rs = 0;
     uint32_t fph = 0, rph = 0;
     bool ok = true;
     for (int unit = cluster; unit < total && ok; unit += nclusters) {
-      const int tile = unit % tiles, sp = unit / tiles;
-      int mt, nt;
-      pair_tile(a, tile, mt, nt);
+      const int sp = unit / tiles;
       const int k1 = min(kqn, (sp + 1) * kqs);
       for (int kq = sp * kqs; kq < k1 && ok; kq++) {
         // the lanes agree on the outcome of a wait, so a timeout never splits the warp
@@ -306,20 +346,10 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         const uint8_t* raw = sRaw + rs * Q8_RAW + t * 128;
         const __half* scl = reinterpret_cast<const __half*>(sScl + rs * Q8_SCL);
         for (int h = 0; h < 2; h++) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&empty[fs], fph ^ 1, budget))) {
+          if (!__all_sync(0xffffffffu, mbar_poll_cluster(&bempty[fs], fph ^ 1, budget))) {
             if (lane == 0) atomicOr(a.err, 32u);
             ok = false;
             break;
-          }
-          if (xload) {
-            if (!waited) {
-              pdl_wait();
-              pdl_trigger();
-              waited = true;
-            }
-            if (leader) mbar_expect_tx(&full[fs], 2 * Q8_PA);
-            tma_load_2d_pair(sA + fs * Q8_PA, &tmA, cluster_addr(&full[fs], 0), kq * 128 + h * 64,
-                             mt * 256 + (int)rank * 128);
           }
           uint8_t* dst = sB + fs * Q8_PB + t * 128;
 #pragma unroll
@@ -333,36 +363,19 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
           }
           fence_async_smem();  // the tensor cores read what this thread wrote
           __syncwarp();
-          if (lane == 0) mbar_arrive_remote(cluster_addr(&full[fs], 0));
-          if (++fs == Q8_FS) {
-            fs = 0;
-            fph ^= 1;
-          }
+          if (lane == 0) mbar_arrive_remote(cluster_addr(&bfull[fs], 0));
+          ring_next<Q8_FS>(fs, fph);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[rs]);
-        if (++rs == Q8_RS) {
-          rs = 0;
-          rph ^= 1;
-        }
+        ring_next<Q8_RS>(rs, rph);
       }
     }
-    if (xload) {
-      if (!waited) {
-        pdl_wait();
-        pdl_trigger();
-      }
-      // Drain: every operand stage's last fill is consumed before this CTA
-      // may exit (no MMA still reads its shared memory, no commit arrives
-      // after exit).
+    if (t == 0)  // every converted stage consumed before exit
       for (int i = 0; i < Q8_FS; i++) {
-        if (!mbar_wait(&empty[fs], fph ^ 1, budget)) atomicOr(a.err, 16u);
-        if (++fs == Q8_FS) {
-          fs = 0;
-          fph ^= 1;
-        }
+        if (!mbar_wait(&bempty[fs], fph ^ 1, budget)) atomicOr(a.err, 16u);
+        ring_next<Q8_FS>(fs, fph);
       }
-    }
   }
   if constexpr (EPI == EPI_RESID)
     if (warp >= 2 && warp < 6 && lane == 0) bulk_wait<0>();  // residual reductions complete before exit

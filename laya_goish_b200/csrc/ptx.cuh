@@ -90,26 +90,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long l
   return true;
 }
 
-// Bounded wait with acquire at cluster scope: for a barrier that other CTAs
-// of the cluster arrive on (release.cluster) after writing their own shared
-// memory, which this thread's tensor-core instructions then read.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+// Bounded poll with test_wait (acquire at cluster scope), which never
+// suspends the thread: for barriers completed by arrivals from the other CTA
+// of a pair, where a thread suspended in try_wait may only notice the
+// completion at the end of its suspend window.
+__device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred P;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "{\n\t.reg .pred P;\n\tmbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, P;\n\t}\n"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, long long budget) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_poll_cluster(uint64_t* bar, uint32_t parity, long long budget) {
+  if (mbar_test_cluster(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (clock64() - t0 > budget) return false;
+  for (unsigned i = 1;; i++) {
+    if (mbar_test_cluster(bar, parity)) return true;
+    if ((i & 63) == 0 && clock64() - t0 > budget) return false;
   }
-  return true;
 }
 
 // ---------------------------------------------------------------- TMA
