@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
           }
           fence_async_smem();  // the tensor cores read what this thread wrote
           __syncwarp();
-          if (lane == 0) mbar_arrive_remote(cluster_addr(&bfull[fs], 0));
+          if (lane == 0) mbar_arrive_peer(cluster_addr(&bfull[fs], 0));
           ring_next<Q8_FS>(fs, fph);
         }
         __syncwarp();

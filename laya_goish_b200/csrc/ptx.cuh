@@ -164,6 +164,13 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
   return r;
 }
+// Arrive on a barrier of another CTA of the cluster with the default
+// (CTA-scope) release: after fence.proxy.async, for shared-memory operands
+// written with ordinary stores that the peer's tensor-core instructions read;
+// it does not pay for a cluster-wide memory fence per arrival.
+__device__ __forceinline__ void mbar_arrive_peer(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
