@@ -49,10 +49,11 @@ namespace laya {
 // flight (a CTA streams its weight rows only as fast as it keeps boxes
 // outstanding); the X ring runs ahead of the MMAs by its own depth, since X
 // comes from L2 at about a microsecond per round trip; the converted W ring
-// needs only two stages (the converters fill one while the MMAs read the other).
-constexpr int Q8_XS = 4;               // X stages, 64 K columns each
-constexpr int Q8_FS = 2;               // converted W stages, 64 K columns each
-constexpr int Q8_RS = 5;               // raw stages, 128 K columns each
+// lets the converters work two stages ahead of the MMAs, so that the barrier
+// hand-offs between them (commit -> converters -> leader) overlap the MMAs.
+constexpr int Q8_XS = 3;               // X stages, 64 K columns each
+constexpr int Q8_FS = 4;               // converted W stages, 64 K columns each
+constexpr int Q8_RS = 4;               // raw stages, 128 K columns each
 constexpr int Q8_THREADS = 352;
 constexpr int Q8_PA = 128 * BK * 2;    // this CTA's 128 X rows of a stage
 constexpr int Q8_PB = 128 * BK * 2;    // this CTA's 128 W rows of a stage, as F16
