@@ -23,7 +23,7 @@
 //   warps 2..5  epilogue (the F16 GEMM's: bias, residual TMA reduce-add or
 //               K-split planes, SwiGLU, QKV + RoPE + paged KV cache)
 //   warps 6..9  converters: thread t decodes row t of the raw stage into row t
-//               of the operand stage's W half in the UMMA 128-byte swizzle
+//               of two operand stages' W halves in the UMMA 128-byte swizzle
 //               (16-byte unit j of row r at (j ^ r % 8) * 16) and arrives on
 //               the leader's barrier of that stage
 // Barriers:
@@ -67,6 +67,7 @@ constexpr int Q8_OFF_BAR = Q8_OFF_STG + 4 * 2 * 4096;
 constexpr int Q8_SMEM = Q8_OFF_BAR + 256 + 1024;
 static_assert(Q8_SMEM <= 227 * 1024, "Q8_0 pair GEMM shared memory");
 static_assert((Q8_OFF_B | Q8_OFF_RAW | Q8_OFF_STG) % 1024 == 0, "swizzled stages must be 1024-byte aligned");
+static_assert(Q8_FS % 2 == 0, "a raw stage fills two consecutive operand stages of one phase");
 static_assert(2 * (Q8_XS + Q8_FS + Q8_RS + 4) * 8 + 4 <= 256, "Q8_0 pair GEMM barriers");
 
 // Row layout of the W operand across its tensors (see Q8Weights).
@@ -346,27 +347,41 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         }
         const uint8_t* raw = sRaw + rs * Q8_RAW + t * 128;
         const __half* scl = reinterpret_cast<const __half*>(sScl + rs * Q8_SCL);
-        for (int h = 0; h < 2; h++) {
-          if (!__all_sync(0xffffffffu, mbar_poll_cluster(&bempty[fs], fph ^ 1, budget))) {
-            if (lane == 0) atomicOr(a.err, 32u);
-            ok = false;
-            break;
-          }
-          uint8_t* dst = sB + fs * Q8_PB + t * 128;
-#pragma unroll
-          for (int cc = 0; cc < 4; cc++) {
-            const int c = 4 * h + cc;  // 16-quant unit of the raw row; scale block c / 2
-            const uint4 v = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
-            uint4 lo, hi;
-            q8_decode16(v, __half2half2(scl[(c >> 1) * 128 + t]), lo, hi);
-            *reinterpret_cast<uint4*>(dst + (((2 * cc) ^ sw) << 4)) = lo;
-            *reinterpret_cast<uint4*>(dst + (((2 * cc + 1) ^ sw) << 4)) = hi;
-          }
-          fence_async_smem();  // the tensor cores read what this thread wrote
-          __syncwarp();
-          if (lane == 0) mbar_arrive_peer(cluster_addr(&bfull[fs], 0));
-          ring_next<Q8_FS>(fs, fph);
+        // both 64-column halves of the raw stage go to operand stages fs and
+        // fs + 1 (same phase: the ring has an even number of stages)
+        if (!__all_sync(0xffffffffu, mbar_poll_cluster(&bempty[fs], fph ^ 1, budget) &&
+                                         mbar_poll_cluster(&bempty[fs + 1], fph ^ 1, budget))) {
+          if (lane == 0) atomicOr(a.err, 32u);
+          ok = false;
+          break;
         }
+        uint8_t* dst0 = sB + fs * Q8_PB + t * 128;
+        uint8_t* dst1 = dst0 + Q8_PB;
+        // eight independent 16-quant units per thread: loads first, then the
+        // decodes, so their latencies overlap
+        uint4 v[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) v[c] = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
+        __half2 d[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) d[j] = __half2half2(scl[j * 128 + t]);
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          uint4 lo, hi;
+          q8_decode16(v[c], d[c >> 1], lo, hi);
+          uint8_t* dst = c < 4 ? dst0 : dst1;
+          const int j = 2 * (c & 3);
+          *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = lo;
+          *reinterpret_cast<uint4*>(dst + (((j + 1) ^ sw) << 4)) = hi;
+        }
+        fence_async_smem();  // the tensor cores read what this thread wrote
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_peer(cluster_addr(&bfull[fs], 0));
+          mbar_arrive_peer(cluster_addr(&bfull[fs + 1], 0));
+        }
+        ring_next<Q8_FS>(fs, fph);
+        ring_next<Q8_FS>(fs, fph);
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[rs]);
         ring_next<Q8_RS>(rs, rph);
