@@ -482,6 +482,9 @@ def run_aux(args):
     from laya_goish_b200 import engine
 
     cname, requests, tokens, qdesc, desc = AUX[args.workload]
+    if args.tokens:
+        tokens = args.tokens
+        desc += f" (prompt cut to {tokens} tokens)"
     cfg = synth.CONFIGS[cname]
     path = synth.model_path(cname)
     rng = np.random.default_rng(1000)
@@ -757,6 +760,7 @@ def main():
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "decode", "cfg0", "cfg0q8", "cfg2", "cfg3", "load", "openthai", "inproc"])
     ap.add_argument("--load-cfg", default="cfg3", help="load: synthetic model to open")
     ap.add_argument("--batch", type=int, default=1, help="decode: sequences per GPU")
+    ap.add_argument("--tokens", type=int, default=0, help="cfg0/cfg0q8/cfg2/cfg3: prompt tokens instead of the configured length")
     ap.add_argument("--ctx", type=int, default=4096, help="decode: context tokens")
     ap.add_argument("--gen", type=int, default=128, help="decode: generated tokens")
     ap.add_argument("--ot-tokens", type=int, default=1024, help="openthai: tokens per pass")
