@@ -20,18 +20,20 @@
 //               on the leader's barrier), up to Q8_XS stages ahead
 //   warp 1      TMEM allocation; on the leader one thread issues
 //               tcgen05.mma.cta_group::2 per operand stage
-//   warps 2..5  epilogue (the F16 GEMM's: bias, residual TMA reduce-add or
-//               K-split planes, SwiGLU, QKV + RoPE + paged KV cache)
-//   warps 6..9  converters: thread t decodes row t of the raw stage into row t
-//               of two operand stages' W halves in the UMMA 128-byte swizzle
-//               (16-byte unit j of row r at (j ^ r % 8) * 16) and arrives on
-//               the leader's barrier of that stage
+//   warps 6..9  converters: thread t decodes the first 64 columns of row t of
+//               each raw stage into row t of an operand stage's W half in the
+//               UMMA 128-byte swizzle (16-byte unit j of row r at
+//               (j ^ r % 8) * 16) and arrives on the leader's barrier of that
+//               stage
+//   warps 2..5  the second 64 columns the same way while the unit's MMAs run,
+//               then the epilogue (the F16 GEMM's: bias, residual TMA
+//               reduce-add or K-split planes, SwiGLU, QKV + RoPE + paged KV)
 // Barriers:
 //   xfull[s]   leader only; 1 arrival (leader's expect_tx) + both CTAs' X bytes
 //   bfull[s]   leader only; 8 converter-warp arrivals (4 per CTA)
 //   x/bempty   each CTA; the leader's MMA commits to both CTAs
 //   rfull[r]   each CTA; its producer's expect_tx + the raw boxes' bytes
-//   rempty[r]  each CTA; 4 converter-warp arrivals
+//   rempty[r]  each CTA; 8 converter-warp arrivals (4 per half)
 //   tfull/tempty as in the F16 pair kernel
 // Every TMA load reads this GPU's own memory into the issuing CTA's own
 // shared memory.  Every wait is bounded and a timeout sets a bit of a.err.
@@ -124,6 +126,53 @@ __device__ __forceinline__ void ring_next(int& s, uint32_t& ph) {
   }
 }
 
+// Decodes, for the raw stages of K blocks k0..k1-1 of one work unit, the
+// 64-column half `half` of weight row t into operand stage fs + half (each
+// raw stage fills operand stages fs and fs + 1, which share a phase), then
+// arrives on the leader's barrier of that stage and releases the raw stage.
+// Four warps per CTA take each half.  False after a timed-out wait (the
+// lanes agree on the outcome of every wait, so a timeout never splits a warp).
+__device__ __forceinline__ bool q8_convert_unit(int k0, int k1, int t, int half, int lane, const uint8_t* sRaw,
+                                                const uint8_t* sScl, uint8_t* sB, uint64_t* rfull, uint64_t* rempty,
+                                                uint64_t* bfull, uint64_t* bempty, int& fs, uint32_t& fph, int& rs,
+                                                uint32_t& rph, long long budget, unsigned* err) {
+  const int sw = t & 7;
+  for (int kq = k0; kq < k1; kq++) {
+    const int os = fs + half;
+    if (!__all_sync(0xffffffffu, mbar_wait(&rfull[rs], rph, budget)) ||
+        !__all_sync(0xffffffffu, mbar_poll_cluster(&bempty[os], fph ^ 1, budget))) {
+      if (lane == 0) atomicOr(err, 32u);
+      return false;
+    }
+    const uint8_t* raw = sRaw + rs * Q8_RAW + t * 128;
+    const __half* scl = reinterpret_cast<const __half*>(sScl + rs * Q8_SCL);
+    // four independent 16-quant units per thread: loads first, then the
+    // decodes, so their latencies overlap
+    uint4 v[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) v[c] = *reinterpret_cast<const uint4*>(raw + (((4 * half + c) ^ sw) << 4));
+    const __half2 d0 = __half2half2(scl[(2 * half) * 128 + t]), d1 = __half2half2(scl[(2 * half + 1) * 128 + t]);
+    uint8_t* dst = sB + os * Q8_PB + t * 128;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      uint4 lo, hi;
+      q8_decode16(v[c], c < 2 ? d0 : d1, lo, hi);
+      *reinterpret_cast<uint4*>(dst + (((2 * c) ^ sw) << 4)) = lo;
+      *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ sw) << 4)) = hi;
+    }
+    fence_async_smem();  // the tensor cores read what this thread wrote
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive_peer(cluster_addr(&bfull[os], 0));
+      mbar_arrive(&rempty[rs]);
+    }
+    ring_next<Q8_FS>(fs, fph);
+    ring_next<Q8_FS>(fs, fph);
+    ring_next<Q8_RS>(rs, rph);
+  }
+  return true;
+}
+
 template <int EPI, int HD>
 __global__ void __launch_bounds__(Q8_THREADS, 1)
     gemm_q8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ0,
@@ -160,7 +209,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     }
     for (int s = 0; s < Q8_RS; s++) {
       mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], 4);
+      mbar_init(&rempty[s], 8);  // 4 converter warps per half
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
@@ -298,15 +347,26 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
       }
     }
   } else if (warp < 6) {
-    pdl_wait();  // outputs and residual rows may be in use by the previous kernel until it ends
+    // Epilogue warps: while a unit's MMAs run they decode the second
+    // 64-column half of each raw stage, then read the unit's accumulator.
     const int quarter = warp % 4;
     uint8_t* stg = smem + Q8_OFF_STG + quarter * 2 * 4096;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int fs = 0, rs = 0;
+    uint32_t fph = 0, rph = 0;
+    bool cok = true, waited = false;
     for (int unit = cluster; unit < total; unit += nclusters) {
-      const int tile = unit % tiles;
+      const int tile = unit % tiles, sp = unit / tiles;
       int mt, nt;
       pair_tile(a, tile, mt, nt);
+      if (cok)
+        cok = q8_convert_unit(sp * kqs, min(kqn, (sp + 1) * kqs), (warp - 2) * 32 + lane, 1, lane, sRaw, sScl, sB,
+                              rfull, rempty, bfull, bempty, fs, fph, rs, rph, budget, a.err);
+      if (!waited) {
+        pdl_wait();  // outputs and residual rows may be in use by the previous kernel until it ends
+        waited = true;
+      }
       const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
       if (!mbar_wait(&tfull[acc], acc_phase, budget)) {
         atomicOr(a.err, 8u);
@@ -328,64 +388,16 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
       }
     }
   } else {
-    // Converters (warps 6..9): thread t owns W row t of this CTA's half of
-    // every stage.
+    // Converters (warps 6..9): the first 64-column half of each raw stage,
+    // thread t owning weight row t of this CTA's half of the tile.
     const int t = threadIdx.x - 192;
-    const int sw = t & 7;
     int fs = 0, rs = 0;
     uint32_t fph = 0, rph = 0;
-    bool ok = true;
-    for (int unit = cluster; unit < total && ok; unit += nclusters) {
+    for (int unit = cluster; unit < total; unit += nclusters) {
       const int sp = unit / tiles;
-      const int k1 = min(kqn, (sp + 1) * kqs);
-      for (int kq = sp * kqs; kq < k1 && ok; kq++) {
-        // the lanes agree on the outcome of a wait, so a timeout never splits the warp
-        if (!__all_sync(0xffffffffu, mbar_wait(&rfull[rs], rph, budget))) {
-          if (lane == 0) atomicOr(a.err, 32u);
-          ok = false;
-          break;
-        }
-        const uint8_t* raw = sRaw + rs * Q8_RAW + t * 128;
-        const __half* scl = reinterpret_cast<const __half*>(sScl + rs * Q8_SCL);
-        // both 64-column halves of the raw stage go to operand stages fs and
-        // fs + 1 (same phase: the ring has an even number of stages)
-        if (!__all_sync(0xffffffffu, mbar_poll_cluster(&bempty[fs], fph ^ 1, budget) &&
-                                         mbar_poll_cluster(&bempty[fs + 1], fph ^ 1, budget))) {
-          if (lane == 0) atomicOr(a.err, 32u);
-          ok = false;
-          break;
-        }
-        uint8_t* dst0 = sB + fs * Q8_PB + t * 128;
-        uint8_t* dst1 = dst0 + Q8_PB;
-        // eight independent 16-quant units per thread: loads first, then the
-        // decodes, so their latencies overlap
-        uint4 v[8];
-#pragma unroll
-        for (int c = 0; c < 8; c++) v[c] = *reinterpret_cast<const uint4*>(raw + ((c ^ sw) << 4));
-        __half2 d[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) d[j] = __half2half2(scl[j * 128 + t]);
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          uint4 lo, hi;
-          q8_decode16(v[c], d[c >> 1], lo, hi);
-          uint8_t* dst = c < 4 ? dst0 : dst1;
-          const int j = 2 * (c & 3);
-          *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = lo;
-          *reinterpret_cast<uint4*>(dst + (((j + 1) ^ sw) << 4)) = hi;
-        }
-        fence_async_smem();  // the tensor cores read what this thread wrote
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_peer(cluster_addr(&bfull[fs], 0));
-          mbar_arrive_peer(cluster_addr(&bfull[fs + 1], 0));
-        }
-        ring_next<Q8_FS>(fs, fph);
-        ring_next<Q8_FS>(fs, fph);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rempty[rs]);
-        ring_next<Q8_RS>(rs, rph);
-      }
+      if (!q8_convert_unit(sp * kqs, min(kqn, (sp + 1) * kqs), t, 0, lane, sRaw, sScl, sB, rfull, rempty, bfull,
+                           bempty, fs, fph, rs, rph, budget, a.err))
+        break;
     }
     if (t == 0)  // every converted stage consumed before exit
       for (int i = 0; i < Q8_FS; i++) {
