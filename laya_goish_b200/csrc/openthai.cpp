@@ -70,18 +70,44 @@ int dalloc(Model& m, size_t bytes, void** p) {
   return 0;
 }
 
-// The tensor's elements as F32 on the host (F32 or F16 tensors).
+// Decodes a block-quantised tensor (Q8_0, Q4_0, Q4_K, Q6_K) into `dst`, a
+// device buffer of t->count() floats, with the reference decoder's block
+// arithmetic (gguf::decode, src/gguf.rs:250-336; the values are bit-identical).
+int decode_on_device(const Gguf& g, const TensorInfo* t, const std::string& name, float* dst) {
+  int block = 0, size = 0;
+  if (!ggml_layout(t->kind, &block, &size) || t->count() % block)
+    return fail(LAYA_E_FORMAT, name + ": unsupported tensor type for OpenThai");
+  void* raw = nullptr;
+  LAYA_CK(cudaMalloc(&raw, t->len ? t->len : 16));
+  cudaError_t e = cudaMemcpy(raw, g.data(*t), t->len, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = dequant_raw((int)t->kind, static_cast<const uint8_t*>(raw), t->count() / block, dst, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(raw);
+  if (e != cudaSuccess) return cuda_fail(e, "OpenThai tensor decode");
+  return 0;
+}
+
+// The tensor's elements as F32 on the host: F32 / F16 read directly, the
+// block-quantised types decoded as the reference decodes them when it
+// loads the model (g.floats, src/models/openthai/model.rs:61).
 int host_f32(const Gguf& g, const std::string& name, size_t count, std::vector<float>* out) {
   const TensorInfo* t = g.tensor(name);
   if (!t) return fail(LAYA_E_FORMAT, "missing tensor " + name);
   if (t->count() != count) return fail(LAYA_E_FORMAT, name + ": unexpected shape");
-  if (t->kind != K_F32 && t->kind != K_F16) return fail(LAYA_E_FORMAT, name + ": only F32/F16 OpenThai tensors");
   out->resize(count);
   const uint8_t* d = g.data(*t);
   if (t->kind == K_F32) {
     std::memcpy(out->data(), d, count * 4);
-  } else {
+  } else if (t->kind == K_F16) {
     for (size_t i = 0; i < count; i++) (*out)[i] = half_bits((uint16_t)(d[2 * i] | (d[2 * i + 1] << 8)));
+  } else {
+    void* f = nullptr;
+    LAYA_CK(cudaMalloc(&f, count * 4));
+    int rc = decode_on_device(g, t, name, static_cast<float*>(f));
+    cudaError_t e = rc ? cudaSuccess : cudaMemcpy(out->data(), f, count * 4, cudaMemcpyDeviceToHost);
+    cudaFree(f);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "OpenThai tensor read-back");
   }
   return 0;
 }
@@ -164,14 +190,20 @@ int load(Model& m, const Gguf& g, const uint8_t* layer_full) {
   const int d = c.d, H = c.heads, KV = c.kv_heads, hd = c.head_dim, nh = c.lin_heads, hk = c.lin_dim;
   const int w = nh * hk;
   const TensorInfo* e = g.tensor("model.embed_tokens.weight");
-  if (!e || e->dims.size() != 2 || e->dims[0] != (uint64_t)d || e->dims[1] != (uint64_t)c.vocab ||
-      (e->kind != K_F32 && e->kind != K_F16))
-    return fail(LAYA_E_FORMAT, "OpenThai embeddings must be F32/F16 with shape [vocab, hidden]");
+  if (!e || e->dims.size() != 2 || e->dims[0] != (uint64_t)d || e->dims[1] != (uint64_t)c.vocab)
+    return fail(LAYA_E_FORMAT, "OpenThai embeddings must have shape [vocab, hidden]");
   void* pe;
-  if (int rc = dalloc(m, e->len, &pe)) return rc;
-  LAYA_CK(cudaMemcpy(pe, g.data(*e), e->len, cudaMemcpyHostToDevice));
   m.embd = QTensor{};
-  m.embd.kind = (int)e->kind;
+  if (e->kind == K_F32 || e->kind == K_F16) {
+    if (int rc = dalloc(m, e->len, &pe)) return rc;
+    LAYA_CK(cudaMemcpy(pe, g.data(*e), e->len, cudaMemcpyHostToDevice));
+    m.embd.kind = (int)e->kind;
+  } else {
+    // a block-quantised table is decoded once to F32, the rows the reference gathers
+    if (int rc = dalloc(m, (size_t)c.vocab * d * 4, &pe)) return rc;
+    if (int rc = decode_on_device(g, e, "model.embed_tokens.weight", static_cast<float*>(pe))) return rc;
+    m.embd.kind = K_F32;
+  }
   m.embd.rows = c.vocab;
   m.embd.cols = d;
   m.embd.q = static_cast<const uint8_t*>(pe);

@@ -110,13 +110,16 @@ def _parse(buf, tensors: bool = False):
 
 
 _ELEM = {0: (4, "<f4"), 1: (2, "<f2")}
+# (elements, bytes) per block of the block-quantised GGML types (src/gguf.rs:81-93)
+_BLOCK = {2: (32, 18), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
 
 
-def read_tensors_f32(path: str, names=None) -> tuple[dict, dict]:
+def read_tensors_f32(path: str, names=None, decode=None) -> tuple[dict, dict]:
     """Metadata and the F32 / F16 tensors of a GGUF file (all of them, or
     those in `names`) as F32 arrays of shape dims reversed (GGUF dims are
-    innermost first: a matrix [K, N] is N rows of K).  Other tensor types
-    raise GGUFError."""
+    innermost first: a matrix [K, N] is N rows of K).  Block-quantised
+    tensors (Q4_0, Q8_0, Q4_K, Q6_K) go through `decode(kind, raw_bytes)`
+    when one is given; without it, and for other types, GGUFError."""
     import numpy as np
 
     with open(path, "rb") as f:
@@ -128,13 +131,20 @@ def read_tensors_f32(path: str, names=None) -> tuple[dict, dict]:
                 for name, dims, kind, off in infos:
                     if names is not None and name not in names:
                         continue
-                    if kind not in _ELEM:
-                        raise GGUFError(f"{name}: tensor type {kind} is not F32/F16")
-                    size, dt = _ELEM[kind]
                     n = 1
                     for d in dims:
                         n *= d
                     start = base + off
+                    if kind in _BLOCK and decode is not None:
+                        block, bsize = _BLOCK[kind]
+                        if n % block or start + n // block * bsize > len(data):
+                            raise GGUFError(f"{name}: tensor data out of range")
+                        a = np.asarray(decode(kind, bytes(mv[start:start + n // block * bsize])), np.float32)
+                        out[name] = a.reshape(list(reversed(dims))) if dims else a
+                        continue
+                    if kind not in _ELEM:
+                        raise GGUFError(f"{name}: tensor type {kind} is not F32/F16")
+                    size, dt = _ELEM[kind]
                     if start + n * size > len(data):
                         raise GGUFError(f"{name}: tensor data out of range")
                     a = np.frombuffer(mv[start:start + n * size], dtype=dt, count=n).astype(np.float32)

@@ -321,12 +321,13 @@ def load_config(meta: dict, strict: bool = True) -> dict:
             "max_tokens": max_tokens, "max_state": max_state}
 
 
-def load_weights(path: str, strict: bool = True) -> dict:
+def load_weights(path: str, strict: bool = True, decode=None) -> dict:
     """Config and F32 weights of an OpenThai GGUF under its tensor names
-    (model.rs:103-174), with `temperature` = exp(log_temperature)."""
+    (model.rs:103-174), with `temperature` = exp(log_temperature).
+    Block-quantised tensors need `decode(kind, raw_bytes)`."""
     from .gguf_meta import read_tensors_f32
 
-    meta, t = read_tensors_f32(path)
+    meta, t = read_tensors_f32(path, decode=decode)
     cfg = load_config(meta, strict)
     t["config"] = cfg
     t["temperature"] = np.exp(t["log_temperature"].astype(np.float32)).astype(np.float32)

@@ -2,8 +2,9 @@
 src/models/openthai/model.rs: the gated DeltaNet recurrence
 (laya_gated_delta, Delta::run 322-355) and its whole mixer after the
 projections, the gated attention (Full::run 248-296), the native forward
-(laya_openthai_forward, Model::forward 192-241) and a whole decision through
-it.  Parity of the forward with the reference itself is unpinned (its
+(laya_openthai_forward, Model::forward 192-241), with F16 or block-quantised
+matrices (Q8_0, Q4_K: decoded at load as the reference's g.floats does), and
+a whole decision through it.  Parity of the forward with the reference itself is unpinned (its
 goldens need the real OpenThai weights)."""
 import numpy as np
 import pytest
@@ -222,3 +223,26 @@ def test_openthai_batch_over_two_gpus(tmp_path):
     assert one.status == two.status == 200
     strip = lambda b: [{k: v for k, v in r.items() if k not in ("usage", "id")} for r in b["results"]]
     assert strip(one.body) == strip(two.body)
+
+
+@pytest.mark.parametrize("quant,shape", [
+    (8, dict(d=128, ffn=256, heads=4, kv=2, hd=64, lin_heads=2, lin_dim=64)),      # Q8_0
+    (12, dict(d=256, ffn=512, heads=4, kv=2, hd=64, lin_heads=2, lin_dim=128)),    # Q4_K
+])
+def test_openthai_forward_quantised_matrices_match_oracle(tmp_path, quant, shape):
+    # every matrix and the embedding table in a block type: the library
+    # decodes them at load with the reference's block arithmetic
+    # (src/models/openthai/model.rs:61, src/gguf.rs:250-336); the oracle gets
+    # the same values from its own pinned decoder
+    from laya_goish_b200 import openthai, synth
+
+    path = synth.write_openthai(str(tmp_path / f"ot_q{quant}.gguf"), seed=12, quant=quant, **shape)
+    w = openthai.load_weights(path, strict=False, decode=oracle.decode)
+    rng = np.random.default_rng(5)
+    with openthai.Model(path, strict=False) as m:
+        for s, pos in [(33, [0, 16, 32]), (130, [7, 129])]:
+            ids = rng.integers(0, 300, s)
+            got = m.forward(ids, pos)
+            want = oracle.ot_forward(w, ids, pos)
+            tol = 5e-3 * np.abs(want).max()
+            assert np.abs(got - want).max() < tol, (quant, s, np.abs(got - want).max(), tol)

@@ -209,3 +209,23 @@ def test_openthai_gguf_round_trip_and_forward(tmp_path):
     assert got.shape == (3, 256)
     assert np.allclose(got, want, atol=2e-3, rtol=2e-3), np.abs(got - want).max()
     assert np.allclose(m["temperature"], np.exp(m["log_temperature"]))
+
+
+def test_openthai_quantised_gguf_decodes_through_the_oracle(tmp_path):
+    # the reference decodes any supported block type when it loads OpenThai
+    # matrices (src/models/openthai/model.rs:61 -> src/gguf.rs:250-336)
+    from laya_goish_b200 import openthai, synth
+    from laya_goish_b200.gguf_meta import GGUFError
+
+    path = synth.write_openthai(str(tmp_path / "ot_q8.gguf"), seed=5, d=64, ffn=128, quant=synth.Q8_0)
+    with pytest.raises(GGUFError, match="not F32/F16"):
+        openthai.load_weights(path, strict=False)  # a block type needs a decoder
+    m = openthai.load_weights(path, strict=False, decode=oracle.decode)
+    f = openthai.load_weights(synth.write_openthai(str(tmp_path / "ot_f16.gguf"), seed=5, d=64, ffn=128),
+                              strict=False)
+    w = "model.layers.0.mlp.gate_proj.weight"
+    assert m[w].shape == f[w].shape == (128, 64)
+    # Q8_0 of the same F16 draw: within half a quantisation step per block
+    step = np.abs(f[w]).reshape(-1, 32).max(axis=1) / 127
+    assert (np.abs(m[w] - f[w]).reshape(-1, 32).max(axis=1) <= 0.5 * step + 1e-3).all()
+    assert np.array_equal(m["model.norm.weight"], f["model.norm.weight"])  # vectors stay F32
