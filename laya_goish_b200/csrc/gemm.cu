@@ -7,12 +7,13 @@
 // one output row per token, optional bias), computed as a persistent,
 // warp-specialised kernel in two shapes:
 //
-// gemm_pair_kernel (M > 128): clusters of two CTAs on two SMs share one
+// gemm_pair_kernel (any M): clusters of two CTAs on two SMs share one
 //   256x256 output tile through tcgen05.mma.cta_group::2.  Each CTA stages
 //   its own 128 rows of A and 128 rows of B per 64-wide K block (32 KB per
 //   stage, 6 stages), so an SM moves a third fewer operand bytes from L2 per
 //   FLOP than with single-CTA 128x256 tiles.
-// gemm_tc_kernel (M <= 128): one CTA per 128x256 tile, 4 stages of 48 KB.
+// gemm_tc_kernel (a GPU without a second SM): one CTA per 128x256 tile, 4
+//   stages of 48 KB.
 //
 // Roles in both: warp 0 is the TMA producer (128-byte swizzle), warp 1
 // allocates 512 TMEM columns (two 256-column accumulators, so the epilogue of
@@ -525,7 +526,7 @@ int gemm_pair_group(int n_tiles) {
 }
 
 int gemm_ksplit(int M, int N, int K, int num_sms) {
-  if (M <= BM || num_sms < 2) return 1;
+  if (M < 1 || num_sms < 2) return 1;
   const int tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
   const int pairs = num_sms / 2, kblocks = (K + BK - 1) / BK;
   if (2 * tiles >= pairs) return 1;
@@ -542,7 +543,10 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
   if ((lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
-  if (a.M > BM && num_sms >= 2) {
+  // CTA pairs for every M (a pass of <= 128 rows leaves the second CTA's
+  // rows empty, but its weight tiles are split over twice the SMs and the
+  // residual GEMMs can split K); one CTA per tile only without a second SM
+  if (num_sms >= 2) {
     if (!make_map(&ta, A, a.M, a.K, lda, 128) || !make_map(&tb, B, a.N, a.K, ldb, 128))
       return cudaErrorInvalidValue;
     CUtensorMap tr = ta;
@@ -584,7 +588,7 @@ cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb,
     }
     return cudaErrorInvalidValue;
   }
-  if (epi == EPI_RESID && a.ksplit > 1) return cudaErrorInvalidValue;  // K splits need M > 128
+  if (epi == EPI_RESID && a.ksplit > 1) return cudaErrorInvalidValue;  // K splits need CTA pairs
   if (!make_map(&ta, A, a.M, a.K, lda, BM) || !make_map(&tb, B, a.N, a.K, ldb, BN)) return cudaErrorInvalidValue;
   a.m_tiles = (a.M + BM - 1) / BM;
   a.n_tiles = (a.N + BN - 1) / BN;

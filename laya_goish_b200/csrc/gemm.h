@@ -57,7 +57,7 @@ bool encode_tiled(CUtensorMap* m, int dtype, int rank, const void* base, const u
 cudaError_t gemm_launch(int epi, const half* A, int lda, const half* B, int ldb, GemmArgs a, int num_sms,
                         cudaStream_t st, bool pdl = false);
 // K splits for an EPI_RESID GEMM of this shape: more than 1 when its 256 x 256
-// output tiles would leave most CTA pairs idle (M > 128 only).
+// output tiles would leave most CTA pairs idle.
 int gemm_ksplit(int M, int N, int K, int num_sms);
 // Row bands per group of the CTA-pair tile walk for a GEMM of n_tiles column tiles.
 int gemm_pair_group(int n_tiles);
