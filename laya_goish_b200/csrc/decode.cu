@@ -1357,13 +1357,17 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
   const bool small = gemv_batch(c, nb);
   const int nbp = small ? pad_batch(nb) : nb;  // GEMV batch (padded rows are zero)
   // Batches past the GEMV run the layer GEMMs on the Q8_0 blocks where the
-  // model allows (scales and split planes were prepared by decode_run): the
-  // residual and QKV GEMMs split K when their output tiles are few, and the
-  // next RMSNorm / qkv_merge adds the partial planes in split order.
+  // model allows (scales and split planes were prepared by decode_run), else
+  // on the F16 operands: the residual and QKV GEMMs split K when their output
+  // tiles are few, and the next RMSNorm / qkv_merge adds the partial planes
+  // in split order.
   const bool q8 = !small && use_q8_gemm(m, r, nb) && r.layers.back().sqkv_t;
-  const int ks_q = q8 ? gemm_q8_ksplit(nb, qd + 2 * kd, d, r.num_sms) : 1;
-  const int ks_o = q8 ? gemm_q8_ksplit(nb, d, qd, r.num_sms) : 1;
-  const int ks_d = q8 ? gemm_q8_ksplit(nb, d, ffn, r.num_sms) : 1;
+  auto dsplit = [&](int N, int K) {
+    return small ? 1 : q8 ? gemm_q8_ksplit(nb, N, K, r.num_sms) : gemm_ksplit(nb, N, K, r.num_sms);
+  };
+  const int ks_q = dsplit(qd + 2 * kd, d);
+  const int ks_o = dsplit(d, qd);
+  const int ks_d = dsplit(d, ffn);
   int pend = 0;  // K splits of x not yet merged
   int rc;
   r.launches++;
@@ -1581,7 +1585,21 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       a.kcache = kcl;
       a.vcache = vcl;
       a.page_size = PAGE;
-      if ((rc = gemm_d(P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) return rc;
+      if (ks_q > 1) {
+        GemmArgs sp{};
+        sp.M = nb;
+        sp.N = qd + 2 * kd;
+        sp.K = d;
+        sp.ldo = qd + 2 * kd;
+        sp.ksplit = ks_q;
+        sp.part = r.kpart.as<float>();
+        if ((rc = gemm_d(P_GEMM_QKV, EPI_RESID, h, d, wqkv, d, sp))) return rc;
+        r.launches++;
+        LAYA_CK(qkv_merge(r.kpart.as<float>(), ks_q, (size_t)nb * (qd + 2 * kd), nb, L.bqkv, qd, kd, c.hd, c.KV,
+                          io.cur_pos, io.cur_slot, r.rope, PAGE, r.qb.as<half>(), qd, kcl, vcl, st));
+      } else if ((rc = gemm_d(P_GEMM_QKV, EPI_QKV, h, d, wqkv, d, a))) {
+        return rc;
+      }
     }
     if ((rc = decode_attention(m, r, nb, r.qb.as<half>(), kcl, vcl, io.cur_seq, sh, r.att.as<half>()))) return rc;
     if (seq) {
@@ -1620,7 +1638,10 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       b.K = qd;
       b.resid = x;
       b.ldo = d;
+      b.ksplit = ks_o;
+      b.part = r.kpart.as<float>();
       if ((rc = gemm_d(P_GEMM_O, EPI_RESID, r.att.as<half>(), qd, wo, qd, b))) return rc;
+      pend = ks_o;
     }
     if (!small && (rc = dnorm(L.ffn_norm))) return rc;
     if (small && v3) {
@@ -1689,7 +1710,10 @@ static int decode_step(Model& m, Replica& r, int nb, const StepIO& io, const Att
       dn.K = ffn;
       dn.resid = x;
       dn.ldo = d;
+      dn.ksplit = ks_d;
+      dn.part = r.kpart.as<float>();
       if ((rc = gemm_d(P_GEMM_DOWN, EPI_RESID, r.act.as<half>(), ffn, wd, ffn, dn))) return rc;
+      pend = ks_d;
     }
   }
   // final norm + full-vocabulary logits + greedy argmax
@@ -1854,10 +1878,13 @@ int decode_run(Model& m, Replica& r, const int32_t* ids, const int64_t* off, int
       (rc = r.qb.ensure((size_t)nbp * qd * 2)) || (rc = r.att.ensure((size_t)nbp * qd * 2)) ||
       (rc = r.act.ensure((size_t)nbp * c.ffn * 2)))
     return rc;
-  if (q8) {
-    // K-split partial planes of the step's Q8_0 GEMMs (allocated before any capture)
-    const int sq = gemm_q8_ksplit(n_seqs, qd + 2 * kd, c.d, r.num_sms);
-    const int so = std::max(gemm_q8_ksplit(n_seqs, c.d, qd, r.num_sms), gemm_q8_ksplit(n_seqs, c.d, c.ffn, r.num_sms));
+  if (!small) {
+    // K-split partial planes of the step's GEMMs (allocated before any capture)
+    auto ks = [&](int N, int K) {
+      return q8 ? gemm_q8_ksplit(n_seqs, N, K, r.num_sms) : gemm_ksplit(n_seqs, N, K, r.num_sms);
+    };
+    const int sq = ks(qd + 2 * kd, c.d);
+    const int so = std::max(ks(c.d, qd), ks(c.d, c.ffn));
     const size_t f = std::max((size_t)sq * n_seqs * (qd + 2 * kd), (size_t)so * n_seqs * c.d);
     if (std::max(sq, so) > 1 && (rc = r.kpart.ensure(f * 4))) return rc;
   }
