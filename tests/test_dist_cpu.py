@@ -69,3 +69,19 @@ def test_shard_ranges_cover_the_batch_in_order(world):
     # ragged lengths: balanced by tokens, not by count
     ragged = [1000] + [100] * 10
     assert bench.shard(ragged, 2, 0) == (0, 1) and bench.shard(ragged, 2, 1) == (1, 11)
+
+
+def test_cfg0q8_workload_is_cfg0s_request_on_the_q8_decoder():
+    # the auxiliary line that times the Q8_0-block GEMMs runs cfg0's request
+    # (one 256-token check over 2 candidates) on the cfg1 Q8_0 decoder
+    import bench
+    from laya_goish_b200 import synth
+
+    cname, requests, tokens, qdesc, _ = bench.AUX["cfg0q8"]
+    assert (cname, requests, tokens) == ("cfg1", 1, 256)
+    assert bench.AUX["cfg0"][1:4] == (requests, tokens, qdesc)
+    assert synth.CONFIGS[cname].quant == "q8_0"
+    a, na = bench.aux_questions("cfg0q8", 32000)
+    b, nb = bench.aux_questions("cfg0", 32000)
+    assert na == nb == 0
+    assert [[x.tolist() for x in q.arrays()[1:]] for q in a] == [[x.tolist() for x in q.arrays()[1:]] for q in b]
